@@ -1,0 +1,311 @@
+"""Benchmark of the recurrent hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+
+Headline workload: the fused selective scan at batch 8, seqlen 32768,
+dim 4096, dstate 16, bf16 I/O with fp32 state (inputs 8.6 GB per rank, far
+larger than L2, so no flush is needed between steps).  One step = one fused
+scan pass (softplus(delta+bias), exp(delta*A), recurrence, C.h + D*u,
+y*silu(z), final state) over the rank's batch.  Multi-GPU: every rank scans
+its own batch (units are independent channels; no collective on the data
+path) -> weak scaling; time = max over ranks of CUDA-event time.
+
+Prints ONE JSON line (rank 0).  ``--impl reference`` times the CPU
+restatement of the reference loop (the C oracle, all host threads) on a
+bounded sample of the same workload and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "selective-scan HBM GB/s (fused scan, bf16 I/O, fp32 state)"
+WORKLOAD = dict(batch=8, seqlen=32768, dim=4096, dstate=16)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def profile_traffic(kernel_key):
+    """DRAM bytes per launch from a committed ncu capture (profiles/traffic.json)."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(kernel_key)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    mhz.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for nm, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(nm)
+        os.unlink(self.path)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_scan_sample(seqlen, dim_sample, dstate, seed=0):
+    """Bounded CPU sample: one batch row x `dim_sample` channels x full seqlen."""
+    import numpy as np
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    from oracle import build as OC
+    inp = scan_inputs(1, seqlen, dim_sample, dstate, torch.float32, seed=seed)
+    n = lambda t: t.numpy()
+    args = (n(inp.u), n(inp.delta), n(inp.A), n(inp.B), n(inp.C), n(inp.D), n(inp.z), n(inp.delta_bias))
+    es = 2  # bytes per element of the bf16 workload the sample stands for
+    nbytes = (1 * seqlen * dim_sample * 4 * es + 2 * seqlen * dstate * es + (dim_sample * dstate + 2 * dim_sample) * 4
+              + dim_sample * dstate * 4)
+    sl = lambda a: np.ascontiguousarray(a[..., :64])
+    OC.scan(sl(args[0]), sl(args[1]), args[2], sl(args[3]), sl(args[4]), args[5], sl(args[6]), args[7],
+            softplus=True, z_mode=2, disc=0)  # warm the thread pool
+
+    def run():
+        t0 = time.perf_counter()
+        OC.scan(*args, softplus=True, z_mode=2, disc=0)
+        return time.perf_counter() - t0
+    return run, nbytes, OC.lib().hxm_oracle_max_threads()
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the CPU restatement of the reference loop on host cores."""
+    if rank != 0:
+        return
+    dim_sample = 2048
+    run, nbytes, threads = cpu_scan_sample(WORKLOAD["seqlen"], dim_sample, WORKLOAD["dstate"])
+    for _ in range(args.warmup):
+        run()
+    ts = [run() for _ in range(args.steps)]
+    t = sum(ts) / len(ts)
+    gbs = nbytes / t / 1e9
+    sample = f"1 batch row x {dim_sample} channels x seqlen {WORKLOAD['seqlen']} x dstate {WORKLOAD['dstate']} per step"
+    out = {"metric": METRIC, "value": gbs, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "selective scan b8 l32768 d4096 n16 (bounded CPU sample)", **WORKLOAD},
+           "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+           "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    from hybrid_model_mamba_xlstm_b200.kernels.selective_scan import selective_scan_fn
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    dev = torch.device("cuda", local if world > 1 else 0)
+    W = WORKLOAD
+    inp = scan_inputs(W["batch"], W["seqlen"], W["dim"], W["dstate"], torch.bfloat16, seed=1000 + rank,
+                      device=dev, on_device=True)
+    y = torch.empty_like(inp.u)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return selective_scan_fn(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, z=inp.z, delta_bias=inp.delta_bias,
+                                 delta_softplus=True, return_last_state=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(dev.index) as clk:
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        ev[0].record(stream)
+        for i in range(args.steps):
+            step()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    total_ms = ev[0].elapsed_time(ev[-1])
+    total_ms = max_over_ranks(total_ms, world)
+    clocks = clk.summary()
+    nbytes = inp.bytes_moved()
+    value = world * nbytes * args.steps / (total_ms / 1e3) / 1e9
+    pk, pk_kind = peaks()
+    launch_ms = sum(per) / len(per)
+    achieved = nbytes / (launch_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind,
+                "traffic": profile_traffic("scan_fwd_kernel bf16 b8 l32768 d4096 n16"),
+                "kernel": "hxm::scan::scan_fwd_kernel<bf16,16,64>", "algorithmic_bytes": nbytes}
+
+    # ---- end to end through the public API with host buffers (bounded: 1 batch row per rank)
+    e2e = e2e_scan(dev, args, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        run, cb, threads = cpu_scan_sample(W["seqlen"], 2048, W["dstate"])
+        run()
+        tcpu = min(run() for _ in range(2))
+        cpu = {"value": cb / tcpu / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"1 batch row x 2048 channels x seqlen {W['seqlen']} (C oracle, fp32, OpenMP)"}
+    if rank == 0:
+        out = {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+               "config": {"workload": "selective scan b8 l32768 d4096 n16 per rank", **W,
+                          "l2": "inputs 8.6 GB per step > L2 (no flush needed)", "parallelism": f"dp{world}"},
+               "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+               "clocks": clocks}
+        print(json.dumps(out), flush=True)
+
+
+def e2e_scan(dev, args, world):
+    from hybrid_model_mamba_xlstm_b200.kernels.selective_scan import selective_scan_fn
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    W = WORKLOAD
+    host = scan_inputs(1, W["seqlen"], W["dim"], W["dstate"], torch.bfloat16, seed=7, device=dev, on_device=True)
+    names = ["u", "delta", "z", "B", "C"]
+    pinned = {k: getattr(host, k).cpu().pin_memory() for k in names}
+    dbuf = {k: torch.empty_like(getattr(host, k)) for k in names}
+    y_host = torch.empty(pinned["u"].shape, dtype=torch.bfloat16).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    h2d = sum(t.numel() * t.element_size() for t in pinned.values())
+    d2h = y_host.numel() * y_host.element_size()
+
+    def step():
+        for k in names:
+            dbuf[k].copy_(pinned[k], non_blocking=True)
+        y = selective_scan_fn(dbuf["u"], dbuf["delta"], host.A, dbuf["B"], dbuf["C"], host.D, z=dbuf["z"],
+                              delta_bias=host.delta_bias, delta_softplus=True)
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    steps = max(1, min(args.steps, 5))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    nbytes = scan_inputs_bytes(1, W)
+    return {"value": world * nbytes * steps / (ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "sample": "1 batch row per rank per step, pinned host buffers",
+            "ms_per_step": ms / steps}
+
+
+def scan_inputs_bytes(batch, W):
+    L, dm, n, es = W["seqlen"], W["dim"], W["dstate"], 2
+    return batch * L * dm * 4 * es + 2 * batch * L * n * es + (dm * n + 2 * dm) * 4 + batch * dm * n * 4
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+"""ctypes binding of libhxm.so (include/hxm.h).
+
+The library is the product: every public op in this package ends in one of
+these C-ABI calls.  There is no CPU fallback — if the library is missing or
+a CUDA device is absent, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("HXM_LIB", os.path.join(_HERE, "lib", "libhxm.so"))
+
+HXM_OK, HXM_EBADARG, HXM_EUNSUPPORTED, HXM_ECUDA, HXM_ETIMEOUT = range(5)
+_STATUS = {0: "HXM_OK", 1: "HXM_EBADARG", 2: "HXM_EUNSUPPORTED", 3: "HXM_ECUDA", 4: "HXM_ETIMEOUT"}
+HXM_F32, HXM_BF16, HXM_F16 = 0, 1, 2
+
+_i64x3 = ct.c_int64 * 3
+_i64x2 = ct.c_int64 * 2
+
+
+class ScanArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("seqlen", ct.c_int32), ("dim", ct.c_int32), ("dstate", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("u", ct.c_void_p), ("u_stride", _i64x3),
+        ("delta", ct.c_void_p), ("delta_stride", _i64x3),
+        ("A", ct.c_void_p), ("A_stride", _i64x2),
+        ("B", ct.c_void_p), ("B_stride", _i64x3),
+        ("C", ct.c_void_p), ("C_stride", _i64x3),
+        ("D", ct.c_void_p),
+        ("z", ct.c_void_p), ("z_stride", _i64x3),
+        ("delta_bias", ct.c_void_p),
+        ("y", ct.c_void_p), ("y_stride", _i64x3),
+        ("h0", ct.c_void_p),
+        ("hT", ct.c_void_p),
+        ("z_mode", ct.c_int32), ("delta_softplus", ct.c_int32), ("discretization", ct.c_int32),
+    ]
+
+
+class MlstmArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("heads", ct.c_int32), ("seqlen", ct.c_int32), ("dqk", ct.c_int32),
+        ("dv", ct.c_int32), ("chunk", ct.c_int32), ("gate_mode", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("q", ct.c_void_p), ("q_stride", _i64x2),
+        ("k", ct.c_void_p), ("k_stride", _i64x2),
+        ("v", ct.c_void_p), ("v_stride", _i64x2),
+        ("log_i", ct.c_void_p), ("i_stride", _i64x2),
+        ("log_f", ct.c_void_p), ("f_stride", _i64x2),
+        ("h", ct.c_void_p), ("h_stride", _i64x2),
+        ("C0", ct.c_void_p), ("n0", ct.c_void_p), ("m0", ct.c_void_p),
+        ("CT", ct.c_void_p), ("nT", ct.c_void_p), ("mT", ct.c_void_p),
+        ("workspace", ct.c_void_p), ("workspace_bytes", ct.c_size_t),
+    ]
+
+
+class SsdArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("seqlen", ct.c_int32), ("heads", ct.c_int32), ("headdim", ct.c_int32),
+        ("dstate", ct.c_int32), ("chunk", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("x", ct.c_void_p), ("dt", ct.c_void_p), ("A", ct.c_void_p),
+        ("B", ct.c_void_p), ("C", ct.c_void_p),
+        ("D", ct.c_void_p), ("dt_bias", ct.c_void_p), ("dt_softplus", ct.c_int32),
+        ("y", ct.c_void_p), ("h0", ct.c_void_p), ("hT", ct.c_void_p),
+        ("workspace", ct.c_void_p), ("workspace_bytes", ct.c_size_t),
+    ]
+
+
+class SlstmArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("seqlen", ct.c_int32), ("heads", ct.c_int32), ("head_dim", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("gates_pre", ct.c_void_p), ("R", ct.c_void_p), ("norm_weight", ct.c_void_p),
+        ("eps", ct.c_float), ("exponential_gate", ct.c_int32),
+        ("h_out", ct.c_void_p),
+        ("h0", ct.c_void_p), ("c0", ct.c_void_p), ("m0", ct.c_void_p),
+        ("hT", ct.c_void_p), ("cT", ct.c_void_p), ("mT", ct.c_void_p),
+        ("error_flag", ct.c_void_p),
+    ]
+
+
+# symbol -> (restype, argtypes)
+SYMBOLS = {
+    "hxm_abi_version": (ct.c_int, []),
+    "hxm_last_error_string": (ct.c_char_p, []),
+    "hxm_selective_scan_fwd": (ct.c_int, [ct.POINTER(ScanArgs), ct.c_void_p]),
+    "hxm_mlstm_workspace_size": (ct.c_size_t, [ct.POINTER(MlstmArgs)]),
+    "hxm_mlstm_chunkwise_fwd": (ct.c_int, [ct.POINTER(MlstmArgs), ct.c_void_p]),
+    "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),
+    "hxm_ssd_chunk_scan_fwd": (ct.c_int, [ct.POINTER(SsdArgs), ct.c_void_p]),
+    "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class HxmError(RuntimeError):
+    """A non-OK hxm_status from the C ABI."""
+
+    def __init__(self, fn, status, msg):
+        super().__init__(f"{fn} returned {_STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+def lib() -> ct.CDLL:
+    """Load libhxm.so once (raises if it is missing: build it first)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(f"{LIB_PATH} not found: run `python -m hybrid_model_mamba_xlstm_b200.build`")
+                l = ct.CDLL(LIB_PATH)
+                for name, (res, args) in SYMBOLS.items():
+                    f = getattr(l, name)
+                    f.restype = res
+                    f.argtypes = args
+                _lib = l
+    return _lib
+
+
+def check(fn: str, status: int):
+    if status != HXM_OK:
+        msg = lib().hxm_last_error_string()
+        raise HxmError(fn, status, msg.decode() if msg else "")
+
+
+def call(fn: str, args, stream: int = 0):
+    """Call an hxm entry point with an args struct on `stream` (raw cudaStream_t)."""
+    args.struct_size = ct.sizeof(args)
+    check(fn, getattr(lib(), fn)(ct.byref(args), ct.c_void_p(stream)))

@@ -1,0 +1,12 @@
+// scan_inst_f32_euler.cu — instantiation of the selective-scan kernels
+// for float I/O with euler discretization (own translation unit so the
+// variants compile in parallel).
+#include "scan_kernel.cuh"
+
+namespace hxm {
+namespace scan {
+hxm_status dispatch_f32_euler(const Params& p, cudaStream_t s, int num_sms) {
+  return pick_ns<float, true, false>(p, s, num_sms);
+}
+}  // namespace scan
+}  // namespace hxm

@@ -1,0 +1,147 @@
+"""Chunkwise mLSTM ("TFLA") on B200: the reference's interface over the C ABI.
+
+Mirrors hybrid_xmamba/kernels/tfla/tfla_interface.py:
+  * ``apply_tfla(q, k, v, i_gate, f_gate)`` — same signature and semantics as
+    the reference (:142-163): activated gates (i = exp(.), f = sigmoid(.)) of
+    shape (B, H, L, D); the recurrence of ``tfla_forward_pytorch`` (:84-139)
+    C = f*C + i*k v^T, n = f*n + i*k, h = q C / max(q.n, 1).  Gates that are
+    per-head scalars broadcast over D (an ``expand``ed view, stride 0 on D)
+    take the scalar-gate kernel without being materialised.
+  * ``TFLAFunction`` — autograd Function with the reference's name (:18-81);
+    backward recomputes the recurrence under autograd with torch ops, as the
+    reference does (:52-81).
+  * ``mlstm_chunkwise_fwd(q, k, v, log_i, log_f, ...)`` — the extended entry:
+    gates in log space (log_i = input-gate pre-activation, log_f =
+    logsigmoid(forget pre-activation)), per head (B, H, L) or per channel
+    (B, H, L, Dqk), optional initial state and the final stabilized state
+    (C, n, m) with the true state equal to exp(m) * (C, n).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ... import _lib
+from .._common import dtype_code, ptr, require_cuda, stream_of
+
+__all__ = ["apply_tfla", "mlstm_chunkwise_fwd", "TFLAFunction"]
+
+
+def _dense_td(t):
+    """(B, H, L, D) with one dense (L, D) panel per head."""
+    if t.stride(-1) == 1 and t.stride(-2) == t.shape[-1]:
+        return t
+    return t.contiguous()
+
+
+def mlstm_chunkwise_fwd(q, k, v, log_i, log_f, C0=None, n0=None, m0=None, *, chunk=64, return_state=False,
+                        out=None):
+    """h (B, H, L, Dv) [, (C, n, m)] of the mLSTM recurrence with log-space gates.
+
+    q, k: (B, H, L, Dqk); v: (B, H, L, Dv) — bf16 runs the tcgen05 chunkwise
+    kernel, fp32 runs the exact fp32 recurrent kernel.  log_i, log_f: fp32
+    (B, H, L) (per-head gates) or (B, H, L, Dqk) (per-channel gates).
+    C0 (B, H, Dqk, Dv), n0 (B, H, Dqk), m0 (B, H): stabilized initial state.
+    """
+    who = "mlstm_chunkwise_fwd"
+    dev = require_cuda(q, k, v, log_i, log_f, C0, n0, m0, who=who)
+    if q.dim() != 4 or k.shape != q.shape or v.shape[:3] != q.shape[:3]:
+        raise ValueError(f"{who}: q, k (B,H,L,Dqk) and v (B,H,L,Dv) expected; got "
+                         f"{tuple(q.shape)} {tuple(k.shape)} {tuple(v.shape)}")
+    bsz, nh, L, dqk = q.shape
+    dv = v.shape[-1]
+    if log_i.shape == (bsz, nh, L) and log_f.shape == (bsz, nh, L):
+        gate_mode = 0
+    elif log_i.shape == (bsz, nh, L, dqk) and log_f.shape == (bsz, nh, L, dqk):
+        gate_mode = 1
+    else:
+        raise ValueError(f"{who}: gates must be (B,H,L) or (B,H,L,Dqk); got {tuple(log_i.shape)} {tuple(log_f.shape)}")
+    io = q.dtype if q.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    q, k, v = (_dense_td(t if t.dtype == io else t.to(io)) for t in (q, k, v))
+    gi = log_i.float()
+    gf = log_f.float()
+    # gates: (b, h) strides free, (t[, d]) dense
+    if gate_mode == 0:
+        gi = gi if gi.stride(-1) == 1 else gi.contiguous()
+        gf = gf if gf.stride(-1) == 1 else gf.contiguous()
+    else:
+        gi, gf = _dense_td(gi), _dense_td(gf)
+    h = torch.empty((bsz, nh, L, dv), device=dev, dtype=io) if out is None else out
+    st = None
+    if return_state:
+        st = (torch.empty((bsz, nh, dqk, dv), device=dev, dtype=torch.float32),
+              torch.empty((bsz, nh, dqk), device=dev, dtype=torch.float32),
+              torch.empty((bsz, nh), device=dev, dtype=torch.float32))
+    c32 = lambda t: None if t is None else t.float().contiguous()
+    C0, n0, m0 = c32(C0), c32(n0), c32(m0)
+    a = _lib.MlstmArgs()
+    a.batch, a.heads, a.seqlen, a.dqk, a.dv = bsz, nh, L, dqk, dv
+    a.chunk, a.gate_mode, a.io_dtype = chunk, gate_mode, dtype_code(q)
+    a.q, a.q_stride = ptr(q), q.stride()[:2]
+    a.k, a.k_stride = ptr(k), k.stride()[:2]
+    a.v, a.v_stride = ptr(v), v.stride()[:2]
+    a.log_i, a.i_stride = ptr(gi), gi.stride()[:2]
+    a.log_f, a.f_stride = ptr(gf), gf.stride()[:2]
+    a.h, a.h_stride = ptr(h), h.stride()[:2]
+    a.C0, a.n0, a.m0 = ptr(C0), ptr(n0), ptr(m0)
+    if st is not None:
+        a.CT, a.nT, a.mT = ptr(st[0]), ptr(st[1]), ptr(st[2])
+    a.struct_size = ctypes.sizeof(a)
+    ws_bytes = _lib.lib().hxm_mlstm_workspace_size(a)
+    ws = torch.empty(max(int(ws_bytes), 1), device=dev, dtype=torch.uint8) if ws_bytes else None
+    a.workspace, a.workspace_bytes = ptr(ws), int(ws_bytes)
+    _lib.call("hxm_mlstm_chunkwise_fwd", a, stream_of(dev))
+    return (h, st) if return_state else h
+
+
+def _gate_logs(i_gate, f_gate):
+    """log-space gates; per-head when the gates are broadcast views over D."""
+    if i_gate.dim() == 4 and i_gate.stride(-1) == 0 and f_gate.stride(-1) == 0:
+        return torch.log(i_gate[..., 0].float()), torch.log(f_gate[..., 0].float())
+    return torch.log(i_gate.float()), torch.log(f_gate.float())
+
+
+def _tfla_torch(q, k, v, ig, fg):
+    """Differentiable torch restatement (backward only; reference :84-139)."""
+    bsz, nh, L, d = q.shape
+    C = torch.zeros(bsz, nh, d, v.shape[-1], device=q.device, dtype=torch.float32)
+    n = torch.zeros(bsz, nh, d, device=q.device, dtype=torch.float32)
+    hs = []
+    for t in range(L):
+        f_t, i_t = fg[:, :, t].float(), ig[:, :, t].float()
+        C = f_t[..., None] * C + i_t[..., None] * (k[:, :, t, :, None].float() * v[:, :, t, None, :].float())
+        n = f_t * n + i_t * k[:, :, t].float()
+        num = torch.einsum("bhd,bhde->bhe", q[:, :, t].float(), C)
+        den = torch.clamp(torch.einsum("bhd,bhd->bh", q[:, :, t].float(), n), min=1.0)[..., None]
+        hs.append(num / den)
+    return torch.stack(hs, 2)
+
+
+class TFLAFunction(torch.autograd.Function):
+    """Autograd wrapper with the reference's name (tfla_interface.py:18-81)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, i_gate, f_gate):
+        ctx.save_for_backward(q, k, v, i_gate, f_gate)
+        log_i, log_f = _gate_logs(i_gate, f_gate)
+        return mlstm_chunkwise_fwd(q, k, v, log_i, log_f)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, i_gate, f_gate = ctx.saved_tensors
+        with torch.enable_grad():
+            ins = [t.detach().requires_grad_(True) for t in (q, k, v, i_gate, f_gate)]
+            out = _tfla_torch(*ins)
+            out.backward(grad_output.float())
+        return tuple(t.grad.to(o.dtype) if t.grad is not None else None
+                     for t, o in zip(ins, (q, k, v, i_gate, f_gate)))
+
+
+def apply_tfla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, i_gate: torch.Tensor,
+               f_gate: torch.Tensor) -> torch.Tensor:
+    """Drop-in for hybrid_xmamba.kernels.tfla.apply_tfla (tfla_interface.py:142-163).
+
+    q, k, v, i_gate, f_gate: (B, H, L, D); i_gate > 0 and f_gate > 0 (as
+    mLSTMBlock produces them: exp and sigmoid)."""
+    return TFLAFunction.apply(q, k, v, i_gate, f_gate)

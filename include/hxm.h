@@ -1,0 +1,202 @@
+/*
+ * hxm.h — C ABI of the B200 (sm_100a) recurrent hot path of the hybrid
+ * Mamba / xLSTM model (selective scan, chunkwise mLSTM, Mamba-2 SSD chunked
+ * scan, sLSTM recurrence).
+ *
+ * Conventions shared by every entry point
+ *   - All tensors are caller-owned DEVICE buffers passed as raw pointers plus
+ *     strides counted in ELEMENTS (not bytes).  Nothing on the hot path
+ *     allocates; an entry point that needs scratch says so through its
+ *     *_workspace_size() companion and takes a caller-owned workspace.
+ *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream).
+ *     Work is enqueued asynchronously; no entry point synchronizes the host.
+ *   - Entry points never throw and never abort: they return an hxm_status.
+ *     On failure hxm_last_error_string() returns a thread-local message.
+ *   - Argument structs start with `struct_size` = sizeof(the struct) so the
+ *     ABI can grow; a caller built against an older header is rejected with
+ *     HXM_EBADARG instead of being misread.
+ *   - Stateless and re-entrant; one process per GPU; the device is the
+ *     caller's current device.
+ */
+#ifndef HXM_H_
+#define HXM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HXM_ABI_VERSION 1
+
+typedef enum hxm_status {
+  HXM_OK = 0,
+  HXM_EBADARG = 1,      /* shape / stride / dtype / pointer validation failed   */
+  HXM_EUNSUPPORTED = 2, /* valid request this build has no kernel for           */
+  HXM_ECUDA = 3,        /* a CUDA runtime call or kernel launch failed          */
+  HXM_ETIMEOUT = 4      /* a bounded device-side wait gave up (error flag set)  */
+} hxm_status;
+
+typedef enum hxm_dtype { HXM_F32 = 0, HXM_BF16 = 1, HXM_F16 = 2 } hxm_dtype;
+
+/* ------------------------------------------------------------------------ */
+/* Library                                                                   */
+/* ------------------------------------------------------------------------ */
+
+/* ABI version compiled into the library (HXM_ABI_VERSION). */
+int hxm_abi_version(void);
+
+/* Thread-local description of the last failure in this thread ("" if none). */
+const char* hxm_last_error_string(void);
+
+/* ------------------------------------------------------------------------ */
+/* 1. Selective scan (Mamba S6)                                               */
+/*                                                                           */
+/* Replaces selective_scan / SelectiveScanFunction.forward                   */
+/*   (hybrid_xmamba/kernels/selective_scan/scan_interface.py:17-60,155-180)  */
+/* and its CPU loop selective_scan_pytorch (scan_interface.py:103-152), plus */
+/* the CUDA kernel selective_scan_triton (scan_triton.py:408-500).           */
+/*                                                                           */
+/* Per (b, d) channel, state h[n] (fp32, starts at h0 or 0):                  */
+/*   delta   = softplus(dt + delta_bias)   (softplus/bias optional)          */
+/*   euler:  h = exp(delta*A[d,n]) * h + delta * B[b,t,n] * u              */
+/*   zoh:    h = exp(dA) * h + Bbar * u, Bbar = (exp(dA)-1)/A * B, or         */
+/*           delta*B when |delta*A| < 0.01 (scan_triton.py:135-160)           */
+/*   y       = sum_n C[b,t,n] h[n] + D[d] * u                                */
+/*   z_mode: 0 none, 1 y*z (scan_interface.py:57-58), 2 y*silu(z)            */
+/* Logical shapes: u, delta, z, y (batch, seqlen, dim); A (dim, dstate);     */
+/* B, C (batch, seqlen, dstate); D, delta_bias (dim); h0, hT                 */
+/* (batch, dim, dstate) fp32 contiguous.  Any element strides are accepted;  */
+/* the fast path wants either the time axis or the channel axis unit-stride. */
+/* ------------------------------------------------------------------------ */
+typedef struct hxm_scan_args {
+  size_t struct_size;
+  int32_t batch, seqlen, dim, dstate;
+  hxm_dtype io_dtype;       /* dtype of u, delta, z, B, C, y                 */
+  const void* u;      int64_t u_stride[3];      /* (b, t, d)                 */
+  const void* delta;  int64_t delta_stride[3];  /* (b, t, d)                 */
+  const float* A;     int64_t A_stride[2];      /* (d, n)   fp32             */
+  const void* B;      int64_t B_stride[3];      /* (b, t, n)                 */
+  const void* C;      int64_t C_stride[3];      /* (b, t, n)                 */
+  const float* D;                               /* (d) fp32 or NULL          */
+  const void* z;      int64_t z_stride[3];      /* (b, t, d) or NULL         */
+  const float* delta_bias;                      /* (d) fp32 or NULL          */
+  void* y;            int64_t y_stride[3];      /* (b, t, d)                 */
+  const float* h0;                              /* (b, d, n) fp32 or NULL    */
+  float* hT;                                    /* (b, d, n) fp32 or NULL    */
+  int32_t z_mode;           /* 0 none, 1 multiply, 2 silu-gate               */
+  int32_t delta_softplus;   /* 0/1                                           */
+  int32_t discretization;   /* 0 euler (reference CPU path), 1 zoh           */
+} hxm_scan_args;
+
+hxm_status hxm_selective_scan_fwd(const hxm_scan_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 2. mLSTM chunkwise forward ("TFLA")                                        */
+/*                                                                           */
+/* Replaces apply_tfla / TFLAFunction.forward / tfla_forward_pytorch         */
+/*   (hybrid_xmamba/kernels/tfla/tfla_interface.py:18-49,84-139,142-163)     */
+/* and the intended chunkwise kernels of tfla_triton.py:23-359.              */
+/*                                                                           */
+/* Per (b, h): C (dqk x dv), n (dqk) with                                     */
+/*   C_t = f_t * C_{t-1} + i_t * k_t v_t^T,  n_t = f_t * n_{t-1} + i_t * k_t */
+/*   h_t = (q_t^T C_t) / max(q_t . n_t, 1)                                   */
+/* Gates are given as PRE-activations in log space:                          */
+/*   log_i = input-gate preactivation (i = exp(log_i)),                      */
+/*   log_f = log forget gate (f = exp(log_f), e.g. logsigmoid(preact)).      */
+/* gate_mode 0: per-head scalar gates (b, h, t); 1: per-channel gates        */
+/* (b, h, t, dqk) as in mLSTMBlock (mlstm_block.py:117-129).                 */
+/* The state is kept stabilized: C = exp(m) * Cs, n = exp(m) * ns.  Inputs    */
+/* C0/n0/m0 and outputs CT/nT/mT use that representation (NULL = zero).      */
+/* q, k, v, h: (b, h, t, d) with arbitrary (b, h) strides, unit d stride and */
+/* t stride = d (one contiguous (t, d) panel per head); bf16.                */
+/* Requires a workspace of hxm_mlstm_workspace_size() bytes.                 */
+/* ------------------------------------------------------------------------ */
+typedef struct hxm_mlstm_args {
+  size_t struct_size;
+  int32_t batch, heads, seqlen, dqk, dv;
+  int32_t chunk;            /* chunk length (64 or 128)                      */
+  int32_t gate_mode;        /* 0 scalar per head, 1 per channel              */
+  hxm_dtype io_dtype;       /* q, k, v, h                                    */
+  const void* q; int64_t q_stride[2];   /* (b, h) strides; (t, d) dense      */
+  const void* k; int64_t k_stride[2];
+  const void* v; int64_t v_stride[2];
+  const float* log_i;  int64_t i_stride[2];   /* (b, h); t[,d] dense         */
+  const float* log_f;  int64_t f_stride[2];
+  void* h;   int64_t h_stride[2];
+  const float* C0; const float* n0; const float* m0;  /* (b,h,dqk,dv) (b,h,dqk) (b,h) fp32 or NULL */
+  float* CT; float* nT; float* mT;                    /* same shapes, or NULL */
+  void* workspace; size_t workspace_bytes;
+} hxm_mlstm_args;
+
+size_t hxm_mlstm_workspace_size(const hxm_mlstm_args* args);
+hxm_status hxm_mlstm_chunkwise_fwd(const hxm_mlstm_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 3. Mamba-2 SSD chunked scan (ngroups = 1)                                  */
+/*                                                                           */
+/* No function of the reference computes this; its arithmetic is the Euler   */
+/* selective scan (scan_interface.py:103-152) with channel d = (head, p),    */
+/* A[d, :] = A[head], delta[b, t, d] = dt[b, t, head] and B, C shared.       */
+/*   h[p, n] = exp(dt*A) h[p, n] + dt * x[p] * B[n];  y[p] = C.h[p,:] + D*x  */
+/* x, y (b, t, heads, p) bf16; B, C (b, t, n) bf16; dt (b, t, heads) fp32;   */
+/* A, D, dt_bias (heads) fp32; state (b, heads, p, n) fp32.  All dense.      */
+/* ------------------------------------------------------------------------ */
+typedef struct hxm_ssd_args {
+  size_t struct_size;
+  int32_t batch, seqlen, heads, headdim, dstate;
+  int32_t chunk;            /* 64, 128 or 256                                */
+  hxm_dtype io_dtype;       /* x, B, C, y                                    */
+  const void* x; const float* dt; const float* A;
+  const void* B; const void* C;
+  const float* D;           /* (heads) or NULL                               */
+  const float* dt_bias;     /* (heads) or NULL                               */
+  int32_t dt_softplus;
+  void* y;
+  const float* h0;          /* (b, heads, p, n) or NULL                      */
+  float* hT;                /* (b, heads, p, n) or NULL                      */
+  void* workspace; size_t workspace_bytes;
+} hxm_ssd_args;
+
+size_t hxm_ssd_workspace_size(const hxm_ssd_args* args);
+hxm_status hxm_ssd_chunk_scan_fwd(const hxm_ssd_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 4. sLSTM recurrence                                                        */
+/*                                                                           */
+/* Replaces the inline loop of sLSTMBlock.forward                            */
+/*   (hybrid_xmamba/layers/slstm_block.py:91-127) including its fused        */
+/* RMSNorm over head_dim (layers/normalization.py:32-34).                    */
+/* Per (b, head) with hd = head_dim and gate pre-activations                 */
+/*   g_t = gates_pre[b, t, head, :, :] + R[head]^T h_{t-1}    (4 x hd)       */
+/* ordered [i | f | o | ctilde] as gates.chunk(4, -1) splits them:           */
+/*   i = exp(g_i) (or sigmoid), f = sigmoid(g_f), o = sigmoid(g_o),          */
+/*   c = f*c + i*tanh(g_c);  h = o * tanh(w * c / sqrt(mean(c^2) + eps))     */
+/* R (heads, hd, 4*hd) bf16 or NULL (the reference has no recurrent R).      */
+/* gates_pre (b, t, heads, 4, hd) bf16/fp32 dense; h_out (b, t, heads, hd);  */
+/* h0, c0, hT, cT (b, heads, hd) fp32 or NULL.  The cell is stored           */
+/* stabilized: c = exp(m) * cs with m >= 0 (mT optional, (b, heads)).        */
+/* ------------------------------------------------------------------------ */
+typedef struct hxm_slstm_args {
+  size_t struct_size;
+  int32_t batch, seqlen, heads, head_dim;
+  hxm_dtype io_dtype;       /* gates_pre, h_out                              */
+  const void* gates_pre;
+  const void* R;            /* bf16 (heads, hd, 4*hd) or NULL                */
+  const float* norm_weight; /* (hd)                                          */
+  float eps;
+  int32_t exponential_gate; /* 1: i = exp, 0: i = sigmoid                    */
+  void* h_out;
+  const float* h0; const float* c0; const float* m0;
+  float* hT; float* cT; float* mT;
+  int32_t* error_flag;      /* device int, set nonzero if a bounded wait gave up; may be NULL */
+} hxm_slstm_args;
+
+hxm_status hxm_slstm_scan_fwd(const hxm_slstm_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HXM_H_ */

@@ -1,0 +1,72 @@
+"""C-ABI library checks that need no GPU: it loads, exports every symbol the
+header declares, reports its ABI version and rejects malformed arguments
+with HXM_EBADARG before touching CUDA."""
+import ctypes as ct
+import os
+import re
+
+import pytest
+
+from hybrid_model_mamba_xlstm_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    names = set()
+    for f in os.listdir(os.path.join(ROOT, "include")):
+        if f.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", f)).read()
+            names |= set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(hxm_[a-z0-9_]+)\s*\(", text, re.M))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    declared = _declared_symbols()
+    assert {"hxm_selective_scan_fwd", "hxm_mlstm_chunkwise_fwd", "hxm_ssd_chunk_scan_fwd",
+            "hxm_slstm_scan_fwd", "hxm_last_error_string", "hxm_abi_version"} <= declared
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert set(_lib.SYMBOLS) >= declared
+
+
+def test_abi_version():
+    assert _lib.lib().hxm_abi_version() == 1
+
+
+def test_struct_sizes_match_header_layout():
+    # the C side checks struct_size == sizeof(struct); a mismatch is HXM_EBADARG
+    for cls, fn in [(_lib.ScanArgs, "hxm_selective_scan_fwd"), (_lib.MlstmArgs, "hxm_mlstm_chunkwise_fwd"),
+                    (_lib.SsdArgs, "hxm_ssd_chunk_scan_fwd"), (_lib.SlstmArgs, "hxm_slstm_scan_fwd")]:
+        a = cls()
+        a.struct_size = ct.sizeof(a) + 8
+        st = getattr(_lib.lib(), fn)(ct.byref(a), None)
+        assert st == _lib.HXM_EBADARG, fn
+        assert b"struct_size" in _lib.lib().hxm_last_error_string()
+
+
+def test_scan_rejects_bad_arguments_without_cuda():
+    lib = _lib.lib()
+    assert lib.hxm_selective_scan_fwd(None, None) == _lib.HXM_EBADARG
+    a = _lib.ScanArgs()
+    a.struct_size = ct.sizeof(a)
+    a.batch, a.seqlen, a.dim, a.dstate = 1, 4, 8, 0  # dstate 0 invalid
+    assert lib.hxm_selective_scan_fwd(ct.byref(a), None) == _lib.HXM_EBADARG
+    a.dstate = 65
+    assert lib.hxm_selective_scan_fwd(ct.byref(a), None) == _lib.HXM_EUNSUPPORTED
+    a.dstate, a.z_mode = 16, 2  # silu gate without z
+    assert lib.hxm_selective_scan_fwd(ct.byref(a), None) == _lib.HXM_EBADARG
+    a.z_mode, a.io_dtype = 0, 7
+    assert lib.hxm_selective_scan_fwd(ct.byref(a), None) == _lib.HXM_EBADARG
+    # empty batch is a no-op success (nothing is launched)
+    a.io_dtype, a.batch = _lib.HXM_F32, 0
+    assert lib.hxm_selective_scan_fwd(ct.byref(a), None) == _lib.HXM_OK
+
+
+def test_python_wrapper_refuses_cpu_tensors():
+    import torch
+    from hybrid_model_mamba_xlstm_b200.kernels import selective_scan
+    x = torch.zeros(1, 4, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        selective_scan(x, x, torch.zeros(8, 16), torch.zeros(1, 4, 16), torch.zeros(1, 4, 16), torch.ones(8))

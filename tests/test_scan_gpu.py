@@ -1,0 +1,183 @@
+"""Selective scan on the GPU vs the oracle and the reference's golden vectors.
+
+Tolerances (normwise relative error): fp32 I/O 1e-5; bf16 I/O 2e-2 against
+the oracle run in float64 on the same bf16-rounded inputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import numpy_ref as R
+from tests.conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL32, TOL16 = 1e-5, 2e-2
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("needs CUDA")
+    from hybrid_model_mamba_xlstm_b200.kernels.selective_scan import scan_interface as si
+    return si
+
+
+def cu(a, dtype=torch.float32):
+    return torch.as_tensor(np.asarray(a)).to(device="cuda", dtype=dtype)
+
+
+def np64(t):
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def test_golden_reference_api_fp32(ops, golden):
+    g = golden("scan_small")
+    y = ops.selective_scan(cu(g["x"]), cu(g["dt"]), cu(g["A"]), cu(g["B"]), cu(g["C"]), cu(g["D"]))
+    assert rel_err(np64(y), g["y"]) < TOL32
+    yz = ops.selective_scan(cu(g["x"]), cu(g["dt"]), cu(g["A"]), cu(g["B"]), cu(g["C"]), cu(g["D"]), z=cu(g["z"]))
+    assert rel_err(np64(yz), g["y_z"]) < TOL32
+
+
+def test_golden_fused_bdl_fp32(ops, golden):
+    g = golden("scan_cfg1_slice")
+    y = ops.selective_scan_fn(cu(g["u"]), cu(g["raw"]), cu(g["A"]), cu(g["B"]), cu(g["C"]), cu(g["D"]),
+                              z=cu(g["z"]), delta_bias=cu(g["bias"]), delta_softplus=True)
+    assert rel_err(np64(y), g["y"]) < TOL32
+
+
+def _oracle_bdl(inp, dtype_round=None, disc="euler", h0=None):
+    t = lambda a: np.swapaxes(np64(a), 1, 2)
+    return R.selective_scan(t(inp.u), t(inp.delta), np64(inp.A), t(inp.B), t(inp.C), np64(inp.D), z=t(inp.z),
+                            z_mode="silu", delta_bias=np64(inp.delta_bias), delta_softplus=True,
+                            discretization=disc, h0=h0)
+
+
+def test_fp32_full_parity_workload_with_final_state(ops):
+    """batch 2, seqlen 512, dim 1536, dstate 16, fp32: y and h_L within 1e-5."""
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    inp = scan_inputs(2, 512, 1536, 16, torch.float32, seed=0, device="cuda")
+    y, h = ops.selective_scan_fn(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, z=inp.z,
+                                 delta_bias=inp.delta_bias, delta_softplus=True, return_last_state=True)
+    yr, hr = _oracle_bdl(inp)
+    assert rel_err(np.swapaxes(np64(y), 1, 2), yr) < TOL32
+    assert rel_err(np64(h), hr) < TOL32
+
+
+@pytest.mark.parametrize("shape", [(2, 2048, 256, 16), (1, 1000, 200, 16), (3, 37, 40, 8), (1, 1, 64, 16)])
+def test_bf16_parity(ops, shape):
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    b, L, dm, n = shape
+    inp = scan_inputs(b, L, dm, n, torch.bfloat16, seed=1, device="cuda")
+    y, h = ops.selective_scan_fn(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, z=inp.z,
+                                 delta_bias=inp.delta_bias, delta_softplus=True, return_last_state=True)
+    yr, hr = _oracle_bdl(inp)
+    assert rel_err(np.swapaxes(np64(y), 1, 2), yr) < TOL16
+    assert rel_err(np64(h), hr) < TOL16
+
+
+def _rand_blD(b, L, dm, n, seed, dtype):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(b, L, dm, generator=g)
+    dt = torch.nn.functional.softplus(torch.randn(b, L, dm, generator=g) - 2.0)
+    A = -torch.exp(torch.randn(dm, n, generator=g))
+    B = torch.randn(b, L, n, generator=g)
+    C = torch.randn(b, L, n, generator=g)
+    D = torch.randn(dm, generator=g)
+    z = torch.randn(b, L, dm, generator=g)
+    return [t.to("cuda", dtype) for t in (x, dt)] + [A.cuda()] + [t.to("cuda", dtype) for t in (B, C)] + \
+        [D.cuda(), z.to("cuda", dtype)]
+
+
+@pytest.mark.parametrize("layout", ["bld", "bdl", "strided", "unaligned"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_layouts_general_A(ops, layout, dtype):
+    """Reference layout (B,L,D), time-major memory, non-unit strides and
+    16-byte-misaligned bases all give the oracle's answer (general-A path)."""
+    b, L, dm, n = 2, 77, 96, 16
+    x, dt, A, B, C, D, z = _rand_blD(b, L, dm, n, 3, dtype)
+
+    def relayout(t):
+        if layout == "bld":
+            return t
+        if layout == "bdl":
+            return t.transpose(1, 2).contiguous().transpose(1, 2)
+        if layout == "strided":
+            big = torch.zeros(t.shape[0], t.shape[1], 2 * t.shape[2], device=t.device, dtype=t.dtype)
+            big[:, :, ::2] = t
+            return big[:, :, ::2]
+        buf = torch.zeros(t.numel() + 1, device=t.device, dtype=t.dtype)
+        v = buf[1:].view(t.shape)
+        v.copy_(t)
+        return v
+
+    xs, dts, Bs, Cs, zs = (relayout(t) for t in (x, dt, B, C, z))
+    y = ops.selective_scan(xs, dts, A, Bs, Cs, D, z=zs)
+    yr, _ = R.selective_scan(np64(x), np64(dt), np64(A), np64(B), np64(C), np64(D), z=np64(z), z_mode="mul")
+    tol = TOL32 if dtype == torch.float32 else TOL16
+    assert rel_err(np64(y), yr) < tol
+
+
+@pytest.mark.parametrize("n", [1, 4, 16, 33, 64])
+def test_dstate_sizes(ops, n):
+    x, dt, A, B, C, D, z = _rand_blD(1, 50, 64, n, 4, torch.float32)
+    y, h = ops.selective_scan_raw(x, dt, A, B, C, D, return_last_state=True)
+    yr, hr = R.selective_scan(np64(x), np64(dt), np64(A), np64(B), np64(C), np64(D))
+    assert rel_err(np64(y), yr) < TOL32
+    assert rel_err(np64(h), hr) < TOL32
+
+
+def test_zoh_discretization(ops):
+    x, dt, A, B, C, D, z = _rand_blD(2, 64, 64, 16, 5, torch.float32)
+    dt = dt * 0.2  # straddle the |dt*A| < 0.01 Taylor threshold
+    y, h = ops.selective_scan_raw(x, dt, A, B, C, D, discretization="zoh", return_last_state=True)
+    yr, hr = R.selective_scan(np64(x), np64(dt), np64(A), np64(B), np64(C), np64(D), discretization="zoh")
+    assert rel_err(np64(y), yr) < TOL32
+    assert rel_err(np64(h), hr) < TOL32
+
+
+def test_segmented_equals_whole(ops):
+    """Final state out + initial state in: two segments reproduce one pass."""
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    inp = scan_inputs(2, 300, 128, 16, torch.float32, seed=6, device="cuda")
+    kw = dict(delta_bias=inp.delta_bias, delta_softplus=True, return_last_state=True)
+    y, h = ops.selective_scan_fn(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, z=inp.z, **kw)
+    s = slice(0, 131)
+    e = slice(131, None)
+    y1, h1 = ops.selective_scan_fn(inp.u[..., s], inp.delta[..., s], inp.A, inp.B[..., s], inp.C[..., s], inp.D,
+                                   z=inp.z[..., s], **kw)
+    y2, h2 = ops.selective_scan_fn(inp.u[..., e], inp.delta[..., e], inp.A, inp.B[..., e], inp.C[..., e], inp.D,
+                                   z=inp.z[..., e], initial_state=h1, **kw)
+    assert rel_err(np64(torch.cat([y1, y2], -1)), np64(y)) < 1e-6
+    assert rel_err(np64(h2), np64(h)) < 1e-6
+
+
+def test_empty_and_deterministic(ops):
+    x, dt, A, B, C, D, z = _rand_blD(2, 40, 64, 16, 7, torch.bfloat16)
+    y1 = ops.selective_scan(x, dt, A, B, C, D)
+    y2 = ops.selective_scan(x, dt, A, B, C, D)
+    assert torch.equal(y1, y2)
+    h0 = torch.randn(2, 64, 16, device="cuda")
+    y0, hT = ops.selective_scan_raw(x[:, :0], dt[:, :0], A, B[:, :0], C[:, :0], D, h0=h0, return_last_state=True)
+    assert y0.shape == (2, 0, 64) and torch.equal(hT, h0)
+    e = ops.selective_scan(x[:0], dt[:0], A, B[:0], C[:0], D)
+    assert e.shape == (0, 40, 64)
+
+
+def test_large_workload_sampled_channels(ops):
+    """batch 8, seqlen 32768, dim 4096, dstate 16, bf16 (the GB/s workload):
+    a sample of channels checked against the float64 oracle at full length."""
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    inp = scan_inputs(8, 32768, 4096, 16, torch.bfloat16, seed=0, device="cuda", on_device=True)
+    y, h = ops.selective_scan_fn(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, z=inp.z,
+                                 delta_bias=inp.delta_bias, delta_softplus=True, return_last_state=True)
+    assert torch.isfinite(y).all()
+    chans = torch.tensor([0, 1, 777, 2048, 4095], device="cuda")
+    for b in (0, 7):
+        t = lambda a: np.swapaxes(np64(a[b:b + 1, chans]), 1, 2)
+        tb = lambda a: np.swapaxes(np64(a[b:b + 1]), 1, 2)
+        yr, hr = R.selective_scan(t(inp.u), t(inp.delta), np64(inp.A[chans]), tb(inp.B), tb(inp.C),
+                                  np64(inp.D[chans]), z=t(inp.z), z_mode="silu",
+                                  delta_bias=np64(inp.delta_bias[chans]), delta_softplus=True)
+        assert rel_err(np.swapaxes(np64(y[b:b + 1, chans]), 1, 2), yr) < TOL16
+        assert rel_err(np64(h[b:b + 1, chans]), hr) < TOL16
