@@ -26,6 +26,17 @@ template <> HXM_DEV float from_f32<float>(float v) { return v; }
 template <> HXM_DEV __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 template <> HXM_DEV __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
+// two floats -> one 32-bit word of two 16-bit values (one packed convert)
+template <typename T> HXM_DEV uint32_t pack2(float lo, float hi);
+template <> HXM_DEV uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> HXM_DEV uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 // ---- hardware transcendental instructions (MUFU) ---------------------------
 HXM_DEV float ex2_approx(float x) {
   float y;

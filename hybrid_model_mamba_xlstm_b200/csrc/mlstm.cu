@@ -1,0 +1,56 @@
+// mlstm.cu — C ABI of the mLSTM chunkwise forward (argument checks + dispatch).
+//
+// Replaces apply_tfla / TFLAFunction.forward / tfla_forward_pytorch
+// (hybrid_xmamba/kernels/tfla/tfla_interface.py:18-49,84-139,142-163).
+// bf16 I/O with per-head gates runs the tcgen05 chunkwise kernel; fp32 I/O,
+// per-channel gates and other shapes run the exact CUDA-core recurrence.
+#include "capi_internal.h"
+#include "mlstm.h"
+
+using hxm::mlstm::Params;
+
+static hxm_status fill(const hxm_mlstm_args* a, Params& p) {
+  HXM_REQUIRE(a != nullptr, "hxm_mlstm_chunkwise_fwd: args is NULL");
+  HXM_REQUIRE(a->struct_size == sizeof(hxm_mlstm_args), "hxm_mlstm_chunkwise_fwd: struct_size %zu != %zu",
+              a->struct_size, sizeof(hxm_mlstm_args));
+  HXM_REQUIRE(a->batch >= 0 && a->heads >= 0 && a->seqlen >= 0 && a->dqk >= 1 && a->dv >= 1,
+              "hxm_mlstm_chunkwise_fwd: bad dims B=%d H=%d L=%d dqk=%d dv=%d", a->batch, a->heads, a->seqlen,
+              a->dqk, a->dv);
+  HXM_REQUIRE(a->gate_mode == 0 || a->gate_mode == 1, "hxm_mlstm_chunkwise_fwd: bad gate_mode %d", a->gate_mode);
+  HXM_REQUIRE(a->io_dtype == HXM_F32 || a->io_dtype == HXM_BF16, "hxm_mlstm_chunkwise_fwd: io_dtype must be f32 or bf16");
+  HXM_REQUIRE(a->chunk == 64 || a->chunk == 128, "hxm_mlstm_chunkwise_fwd: chunk must be 64 or 128 (got %d)", a->chunk);
+  HXM_REQUIRE_SUPPORTED(a->dqk <= 512 && a->dv <= 512, "hxm_mlstm_chunkwise_fwd: dqk, dv <= 512 supported");
+  p.batch = a->batch; p.heads = a->heads; p.seqlen = a->seqlen; p.dqk = a->dqk; p.dv = a->dv;
+  p.chunk = a->chunk; p.gate_mode = a->gate_mode; p.io_dtype = a->io_dtype;
+  p.q = a->q; p.k = a->k; p.v = a->v; p.log_i = a->log_i; p.log_f = a->log_f; p.h = a->h;
+  for (int i = 0; i < 2; ++i) {
+    p.sq[i] = a->q_stride[i]; p.sk[i] = a->k_stride[i]; p.sv[i] = a->v_stride[i];
+    p.si[i] = a->i_stride[i]; p.sf[i] = a->f_stride[i]; p.sh[i] = a->h_stride[i];
+  }
+  p.C0 = a->C0; p.n0 = a->n0; p.m0 = a->m0; p.CT = a->CT; p.nT = a->nT; p.mT = a->mT;
+  p.workspace = a->workspace; p.workspace_bytes = a->workspace_bytes;
+  return HXM_OK;
+}
+
+static bool use_tc(const Params& p) {
+  return p.io_dtype == HXM_BF16 && p.gate_mode == 0 && hxm::mlstm::chunkwise_tc_workspace(p) != (size_t)-1;
+}
+
+extern "C" size_t hxm_mlstm_workspace_size(const hxm_mlstm_args* a) {
+  Params p{};
+  if (fill(a, p) != HXM_OK) return 0;
+  return use_tc(p) ? hxm::mlstm::chunkwise_tc_workspace(p) : 0;
+}
+
+extern "C" hxm_status hxm_mlstm_chunkwise_fwd(const hxm_mlstm_args* a, void* stream) {
+  hxm::clear_error();
+  Params p{};
+  hxm_status s = fill(a, p);
+  if (s != HXM_OK) return s;
+  if (p.batch == 0 || p.heads == 0) return HXM_OK;
+  HXM_REQUIRE(p.seqlen == 0 || (p.q && p.k && p.v && p.log_i && p.log_f && p.h),
+              "hxm_mlstm_chunkwise_fwd: NULL tensor pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_tc(p)) return hxm::mlstm::launch_chunkwise_tc(p, st);
+  return hxm::mlstm::launch_recurrent(p, st);
+}

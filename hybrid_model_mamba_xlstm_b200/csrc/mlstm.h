@@ -1,0 +1,44 @@
+// mlstm.h — shared parameter block of the mLSTM kernels (host + device).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/hxm.h"
+
+namespace hxm {
+namespace mlstm {
+
+struct Params {
+  int batch, heads, seqlen, dqk, dv, chunk, gate_mode;
+  hxm_dtype io_dtype;
+  const void* q;
+  int64_t sq[2];
+  const void* k;
+  int64_t sk[2];
+  const void* v;
+  int64_t sv[2];
+  const float* log_i;
+  int64_t si[2];
+  const float* log_f;
+  int64_t sf[2];
+  void* h;
+  int64_t sh[2];
+  const float* C0;
+  const float* n0;
+  const float* m0;
+  float* CT;
+  float* nT;
+  float* mT;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+// Exact step-by-step recurrence on CUDA cores (any gate mode / dtype / dims <= 512).
+hxm_status launch_recurrent(const Params& p, cudaStream_t st);
+// tcgen05 chunkwise kernel (bf16, per-head gates); returns HXM_EUNSUPPORTED for shapes it does not cover.
+hxm_status launch_chunkwise_tc(const Params& p, cudaStream_t st);
+size_t chunkwise_tc_workspace(const Params& p);
+
+}  // namespace mlstm
+}  // namespace hxm

@@ -1,0 +1,317 @@
+// scan_fast.cuh — selective-scan kernel for the dominant layout (sm_100a).
+//
+// Covers dstate <= 16 with u / delta / z / y time-major (unit time stride,
+// 16-byte aligned rows, i.e. (batch, dim, seqlen) memory) and B, C
+// time-major ((batch, dstate, seqlen) memory).  Every other layout runs the
+// generic kernel of scan_kernel.cuh.
+//
+// Per CTA: CH channels of one batch row.  Per tile of kT steps, cp.async
+// stages the u / delta / z rows and the raw bf16/fp32 B, C rows (double
+// buffered); one cooperative pass converts B, C to an fp32 [t][B0..15 C0..15]
+// table read with broadcast LDS.128.  Each thread runs one channel's 16
+// states in 8 packed fp32x2 registers (FFMA2/FMUL2), the powers
+// r^1..r^16 of r = exp(delta*A[0]) come from a depth-4 product tree when
+// A[d, n] = (n+1)*A[d, 0] (checked per warp on the device), otherwise one
+// exp per state.
+#pragma once
+
+#include "scan_kernel.cuh"
+
+namespace hxm {
+namespace scan {
+
+template <typename T, int CH, int kT>
+struct FastSmem {
+  static constexpr int kPad = 16 / sizeof(T);
+  static constexpr int kTP = kT + kPad;                        // io row pitch (elements)
+  static constexpr int kIoSlot = CH * kTP;                     // one tensor tile
+  static constexpr int kBcRaw = 32 * kTP;                      // raw B, C rows [32][kTP]
+  static constexpr size_t kStageBytes = sizeof(T) * (3 * kIoSlot + kBcRaw);
+  static constexpr size_t kBytes = 2 * kStageBytes + sizeof(float) * kT * 32;
+};
+
+HXM_DEV float2 f2(float a) { return make_float2(a, a); }
+
+// State update of one step.  h[q] holds states (2q, 2q+1).  `r` = exp(delta*A[0])
+// (POW) or delta (general path: exponents formed here).  Returns sum_n C_n h_n.
+template <bool ZOH, bool POW>
+HXM_DEV float fast_step(float r, float dl, float du, float u, const float* __restrict__ bc, float2 (&h)[8],
+                        const float* __restrict__ Arow) {
+  const float4* b4 = reinterpret_cast<const float4*>(bc);
+  const float4* c4 = reinterpret_cast<const float4*>(bc + 16);
+  float2 ya = make_float2(0.f, 0.f), yb = make_float2(0.f, 0.f);
+  if (POW) {
+    // r^1..r^16 by a depth-4 product tree
+    const float r2 = r * r;
+    const float r4 = r2 * r2;
+    const float r8 = r4 * r4;
+    float2 pw[8];
+    pw[0] = make_float2(r, r2);
+    pw[1] = make_float2(r2 * r, r4);
+    pw[2] = __fmul2_rn(f2(r4), pw[0]);
+    pw[3] = __fmul2_rn(f2(r4), pw[1]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) pw[4 + q] = __fmul2_rn(f2(r8), pw[q]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 bb = b4[q], cc = c4[q];
+      const float2 w0 = __fmul2_rn(f2(du), make_float2(bb.x, bb.y));
+      const float2 w1 = __fmul2_rn(f2(du), make_float2(bb.z, bb.w));
+      h[2 * q] = __ffma2_rn(pw[2 * q], h[2 * q], w0);
+      h[2 * q + 1] = __ffma2_rn(pw[2 * q + 1], h[2 * q + 1], w1);
+      ya = __ffma2_rn(make_float2(cc.x, cc.y), h[2 * q], ya);
+      yb = __ffma2_rn(make_float2(cc.z, cc.w), h[2 * q + 1], yb);
+    }
+  } else {
+    // general A: one exp per state; Arow = A[d, :] * log2(e) in shared memory
+    const float4* a4 = reinterpret_cast<const float4*>(Arow);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 bb = b4[q], cc = c4[q], aa = a4[q];
+      const float av[4] = {aa.x, aa.y, aa.z, aa.w};
+      const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+      float dA[4], bbar[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x = dl * av[j];  // delta*A*log2(e)
+        dA[j] = ex2_approx(x);
+        if (ZOH) {
+          // Bbar = (exp(dA)-1)/A * B, or delta*B when |delta*A| < 0.01
+          const float xa = x * kLn2;
+          bbar[j] = (fabsf(xa) < 0.01f) ? du * bv[j] : (dA[j] - 1.f) * (dl / xa) * bv[j] * u;
+        } else {
+          bbar[j] = du * bv[j];
+        }
+      }
+      h[2 * q] = __ffma2_rn(make_float2(dA[0], dA[1]), h[2 * q], make_float2(bbar[0], bbar[1]));
+      h[2 * q + 1] = __ffma2_rn(make_float2(dA[2], dA[3]), h[2 * q + 1], make_float2(bbar[2], bbar[3]));
+      ya = __ffma2_rn(make_float2(cc.x, cc.y), h[2 * q], ya);
+      yb = __ffma2_rn(make_float2(cc.z, cc.w), h[2 * q + 1], yb);
+    }
+  }
+  const float2 ys = __fadd2_rn(ya, yb);
+  return ys.x + ys.y;
+}
+
+template <typename T, int CH, int kT, bool POW, int ZMODE, bool SP, bool MASK>
+HXM_DEV void fast_tile(T* us, const T* ds, const T* zs, const float* __restrict__ bc, int tk, float2 (&h)[8],
+                       float a0l2, const float* Arow, float bias, float Dd, int tid) {
+  using S = FastSmem<T, CH, kT>;
+  T* urow = us + tid * S::kTP;
+  const T* drow = ds + tid * S::kTP;
+  const T* zrow = zs + tid * S::kTP;
+#pragma unroll 1
+  for (int tt = 0; tt < kT; tt += 8) {
+    float uv[8], dv[8], zv[8], yv[8];
+    read8<T, CH, kT>(urow, kTimeMaj, 0, tt, uv);
+    read8<T, CH, kT>(drow, kTimeMaj, 0, tt, dv);
+    if (ZMODE != 0) read8<T, CH, kT>(zrow, kTimeMaj, 0, tt, zv);
+    // phase A: the per-step scalar work of all 8 steps (independent, overlappable)
+    float dl[8], du[8], rr[8], gz[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float x = dv[j] + bias;
+      if (SP) x = softplus<false>(x);
+      if (MASK) x = (tt + j < tk) ? x : 0.f;  // steps past the end leave h unchanged
+      dl[j] = x;
+      du[j] = x * uv[j];
+      rr[j] = POW ? ex2_approx(x * a0l2) : x;
+      gz[j] = ZMODE == 2 ? zv[j] * sigmoid<false>(zv[j]) : (ZMODE == 1 ? zv[j] : 1.f);
+    }
+    // phase B: the recurrence (short dependency chain through h)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float yy = fast_step<false, POW>(rr[j], dl[j], du[j], uv[j], bc + (tt + j) * 32, h, Arow);
+      yv[j] = ZMODE == 0 ? fmaf(Dd, uv[j], yy) : fmaf(Dd, uv[j], yy) * gz[j];
+    }
+    write8<T, CH, kT>(urow, kTimeMaj, 0, tt, yv);
+  }
+}
+
+template <typename T, int CH, int kT, int ZMODE, bool SP>
+__global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
+  using S = FastSmem<T, CH, kT>;
+  constexpr int kE = 16 / sizeof(T);
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* bcf = reinterpret_cast<float*>(smem_raw + 2 * S::kStageBytes);  // [kT][32] fp32
+  __shared__ __align__(16) float Ash[CH * 16];                             // A[d, :] * log2(e)
+
+  const int tid = threadIdx.x;
+  const int b = blockIdx.y;
+  const int d0 = blockIdx.x * CH;
+  const int d = d0 + tid;
+  const bool dvalid = d < p.dim;
+  const int dc = dvalid ? d : 0;
+
+  bool pattern = true;
+  const float a0 = p.A[(int64_t)dc * p.sA[0]];
+  float2 h[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float hv[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int n = 2 * q + j;
+      const float a = n < p.dstate ? p.A[(int64_t)dc * p.sA[0] + (int64_t)n * p.sA[1]] : 0.f;
+      Ash[tid * 16 + n] = a * kLog2e;
+      if (n < p.dstate && a != a0 * (float)(n + 1)) pattern = false;
+      hv[j] = (p.h0 && dvalid && n < p.dstate) ? p.h0[((int64_t)b * p.dim + d) * p.dstate + n] : 0.f;
+    }
+    h[q] = make_float2(hv[0], hv[1]);
+  }
+  const bool use_pow = __all_sync(0xffffffffu, pattern);
+  const float a0l2 = a0 * kLog2e;
+  const float Dd = (p.D && dvalid) ? p.D[d] : 0.f;
+  const float bias = (p.bias && dvalid) ? p.bias[d] : 0.f;
+  const bool has_z = ZMODE != 0;
+
+  // per-thread global row pointers (time-major rows)
+  const T* ug = static_cast<const T*>(p.u) + b * p.su[0];
+  const T* dtg = static_cast<const T*>(p.dt) + b * p.sdt[0];
+  const T* zg = has_z ? static_cast<const T*>(p.z) + b * p.sz[0] : nullptr;
+  const T* Bg = static_cast<const T*>(p.B) + b * p.sB[0];
+  const T* Cg = static_cast<const T*>(p.C) + b * p.sC[0];
+  T* yg = static_cast<T*>(p.y) + b * p.sy[0];
+  const int ntiles = (p.seqlen + kT - 1) / kT;
+
+  auto stage_ptr = [&](int st) { return reinterpret_cast<T*>(smem_raw + st * S::kStageBytes); };
+  auto issue = [&](int k) {
+    T* base = stage_ptr(k & 1);
+    const int t0 = k * kT, tk = min(kT, p.seqlen - t0);
+    constexpr int kChunks = kT / kE;
+    // u, delta, z rows
+#pragma unroll 1
+    for (int which = 0; which < 3; ++which) {
+      if (which == 2 && !has_z) break;
+      const T* g = which == 0 ? ug : (which == 1 ? dtg : zg);
+      const int64_t sd = which == 0 ? p.su[2] : (which == 1 ? p.sdt[2] : p.sz[2]);
+      T* slot = base + which * S::kIoSlot;
+      for (int c = tid; c < CH * kChunks; c += CH) {
+        const int ch = c / kChunks, t = (c % kChunks) * kE;
+        const int dd = d0 + ch;
+        const int valid = (dd < p.dim) ? max(0, min(kE, tk - t)) : 0;
+        const T* src = valid > 0 ? g + (int64_t)dd * sd + t0 + t : g;
+        cp_async16(slot + ch * S::kTP + t, src, valid * (int)sizeof(T));
+      }
+    }
+    // raw B, C rows [2][16][kT]
+    T* raw = base + 3 * S::kIoSlot;
+    for (int c = tid; c < 2 * 16 * kChunks; c += CH) {
+      const int row = c / kChunks, t = (c % kChunks) * kE;
+      const int which = row / 16, n = row % 16;
+      const int valid = (n < p.dstate) ? max(0, min(kE, tk - t)) : 0;
+      const T* g = which ? Cg + (int64_t)n * p.sC[2] : Bg + (int64_t)n * p.sB[2];
+      cp_async16(raw + row * S::kTP + t, valid > 0 ? g + t0 + t : Bg, valid * (int)sizeof(T));
+    }
+    cp_async_commit();
+  };
+
+  issue(0);
+  for (int k = 0; k < ntiles; ++k) {
+    const int st = k & 1;
+    const int t0 = k * kT, tk = min(kT, p.seqlen - t0);
+    cp_async_wait<0>();
+    __syncthreads();  // tile k staged; previous tile's y stored and bc table consumed
+    if (k + 1 < ntiles) issue(k + 1);
+    // B, C rows -> fp32 [t][32] table: a thread reads 8 steps of one row with
+    // one 16-byte load (padded rows: conflict-free) and writes them down the
+    // column (lanes = 32 distinct columns: conflict-free).
+    {
+      const T* raw = stage_ptr(st) + 3 * S::kIoSlot;
+      for (int c = tid; c < 32 * (kT / 8); c += CH) {
+        const int col = c % 32, t8 = (c / 32) * 8;
+        float v[8];
+        read8<T, CH, kT>(raw + col * S::kTP, kTimeMaj, 0, t8, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) bcf[(t8 + j) * 32 + col] = v[j];
+      }
+    }
+    __syncthreads();
+    T* us = stage_ptr(st);
+    const T* ds = us + S::kIoSlot;
+    const T* zs = us + 2 * S::kIoSlot;
+    const float* Arow = Ash + tid * 16;
+    if (tk == kT) {
+      if (use_pow) fast_tile<T, CH, kT, true, ZMODE, SP, false>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
+      else fast_tile<T, CH, kT, false, ZMODE, SP, false>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
+    } else {
+      if (use_pow) fast_tile<T, CH, kT, true, ZMODE, SP, true>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
+      else fast_tile<T, CH, kT, false, ZMODE, SP, true>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
+    }
+    __syncthreads();
+    // y tile (in u's slot) -> global, 16-byte stores along each channel row
+    {
+      constexpr int kChunks = kT / kE;
+      for (int c = tid; c < CH * kChunks; c += CH) {
+        const int ch = c / kChunks, t = (c % kChunks) * kE;
+        const int dd = d0 + ch;
+        if (dd >= p.dim || t >= tk) continue;
+        const T* src = us + ch * S::kTP + t;
+        T* dst = yg + (int64_t)dd * p.sy[2] + t0 + t;
+        if (t + kE <= tk) *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        else
+          for (int j = 0; j < tk - t; ++j) dst[j] = src[j];
+      }
+    }
+  }
+
+  if (p.hT && dvalid) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (2 * q < p.dstate) p.hT[((int64_t)b * p.dim + d) * p.dstate + 2 * q] = h[q].x;
+      if (2 * q + 1 < p.dstate) p.hT[((int64_t)b * p.dim + d) * p.dstate + 2 * q + 1] = h[q].y;
+    }
+  }
+}
+
+template <typename T, int CH, int kT, int ZMODE, bool SP>
+hxm_status launch_fast(const Params& p, cudaStream_t stream) {
+  using S = FastSmem<T, CH, kT>;
+  const size_t smem = S::kBytes;
+  auto kern = scan_fast_kernel<T, CH, kT, ZMODE, SP>;
+  if (smem > 48 * 1024 - sizeof(float) * CH * 16)
+    HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((p.dim + CH - 1) / CH, p.batch);
+  kern<<<grid, CH, smem, stream>>>(p);
+  return check_launch("hxm_selective_scan_fwd (fast)");
+}
+
+// Can the fast kernel run this request?
+inline bool fast_ok(const Params& p, size_t esize) {
+  if (p.dstate > 16) return false;
+  if (p.mode_u != kTimeMaj || p.mode_dt != kTimeMaj || p.mode_y != kTimeMaj) return false;
+  if (p.z && p.mode_z != kTimeMaj) return false;
+  const int64_t e16 = 16 / (int64_t)esize;
+  auto tm = [&](const void* ptr, const int64_t* s) {
+    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && s[1] == 1 && s[0] % e16 == 0 && s[2] % e16 == 0;
+  };
+  return tm(p.B, p.sB) && tm(p.C, p.sC);
+}
+
+template <typename T, int CH>
+hxm_status pick_fast_modes(const Params& p, cudaStream_t stream) {
+  const int zm = p.z ? p.z_mode : 0;
+  if (p.softplus) {
+    if (zm == 2) return launch_fast<T, CH, 32, 2, true>(p, stream);
+    if (zm == 1) return launch_fast<T, CH, 32, 1, true>(p, stream);
+    return launch_fast<T, CH, 32, 0, true>(p, stream);
+  }
+  if (zm == 2) return launch_fast<T, CH, 32, 2, false>(p, stream);
+  if (zm == 1) return launch_fast<T, CH, 32, 1, false>(p, stream);
+  return launch_fast<T, CH, 32, 0, false>(p, stream);
+}
+
+template <typename T>
+hxm_status pick_fast(const Params& p, cudaStream_t stream, int num_sms) {
+  auto eff = [&](int ch) {
+    const double ctas = (double)((p.dim + ch - 1) / ch) * p.batch;
+    const double per_sm = ctas / num_sms;
+    return per_sm / std::ceil(per_sm) * ((double)p.dim / (((p.dim + ch - 1) / ch) * ch));
+  };
+  int ch = env_knob("HXM_SCAN_CH");
+  if (ch != 32 && ch != 64) ch = (eff(64) >= eff(32) - 0.02) ? 64 : 32;
+  return ch == 64 ? pick_fast_modes<T, 64>(p, stream) : pick_fast_modes<T, 32>(p, stream);
+}
+
+}  // namespace scan
+}  // namespace hxm

@@ -1,6 +1,6 @@
-// scan_inst_bf16_zoh.cu — instantiation of the selective-scan kernels
-// for __nv_bfloat16 I/O with zoh discretization (own translation unit so the
-// variants compile in parallel).
+// scan_inst_bf16_zoh.cu — instantiation of the selective-scan kernels for
+// bf16 I/O with zoh discretization (own translation unit so the variants
+// compile in parallel). 
 #include "scan_kernel.cuh"
 
 namespace hxm {

@@ -24,7 +24,6 @@
 namespace hxm {
 namespace scan {
 
-constexpr int kT = 32;  // timesteps per tile
 
 // Tensor I/O mode of u / delta / z / y:
 //   kGeneric  element loads with arbitrary strides, staged time-major
@@ -56,7 +55,7 @@ struct Params {
   int mode_u, mode_dt, mode_z, mode_y;
 };
 
-template <typename T, int CH>
+template <typename T, int CH, int kT>
 struct Smem {
   static constexpr int kPad = 16 / sizeof(T);  // 16-byte row padding (bank spread)
   static constexpr int kTP = kT + kPad;        // time-major row pitch (elements)
@@ -64,14 +63,14 @@ struct Smem {
 };
 
 // Element (ch, t) of a staging slot in its layout.
-template <typename T, int CH>
+template <typename T, int CH, int kT>
 HXM_DEV int slot_index(int mode, int ch, int t) {
-  return mode == kChanMaj ? t * CH + ch : ch * Smem<T, CH>::kTP + t;
+  return mode == kChanMaj ? t * CH + ch : ch * Smem<T, CH, kT>::kTP + t;
 }
 
 // Issue the loads of one u/delta/z tile into a staging slot.  Async modes
 // use cp.async (caller commits); the generic mode loads synchronously.
-template <typename T, int CH>
+template <typename T, int CH, int kT>
 HXM_DEV void load_io_tile(T* slot, int mode, const T* __restrict__ g, const int64_t* s, int b, int d0, int t0,
                           int tk, int dim) {
   const int tid = threadIdx.x;
@@ -81,7 +80,7 @@ HXM_DEV void load_io_tile(T* slot, int mode, const T* __restrict__ g, const int6
     for (int c = tid; c < CH * kChunks; c += CH) {
       const int ch = c / kChunks, part = c % kChunks;
       const int d = d0 + ch, t = part * kE;
-      T* dst = slot + ch * Smem<T, CH>::kTP + t;
+      T* dst = slot + ch * Smem<T, CH, kT>::kTP + t;
       int valid = (d < dim) ? min(kE, tk - t) : 0;
       valid = max(valid, 0);
       const T* src = g + b * s[0] + (int64_t)(t0 + t) * s[1] + (int64_t)(d < dim ? d : 0) * s[2];
@@ -107,13 +106,13 @@ HXM_DEV void load_io_tile(T* slot, int mode, const T* __restrict__ g, const int6
       const int d = d0 + ch;
       T v = from_f32<T>(0.f);
       if (d < dim && t < tk) v = g[b * s[0] + (int64_t)(t0 + t) * s[1] + (int64_t)d * s[2]];
-      slot[ch * Smem<T, CH>::kTP + t] = v;
+      slot[ch * Smem<T, CH, kT>::kTP + t] = v;
     }
   }
 }
 
 // Store the y tile (held in u's staging slot, layout `smode`).
-template <typename T, int CH>
+template <typename T, int CH, int kT>
 HXM_DEV void store_y_tile(const T* slot, int smode, int ymode, T* __restrict__ g, const int64_t* s, int b, int d0,
                           int t0, int tk, int dim) {
   const int tid = threadIdx.x;
@@ -124,7 +123,7 @@ HXM_DEV void store_y_tile(const T* slot, int smode, int ymode, T* __restrict__ g
       const int ch = c / kChunks, t = (c % kChunks) * kE;
       const int d = d0 + ch;
       if (d >= dim || t >= tk) continue;
-      const T* src = slot + ch * Smem<T, CH>::kTP + t;
+      const T* src = slot + ch * Smem<T, CH, kT>::kTP + t;
       T* dst = g + b * s[0] + (int64_t)(t0 + t) * s[1] + (int64_t)d * s[2];
       if (t + kE <= tk) {
         *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
@@ -153,16 +152,16 @@ HXM_DEV void store_y_tile(const T* slot, int smode, int ymode, T* __restrict__ g
       const int t = tfast ? e % kT : e / CH;
       const int d = d0 + ch;
       if (d < dim && t < tk)
-        g[b * s[0] + (int64_t)(t0 + t) * s[1] + (int64_t)d * s[2]] = slot[slot_index<T, CH>(smode, ch, t)];
+        g[b * s[0] + (int64_t)(t0 + t) * s[1] + (int64_t)d * s[2]] = slot[slot_index<T, CH, kT>(smode, ch, t)];
     }
   }
 }
 
 // Read 8 consecutive timesteps (t0..t0+7) of channel `ch` from a slot.
-template <typename T, int CH>
+template <typename T, int CH, int kT>
 HXM_DEV void read8(const T* slot, int mode, int ch, int t0, float (&v)[8]) {
   if (mode != kChanMaj) {
-    const T* p = slot + ch * Smem<T, CH>::kTP + t0;
+    const T* p = slot + ch * Smem<T, CH, kT>::kTP + t0;
     if constexpr (sizeof(T) == 2) {
       uint4 w = *reinterpret_cast<const uint4*>(p);
       const T* e = reinterpret_cast<const T*>(&w);
@@ -180,15 +179,15 @@ HXM_DEV void read8(const T* slot, int mode, int ch, int t0, float (&v)[8]) {
   }
 }
 
-template <typename T, int CH>
+template <typename T, int CH, int kT>
 HXM_DEV void write8(T* slot, int mode, int ch, int t0, const float (&v)[8]) {
   if (mode != kChanMaj) {
-    T* p = slot + ch * Smem<T, CH>::kTP + t0;
+    T* p = slot + ch * Smem<T, CH, kT>::kTP + t0;
     if constexpr (sizeof(T) == 2) {
       uint4 w;
-      T* e = reinterpret_cast<T*>(&w);
+      uint32_t* e = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) e[j] = from_f32<T>(v[j]);
+      for (int j = 0; j < 4; ++j) e[j] = pack2<T>(v[2 * j], v[2 * j + 1]);
       *reinterpret_cast<uint4*>(p) = w;
     } else {
       *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
@@ -201,7 +200,7 @@ HXM_DEV void write8(T* slot, int mode, int ch, int t0, const float (&v)[8]) {
 }
 
 // Per-thread register prefetch of one B/C tile (kT x NS each), converted to fp32.
-template <typename T, int NS, int CH>
+template <typename T, int NS, int CH, int kT>
 struct BCPrefetch {
   static constexpr int kElems = 2 * kT * NS;
   static constexpr int kPer = (kElems + CH - 1) / CH;
@@ -298,9 +297,58 @@ HXM_DEV float ssm_step(float dl, float u, const float* __restrict__ bc, float (&
   return y0 + y1;
 }
 
-template <typename T, int NS, int CH, bool ACC, bool ZOH>
+// One staged tile of kT steps for one channel.  Branch-free step bodies:
+// steps past the end of the sequence get delta = 0 (h unchanged, y unused).
+template <typename T, int NS, int CH, int kT, bool ACC, bool ZOH, bool POW>
+HXM_DEV void compute_tile(T* us, const T* ds, const T* zs, int mode_u, int mode_dt, int mode_z, bool has_z,
+                          const float* __restrict__ bc, int tk, float (&h)[NS], const float (&Al2)[NS],
+                          const float (&Aval)[NS], const float (&invA)[NS], float bias, float Dd, bool sp,
+                          int z_mode, int tid) {
+  const bool vec = mode_u != kChanMaj && mode_dt != kChanMaj && (!has_z || mode_z != kChanMaj);
+  if (vec) {
+#pragma unroll 1
+    for (int tt = 0; tt < kT; tt += 8) {
+      float uv[8], dv[8], zv[8], yv[8];
+      read8<T, CH, kT>(us, kTimeMaj, tid, tt, uv);
+      read8<T, CH, kT>(ds, kTimeMaj, tid, tt, dv);
+      if (has_z) {
+        read8<T, CH, kT>(zs, kTimeMaj, tid, tt, zv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) zv[j] = 1.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float dl = dv[j] + bias;
+        dl = sp ? softplus<ACC>(dl) : dl;
+        dl = (tt + j < tk) ? dl : 0.f;
+        float yy = ssm_step<ACC, ZOH, POW, NS>(dl, uv[j], bc + (tt + j) * 2 * NS, h, Al2, Aval, invA);
+        yy = fmaf(Dd, uv[j], yy);
+        const float g = (z_mode == 2) ? zv[j] * sigmoid<ACC>(zv[j]) : (z_mode == 1 ? zv[j] : 1.f);
+        yv[j] = yy * g;
+      }
+      write8<T, CH, kT>(us, kTimeMaj, tid, tt, yv);
+    }
+  } else {
+#pragma unroll 1
+    for (int t = 0; t < tk; ++t) {
+      const float u = to_f32<T>(us[slot_index<T, CH, kT>(mode_u, tid, t)]);
+      float dl = to_f32<T>(ds[slot_index<T, CH, kT>(mode_dt, tid, t)]) + bias;
+      dl = sp ? softplus<ACC>(dl) : dl;
+      float yy = ssm_step<ACC, ZOH, POW, NS>(dl, u, bc + t * 2 * NS, h, Al2, Aval, invA);
+      yy = fmaf(Dd, u, yy);
+      if (has_z) {
+        const float z = to_f32<T>(zs[slot_index<T, CH, kT>(mode_z, tid, t)]);
+        yy *= (z_mode == 2) ? z * sigmoid<ACC>(z) : z;
+      }
+      us[slot_index<T, CH, kT>(mode_u, tid, t)] = from_f32<T>(yy);
+    }
+  }
+}
+
+template <typename T, int NS, int CH, int kT, bool ACC, bool ZOH>
 __global__ void __launch_bounds__(CH) scan_fwd_kernel(const Params p) {
-  using S = Smem<T, CH>;
+  using S = Smem<T, CH, kT>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* io = reinterpret_cast<T*>(smem_raw);                                   // [2][3][kSlot]
   float* bcs = reinterpret_cast<float*>(smem_raw + sizeof(T) * 2 * 3 * S::kSlot);  // [2][kT][2NS]
@@ -326,7 +374,7 @@ __global__ void __launch_bounds__(CH) scan_fwd_kernel(const Params p) {
     h[n] = (p.h0 && dvalid && n < p.dstate) ? p.h0[((int64_t)b * p.dim + d) * p.dstate + n] : 0.f;
   }
   // exp(delta*A[n]) as powers of r = exp(delta*A[0]) — fast path only, decided per warp
-  const bool use_pow = (!ACC && !ZOH) && __all_sync(0xffffffffu, pattern);
+  const bool use_pow = __all_sync(0xffffffffu, pattern);
   const float Dd = (p.D && dvalid) ? p.D[d] : 0.f;
   const float bias = (p.bias && dvalid) ? p.bias[d] : 0.f;
 
@@ -340,13 +388,13 @@ __global__ void __launch_bounds__(CH) scan_fwd_kernel(const Params p) {
   auto slot = [&](int stage, int which) { return io + (stage * 3 + which) * S::kSlot; };
   auto issue = [&](int k) {
     const int st = k & 1, t0 = k * kT, tk = min(kT, p.seqlen - t0);
-    load_io_tile<T, CH>(slot(st, 0), p.mode_u, ug, p.su, b, d0, t0, tk, p.dim);
-    load_io_tile<T, CH>(slot(st, 1), p.mode_dt, dtg, p.sdt, b, d0, t0, tk, p.dim);
-    if (zg) load_io_tile<T, CH>(slot(st, 2), mode_z, zg, p.sz, b, d0, t0, tk, p.dim);
+    load_io_tile<T, CH, kT>(slot(st, 0), p.mode_u, ug, p.su, b, d0, t0, tk, p.dim);
+    load_io_tile<T, CH, kT>(slot(st, 1), p.mode_dt, dtg, p.sdt, b, d0, t0, tk, p.dim);
+    if (zg) load_io_tile<T, CH, kT>(slot(st, 2), mode_z, zg, p.sz, b, d0, t0, tk, p.dim);
     cp_async_commit();
   };
 
-  BCPrefetch<T, NS, CH> pre;
+  BCPrefetch<T, NS, CH, kT> pre;
   pre.load(p, b, 0, min(kT, p.seqlen));
   pre.store(bcs, p);
   issue(0);
@@ -367,32 +415,22 @@ __global__ void __launch_bounds__(CH) scan_fwd_kernel(const Params p) {
     const T* ds = slot(st, 1);
     const T* zs = slot(st, 2);
     const float* bc = bcs + st * kT * 2 * NS;
-    for (int tt = 0; tt < tk; tt += 8) {
-      float uv[8], dv[8], zv[8], yv[8];
-      read8<T, CH>(us, p.mode_u, tid, tt, uv);
-      read8<T, CH>(ds, p.mode_dt, tid, tt, dv);
-      if (zg) read8<T, CH>(zs, mode_z, tid, tt, zv);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (tt + j < tk) {
-          float dl = dv[j] + bias;
-          if (p.softplus) dl = softplus<ACC>(dl);
-          const float* row = bc + (tt + j) * 2 * NS;
-          float yy = use_pow ? ssm_step<ACC, ZOH, true, NS>(dl, uv[j], row, h, Al2, Aval, invA)
-                             : ssm_step<ACC, ZOH, false, NS>(dl, uv[j], row, h, Al2, Aval, invA);
-          yy = fmaf(Dd, uv[j], yy);
-          if (p.z_mode == 1) yy *= zv[j];
-          else if (p.z_mode == 2) yy *= zv[j] * sigmoid<ACC>(zv[j]);
-          yv[j] = yy;
-        } else {
-          yv[j] = 0.f;
-        }
-      }
-      write8<T, CH>(us, p.mode_u, tid, tt, yv);
+    const bool has_z = zg != nullptr;
+    const bool sp = p.softplus != 0;
+    if constexpr (!ACC && !ZOH) {
+      if (use_pow)
+        compute_tile<T, NS, CH, kT, ACC, ZOH, true>(us, ds, zs, p.mode_u, p.mode_dt, mode_z, has_z, bc, tk, h, Al2, Aval,
+                                                invA, bias, Dd, sp, p.z_mode, tid);
+      else
+        compute_tile<T, NS, CH, kT, ACC, ZOH, false>(us, ds, zs, p.mode_u, p.mode_dt, mode_z, has_z, bc, tk, h, Al2,
+                                                 Aval, invA, bias, Dd, sp, p.z_mode, tid);
+    } else {
+      compute_tile<T, NS, CH, kT, ACC, ZOH, false>(us, ds, zs, p.mode_u, p.mode_dt, mode_z, has_z, bc, tk, h, Al2, Aval,
+                                               invA, bias, Dd, sp, p.z_mode, tid);
     }
     if (k + 1 < ntiles) pre.store(bcs + (st ^ 1) * kT * 2 * NS, p);
     __syncthreads();
-    store_y_tile<T, CH>(us, p.mode_u, p.mode_y, yg, p.sy, b, d0, t0, tk, p.dim);
+    store_y_tile<T, CH, kT>(us, p.mode_u, p.mode_y, yg, p.sy, b, d0, t0, tk, p.dim);
     __syncthreads();
   }
 
@@ -403,16 +441,20 @@ __global__ void __launch_bounds__(CH) scan_fwd_kernel(const Params p) {
   }
 }
 
-template <typename T, int NS, int CH, bool ACC, bool ZOH>
+template <typename T, int NS, int CH, int kT, bool ACC, bool ZOH>
 hxm_status launch(const Params& p, cudaStream_t stream) {
-  using S = Smem<T, CH>;
+  using S = Smem<T, CH, kT>;
   const size_t smem = sizeof(T) * 2 * 3 * S::kSlot + sizeof(float) * 2 * kT * 2 * NS;
-  auto kern = scan_fwd_kernel<T, NS, CH, ACC, ZOH>;
+  auto kern = scan_fwd_kernel<T, NS, CH, kT, ACC, ZOH>;
   if (smem > 48 * 1024) HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dim + CH - 1) / CH, p.batch);
   kern<<<grid, CH, smem, stream>>>(p);
   return check_launch("hxm_selective_scan_fwd");
 }
+
+// Launch-shape tuning knobs: HXM_SCAN_CH = 32|64 channels per CTA,
+// HXM_SCAN_T = 32|64 timesteps per staged tile.  Unset = automatic choice.
+int env_knob(const char* name);
 
 template <typename T, int NS, bool ACC, bool ZOH>
 hxm_status pick_ch(const Params& p, cudaStream_t stream, int num_sms) {
@@ -422,8 +464,15 @@ hxm_status pick_ch(const Params& p, cudaStream_t stream, int num_sms) {
     const double per_sm = ctas / num_sms;
     return per_sm / std::ceil(per_sm) * ((double)p.dim / (((p.dim + ch - 1) / ch) * ch));
   };
-  if (eff(64) >= eff(32) - 0.02) return launch<T, NS, 64, ACC, ZOH>(p, stream);
-  return launch<T, NS, 32, ACC, ZOH>(p, stream);
+  int ch = env_knob("HXM_SCAN_CH");
+  if (ch != 32 && ch != 64) ch = (eff(64) >= eff(32) - 0.02) ? 64 : 32;
+  int tt = env_knob("HXM_SCAN_T");
+  if (tt != 32 && tt != 64) tt = 32;
+  if constexpr (NS <= 16) {
+    if (tt == 64)
+      return ch == 64 ? launch<T, NS, 64, 64, ACC, ZOH>(p, stream) : launch<T, NS, 32, 64, ACC, ZOH>(p, stream);
+  }
+  return ch == 64 ? launch<T, NS, 64, 32, ACC, ZOH>(p, stream) : launch<T, NS, 32, 32, ACC, ZOH>(p, stream);
 }
 
 template <typename T, bool ACC, bool ZOH>
