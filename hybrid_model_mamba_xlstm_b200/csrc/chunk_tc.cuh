@@ -1,0 +1,539 @@
+// chunk_tc.cuh — tcgen05 chunkwise linear recurrence with a per-head scalar
+// decay: the chunkwise mLSTM ("TFLA", per-head gates) and the Mamba-2 SSD
+// chunked scan share this kernel.
+//
+// Per (batch, head, 64-wide value tile) one CTA walks the sequence in chunks
+// of 128 steps.  State S (DK x 64, fp32) lives in TMEM; per chunk
+//   b_t = cumsum(log f), u_s = log i_s - b_s, M_t / m the stabilizers:
+//   S    = Q K^T                                   (tcgen05, M=N=128)
+//   P    = causal(S) * exp(b_t + u_s - M_t)         (threads, bf16 -> smem)
+//   Hint = Q . Ssnap     Hintra = P . V            (tcgen05, N=64)
+//   qn   = Q . n_snap                              (tcgen05, N=16; mLSTM only)
+//   S    = rho * S + (K * kscale)^T V, n likewise   (TMEM rescale + tcgen05)
+//   out_t = (sc_t Hint + Hintra) / max(sc_t qn + rowsum P, e^-M_t)   (mLSTM)
+//   out_t = e^(b_t) Hint + Hintra + D x_t                              (SSD)
+// All exponents are <= 0, so nothing overflows for any gate values; the
+// algebra is the reference recurrence (tfla_interface.py:113-137, and the
+// Euler scan of scan_interface.py:132-150 for SSD) regrouped by chunk.
+//
+// Operands arrive by TMA (128B swizzle) into shared memory; the tensor-core
+// operands written by threads (P, the bf16 state snapshot, n) use the same
+// swizzled layouts.  One elected thread issues TMA and MMA; all 4 warps do
+// the element-wise work (warp w owns TMEM lanes 32w..32w+31).
+#pragma once
+
+#include "common.cuh"
+#include "tc_sm100.cuh"
+
+namespace hxm {
+namespace chunk {
+
+constexpr int kC = 128;      // chunk length (TMEM lanes / MMA M)
+constexpr int kDV = 64;      // value columns per CTA
+constexpr int kThreads = 128;
+constexpr int kPanel = 16384;  // one 128-row x 128-byte swizzled panel
+
+enum Mode : int { kMlstm = 0, kSsd = 1 };
+
+struct Params {
+  int batch, heads, seqlen, dv;
+  // per-step gates, element strides (b, h, t)
+  const float* g0;  // mLSTM: log input gate;  SSD: raw dt
+  int64_t sg0[3];
+  const float* g1;  // mLSTM: log forget gate; SSD: unused
+  int64_t sg1[3];
+  const float* A;        // SSD: (heads)
+  const float* dt_bias;  // SSD: (heads) or null
+  int dt_softplus;
+  const float* Dskip;    // SSD: (heads) or null
+  const __nv_bfloat16* x;  // SSD: x for the D skip, element strides (b, h, t)
+  int64_t sx[3];
+  __nv_bfloat16* out;    // out[b,h,t,e] element strides (b, h, t), unit e
+  int64_t so[3];
+  const float* C0;  // (b, h, DK, dv) or SSD (b, h, dv, DK) when state_t
+  const float* n0;  // (b, h, DK)
+  const float* m0;  // (b, h)
+  float* CT;
+  float* nT;
+  float* mT;
+  int state_t;  // state stored transposed (SSD: (b, h, p, n))
+  int* error_flag;
+};
+
+template <int DK>
+struct Layout {
+  static constexpr int kNB = DK / 128;         // 128-row TMEM blocks of the state
+  static constexpr int kQ = 0;                  // DK/64 panels
+  static constexpr int kK = kQ + DK / 64 * kPanel;
+  static constexpr int kV = kK + DK / 64 * kPanel;
+  static constexpr int kP = kV + kPanel;        // 2 panels
+  static constexpr int kSnap = kP + 2 * kPanel; // DK rows x 128 B (MN-major, one N panel)
+  static constexpr int kN = kSnap + DK * 128;   // n snapshot, K-major [16][DK]: DK/64 panels of 2 KB
+  static constexpr int kOnes = kN + DK / 64 * 2048;  // K-major [16][128]: 2 panels of 2 KB
+  static constexpr int kMisc = kOnes + 2 * 2048;
+  // misc: row vectors and barriers
+  static constexpr int kRowB = kMisc;                 // float[128] b_t * log2e
+  static constexpr int kRowU = kRowB + 512;           // float[128] u_s * log2e
+  static constexpr int kRowM = kRowU + 512;           // float[128] M_t * log2e
+  static constexpr int kRowK = kRowM + 512;           // float[128] kscale_s
+  static constexpr int kRed = kRowK + 512;            // float[64] reductions
+  static constexpr int kBar = kRed + 256;             // 2 x uint64
+  static constexpr int kTmemSlot = kBar + 16;
+  static constexpr int kAbort = kTmemSlot + 4;
+  static constexpr int kBytes = kAbort + 12;
+  // TMEM columns
+  static constexpr int tS = 0, tHint = 128, tHintra = 192, tAcc = 256, tQN = 384, tAccN = 416;
+  static_assert(tAcc + 64 * kNB <= tQN, "TMEM layout");
+  static_assert(tAccN + 32 * kNB <= 512, "TMEM layout");
+};
+
+// ---- block-wide scans over the 128 rows (thread t owns row t) -------------
+HXM_DEV float block_incl_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  if (lane == 31) red[w] = v;
+  __syncthreads();
+  float pre = 0.f;
+  for (int i = 0; i < w; ++i) pre += red[i];
+  __syncthreads();
+  return v + pre;
+}
+HXM_DEV float block_incl_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v = fmaxf(v, n);
+  }
+  if (lane == 31) red[w] = v;
+  __syncthreads();
+  float pre = -INFINITY;
+  for (int i = 0; i < w; ++i) pre = fmaxf(pre, red[i]);
+  __syncthreads();
+  return fmaxf(v, pre);
+}
+HXM_DEV float bcast_from(float v, int src, float* red) {
+  if (threadIdx.x == src) red[8] = v;
+  __syncthreads();
+  const float r = red[8];
+  __syncthreads();
+  return r;
+}
+
+template <int DK, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using Lt = Layout<DK>;
+  constexpr bool kNorm = MODE == kMlstm;
+  constexpr int kNP = DK / 64;  // Q/K panels
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte alignment for the swizzled panels
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  float* rowB = reinterpret_cast<float*>(sm + Lt::kRowB);
+  float* rowU = reinterpret_cast<float*>(sm + Lt::kRowU);
+  float* rowM = reinterpret_cast<float*>(sm + Lt::kRowM);
+  float* rowK = reinterpret_cast<float*>(sm + Lt::kRowK);
+  float* red = reinterpret_cast<float*>(sm + Lt::kRed);
+  uint64_t* bar_load = reinterpret_cast<uint64_t*>(sm + Lt::kBar);
+  uint64_t* bar_mma = bar_load + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Lt::kTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + Lt::kAbort);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int e0 = blockIdx.x * kDV;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int bh = b * p.heads + h;
+  const int nchunks = (p.seqlen + kC - 1) / kC;
+  const uint32_t sbase = smem_u32(sm);
+
+  if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
+  if (tid == 0) {
+    tc::mbar_init(bar_load, 1);
+    tc::mbar_init(bar_mma, 1);
+    tc::fence_mbar_init();
+    *abort_flag = 0;
+    tc::prefetch_tmap(&tmQ);
+    tc::prefetch_tmap(&tmK);
+    tc::prefetch_tmap(&tmV);
+  }
+  // ones operand (K-major [16][128]: row 0 = 1) and the n snapshot ([16][DK]: zero)
+  {
+    uint4* z = reinterpret_cast<uint4*>(sm + Lt::kN);
+    for (int i = tid; i < (DK / 64 * 2048 + 2 * 2048) / 16; i += kThreads) z[i] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    __nv_bfloat16* ones = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kOnes);
+    if (tid < 128) {
+      const int panel = tid / 64, col = tid % 64;
+      ones[(panel * 2048 + tc::sw128_offset(0, col)) / 2] = __float2bfloat16_rn(1.f);
+    }
+  }
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tm = *tmem_slot;
+
+  // ---- initial state -> TMEM (fp32) ----------------------------------------
+  float m_prev = (kNorm && p.m0) ? p.m0[bh] : 0.f;
+#pragma unroll 1
+  for (int blk = 0; blk < Lt::kNB; ++blk) {
+    const int row = blk * 128 + warp * 32 + lane;  // state row (dk index)
+#pragma unroll 1
+    for (int c0 = 0; c0 < kDV; c0 += 32) {
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = e0 + c0 + j;
+        float x = 0.f;
+        if (p.C0 && col < p.dv)
+          x = p.state_t ? p.C0[((int64_t)bh * p.dv + col) * DK + row] : p.C0[((int64_t)bh * DK + row) * p.dv + col];
+        v[j] = x;
+      }
+      tc::tmem_st32(tc::taddr(tm, warp * 32, Lt::tAcc + blk * 64 + c0), v);
+    }
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    if (kNorm && p.n0) v[0] = p.n0[(int64_t)bh * DK + row];
+    tc::tmem_st32(tc::taddr(tm, warp * 32, Lt::tAccN + blk * 32), v);
+  }
+  tc::tmem_wait_st();
+
+  // state (TMEM fp32) -> bf16 snapshots in shared memory
+  auto snapshot = [&]() {
+#pragma unroll 1
+    for (int blk = 0; blk < Lt::kNB; ++blk) {
+      const int row = blk * 128 + warp * 32 + lane;
+      unsigned char* srow = sm + Lt::kSnap;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kDV; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tAcc + blk * 64 + c0), v);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
+          w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
+          w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
+          w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
+          *reinterpret_cast<uint4*>(srow + tc::sw128_offset(row, c0 + 8 * q)) = w;
+        }
+      }
+      if (kNorm) {
+        float v[32];
+        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tAccN + blk * 32), v);
+        tc::tmem_wait_ld();
+        __nv_bfloat16* nb = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kN + (row / 64) * 2048 + tc::sw128_offset(0, row % 64));
+        *nb = __float2bfloat16_rn(v[0]);
+      }
+    }
+  };
+  snapshot();
+  tc::fence_async_smem();
+  tc::tc_fence_before();
+  __syncthreads();
+
+  constexpr uint32_t kLoadBytes = (2 * kNP + 1) * kPanel;
+  auto issue_load = [&](int c) {
+    tc::mbar_expect_tx(bar_load, kLoadBytes);
+    const int t0 = c * kC;
+    const int hq = (MODE == kSsd) ? 0 : h;
+#pragma unroll 1
+    for (int pnl = 0; pnl < kNP; ++pnl) {
+      tc::tma_load_4d(sm + Lt::kQ + pnl * kPanel, &tmQ, bar_load, pnl * 64, t0, hq, b);
+      tc::tma_load_4d(sm + Lt::kK + pnl * kPanel, &tmK, bar_load, pnl * 64, t0, hq, b);
+    }
+    tc::tma_load_4d(sm + Lt::kV, &tmV, bar_load, e0, t0, h, b);
+  };
+  if (tid == 0) issue_load(0);
+
+  constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, false);
+  constexpr uint32_t idH = tc::idesc_bf16(128, kDV, false, true);
+  constexpr uint32_t idQN = tc::idesc_bf16(128, 16, false, false);
+  constexpr uint32_t idAcc = tc::idesc_bf16(128, kDV, true, true);
+  constexpr uint32_t idAccN = tc::idesc_bf16(128, 16, true, false);
+  const float A_h = (MODE == kSsd) ? p.A[h] : 0.f;
+  const float dtb = (MODE == kSsd && p.dt_bias) ? p.dt_bias[h] : 0.f;
+  const float Dh = (MODE == kSsd && p.Dskip) ? p.Dskip[h] : 0.f;
+
+  int bad = 0;
+  uint32_t mma_uses = 0;
+#pragma unroll 1
+  for (int c = 0; c < nchunks; ++c) {
+    const int t0 = c * kC;
+    if (!tc::mbar_wait(bar_load, c & 1, abort_flag)) bad = 1;
+    if (__syncthreads_or(bad)) { bad = 1; break; }
+    // ---- S = Q K^T --------------------------------------------------------
+    if (tid == 0) {
+      tc::tc_fence_after();
+#pragma unroll 1
+      for (int ks = 0; ks < DK / 16; ++ks) {
+        const uint32_t off = (ks / 4) * kPanel + (ks % 4) * 32;
+        tc::mma_bf16(tm + Lt::tS, tc::sdesc_sw128(sbase + Lt::kQ + off, 16, 1024),
+                     tc::sdesc_sw128(sbase + Lt::kK + off, 16, 1024), idS, ks > 0);
+      }
+      tc::mma_commit(bar_mma);
+    }
+    // ---- gates (overlaps the MMA) ------------------------------------------
+    const int tg = t0 + tid;
+    const bool valid = tg < p.seqlen;
+    float li, lf;
+    if (MODE == kMlstm) {
+      li = valid ? p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tg * p.sg0[2]] : -INFINITY;
+      lf = valid ? p.g1[b * p.sg1[0] + h * p.sg1[1] + (int64_t)tg * p.sg1[2]] : 0.f;
+    } else {
+      float dtv = valid ? p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tg * p.sg0[2]] + dtb : 0.f;
+      if (p.dt_softplus) dtv = (dtv > 20.f) ? dtv : log1pf(__expf(dtv));
+      li = (valid && dtv > 0.f) ? __logf(dtv) : -INFINITY;
+      lf = valid ? dtv * A_h : 0.f;
+    }
+    const float bt = block_incl_sum(lf, red);
+    const float g = bcast_from(bt, kC - 1, red);
+    const float us = li - bt;
+    float Mt, m_new;
+    if (kNorm) {
+      const float pm = block_incl_max(us, red);
+      const float pmax = bcast_from(pm, kC - 1, red);
+      Mt = bt + fmaxf(m_prev, pm);
+      m_new = g + fmaxf(m_prev, pmax);
+    } else {
+      Mt = 0.f;
+      m_new = 0.f;
+    }
+    const float rho = __expf(g + m_prev - m_new);
+    rowB[tid] = bt * kLog2e;
+    rowU[tid] = us * kLog2e;
+    rowM[tid] = Mt * kLog2e;
+    rowK[tid] = __expf(g + us - m_new);
+    __syncthreads();
+    // ---- wait S; P = causal(S) * exp(b_t + u_s - M_t) -> smem (bf16) ----------
+    if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
+    ++mma_uses;
+    tc::tc_fence_after();
+    float den_intra = 0.f;
+    {
+      const float bm = rowB[tid] - rowM[tid];
+#pragma unroll 1
+      for (int s0 = 0; s0 < kC; s0 += 32) {
+        float v[32];
+        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tS + s0), v);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int s = s0 + j;
+          const float w = ex2_approx(bm + rowU[s]);
+          const float pv = (s <= tid) ? v[j] * w : 0.f;
+          v[j] = pv;
+          den_intra += pv;
+        }
+        unsigned char* prow = sm + Lt::kP + (s0 / 64) * kPanel;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
+          w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
+          w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
+          w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
+          *reinterpret_cast<uint4*>(prow + tc::sw128_offset(tid, (s0 % 64) + 8 * q)) = w;
+        }
+      }
+    }
+    // ---- K rows *= kscale (row s = this thread) ------------------------------
+    {
+      const float ks = rowK[tid];
+#pragma unroll 1
+      for (int pnl = 0; pnl < kNP; ++pnl) {
+        unsigned char* krow = sm + Lt::kK + pnl * kPanel + tid * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint4* ptr = reinterpret_cast<uint4*>(krow + q * 16);
+          uint4 w = *ptr;
+          uint32_t* e = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&e[j]);
+            float2 f = __bfloat1622float2(x);
+            e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+          }
+          *ptr = w;
+        }
+      }
+    }
+    // ---- state *= rho (TMEM read-modify-write) -------------------------------
+    if (rho != 1.f) {
+#pragma unroll 1
+      for (int blk = 0; blk < Lt::kNB; ++blk) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < kDV; c0 += 32) {
+          float v[32];
+          const uint32_t a = tc::taddr(tm, warp * 32, Lt::tAcc + blk * 64 + c0);
+          tc::tmem_ld32(a, v);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= rho;
+          tc::tmem_st32(a, v);
+        }
+        if (kNorm) {
+          float v[32];
+          const uint32_t a = tc::taddr(tm, warp * 32, Lt::tAccN + blk * 32);
+          tc::tmem_ld32(a, v);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= rho;
+          tc::tmem_st32(a, v);
+        }
+      }
+      tc::tmem_wait_st();
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    if (__syncthreads_or(bad)) { bad = 1; break; }
+    // ---- Hint = Q.Snap, Hintra = P.V, qn = Q.n, state += K~^T V, n += K~^T 1 ---
+    if (tid == 0) {
+      tc::tc_fence_after();
+#pragma unroll 1
+      for (int ks = 0; ks < DK / 16; ++ks) {
+        const uint32_t qoff = (ks / 4) * kPanel + (ks % 4) * 32;
+        const uint64_t ad = tc::sdesc_sw128(sbase + Lt::kQ + qoff, 16, 1024);
+        tc::mma_bf16(tm + Lt::tHint, ad, tc::sdesc_sw128(sbase + Lt::kSnap + ks * 2048, kPanel, 1024), idH, ks > 0);
+        if (kNorm)
+          tc::mma_bf16(tm + Lt::tQN, ad,
+                       tc::sdesc_sw128(sbase + Lt::kN + (ks / 4) * 2048 + (ks % 4) * 32, 16, 1024), idQN, ks > 0);
+      }
+#pragma unroll 1
+      for (int ks = 0; ks < kC / 16; ++ks) {
+        const uint32_t poff = (ks / 4) * kPanel + (ks % 4) * 32;
+        tc::mma_bf16(tm + Lt::tHintra, tc::sdesc_sw128(sbase + Lt::kP + poff, 16, 1024),
+                     tc::sdesc_sw128(sbase + Lt::kV + ks * 2048, kPanel, 1024), idH, ks > 0);
+      }
+#pragma unroll 1
+      for (int blk = 0; blk < Lt::kNB; ++blk) {
+#pragma unroll 1
+        for (int ks = 0; ks < kC / 16; ++ks) {
+          // A = K~^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO = panel stride); K step = 16 rows
+          const uint64_t ad = tc::sdesc_sw128(sbase + Lt::kK + (2 * blk) * kPanel + ks * 2048, kPanel, 1024);
+          tc::mma_bf16(tm + Lt::tAcc + blk * 64, ad, tc::sdesc_sw128(sbase + Lt::kV + ks * 2048, kPanel, 1024),
+                       idAcc, true);
+          if (kNorm)
+            tc::mma_bf16(tm + Lt::tAccN + blk * 32, ad,
+                         tc::sdesc_sw128(sbase + Lt::kOnes + (ks / 4) * 2048 + (ks % 4) * 32, 16, 1024), idAccN,
+                         true);
+        }
+      }
+      tc::mma_commit(bar_mma);
+    }
+    if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
+    ++mma_uses;
+    tc::tc_fence_after();
+    if (__syncthreads_or(bad)) { bad = 1; break; }
+    if (tid == 0 && c + 1 < nchunks) issue_load(c + 1);
+    // ---- epilogue: output row t -------------------------------------------------
+    {
+      const float bt2 = rowB[tid], Mt2 = rowM[tid];
+      const float sc = ex2_approx(bt2 + m_prev * kLog2e - Mt2);
+      float qn = 0.f;
+      if (kNorm) {
+        float v[32];
+        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tQN), v);
+        tc::tmem_wait_ld();
+        qn = v[0];
+      }
+      const float den = fmaxf(sc * qn + den_intra, ex2_approx(-Mt2));
+      const float inv = 1.f / den;
+      const bool ok = valid;
+      __nv_bfloat16* orow = p.out + b * p.so[0] + h * p.so[1] + (int64_t)tg * p.so[2] + e0;
+      const __nv_bfloat16* xrow = (MODE == kSsd) ? p.x + b * p.sx[0] + h * p.sx[1] + (int64_t)tg * p.sx[2] + e0 : nullptr;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kDV; c0 += 32) {
+        float hi[32], ha[32];
+        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tHint + c0), hi);
+        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tHintra + c0), ha);
+        tc::tmem_wait_ld();
+        float o[32];
+        if (kNorm) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = (sc * hi[j] + ha[j]) * inv;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = fmaf(sc, hi[j], ha[j]);
+          if (ok && Dh != 0.f && e0 + c0 < p.dv) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 w = *reinterpret_cast<const uint4*>(xrow + c0 + 8 * q);
+              const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __bfloat1622float2(x2[j]);
+                o[8 * q + 2 * j] = fmaf(Dh, f.x, o[8 * q + 2 * j]);
+                o[8 * q + 2 * j + 1] = fmaf(Dh, f.y, o[8 * q + 2 * j + 1]);
+              }
+            }
+          }
+        }
+        if (ok && e0 + c0 < p.dv) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack2<__nv_bfloat16>(o[8 * q + 0], o[8 * q + 1]);
+            w.y = pack2<__nv_bfloat16>(o[8 * q + 2], o[8 * q + 3]);
+            w.z = pack2<__nv_bfloat16>(o[8 * q + 4], o[8 * q + 5]);
+            w.w = pack2<__nv_bfloat16>(o[8 * q + 6], o[8 * q + 7]);
+            *reinterpret_cast<uint4*>(orow + c0 + 8 * q) = w;
+          }
+        }
+      }
+    }
+    snapshot();
+    m_prev = m_new;
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+  }
+
+  // ---- final state ---------------------------------------------------------------
+  if (!bad) {
+    tc::tc_fence_after();
+#pragma unroll 1
+    for (int blk = 0; blk < Lt::kNB; ++blk) {
+      const int row = blk * 128 + warp * 32 + lane;
+      if (p.CT) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < kDV; c0 += 32) {
+          float v[32];
+          tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tAcc + blk * 64 + c0), v);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = e0 + c0 + j;
+            if (col < p.dv) {
+              if (p.state_t) p.CT[((int64_t)bh * p.dv + col) * DK + row] = v[j];
+              else p.CT[((int64_t)bh * DK + row) * p.dv + col] = v[j];
+            }
+          }
+        }
+      }
+      if (kNorm && p.nT && blockIdx.x == 0) {
+        float v[32];
+        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tAccN + blk * 32), v);
+        tc::tmem_wait_ld();
+        p.nT[(int64_t)bh * DK + row] = v[0];
+      }
+    }
+    if (kNorm && p.mT && blockIdx.x == 0 && tid == 0) p.mT[bh] = m_prev;
+  } else if (tid == 0) {
+    if (p.error_flag) atomicExch(p.error_flag, 1);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tm, 512);
+  }
+}
+
+}  // namespace chunk
+}  // namespace hxm

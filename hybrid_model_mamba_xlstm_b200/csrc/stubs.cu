@@ -2,12 +2,6 @@
 // Each returns HXM_EUNSUPPORTED with a message; none touches the GPU.
 #include "capi_internal.h"
 
-extern "C" size_t hxm_ssd_workspace_size(const hxm_ssd_args*) { return 0; }
-extern "C" hxm_status hxm_ssd_chunk_scan_fwd(const hxm_ssd_args* a, void*) {
-  HXM_REQUIRE(a && a->struct_size == sizeof(hxm_ssd_args), "hxm_ssd_chunk_scan_fwd: bad struct_size");
-  hxm::set_error("hxm_ssd_chunk_scan_fwd: not built in this library version");
-  return HXM_EUNSUPPORTED;
-}
 extern "C" hxm_status hxm_slstm_scan_fwd(const hxm_slstm_args* a, void*) {
   HXM_REQUIRE(a && a->struct_size == sizeof(hxm_slstm_args), "hxm_slstm_scan_fwd: bad struct_size");
   hxm::set_error("hxm_slstm_scan_fwd: not built in this library version");

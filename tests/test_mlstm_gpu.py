@@ -109,6 +109,28 @@ def test_segmented_state_roundtrip(ops):
     assert rel_err(np64(torch.cat([a, b2], 2)), np64(full)) < 1e-2
 
 
+@pytest.mark.parametrize("d", [128, 256])
+def test_tensor_core_path_segmented_state(ops, d):
+    """The tcgen05 chunkwise kernel (bf16, per-head gates, dqk 128/256): a
+    sequence split at a non-chunk boundary with the stabilized (C, n, m)
+    carried over matches one pass and the float64 oracle."""
+    from hybrid_model_mamba_xlstm_b200.workloads import mlstm_inputs
+    inp = mlstm_inputs(2, 2, 700, d, torch.bfloat16, seed=11, device="cuda")
+    full, (C, n, m) = ops.mlstm_chunkwise_fwd(inp.q, inp.k, inp.v, inp.log_i, inp.log_f, return_state=True)
+    s = 333
+    a, st = ops.mlstm_chunkwise_fwd(inp.q[:, :, :s], inp.k[:, :, :s], inp.v[:, :, :s], inp.log_i[:, :, :s],
+                                    inp.log_f[:, :, :s], return_state=True)
+    b2, st2 = ops.mlstm_chunkwise_fwd(inp.q[:, :, s:], inp.k[:, :, s:], inp.v[:, :, s:], inp.log_i[:, :, s:],
+                                      inp.log_f[:, :, s:], *st, return_state=True)
+    ref_h, ref_C, ref_n = _oracle_state([np64(t) for t in (inp.q, inp.k, inp.v, inp.log_i, inp.log_f)])
+    assert rel_err(np64(full), ref_h) < TOL16
+    assert rel_err(np64(torch.cat([a, b2], 2)), ref_h) < TOL16
+    for (Cx, nx, mx) in ((C, n, m), st2):
+        em = np.exp(np64(mx))
+        assert rel_err(np64(Cx) * em[..., None, None], ref_C) < TOL16
+        assert rel_err(np64(nx) * em[..., None], ref_n) < TOL16
+
+
 def test_den_clamp_and_large_input_gates(ops):
     """Large input-gate pre-activations (exp(60) would overflow the reference's
     unstabilized fp32 state) stay finite and match the float64 oracle."""
