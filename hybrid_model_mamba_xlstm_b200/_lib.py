@@ -81,8 +81,8 @@ class SlstmArgs(ct.Structure):
         ("gates_pre", ct.c_void_p), ("R", ct.c_void_p), ("norm_weight", ct.c_void_p),
         ("eps", ct.c_float), ("exponential_gate", ct.c_int32),
         ("h_out", ct.c_void_p),
-        ("h0", ct.c_void_p), ("c0", ct.c_void_p), ("m0", ct.c_void_p),
-        ("hT", ct.c_void_p), ("cT", ct.c_void_p), ("mT", ct.c_void_p),
+        ("h0", ct.c_void_p), ("c0", ct.c_void_p),
+        ("hT", ct.c_void_p), ("cT", ct.c_void_p),
         ("error_flag", ct.c_void_p),
     ]
 

@@ -349,7 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int pnl = 0; pnl < kNP; ++pnl) {
         unsigned char* krow = sm + Lt::kK + pnl * kPanel + tid * 128;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q0 = 0; q0 < 8; ++q0) {
+          const int q = (q0 + tid) & 7;  // stagger chunks across lanes: conflict-free rows
           uint4* ptr = reinterpret_cast<uint4*>(krow + q * 16);
           uint4 w = *ptr;
           uint32_t* e = reinterpret_cast<uint32_t*>(&w);

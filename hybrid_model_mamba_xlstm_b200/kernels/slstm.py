@@ -16,15 +16,15 @@ from ._common import dtype_code, ptr, require_cuda, stream_of
 __all__ = ["slstm_scan"]
 
 
-def slstm_scan(gates_pre, norm_weight, *, R=None, eps=1e-6, exponential_gate=True, h0=None, c0=None, m0=None,
+def slstm_scan(gates_pre, norm_weight, *, R=None, eps=1e-6, exponential_gate=True, h0=None, c0=None,
                return_state=True, error_flag=None):
     """gates_pre (B, L, H, 4, hd) — gate_proj output viewed per head, blocks
     [i | f | o | c~]; norm_weight (hd,); R (H, hd, 4*hd) or None;
-    h0, c0 (B, H, hd) fp32 (true cell); m0 (B, H).
-    Returns h_seq (B, L, H, hd) in gates_pre's dtype [and (h, c, m) fp32,
-    with the true cell = exp(m) * c]."""
+    h0, c0 (B, H, hd) fp32: the true hidden / cell state (the reference's
+    cache['h'], cache['c']).
+    Returns h_seq (B, L, H, hd) in gates_pre's dtype [and (h, c) fp32]."""
     who = "slstm_scan"
-    dev = require_cuda(gates_pre, norm_weight, R, h0, c0, m0, who=who)
+    dev = require_cuda(gates_pre, norm_weight, R, h0, c0, who=who)
     if gates_pre.dim() != 5 or gates_pre.shape[3] != 4:
         raise ValueError(f"{who}: gates_pre must be (B, L, H, 4, hd); got {tuple(gates_pre.shape)}")
     bsz, L, nh, _, hd = gates_pre.shape
@@ -39,22 +39,21 @@ def slstm_scan(gates_pre, norm_weight, *, R=None, eps=1e-6, exponential_gate=Tru
             raise ValueError(f"{who}: R must be {(nh, hd, 4 * hd)}; got {tuple(R.shape)}")
         Rb = R.to(torch.bfloat16).contiguous()
     f32 = lambda t: None if t is None else t.float().contiguous()
-    h0, c0, m0 = f32(h0), f32(c0), f32(m0)
+    h0, c0 = f32(h0), f32(c0)
     out = torch.empty((bsz, L, nh, hd), device=dev, dtype=io)
     st = None
     if return_state:
         st = (torch.empty((bsz, nh, hd), device=dev, dtype=torch.float32),
-              torch.empty((bsz, nh, hd), device=dev, dtype=torch.float32),
-              torch.empty((bsz, nh), device=dev, dtype=torch.float32))
+              torch.empty((bsz, nh, hd), device=dev, dtype=torch.float32))
     a = _lib.SlstmArgs()
     a.batch, a.seqlen, a.heads, a.head_dim = bsz, L, nh, hd
     a.io_dtype = dtype_code(g)
     a.gates_pre, a.R, a.norm_weight = ptr(g), ptr(Rb), ptr(w)
     a.eps, a.exponential_gate = float(eps), int(bool(exponential_gate))
     a.h_out = ptr(out)
-    a.h0, a.c0, a.m0 = ptr(h0), ptr(c0), ptr(m0)
+    a.h0, a.c0 = ptr(h0), ptr(c0)
     if st is not None:
-        a.hT, a.cT, a.mT = ptr(st[0]), ptr(st[1]), ptr(st[2])
+        a.hT, a.cT = ptr(st[0]), ptr(st[1])
     a.error_flag = ptr(error_flag)
     _lib.call("hxm_slstm_scan_fwd", a, stream_of(dev))
     return (out, st) if return_state else out

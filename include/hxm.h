@@ -175,9 +175,11 @@ hxm_status hxm_ssd_chunk_scan_fwd(const hxm_ssd_args* args, void* stream);
 /*   c = f*c + i*tanh(g_c);  h = o * tanh(w * c / sqrt(mean(c^2) + eps))     */
 /* R (heads, hd, 4*hd) bf16 or NULL (the reference has no recurrent R).      */
 /* gates_pre (b, t, heads, 4, hd) bf16/fp32 dense; h_out (b, t, heads, hd);  */
-/* h0, c0, hT, cT (b, heads, hd) fp32 or NULL.  The cell is stored           */
-/* stabilized: c = exp(m) * cs with m >= 0 (mT optional, (b, heads)).        */
-/* ------------------------------------------------------------------------ */
+/* h0, c0, hT, cT (b, heads, hd) fp32 or NULL: the true hidden and cell      */
+/* states, i.e. the reference's cache['h'], cache['c'] (slstm_block.py:      */
+/* 105-107,139-141).  Exponential input gates are stabilized internally per  */
+/* channel; head_dim 128 / 256 with R run the 8-CTA cluster kernel.          */
+/* error_flag: device int set to 1 if a bounded cross-CTA wait gave up.      */
 typedef struct hxm_slstm_args {
   size_t struct_size;
   int32_t batch, seqlen, heads, head_dim;
@@ -188,9 +190,9 @@ typedef struct hxm_slstm_args {
   float eps;
   int32_t exponential_gate; /* 1: i = exp, 0: i = sigmoid                    */
   void* h_out;
-  const float* h0; const float* c0; const float* m0;
-  float* hT; float* cT; float* mT;
-  int32_t* error_flag;      /* device int, set nonzero if a bounded wait gave up; may be NULL */
+  const float* h0; const float* c0;
+  float* hT; float* cT;
+  int32_t* error_flag;      /* device int or NULL                            */
 } hxm_slstm_args;
 
 hxm_status hxm_slstm_scan_fwd(const hxm_slstm_args* args, void* stream);
