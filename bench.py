@@ -179,6 +179,87 @@ def run_reference(args, world, rank):
     print(json.dumps(out), flush=True)
 
 
+def _time_cuda(fn, steps, warmup, dev, world):
+    """Mean ms per call over `steps` timed calls (CUDA events, max over ranks)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        fn()
+    e1.record(s)
+    torch.cuda.synchronize(dev)
+    return max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+
+def secondary_metrics(args, dev, world, rank):
+    """The other hot-path workloads, each timed on every rank (same order on all ranks)."""
+    from hybrid_model_mamba_xlstm_b200.kernels.slstm import slstm_scan
+    from hybrid_model_mamba_xlstm_b200.kernels.ssd import ssd_chunk_scan
+    from hybrid_model_mamba_xlstm_b200.kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
+    from hybrid_model_mamba_xlstm_b200.workloads import mlstm_inputs, ssd_inputs
+    pk, pk_kind = peaks()
+    tf_peak = pk["bf16_tflops"]
+    out = {}
+    steps = max(3, min(args.steps, 10))
+    # mLSTM chunkwise, per-head gates (tcgen05): the large-batch d=256 case and the exact 2x4x2048x256 case
+    for name, (b, h, L, d, c) in {"mlstm_b8_h8_l8192_d256": (8, 8, 8192, 256, 128),
+                                  "mlstm_b2_h4_l2048_d256_c64": (2, 4, 2048, 256, 64)}.items():
+        inp = mlstm_inputs(b, h, L, d, torch.bfloat16, seed=rank, device=dev, on_device=True)
+        ms = _time_cuda(lambda: mlstm_chunkwise_fwd(inp.q, inp.k, inp.v, inp.log_i, inp.log_f, chunk=c),
+                        steps, 3, dev, world)
+        fl = inp.flops(c)
+        out[name] = {"metric": "mLSTM chunkwise TFLOP/s (algorithmic)", "value": world * fl / ms / 1e9,
+                     "unit": "TFLOP/s", "ms": ms, "frac_of_bf16_peak": fl / ms / 1e9 / tf_peak,
+                     "peak_kind": pk_kind, "scaling": "weak", "kernel": "chunk_tc_kernel<%d, mLSTM>" % d}
+        del inp
+    # Mamba-2 SSD, batch 8, 32 heads x 64, dstate 128, seqlen 4096 (tcgen05)
+    inp = ssd_inputs(8, 4096, 32, 64, 128, seed=rank, device=dev, on_device=True)
+    ms = _time_cuda(lambda: ssd_chunk_scan(inp.x, inp.dt, inp.A, inp.B, inp.C, inp.D), steps, 3, dev, world)
+    fl = inp.flops(256)
+    out["ssd_b8_h32_p64_n128_l4096"] = {"metric": "SSD chunked scan TFLOP/s (algorithmic, chunk-256 formula)",
+                                        "value": world * fl / ms / 1e9, "unit": "TFLOP/s", "ms": ms,
+                                        "frac_of_bf16_peak": fl / ms / 1e9 / tf_peak, "peak_kind": pk_kind,
+                                        "scaling": "weak", "kernel": "chunk_tc_kernel<128, SSD>"}
+    del inp
+    # sLSTM recurrence with block-diagonal R, the prefill's layer shape: batch 8, 4 heads x 256, seqlen 2048
+    g = torch.Generator(device=dev)
+    g.manual_seed(rank)
+    gates = torch.randn(8, 2048, 4, 4, 256, generator=g, device=dev).mul_(0.5).to(torch.bfloat16)
+    Rw = (torch.randn(4, 256, 1024, generator=g, device=dev) / 16).to(torch.bfloat16)
+    w = torch.ones(256, device=dev)
+    ms = _time_cuda(lambda: slstm_scan(gates, w, R=Rw), min(steps, 3), 2, dev, world)
+    out["slstm_b8_h4_hd256_l2048"] = {"metric": "sLSTM recurrence us/step (sequential over seqlen)",
+                                      "value": ms * 1e3 / 2048, "unit": "us/step", "ms": ms,
+                                      "kernel": "slstm_cluster_kernel<bf16, 256>"}
+    del gates, Rw
+    out["prefill"] = prefill_metric(args, dev, world, rank)
+    return out
+
+
+def prefill_metric(args, dev, world, rank):
+    """Hybrid-350M prefill (24 layers [Mamba, Mamba, mLSTM, sLSTM], d 1024, vocab
+    50304, bf16), global batch 8 x seqlen 2048 data-parallel over the ranks."""
+    import hybrid_model_mamba_xlstm_b200.layers as Lyr
+    gb, seqlen = 8, 2048
+    per = max(1, gb // world)
+    torch.manual_seed(1234)  # identical weights on every rank
+    model = Lyr.HybridLanguageModel(Lyr.hybrid_350m_config()).to(dev).to(torch.bfloat16).eval()
+    g = torch.Generator(device=dev)
+    g.manual_seed(99 + rank)
+    ids = torch.randint(0, 50304, (per, seqlen), generator=g, device=dev)
+    with torch.no_grad():
+        ms = _time_cuda(lambda: model(ids), 3, 2, dev, world)
+    nparam = sum(p.numel() for p in model.parameters())
+    del model
+    return {"metric": "hybrid-350M prefill tokens/s", "value": world * per * seqlen / ms * 1e3, "unit": "tok/s",
+            "ms_per_step": ms, "global_batch": world * per, "seqlen": seqlen, "params": nparam,
+            "scaling": "strong (global batch 8 split over ranks)", "parallelism": f"dp{world}"}
+
+
 def run_ours(args, world, rank, local):
     from hybrid_model_mamba_xlstm_b200.kernels.selective_scan import selective_scan_fn
     from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
@@ -219,10 +300,12 @@ def run_ours(args, world, rank, local):
     roofline = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / pk["hbm_gbs"], "peak_kind": pk_kind,
                 "traffic": profile_traffic("scan_fwd_kernel bf16 b8 l32768 d4096 n16"),
-                "kernel": "hxm::scan::scan_fwd_kernel<bf16,16,64>", "algorithmic_bytes": nbytes}
+                "kernel": "hxm::scan::scan_fast_kernel<bf16, 64, 32, silu, softplus>", "algorithmic_bytes": nbytes}
 
     # ---- end to end through the public API with host buffers (bounded: 1 batch row per rank)
     e2e = e2e_scan(dev, args, world)
+
+    secondary = None if args.no_secondary else secondary_metrics(args, dev, world, rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -238,7 +321,7 @@ def run_ours(args, world, rank, local):
                "config": {"workload": "selective scan b8 l32768 d4096 n16 per rank", **W,
                           "l2": "inputs 8.6 GB per step > L2 (no flush needed)", "parallelism": f"dp{world}"},
                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
-               "clocks": clocks}
+               "clocks": clocks, "secondary": secondary}
         print(json.dumps(out), flush=True)
 
 
@@ -292,6 +375,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-secondary", action="store_true", help="only the headline scan workload")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     if args.impl == "reference":

@@ -1,0 +1,201 @@
+"""The reference's layer callers of the recurrent hot path, wired to the B200 kernels.
+
+Module and parameter names follow hybrid_xmamba/layers so a reference
+state_dict loads unchanged:
+  RMSNorm        layers/normalization.py:8-34
+  MambaBlock     layers/mamba_block.py:17-133
+  mLSTMBlock     layers/mlstm_block.py:19-146
+  sLSTMBlock     layers/slstm_block.py:18-143 (+ optional block-diagonal
+                 recurrent weights ``recurrent_weight`` (H, hd, 4*hd); zero
+                 reproduces the reference, which has none)
+  HybridBlock    layers/hybrid_block.py:20-147
+
+The projections are plain GEMMs (torch / cuBLAS); the recurrences are the hxm
+kernels.  Activations are laid out so every kernel gets its fast layout
+without copies: the Mamba branch runs channel-major (batch, dim, seqlen) —
+in_proj, x_proj and dt_proj are computed as W @ X^T — so u, delta, z, B, C
+reach the fused scan time-major, and softplus(dt + dt_proj.bias) and
+y * silu(z) happen inside the scan kernel.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..kernels.selective_scan.scan_interface import selective_scan_fn
+from ..kernels.slstm import slstm_scan
+from ..kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
+
+
+class RMSNorm(nn.Module):
+    """w * x / sqrt(mean(x^2) + eps) over the last dim (normalization.py:8-34)."""
+
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return (self.weight.float() * y).to(x.dtype)
+
+
+class MambaBlock(nn.Module):
+    """Mamba mixer (mamba_block.py:29-133): in_proj -> causal depthwise conv +
+    SiLU -> x_proj -> dt_proj -> fused selective scan (Euler, softplus(dt+bias),
+    + D*u, * silu(z)) -> out_proj."""
+
+    def __init__(self, dim, state_size=16, conv_size=4, expand_factor=2, dt_rank=None, use_fast_path=True):
+        super().__init__()
+        self.dim, self.state_size, self.conv_size = dim, state_size, conv_size
+        self.inner_dim = dim * expand_factor
+        self.dt_rank = max(1, dim // 16) if dt_rank is None else dt_rank
+        self.use_fast_path = use_fast_path
+        self.in_proj = nn.Linear(dim, self.inner_dim * 2, bias=False)
+        self.conv1d = nn.Conv1d(self.inner_dim, self.inner_dim, conv_size, padding=conv_size - 1,
+                                groups=self.inner_dim, bias=True)
+        self.x_proj = nn.Linear(self.inner_dim, self.dt_rank + 2 * state_size, bias=False)
+        self.dt_proj = nn.Linear(self.dt_rank, self.inner_dim, bias=True)
+        A = torch.arange(1, state_size + 1, dtype=torch.float32).repeat(self.inner_dim, 1)
+        self.A_log = nn.Parameter(torch.log(A))
+        self.D = nn.Parameter(torch.ones(self.inner_dim))
+        self.out_proj = nn.Linear(self.inner_dim, dim, bias=False)
+
+    def forward(self, x, cache=None):
+        bsz, L, _ = x.shape
+        di, n, r = self.inner_dim, self.state_size, self.dt_rank
+        xt = x.transpose(1, 2)                                   # (B, dim, L) view
+        xz = torch.matmul(self.in_proj.weight, xt)               # (B, 2*di, L) channel-major
+        x_in, z = xz[:, :di], xz[:, di:]
+        u = F.conv1d(F.pad(x_in, (self.conv_size - 1, 0)), self.conv1d.weight, self.conv1d.bias, groups=di)
+        u = F.silu(u)                                            # (B, di, L)
+        dbc = torch.matmul(self.x_proj.weight, u)                # (B, r + 2n, L)
+        dt_low, Bm, Cm = dbc[:, :r], dbc[:, r:r + n], dbc[:, r + n:]
+        delta = torch.matmul(self.dt_proj.weight, dt_low)        # (B, di, L), bias folded into the scan
+        A = -torch.exp(self.A_log.float())
+        y = selective_scan_fn(u, delta, A, Bm, Cm, self.D.float(), z=z, delta_bias=self.dt_proj.bias.float(),
+                              delta_softplus=True)               # (B, di, L)
+        return torch.matmul(y.transpose(1, 2), self.out_proj.weight.t())
+
+
+class mLSTMBlock(nn.Module):
+    """mLSTM mixer (mlstm_block.py:32-146): projections, per-head RMSNorm of
+    q and k, i = exp, f = sigmoid, o = sigmoid per channel, the mLSTM
+    recurrence, h*o*sigmoid(x_gate), out_proj."""
+
+    def __init__(self, dim, head_dim=64, num_heads=None, use_tfla=True, proj_factor=2):
+        super().__init__()
+        self.dim, self.head_dim = dim, head_dim
+        self.num_heads = max(1, dim // head_dim) if num_heads is None else num_heads
+        self.inner_dim = self.num_heads * head_dim
+        self.use_tfla, self.proj_factor = use_tfla, proj_factor
+        self.in_proj = nn.Linear(dim, self.inner_dim * proj_factor, bias=False)
+        self.q_proj = nn.Linear(self.inner_dim, self.inner_dim, bias=False)
+        self.k_proj = nn.Linear(self.inner_dim, self.inner_dim, bias=False)
+        self.v_proj = nn.Linear(self.inner_dim, self.inner_dim, bias=False)
+        self.i_gate_proj = nn.Linear(self.inner_dim, self.inner_dim, bias=True)
+        self.f_gate_proj = nn.Linear(self.inner_dim, self.inner_dim, bias=True)
+        self.o_gate_proj = nn.Linear(self.inner_dim, self.inner_dim, bias=True)
+        self.q_norm = RMSNorm(head_dim)
+        self.k_norm = RMSNorm(head_dim)
+        self.out_proj = nn.Linear(self.inner_dim, dim, bias=False)
+        self.register_buffer("eps", torch.tensor(1e-6))
+
+    def forward(self, x, cache=None):
+        bsz, L, _ = x.shape
+        nh, hd = self.num_heads, self.head_dim
+        xp = self.in_proj(x)
+        if self.proj_factor == 2:
+            x_inner, x_gate = xp.chunk(2, dim=-1)
+        else:
+            x_inner = x_gate = xp
+        heads = lambda t: t.view(bsz, L, nh, hd).transpose(1, 2)   # (B, H, L, hd)
+        q = self.q_norm(heads(self.q_proj(x_inner))).contiguous()
+        k = self.k_norm(heads(self.k_proj(x_inner))).contiguous()
+        v = heads(self.v_proj(x_inner)).contiguous()
+        log_i = heads(self.i_gate_proj(x_inner).float())            # log of i = exp(pre)
+        log_f = heads(F.logsigmoid(self.f_gate_proj(x_inner).float()))
+        o = torch.sigmoid(self.o_gate_proj(x_inner))
+        h = mlstm_chunkwise_fwd(q, k, v, log_i, log_f)               # (B, H, L, hd)
+        h = h.transpose(1, 2).reshape(bsz, L, nh * hd) * o * torch.sigmoid(x_gate)
+        return self.out_proj(h)
+
+
+class sLSTMBlock(nn.Module):
+    """sLSTM mixer (slstm_block.py:30-143) with the recurrence in the hxm
+    kernel.  ``recurrent_weight`` (H, hd, 4*hd) adds R[head]^T h_{t-1} to the
+    gate pre-activations (zero-initialised: the reference block has no R)."""
+
+    def __init__(self, dim, hidden_dim=None, num_heads=4, use_exponential_gate=True, recurrent=False):
+        super().__init__()
+        self.dim = dim
+        self.hidden_dim = hidden_dim or dim
+        self.num_heads = num_heads
+        self.use_exponential_gate = use_exponential_gate
+        assert self.hidden_dim % num_heads == 0
+        self.head_dim = self.hidden_dim // num_heads
+        self.in_proj = nn.Linear(dim, self.hidden_dim, bias=False)
+        self.gate_proj = nn.Linear(self.hidden_dim, self.hidden_dim * 4, bias=True)
+        self.h_norm = RMSNorm(self.head_dim)
+        self.out_proj = nn.Linear(self.hidden_dim, dim, bias=False)
+        self.register_buffer("eps", torch.tensor(1e-6))
+        self.recurrent_weight = (nn.Parameter(torch.zeros(num_heads, self.head_dim, 4 * self.head_dim))
+                                 if recurrent else None)
+
+    def forward(self, x, cache=None):
+        bsz, L, _ = x.shape
+        gates = self.gate_proj(self.in_proj(x)).view(bsz, L, self.num_heads, 4, self.head_dim)
+        h0 = c0 = None
+        if cache is not None and "h" in cache and "c" in cache:
+            h0, c0 = cache["h"], cache["c"]
+        h_seq, (h, c) = slstm_scan(gates, self.h_norm.weight, R=self.recurrent_weight, eps=self.h_norm.eps,
+                                   exponential_gate=self.use_exponential_gate, h0=h0, c0=c0)
+        if cache is not None:
+            cache["h"], cache["c"] = h.to(x.dtype), c.to(x.dtype)
+        return self.out_proj(h_seq.reshape(bsz, L, self.hidden_dim))
+
+
+class HybridBlock(nn.Module):
+    """Pre-norm mixer + residual, optional pre-norm GELU MLP + residual
+    (hybrid_block.py:38-134), with the reference's kwarg routing (:58-88)."""
+
+    def __init__(self, dim, layer_type="mamba", norm_type="rms", use_mlp=True, mlp_ratio=4.0, **kw):
+        super().__init__()
+        self.dim, self.layer_type, self.use_mlp = dim, layer_type.lower(), use_mlp
+        norm = (lambda: RMSNorm(dim)) if norm_type.lower() == "rms" else (lambda: nn.LayerNorm(dim))
+        self.norm1 = norm()
+        if self.layer_type == "mamba":
+            keys = {"state_size", "conv_size", "expand_factor", "dt_rank", "use_fast_path"}
+            self.mixer = MambaBlock(dim, **{k: v for k, v in kw.items() if k in keys})
+        elif self.layer_type == "mlstm":
+            keys = {"head_dim", "num_heads", "use_tfla", "proj_factor"}
+            self.mixer = mLSTMBlock(dim, **{k: v for k, v in kw.items() if k in keys})
+        elif self.layer_type == "slstm":
+            sk = {}
+            for k, v in kw.items():
+                if k.startswith("slstm_"):
+                    name = k[len("slstm_"):]
+                    if name in ("hidden_dim", "num_heads", "use_exponential_gate", "recurrent"):
+                        sk[name] = v
+                elif k in ("num_heads", "use_exponential_gate"):
+                    sk[k] = v
+            self.mixer = sLSTMBlock(dim, **sk)
+        else:
+            raise ValueError(f"Unknown layer type: {layer_type}")
+        if use_mlp:
+            self.norm2 = norm()
+            self.mlp = nn.Sequential(nn.Linear(dim, int(dim * mlp_ratio), bias=False), nn.GELU(),
+                                     nn.Linear(int(dim * mlp_ratio), dim, bias=False))
+        else:
+            self.norm2 = self.mlp = None
+
+    def forward(self, x, cache=None):
+        x = x + self.mixer(self.norm1(x), cache=cache)
+        if self.use_mlp:
+            x = x + self.mlp(self.norm2(x))
+        return x

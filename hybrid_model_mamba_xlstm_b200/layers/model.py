@@ -1,0 +1,125 @@
+"""Hybrid Mamba / xLSTM language model (prefill forward) on the hxm kernels.
+
+Mirrors HybridConfig (hybrid_xmamba/models/configuration_hybrid.py:11-111)
+and HybridLanguageModel.forward (hybrid_xmamba/models/hybrid_lm.py:88-209):
+embedding -> HybridBlocks cycling ``layer_pattern`` -> final RMSNorm ->
+lm_head.  State-dict keys match the reference.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import torch
+import torch.nn as nn
+
+from .blocks import HybridBlock, RMSNorm
+
+
+@dataclass
+class HybridConfig:
+    """Fields and defaults of the reference HybridConfig (:47-111), plus
+    ``slstm_recurrent`` (block-diagonal recurrent weights in sLSTM layers)
+    and ``residual_init_scale`` (scale residual-out projections by
+    1/sqrt(2 * num_layers) at init)."""
+    vocab_size: int = 50257
+    dim: int = 768
+    num_layers: int = 12
+    layer_pattern: List[str] = field(default_factory=lambda: ["mamba", "mamba", "mlstm"])
+    state_size: int = 16
+    conv_size: int = 4
+    expand_factor: int = 2
+    dt_rank: Optional[int] = None
+    use_fast_path: bool = True
+    head_dim: int = 64
+    num_heads: Optional[int] = None
+    use_tfla: bool = True
+    proj_factor: int = 2
+    slstm_hidden_dim: Optional[int] = None
+    slstm_num_heads: int = 4
+    use_exponential_gate: bool = True
+    norm_type: str = "rms"
+    use_mlp: bool = True
+    mlp_ratio: float = 4.0
+    max_position_embeddings: int = 2048
+    dropout: float = 0.1
+    initializer_range: float = 0.02
+    use_cache: bool = True
+    tie_word_embeddings: bool = False
+    slstm_recurrent: bool = False
+    residual_init_scale: bool = False
+
+    def __post_init__(self):
+        if self.num_heads is None:
+            self.num_heads = max(1, self.dim // self.head_dim)
+        if self.dt_rank is None:
+            self.dt_rank = max(1, self.dim // 16)
+        if self.slstm_hidden_dim is None:
+            self.slstm_hidden_dim = self.dim
+        for t in self.layer_pattern:
+            if t not in ("mamba", "mlstm", "slstm"):
+                raise ValueError(f"Invalid layer type '{t}'")
+
+
+def hybrid_350m_config(**over) -> HybridConfig:
+    """d_model 1024, 24 layers of [Mamba, Mamba, mLSTM, sLSTM]; Mamba expand 2,
+    d_state 16, conv 4; mLSTM 4 heads of 512; sLSTM 4 heads with block-diagonal
+    recurrent weights; vocab 50304; residual projections scaled 1/sqrt(48)."""
+    kw = dict(vocab_size=50304, dim=1024, num_layers=24, layer_pattern=["mamba", "mamba", "mlstm", "slstm"],
+              state_size=16, conv_size=4, expand_factor=2, head_dim=512, num_heads=4, slstm_num_heads=4,
+              dropout=0.0, slstm_recurrent=True, residual_init_scale=True)
+    kw.update(over)
+    return HybridConfig(**kw)
+
+
+class HybridLanguageModel(nn.Module):
+    def __init__(self, config: HybridConfig):
+        super().__init__()
+        self.config = c = config
+        self.embeddings = nn.Module()
+        self.embeddings.token_embedding = nn.Embedding(c.vocab_size, c.dim)
+        self.layers = nn.ModuleList([
+            HybridBlock(c.dim, layer_type=c.layer_pattern[i % len(c.layer_pattern)], norm_type=c.norm_type,
+                        use_mlp=c.use_mlp, mlp_ratio=c.mlp_ratio, state_size=c.state_size, conv_size=c.conv_size,
+                        expand_factor=c.expand_factor, dt_rank=c.dt_rank, use_fast_path=c.use_fast_path,
+                        head_dim=c.head_dim, num_heads=c.num_heads, use_tfla=c.use_tfla, proj_factor=c.proj_factor,
+                        slstm_hidden_dim=c.slstm_hidden_dim, slstm_num_heads=c.slstm_num_heads,
+                        use_exponential_gate=c.use_exponential_gate, slstm_recurrent=c.slstm_recurrent)
+            for i in range(c.num_layers)])
+        self.final_norm = RMSNorm(c.dim) if c.norm_type.lower() == "rms" else nn.LayerNorm(c.dim)
+        self.lm_head = nn.Linear(c.dim, c.vocab_size, bias=False)
+        if c.tie_word_embeddings:
+            self.lm_head.weight = self.embeddings.token_embedding.weight
+        self.apply(self._init_weights)
+        if c.residual_init_scale:
+            s = 1.0 / math.sqrt(2 * c.num_layers)
+            with torch.no_grad():
+                for blk in self.layers:
+                    blk.mixer.out_proj.weight.mul_(s)
+                    if blk.mlp is not None:
+                        blk.mlp[2].weight.mul_(s)
+        if c.slstm_recurrent:
+            with torch.no_grad():
+                for blk in self.layers:
+                    rw = getattr(blk.mixer, "recurrent_weight", None)
+                    if rw is not None:
+                        rw.normal_(0.0, 1.0 / math.sqrt(blk.mixer.head_dim))
+
+    def _init_weights(self, module):
+        """N(0, initializer_range) weights, zero biases (hybrid_lm.py:136-143)."""
+        if isinstance(module, nn.Linear):
+            nn.init.normal_(module.weight, mean=0.0, std=self.config.initializer_range)
+            if module.bias is not None:
+                nn.init.zeros_(module.bias)
+        elif isinstance(module, nn.Embedding):
+            nn.init.normal_(module.weight, mean=0.0, std=self.config.initializer_range)
+
+    def forward(self, input_ids, return_hidden=False):
+        h = self.embeddings.token_embedding(input_ids)
+        for layer in self.layers:
+            h = layer(h)
+        h = self.final_norm(h)
+        if return_hidden:
+            return h
+        return self.lm_head(h)
