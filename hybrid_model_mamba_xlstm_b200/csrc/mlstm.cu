@@ -2,8 +2,10 @@
 //
 // Replaces apply_tfla / TFLAFunction.forward / tfla_forward_pytorch
 // (hybrid_xmamba/kernels/tfla/tfla_interface.py:18-49,84-139,142-163).
-// bf16 I/O with per-head gates runs the tcgen05 chunkwise kernel; fp32 I/O,
-// per-channel gates and other shapes run the exact CUDA-core recurrence.
+// bf16 I/O: per-head gates with dqk 128/256 run the fused tcgen05 chunkwise
+// kernel; per-channel gates (mLSTMBlock) and dqk 512 run the key-streaming
+// tcgen05 kernel (workspace: hxm_mlstm_workspace_size); fp32 I/O and other
+// shapes run the exact CUDA-core recurrence.
 #include "capi_internal.h"
 #include "mlstm.h"
 
@@ -35,11 +37,13 @@ static hxm_status fill(const hxm_mlstm_args* a, Params& p) {
 static bool use_tc(const Params& p) {
   return p.io_dtype == HXM_BF16 && p.gate_mode == 0 && hxm::mlstm::chunkwise_tc_workspace(p) != (size_t)-1;
 }
+static bool use_stream(const Params& p) { return !use_tc(p) && hxm::mlstm::stream_shape_ok(p); }
 
 extern "C" size_t hxm_mlstm_workspace_size(const hxm_mlstm_args* a) {
   Params p{};
   if (fill(a, p) != HXM_OK) return 0;
-  return use_tc(p) ? hxm::mlstm::chunkwise_tc_workspace(p) : 0;
+  if (use_tc(p)) return hxm::mlstm::chunkwise_tc_workspace(p);
+  return use_stream(p) ? hxm::mlstm::stream_workspace(p) : 0;
 }
 
 extern "C" hxm_status hxm_mlstm_chunkwise_fwd(const hxm_mlstm_args* a, void* stream) {
@@ -52,5 +56,6 @@ extern "C" hxm_status hxm_mlstm_chunkwise_fwd(const hxm_mlstm_args* a, void* str
               "hxm_mlstm_chunkwise_fwd: NULL tensor pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (use_tc(p)) return hxm::mlstm::launch_chunkwise_tc(p, st);
+  if (use_stream(p)) return hxm::mlstm::launch_stream(p, st);
   return hxm::mlstm::launch_recurrent(p, st);
 }

@@ -36,9 +36,14 @@ struct Params {
 
 // Exact step-by-step recurrence on CUDA cores (any gate mode / dtype / dims <= 512).
 hxm_status launch_recurrent(const Params& p, cudaStream_t st);
-// tcgen05 chunkwise kernel (bf16, per-head gates); returns HXM_EUNSUPPORTED for shapes it does not cover.
+// tcgen05 chunkwise kernel (bf16, per-head gates, dqk 128/256, stabilized); no workspace.
 hxm_status launch_chunkwise_tc(const Params& p, cudaStream_t st);
-size_t chunkwise_tc_workspace(const Params& p);
+size_t chunkwise_tc_workspace(const Params& p);  // (size_t)-1 when the shape is not covered
+// Key-streaming tcgen05 kernel (bf16, per-head or per-channel gates, dqk 128/256/512) with a
+// prescale pass into a caller-owned workspace of stream_workspace() bytes.
+bool stream_shape_ok(const Params& p);
+size_t stream_workspace(const Params& p);
+hxm_status launch_stream(const Params& p, cudaStream_t st);
 
 }  // namespace mlstm
 }  // namespace hxm

@@ -7,8 +7,8 @@
 // register-resident m16n8k16 MMAs.  The per-channel exponential-gate
 // stabilizer m and the cell live in registers.  After the cell update each
 // CTA broadcasts (cell, m, o) of its channels into every CTA's shared memory
-// (distributed shared memory stores) and signals with one remote mbarrier
-// arrive per peer; every CTA then has all hd channels and finishes the
+// with st.async stores that complete transaction bytes on the receiver's
+// mbarrier (no separate signal); every CTA then has all hd channels and finishes the
 // RMSNorm over head_dim and h = o*tanh(.) locally — one cluster exchange per
 // step.  Waits are bounded (error flag + early exit, no hang).
 #include <cuda_bf16.h>
@@ -36,13 +36,15 @@ HXM_DEV uint32_t map_to_rank(uint32_t local_smem_addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
   return r;
 }
-HXM_DEV void st_cluster_v4(uint32_t addr, float4 v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
-               "f"(v.w)
+// 16-byte store into a peer CTA's shared memory that completes 16 bytes of
+// transaction count on the peer's mbarrier (no separate signal needed).
+HXM_DEV void st_async_v4(uint32_t raddr, float4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
                : "memory");
 }
-HXM_DEV void arrive_remote(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+HXM_DEV void arm_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 HXM_DEV bool try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -141,9 +143,14 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
     hprev[bl * (HD + 8) + j] = __float2bfloat16_rn(hv);
   }
   if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&bars[0])), "r"(kCL) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&bars[1])), "r"(kCL) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&bars[0])), "r"(1) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&bars[1])), "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // each phase = one local arrive (with the byte expectation) + kBR*HD*16
+    // bytes of st.async stores from the 8 CTAs; arm steps 0 and 1 before the
+    // start-up cluster barrier so no peer data can precede its arm.
+    arm_tx(&bars[0], kBR * HD * 16);
+    arm_tx(&bars[1], kBR * HD * 16);
   }
   // per-thread (channel, batch) pairs: stabilized cell and its log-scale
   float cs[L::kPPT], ms[L::kPPT];
@@ -198,14 +205,17 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
       const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
       for (int mw = 0; mw < L::kMW; ++mw) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // two independent chains
 #pragma unroll
         for (int kt = 0; kt < L::kKT; ++kt) {
           const __nv_bfloat16* hb = hprev + g * (HD + 8) + kt * 16 + t4 * 2;
           const uint32_t b0r = *reinterpret_cast<const uint32_t*>(hb);
           const uint32_t b1r = *reinterpret_cast<const uint32_t*>(hb + 8);
-          mma_16816(d, afr[mw][kt], b0r, b1r);
+          if (kt & 1) mma_16816(e, afr[mw][kt], b0r, b1r);
+          else mma_16816(d, afr[mw][kt], b0r, b1r);
         }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) d[r] += e[r];
         const int m = (warp * L::kMW + mw) * 16 + g;
         pre[(2 * t4) * L::kCols + m] = d[0];
         pre[(2 * t4 + 1) * L::kCols + m] = d[1];
@@ -227,20 +237,14 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
         const float lf = log_sigmoid_f(gp[1]);
         const float li = p.exp_gate ? gp[0] : log_sigmoid_f(gp[0]);
         const float mn = fmaxf(ms[i] + lf, li);
-        cs[i] = __expf(ms[i] + lf - mn) * cs[i] + __expf(li - mn) * tanhf(gp[3]);
+        cs[i] = __expf(ms[i] + lf - mn) * cs[i] + __expf(li - mn) * tanh_approx(gp[3]);
         ms[i] = mn;
-        const float og = 1.f / (1.f + __expf(-gp[2]));
+        const float og = fmaf(0.5f, tanh_approx(0.5f * gp[2]), 0.5f);
         const float4 v = make_float4(cs[i], ms[i], og, 0.f);
         const uint32_t off = (uint32_t)(((par * kBR + bl) * HDs + c0 + c) * 16);
 #pragma unroll
-        for (int r = 0; r < kCL; ++r) st_cluster_v4(map_to_rank(xaddr0 + off, r), v);
+        for (int r = 0; r < kCL; ++r) st_async_v4(map_to_rank(xaddr0 + off, r), v, map_to_rank(baddr0 + par * 8, r));
       }
-    }
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("fence.acq_rel.cluster;" ::: "memory");
-#pragma unroll
-      for (int r = 0; r < kCL; ++r) arrive_remote(map_to_rank(baddr0 + par * 8, r));
     }
     // (c) wait for all 8 slices (bounded)
     {
@@ -259,6 +263,10 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
       bad = true;
       break;
     }
+    // re-arm this buffer's barrier for step t + 2.  Peers can only send step
+    // t + 2 after waiting on step t + 1, which needs this CTA's step t + 1
+    // stores — issued after this point — so the arm always precedes the data.
+    if (tid == 0 && t + 2 < p.seqlen) arm_tx(&bars[par], kBR * HD * 16);
     // (d) RMSNorm over head_dim and h for every channel (kTPB threads per batch row)
     {
       const int bl = tid / L::kTPB, sub = tid % L::kTPB;
@@ -282,7 +290,7 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
       for (int i = 0; i < L::kCPT; ++i) {
         const int j = sub + L::kTPB * i;
         const float4 x = xr[j];
-        const float hv = x.z * tanhf(wsm[j] * __expf(x.y - M) * x.x * rinv);
+        const float hv = x.z * tanh_approx(wsm[j] * __expf(x.y - M) * x.x * rinv);
         hprev[bl * (HD + 8) + j] = __float2bfloat16_rn(hv);
         hlast[i] = hv;
         if (bl < nb && j >= c0 && j < c0 + L::kCPC)
