@@ -94,6 +94,7 @@ SYMBOLS = {
     "hxm_selective_scan_fwd": (ct.c_int, [ct.POINTER(ScanArgs), ct.c_void_p]),
     "hxm_mlstm_workspace_size": (ct.c_size_t, [ct.POINTER(MlstmArgs)]),
     "hxm_mlstm_chunkwise_fwd": (ct.c_int, [ct.POINTER(MlstmArgs), ct.c_void_p]),
+    "hxm_mlstm_chunkwise_fwd_noalloc": (ct.c_int, [ct.POINTER(MlstmArgs), ct.c_void_p]),
     "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),
     "hxm_ssd_chunk_scan_fwd": (ct.c_int, [ct.POINTER(SsdArgs), ct.c_void_p]),
     "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),

@@ -133,6 +133,18 @@ typedef struct hxm_mlstm_args {
 size_t hxm_mlstm_workspace_size(const hxm_mlstm_args* args);
 hxm_status hxm_mlstm_chunkwise_fwd(const hxm_mlstm_args* args, void* stream);
 
+/* No counterpart in the reference.  Same computation as
+ * hxm_mlstm_chunkwise_fwd on its key-streaming tensor-core path (bf16,
+ * dqk 128/256/512, per-head or per-channel gates), for callers that cannot
+ * allocate device memory at call time (plugin hosts whose execute callbacks
+ * forbid cudaMalloc, programs that pre-reserve all device memory): it needs
+ * no workspace — args->workspace is ignored — and allocates nothing.  Its
+ * scratch is one library-owned 32 MiB device array per GPU, held until exit;
+ * requests needing more return HXM_EBADARG.  The first call on a device looks
+ * up the array's address (make it before any stream capture); calls that
+ * overlap on the GPU race on the shared array. */
+hxm_status hxm_mlstm_chunkwise_fwd_noalloc(const hxm_mlstm_args* args, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* 3. Mamba-2 SSD chunked scan (ngroups = 1)                                  */
 /*                                                                           */
