@@ -110,30 +110,23 @@ class ClockSampler:
 
 
 def dist_setup(args):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from hybrid_model_mamba_xlstm_b200 import dist as D
+    world, rank, local = D.env_world()
     if world > 1:
-        import datetime
-        torch.cuda.set_device(local)
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=torch.device("cuda", local))
+        D.init("nccl", timeout_s=120.0)
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
 
 
 def barrier(world):
-    if world > 1:
-        torch.distributed.barrier()
+    from hybrid_model_mamba_xlstm_b200 import dist as D
+    D.barrier(world)
 
 
 def max_over_ranks(x, world):
-    if world == 1:
-        return x
-    t = torch.tensor([x], device="cuda", dtype=torch.float64)
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
+    from hybrid_model_mamba_xlstm_b200 import dist as D
+    return D.max_over_ranks(x, world)
 
 
 def cpu_scan_sample(seqlen, dim_sample, dstate, seed=0):
@@ -302,6 +295,14 @@ def run_ours(args, world, rank, local):
                 "traffic": profile_traffic("scan_fwd_kernel bf16 b8 l32768 d4096 n16"),
                 "kernel": "hxm::scan::scan_fast_kernel<bf16, 64, 32, silu, softplus>", "algorithmic_bytes": nbytes}
 
+    # ---- verification: NCCL all-gather of per-rank output checksums (outside the timed region)
+    from hybrid_model_mamba_xlstm_b200 import dist as D
+    yv, hv = step()
+    cs = D.gather_checksums(D.checksum(yv[:, :64, :4096]) + D.checksum(hv), world)
+    verification = {"per_rank_checksums": cs.tolist(), "finite": bool(torch.isfinite(cs).all()),
+                    "note": "sum, sum of squares, max|.| of a y slice and of the final state, gathered after timing"}
+    del yv, hv
+
     # ---- end to end through the public API with host buffers (bounded: 1 batch row per rank)
     e2e = e2e_scan(dev, args, world)
 
@@ -321,7 +322,7 @@ def run_ours(args, world, rank, local):
                "config": {"workload": "selective scan b8 l32768 d4096 n16 per rank", **W,
                           "l2": "inputs 8.6 GB per step > L2 (no flush needed)", "parallelism": f"dp{world}"},
                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
-               "clocks": clocks, "secondary": secondary}
+               "clocks": clocks, "verification": verification, "secondary": secondary}
         print(json.dumps(out), flush=True)
 
 
@@ -387,8 +388,8 @@ def main():
     try:
         run_ours(args, world, rank, local)
     finally:
-        if world > 1:
-            torch.distributed.destroy_process_group()
+        from hybrid_model_mamba_xlstm_b200 import dist as D
+        D.finalize(world)
 
 
 if __name__ == "__main__":

@@ -1,6 +1,6 @@
 // tc_sm100.cuh — thin inline-PTX layer over the Blackwell (sm_100a) async
 // machinery used by the chunkwise kernels: mbarriers with bounded waits, TMA
-// tensor loads (no multicast), TMEM allocation, tcgen05.mma / commit / ld / st,
+// tensor loads into this CTA only, TMEM allocation, tcgen05.mma / commit / ld / st,
 // and the UMMA shared-memory + instruction descriptors.
 //
 // Descriptor bit layouts follow the PTX ISA "tcgen05 matrix descriptors" /
@@ -66,7 +66,7 @@ HXM_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync
 HXM_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // ---------------------------------------------------------------------- TMA --
-// Tiled 4-D load of a box into shared memory, completing on `bar` (no multicast).
+// Tiled 4-D load of a box into this CTA's shared memory, completing on `bar`.
 HXM_DEV void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2, int c3) {
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "

@@ -39,6 +39,9 @@ def lib():
         l.hxm_oracle_mlstm.argtypes = [ct.c_int] * 4 + [fp] * 5 + [ct.c_int, fp, fp, fp]
         l.hxm_oracle_slstm.argtypes = [ct.c_int] * 4 + [fp] * 3 + [ct.c_float, ct.c_int, fp, fp, fp]
         l.hxm_oracle_max_threads.restype = ct.c_int
+        l.hxm_oracle_set_threads.argtypes = [ct.c_int]
+        # all host threads (a launcher may have pinned OMP_NUM_THREADS to 1)
+        l.hxm_oracle_set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count())
         _lib = l
     return _lib
 
