@@ -87,6 +87,19 @@ class SlstmArgs(ct.Structure):
     ]
 
 
+class ConvArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("seqlen", ct.c_int32), ("channels", ct.c_int32), ("width", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("x", ct.c_void_p), ("x_stride", ct.c_int64 * 3),
+        ("weight", ct.c_void_p), ("bias", ct.c_void_p),
+        ("out", ct.c_void_p), ("out_stride", ct.c_int64 * 3),
+        ("init_state", ct.c_void_p), ("final_state", ct.c_void_p),
+        ("activation", ct.c_int32),
+    ]
+
+
 # symbol -> (restype, argtypes)
 SYMBOLS = {
     "hxm_abi_version": (ct.c_int, []),
@@ -98,6 +111,7 @@ SYMBOLS = {
     "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),
     "hxm_ssd_chunk_scan_fwd": (ct.c_int, [ct.POINTER(SsdArgs), ct.c_void_p]),
     "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),
+    "hxm_causal_conv1d_fwd": (ct.c_int, [ct.POINTER(ConvArgs), ct.c_void_p]),
 }
 
 _lib = None

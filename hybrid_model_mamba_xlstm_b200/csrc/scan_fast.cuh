@@ -1,9 +1,13 @@
 // scan_fast.cuh — selective-scan kernel for the dominant layout (sm_100a).
 //
-// Covers dstate <= 16 with u / delta / z / y time-major (unit time stride,
-// 16-byte aligned rows, i.e. (batch, dim, seqlen) memory) and B, C
-// time-major ((batch, dstate, seqlen) memory).  Every other layout runs the
-// generic kernel of scan_kernel.cuh.
+// Covers dstate <= 16 in two layouts (16-byte aligned rows):
+//   time-major:    u / delta / z / y unit time stride ((batch, dim, seqlen)
+//                  memory), B, C unit time stride ((batch, dstate, seqlen));
+//   channel-major: u / delta / z / y unit channel stride ((batch, seqlen, dim)
+//                  memory, views with any row stride, e.g. the x / z halves of
+//                  one in_proj output), B, C unit state stride ((batch, seqlen,
+//                  dstate), e.g. column slices of the x_proj output).
+// Every other layout runs the generic kernel of scan_kernel.cuh.
 //
 // Per CTA: CH channels of one batch row.  Per tile of kT steps, cp.async
 // stages the u / delta / z rows and the raw bf16/fp32 B, C rows (double
@@ -93,19 +97,36 @@ HXM_DEV float fast_step(float r, float dl, float du, float u, const float* __res
   return ys.x + ys.y;
 }
 
-template <typename T, int CH, int kT, bool POW, int ZMODE, bool SP, bool MASK>
+// 8 steps of one channel from a staged tile: time-major rows [CH][kTP] (one
+// 16-byte load) or channel-major rows [kT][CH] (8 conflict-free 2-byte loads).
+template <typename T, int CH, int kT, bool CM>
+HXM_DEV void tile_read8(const T* slot, int tid, int tt, float (&v)[8]) {
+  if (CM) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = to_f32<T>(slot[(tt + j) * CH + tid]);
+  } else {
+    read8<T, CH, kT>(slot + tid * FastSmem<T, CH, kT>::kTP, kTimeMaj, 0, tt, v);
+  }
+}
+template <typename T, int CH, int kT, bool CM>
+HXM_DEV void tile_write8(T* slot, int tid, int tt, const float (&v)[8]) {
+  if (CM) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) slot[(tt + j) * CH + tid] = from_f32<T>(v[j]);
+  } else {
+    write8<T, CH, kT>(slot + tid * FastSmem<T, CH, kT>::kTP, kTimeMaj, 0, tt, v);
+  }
+}
+
+template <typename T, int CH, int kT, bool POW, int ZMODE, bool SP, bool MASK, bool CM>
 HXM_DEV void fast_tile(T* us, const T* ds, const T* zs, const float* __restrict__ bc, int tk, float2 (&h)[8],
                        float a0l2, const float* Arow, float bias, float Dd, int tid) {
-  using S = FastSmem<T, CH, kT>;
-  T* urow = us + tid * S::kTP;
-  const T* drow = ds + tid * S::kTP;
-  const T* zrow = zs + tid * S::kTP;
 #pragma unroll 1
   for (int tt = 0; tt < kT; tt += 8) {
     float uv[8], dv[8], zv[8], yv[8];
-    read8<T, CH, kT>(urow, kTimeMaj, 0, tt, uv);
-    read8<T, CH, kT>(drow, kTimeMaj, 0, tt, dv);
-    if (ZMODE != 0) read8<T, CH, kT>(zrow, kTimeMaj, 0, tt, zv);
+    tile_read8<T, CH, kT, CM>(us, tid, tt, uv);
+    tile_read8<T, CH, kT, CM>(ds, tid, tt, dv);
+    if (ZMODE != 0) tile_read8<T, CH, kT, CM>(zs, tid, tt, zv);
     // phase A: the per-step scalar work of all 8 steps (independent, overlappable)
     float dl[8], du[8], rr[8], gz[8];
 #pragma unroll
@@ -124,11 +145,11 @@ HXM_DEV void fast_tile(T* us, const T* ds, const T* zs, const float* __restrict_
       const float yy = fast_step<false, POW>(rr[j], dl[j], du[j], uv[j], bc + (tt + j) * 32, h, Arow);
       yv[j] = ZMODE == 0 ? fmaf(Dd, uv[j], yy) : fmaf(Dd, uv[j], yy) * gz[j];
     }
-    write8<T, CH, kT>(urow, kTimeMaj, 0, tt, yv);
+    tile_write8<T, CH, kT, CM>(us, tid, tt, yv);
   }
 }
 
-template <typename T, int CH, int kT, int ZMODE, bool SP>
+template <typename T, int CH, int kT, int ZMODE, bool SP, bool CM>
 __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   using S = FastSmem<T, CH, kT>;
   constexpr int kE = 16 / sizeof(T);
@@ -186,22 +207,46 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
       const T* g = which == 0 ? ug : (which == 1 ? dtg : zg);
       const int64_t sd = which == 0 ? p.su[2] : (which == 1 ? p.sdt[2] : p.sz[2]);
       T* slot = base + which * S::kIoSlot;
-      for (int c = tid; c < CH * kChunks; c += CH) {
-        const int ch = c / kChunks, t = (c % kChunks) * kE;
-        const int dd = d0 + ch;
-        const int valid = (dd < p.dim) ? max(0, min(kE, tk - t)) : 0;
-        const T* src = valid > 0 ? g + (int64_t)dd * sd + t0 + t : g;
-        cp_async16(slot + ch * S::kTP + t, src, valid * (int)sizeof(T));
+      if (CM) {
+        // [kT][CH]: step rows of CH channels (sd = time stride)
+        const int64_t st = which == 0 ? p.su[1] : (which == 1 ? p.sdt[1] : p.sz[1]);
+        constexpr int kRowChunks = CH / kE;
+        for (int c = tid; c < kT * kRowChunks; c += CH) {
+          const int t = c / kRowChunks, ch = (c % kRowChunks) * kE;
+          const int valid = (t < tk) ? max(0, min(kE, p.dim - (d0 + ch))) : 0;
+          const T* src = valid > 0 ? g + (int64_t)(t0 + t) * st + d0 + ch : g;
+          cp_async16(slot + t * CH + ch, src, valid * (int)sizeof(T));
+        }
+      } else {
+        for (int c = tid; c < CH * kChunks; c += CH) {
+          const int ch = c / kChunks, t = (c % kChunks) * kE;
+          const int dd = d0 + ch;
+          const int valid = (dd < p.dim) ? max(0, min(kE, tk - t)) : 0;
+          const T* src = valid > 0 ? g + (int64_t)dd * sd + t0 + t : g;
+          cp_async16(slot + ch * S::kTP + t, src, valid * (int)sizeof(T));
+        }
       }
     }
-    // raw B, C rows [2][16][kT]
     T* raw = base + 3 * S::kIoSlot;
-    for (int c = tid; c < 2 * 16 * kChunks; c += CH) {
-      const int row = c / kChunks, t = (c % kChunks) * kE;
-      const int which = row / 16, n = row % 16;
-      const int valid = (n < p.dstate) ? max(0, min(kE, tk - t)) : 0;
-      const T* g = which ? Cg + (int64_t)n * p.sC[2] : Bg + (int64_t)n * p.sB[2];
-      cp_async16(raw + row * S::kTP + t, valid > 0 ? g + t0 + t : Bg, valid * (int)sizeof(T));
+    if (CM) {
+      // raw B, C step rows [kT][B0..15 C0..15]
+      constexpr int kRowChunks = 32 / kE;
+      for (int c = tid; c < kT * kRowChunks; c += CH) {
+        const int t = c / kRowChunks, n = (c % kRowChunks) * kE;
+        const int which = n / 16, n0 = n % 16;
+        const int valid = (t < tk) ? max(0, min(kE, p.dstate - n0)) : 0;
+        const T* g = which ? Cg + (int64_t)(t0 + t) * p.sC[1] + n0 : Bg + (int64_t)(t0 + t) * p.sB[1] + n0;
+        cp_async16(raw + t * 32 + n, valid > 0 ? g : Bg, valid * (int)sizeof(T));
+      }
+    } else {
+      // raw B, C rows [2][16][kT]
+      for (int c = tid; c < 2 * 16 * kChunks; c += CH) {
+        const int row = c / kChunks, t = (c % kChunks) * kE;
+        const int which = row / 16, n = row % 16;
+        const int valid = (n < p.dstate) ? max(0, min(kE, tk - t)) : 0;
+        const T* g = which ? Cg + (int64_t)n * p.sC[2] : Bg + (int64_t)n * p.sB[2];
+        cp_async16(raw + row * S::kTP + t, valid > 0 ? g + t0 + t : Bg, valid * (int)sizeof(T));
+      }
     }
     cp_async_commit();
   };
@@ -219,11 +264,19 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
     {
       const T* raw = stage_ptr(st) + 3 * S::kIoSlot;
       for (int c = tid; c < 32 * (kT / 8); c += CH) {
-        const int col = c % 32, t8 = (c / 32) * 8;
         float v[8];
-        read8<T, CH, kT>(raw + col * S::kTP, kTimeMaj, 0, t8, v);
+        if (CM) {
+          // step rows are already [t][32]: convert 8 consecutive values in place
+          read8<T, CH, kT>(raw + c * 8, kTimeMaj, 0, 0, v);
+          float4* dst = reinterpret_cast<float4*>(bcf + c * 8);
+          dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+          dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+          const int col = c % 32, t8 = (c / 32) * 8;
+          read8<T, CH, kT>(raw + col * S::kTP, kTimeMaj, 0, t8, v);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) bcf[(t8 + j) * 32 + col] = v[j];
+          for (int j = 0; j < 8; ++j) bcf[(t8 + j) * 32 + col] = v[j];
+        }
       }
     }
     __syncthreads();
@@ -232,15 +285,27 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
     const T* zs = us + 2 * S::kIoSlot;
     const float* Arow = Ash + tid * 16;
     if (tk == kT) {
-      if (use_pow) fast_tile<T, CH, kT, true, ZMODE, SP, false>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
-      else fast_tile<T, CH, kT, false, ZMODE, SP, false>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
+      if (use_pow) fast_tile<T, CH, kT, true, ZMODE, SP, false, CM>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
+      else fast_tile<T, CH, kT, false, ZMODE, SP, false, CM>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
     } else {
-      if (use_pow) fast_tile<T, CH, kT, true, ZMODE, SP, true>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
-      else fast_tile<T, CH, kT, false, ZMODE, SP, true>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
+      if (use_pow) fast_tile<T, CH, kT, true, ZMODE, SP, true, CM>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
+      else fast_tile<T, CH, kT, false, ZMODE, SP, true, CM>(us, ds, zs, bcf, tk, h, a0l2, Arow, bias, Dd, tid);
     }
     __syncthreads();
     // y tile (in u's slot) -> global, 16-byte stores along each channel row
-    {
+    if (CM) {
+      constexpr int kRowChunks = CH / kE;
+      for (int c = tid; c < kT * kRowChunks; c += CH) {
+        const int t = c / kRowChunks, ch = (c % kRowChunks) * kE;
+        const int nv = min(kE, p.dim - (d0 + ch));
+        if (t >= tk || nv <= 0) continue;
+        const T* src = us + t * CH + ch;
+        T* dst = yg + (int64_t)(t0 + t) * p.sy[1] + d0 + ch;
+        if (nv == kE) *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+        else
+          for (int j = 0; j < nv; ++j) dst[j] = src[j];
+      }
+    } else {
       constexpr int kChunks = kT / kE;
       for (int c = tid; c < CH * kChunks; c += CH) {
         const int ch = c / kChunks, t = (c % kChunks) * kE;
@@ -264,11 +329,11 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   }
 }
 
-template <typename T, int CH, int kT, int ZMODE, bool SP>
+template <typename T, int CH, int kT, int ZMODE, bool SP, bool CM>
 hxm_status launch_fast(const Params& p, cudaStream_t stream) {
   using S = FastSmem<T, CH, kT>;
   const size_t smem = S::kBytes;
-  auto kern = scan_fast_kernel<T, CH, kT, ZMODE, SP>;
+  auto kern = scan_fast_kernel<T, CH, kT, ZMODE, SP, CM>;
   if (smem > 48 * 1024 - sizeof(float) * CH * 16)
     HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dim + CH - 1) / CH, p.batch);
@@ -276,29 +341,36 @@ hxm_status launch_fast(const Params& p, cudaStream_t stream) {
   return check_launch("hxm_selective_scan_fwd (fast)");
 }
 
-// Can the fast kernel run this request?
-inline bool fast_ok(const Params& p, size_t esize) {
-  if (p.dstate > 16) return false;
-  if (p.mode_u != kTimeMaj || p.mode_dt != kTimeMaj || p.mode_y != kTimeMaj) return false;
-  if (p.z && p.mode_z != kTimeMaj) return false;
+// Which layout the fast kernel can run this request in: 1 time-major,
+// 2 channel-major, 0 neither (generic kernel).
+inline int fast_layout(const Params& p, size_t esize) {
+  if (p.dstate > 16) return 0;
   const int64_t e16 = 16 / (int64_t)esize;
-  auto tm = [&](const void* ptr, const int64_t* s) {
-    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && s[1] == 1 && s[0] % e16 == 0 && s[2] % e16 == 0;
+  auto bc_ok = [&](const void* ptr, const int64_t* s, int unit) {
+    const int o1 = unit == 1 ? 2 : 1;
+    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && s[unit] == 1 && s[0] % e16 == 0 && s[o1] % e16 == 0;
   };
-  return tm(p.B, p.sB) && tm(p.C, p.sC);
+  for (int mode : {(int)kTimeMaj, (int)kChanMaj}) {
+    if (p.mode_u != mode || p.mode_dt != mode || p.mode_y != mode) continue;
+    if (p.z && p.mode_z != mode) continue;
+    const int unit = mode == kTimeMaj ? 1 : 2;  // B, C: unit time stride / unit state stride
+    if (bc_ok(p.B, p.sB, unit) && bc_ok(p.C, p.sC, unit)) return mode == kTimeMaj ? 1 : 2;
+  }
+  return 0;
 }
+inline bool fast_ok(const Params& p, size_t esize) { return fast_layout(p, esize) != 0; }
 
-template <typename T, int CH>
+template <typename T, int CH, bool CM>
 hxm_status pick_fast_modes(const Params& p, cudaStream_t stream) {
   const int zm = p.z ? p.z_mode : 0;
   if (p.softplus) {
-    if (zm == 2) return launch_fast<T, CH, 32, 2, true>(p, stream);
-    if (zm == 1) return launch_fast<T, CH, 32, 1, true>(p, stream);
-    return launch_fast<T, CH, 32, 0, true>(p, stream);
+    if (zm == 2) return launch_fast<T, CH, 32, 2, true, CM>(p, stream);
+    if (zm == 1) return launch_fast<T, CH, 32, 1, true, CM>(p, stream);
+    return launch_fast<T, CH, 32, 0, true, CM>(p, stream);
   }
-  if (zm == 2) return launch_fast<T, CH, 32, 2, false>(p, stream);
-  if (zm == 1) return launch_fast<T, CH, 32, 1, false>(p, stream);
-  return launch_fast<T, CH, 32, 0, false>(p, stream);
+  if (zm == 2) return launch_fast<T, CH, 32, 2, false, CM>(p, stream);
+  if (zm == 1) return launch_fast<T, CH, 32, 1, false, CM>(p, stream);
+  return launch_fast<T, CH, 32, 0, false, CM>(p, stream);
 }
 
 template <typename T>
@@ -310,7 +382,9 @@ hxm_status pick_fast(const Params& p, cudaStream_t stream, int num_sms) {
   };
   int ch = env_knob("HXM_SCAN_CH");
   if (ch != 32 && ch != 64) ch = (eff(64) >= eff(32) - 0.02) ? 64 : 32;
-  return ch == 64 ? pick_fast_modes<T, 64>(p, stream) : pick_fast_modes<T, 32>(p, stream);
+  if (fast_layout(p, sizeof(T)) == 2)
+    return ch == 64 ? pick_fast_modes<T, 64, true>(p, stream) : pick_fast_modes<T, 32, true>(p, stream);
+  return ch == 64 ? pick_fast_modes<T, 64, false>(p, stream) : pick_fast_modes<T, 32, false>(p, stream);
 }
 
 }  // namespace scan

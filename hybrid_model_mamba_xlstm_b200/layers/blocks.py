@@ -10,12 +10,11 @@ state_dict loads unchanged:
                  reproduces the reference, which has none)
   HybridBlock    layers/hybrid_block.py:20-147
 
-The projections are plain GEMMs (torch / cuBLAS); the recurrences are the hxm
-kernels.  Activations are laid out so every kernel gets its fast layout
-without copies: the Mamba branch runs channel-major (batch, dim, seqlen) —
-in_proj, x_proj and dt_proj are computed as W @ X^T — so u, delta, z, B, C
-reach the fused scan time-major, and softplus(dt + dt_proj.bias) and
-y * silu(z) happen inside the scan kernel.
+The projections are plain GEMMs (torch / cuBLAS); the recurrences and the
+Mamba causal conv + SiLU are the hxm kernels.  Activations stay in the GEMMs'
+(batch, seqlen, features) layout: the kernels read strided column views of
+the projection outputs in place, so no transpose or copy runs between them,
+and softplus(dt + dt_proj.bias) and y * silu(z) happen inside the scan.
 """
 from __future__ import annotations
 
@@ -26,7 +25,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from ..kernels.selective_scan.scan_interface import selective_scan_fn
+from ..kernels.conv import causal_conv1d
+from ..kernels.selective_scan.scan_interface import selective_scan_raw
 from ..kernels.slstm import slstm_scan
 from ..kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
 
@@ -67,20 +67,21 @@ class MambaBlock(nn.Module):
         self.out_proj = nn.Linear(self.inner_dim, dim, bias=False)
 
     def forward(self, x, cache=None):
-        bsz, L, _ = x.shape
+        # Everything stays in (B, L, .) layout: the x / z halves of in_proj and
+        # the dt / B / C columns of x_proj are strided views that the conv and
+        # scan kernels read in place (unit channel stride), so no transpose or
+        # copy kernel runs between the GEMMs.
         di, n, r = self.inner_dim, self.state_size, self.dt_rank
-        xt = x.transpose(1, 2)                                   # (B, dim, L) view
-        xz = torch.matmul(self.in_proj.weight, xt)               # (B, 2*di, L) channel-major
-        x_in, z = xz[:, :di], xz[:, di:]
-        u = F.conv1d(F.pad(x_in, (self.conv_size - 1, 0)), self.conv1d.weight, self.conv1d.bias, groups=di)
-        u = F.silu(u)                                            # (B, di, L)
-        dbc = torch.matmul(self.x_proj.weight, u)                # (B, r + 2n, L)
-        dt_low, Bm, Cm = dbc[:, :r], dbc[:, r:r + n], dbc[:, r + n:]
-        delta = torch.matmul(self.dt_proj.weight, dt_low)        # (B, di, L), bias folded into the scan
+        xz = self.in_proj(x)                                     # (B, L, 2*di)
+        x_in, z = xz[..., :di], xz[..., di:]
+        u = causal_conv1d(x_in, self.conv1d.weight, self.conv1d.bias, activation="silu")   # (B, L, di)
+        dbc = self.x_proj(u)                                     # (B, L, r + 2n)
+        dt_low, Bm, Cm = dbc[..., :r], dbc[..., r:r + n], dbc[..., r + n:]
+        delta = F.linear(dt_low, self.dt_proj.weight)            # (B, L, di); bias folded into the scan
         A = -torch.exp(self.A_log.float())
-        y = selective_scan_fn(u, delta, A, Bm, Cm, self.D.float(), z=z, delta_bias=self.dt_proj.bias.float(),
-                              delta_softplus=True)               # (B, di, L)
-        return torch.matmul(y.transpose(1, 2), self.out_proj.weight.t())
+        y = selective_scan_raw(u, delta, A, Bm, Cm, self.D.float(), z, z_mode="silu",
+                               delta_bias=self.dt_proj.bias.float(), delta_softplus=True)   # (B, L, di)
+        return self.out_proj(y)
 
 
 class mLSTMBlock(nn.Module):

@@ -1,0 +1,138 @@
+"""Small, self-contained GPU workloads for profiling one kernel family at a time.
+
+    python -m hybrid_model_mamba_xlstm_b200.profile_cases <case> [sizes...] [--reps N]
+
+Each case builds seeded synthetic inputs on ``cuda:0``, runs the public entry
+point ``reps`` times (default 2: one warm-up launch, one to capture) and prints
+one JSON line with the last launch's CUDA-event time.  The sizes keep the
+device footprint to a few GB so that a profiler capture of one launch ends in
+a minute or two.
+
+cases (default sizes):
+  scan         B L D             (8 4096 4096)   selective_scan_fn, bf16, dstate 16, softplus, y*silu(z)
+  ssd          B L H P N         (8 4096 32 64 128)
+  mlstm        B H L D chunk     (8 8 2048 256 128)  per-head gates
+  mlstm_stream B H L D           (8 4 2048 512)   per-channel gates (key-streaming kernel)
+  slstm        B L H HD          (8 256 4 256)    recurrent R
+  conv         B D L             (8 4096 2048)    causal depthwise conv1d(4) + SiLU
+  mamba_layer  B L               (8 2048)         one hybrid-350M Mamba block
+  prefill      B L               (8 2048)         the hybrid-350M model forward
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+
+def _time(fn, reps):
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    out = None
+    for i in range(reps):
+        if i == reps - 1:
+            ev[0].record()
+        out = fn()
+        if i == reps - 1:
+            ev[1].record()
+    torch.cuda.synchronize()
+    return ev[0].elapsed_time(ev[1]), out
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("sizes", nargs="*", type=int)
+    ap.add_argument("--reps", type=int, default=2)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    s = a.sizes
+
+    if a.case == "scan":
+        from .kernels.selective_scan import selective_scan_fn
+        from .workloads import scan_inputs
+        B, L, D = (s + [8, 4096, 4096][len(s):])[:3]
+        inp = scan_inputs(B, L, D, 16, torch.bfloat16, seed=0, device="cuda", on_device=True)
+        fn = lambda: selective_scan_fn(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, z=inp.z,  # noqa: E731
+                                       delta_bias=inp.delta_bias, delta_softplus=True, return_last_state=True)
+        extra = {"GB/s": None, "bytes": inp.bytes_moved()}
+    elif a.case == "ssd":
+        from .kernels.ssd import ssd_chunk_scan
+        from .workloads import ssd_inputs
+        B, L, H, P, N = (s + [8, 4096, 32, 64, 128][len(s):])[:5]
+        inp = ssd_inputs(B, L, H, P, N, seed=0, device="cuda")
+        fn = lambda: ssd_chunk_scan(inp.x, inp.dt, inp.A, inp.B, inp.C, inp.D)  # noqa: E731
+        extra = {"flops": inp.flops(256)}
+    elif a.case == "mlstm":
+        from .kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
+        from .workloads import mlstm_inputs
+        B, H, L, D, c = (s + [8, 8, 2048, 256, 128][len(s):])[:5]
+        inp = mlstm_inputs(B, H, L, D, torch.bfloat16, seed=0, device="cuda", on_device=True)
+        fn = lambda: mlstm_chunkwise_fwd(inp.q, inp.k, inp.v, inp.log_i, inp.log_f, chunk=c)  # noqa: E731
+        extra = {"flops": inp.flops(c)}
+    elif a.case == "mlstm_stream":
+        from .kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
+        B, H, L, D = (s + [8, 4, 2048, 512][len(s):])[:4]
+        g = torch.Generator(device=dev)
+        g.manual_seed(0)
+        q = (torch.randn(B, H, L, D, generator=g, device=dev) / D ** 0.5).to(torch.bfloat16)
+        k = torch.randn(B, H, L, D, generator=g, device=dev).to(torch.bfloat16)
+        v = torch.randn(B, H, L, D, generator=g, device=dev).to(torch.bfloat16)
+        li = torch.randn(B, H, L, D, generator=g, device=dev) * 0.1
+        lf = torch.nn.functional.logsigmoid(torch.randn(B, H, L, D, generator=g, device=dev) * 0.1)
+        fn = lambda: mlstm_chunkwise_fwd(q, k, v, li, lf)  # noqa: E731
+        extra = {}
+    elif a.case == "slstm":
+        from .kernels.slstm import slstm_scan
+        B, L, H, HD = (s + [8, 256, 4, 256][len(s):])[:4]
+        g = torch.Generator(device=dev)
+        g.manual_seed(0)
+        gates = (torch.randn(B, L, H, 4, HD, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        R = (torch.randn(H, HD, 4 * HD, generator=g, device=dev) / HD ** 0.5).to(torch.bfloat16)
+        w = torch.ones(HD, device=dev)
+        fn = lambda: slstm_scan(gates, w, R=R)  # noqa: E731
+        extra = {"steps": L}
+    elif a.case == "conv":
+        from .kernels.conv import causal_conv1d
+        B, D, L = (s + [8, 4096, 2048][len(s):])[:3]
+        g = torch.Generator(device=dev)
+        g.manual_seed(0)
+        x = torch.randn(B, D, L, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.randn(D, 4, generator=g, device=dev) * 0.5
+        bias = torch.randn(D, generator=g, device=dev) * 0.1
+        fn = lambda: causal_conv1d(x, w, bias, activation="silu")  # noqa: E731
+        extra = {"bytes": 2 * x.numel() * 2}
+    elif a.case in ("mamba_layer", "prefill"):
+        from . import layers as Lyr
+        B, L = (s + [8, 2048][len(s):])[:2]
+        torch.manual_seed(0)
+        if a.case == "mamba_layer":
+            cfg = Lyr.hybrid_350m_config(num_layers=1, layer_pattern=["mamba"])
+            blk = Lyr.HybridLanguageModel(cfg).to(dev).to(torch.bfloat16).eval().layers[0]
+            x = torch.randn(B, L, cfg.dim, device=dev, dtype=torch.bfloat16)
+            fn = lambda: blk(x)  # noqa: E731
+        else:
+            model = Lyr.HybridLanguageModel(Lyr.hybrid_350m_config()).to(dev).to(torch.bfloat16).eval()
+            ids = torch.randint(0, model.config.vocab_size, (B, L), device=dev)
+            fn = lambda: model(ids)  # noqa: E731
+        extra = {"tokens": B * L}
+    else:
+        raise SystemExit(f"unknown case {a.case!r}")
+
+    with torch.no_grad():
+        ms, _ = _time(fn, max(1, a.reps))
+    out = {"case": a.case, "sizes": s, "ms": ms}
+    if "bytes" in extra:
+        out["GB/s"] = extra["bytes"] / ms / 1e6
+    if "flops" in extra:
+        out["TFLOP/s"] = extra["flops"] / ms / 1e9
+    if "tokens" in extra:
+        out["tokens/s"] = extra["tokens"] / ms * 1e3
+    if "steps" in extra:
+        out["us/step"] = ms * 1e3 / extra["steps"]
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -209,6 +209,33 @@ typedef struct hxm_slstm_args {
 
 hxm_status hxm_slstm_scan_fwd(const hxm_slstm_args* args, void* stream);
 
+/* ---- causal depthwise conv1d (+ SiLU) ------------------------------------ */
+/* Replaces the Mamba pre-scan convolution of MambaBlock.forward             */
+/*   (hybrid_xmamba/layers/mamba_block.py:101-104): nn.Conv1d(groups=dim,    */
+/*   padding=width-1) trimmed to the first seqlen outputs, then SiLU:        */
+/*   out[b, t, c] = act(bias[c] + sum_k weight[c, k] * x[b, t - width+1+k, c]) */
+/* with x[b, t < 0, c] taken from init_state (or zero).                      */
+/* x, out: (batch, seqlen, channels) element strides, bf16 / fp32; the       */
+/* channel stride should be 1 (other strides run a slower element kernel).   */
+/* weight (channels, width) fp32 dense; bias (channels) fp32 or NULL;        */
+/* width 1..4.  init_state / final_state: (batch, channels, width-1) in the  */
+/* io dtype, dense, or NULL: the width-1 inputs before t = 0 / the last      */
+/* width-1 inputs (for continuing a sequence).                               */
+typedef struct hxm_conv1d_args {
+  size_t struct_size;
+  int32_t batch, seqlen, channels, width;
+  hxm_dtype io_dtype;
+  const void* x;       int64_t x_stride[3];
+  const float* weight;
+  const float* bias;
+  void* out;           int64_t out_stride[3];
+  const void* init_state;
+  void* final_state;
+  int32_t activation;  /* 0 none, 1 SiLU                                     */
+} hxm_conv1d_args;
+
+hxm_status hxm_causal_conv1d_fwd(const hxm_conv1d_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -22,6 +22,7 @@ __all__ = [
     "ssd_scan",
     "slstm_recurrent",
     "rmsnorm",
+    "causal_conv1d",
 ]
 
 
@@ -51,6 +52,28 @@ def rmsnorm(x, weight, eps=1e-6):
     x = np.asarray(x, dtype=np.float64)
     rms = np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
     return np.asarray(weight, np.float64) * (x / rms)
+
+
+def causal_conv1d(x, weight, bias=None, *, activation=None, init_state=None):
+    """The Mamba pre-scan convolution (hybrid_xmamba/layers/mamba_block.py:101-104):
+    nn.Conv1d(D, D, K, groups=D, padding=K-1) over (B, D, L), trimmed to the
+    first L outputs, optionally followed by SiLU; here on x (B, L, D):
+        out[b, t, c] = bias[c] + sum_k weight[c, k] * x[b, t - (K-1) + k, c]
+    with x before t = 0 from init_state (B, D, K-1) or zero.
+    Returns (out, final_state) — final_state[b, c, j] = x[b, L-(K-1)+j, c]."""
+    x = np.asarray(x, np.float64)
+    w = np.asarray(weight, np.float64).reshape(np.shape(weight)[0], -1)
+    bsz, L, d = x.shape
+    K = w.shape[1]
+    pre = np.zeros((bsz, K - 1, d)) if init_state is None else np.swapaxes(np.asarray(init_state, np.float64), 1, 2)
+    xp = np.concatenate([pre, x], axis=1)                      # (B, K-1+L, D)
+    out = np.zeros((bsz, L, d)) + (0.0 if bias is None else np.asarray(bias, np.float64))
+    for k in range(K):
+        out += w[:, k] * xp[:, k:k + L, :]
+    if activation == "silu":
+        out = silu(out)
+    fin = np.swapaxes(xp[:, xp.shape[1] - (K - 1):, :], 1, 2) if K > 1 else np.zeros((bsz, d, 0))
+    return out, fin
 
 
 def selective_scan(x, dt, A, B, C, D=None, z=None, *, z_mode="mul",

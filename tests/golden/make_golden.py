@@ -15,11 +15,14 @@ What each fixture pins (reference file:line of the code that produced it):
                  the out_proj input are captured with forward hooks
   mamba_block.npz, mlstm_block.npz   layer forwards (mamba_block.py:80-133,
                  mlstm_block.py:77-146) with their state_dicts
+  conv_block.npz the Mamba conv + SiLU (mamba_block.py:97-104), captured with a
+                 forward hook on the block's SiLU module
   hybrid_lm.npz  HybridLanguageModel.forward (hybrid_xmamba/models/hybrid_lm.py:145-209)
                  at a tiny size; sLSTM blocks get the correctly shaped zero cache
                  (the reference crashes without it, slstm_block.py:109-112)
 
-Usage:  python tests/golden/make_golden.py
+Usage:  python tests/golden/make_golden.py [fixture-function ...]
+        (no argument: all fixtures; e.g. ``make_conv`` regenerates one)
 """
 from __future__ import annotations
 
@@ -153,6 +156,24 @@ def make_layers(mb, lb):
                         **{"sd_" + k: v.detach().numpy() for k, v in blk.state_dict().items() if k != "eps"})
 
 
+def make_conv(mb):
+    """The reference MambaBlock's conv + SiLU output (mamba_block.py:101-104),
+    captured at the first call of its SiLU module, and the conv input
+    (the x half of in_proj, mamba_block.py:97-98)."""
+    gen = torch.Generator().manual_seed(5)
+    torch.manual_seed(5)
+    blk = mb.MambaBlock(32, state_size=8, conv_size=4).double()
+    x = torch.randn(2, 40, 32, generator=gen, dtype=torch.float64)
+    seen = []
+    h = blk.activation.register_forward_hook(lambda m, i, o: seen.append(o.detach().clone()))
+    with torch.no_grad():
+        blk(x)
+        x_inner = blk.in_proj(x).chunk(2, dim=-1)[0]
+    h.remove()
+    np.savez_compressed(os.path.join(HERE, "conv_block.npz"), x_inner=x_inner.numpy(), conv_silu=seen[0].numpy(),
+                        weight=blk.conv1d.weight.detach().numpy(), bias=blk.conv1d.bias.detach().numpy())
+
+
 def make_lm(hl, cfgmod, sb):
     orig = sb.sLSTMBlock.forward
 
@@ -182,10 +203,17 @@ def make_lm(hl, cfgmod, sb):
 def main():
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     si, ti, sb, mb, lb, hl, cfgmod = _import_reference()
+    if len(sys.argv) > 1:
+        args = {"make_scan": (si,), "make_tfla": (ti,), "make_slstm": (sb,), "make_layers": (mb, lb),
+                "make_conv": (mb,), "make_lm": (hl, cfgmod, sb)}
+        for name in sys.argv[1:]:
+            globals()[name](*args[name])
+        return
     make_scan(si)
     make_tfla(ti)
     make_slstm(sb)
     make_layers(mb, lb)
+    make_conv(mb)
     make_lm(hl, cfgmod, sb)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):

@@ -38,7 +38,8 @@ def test_abi_version():
 def test_struct_sizes_match_header_layout():
     # the C side checks struct_size == sizeof(struct); a mismatch is HXM_EBADARG
     for cls, fn in [(_lib.ScanArgs, "hxm_selective_scan_fwd"), (_lib.MlstmArgs, "hxm_mlstm_chunkwise_fwd"),
-                    (_lib.SsdArgs, "hxm_ssd_chunk_scan_fwd"), (_lib.SlstmArgs, "hxm_slstm_scan_fwd")]:
+                    (_lib.SsdArgs, "hxm_ssd_chunk_scan_fwd"), (_lib.SlstmArgs, "hxm_slstm_scan_fwd"),
+                    (_lib.ConvArgs, "hxm_causal_conv1d_fwd")]:
         a = cls()
         a.struct_size = ct.sizeof(a) + 8
         st = getattr(_lib.lib(), fn)(ct.byref(a), None)
@@ -70,3 +71,18 @@ def test_python_wrapper_refuses_cpu_tensors():
     x = torch.zeros(1, 4, 8)
     with pytest.raises(RuntimeError, match="CUDA"):
         selective_scan(x, x, torch.zeros(8, 16), torch.zeros(1, 4, 16), torch.zeros(1, 4, 16), torch.ones(8))
+
+
+def test_conv_rejects_bad_arguments_without_cuda():
+    lib = _lib.lib()
+    assert lib.hxm_causal_conv1d_fwd(None, None) == _lib.HXM_EBADARG
+    a = _lib.ConvArgs()
+    a.struct_size = ct.sizeof(a)
+    a.batch, a.seqlen, a.channels, a.width, a.io_dtype = 1, 4, 8, 5, _lib.HXM_BF16
+    assert lib.hxm_causal_conv1d_fwd(ct.byref(a), None) == _lib.HXM_EUNSUPPORTED   # width > 4
+    a.width, a.activation = 4, 3
+    assert lib.hxm_causal_conv1d_fwd(ct.byref(a), None) == _lib.HXM_EBADARG
+    a.activation = 1
+    assert lib.hxm_causal_conv1d_fwd(ct.byref(a), None) == _lib.HXM_EBADARG        # NULL weight
+    a.batch = 0
+    assert lib.hxm_causal_conv1d_fwd(ct.byref(a), None) == _lib.HXM_OK

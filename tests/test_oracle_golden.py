@@ -97,3 +97,22 @@ def test_slstm_recurrent_R_zero_is_reference():
     b = R.slstm_recurrent(g, w, R=np.zeros((2, 8, 32)))
     for u, v in zip(a, b):
         assert np.array_equal(u, v)
+
+
+def test_conv_matches_reference(golden):
+    """The conv restatement reproduces the reference MambaBlock's conv + SiLU."""
+    g = golden("conv_block")
+    out, fin = R.causal_conv1d(g["x_inner"], g["weight"], g["bias"], activation="silu")
+    assert rel_err(out, g["conv_silu"]) < TOL64
+    assert np.array_equal(fin, np.swapaxes(g["x_inner"][:, -3:, :], 1, 2))
+
+
+def test_conv_continuation():
+    """Running two halves with the carried state equals one pass (the state is the last width-1 inputs)."""
+    rng = np.random.default_rng(1)
+    x, w, b = rng.standard_normal((2, 30, 6)), rng.standard_normal((6, 4)), rng.standard_normal(6)
+    whole, fin = R.causal_conv1d(x, w, b, activation="silu")
+    a, s = R.causal_conv1d(x[:, :11], w, b, activation="silu")
+    c, fin2 = R.causal_conv1d(x[:, 11:], w, b, activation="silu", init_state=s)
+    assert np.allclose(np.concatenate([a, c], 1), whole, rtol=0, atol=1e-12)
+    assert np.array_equal(fin, fin2)

@@ -181,3 +181,38 @@ def test_large_workload_sampled_channels(ops):
                                   delta_bias=np64(inp.delta_bias[chans]), delta_softplus=True)
         assert rel_err(np.swapaxes(np64(y[b:b + 1, chans]), 1, 2), yr) < TOL16
         assert rel_err(np64(h[b:b + 1, chans]), hr) < TOL16
+
+
+@pytest.mark.parametrize("shape", [(2, 1000, 200, 16), (3, 37, 40, 8), (1, 4100, 512, 16)])
+def test_bf16_channel_major_fast_path(ops, shape):
+    """(batch, seqlen, dim) memory with unit channel stride — the reference's own
+    selective_scan layout and the Mamba layer's — runs the fast kernel's
+    channel-major variant: softplus(dt + bias), y * silu(z), final state."""
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    b, L, dm, n = shape
+    inp = scan_inputs(b, L, dm, n, torch.bfloat16, seed=2, device="cuda")
+    t = lambda a: a.transpose(1, 2).contiguous()        # (B, L, D) / (B, L, N) dense
+    y, h = ops.selective_scan_raw(t(inp.u), t(inp.delta), inp.A, t(inp.B), t(inp.C), inp.D, t(inp.z), z_mode="silu",
+                                  delta_bias=inp.delta_bias, delta_softplus=True, return_last_state=True)
+    yr, hr = _oracle_bdl(inp)
+    assert rel_err(np64(y), yr) < TOL16
+    assert rel_err(np64(h), hr) < TOL16
+
+
+def test_bf16_channel_major_projection_views(ops):
+    """The Mamba layer's views: x / z halves of one in_proj output and the B / C
+    column slices of the x_proj output (row strides 2*dim and r + 2n)."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    b, L, dm, n, r = 2, 300, 128, 16, 8
+    xz = torch.randn(b, L, 2 * dm, device="cuda", generator=g).to(torch.bfloat16)
+    dbc = torch.randn(b, L, r + 2 * n, device="cuda", generator=g).to(torch.bfloat16)
+    dt = (torch.randn(b, L, dm, device="cuda", generator=g) * 0.5 - 3.0).to(torch.bfloat16)
+    A = -torch.arange(1, n + 1, device="cuda", dtype=torch.float32).repeat(dm, 1)
+    D = torch.ones(dm, device="cuda")
+    bias = torch.full((dm,), -1.0, device="cuda")
+    u, z = xz[..., :dm], xz[..., dm:]
+    Bm, Cm = dbc[..., r:r + n], dbc[..., r + n:]
+    y = ops.selective_scan_raw(u, dt, A, Bm, Cm, D, z, z_mode="silu", delta_bias=bias, delta_softplus=True)
+    yr, _ = R.selective_scan(np64(u), np64(dt), np64(A), np64(Bm), np64(Cm), np64(D), z=np64(z), z_mode="silu",
+                             delta_bias=np64(bias), delta_softplus=True)
+    assert rel_err(np64(y), yr) < TOL16
