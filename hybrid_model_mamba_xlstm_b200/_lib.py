@@ -100,6 +100,19 @@ class ConvArgs(ct.Structure):
     ]
 
 
+class RmsnormArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("rows", ct.c_int64), ("dim", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("x", ct.c_void_p), ("x_row_stride", ct.c_int64),
+        ("residual", ct.c_void_p), ("residual_row_stride", ct.c_int64),
+        ("sum_out", ct.c_void_p), ("sum_row_stride", ct.c_int64),
+        ("weight", ct.c_void_p), ("eps", ct.c_float),
+        ("out", ct.c_void_p), ("out_row_stride", ct.c_int64),
+    ]
+
+
 # symbol -> (restype, argtypes)
 SYMBOLS = {
     "hxm_abi_version": (ct.c_int, []),
@@ -112,6 +125,7 @@ SYMBOLS = {
     "hxm_ssd_chunk_scan_fwd": (ct.c_int, [ct.POINTER(SsdArgs), ct.c_void_p]),
     "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),
     "hxm_causal_conv1d_fwd": (ct.c_int, [ct.POINTER(ConvArgs), ct.c_void_p]),
+    "hxm_rmsnorm_fwd": (ct.c_int, [ct.POINTER(RmsnormArgs), ct.c_void_p]),
 }
 
 _lib = None

@@ -70,44 +70,51 @@ __global__ void __launch_bounds__(128) conv_fast_kernel(const Params p) {
 #pragma unroll
     for (int j = 0; j < V; ++j) win[k][j] = j < nv ? load_x<T>(p, b, t0 - (K - 1) + k, c0 + j) : 0.f;
 
-  const T* xb = static_cast<const T*>(p.x) + b * p.sx[0] + c0;
-  T* ob = static_cast<T*>(p.out) + b * p.so[0] + c0;
+  const T* __restrict__ xb = static_cast<const T*>(p.x) + b * p.sx[0] + c0;
+  T* __restrict__ ob = static_cast<T*>(p.out) + b * p.so[0] + c0;
   const int t_end = min(p.seqlen, t0 + kRun);
-#pragma unroll 8
-  for (int t = t0; t < t_end; ++t) {
-    float xv[V];
+  // groups of 8 steps: the 8 row loads are issued together, then computed
+  for (int tg = t0; tg < t_end; tg += 8) {
+    uint4 raw[8];
     if (nv == V) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(xb + (int64_t)t * p.sx[1]);
-      const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-      for (int j = 0; j < V; ++j) xv[j] = to_f32<T>(e[j]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < V; ++j) xv[j] = j < nv ? to_f32<T>(xb[(int64_t)t * p.sx[1] + j]) : 0.f;
+      for (int i = 0; i < 8; ++i)
+        if (tg + i < t_end) raw[i] = *reinterpret_cast<const uint4*>(xb + (int64_t)(tg + i) * p.sx[1]);
     }
 #pragma unroll
-    for (int j = 0; j < V; ++j) win[K - 1][j] = xv[j];
-    float ov[V];
+    for (int i = 0; i < 8; ++i) {
+      if (tg + i >= t_end) break;
+      if (nv == V) {
+        const T* e = reinterpret_cast<const T*>(&raw[i]);
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-      float acc = bv[j];
+        for (int j = 0; j < V; ++j) win[K - 1][j] = to_f32<T>(e[j]);
+      } else {
 #pragma unroll
-      for (int k = 0; k < K; ++k) acc = fmaf(wv[j][k], win[k][j], acc);
-      ov[j] = act_fn<T>(acc, p.act);
+        for (int j = 0; j < V; ++j) win[K - 1][j] = j < nv ? to_f32<T>(xb[(int64_t)(tg + i) * p.sx[1] + j]) : 0.f;
+      }
+      float ov[V];
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        float acc = bv[j];
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(wv[j][k], win[k][j], acc);
+        ov[j] = act_fn<T>(acc, p.act);
+      }
+      T* dst = ob + (int64_t)(tg + i) * p.so[1];
+      if (nv == V) {
+        uint4 o;
+        T* e = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int j = 0; j < V; ++j) e[j] = from_f32<T>(ov[j]);
+        *reinterpret_cast<uint4*>(dst) = o;
+      } else {
+        for (int j = 0; j < nv; ++j) dst[j] = from_f32<T>(ov[j]);
+      }
+#pragma unroll
+      for (int k = 0; k < K - 1; ++k)
+#pragma unroll
+        for (int j = 0; j < V; ++j) win[k][j] = win[k + 1][j];
     }
-    if (nv == V) {
-      uint4 raw;
-      T* e = reinterpret_cast<T*>(&raw);
-#pragma unroll
-      for (int j = 0; j < V; ++j) e[j] = from_f32<T>(ov[j]);
-      *reinterpret_cast<uint4*>(ob + (int64_t)t * p.so[1]) = raw;
-    } else {
-      for (int j = 0; j < nv; ++j) ob[(int64_t)t * p.so[1] + j] = from_f32<T>(ov[j]);
-    }
-#pragma unroll
-    for (int k = 0; k < K - 1; ++k)
-#pragma unroll
-      for (int j = 0; j < V; ++j) win[k][j] = win[k + 1][j];
   }
 }
 

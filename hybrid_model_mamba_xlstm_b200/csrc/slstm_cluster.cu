@@ -5,12 +5,15 @@
 // 64 KB at hd = 256) is loaded ONCE into registers as mma.sync A fragments,
 // so every step's R^T h_{t-1} for up to 8 batch rows is a handful of
 // register-resident m16n8k16 MMAs.  The per-channel exponential-gate
-// stabilizer m and the cell live in registers.  After the cell update each
-// CTA broadcasts (cell, m, o) of its channels into every CTA's shared memory
-// with st.async stores that complete transaction bytes on the receiver's
-// mbarrier (no separate signal); every CTA then has all hd channels and finishes the
-// RMSNorm over head_dim and h = o*tanh(.) locally — one cluster exchange per
-// step.  Waits are bounded (error flag + early exit, no hang).
+// stabilizer m and the cell live in registers, one (channel, batch row) per
+// thread.  The RMSNorm over head_dim couples the CTAs; each step makes two
+// small cluster exchanges with st.async stores that complete transaction
+// bytes on the receiver's mbarrier (no separate signal):
+//   1. per batch row, this CTA's (max m, sum of squares of its stabilized
+//      cells) — 8 bytes per row to every CTA;
+//   2. after combining the 8 partials into the row's norm, h of this CTA's
+//      channels as bf16, written straight into every CTA's MMA operand.
+// Waits are bounded (error flag + early exit, no hang).
 #include <cuda_bf16.h>
 
 #include "capi_internal.h"
@@ -24,7 +27,11 @@ constexpr int kCL = 8;        // CTAs per cluster (one head)
 constexpr int kBR = 8;        // batch rows per cluster (mma N)
 constexpr int kRing = 2;      // gate pre-activation slots (current, next step)
 
-HXM_DEV float log_sigmoid_f(float x) { return fminf(x, 0.f) - log1pf(__expf(-fabsf(x))); }
+// log(sigmoid(x)) = min(x, 0) - log1p(exp(-|x|)), the log1p on the MUFU pipe
+// as ln2 * lg2(1 + 2^(-|x| log2 e)) (absolute error ~1e-7)
+HXM_DEV float log_sigmoid_f(float x) {
+  return fminf(x, 0.f) - kLn2 * lg2_approx(1.f + ex2_approx(-fabsf(x) * kLog2e));
+}
 
 HXM_DEV uint32_t cluster_rank() {
   uint32_t r;
@@ -36,11 +43,16 @@ HXM_DEV uint32_t map_to_rank(uint32_t local_smem_addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
   return r;
 }
-// 16-byte store into a peer CTA's shared memory that completes 16 bytes of
-// transaction count on the peer's mbarrier (no separate signal needed).
-HXM_DEV void st_async_v4(uint32_t raddr, float4 v, uint32_t rbar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
-               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
+// Stores into a peer CTA's shared memory that complete their byte count of
+// transaction on the peer's mbarrier (no separate signal needed).
+HXM_DEV void st_async_v2(uint32_t raddr, float2 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(raddr),
+               "f"(v.x), "f"(v.y), "r"(rbar)
+               : "memory");
+}
+HXM_DEV void st_async_v4u(uint32_t raddr, uint4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rbar)
                : "memory");
 }
 HXM_DEV void arm_tx(uint64_t* bar, uint32_t bytes) {
@@ -56,6 +68,14 @@ HXM_DEV bool try_wait_cluster(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+// Bounded wait on phase `parity`: false if it gave up (~2 s at the SM clock).
+HXM_DEV bool wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!try_wait_cluster(bar, parity))
+    if (clock64() - t0 > 4000000000ll) return false;
+  return true;
 }
 HXM_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -76,38 +96,41 @@ struct CL {
   static constexpr int kKT = HD / 16;         // k-tiles
   static constexpr int kNT = HD;              // threads per CTA (one m-tile per warp)
   static constexpr int kMW = kMT / (kNT / 32);  // m-tiles per warp (= 1)
-  static constexpr int kTPB = kNT / kBR;      // threads per batch row in the norm phase
-  static constexpr int kCPT = HD / kTPB;      // channels per thread in the norm phase
-  static constexpr int kPairs = kCPC * kBR;   // (channel, batch) pairs per CTA
-  static constexpr int kPPT = kPairs / kNT;
+  static_assert(kCPC * kBR == kNT, "one (channel, batch row) pair per thread");
+  static_assert(kCPC >= 8 && kCPC <= 32, "a batch row's channels sit in one warp, in groups of 8");
+  static constexpr int kHP = HD + 8;          // bf16 row pitch of the MMA operand (16-byte multiple)
   // shared memory (bytes)
-  static constexpr int kX = 0;                                       // float4 [2][kBR][HD]
-  static constexpr int kH = kX + 2 * kBR * HD * 16;                  // bf16 [kBR][HD + 8]
-  static constexpr int kPre = kH + kBR * (HD + 8) * 2;               // float [kBR][kCols]
+  static constexpr int kH = 0;                                       // bf16 [kBR][kHP]
+  static constexpr int kPart = kH + kBR * kHP * 2;                   // float2 [kCL][kBR]
+  static constexpr int kPre = kPart + kCL * kBR * 8;                 // float [kBR][kCols]
   static constexpr int kG = kPre + kBR * kCols * 4;                  // float [kRing][kBR][4][kCPC]
   static constexpr int kW = kG + kRing * kBR * 4 * kCPC * 4;         // float [HD]
   static constexpr int kBar = kW + HD * 4;                           // 2 x uint64
   static constexpr int kBytes = kBar + 32;
+  static constexpr uint32_t kPartTx = kCL * kBR * 8;                 // bytes per exchange-1 phase
+  static constexpr uint32_t kHTx = kBR * HD * 2;                     // bytes per exchange-2 phase
+  static_assert(kH % 16 == 0 && kPart % 16 == 0 && (kHP * 2) % 16 == 0, "st.async alignment");
 };
 
 template <typename T, int HD>
 __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_cluster_kernel(const Params p) {
   using L = CL<HD>;
   extern __shared__ __align__(16) unsigned char sm[];
-  float4* xbuf = reinterpret_cast<float4*>(sm + L::kX);
   __nv_bfloat16* hprev = reinterpret_cast<__nv_bfloat16*>(sm + L::kH);
+  float2* part = reinterpret_cast<float2*>(sm + L::kPart);
   float* pre = reinterpret_cast<float*>(sm + L::kPre);
   float* gring = reinterpret_cast<float*>(sm + L::kG);
   float* wsm = reinterpret_cast<float*>(sm + L::kW);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::kBar);  // [0] partials, [1] h
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rank = (int)cluster_rank();
   const int head = blockIdx.x / kCL;
   const int b0 = blockIdx.y * kBR;
   const int nb = min(kBR, p.batch - b0);
-  const int HDs = HD;
   const int c0 = rank * L::kCPC;  // first channel of this CTA
+  // this thread's (channel, batch row) pair: a row's kCPC channels are kCPC consecutive lanes
+  const int c = tid % L::kCPC, bl = tid / L::kCPC;
 
   // ---- R slice -> mma A fragments (registers), once ------------------------------
   // local column m = q*kCPC + c  <->  R[head][k][q*HD + c0 + c]
@@ -124,8 +147,8 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
         for (int r = 0; r < 4; ++r) {
           const int m = mt * 16 + g + ((r & 1) ? 8 : 0);
           const int k = kt * 16 + t4 * 2 + ((r & 2) ? 8 : 0);
-          const int q = m / L::kCPC, c = m % L::kCPC;
-          const int64_t col = (int64_t)q * HD + c0 + c;
+          const int q = m / L::kCPC, cc = m % L::kCPC;
+          const int64_t col = (int64_t)q * HD + c0 + cc;
           __nv_bfloat162 v;
           v.x = R[(int64_t)k * 4 * HD + col];
           v.y = R[(int64_t)(k + 1) * 4 * HD + col];
@@ -137,40 +160,35 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
   for (int j = tid; j < HD; j += L::kNT) wsm[j] = p.w[j];
   // initial h (bf16 operand) for all channels
   for (int e = tid; e < kBR * HD; e += L::kNT) {
-    const int bl = e / HD, j = e % HD;
+    const int r = e / HD, j = e % HD;
     float hv = 0.f;
-    if (bl < nb && p.h0) hv = p.h0[((int64_t)(b0 + bl) * p.heads + head) * HD + j];
-    hprev[bl * (HD + 8) + j] = __float2bfloat16_rn(hv);
+    if (r < nb && p.h0) hv = p.h0[((int64_t)(b0 + r) * p.heads + head) * HD + j];
+    hprev[r * L::kHP + j] = __float2bfloat16_rn(hv);
   }
   if (tid == 0) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&bars[0])), "r"(1) : "memory");
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&bars[1])), "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    // each phase = one local arrive (with the byte expectation) + kBR*HD*16
-    // bytes of st.async stores from the 8 CTAs; arm steps 0 and 1 before the
-    // start-up cluster barrier so no peer data can precede its arm.
-    arm_tx(&bars[0], kBR * HD * 16);
-    arm_tx(&bars[1], kBR * HD * 16);
+    // each phase = one local arrive (with the byte expectation) + the peers'
+    // st.async bytes; phase 0 of both is armed before the start-up cluster
+    // barrier, so no peer data can precede its arm.
+    arm_tx(&bars[0], L::kPartTx);
+    arm_tx(&bars[1], L::kHTx);
   }
-  // per-thread (channel, batch) pairs: stabilized cell and its log-scale
-  float cs[L::kPPT], ms[L::kPPT];
-#pragma unroll
-  for (int i = 0; i < L::kPPT; ++i) {
-    const int pi = tid + i * L::kNT;
-    const int c = pi % L::kCPC, bl = pi / L::kCPC;
-    cs[i] = (bl < nb && p.c0) ? p.c0[((int64_t)(b0 + bl) * p.heads + head) * HD + c0 + c] : 0.f;
-    ms[i] = 0.f;
-  }
+  // stabilized cell and its log-scale for this thread's pair
+  float cs = (bl < nb && p.c0) ? p.c0[((int64_t)(b0 + bl) * p.heads + head) * HD + c0 + c] : 0.f;
+  float ms = 0.f;
+  const float wc = p.w[c0 + c];
   const T* gsrc = static_cast<const T*>(p.gates);
-  // gate pre-activations of step t: element e = (bl, q, c) of this CTA's slice
+  // gate pre-activations of step t: element e = (row, q, channel) of this CTA's slice
   constexpr int kGE = (kBR * 4 * L::kCPC) / L::kNT;
   auto fetch_gates = [&](int t, float (&v)[kGE]) {
 #pragma unroll
     for (int i = 0; i < kGE; ++i) {
       const int e = tid + i * L::kNT;
-      const int c = e % L::kCPC, q = (e / L::kCPC) % 4, bl = e / (4 * L::kCPC);
-      v[i] = (bl < nb && t < p.seqlen)
-                 ? to_f32<T>(gsrc[(((int64_t)(b0 + bl) * p.seqlen + t) * p.heads + head) * 4 * HD + q * HD + c0 + c])
+      const int cc = e % L::kCPC, q = (e / L::kCPC) % 4, r = e / (4 * L::kCPC);
+      v[i] = (r < nb && t < p.seqlen)
+                 ? to_f32<T>(gsrc[(((int64_t)(b0 + r) * p.seqlen + t) * p.heads + head) * 4 * HD + q * HD + c0 + cc])
                  : 0.f;
     }
   };
@@ -179,43 +197,41 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
 #pragma unroll
     for (int i = 0; i < kGE; ++i) dst[tid + i * L::kNT] = v[i];
   };
-  auto load_gates = [&](int t) {
+  {
     float v[kGE];
-    fetch_gates(t, v);
-    store_gates(t, v);
-  };
-  load_gates(0);
+    fetch_gates(0, v);
+    store_gates(0, v);
+  }
   __syncthreads();
   cluster_sync();  // every CTA's barriers initialized before any remote arrive
 
-  uint32_t xaddr0 = smem_u32(xbuf);
-  uint32_t baddr0 = smem_u32(&bars[0]);
+  const uint32_t part_addr = smem_u32(part + rank * kBR + bl);                 // my slot in every peer
+  const uint32_t h_addr = smem_u32(hprev + bl * L::kHP + c0 + c);              // my channels in every peer
+  const uint32_t bar_part = smem_u32(&bars[0]), bar_h = smem_u32(&bars[1]);
   T* hout = static_cast<T*>(p.h_out);
   bool bad = false;
-  float hlast[L::kCPT];
-#pragma unroll
-  for (int i = 0; i < L::kCPT; ++i) hlast[i] = 0.f;
+  float hlast = 0.f;
 
   for (int t = 0; t < p.seqlen; ++t) {
-    const int par = t & 1;
+    const uint32_t parity = t & 1;
     float gnext[kGE];
     fetch_gates(t + 1, gnext);  // consumed at the end of the step: latency hidden behind the step
-    // (a) gate pre-activations R^T h_{t-1}: D[m][n] (m = gate column, n = batch row)
+    // (a) gate pre-activations R^T h_{t-1}: D[m][n] (m = gate column, n = batch row), 4 MMA chains
     {
       const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
       for (int mw = 0; mw < L::kMW; ++mw) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // two independent chains
+        float acc[4][4] = {};
 #pragma unroll
         for (int kt = 0; kt < L::kKT; ++kt) {
-          const __nv_bfloat16* hb = hprev + g * (HD + 8) + kt * 16 + t4 * 2;
+          const __nv_bfloat16* hb = hprev + g * L::kHP + kt * 16 + t4 * 2;
           const uint32_t b0r = *reinterpret_cast<const uint32_t*>(hb);
           const uint32_t b1r = *reinterpret_cast<const uint32_t*>(hb + 8);
-          if (kt & 1) mma_16816(e, afr[mw][kt], b0r, b1r);
-          else mma_16816(d, afr[mw][kt], b0r, b1r);
+          mma_16816(acc[kt & 3], afr[mw][kt], b0r, b1r);
         }
+        float d[4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) d[r] += e[r];
+        for (int r = 0; r < 4; ++r) d[r] = (acc[0][r] + acc[1][r]) + (acc[2][r] + acc[3][r]);
         const int m = (warp * L::kMW + mw) * 16 + g;
         pre[(2 * t4) * L::kCols + m] = d[0];
         pre[(2 * t4 + 1) * L::kCols + m] = d[1];
@@ -224,100 +240,87 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
       }
     }
     __syncthreads();
-    // (b) cell update of own (channel, batch) pairs; broadcast (cell, m, o) to the cluster
+    // (b) cell update of this thread's pair; per-row partial (max m, sum of squares) to every CTA
+    float og;
     {
       const float* gt = gring + (t % kRing) * kBR * 4 * L::kCPC;
+      float gp[4];
 #pragma unroll
-      for (int i = 0; i < L::kPPT; ++i) {
-        const int pi = tid + i * L::kNT;
-        const int c = pi % L::kCPC, bl = pi / L::kCPC;
-        float gp[4];
+      for (int q = 0; q < 4; ++q) gp[q] = pre[bl * L::kCols + q * L::kCPC + c] + gt[(bl * 4 + q) * L::kCPC + c];
+      const float lf = log_sigmoid_f(gp[1]);
+      const float li = p.exp_gate ? gp[0] : log_sigmoid_f(gp[0]);
+      const float mn = fmaxf(ms + lf, li);
+      cs = ex2_approx((ms + lf - mn) * kLog2e) * cs + ex2_approx((li - mn) * kLog2e) * tanh_approx(gp[3]);
+      ms = mn;
+      og = fmaf(0.5f, tanh_approx(0.5f * gp[2]), 0.5f);
+      float mloc = ms;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) gp[q] = pre[bl * L::kCols + q * L::kCPC + c] + gt[(bl * 4 + q) * L::kCPC + c];
-        const float lf = log_sigmoid_f(gp[1]);
-        const float li = p.exp_gate ? gp[0] : log_sigmoid_f(gp[0]);
-        const float mn = fmaxf(ms[i] + lf, li);
-        cs[i] = __expf(ms[i] + lf - mn) * cs[i] + __expf(li - mn) * tanh_approx(gp[3]);
-        ms[i] = mn;
-        const float og = fmaf(0.5f, tanh_approx(0.5f * gp[2]), 0.5f);
-        const float4 v = make_float4(cs[i], ms[i], og, 0.f);
-        const uint32_t off = (uint32_t)(((par * kBR + bl) * HDs + c0 + c) * 16);
+      for (int o = L::kCPC / 2; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+      const float sc = ex2_approx((ms - mloc) * kLog2e) * cs;
+      float sloc = sc * sc;
 #pragma unroll
-        for (int r = 0; r < kCL; ++r) st_async_v4(map_to_rank(xaddr0 + off, r), v, map_to_rank(baddr0 + par * 8, r));
+      for (int o = L::kCPC / 2; o > 0; o >>= 1) sloc += __shfl_xor_sync(0xffffffffu, sloc, o);
+      if (c == 0) {
+#pragma unroll
+        for (int r = 0; r < kCL; ++r)
+          st_async_v2(map_to_rank(part_addr, r), make_float2(mloc, sloc), map_to_rank(bar_part, r));
       }
     }
-    // (c) wait for all 8 slices (bounded)
-    {
-      const uint32_t parity = (t >> 1) & 1;
-      if (!try_wait_cluster(&bars[par], parity)) {
-        const long long t0 = clock64();
-        while (!try_wait_cluster(&bars[par], parity)) {
-          if (clock64() - t0 > 4000000000ll) {
-            bad = true;
-            break;
-          }
-        }
-      }
-    }
+    // (c) wait for the 8 partials of every row (bounded), then re-arm for step
+    //     t + 1 before the barrier below: peers send step t + 1 partials only
+    //     after their step t + 1 MMA, which needs this CTA's step t h, sent
+    //     after that barrier.
+    bad = !wait_bounded(&bars[0], parity);
+    if (tid == 0 && !bad && t + 1 < p.seqlen) arm_tx(&bars[0], L::kPartTx);
     if (__syncthreads_or(bad)) {
       bad = true;
       break;
     }
-    // re-arm this buffer's barrier for step t + 2.  Peers can only send step
-    // t + 2 after waiting on step t + 1, which needs this CTA's step t + 1
-    // stores — issued after this point — so the arm always precedes the data.
-    if (tid == 0 && t + 2 < p.seqlen) arm_tx(&bars[par], kBR * HD * 16);
-    // (d) RMSNorm over head_dim and h for every channel (kTPB threads per batch row)
+    // (d) the row's norm from the 8 partials; h of this pair; bf16 h of 8
+    //     consecutive channels to every CTA's MMA operand
     {
-      const int bl = tid / L::kTPB, sub = tid % L::kTPB;
-      const float4* xr = xbuf + (par * kBR + bl) * HD;
       float M = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < L::kCPT; ++i) M = fmaxf(M, xr[sub + L::kTPB * i].y);
-#pragma unroll
-      for (int o = L::kTPB / 2; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      for (int k = 0; k < kCL; ++k) M = fmaxf(M, part[k * kBR + bl].x);
       float S = 0.f;
 #pragma unroll
-      for (int i = 0; i < L::kCPT; ++i) {
-        const float4 x = xr[sub + L::kTPB * i];
-        const float sc = __expf(x.y - M) * x.x;
-        S = fmaf(sc, sc, S);
+      for (int k = 0; k < kCL; ++k) {
+        const float2 pk = part[k * kBR + bl];
+        const float e = ex2_approx((pk.x - M) * kLog2e);
+        S = fmaf(e * e, pk.y, S);
       }
+      const float rinv = rsqrtf(S / HD + p.eps * ex2_approx(-2.f * M * kLog2e));
+      const float hv = og * tanh_approx(wc * ex2_approx((ms - M) * kLog2e) * cs * rinv);
+      hlast = hv;
+      if (bl < nb) hout[(((int64_t)(b0 + bl) * p.seqlen + t) * p.heads + head) * HD + c0 + c] = from_f32<T>(hv);
+      // pack: lane pairs -> bf16x2, then 4 pairs -> 16 bytes at the group's first lane
+      const float hn = __shfl_down_sync(0xffffffffu, hv, 1);
+      __nv_bfloat162 pr = __floats2bfloat162_rn(hv, hn);
+      const uint32_t w0 = *reinterpret_cast<uint32_t*>(&pr);
+      const uint32_t w1 = __shfl_down_sync(0xffffffffu, w0, 2);
+      const uint32_t w2 = __shfl_down_sync(0xffffffffu, w0, 4);
+      const uint32_t w3 = __shfl_down_sync(0xffffffffu, w0, 6);
+      if ((c & 7) == 0) {
+        const uint4 v = make_uint4(w0, w1, w2, w3);
 #pragma unroll
-      for (int o = L::kTPB / 2; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-      const float rinv = rsqrtf(S / HD + p.eps * __expf(-2.f * M));
-#pragma unroll
-      for (int i = 0; i < L::kCPT; ++i) {
-        const int j = sub + L::kTPB * i;
-        const float4 x = xr[j];
-        const float hv = x.z * tanh_approx(wsm[j] * __expf(x.y - M) * x.x * rinv);
-        hprev[bl * (HD + 8) + j] = __float2bfloat16_rn(hv);
-        hlast[i] = hv;
-        if (bl < nb && j >= c0 && j < c0 + L::kCPC)
-          hout[(((int64_t)(b0 + bl) * p.seqlen + t) * p.heads + head) * HD + j] = from_f32<T>(hv);
+        for (int r = 0; r < kCL; ++r) st_async_v4u(map_to_rank(h_addr, r), v, map_to_rank(bar_h, r));
       }
     }
     store_gates(t + 1, gnext);
-    __syncthreads();
+    // (e) wait for every CTA's h (bounded); it lands directly in hprev.  Re-arm
+    //     for step t + 1 first: peers send step t + 1 h only after this CTA's
+    //     step t + 1 partials, sent after the barrier below.
+    bad = !wait_bounded(&bars[1], parity);
+    if (tid == 0 && !bad && t + 1 < p.seqlen) arm_tx(&bars[1], L::kHTx);
+    if (__syncthreads_or(bad)) {
+      bad = true;
+      break;
+    }
   }
 
   if (!bad) {
-    const int bl = tid / L::kTPB, sub = tid % L::kTPB;
-    if (p.hT && bl < nb) {
-#pragma unroll
-      for (int i = 0; i < L::kCPT; ++i) {
-        const int j = sub + L::kTPB * i;
-        if (j >= c0 && j < c0 + L::kCPC) p.hT[((int64_t)(b0 + bl) * p.heads + head) * HD + j] = hlast[i];
-      }
-    }
-    if (p.cT) {
-#pragma unroll
-      for (int i = 0; i < L::kPPT; ++i) {
-        const int pi = tid + i * L::kNT;
-        const int c = pi % L::kCPC, bl2 = pi / L::kCPC;
-        if (bl2 < nb) p.cT[((int64_t)(b0 + bl2) * p.heads + head) * HD + c0 + c] = __expf(ms[i]) * cs[i];
-      }
-    }
+    if (p.hT && bl < nb) p.hT[((int64_t)(b0 + bl) * p.heads + head) * HD + c0 + c] = hlast;
+    if (p.cT && bl < nb) p.cT[((int64_t)(b0 + bl) * p.heads + head) * HD + c0 + c] = ex2_approx(ms * kLog2e) * cs;
   } else if (tid == 0 && p.error_flag) {
     atomicExch(p.error_flag, 1);
   }

@@ -1,12 +1,13 @@
 """B200 kernels behind the reference's kernel entry points
 (hybrid_xmamba/kernels/__init__.py:3-9): ``apply_tfla`` and ``selective_scan``,
 plus the extended entries ``selective_scan_fn``, ``mlstm_chunkwise_fwd``,
-``ssd_chunk_scan``, ``slstm_scan`` and ``causal_conv1d``."""
+``ssd_chunk_scan``, ``slstm_scan``, ``causal_conv1d`` and ``rmsnorm``."""
 from .selective_scan.scan_interface import selective_scan, selective_scan_fn
 from .tfla.tfla_interface import apply_tfla, mlstm_chunkwise_fwd
 from .ssd import ssd_chunk_scan
 from .slstm import slstm_scan
 from .conv import causal_conv1d
+from .norm import rmsnorm
 
 __all__ = ["apply_tfla", "selective_scan", "selective_scan_fn", "mlstm_chunkwise_fwd", "ssd_chunk_scan",
-           "slstm_scan", "causal_conv1d"]
+           "slstm_scan", "causal_conv1d", "rmsnorm"]

@@ -26,23 +26,26 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..kernels.conv import causal_conv1d
+from ..kernels.norm import rmsnorm
 from ..kernels.selective_scan.scan_interface import selective_scan_raw
 from ..kernels.slstm import slstm_scan
 from ..kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
 
 
 class RMSNorm(nn.Module):
-    """w * x / sqrt(mean(x^2) + eps) over the last dim (normalization.py:8-34)."""
+    """w * x / sqrt(mean(x^2) + eps) over the last dim (normalization.py:8-34),
+    one pass of the hxm RMSNorm kernel."""
 
     def __init__(self, dim: int, eps: float = 1e-6):
         super().__init__()
         self.eps = eps
         self.weight = nn.Parameter(torch.ones(dim))
 
-    def forward(self, x):
-        xf = x.float()
-        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
-        return (self.weight.float() * y).to(x.dtype)
+    def forward(self, x, residual=None):
+        """RMSNorm(x), or with ``residual``: (RMSNorm(x + residual), x + residual)."""
+        if residual is None:
+            return rmsnorm(x, self.weight, self.eps)
+        return rmsnorm(x, self.weight, self.eps, residual=residual, return_sum=True)
 
 
 class MambaBlock(nn.Module):
@@ -74,14 +77,28 @@ class MambaBlock(nn.Module):
         di, n, r = self.inner_dim, self.state_size, self.dt_rank
         xz = self.in_proj(x)                                     # (B, L, 2*di)
         x_in, z = xz[..., :di], xz[..., di:]
-        u = causal_conv1d(x_in, self.conv1d.weight, self.conv1d.bias, activation="silu")   # (B, L, di)
+        u = causal_conv1d(x_in, self.conv1d.weight, self.conv1d.bias, activation="silu")  # (B, L, di)
         dbc = self.x_proj(u)                                     # (B, L, r + 2n)
         dt_low, Bm, Cm = dbc[..., :r], dbc[..., r:r + n], dbc[..., r + n:]
         delta = F.linear(dt_low, self.dt_proj.weight)            # (B, L, di); bias folded into the scan
-        A = -torch.exp(self.A_log.float())
-        y = selective_scan_raw(u, delta, A, Bm, Cm, self.D.float(), z, z_mode="silu",
-                               delta_bias=self.dt_proj.bias.float(), delta_softplus=True)   # (B, L, di)
+        A, D, dt_bias = self._scan_params()
+        y = selective_scan_raw(u, delta, A, Bm, Cm, D, z, z_mode="silu", delta_bias=dt_bias,
+                               delta_softplus=True)                                        # (B, L, di)
         return self.out_proj(y)
+
+    def _scan_params(self):
+        """fp32 A = -exp(A_log), D and dt_proj.bias; cached while the parameters
+        are unchanged and no gradient is being recorded (inference)."""
+        params = (self.A_log, self.D, self.dt_proj.bias)
+        derive = lambda: (-torch.exp(self.A_log.float()), self.D.float(), self.dt_proj.bias.float())
+        if torch.is_grad_enabled() and any(p.requires_grad for p in params):
+            return derive()
+        key = tuple((p.data_ptr(), p._version, p.device) for p in params)
+        if getattr(self, "_scan_key", None) != key:
+            with torch.no_grad():
+                self._scan_val = derive()
+            self._scan_key = key
+        return self._scan_val
 
 
 class mLSTMBlock(nn.Module):
@@ -115,9 +132,10 @@ class mLSTMBlock(nn.Module):
             x_inner, x_gate = xp.chunk(2, dim=-1)
         else:
             x_inner = x_gate = xp
-        heads = lambda t: t.view(bsz, L, nh, hd).transpose(1, 2)   # (B, H, L, hd)
-        q = self.q_norm(heads(self.q_proj(x_inner))).contiguous()
-        k = self.k_norm(heads(self.k_proj(x_inner))).contiguous()
+        split = lambda t: t.view(bsz, L, nh, hd)                    # (B, L, H, hd) rows of hd
+        heads = lambda t: split(t).transpose(1, 2)                  # (B, H, L, hd)
+        q = self.q_norm(split(self.q_proj(x_inner))).transpose(1, 2).contiguous()
+        k = self.k_norm(split(self.k_proj(x_inner))).transpose(1, 2).contiguous()
         v = heads(self.v_proj(x_inner)).contiguous()
         log_i = heads(self.i_gate_proj(x_inner).float())            # log of i = exp(pre)
         log_f = heads(F.logsigmoid(self.f_gate_proj(x_inner).float()))
@@ -196,7 +214,29 @@ class HybridBlock(nn.Module):
             self.norm2 = self.mlp = None
 
     def forward(self, x, cache=None):
-        x = x + self.mixer(self.norm1(x), cache=cache)
-        if self.use_mlp:
-            x = x + self.mlp(self.norm2(x))
-        return x
+        out, pending = self.forward_pending(x, None, cache=cache)
+        return out + pending if pending is not None else out
+
+    def forward_pending(self, x, pending, cache=None):
+        """The block with its last residual add left pending: returns (x, d)
+        with the block output = x + d (d None when nothing is pending).  A
+        pending add from the previous block is fused into norm1, and the mixer's
+        residual add into norm2 (one RMSNorm kernel pass each)."""
+        fused = isinstance(self.norm1, RMSNorm)
+        if pending is not None:
+            if fused:
+                h, x = self.norm1(pending, residual=x)
+            else:
+                x = x + pending
+                h = self.norm1(x)
+        else:
+            h = self.norm1(x)
+        m = self.mixer(h, cache=cache)
+        if not self.use_mlp:
+            return x, m
+        if fused:
+            h2, x = self.norm2(m, residual=x)
+        else:
+            x = x + m
+            h2 = self.norm2(x)
+        return x, self.mlp(h2)

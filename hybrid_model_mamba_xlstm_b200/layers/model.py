@@ -117,9 +117,15 @@ class HybridLanguageModel(nn.Module):
 
     def forward(self, input_ids, return_hidden=False):
         h = self.embeddings.token_embedding(input_ids)
+        pending = None  # each block's last residual add is fused into the next RMSNorm
         for layer in self.layers:
-            h = layer(h)
-        h = self.final_norm(h)
+            h, pending = layer.forward_pending(h, pending)
+        if pending is None:
+            h = self.final_norm(h)
+        elif isinstance(self.final_norm, RMSNorm):
+            h, _ = self.final_norm(pending, residual=h)
+        else:
+            h = self.final_norm(h + pending)
         if return_hidden:
             return h
         return self.lm_head(h)

@@ -236,6 +236,29 @@ typedef struct hxm_conv1d_args {
 
 hxm_status hxm_causal_conv1d_fwd(const hxm_conv1d_args* args, void* stream);
 
+/* ---- RMSNorm (optionally fused with the residual add before it) ---------- */
+/* Replaces RMSNorm.forward (hybrid_xmamba/layers/normalization.py:32-34):   */
+/*   out = weight * s / sqrt(mean(s^2) + eps)   over the last dim            */
+/* where s = x, or s = x + residual (the residual adds of HybridBlock.forward,*/
+/* hybrid_xmamba/layers/hybrid_block.py:125,132) rounded to the io dtype and  */
+/* also written to sum_out when it is not NULL (it may alias x or residual). */
+/* Rows of dim contiguous elements, bf16 / fp32, row strides in elements;    */
+/* weight (dim) fp32 or NULL (ones).                                         */
+typedef struct hxm_rmsnorm_args {
+  size_t struct_size;
+  int64_t rows;
+  int32_t dim;
+  hxm_dtype io_dtype;
+  const void* x;        int64_t x_row_stride;
+  const void* residual; int64_t residual_row_stride;
+  void* sum_out;        int64_t sum_row_stride;
+  const float* weight;
+  float eps;
+  void* out;            int64_t out_row_stride;
+} hxm_rmsnorm_args;
+
+hxm_status hxm_rmsnorm_fwd(const hxm_rmsnorm_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
