@@ -56,6 +56,8 @@ class MlstmArgs(ct.Structure):
         ("C0", ct.c_void_p), ("n0", ct.c_void_p), ("m0", ct.c_void_p),
         ("CT", ct.c_void_p), ("nT", ct.c_void_p), ("mT", ct.c_void_p),
         ("workspace", ct.c_void_p), ("workspace_bytes", ct.c_size_t),
+        ("q_tstride", ct.c_int64), ("k_tstride", ct.c_int64), ("v_tstride", ct.c_int64),
+        ("h_tstride", ct.c_int64), ("i_tstride", ct.c_int64), ("f_tstride", ct.c_int64),
     ]
 
 

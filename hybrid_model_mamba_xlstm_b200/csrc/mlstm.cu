@@ -30,6 +30,7 @@ static hxm_status fill(const hxm_mlstm_args* a, Params& p) {
     p.si[i] = a->i_stride[i]; p.sf[i] = a->f_stride[i]; p.sh[i] = a->h_stride[i];
   }
   p.C0 = a->C0; p.n0 = a->n0; p.m0 = a->m0; p.CT = a->CT; p.nT = a->nT; p.mT = a->mT;
+  hxm::mlstm::set_time_strides(p, a);
   p.workspace = a->workspace; p.workspace_bytes = a->workspace_bytes;
   return HXM_OK;
 }

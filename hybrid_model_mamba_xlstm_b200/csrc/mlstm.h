@@ -32,7 +32,19 @@ struct Params {
   float* mT;
   void* workspace;
   size_t workspace_bytes;
+  int64_t tq, tk, tv, th, ti, tf;  // time strides (elements)
 };
+
+// Time strides from the ABI struct (0 = dense).
+inline void set_time_strides(Params& p, const hxm_mlstm_args* a) {
+  const int64_t g = p.gate_mode == 1 ? p.dqk : 1;
+  p.tq = a->q_tstride ? a->q_tstride : p.dqk;
+  p.tk = a->k_tstride ? a->k_tstride : p.dqk;
+  p.tv = a->v_tstride ? a->v_tstride : p.dv;
+  p.th = a->h_tstride ? a->h_tstride : p.dv;
+  p.ti = a->i_tstride ? a->i_tstride : g;
+  p.tf = a->f_tstride ? a->f_tstride : g;
+}
 
 // Exact step-by-step recurrence on CUDA cores (any gate mode / dtype / dims <= 512).
 hxm_status launch_recurrent(const Params& p, cudaStream_t st);

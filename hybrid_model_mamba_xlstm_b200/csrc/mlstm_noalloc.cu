@@ -79,6 +79,7 @@ extern "C" hxm_status hxm_mlstm_chunkwise_fwd_noalloc(const hxm_mlstm_args* a, v
     p.si[i] = a->i_stride[i]; p.sf[i] = a->f_stride[i]; p.sh[i] = a->h_stride[i];
   }
   p.C0 = a->C0; p.n0 = a->n0; p.m0 = a->m0; p.CT = a->CT; p.nT = a->nT; p.mT = a->mT;
+  hxm::mlstm::set_time_strides(p, a);
   if (p.batch == 0 || p.heads == 0 || p.seqlen == 0) {
     hxm::set_error("hxm_mlstm_chunkwise_fwd_noalloc: empty problem (batch, heads and seqlen must be > 0)");
     return HXM_EBADARG;

@@ -54,7 +54,6 @@ __global__ void __launch_bounds__(kThreads) mlstm_recurrent_kernel(const Params 
   T* hg = static_cast<T*>(p.h) + b * p.sh[0] + hh * p.sh[1];
   const float* lig = p.log_i + b * p.si[0] + hh * p.si[1];
   const float* lfg = p.log_f + b * p.sf[0] + hh * p.sf[1];
-  const int gstride = p.gate_mode ? dqk : 1;
 
   // state: rows j = rg + kRG*r of column `col`
   float C[RPT];
@@ -81,9 +80,9 @@ __global__ void __launch_bounds__(kThreads) mlstm_recurrent_kernel(const Params 
     for (int r2 = 0; r2 < kRows2; ++r2) {
       const int j = tid + kThreads * r2;
       if (j < dqk) {
-        const float li = lig[(int64_t)t * gstride + (p.gate_mode ? j : 0)];
-        const float lf = lfg[(int64_t)t * gstride + (p.gate_mode ? j : 0)];
-        const float kj = to_f32<T>(kg[(int64_t)t * dqk + j]);
+        const float li = lig[(int64_t)t * p.ti + (p.gate_mode ? j : 0)];
+        const float lf = lfg[(int64_t)t * p.tf + (p.gate_mode ? j : 0)];
+        const float kj = to_f32<T>(kg[(int64_t)t * p.tk + j]);
         const float mn = fmaxf(m_row[r2] + lf, li);
         const float a = __expf(m_row[r2] + lf - mn);
         const float bk = __expf(li - mn) * kj;
@@ -94,7 +93,7 @@ __global__ void __launch_bounds__(kThreads) mlstm_recurrent_kernel(const Params 
         mloc = fmaxf(mloc, mn);
       }
     }
-    if (tid < kE) v_s[tid] = (e0 + tid < p.dv) ? to_f32<T>(vg[(int64_t)t * p.dv + e0 + tid]) : 0.f;
+    if (tid < kE) v_s[tid] = (e0 + tid < p.dv) ? to_f32<T>(vg[(int64_t)t * p.tv + e0 + tid]) : 0.f;
     // block max of m'
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
@@ -109,7 +108,7 @@ __global__ void __launch_bounds__(kThreads) mlstm_recurrent_kernel(const Params 
     for (int r2 = 0; r2 < kRows2; ++r2) {
       const int j = tid + kThreads * r2;
       if (j < dqk) {
-        const float qt = to_f32<T>(qg[(int64_t)t * dqk + j]) * __expf(m_row[r2] - M);
+        const float qt = to_f32<T>(qg[(int64_t)t * p.tq + j]) * __expf(m_row[r2] - M);
         q_s[j] = qt;
         dloc = fmaf(qt, n_row[r2], dloc);
       }
@@ -139,7 +138,7 @@ __global__ void __launch_bounds__(kThreads) mlstm_recurrent_kernel(const Params 
 #pragma unroll
       for (int w = 0; w < kThreads / 32; ++w) den += red[8 + w];
       const float hv = num / fmaxf(den, __expf(-M));
-      if (e0 + tid < p.dv) hg[(int64_t)t * p.dv + e0 + tid] = from_f32<T>(hv);
+      if (e0 + tid < p.dv) hg[(int64_t)t * p.th + e0 + tid] = from_f32<T>(hv);
     }
     __syncthreads();
   }

@@ -54,19 +54,18 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
   const float* li = p.log_i + b * p.si[0] + h * p.si[1];
   const float* lf = p.log_f + b * p.sf[0] + h * p.sf[1];
   const bool pc = p.gate_mode == 1;
-  const int64_t gs = pc ? p.dqk : 1;
   const int gj = pc ? j : 0;
   float g = 0.f;
-  for (int t = 0; t < tn; ++t) g += lf[(int64_t)(t0 + t) * gs + gj];
+  for (int t = 0; t < tn; ++t) g += lf[(int64_t)(t0 + t) * p.tf + gj];
   const float rho = 0.5f * g;
   const int64_t ob = (int64_t)bh * p.seqlen * p.dqk;
   float bt = 0.f;
   for (int t = 0; t < tn; ++t) {
     const int64_t tt = t0 + t;
-    bt += lf[tt * gs + gj];
-    const float lit = li[tt * gs + gj];
-    const float qv = to_f32<T>(q[tt * p.dqk + j]);
-    const float kv = to_f32<T>(k[tt * p.dqk + j]);
+    bt += lf[tt * p.tf + gj];
+    const float lit = li[tt * p.ti + gj];
+    const float qv = to_f32<T>(q[tt * p.tq + j]);
+    const float kv = to_f32<T>(k[tt * p.tk + j]);
     Qs[ob + tt * p.dqk + j] = __float2bfloat16_rn(qv * __expf(bt - rho));
     Ks[ob + tt * p.dqk + j] = __float2bfloat16_rn(kv * __expf(rho - bt + lit));
     Kh[ob + tt * p.dqk + j] = __float2bfloat16_rn(kv * __expf(g - bt + lit));
@@ -393,7 +392,7 @@ __global__ void __launch_bounds__(128, 1)
     // ---- epilogue: h_t = H / max(den, 1) ------------------------------------------------
     {
       const float inv = 1.f / fmaxf(qn + den_intra, 1.f);
-      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.h) + b * p.sh[0] + h * p.sh[1] + (int64_t)tg * p.dv + e0;
+      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.h) + b * p.sh[0] + h * p.sh[1] + (int64_t)tg * p.th + e0;
 #pragma unroll 1
       for (int c0 = 0; c0 < kDV; c0 += 32) {
         float v[32];
@@ -467,7 +466,8 @@ bool stream_shape_ok(const Params& p) {
   if (p.dqk != 128 && p.dqk != 256 && p.dqk != 512) return false;
   if (p.dv % 32 != 0 || p.seqlen <= 0) return false;
   auto a16 = [](const void* x) { return reinterpret_cast<uintptr_t>(x) % 16 == 0; };
-  return a16(p.v) && a16(p.h) && p.sv[0] % 8 == 0 && p.sv[1] % 8 == 0 && p.sh[0] % 8 == 0 && p.sh[1] % 8 == 0;
+  return a16(p.v) && a16(p.h) && p.sv[0] % 8 == 0 && p.sv[1] % 8 == 0 && p.sh[0] % 8 == 0 && p.sh[1] % 8 == 0 &&
+         p.tv % 8 == 0 && p.th % 8 == 0;
 }
 
 template <int DK>
@@ -495,7 +495,7 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   const uint64_t dd[4] = {(uint64_t)DK, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
   const uint64_t sd[3] = {(uint64_t)DK * 2, (uint64_t)p.seqlen * DK * 2, (uint64_t)p.heads * p.seqlen * DK * 2};
   const uint64_t dvd[4] = {(uint64_t)p.dv, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
-  const uint64_t sv[3] = {(uint64_t)p.dv * 2, (uint64_t)p.sv[1] * 2, (uint64_t)p.sv[0] * 2};
+  const uint64_t sv[3] = {(uint64_t)p.tv * 2, (uint64_t)p.sv[1] * 2, (uint64_t)p.sv[0] * 2};
   if ((s = make_map_bf16_4d(&mq, Qs, dd, sd, "mlstm Qs")) != HXM_OK) return s;
   if ((s = make_map_bf16_4d(&mk, Ks, dd, sd, "mlstm Ks")) != HXM_OK) return s;
   if ((s = make_map_bf16_4d(&mh, Kh, dd, sd, "mlstm Kh")) != HXM_OK) return s;

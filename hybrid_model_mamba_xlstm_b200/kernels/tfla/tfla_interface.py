@@ -28,11 +28,9 @@ from .._common import dtype_code, ptr, require_cuda, stream_of
 __all__ = ["apply_tfla", "mlstm_chunkwise_fwd", "TFLAFunction"]
 
 
-def _dense_td(t):
-    """(B, H, L, D) with one dense (L, D) panel per head."""
-    if t.stride(-1) == 1 and t.stride(-2) == t.shape[-1]:
-        return t
-    return t.contiguous()
+def _unit_last(t):
+    """(B, H, L, D) views pass as they are (any b / h / t strides) when D is unit-stride."""
+    return t if t.stride(-1) == 1 or t.shape[-1] == 1 else t.contiguous()
 
 
 def mlstm_chunkwise_fwd(q, k, v, log_i, log_f, C0=None, n0=None, m0=None, *, chunk=64, return_state=False,
@@ -58,16 +56,13 @@ def mlstm_chunkwise_fwd(q, k, v, log_i, log_f, C0=None, n0=None, m0=None, *, chu
     else:
         raise ValueError(f"{who}: gates must be (B,H,L) or (B,H,L,Dqk); got {tuple(log_i.shape)} {tuple(log_f.shape)}")
     io = q.dtype if q.dtype in (torch.float32, torch.bfloat16) else torch.float32
-    q, k, v = (_dense_td(t if t.dtype == io else t.to(io)) for t in (q, k, v))
-    gi = log_i.float()
-    gf = log_f.float()
-    # gates: (b, h) strides free, (t[, d]) dense
-    if gate_mode == 0:
-        gi = gi if gi.stride(-1) == 1 else gi.contiguous()
-        gf = gf if gf.stride(-1) == 1 else gf.contiguous()
-    else:
-        gi, gf = _dense_td(gi), _dense_td(gf)
+    q, k, v = (_unit_last(t if t.dtype == io else t.to(io)) for t in (q, k, v))
+    gi, gf = log_i.float(), log_f.float()
+    if gate_mode == 1:  # per-channel gates: unit channel stride; (b, h, t) strides free
+        gi, gf = _unit_last(gi), _unit_last(gf)
     h = torch.empty((bsz, nh, L, dv), device=dev, dtype=io) if out is None else out
+    if h.shape != (bsz, nh, L, dv) or h.dtype != io or h.stride(-1) != 1:
+        raise ValueError(f"{who}: out must be a ({bsz}, {nh}, {L}, {dv}) {io} view with unit last stride")
     st = None
     if return_state:
         st = (torch.empty((bsz, nh, dqk, dv), device=dev, dtype=torch.float32),
@@ -84,6 +79,8 @@ def mlstm_chunkwise_fwd(q, k, v, log_i, log_f, C0=None, n0=None, m0=None, *, chu
     a.log_i, a.i_stride = ptr(gi), gi.stride()[:2]
     a.log_f, a.f_stride = ptr(gf), gf.stride()[:2]
     a.h, a.h_stride = ptr(h), h.stride()[:2]
+    a.q_tstride, a.k_tstride, a.v_tstride, a.h_tstride = q.stride(2), k.stride(2), v.stride(2), h.stride(2)
+    a.i_tstride, a.f_tstride = gi.stride(2), gf.stride(2)
     a.C0, a.n0, a.m0 = ptr(C0), ptr(n0), ptr(m0)
     if st is not None:
         a.CT, a.nT, a.mT = ptr(st[0]), ptr(st[1]), ptr(st[2])

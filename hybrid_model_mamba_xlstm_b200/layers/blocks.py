@@ -132,16 +132,19 @@ class mLSTMBlock(nn.Module):
             x_inner, x_gate = xp.chunk(2, dim=-1)
         else:
             x_inner = x_gate = xp
-        split = lambda t: t.view(bsz, L, nh, hd)                    # (B, L, H, hd) rows of hd
-        heads = lambda t: split(t).transpose(1, 2)                  # (B, H, L, hd)
-        q = self.q_norm(split(self.q_proj(x_inner))).transpose(1, 2).contiguous()
-        k = self.k_norm(split(self.k_proj(x_inner))).transpose(1, 2).contiguous()
-        v = heads(self.v_proj(x_inner)).contiguous()
+        # (B, L, H, hd) memory throughout; the mLSTM kernels take the (B, H, L, hd)
+        # views with their time stride, so no transpose copy runs.
+        split = lambda t: t.view(bsz, L, nh, hd)
+        heads = lambda t: split(t).transpose(1, 2)                  # (B, H, L, hd) view
+        q = self.q_norm(split(self.q_proj(x_inner))).transpose(1, 2)
+        k = self.k_norm(split(self.k_proj(x_inner))).transpose(1, 2)
+        v = heads(self.v_proj(x_inner))
         log_i = heads(self.i_gate_proj(x_inner).float())            # log of i = exp(pre)
         log_f = heads(F.logsigmoid(self.f_gate_proj(x_inner).float()))
         o = torch.sigmoid(self.o_gate_proj(x_inner))
-        h = mlstm_chunkwise_fwd(q, k, v, log_i, log_f)               # (B, H, L, hd)
-        h = h.transpose(1, 2).reshape(bsz, L, nh * hd) * o * torch.sigmoid(x_gate)
+        h = torch.empty(bsz, L, nh, hd, device=x.device, dtype=q.dtype)
+        mlstm_chunkwise_fwd(q, k, v, log_i, log_f, out=h.transpose(1, 2))
+        h = h.view(bsz, L, nh * hd) * o * torch.sigmoid(x_gate)
         return self.out_proj(h)
 
 

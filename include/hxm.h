@@ -110,7 +110,8 @@ hxm_status hxm_selective_scan_fwd(const hxm_scan_args* args, void* stream);
 /* The state is kept stabilized: C = exp(m) * Cs, n = exp(m) * ns.  Inputs    */
 /* C0/n0/m0 and outputs CT/nT/mT use that representation (NULL = zero).      */
 /* q, k, v, h: (b, h, t, d) with arbitrary (b, h) strides, unit d stride and */
-/* t stride = d (one contiguous (t, d) panel per head); bf16.                */
+/* a time stride (*_tstride; 0 = d, one dense (t, d) panel per head), so     */
+/* (b, t, h, d) projection outputs are passed without a transpose.           */
 /* Requires a workspace of hxm_mlstm_workspace_size() bytes.                 */
 /* ------------------------------------------------------------------------ */
 typedef struct hxm_mlstm_args {
@@ -119,15 +120,18 @@ typedef struct hxm_mlstm_args {
   int32_t chunk;            /* chunk length (64 or 128)                      */
   int32_t gate_mode;        /* 0 scalar per head, 1 per channel              */
   hxm_dtype io_dtype;       /* q, k, v, h                                    */
-  const void* q; int64_t q_stride[2];   /* (b, h) strides; (t, d) dense      */
+  const void* q; int64_t q_stride[2];   /* (b, h) strides; time: q_tstride   */
   const void* k; int64_t k_stride[2];
   const void* v; int64_t v_stride[2];
-  const float* log_i;  int64_t i_stride[2];   /* (b, h); t[,d] dense         */
+  const float* log_i;  int64_t i_stride[2];   /* (b, h); time: i_tstride; d dense */
   const float* log_f;  int64_t f_stride[2];
   void* h;   int64_t h_stride[2];
   const float* C0; const float* n0; const float* m0;  /* (b,h,dqk,dv) (b,h,dqk) (b,h) fp32 or NULL */
   float* CT; float* nT; float* mT;                    /* same shapes, or NULL */
   void* workspace; size_t workspace_bytes;
+  /* time strides in elements; 0 = dense (dqk for q, k; dv for v, h; 1 per-head */
+  /* or dqk per-channel gates)                                                 */
+  int64_t q_tstride, k_tstride, v_tstride, h_tstride, i_tstride, f_tstride;
 } hxm_mlstm_args;
 
 size_t hxm_mlstm_workspace_size(const hxm_mlstm_args* args);

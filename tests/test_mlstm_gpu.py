@@ -208,3 +208,27 @@ def test_mlstm_block_bf16_head512_matches_fp32_path(ops):
         ref = blk.float()(x)
         out = blk.to(torch.bfloat16)(x.to(torch.bfloat16))
     assert rel_err(np64(out), np64(ref)) < 3e-2
+
+
+@pytest.mark.parametrize("path", ["tc_head_gates_d256", "stream_channel_gates_d128", "recurrent_fp32_d64"])
+def test_time_strided_views(ops, path):
+    """q, k, v, gates and the output in (B, L, H, d) memory passed as (B, H, L, d)
+    views (time stride H*d): the layer's projection layout, no transpose copies."""
+    g = torch.Generator().manual_seed(31)
+    dtype = torch.float32 if path.startswith("recurrent") else torch.bfloat16
+    d = {"tc_head_gates_d256": 256, "stream_channel_gates_d128": 128, "recurrent_fp32_d64": 64}[path]
+    b, h, L = 2, 3, 200
+    blhd = lambda: torch.randn(b, L, h, d, generator=g)
+    q = (blhd() / d ** 0.5).to("cuda", dtype).transpose(1, 2)
+    k, v = (blhd().to("cuda", dtype).transpose(1, 2) for _ in range(2))
+    if path.startswith("tc"):
+        li = (torch.randn(b, L, h, generator=g)).cuda().transpose(1, 2)
+        lf = torch.nn.functional.logsigmoid(torch.randn(b, L, h, generator=g) + 3).cuda().transpose(1, 2)
+    else:
+        li = (blhd() * 0.5).cuda().transpose(1, 2)
+        lf = torch.nn.functional.logsigmoid(blhd() + 1.0).cuda().transpose(1, 2)
+    out_mem = torch.empty(b, L, h, d, device="cuda", dtype=dtype)
+    out = ops.mlstm_chunkwise_fwd(q, k, v, li, lf, out=out_mem.transpose(1, 2))
+    assert out.data_ptr() == out_mem.data_ptr()
+    ref, _, _ = R.tfla_recurrent(np64(q), np64(k), np64(v), np.exp(np64(li)), np.exp(np64(lf)))
+    assert rel_err(np64(out), ref) < (TOL32 * 10 if dtype == torch.float32 else TOL16)
