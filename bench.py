@@ -71,7 +71,7 @@ class ClockSampler:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -199,7 +199,9 @@ def secondary_metrics(args, dev, world, rank):
     out = {}
     steps = max(3, min(args.steps, 10))
     # mLSTM chunkwise, per-head gates (tcgen05): the large-batch d=256 case and the exact 2x4x2048x256 case
-    for name, (b, h, L, d, c) in {"mlstm_b8_h8_l8192_d256": (8, 8, 8192, 256, 128),
+    # and the long-context case (batch 8, 8 heads, seqlen 32768, qk = v = 512: key-streaming kernel)
+    for name, (b, h, L, d, c) in {"mlstm_b8_h8_l32768_d512": (8, 8, 32768, 512, 128),
+                                  "mlstm_b8_h8_l8192_d256": (8, 8, 8192, 256, 128),
                                   "mlstm_b2_h4_l2048_d256_c64": (2, 4, 2048, 256, 64)}.items():
         inp = mlstm_inputs(b, h, L, d, torch.bfloat16, seed=rank, device=dev, on_device=True)
         ms = _time_cuda(lambda: mlstm_chunkwise_fwd(inp.q, inp.k, inp.v, inp.log_i, inp.log_f, chunk=c),
@@ -207,7 +209,8 @@ def secondary_metrics(args, dev, world, rank):
         fl = inp.flops(c)
         out[name] = {"metric": "mLSTM chunkwise TFLOP/s (algorithmic)", "value": world * fl / ms / 1e9,
                      "unit": "TFLOP/s", "ms": ms, "frac_of_bf16_peak": fl / ms / 1e9 / tf_peak,
-                     "peak_kind": pk_kind, "scaling": "weak", "kernel": "chunk_tc_kernel<%d, mLSTM>" % d}
+                     "peak_kind": pk_kind, "scaling": "weak",
+                     "kernel": "chunk_tc_kernel<%d, mLSTM>" % d if d <= 256 else "mlstm_stream_kernel<%d>" % d}
         del inp
     # Mamba-2 SSD, batch 8, 32 heads x 64, dstate 128, seqlen 4096 (tcgen05)
     inp = ssd_inputs(8, 4096, 32, 64, 128, seed=rank, device=dev, on_device=True)
