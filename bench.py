@@ -238,22 +238,29 @@ def secondary_metrics(args, dev, world, rank):
 
 def prefill_metric(args, dev, world, rank):
     """Hybrid-350M prefill (24 layers [Mamba, Mamba, mLSTM, sLSTM], d 1024, vocab
-    50304, bf16), global batch 8 x seqlen 2048 data-parallel over the ranks."""
+    50304, bf16), data parallel over the ranks: batch 8 x seqlen 2048 per rank
+    (weak scaling, the data-parallel serving throughput) and the global batch 8
+    split over the ranks (strong scaling)."""
     import hybrid_model_mamba_xlstm_b200.layers as Lyr
     gb, seqlen = 8, 2048
-    per = max(1, gb // world)
     torch.manual_seed(1234)  # identical weights on every rank
     model = Lyr.HybridLanguageModel(Lyr.hybrid_350m_config()).to(dev).to(torch.bfloat16).eval()
+    nparam = sum(p.numel() for p in model.parameters())
     g = torch.Generator(device=dev)
     g.manual_seed(99 + rank)
-    ids = torch.randint(0, 50304, (per, seqlen), generator=g, device=dev)
-    with torch.no_grad():
-        ms = _time_cuda(lambda: model(ids), 3, 2, dev, world)
-    nparam = sum(p.numel() for p in model.parameters())
+    out = {}
+    for kind, per in (("weak", gb), ("strong", max(1, gb // world))):
+        ids = torch.randint(0, 50304, (per, seqlen), generator=g, device=dev)
+        with torch.no_grad():
+            ms = _time_cuda(lambda: model(ids), 3, 2, dev, world)
+        out[kind] = {"metric": "hybrid-350M prefill tokens/s", "value": world * per * seqlen / ms * 1e3,
+                     "unit": "tok/s", "ms_per_step": ms, "batch_per_rank": per, "global_batch": world * per,
+                     "seqlen": seqlen, "params": nparam,
+                     "scaling": "weak (batch 8 per rank)" if kind == "weak" else "strong (global batch 8 split over ranks)",
+                     "parallelism": f"dp{world}"}
+        del ids
     del model
-    return {"metric": "hybrid-350M prefill tokens/s", "value": world * per * seqlen / ms * 1e3, "unit": "tok/s",
-            "ms_per_step": ms, "global_batch": world * per, "seqlen": seqlen, "params": nparam,
-            "scaling": "strong (global batch 8 split over ranks)", "parallelism": f"dp{world}"}
+    return out
 
 
 def run_ours(args, world, rank, local):
