@@ -77,13 +77,23 @@ class MambaBlock(nn.Module):
         di, n, r = self.inner_dim, self.state_size, self.dt_rank
         xz = self.in_proj(x)                                     # (B, L, 2*di)
         x_in, z = xz[..., :di], xz[..., di:]
-        u = causal_conv1d(x_in, self.conv1d.weight, self.conv1d.bias, activation="silu")  # (B, L, di)
+        # with a cache (dict): continue from / update the conv inputs and the scan state
+        conv0 = cache.get("conv") if cache is not None else None
+        ssm0 = cache.get("ssm") if cache is not None else None
+        conv = causal_conv1d(x_in, self.conv1d.weight, self.conv1d.bias, activation="silu", initial_state=conv0,
+                             return_final_state=cache is not None)
+        u, conv_state = conv if cache is not None else (conv, None)                          # (B, L, di)
         dbc = self.x_proj(u)                                     # (B, L, r + 2n)
         dt_low, Bm, Cm = dbc[..., :r], dbc[..., r:r + n], dbc[..., r + n:]
         delta = F.linear(dt_low, self.dt_proj.weight)            # (B, L, di); bias folded into the scan
         A, D, dt_bias = self._scan_params()
-        y = selective_scan_raw(u, delta, A, Bm, Cm, D, z, z_mode="silu", delta_bias=dt_bias,
-                               delta_softplus=True)                                        # (B, L, di)
+        res = selective_scan_raw(u, delta, A, Bm, Cm, D, z, z_mode="silu", delta_bias=dt_bias, delta_softplus=True,
+                                 h0=ssm0, return_last_state=cache is not None)             # (B, L, di)
+        if cache is not None:
+            y, cache["ssm"] = res
+            cache["conv"] = conv_state
+        else:
+            y = res
         return self.out_proj(y)
 
     def _scan_params(self):
@@ -143,7 +153,12 @@ class mLSTMBlock(nn.Module):
         log_f = heads(F.logsigmoid(self.f_gate_proj(x_inner).float()))
         o = torch.sigmoid(self.o_gate_proj(x_inner))
         h = torch.empty(bsz, L, nh, hd, device=x.device, dtype=q.dtype)
-        mlstm_chunkwise_fwd(q, k, v, log_i, log_f, out=h.transpose(1, 2))
+        if cache is None:
+            mlstm_chunkwise_fwd(q, k, v, log_i, log_f, out=h.transpose(1, 2))
+        else:  # continue from / update the stabilized state (C, n, m)
+            _, st = mlstm_chunkwise_fwd(q, k, v, log_i, log_f, cache.get("C"), cache.get("n"), cache.get("m"),
+                                        out=h.transpose(1, 2), return_state=True)
+            cache["C"], cache["n"], cache["m"] = st
         h = h.view(bsz, L, nh * hd) * o * torch.sigmoid(x_gate)
         return self.out_proj(h)
 
@@ -177,8 +192,8 @@ class sLSTMBlock(nn.Module):
             h0, c0 = cache["h"], cache["c"]
         h_seq, (h, c) = slstm_scan(gates, self.h_norm.weight, R=self.recurrent_weight, eps=self.h_norm.eps,
                                    exponential_gate=self.use_exponential_gate, h0=h0, c0=c0)
-        if cache is not None:
-            cache["h"], cache["c"] = h.to(x.dtype), c.to(x.dtype)
+        if cache is not None:  # fp32 true states (the reference keeps them in x's dtype)
+            cache["h"], cache["c"] = h, c
         return self.out_proj(h_seq.reshape(bsz, L, self.hidden_dim))
 
 

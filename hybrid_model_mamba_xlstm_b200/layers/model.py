@@ -115,11 +115,19 @@ class HybridLanguageModel(nn.Module):
         elif isinstance(module, nn.Embedding):
             nn.init.normal_(module.weight, mean=0.0, std=self.config.initializer_range)
 
-    def forward(self, input_ids, return_hidden=False):
+    def init_caches(self):
+        """Empty per-layer recurrent caches (zero states) for :meth:`forward` / :meth:`generate`."""
+        return [dict() for _ in self.layers]
+
+    def forward(self, input_ids, return_hidden=False, caches=None):
+        """Logits (B, L, vocab).  With ``caches`` (from :meth:`init_caches`) every
+        layer starts from and updates its recurrent state (Mamba conv inputs and
+        scan state, mLSTM (C, n, m), sLSTM (h, c)), so a sequence can be fed in
+        pieces — the prefill / decode split of :meth:`generate`."""
         h = self.embeddings.token_embedding(input_ids)
         pending = None  # each block's last residual add is fused into the next RMSNorm
-        for layer in self.layers:
-            h, pending = layer.forward_pending(h, pending)
+        for i, layer in enumerate(self.layers):
+            h, pending = layer.forward_pending(h, pending, cache=None if caches is None else caches[i])
         if pending is None:
             h = self.final_norm(h)
         elif isinstance(self.final_norm, RMSNorm):
@@ -129,3 +137,31 @@ class HybridLanguageModel(nn.Module):
         if return_hidden:
             return h
         return self.lm_head(h)
+
+    @torch.no_grad()
+    def generate(self, input_ids, max_new_tokens=100, temperature=1.0, top_k=None, top_p=None):
+        """Autoregressive sampling with the reference's interface and sampling rule
+        (hybrid_xmamba/models/hybrid_lm.py:211-267), but one prefill over the
+        prompt and then one single-token step per new token on the carried
+        recurrent states, instead of re-running the whole prefix per token."""
+        self.eval()
+        caches = self.init_caches()
+        logits = self.forward(input_ids, caches=caches)[:, -1, :]
+        out = [input_ids]
+        for i in range(max_new_tokens):
+            next_token_logits = logits.float() / temperature
+            if top_k is not None:
+                kth = torch.topk(next_token_logits, top_k)[0][..., -1, None]
+                next_token_logits = next_token_logits.masked_fill(next_token_logits < kth, float("-inf"))
+            if top_p is not None:
+                sorted_logits, sorted_idx = torch.sort(next_token_logits, descending=True)
+                cum = torch.cumsum(torch.softmax(sorted_logits, dim=-1), dim=-1)
+                drop = cum > top_p
+                drop[..., 1:] = drop[..., :-1].clone()
+                drop[..., 0] = False
+                next_token_logits = next_token_logits.masked_fill(drop.scatter(1, sorted_idx, drop), float("-inf"))
+            nxt = torch.multinomial(torch.softmax(next_token_logits, dim=-1), num_samples=1)
+            out.append(nxt)
+            if i + 1 < max_new_tokens:
+                logits = self.forward(nxt, caches=caches)[:, -1, :]
+        return torch.cat(out, dim=1)

@@ -1,0 +1,92 @@
+"""Prefill / decode with carried recurrent states on the GPU.
+
+Feeding a sequence in pieces through the per-layer caches (Mamba conv inputs
+and scan state, mLSTM stabilized (C, n, m), sLSTM (h, c)) must give the logits
+of one full prefill: the state outputs of every kernel are complete.  The
+reference re-runs the whole prefix per generated token
+(hybrid_xmamba/models/hybrid_lm.py:211-267); ``generate`` here decodes one
+token per step on the carried states and must pick the same tokens.
+
+Tolerances (normwise relative error on the logits): fp32 model 1e-4, bf16
+model 3e-2 (one bf16 rounding of the activations per layer on either side).
+"""
+import numpy as np
+import pytest
+import torch
+
+from tests.conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def L():
+    if not torch.cuda.is_available():
+        pytest.skip("needs CUDA")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    import hybrid_model_mamba_xlstm_b200.layers as L
+    return L
+
+
+def np64(t):
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def _small(L, dtype, recurrent=False, head_dim=32, dim=64, slstm_heads=4):
+    torch.manual_seed(0)
+    cfg = L.HybridConfig(vocab_size=97, dim=dim, num_layers=4, layer_pattern=["mamba", "mamba", "mlstm", "slstm"],
+                         state_size=16, conv_size=4, expand_factor=2, head_dim=head_dim, num_heads=2,
+                         slstm_num_heads=slstm_heads, dropout=0.0, slstm_recurrent=recurrent)
+    return L.HybridLanguageModel(cfg).cuda().to(dtype).eval()
+
+
+@pytest.mark.parametrize("split", [1, 17, 39])
+def test_pieces_equal_full_prefill_fp32(L, split):
+    model = _small(L, torch.float32)
+    ids = torch.randint(0, 97, (2, 40), device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    with torch.no_grad():
+        full = model(ids)
+        caches = model.init_caches()
+        parts = [model(ids[:, :split], caches=caches)]
+        for t in range(split, 40):
+            parts.append(model(ids[:, t:t + 1], caches=caches))
+    assert rel_err(np64(torch.cat(parts, 1)), np64(full)) < 1e-4
+
+
+def test_pieces_equal_full_prefill_bf16_tensor_core_paths(L):
+    """bf16 with the prefill's kernel paths: mLSTM heads of 128 with per-channel
+    gates (key-streaming tcgen05 kernel), sLSTM heads of 128 with recurrent
+    weights (cluster kernel), channel-major fast scan, conv kernel."""
+    model = _small(L, torch.bfloat16, recurrent=True, head_dim=128, dim=256, slstm_heads=2)
+    ids = torch.randint(0, 97, (2, 300), device="cuda", generator=torch.Generator(device="cuda").manual_seed(2))
+    with torch.no_grad():
+        full = model(ids)
+        caches = model.init_caches()
+        parts = [model(ids[:, :200], caches=caches), model(ids[:, 200:290], caches=caches)]
+        for t in range(290, 300):
+            parts.append(model(ids[:, t:t + 1], caches=caches))
+    assert rel_err(np64(torch.cat(parts, 1)), np64(full)) < 3e-2
+
+
+def test_generate_greedy_matches_full_recompute(L):
+    """top_k = 1 (greedy): the cached decode picks the tokens that re-running
+    the full prefix each step (the reference's generate) picks."""
+    model = _small(L, torch.float32)
+    prompt = torch.randint(0, 97, (2, 12), device="cuda", generator=torch.Generator(device="cuda").manual_seed(3))
+    out = model.generate(prompt, max_new_tokens=8, top_k=1)
+    seq = prompt
+    with torch.no_grad():
+        for _ in range(8):
+            nxt = model(seq)[:, -1, :].argmax(-1, keepdim=True)
+            seq = torch.cat([seq, nxt], 1)
+    assert out.shape == (2, 20)
+    assert torch.equal(out, seq)
+
+
+def test_generate_sampling_runs(L):
+    model = _small(L, torch.bfloat16)
+    prompt = torch.randint(0, 97, (3, 5), device="cuda")
+    torch.manual_seed(0)
+    out = model.generate(prompt, max_new_tokens=6, temperature=0.8, top_k=20, top_p=0.9)
+    assert out.shape == (3, 11) and torch.equal(out[:, :5], prompt)
+    assert int(out.min()) >= 0 and int(out.max()) < 97
