@@ -139,14 +139,22 @@ class HybridLanguageModel(nn.Module):
         return self.lm_head(h)
 
     @torch.no_grad()
-    def generate(self, input_ids, max_new_tokens=100, temperature=1.0, top_k=None, top_p=None):
+    def generate(self, input_ids, max_new_tokens=100, temperature=1.0, top_k=None, top_p=None, cuda_graph=True):
         """Autoregressive sampling with the reference's interface and sampling rule
         (hybrid_xmamba/models/hybrid_lm.py:211-267), but one prefill over the
         prompt and then one single-token step per new token on the carried
-        recurrent states, instead of re-running the whole prefix per token."""
+        recurrent states, instead of re-running the whole prefix per token.
+        With ``cuda_graph`` the single-token step (a few hundred small kernel
+        launches) is captured once and replayed (:class:`GraphDecoder`)."""
         self.eval()
-        caches = self.init_caches()
-        logits = self.forward(input_ids, caches=caches)[:, -1, :]
+        if cuda_graph and input_ids.is_cuda and max_new_tokens > 1:
+            dec = GraphDecoder(self, input_ids.shape[0], input_ids.device)
+            logits = dec.prefill(input_ids)[:, -1, :]
+            step = dec.step
+        else:
+            caches = self.init_caches()
+            logits = self.forward(input_ids, caches=caches)[:, -1, :]
+            step = lambda t: self.forward(t, caches=caches)
         out = [input_ids]
         for i in range(max_new_tokens):
             next_token_logits = logits.float() / temperature
@@ -163,5 +171,63 @@ class HybridLanguageModel(nn.Module):
             nxt = torch.multinomial(torch.softmax(next_token_logits, dim=-1), num_samples=1)
             out.append(nxt)
             if i + 1 < max_new_tokens:
-                logits = self.forward(nxt, caches=caches)[:, -1, :]
+                logits = step(nxt)[:, -1, :]
         return torch.cat(out, dim=1)
+
+
+class GraphDecoder:
+    """Single-token decode of a :class:`HybridLanguageModel` replayed from one CUDA graph.
+
+    The recurrent states live in static buffers; the captured step reads them,
+    runs every layer on one token (its hxm kernels and cuBLAS GEMMs) and copies
+    the new states back into the same buffers, so each replay advances the
+    sequence by one token with no per-kernel launch overhead on the host."""
+
+    def __init__(self, model, batch, device):
+        self.model, self.batch, self.device = model, batch, torch.device(device)
+        self.graph = None
+        self.states = None
+        self.ids = torch.zeros(batch, 1, dtype=torch.long, device=self.device)
+
+    @torch.no_grad()
+    def prefill(self, input_ids):
+        caches = self.model.init_caches()
+        logits = self.model(input_ids, caches=caches)
+        self.states = [{k: v.clone() for k, v in c.items()} for c in caches]
+        self.graph = None
+        return logits
+
+    def _run(self):
+        caches = [dict(c) for c in self.states]
+        logits = self.model(self.ids, caches=caches)
+        for dst, src in zip(self.states, caches):
+            for k, v in src.items():
+                dst[k].copy_(v)
+        return logits
+
+    @torch.no_grad()
+    def _capture(self):
+        saved = [{k: v.clone() for k, v in c.items()} for c in self.states]
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(2):  # warm-up (lazy library setup, workspace sizes) on scratch states
+                self._run()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        for dst, src in zip(self.states, saved):
+            for k, v in src.items():
+                dst[k].copy_(v)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = self._run()
+
+    @torch.no_grad()
+    def step(self, token_ids):
+        """Logits (batch, 1, vocab) of the next position after feeding `token_ids` (batch, 1)."""
+        if self.states is None:
+            raise RuntimeError("GraphDecoder.step before prefill")
+        self.ids.copy_(token_ids)
+        if self.graph is None:
+            self._capture()
+        self.graph.replay()
+        return self.logits

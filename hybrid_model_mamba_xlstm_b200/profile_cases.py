@@ -17,6 +17,8 @@ cases (default sizes):
   conv         B D L             (8 4096 2048)    causal depthwise conv1d(4) + SiLU
   mamba_layer  B L               (8 2048)         one hybrid-350M Mamba block
   prefill      B L               (8 2048)         the hybrid-350M model forward
+  decode       B P               (1 512)          hybrid-350M: prefill P tokens, then time one-token steps
+                                                  (eager, and replayed from a CUDA graph)
 """
 from __future__ import annotations
 
@@ -117,6 +119,24 @@ def main(argv=None):
             ids = torch.randint(0, model.config.vocab_size, (B, L), device=dev)
             fn = lambda: model(ids)  # noqa: E731
         extra = {"tokens": B * L}
+    elif a.case == "decode":
+        from . import layers as Lyr
+        B, P = (s + [1, 512][len(s):])[:2]
+        torch.manual_seed(0)
+        model = Lyr.HybridLanguageModel(Lyr.hybrid_350m_config()).to(dev).to(torch.bfloat16).eval()
+        ids = torch.randint(0, model.config.vocab_size, (B, P), device=dev)
+        tok = torch.randint(0, model.config.vocab_size, (B, 1), device=dev)
+        with torch.no_grad():
+            caches = model.init_caches()
+            model(ids, caches=caches)
+            eager_ms, _ = _time(lambda: model(tok, caches=caches), max(3, a.reps))
+            dec = Lyr.GraphDecoder(model, B, dev)
+            dec.prefill(ids)
+            dec.step(tok)
+            graph_ms, _ = _time(lambda: dec.step(tok), max(3, a.reps))
+        print(json.dumps({"case": "decode", "sizes": [B, P], "eager_ms_per_token": eager_ms,
+                          "graph_ms_per_token": graph_ms, "tokens/s (graph)": B / graph_ms * 1e3}), flush=True)
+        return
     else:
         raise SystemExit(f"unknown case {a.case!r}")
 

@@ -90,3 +90,31 @@ def test_generate_sampling_runs(L):
     out = model.generate(prompt, max_new_tokens=6, temperature=0.8, top_k=20, top_p=0.9)
     assert out.shape == (3, 11) and torch.equal(out[:, :5], prompt)
     assert int(out.min()) >= 0 and int(out.max()) < 97
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_graph_decoder_replays_the_eager_step(L, dtype):
+    """The CUDA-graph decoder gives the eager single-token steps' logits exactly
+    (same kernels, same data), over several replays that advance the state."""
+    model = _small(L, dtype, recurrent=dtype == torch.bfloat16, head_dim=128 if dtype == torch.bfloat16 else 32,
+                   dim=256 if dtype == torch.bfloat16 else 64, slstm_heads=2 if dtype == torch.bfloat16 else 4)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    prompt = torch.randint(0, 97, (2, 33), device="cuda", generator=g)
+    steps = torch.randint(0, 97, (2, 5), device="cuda", generator=g)
+    with torch.no_grad():
+        caches = model.init_caches()
+        model(prompt, caches=caches)
+        eager = [model(steps[:, i:i + 1], caches=caches).clone() for i in range(5)]
+        dec = L.GraphDecoder(model, 2, "cuda")
+        dec.prefill(prompt)
+        graphed = [dec.step(steps[:, i:i + 1]).clone() for i in range(5)]
+    for a, b in zip(eager, graphed):
+        assert torch.equal(a, b)
+
+
+def test_generate_graph_and_eager_agree(L):
+    model = _small(L, torch.float32)
+    prompt = torch.randint(0, 97, (2, 9), device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+    a = model.generate(prompt, max_new_tokens=7, top_k=1, cuda_graph=True)
+    b = model.generate(prompt, max_new_tokens=7, top_k=1, cuda_graph=False)
+    assert torch.equal(a, b)
