@@ -115,6 +115,22 @@ class RmsnormArgs(ct.Structure):
     ]
 
 
+class MlstmGatesArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("rows", ct.c_int64), ("dim", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("i_pre", ct.c_void_p), ("i_row_stride", ct.c_int64),
+        ("f_pre", ct.c_void_p), ("f_row_stride", ct.c_int64),
+        ("log_i", ct.c_void_p), ("log_i_row_stride", ct.c_int64),
+        ("log_f", ct.c_void_p), ("log_f_row_stride", ct.c_int64),
+        ("h", ct.c_void_p), ("h_row_stride", ct.c_int64),
+        ("o_pre", ct.c_void_p), ("o_row_stride", ct.c_int64),
+        ("x_gate", ct.c_void_p), ("x_gate_row_stride", ct.c_int64),
+        ("out", ct.c_void_p), ("out_row_stride", ct.c_int64),
+    ]
+
+
 # symbol -> (restype, argtypes)
 SYMBOLS = {
     "hxm_abi_version": (ct.c_int, []),
@@ -128,6 +144,8 @@ SYMBOLS = {
     "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),
     "hxm_causal_conv1d_fwd": (ct.c_int, [ct.POINTER(ConvArgs), ct.c_void_p]),
     "hxm_rmsnorm_fwd": (ct.c_int, [ct.POINTER(RmsnormArgs), ct.c_void_p]),
+    "hxm_mlstm_gate_prologue": (ct.c_int, [ct.POINTER(MlstmGatesArgs), ct.c_void_p]),
+    "hxm_mlstm_gate_epilogue": (ct.c_int, [ct.POINTER(MlstmGatesArgs), ct.c_void_p]),
 }
 
 _lib = None

@@ -29,6 +29,7 @@ from ..kernels.conv import causal_conv1d
 from ..kernels.norm import rmsnorm
 from ..kernels.selective_scan.scan_interface import selective_scan_raw
 from ..kernels.slstm import slstm_scan
+from ..kernels.tfla.gates import mlstm_gate_epilogue, mlstm_gate_prologue
 from ..kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
 
 
@@ -137,11 +138,13 @@ class mLSTMBlock(nn.Module):
     def forward(self, x, cache=None):
         bsz, L, _ = x.shape
         nh, hd = self.num_heads, self.head_dim
-        xp = self.in_proj(x)
+        inner = self.inner_dim
         if self.proj_factor == 2:
-            x_inner, x_gate = xp.chunk(2, dim=-1)
+            # the two halves of in_proj as two GEMMs: contiguous x_inner feeds the next GEMMs
+            w = self.in_proj.weight
+            x_inner, x_gate = F.linear(x, w[:inner]), F.linear(x, w[inner:])
         else:
-            x_inner = x_gate = xp
+            x_inner = x_gate = self.in_proj(x)
         # (B, L, H, hd) memory throughout; the mLSTM kernels take the (B, H, L, hd)
         # views with their time stride, so no transpose copy runs.
         split = lambda t: t.view(bsz, L, nh, hd)
@@ -149,9 +152,12 @@ class mLSTMBlock(nn.Module):
         q = self.q_norm(split(self.q_proj(x_inner))).transpose(1, 2)
         k = self.k_norm(split(self.k_proj(x_inner))).transpose(1, 2)
         v = heads(self.v_proj(x_inner))
-        log_i = heads(self.i_gate_proj(x_inner).float())            # log of i = exp(pre)
-        log_f = heads(F.logsigmoid(self.f_gate_proj(x_inner).float()))
-        o = torch.sigmoid(self.o_gate_proj(x_inner))
+        # i, f, o gate projections as one GEMM with the bias in its epilogue
+        w_ifo, b_ifo = self._gate_params()
+        ifo = F.linear(x_inner, w_ifo, b_ifo)                       # (B, L, 3*inner)
+        # log_i = i_pre (i = exp), log_f = logsigmoid(f_pre): one fused pass
+        log_i, log_f = mlstm_gate_prologue(ifo[..., :inner], ifo[..., inner:2 * inner])
+        log_i, log_f = heads(log_i), heads(log_f)
         h = torch.empty(bsz, L, nh, hd, device=x.device, dtype=q.dtype)
         if cache is None:
             mlstm_chunkwise_fwd(q, k, v, log_i, log_f, out=h.transpose(1, 2))
@@ -159,8 +165,25 @@ class mLSTMBlock(nn.Module):
             _, st = mlstm_chunkwise_fwd(q, k, v, log_i, log_f, cache.get("C"), cache.get("n"), cache.get("m"),
                                         out=h.transpose(1, 2), return_state=True)
             cache["C"], cache["n"], cache["m"] = st
-        h = h.view(bsz, L, nh * hd) * o * torch.sigmoid(x_gate)
+        # h * sigmoid(o_pre) * sigmoid(x_gate): one fused pass
+        h = mlstm_gate_epilogue(h.view(bsz, L, nh * hd), ifo[..., 2 * inner:], x_gate)
         return self.out_proj(h)
+
+
+    def _gate_params(self):
+        """[W_i; W_f; W_o] and [b_i; b_f; b_o] stacked; cached while the
+        parameters are unchanged and no gradient is being recorded."""
+        mods = (self.i_gate_proj, self.f_gate_proj, self.o_gate_proj)
+        params = [m.weight for m in mods] + [m.bias for m in mods]
+        derive = lambda: (torch.cat([m.weight for m in mods]), torch.cat([m.bias for m in mods]))
+        if torch.is_grad_enabled() and any(p.requires_grad for p in params):
+            return derive()
+        key = tuple((p.data_ptr(), p._version, p.device, p.dtype) for p in params)
+        if getattr(self, "_gate_key", None) != key:
+            with torch.no_grad():
+                self._gate_val = derive()
+            self._gate_key = key
+        return self._gate_val
 
 
 class sLSTMBlock(nn.Module):

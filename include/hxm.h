@@ -263,6 +263,35 @@ typedef struct hxm_rmsnorm_args {
 
 hxm_status hxm_rmsnorm_fwd(const hxm_rmsnorm_args* args, void* stream);
 
+/* ---- mLSTM gate prologue / epilogue ---------------------------------------- */
+/* Replace the element-wise gate work of mLSTMBlock.forward                  */
+/* (hybrid_xmamba/layers/mlstm_block.py:117-119,138-141) around the           */
+/* recurrence, one HBM pass each, on (rows, dim) matrices with row strides   */
+/* in elements and unit column stride:                                       */
+/*   prologue: log_i = i_pre (fp32), log_f = logsigmoid(f_pre) (fp32)        */
+/*             (the log-space gates of hxm_mlstm_chunkwise_fwd);             */
+/*   epilogue: out = h * sigmoid(o_pre) * sigmoid(x_gate).                    */
+/* i_pre, f_pre, o_pre, x_gate, h, out: io dtype (bf16 / fp32).              */
+typedef struct hxm_mlstm_gates_args {
+  size_t struct_size;
+  int64_t rows;
+  int32_t dim;
+  hxm_dtype io_dtype;
+  /* prologue */
+  const void* i_pre; int64_t i_row_stride;
+  const void* f_pre; int64_t f_row_stride;
+  float* log_i;      int64_t log_i_row_stride;
+  float* log_f;      int64_t log_f_row_stride;
+  /* epilogue */
+  const void* h;      int64_t h_row_stride;
+  const void* o_pre;  int64_t o_row_stride;
+  const void* x_gate; int64_t x_gate_row_stride;
+  void* out;          int64_t out_row_stride;
+} hxm_mlstm_gates_args;
+
+hxm_status hxm_mlstm_gate_prologue(const hxm_mlstm_gates_args* args, void* stream);
+hxm_status hxm_mlstm_gate_epilogue(const hxm_mlstm_gates_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
