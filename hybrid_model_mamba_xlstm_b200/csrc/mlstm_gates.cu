@@ -6,8 +6,8 @@
 // of mLSTMBlock.forward (hybrid_xmamba/layers/mlstm_block.py:117-119,138-141);
 // the recurrence itself takes the gates in log space.
 //
-// Grid-stride over 8-element vectors of each row (16-byte loads for bf16);
-// a ragged row tail or an unaligned row falls back to scalar elements.
+// A thread owns 8 consecutive elements of a row (16-byte loads for bf16,
+// 16-byte stores); a ragged row tail or an unaligned row uses scalar elements.
 #include "capi_internal.h"
 #include "common.cuh"
 
@@ -48,15 +48,14 @@ HXM_DEV void load8(const T* p, bool vec, int n, float (&v)[8]) {
   }
 }
 
+// grid: x over 8-element vectors of a row, y (grid-stride) over rows
 template <typename T>
 __global__ void __launch_bounds__(256) prologue_kernel(const Params p) {
   constexpr bool ACC = sizeof(T) == 4;
-  const int vpr = (p.dim + 7) / 8;
-  const int64_t total = p.rows * vpr;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / vpr;
-    const int c = (int)(i % vpr) * 8;
-    const int n = min(8, p.dim - c);
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= p.dim) return;
+  const int n = min(8, p.dim - c);
+  for (int64_t r = blockIdx.y; r < p.rows; r += gridDim.y) {
     const T* ip = static_cast<const T*>(p.ip) + r * p.si + c;
     const T* fp = static_cast<const T*>(p.fp) + r * p.sf + c;
     const bool vi = n == 8 && (reinterpret_cast<uintptr_t>(ip) % 16 == 0);
@@ -64,13 +63,19 @@ __global__ void __launch_bounds__(256) prologue_kernel(const Params p) {
     float a[8], f[8];
     load8<T>(ip, vi, n, a);
     load8<T>(fp, vf, n, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = log_sigmoid<ACC>(f[j]);
     float* li = p.li + r * p.sli + c;
     float* lf = p.lf + r * p.slf + c;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (j < n) {
+    if (n == 8 && reinterpret_cast<uintptr_t>(li) % 16 == 0 && reinterpret_cast<uintptr_t>(lf) % 16 == 0) {
+      reinterpret_cast<float4*>(li)[0] = make_float4(a[0], a[1], a[2], a[3]);
+      reinterpret_cast<float4*>(li)[1] = make_float4(a[4], a[5], a[6], a[7]);
+      reinterpret_cast<float4*>(lf)[0] = make_float4(f[0], f[1], f[2], f[3]);
+      reinterpret_cast<float4*>(lf)[1] = make_float4(f[4], f[5], f[6], f[7]);
+    } else {
+      for (int j = 0; j < n; ++j) {
         li[j] = a[j];
-        lf[j] = log_sigmoid<ACC>(f[j]);
+        lf[j] = f[j];
       }
     }
   }
@@ -79,12 +84,10 @@ __global__ void __launch_bounds__(256) prologue_kernel(const Params p) {
 template <typename T>
 __global__ void __launch_bounds__(256) epilogue_kernel(const Params p) {
   constexpr bool ACC = sizeof(T) == 4;
-  const int vpr = (p.dim + 7) / 8;
-  const int64_t total = p.rows * vpr;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / vpr;
-    const int c = (int)(i % vpr) * 8;
-    const int n = min(8, p.dim - c);
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= p.dim) return;
+  const int n = min(8, p.dim - c);
+  for (int64_t r = blockIdx.y; r < p.rows; r += gridDim.y) {
     const T* hp = static_cast<const T*>(p.h) + r * p.sh + c;
     const T* op = static_cast<const T*>(p.op) + r * p.so + c;
     const T* xp = static_cast<const T*>(p.xg) + r * p.sx + c;
@@ -123,10 +126,10 @@ static hxm_status fill(const hxm_mlstm_gates_args* a, Params& p, const char* who
   return HXM_OK;
 }
 
-static unsigned grid_for(const Params& p) {
-  const int64_t total = p.rows * ((p.dim + 7) / 8);
-  const int64_t blocks = (total + 255) / 256;
-  return (unsigned)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+static dim3 grid_for(const Params& p) {
+  const int vec_blocks = (p.dim + 8 * 256 - 1) / (8 * 256);
+  const int64_t rows = p.rows < 65535 ? p.rows : 65535;
+  return dim3((unsigned)vec_blocks, (unsigned)(rows > 0 ? rows : 1));
 }
 
 }  // namespace gates
