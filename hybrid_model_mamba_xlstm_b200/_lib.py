@@ -41,6 +41,18 @@ class ScanArgs(ct.Structure):
     ]
 
 
+class ScanBwdArgs(ct.Structure):
+    _fields_ = [
+        ("fwd", ScanArgs),
+        ("struct_size", ct.c_size_t),
+        ("dout", ct.c_void_p), ("dout_stride", _i64x3),
+        ("du", ct.c_void_p), ("ddelta", ct.c_void_p), ("dz", ct.c_void_p),
+        ("dA", ct.c_void_p), ("dB", ct.c_void_p), ("dC", ct.c_void_p), ("dD", ct.c_void_p),
+        ("ddelta_bias", ct.c_void_p), ("dh0", ct.c_void_p),
+        ("workspace", ct.c_void_p), ("workspace_bytes", ct.c_size_t),
+    ]
+
+
 class MlstmArgs(ct.Structure):
     _fields_ = [
         ("struct_size", ct.c_size_t),
@@ -136,6 +148,8 @@ SYMBOLS = {
     "hxm_abi_version": (ct.c_int, []),
     "hxm_last_error_string": (ct.c_char_p, []),
     "hxm_selective_scan_fwd": (ct.c_int, [ct.POINTER(ScanArgs), ct.c_void_p]),
+    "hxm_selective_scan_bwd_workspace_size": (ct.c_size_t, [ct.POINTER(ScanBwdArgs)]),
+    "hxm_selective_scan_bwd": (ct.c_int, [ct.POINTER(ScanBwdArgs), ct.c_void_p]),
     "hxm_mlstm_workspace_size": (ct.c_size_t, [ct.POINTER(MlstmArgs)]),
     "hxm_mlstm_chunkwise_fwd": (ct.c_int, [ct.POINTER(MlstmArgs), ct.c_void_p]),
     "hxm_mlstm_chunkwise_fwd_noalloc": (ct.c_int, [ct.POINTER(MlstmArgs), ct.c_void_p]),

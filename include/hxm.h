@@ -92,6 +92,28 @@ typedef struct hxm_scan_args {
 
 hxm_status hxm_selective_scan_fwd(const hxm_scan_args* args, void* stream);
 
+/* Selective scan backward (Euler discretization).                           */
+/* Replaces the recompute-under-autograd backward of SelectiveScanFunction   */
+/*   (hybrid_xmamba/kernels/selective_scan/scan_interface.py:62-100).        */
+/* Inputs as hxm_scan_args (u, delta, A, B, C, D, z, delta_bias, h0, z_mode, */
+/* delta_softplus; discretization must be 0) plus dout (b, t, d) strided.    */
+/* Outputs, fp32 and dense: du, ddelta (delta's pre-softplus input), dz      */
+/* (b, t, d); dA (d, n); dB, dC (b, t, n); dD, ddelta_bias (d); dh0 (b, d, n).*/
+/* Any output may be NULL when not needed (the sums are still consistent).   */
+/* The per-channel states are recomputed from checkpoints every 16 steps     */
+/* kept in a workspace of hxm_selective_scan_bwd_workspace_size() bytes.     */
+typedef struct hxm_scan_bwd_args {
+  hxm_scan_args fwd;        /* fwd.struct_size = sizeof(hxm_scan_args); y, hT unused */
+  size_t struct_size;       /* sizeof(hxm_scan_bwd_args)                     */
+  const void* dout;   int64_t dout_stride[3];
+  float* du; float* ddelta; float* dz;
+  float* dA; float* dB; float* dC; float* dD; float* ddelta_bias; float* dh0;
+  void* workspace; size_t workspace_bytes;
+} hxm_scan_bwd_args;
+
+size_t hxm_selective_scan_bwd_workspace_size(const hxm_scan_bwd_args* args);
+hxm_status hxm_selective_scan_bwd(const hxm_scan_bwd_args* args, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* 2. mLSTM chunkwise forward ("TFLA")                                        */
 /*                                                                           */

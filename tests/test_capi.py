@@ -40,7 +40,8 @@ def test_struct_sizes_match_header_layout():
     for cls, fn in [(_lib.ScanArgs, "hxm_selective_scan_fwd"), (_lib.MlstmArgs, "hxm_mlstm_chunkwise_fwd"),
                     (_lib.SsdArgs, "hxm_ssd_chunk_scan_fwd"), (_lib.SlstmArgs, "hxm_slstm_scan_fwd"),
                     (_lib.ConvArgs, "hxm_causal_conv1d_fwd"), (_lib.RmsnormArgs, "hxm_rmsnorm_fwd"),
-                    (_lib.MlstmGatesArgs, "hxm_mlstm_gate_prologue"), (_lib.MlstmGatesArgs, "hxm_mlstm_gate_epilogue")]:
+                    (_lib.MlstmGatesArgs, "hxm_mlstm_gate_prologue"), (_lib.MlstmGatesArgs, "hxm_mlstm_gate_epilogue"),
+                    (_lib.ScanBwdArgs, "hxm_selective_scan_bwd")]:
         a = cls()
         a.struct_size = ct.sizeof(a) + 8
         st = getattr(_lib.lib(), fn)(ct.byref(a), None)
