@@ -72,11 +72,12 @@ struct Layout {
   static constexpr int kOnes = kN + DK / 64 * 2048;  // K-major [16][128]: 2 panels of 2 KB
   static constexpr int kMisc = kOnes + 2 * 2048;
   // misc: row vectors and barriers
-  static constexpr int kRowB = kMisc;                 // float[128] b_t * log2e
-  static constexpr int kRowU = kRowB + 512;           // float[128] u_s * log2e
-  static constexpr int kRowM = kRowU + 512;           // float[128] M_t * log2e
-  static constexpr int kRowK = kRowM + 512;           // float[128] kscale_s
-  static constexpr int kRed = kRowK + 512;            // float[64] reductions
+  // per-chunk row vectors, double buffered (chunk c and chunk c + 1)
+  static constexpr int kRowB = kMisc;                 // float[2][128] b_t * log2e
+  static constexpr int kRowU = kRowB + 1024;          // float[2][128] u_s * log2e
+  static constexpr int kRowM = kRowU + 1024;          // float[2][128] M_t * log2e
+  static constexpr int kRowK = kRowM + 1024;          // float[2][128] kscale_s
+  static constexpr int kRed = kRowK + 1024;           // float[64] reductions
   static constexpr int kBar = kRed + 256;             // 2 x uint64
   static constexpr int kTmemSlot = kBar + 16;
   static constexpr int kAbort = kTmemSlot + 4;
@@ -134,10 +135,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzled panels
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  float* rowB = reinterpret_cast<float*>(sm + Lt::kRowB);
-  float* rowU = reinterpret_cast<float*>(sm + Lt::kRowU);
-  float* rowM = reinterpret_cast<float*>(sm + Lt::kRowM);
-  float* rowK = reinterpret_cast<float*>(sm + Lt::kRowK);
+  float* rowB0 = reinterpret_cast<float*>(sm + Lt::kRowB);
+  float* rowU0 = reinterpret_cast<float*>(sm + Lt::kRowU);
+  float* rowM0 = reinterpret_cast<float*>(sm + Lt::kRowM);
+  float* rowK0 = reinterpret_cast<float*>(sm + Lt::kRowK);
   float* red = reinterpret_cast<float*>(sm + Lt::kRed);
   uint64_t* bar_load = reinterpret_cast<uint64_t*>(sm + Lt::kBar);
   uint64_t* bar_mma = bar_load + 1;
@@ -260,6 +261,47 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float dtb = (MODE == kSsd && p.dt_bias) ? p.dt_bias[h] : 0.f;
   const float Dh = (MODE == kSsd && p.Dskip) ? p.Dskip[h] : 0.f;
 
+  // Gates of chunk cc into row-vector slot cc & 1: b_t = cumsum log f, u_s,
+  // the stabilizers M_t / m_new (from m_in, the state's scale entering the
+  // chunk) and the state's decay rho.  Every thread takes part (block scans).
+  auto compute_gates = [&](int cc, float m_in, float& rho_out, float& m_out) {
+    const int tgc = cc * kC + tid;
+    const bool v = tgc < p.seqlen;
+    float li, lf;
+    if (MODE == kMlstm) {
+      li = v ? p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tgc * p.sg0[2]] : -INFINITY;
+      lf = v ? p.g1[b * p.sg1[0] + h * p.sg1[1] + (int64_t)tgc * p.sg1[2]] : 0.f;
+    } else {
+      float dtv = v ? p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tgc * p.sg0[2]] + dtb : 0.f;
+      if (p.dt_softplus) dtv = (dtv > 20.f) ? dtv : log1pf(__expf(dtv));
+      li = (v && dtv > 0.f) ? __logf(dtv) : -INFINITY;
+      lf = v ? dtv * A_h : 0.f;
+    }
+    const float bt = block_incl_sum(lf, red);
+    const float g = bcast_from(bt, kC - 1, red);
+    const float us = li - bt;
+    float Mt, m_new;
+    if (kNorm) {
+      const float pm = block_incl_max(us, red);
+      const float pmax = bcast_from(pm, kC - 1, red);
+      Mt = bt + fmaxf(m_in, pm);
+      m_new = g + fmaxf(m_in, pmax);
+    } else {
+      Mt = 0.f;
+      m_new = 0.f;
+    }
+    const int sl = cc & 1;
+    rowB0[sl * kC + tid] = bt * kLog2e;
+    rowU0[sl * kC + tid] = us * kLog2e;
+    rowM0[sl * kC + tid] = Mt * kLog2e;
+    rowK0[sl * kC + tid] = __expf(g + us - m_new);
+    rho_out = __expf(g + m_in - m_new);
+    m_out = m_new;
+  };
+  float rho_cur, m_new_cur;
+  compute_gates(0, m_prev, rho_cur, m_new_cur);
+  __syncthreads();
+
   int bad = 0;
   uint32_t mma_uses = 0;
 #pragma unroll 1
@@ -278,38 +320,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::mma_commit(bar_mma);
     }
-    // ---- gates (overlaps the MMA) ------------------------------------------
+    // gates of this chunk were computed during the previous chunk's MMAs
+    const int slot = c & 1;
+    float* rowB = rowB0 + slot * kC;
+    float* rowU = rowU0 + slot * kC;
+    float* rowM = rowM0 + slot * kC;
+    float* rowK = rowK0 + slot * kC;
+    const float rho = rho_cur;
     const int tg = t0 + tid;
     const bool valid = tg < p.seqlen;
-    float li, lf;
-    if (MODE == kMlstm) {
-      li = valid ? p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tg * p.sg0[2]] : -INFINITY;
-      lf = valid ? p.g1[b * p.sg1[0] + h * p.sg1[1] + (int64_t)tg * p.sg1[2]] : 0.f;
-    } else {
-      float dtv = valid ? p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tg * p.sg0[2]] + dtb : 0.f;
-      if (p.dt_softplus) dtv = (dtv > 20.f) ? dtv : log1pf(__expf(dtv));
-      li = (valid && dtv > 0.f) ? __logf(dtv) : -INFINITY;
-      lf = valid ? dtv * A_h : 0.f;
-    }
-    const float bt = block_incl_sum(lf, red);
-    const float g = bcast_from(bt, kC - 1, red);
-    const float us = li - bt;
-    float Mt, m_new;
-    if (kNorm) {
-      const float pm = block_incl_max(us, red);
-      const float pmax = bcast_from(pm, kC - 1, red);
-      Mt = bt + fmaxf(m_prev, pm);
-      m_new = g + fmaxf(m_prev, pmax);
-    } else {
-      Mt = 0.f;
-      m_new = 0.f;
-    }
-    const float rho = __expf(g + m_prev - m_new);
-    rowB[tid] = bt * kLog2e;
-    rowU[tid] = us * kLog2e;
-    rowM[tid] = Mt * kLog2e;
-    rowK[tid] = __expf(g + us - m_new);
-    __syncthreads();
     // ---- wait S; P = causal(S) * exp(b_t + u_s - M_t) -> smem (bf16) ----------
     if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
     ++mma_uses;
@@ -427,10 +446,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::mma_commit(bar_mma);
     }
+    // next chunk's gates while the tensor core works on this chunk
+    float rho_next = 1.f, m_new_next = m_new_cur;
+    if (c + 1 < nchunks) compute_gates(c + 1, m_new_cur, rho_next, m_new_next);
     if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
     ++mma_uses;
     tc::tc_fence_after();
     if (__syncthreads_or(bad)) { bad = 1; break; }
+    // SSD D skip: this row's x values from the staged V (= x) panel, before it is refilled
+    uint4 xrow[kDV / 8];
+    if (MODE == kSsd) {
+#pragma unroll
+      for (int q = 0; q < kDV / 8; ++q)
+        xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(tid, 8 * q));
+      __syncthreads();
+    }
     if (tid == 0 && c + 1 < nchunks) issue_load(c + 1);
     // ---- epilogue: output row t -------------------------------------------------
     {
@@ -447,8 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv = 1.f / den;
       const bool ok = valid;
       __nv_bfloat16* orow = p.out + b * p.so[0] + h * p.so[1] + (int64_t)tg * p.so[2] + e0;
-      const __nv_bfloat16* xrow = (MODE == kSsd) ? p.x + b * p.sx[0] + h * p.sx[1] + (int64_t)tg * p.sx[2] + e0 : nullptr;
-#pragma unroll 1
+#pragma unroll
       for (int c0 = 0; c0 < kDV; c0 += 32) {
         float hi[32], ha[32];
         tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tHint + c0), hi);
@@ -464,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (ok && Dh != 0.f && e0 + c0 < p.dv) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const uint4 w = *reinterpret_cast<const uint4*>(xrow + c0 + 8 * q);
+              const uint4 w = xrow[c0 / 8 + q];
               const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
@@ -489,7 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     snapshot();
-    m_prev = m_new;
+    m_prev = m_new_cur;
+    m_new_cur = m_new_next;
+    rho_cur = rho_next;
     tc::fence_async_smem();
     tc::tc_fence_before();
     __syncthreads();
