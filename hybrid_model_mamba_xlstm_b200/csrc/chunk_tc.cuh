@@ -361,28 +361,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    // ---- K rows *= kscale (row s = this thread) ------------------------------
-    {
-      const float ks = rowK[tid];
-#pragma unroll 1
-      for (int pnl = 0; pnl < kNP; ++pnl) {
-        unsigned char* krow = sm + Lt::kK + pnl * kPanel + tid * 128;
-#pragma unroll
-        for (int q0 = 0; q0 < 8; ++q0) {
-          const int q = (q0 + tid) & 7;  // stagger chunks across lanes: conflict-free rows
-          uint4* ptr = reinterpret_cast<uint4*>(krow + q * 16);
-          uint4 w = *ptr;
-          uint32_t* e = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&e[j]);
-            float2 f = __bfloat1622float2(x);
-            e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
-          }
-          *ptr = w;
-        }
-      }
-    }
     // ---- state *= rho (TMEM read-modify-write) -------------------------------
     if (rho != 1.f) {
 #pragma unroll 1
@@ -412,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_async_smem();
     tc::tc_fence_before();
     if (__syncthreads_or(bad)) { bad = 1; break; }
-    // ---- Hint = Q.Snap, Hintra = P.V, qn = Q.n, state += K~^T V, n += K~^T 1 ---
+    // ---- A: Hint = Q.Snap, qn = Q.n, Hintra = P.V ------------------------------
     if (tid == 0) {
       tc::tc_fence_after();
 #pragma unroll 1
@@ -430,11 +408,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mma_bf16(tm + Lt::tHintra, tc::sdesc_sw128(sbase + Lt::kP + poff, 16, 1024),
                      tc::sdesc_sw128(sbase + Lt::kV + ks * 2048, kPanel, 1024), idH, ks > 0);
       }
+      tc::mma_commit(bar_mma);
+    }
+    // next chunk's gates while the tensor core works on this chunk
+    float rho_next = 1.f, m_new_next = m_new_cur;
+    if (c + 1 < nchunks) compute_gates(c + 1, m_new_cur, rho_next, m_new_next);
+    if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
+    ++mma_uses;
+    tc::tc_fence_after();
+    // SSD D skip: this row's x values from the staged V (= x) panel, before it is scaled
+    uint4 xrow[kDV / 8];
+    if (MODE == kSsd) {
+#pragma unroll
+      for (int q = 0; q < kDV / 8; ++q)
+        xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(tid, 8 * q));
+    }
+    // ---- V rows *= kscale (row s = this thread); the normalizer's K^T operand
+    //      row 0 = kscale: the state update below is K^T (kscale . V) ---------
+    {
+      const float ks = rowK[tid];
+      unsigned char* vrow = sm + Lt::kV;
+#pragma unroll
+      for (int q = 0; q < kDV / 8; ++q) {
+        uint4* ptr = reinterpret_cast<uint4*>(vrow + tc::sw128_offset(tid, 8 * q));
+        uint4 w = *ptr;
+        uint32_t* e = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j]));
+          e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+        }
+        *ptr = w;
+      }
+      if (kNorm) {
+        __nv_bfloat16* kv = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kOnes);
+        kv[((tid / 64) * 2048 + tc::sw128_offset(0, tid % 64)) / 2] = __float2bfloat16_rn(ks);
+      }
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    if (__syncthreads_or(bad)) { bad = 1; break; }
+    // ---- B: state += K^T (kscale . V), n += K^T kscale -------------------------
+    if (tid == 0) {
+      tc::tc_fence_after();
 #pragma unroll 1
       for (int blk = 0; blk < Lt::kNB; ++blk) {
 #pragma unroll 1
         for (int ks = 0; ks < kC / 16; ++ks) {
-          // A = K~^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO = panel stride); K step = 16 rows
+          // A = K^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO = panel stride); K step = 16 rows
           const uint64_t ad = tc::sdesc_sw128(sbase + Lt::kK + (2 * blk) * kPanel + ks * 2048, kPanel, 1024);
           tc::mma_bf16(tm + Lt::tAcc + blk * 64, ad, tc::sdesc_sw128(sbase + Lt::kV + ks * 2048, kPanel, 1024),
                        idAcc, true);
@@ -446,22 +467,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::mma_commit(bar_mma);
     }
-    // next chunk's gates while the tensor core works on this chunk
-    float rho_next = 1.f, m_new_next = m_new_cur;
-    if (c + 1 < nchunks) compute_gates(c + 1, m_new_cur, rho_next, m_new_next);
-    if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
-    ++mma_uses;
-    tc::tc_fence_after();
-    if (__syncthreads_or(bad)) { bad = 1; break; }
-    // SSD D skip: this row's x values from the staged V (= x) panel, before it is refilled
-    uint4 xrow[kDV / 8];
-    if (MODE == kSsd) {
-#pragma unroll
-      for (int q = 0; q < kDV / 8; ++q)
-        xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(tid, 8 * q));
-      __syncthreads();
-    }
-    if (tid == 0 && c + 1 < nchunks) issue_load(c + 1);
     // ---- epilogue: output row t -------------------------------------------------
     {
       const float bt2 = rowB[tid], Mt2 = rowM[tid];
@@ -517,6 +522,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // ---- wait B (the state update ran under the epilogue); refill; snapshot -----
+    if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
+    ++mma_uses;
+    tc::tc_fence_after();
+    if (__syncthreads_or(bad)) { bad = 1; break; }
+    if (tid == 0 && c + 1 < nchunks) issue_load(c + 1);
     snapshot();
     m_prev = m_new_cur;
     m_new_cur = m_new_next;
