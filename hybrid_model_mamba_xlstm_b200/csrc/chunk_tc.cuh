@@ -239,18 +239,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   constexpr uint32_t kLoadBytes = (2 * kNP + 1) * kPanel;
-  auto issue_load = [&](int c) {
+  // Chunk c's operands arrive in two parts on one barrier phase: Q (free once
+  // the Hint / qn MMAs are done) and K, V (free once the state update is done).
+  auto issue_load_q = [&](int c) {
     tc::mbar_expect_tx(bar_load, kLoadBytes);
-    const int t0 = c * kC;
     const int hq = (MODE == kSsd) ? 0 : h;
 #pragma unroll 1
-    for (int pnl = 0; pnl < kNP; ++pnl) {
-      tc::tma_load_4d(sm + Lt::kQ + pnl * kPanel, &tmQ, bar_load, pnl * 64, t0, hq, b);
-      tc::tma_load_4d(sm + Lt::kK + pnl * kPanel, &tmK, bar_load, pnl * 64, t0, hq, b);
-    }
-    tc::tma_load_4d(sm + Lt::kV, &tmV, bar_load, e0, t0, h, b);
+    for (int pnl = 0; pnl < kNP; ++pnl)
+      tc::tma_load_4d(sm + Lt::kQ + pnl * kPanel, &tmQ, bar_load, pnl * 64, c * kC, hq, b);
   };
-  if (tid == 0) issue_load(0);
+  auto issue_load_kv = [&](int c) {
+    const int hq = (MODE == kSsd) ? 0 : h;
+#pragma unroll 1
+    for (int pnl = 0; pnl < kNP; ++pnl)
+      tc::tma_load_4d(sm + Lt::kK + pnl * kPanel, &tmK, bar_load, pnl * 64, c * kC, hq, b);
+    tc::tma_load_4d(sm + Lt::kV, &tmV, bar_load, e0, c * kC, h, b);
+  };
+  if (tid == 0) {
+    issue_load_q(0);
+    issue_load_kv(0);
+  }
 
   constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, false);
   constexpr uint32_t idH = tc::idesc_bf16(128, kDV, false, true);
@@ -304,10 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int bad = 0;
   uint32_t mma_uses = 0;
+  int loads_issued = 1, loads_done = 0;  // TMA load phases issued / waited (tid 0's view)
 #pragma unroll 1
   for (int c = 0; c < nchunks; ++c) {
     const int t0 = c * kC;
     if (!tc::mbar_wait(bar_load, c & 1, abort_flag)) bad = 1;
+    loads_done = c + 1;
     if (__syncthreads_or(bad)) { bad = 1; break; }
     // ---- S = Q K^T --------------------------------------------------------
     if (tid == 0) {
@@ -416,6 +426,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
     ++mma_uses;
     tc::tc_fence_after();
+    if (tid == 0 && !bad && c + 1 < nchunks) {  // the MMAs reading Q are done
+      issue_load_q(c + 1);
+      loads_issued = c + 2;
+    }
     // SSD D skip: this row's x values from the staged V (= x) panel, before it is scaled
     uint4 xrow[kDV / 8];
     if (MODE == kSsd) {
@@ -527,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ++mma_uses;
     tc::tc_fence_after();
     if (__syncthreads_or(bad)) { bad = 1; break; }
-    if (tid == 0 && c + 1 < nchunks) issue_load(c + 1);
+    if (tid == 0 && c + 1 < nchunks) issue_load_kv(c + 1);
     snapshot();
     m_prev = m_new_cur;
     m_new_cur = m_new_next;
@@ -537,6 +551,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   }
 
+  // A wait that gave up can leave a load in flight: let it land (bounded)
+  // before the shared memory is released.
+  if (bad && tid == 0 && loads_issued > loads_done) {
+    volatile int no_abort = 0;
+    tc::mbar_wait(bar_load, (loads_issued - 1) & 1, &no_abort, 20000000ll);
+  }
+  __syncthreads();
   // ---- final state ---------------------------------------------------------------
   if (!bad) {
     tc::tc_fence_after();

@@ -47,15 +47,20 @@ HXM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait: gives up after ~`limit_cycles` SM cycles (or as soon as
 // another thread of the CTA raised *abort), raising *abort.  Returns false
 // on give-up.  Every wait of the kernels goes through this.
+// The abort flag and the clock are checked every 32 polls only: a flag read
+// per poll by every waiting thread competes with the tensor core for
+// shared-memory bandwidth.
 HXM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, long long limit_cycles = 4000000000ll) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (clock64() - t0 > limit_cycles) {
-      *abort = 1;
-      return false;
+    if ((i & 31u) == 0) {
+      if (*abort) return false;
+      if (clock64() - t0 > limit_cycles) {
+        *abort = 1;
+        return false;
+      }
     }
   }
 }
