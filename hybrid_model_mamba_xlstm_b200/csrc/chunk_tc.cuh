@@ -260,6 +260,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     issue_load_kv(0);
   }
 
+  // operand descriptors at the region bases; an MMA adds its byte offset
+  const uint64_t dQ = tc::sdesc_sw128(sbase + Lt::kQ, 16, 1024);      // K-major rows t (Q) or s (K)
+  const uint64_t dK = tc::sdesc_sw128(sbase + Lt::kK, 16, 1024);
+  const uint64_t dKT = tc::sdesc_sw128(sbase + Lt::kK, kPanel, 1024);  // K^T: MN-major, panels = 64 dk rows
+  const uint64_t dSnap = tc::sdesc_sw128(sbase + Lt::kSnap, kPanel, 1024);
+  const uint64_t dN = tc::sdesc_sw128(sbase + Lt::kN, 16, 1024);
+  const uint64_t dP = tc::sdesc_sw128(sbase + Lt::kP, 16, 1024);
+  const uint64_t dV = tc::sdesc_sw128(sbase + Lt::kV, kPanel, 1024);
+  const uint64_t dOnes = tc::sdesc_sw128(sbase + Lt::kOnes, 16, 1024);
   constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, false);
   constexpr uint32_t idH = tc::idesc_bf16(128, kDV, false, true);
   constexpr uint32_t idQN = tc::idesc_bf16(128, 16, false, false);
@@ -322,11 +331,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- S = Q K^T --------------------------------------------------------
     if (tid == 0) {
       tc::tc_fence_after();
-#pragma unroll 1
+#pragma unroll
       for (int ks = 0; ks < DK / 16; ++ks) {
         const uint32_t off = (ks / 4) * kPanel + (ks % 4) * 32;
-        tc::mma_bf16(tm + Lt::tS, tc::sdesc_sw128(sbase + Lt::kQ + off, 16, 1024),
-                     tc::sdesc_sw128(sbase + Lt::kK + off, 16, 1024), idS, ks > 0);
+        tc::mma_bf16(tm + Lt::tS, tc::desc_add(dQ, off), tc::desc_add(dK, off), idS, ks > 0);
       }
       tc::mma_commit(bar_mma);
     }
@@ -403,21 +411,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- A: Hint = Q.Snap, qn = Q.n, Hintra = P.V ------------------------------
     if (tid == 0) {
       tc::tc_fence_after();
-#pragma unroll 1
+#pragma unroll
       for (int ks = 0; ks < DK / 16; ++ks) {
-        const uint32_t qoff = (ks / 4) * kPanel + (ks % 4) * 32;
-        const uint64_t ad = tc::sdesc_sw128(sbase + Lt::kQ + qoff, 16, 1024);
-        tc::mma_bf16(tm + Lt::tHint, ad, tc::sdesc_sw128(sbase + Lt::kSnap + ks * 2048, kPanel, 1024), idH, ks > 0);
-        if (kNorm)
-          tc::mma_bf16(tm + Lt::tQN, ad,
-                       tc::sdesc_sw128(sbase + Lt::kN + (ks / 4) * 2048 + (ks % 4) * 32, 16, 1024), idQN, ks > 0);
+        const uint64_t ad = tc::desc_add(dQ, (ks / 4) * kPanel + (ks % 4) * 32);
+        tc::mma_bf16(tm + Lt::tHint, ad, tc::desc_add(dSnap, ks * 2048), idH, ks > 0);
+        if (kNorm) tc::mma_bf16(tm + Lt::tQN, ad, tc::desc_add(dN, (ks / 4) * 2048 + (ks % 4) * 32), idQN, ks > 0);
       }
-#pragma unroll 1
-      for (int ks = 0; ks < kC / 16; ++ks) {
-        const uint32_t poff = (ks / 4) * kPanel + (ks % 4) * 32;
-        tc::mma_bf16(tm + Lt::tHintra, tc::sdesc_sw128(sbase + Lt::kP + poff, 16, 1024),
-                     tc::sdesc_sw128(sbase + Lt::kV + ks * 2048, kPanel, 1024), idH, ks > 0);
-      }
+#pragma unroll
+      for (int ks = 0; ks < kC / 16; ++ks)
+        tc::mma_bf16(tm + Lt::tHintra, tc::desc_add(dP, (ks / 4) * kPanel + (ks % 4) * 32),
+                     tc::desc_add(dV, ks * 2048), idH, ks > 0);
       tc::mma_commit(bar_mma);
     }
     // next chunk's gates while the tensor core works on this chunk
@@ -465,18 +468,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- B: state += K^T (kscale . V), n += K^T kscale -------------------------
     if (tid == 0) {
       tc::tc_fence_after();
-#pragma unroll 1
+#pragma unroll
       for (int blk = 0; blk < Lt::kNB; ++blk) {
-#pragma unroll 1
+#pragma unroll
         for (int ks = 0; ks < kC / 16; ++ks) {
           // A = K^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO = panel stride); K step = 16 rows
-          const uint64_t ad = tc::sdesc_sw128(sbase + Lt::kK + (2 * blk) * kPanel + ks * 2048, kPanel, 1024);
-          tc::mma_bf16(tm + Lt::tAcc + blk * 64, ad, tc::sdesc_sw128(sbase + Lt::kV + ks * 2048, kPanel, 1024),
-                       idAcc, true);
+          const uint64_t ad = tc::desc_add(dKT, (2 * blk) * kPanel + ks * 2048);
+          tc::mma_bf16(tm + Lt::tAcc + blk * 64, ad, tc::desc_add(dV, ks * 2048), idAcc, true);
           if (kNorm)
-            tc::mma_bf16(tm + Lt::tAccN + blk * 32, ad,
-                         tc::sdesc_sw128(sbase + Lt::kOnes + (ks / 4) * 2048 + (ks % 4) * 32, 16, 1024), idAccN,
-                         true);
+            tc::mma_bf16(tm + Lt::tAccN + blk * 32, ad, tc::desc_add(dOnes, (ks / 4) * 2048 + (ks % 4) * 32),
+                         idAccN, true);
         }
       }
       tc::mma_commit(bar_mma);

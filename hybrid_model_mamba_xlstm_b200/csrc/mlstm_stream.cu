@@ -257,12 +257,13 @@ __global__ void __launch_bounds__(128, 1)
       const uint32_t qaddr = sbase + L::kRing + slot * 2 * kPanel;
       if (tid == 0 && !bad) {
         tc::tc_fence_after();
+        const uint64_t dq = tc::sdesc_sw128(qaddr, 16, 1024);
+        const uint64_t dsn = tc::sdesc_sw128(sbase + L::kSnap + pnl * 4 * 2048, kPanel, 1024);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::sdesc_sw128(qaddr + kk * 32, 16, 1024);
-          tc::mma_bf16(tm + L::tS, ad, tc::sdesc_sw128(qaddr + kPanel + kk * 32, 16, 1024), idS, pnl > 0 || kk > 0);
-          tc::mma_bf16(tm + L::tH, ad, tc::sdesc_sw128(sbase + L::kSnap + (pnl * 4 + kk) * 2048, kPanel, 1024), idH,
-                       pnl > 0 || kk > 0);
+          const uint64_t ad = tc::desc_add(dq, kk * 32);
+          tc::mma_bf16(tm + L::tS, ad, tc::desc_add(dq, kPanel + kk * 32), idS, pnl > 0 || kk > 0);
+          tc::mma_bf16(tm + L::tH, ad, tc::desc_add(dsn, kk * 2048), idH, pnl > 0 || kk > 0);
         }
         tc::mma_commit(&empty[slot]);
       }
@@ -349,10 +350,12 @@ __global__ void __launch_bounds__(128, 1)
     // ---- H += P V;  pass B: state += Kh^T V, n += Kh^T 1 ------------------------------------
     if (tid == 0) {
       tc::tc_fence_after();
+      const uint64_t dp = tc::sdesc_sw128(sbase + L::kP, 16, 1024);
+      const uint64_t dv = tc::sdesc_sw128(sbase + L::kV, kPanel, 1024);
 #pragma unroll
       for (int ks = 0; ks < kC / 16; ++ks)
-        tc::mma_bf16(tm + L::tH, tc::sdesc_sw128(sbase + L::kP + (ks / 4) * kPanel + (ks % 4) * 32, 16, 1024),
-                     tc::sdesc_sw128(sbase + L::kV + ks * 2048, kPanel, 1024), idH, true);
+        tc::mma_bf16(tm + L::tH, tc::desc_add(dp, (ks / 4) * kPanel + (ks % 4) * 32), tc::desc_add(dv, ks * 2048),
+                     idH, true);
       tc::mma_commit(bar_h);
     }
 #pragma unroll 1
@@ -362,13 +365,14 @@ __global__ void __launch_bounds__(128, 1)
       const uint32_t kaddr = sbase + L::kRing + slot * 2 * kPanel;
       if (tid == 0 && !bad) {
         tc::tc_fence_after();
+        const uint64_t dk = tc::sdesc_sw128(kaddr, kPanel, 1024);
+        const uint64_t dv = tc::sdesc_sw128(sbase + L::kV, kPanel, 1024);
+        const uint64_t d1 = tc::sdesc_sw128(sbase + L::kOnes, 16, 1024);
 #pragma unroll
         for (int ks = 0; ks < kC / 16; ++ks) {
-          const uint64_t ad = tc::sdesc_sw128(kaddr + ks * 2048, kPanel, 1024);
-          tc::mma_bf16(tm + L::tAcc + blk * 64, ad, tc::sdesc_sw128(sbase + L::kV + ks * 2048, kPanel, 1024), idAcc,
-                       true);
-          tc::mma_bf16(tm + L::tN + blk * 16, ad,
-                       tc::sdesc_sw128(sbase + L::kOnes + (ks / 4) * 2048 + (ks % 4) * 32, 16, 1024), idN, true);
+          const uint64_t ad = tc::desc_add(dk, ks * 2048);
+          tc::mma_bf16(tm + L::tAcc + blk * 64, ad, tc::desc_add(dv, ks * 2048), idAcc, true);
+          tc::mma_bf16(tm + L::tN + blk * 16, ad, tc::desc_add(d1, (ks / 4) * 2048 + (ks % 4) * 32), idN, true);
         }
         tc::mma_commit(&empty[slot]);
       }

@@ -171,6 +171,14 @@ HXM_DEV uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_by
   return d;
 }
 
+// The descriptor of the same operand `bytes` further on (a multiple of 16):
+// the start address field is the low 14 bits, and shared-memory addresses stay
+// below 2^18, so the add never carries out of the field.  With a compile-time
+// offset this is one integer add, which keeps the issuing thread's per-MMA
+// instruction chain short (the issue loop, not the tensor core, otherwise
+// sets the MMA rate).
+HXM_DEV uint64_t desc_add(uint64_t desc, uint32_t bytes) { return desc + (uint64_t)(bytes >> 4); }
+
 // kind::f16 instruction descriptor: bf16 x bf16 -> fp32, M x N tile.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
