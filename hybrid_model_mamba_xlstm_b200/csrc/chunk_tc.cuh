@@ -16,10 +16,21 @@
 // algebra is the reference recurrence (tfla_interface.py:113-137, and the
 // Euler scan of scan_interface.py:132-150 for SSD) regrouped by chunk.
 //
+// Separable weights: with r_t = b_t - M_t, exp(r_t + u_s) = R_t C_s where
+// R_t = exp(r_t + c0) and C_s = exp(u_s - c0) for a per-chunk shift c0.  When
+// a c0 keeps every R_t and C_s within e^+-40 (checked per chunk on the
+// device), P is formed as causal(S) * C_s (one multiply per element, no
+// exponential) and R_t is applied to the row's Hintra and rowsum in the
+// epilogue; otherwise (a gate range wider than ~e^80 inside one chunk, or the
+// ragged last chunk) each element takes its own exponential.
+//
 // Operands arrive by TMA (128B swizzle) into shared memory; the tensor-core
 // operands written by threads (P, the bf16 state snapshot, n) use the same
-// swizzled layouts.  One elected thread issues TMA and MMA; all 4 warps do
-// the element-wise work (warp w owns TMEM lanes 32w..32w+31).
+// swizzled layouts.  One elected thread issues TMA and MMA.  The 8 warps do
+// the element-wise work: warp w reads TMEM lanes 32 (w % 4) .. + 31 (one
+// chunk row or state row per lane), and the two warps of a lane quarter split
+// the columns (half h = w / 4 takes columns 32h .. 32h + 31 of each 64-wide
+// block, and of P the 64-column half h).
 #pragma once
 
 #include "common.cuh"
@@ -30,7 +41,7 @@ namespace chunk {
 
 constexpr int kC = 128;      // chunk length (TMEM lanes / MMA M)
 constexpr int kDV = 64;      // value columns per CTA
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr int kPanel = 16384;  // one 128-row x 128-byte swizzled panel
 
 enum Mode : int { kMlstm = 0, kSsd = 1 };
@@ -71,14 +82,10 @@ struct Layout {
   static constexpr int kN = kSnap + DK * 128;   // n snapshot, K-major [16][DK]: DK/64 panels of 2 KB
   static constexpr int kOnes = kN + DK / 64 * 2048;  // K-major [16][128]: 2 panels of 2 KB
   static constexpr int kMisc = kOnes + 2 * 2048;
-  // misc: row vectors and barriers
-  // per-chunk row vectors, double buffered (chunk c and chunk c + 1)
-  static constexpr int kRowB = kMisc;                 // float[2][128] b_t * log2e
-  static constexpr int kRowU = kRowB + 1024;          // float[2][128] u_s * log2e
-  static constexpr int kRowM = kRowU + 1024;          // float[2][128] M_t * log2e
-  static constexpr int kRowK = kRowM + 1024;          // float[2][128] kscale_s
-  static constexpr int kRed = kRowK + 1024;           // float[64] reductions
-  static constexpr int kBar = kRed + 256;             // 2 x uint64
+  static constexpr int kColW = kMisc;          // float[128]: C_s (separable) or u_s * log2e, by column s
+  static constexpr int kDen = kColW + 512;     // float[2][128]: rowsum(P) partials of the two column halves
+  static constexpr int kRed = kDen + 1024;     // float[64] reductions
+  static constexpr int kBar = kRed + 256;      // 2 x uint64
   static constexpr int kTmemSlot = kBar + 16;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kBytes = kAbort + 12;
@@ -88,42 +95,77 @@ struct Layout {
   static_assert(tAccN + 32 * kNB <= 512, "TMEM layout");
 };
 
-// ---- block-wide scans over the 128 rows (thread t owns row t) -------------
-HXM_DEV float block_incl_sum(float v, float* red) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+// ---- scans over the 128 chunk rows ------------------------------------------
+// Each half of the CTA (warps 0-3, warps 4-7) holds all 128 rows (row =
+// 32 (warp % 4) + lane) and scans them on its own; red = float[64].
+HXM_DEV float rows_incl_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3, hf = threadIdx.x >> 7;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const float n = __shfl_up_sync(0xffffffffu, v, o);
     if (lane >= o) v += n;
   }
-  if (lane == 31) red[w] = v;
+  if (lane == 31) red[hf * 16 + w] = v;
   __syncthreads();
   float pre = 0.f;
-  for (int i = 0; i < w; ++i) pre += red[i];
+  for (int i = 0; i < w; ++i) pre += red[hf * 16 + i];
   __syncthreads();
   return v + pre;
 }
-HXM_DEV float block_incl_max(float v, float* red) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+HXM_DEV float rows_incl_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3, hf = threadIdx.x >> 7;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const float n = __shfl_up_sync(0xffffffffu, v, o);
     if (lane >= o) v = fmaxf(v, n);
   }
-  if (lane == 31) red[w] = v;
+  if (lane == 31) red[hf * 16 + w] = v;
   __syncthreads();
   float pre = -INFINITY;
-  for (int i = 0; i < w; ++i) pre = fmaxf(pre, red[i]);
+  for (int i = 0; i < w; ++i) pre = fmaxf(pre, red[hf * 16 + i]);
   __syncthreads();
   return fmaxf(v, pre);
 }
-HXM_DEV float bcast_from(float v, int src, float* red) {
-  if (threadIdx.x == src) red[8] = v;
+// value of row `src` to every thread of the half
+HXM_DEV float rows_bcast(float v, int src, float* red) {
+  const int hf = threadIdx.x >> 7;
+  if ((threadIdx.x & 127) == src) red[hf * 16 + 8] = v;
   __syncthreads();
-  const float r = red[8];
+  const float r = red[hf * 16 + 8];
   __syncthreads();
   return r;
 }
+// component-wise max over the 128 rows of four values
+HXM_DEV float4 rows_max4(float4 v, float* red) {
+  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3, hf = threadIdx.x >> 7;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    v.x = fmaxf(v.x, __shfl_xor_sync(0xffffffffu, v.x, o));
+    v.y = fmaxf(v.y, __shfl_xor_sync(0xffffffffu, v.y, o));
+    v.z = fmaxf(v.z, __shfl_xor_sync(0xffffffffu, v.z, o));
+    v.w = fmaxf(v.w, __shfl_xor_sync(0xffffffffu, v.w, o));
+  }
+  float4* r4 = reinterpret_cast<float4*>(red + 32 + hf * 16);
+  if (lane == 0) r4[w] = v;
+  __syncthreads();
+  float4 r = r4[0];
+#pragma unroll
+  for (int i = 1; i < 4; ++i) {
+    const float4 o = r4[i];
+    r = make_float4(fmaxf(r.x, o.x), fmaxf(r.y, o.y), fmaxf(r.z, o.z), fmaxf(r.w, o.w));
+  }
+  __syncthreads();
+  return r;
+}
+
+// Per-row gate values of one chunk, held by the threads of that row.
+struct RowGates {
+  float r2;  // (b_t - M_t) * log2 e: the per-element exponent's row part (fallback)
+  float sc;  // weight of the carried state: exp(b_t + m_in - M_t)
+  float R;   // separable row factor exp(b_t - M_t + c0) (1 in the fallback)
+  float F;   // normalizer floor exp(-M_t) (mLSTM)
+  float ks;  // key scale of row s: exp(g + u_s - m_new)
+};
 
 template <int DK, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -135,10 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzled panels
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  float* rowB0 = reinterpret_cast<float*>(sm + Lt::kRowB);
-  float* rowU0 = reinterpret_cast<float*>(sm + Lt::kRowU);
-  float* rowM0 = reinterpret_cast<float*>(sm + Lt::kRowM);
-  float* rowK0 = reinterpret_cast<float*>(sm + Lt::kRowK);
+  float* colw = reinterpret_cast<float*>(sm + Lt::kColW);
+  float* denp = reinterpret_cast<float*>(sm + Lt::kDen);
   float* red = reinterpret_cast<float*>(sm + Lt::kRed);
   uint64_t* bar_load = reinterpret_cast<uint64_t*>(sm + Lt::kBar);
   uint64_t* bar_mma = bar_load + 1;
@@ -146,11 +186,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + Lt::kAbort);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wq = warp & 3;         // TMEM lane quarter
+  const int hf = warp >> 2;        // column half
+  const int row = wq * 32 + lane;  // chunk row t / state row within a 128-row block
+  const int ch = 32 * hf;          // this thread's first column of a 64-wide block
   const int e0 = blockIdx.x * kDV;
   const int h = blockIdx.y, b = blockIdx.z;
   const int bh = b * p.heads + h;
   const int nchunks = (p.seqlen + kC - 1) / kC;
   const uint32_t sbase = smem_u32(sm);
+  const uint32_t tlane = (uint32_t)(wq * 32) << 16;  // this warp's TMEM lane offset
 
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
@@ -175,31 +220,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   tc::tc_fence_after();
-  const uint32_t tm = *tmem_slot;
+  const uint32_t tm = *tmem_slot + tlane;
 
   // ---- initial state -> TMEM (fp32) ----------------------------------------
   float m_prev = (kNorm && p.m0) ? p.m0[bh] : 0.f;
 #pragma unroll 1
   for (int blk = 0; blk < Lt::kNB; ++blk) {
-    const int row = blk * 128 + warp * 32 + lane;  // state row (dk index)
-#pragma unroll 1
-    for (int c0 = 0; c0 < kDV; c0 += 32) {
-      float v[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int col = e0 + c0 + j;
-        float x = 0.f;
-        if (p.C0 && col < p.dv)
-          x = p.state_t ? p.C0[((int64_t)bh * p.dv + col) * DK + row] : p.C0[((int64_t)bh * DK + row) * p.dv + col];
-        v[j] = x;
-      }
-      tc::tmem_st32(tc::taddr(tm, warp * 32, Lt::tAcc + blk * 64 + c0), v);
-    }
+    const int srow = blk * 128 + row;  // state row (dk index)
     float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = 0.f;
-    if (kNorm && p.n0) v[0] = p.n0[(int64_t)bh * DK + row];
-    tc::tmem_st32(tc::taddr(tm, warp * 32, Lt::tAccN + blk * 32), v);
+    for (int j = 0; j < 32; ++j) {
+      const int col = e0 + ch + j;
+      float x = 0.f;
+      if (p.C0 && col < p.dv)
+        x = p.state_t ? p.C0[((int64_t)bh * p.dv + col) * DK + srow] : p.C0[((int64_t)bh * DK + srow) * p.dv + col];
+      v[j] = x;
+    }
+    tc::tmem_st32(tm + Lt::tAcc + blk * 64 + ch, v);
+    if (hf == 1) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      if (kNorm && p.n0) v[0] = p.n0[(int64_t)bh * DK + srow];
+      tc::tmem_st32(tm + Lt::tAccN + blk * 32, v);
+    }
   }
   tc::tmem_wait_st();
 
@@ -207,29 +250,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto snapshot = [&]() {
 #pragma unroll 1
     for (int blk = 0; blk < Lt::kNB; ++blk) {
-      const int row = blk * 128 + warp * 32 + lane;
-      unsigned char* srow = sm + Lt::kSnap;
-#pragma unroll 1
-      for (int c0 = 0; c0 < kDV; c0 += 32) {
-        float v[32];
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tAcc + blk * 64 + c0), v);
-        tc::tmem_wait_ld();
+      const int srow = blk * 128 + row;
+      unsigned char* sp = sm + Lt::kSnap;
+      float v[32];
+      tc::tmem_ld32(tm + Lt::tAcc + blk * 64 + ch, v);
+      tc::tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 w;
-          w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
-          w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
-          w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
-          w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
-          *reinterpret_cast<uint4*>(srow + tc::sw128_offset(row, c0 + 8 * q)) = w;
-        }
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
+        w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
+        w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
+        w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
+        *reinterpret_cast<uint4*>(sp + tc::sw128_offset(srow, ch + 8 * q)) = w;
       }
-      if (kNorm) {
-        float v[32];
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tAccN + blk * 32), v);
+      if (kNorm && hf == 1) {
+        const float n = tc::tmem_ld1(tm + Lt::tAccN + blk * 32);
         tc::tmem_wait_ld();
-        __nv_bfloat16* nb = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kN + (row / 64) * 2048 + tc::sw128_offset(0, row % 64));
-        *nb = __float2bfloat16_rn(v[0]);
+        __nv_bfloat16* nb = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kN + (srow / 64) * 2048 + tc::sw128_offset(0, srow % 64));
+        *nb = __float2bfloat16_rn(n);
       }
     }
   };
@@ -278,11 +317,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float dtb = (MODE == kSsd && p.dt_bias) ? p.dt_bias[h] : 0.f;
   const float Dh = (MODE == kSsd && p.Dskip) ? p.Dskip[h] : 0.f;
 
-  // Gates of chunk cc into row-vector slot cc & 1: b_t = cumsum log f, u_s,
-  // the stabilizers M_t / m_new (from m_in, the state's scale entering the
-  // chunk) and the state's decay rho.  Every thread takes part (block scans).
-  auto compute_gates = [&](int cc, float m_in, float& rho_out, float& m_out) {
-    const int tgc = cc * kC + tid;
+  // Gates of chunk cc: b_t = cumsum log f, u_s, the stabilizers M_t / m_new
+  // (from m_in, the state's scale entering the chunk), the state's decay rho,
+  // this row's RowGates, whether the weights separate, and the column vector
+  // colw (C_s, or u_s * log2e).  Every thread takes part (row scans); colw is
+  // written after the caller's last read of the previous chunk's values.
+  auto compute_gates = [&](int cc, float m_in, RowGates& rg, float& rho_out, float& m_out, bool& sep_out) {
+    const int tgc = cc * kC + row;
     const bool v = tgc < p.seqlen;
     float li, lf;
     if (MODE == kMlstm) {
@@ -294,29 +335,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       li = (v && dtv > 0.f) ? __logf(dtv) : -INFINITY;
       lf = v ? dtv * A_h : 0.f;
     }
-    const float bt = block_incl_sum(lf, red);
-    const float g = bcast_from(bt, kC - 1, red);
+    const float bt = rows_incl_sum(lf, red);
+    const float g = rows_bcast(bt, kC - 1, red);
     const float us = li - bt;
-    float Mt, m_new;
+    float rt, m_new;
     if (kNorm) {
-      const float pm = block_incl_max(us, red);
-      const float pmax = bcast_from(pm, kC - 1, red);
-      Mt = bt + fmaxf(m_in, pm);
+      const float pm = rows_incl_max(us, red);
+      const float pmax = rows_bcast(pm, kC - 1, red);
+      const float Mt = bt + fmaxf(m_in, pm);
       m_new = g + fmaxf(m_in, pmax);
+      rt = bt - Mt;
+      rg.sc = __expf(bt + m_in - Mt);
+      rg.F = __expf(-Mt);
     } else {
-      Mt = 0.f;
       m_new = 0.f;
+      rt = bt;
+      rg.sc = __expf(bt);
+      rg.F = 0.f;
     }
-    const int sl = cc & 1;
-    rowB0[sl * kC + tid] = bt * kLog2e;
-    rowU0[sl * kC + tid] = us * kLog2e;
-    rowM0[sl * kC + tid] = Mt * kLog2e;
-    rowK0[sl * kC + tid] = __expf(g + us - m_new);
+    rg.ks = __expf(g + us - m_new);
+    rg.r2 = rt * kLog2e;
     rho_out = __expf(g + m_in - m_new);
     m_out = m_new;
+    // a shift c0 with every rt + c0 and us - c0 inside [-40, 40]?
+    const float4 ext = rows_max4(make_float4(rt, -rt, us, -us), red);  // max r, -min r, max u, -min u
+    const float lo = fmaxf(ext.y - 40.f, ext.z - 40.f);
+    const float hi = fminf(40.f - ext.x, 40.f - ext.w);
+    const bool sep = lo <= hi;  // false for any non-finite extreme (e.g. a row past the end)
+    const float c0 = 0.5f * (lo + hi);
+    rg.R = sep ? __expf(rt + c0) : 1.f;
+    if (hf == 0) colw[row] = sep ? __expf(us - c0) : us * kLog2e;
+    sep_out = sep;
   };
+  RowGates gc;
   float rho_cur, m_new_cur;
-  compute_gates(0, m_prev, rho_cur, m_new_cur);
+  bool sep_cur;
+  compute_gates(0, m_prev, gc, rho_cur, m_new_cur, sep_cur);
   __syncthreads();
 
   int bad = 0;
@@ -334,40 +388,59 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int ks = 0; ks < DK / 16; ++ks) {
         const uint32_t off = (ks / 4) * kPanel + (ks % 4) * 32;
-        tc::mma_bf16(tm + Lt::tS, tc::desc_add(dQ, off), tc::desc_add(dK, off), idS, ks > 0);
+        tc::mma_bf16(*tmem_slot + Lt::tS, tc::desc_add(dQ, off), tc::desc_add(dK, off), idS, ks > 0);
       }
       tc::mma_commit(bar_mma);
     }
-    // gates of this chunk were computed during the previous chunk's MMAs
-    const int slot = c & 1;
-    float* rowB = rowB0 + slot * kC;
-    float* rowU = rowU0 + slot * kC;
-    float* rowM = rowM0 + slot * kC;
-    float* rowK = rowK0 + slot * kC;
-    const float rho = rho_cur;
-    const int tg = t0 + tid;
+    const int tg = t0 + row;
     const bool valid = tg < p.seqlen;
-    // ---- wait S; P = causal(S) * exp(b_t + u_s - M_t) -> smem (bf16) ----------
+    // ---- wait S; P = causal(S) * weight -> smem (bf16), this half's 64 columns ----
     if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
     ++mma_uses;
     tc::tc_fence_after();
-    float den_intra = 0.f;
     {
-      const float bm = rowB[tid] - rowM[tid];
+      float den = 0.f;
+      unsigned char* pp = sm + Lt::kP + hf * kPanel;
 #pragma unroll 1
-      for (int s0 = 0; s0 < kC; s0 += 32) {
+      for (int sb = 0; sb < 2; ++sb) {
+        const int s0 = 64 * hf + 32 * sb;
         float v[32];
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tS + s0), v);
-        tc::tmem_wait_ld();
+        if (s0 <= wq * 32 + 31) {  // warp-uniform: some row of this warp reaches column s0
+          tc::tmem_ld32(tm + Lt::tS + s0, v);
+          tc::tmem_wait_ld();
+          const float4* cw = reinterpret_cast<const float4*>(colw + s0);
+          if (sep_cur) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int s = s0 + j;
-          const float w = ex2_approx(bm + rowU[s]);
-          const float pv = (s <= tid) ? v[j] * w : 0.f;
-          v[j] = pv;
-          den_intra += pv;
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 c4 = cw[j4];
+              const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int j = 4 * j4 + k;
+                const float pv = (s0 + j <= row) ? v[j] * cv[k] : 0.f;
+                v[j] = pv;
+                den += pv;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 c4 = cw[j4];
+              const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int j = 4 * j4 + k;
+                const float w = ex2_approx(gc.r2 + cv[k]);
+                const float pv = (s0 + j <= row) ? v[j] * w : 0.f;
+                v[j] = pv;
+                den += pv;
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
-        unsigned char* prow = sm + Lt::kP + (s0 / 64) * kPanel;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 w;
@@ -375,32 +448,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
           w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
           w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
-          *reinterpret_cast<uint4*>(prow + tc::sw128_offset(tid, (s0 % 64) + 8 * q)) = w;
+          *reinterpret_cast<uint4*>(pp + tc::sw128_offset(row, 32 * sb + 8 * q)) = w;
         }
       }
+      denp[hf * kC + row] = den;
     }
-    // ---- state *= rho (TMEM read-modify-write) -------------------------------
+    // ---- state *= rho (TMEM read-modify-write, this half's columns) -------------
+    const float rho = rho_cur;
     if (rho != 1.f) {
 #pragma unroll 1
       for (int blk = 0; blk < Lt::kNB; ++blk) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < kDV; c0 += 32) {
-          float v[32];
-          const uint32_t a = tc::taddr(tm, warp * 32, Lt::tAcc + blk * 64 + c0);
-          tc::tmem_ld32(a, v);
+        float v[32];
+        const uint32_t a = tm + Lt::tAcc + blk * 64 + ch;
+        tc::tmem_ld32(a, v);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= rho;
+        tc::tmem_st32(a, v);
+        if (kNorm && hf == 1) {
+          const uint32_t an = tm + Lt::tAccN + blk * 32;
+          tc::tmem_ld32(an, v);
           tc::tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] *= rho;
-          tc::tmem_st32(a, v);
-        }
-        if (kNorm) {
-          float v[32];
-          const uint32_t a = tc::taddr(tm, warp * 32, Lt::tAccN + blk * 32);
-          tc::tmem_ld32(a, v);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= rho;
-          tc::tmem_st32(a, v);
+          tc::tmem_st32(an, v);
         }
       }
       tc::tmem_wait_st();
@@ -411,21 +482,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- A: Hint = Q.Snap, qn = Q.n, Hintra = P.V ------------------------------
     if (tid == 0) {
       tc::tc_fence_after();
+      const uint32_t tb = *tmem_slot;
 #pragma unroll
       for (int ks = 0; ks < DK / 16; ++ks) {
         const uint64_t ad = tc::desc_add(dQ, (ks / 4) * kPanel + (ks % 4) * 32);
-        tc::mma_bf16(tm + Lt::tHint, ad, tc::desc_add(dSnap, ks * 2048), idH, ks > 0);
-        if (kNorm) tc::mma_bf16(tm + Lt::tQN, ad, tc::desc_add(dN, (ks / 4) * 2048 + (ks % 4) * 32), idQN, ks > 0);
+        tc::mma_bf16(tb + Lt::tHint, ad, tc::desc_add(dSnap, ks * 2048), idH, ks > 0);
+        if (kNorm) tc::mma_bf16(tb + Lt::tQN, ad, tc::desc_add(dN, (ks / 4) * 2048 + (ks % 4) * 32), idQN, ks > 0);
       }
 #pragma unroll
       for (int ks = 0; ks < kC / 16; ++ks)
-        tc::mma_bf16(tm + Lt::tHintra, tc::desc_add(dP, (ks / 4) * kPanel + (ks % 4) * 32),
+        tc::mma_bf16(tb + Lt::tHintra, tc::desc_add(dP, (ks / 4) * kPanel + (ks % 4) * 32),
                      tc::desc_add(dV, ks * 2048), idH, ks > 0);
       tc::mma_commit(bar_mma);
     }
     // next chunk's gates while the tensor core works on this chunk
+    RowGates gn = gc;
     float rho_next = 1.f, m_new_next = m_new_cur;
-    if (c + 1 < nchunks) compute_gates(c + 1, m_new_cur, rho_next, m_new_next);
+    bool sep_next = sep_cur;
+    if (c + 1 < nchunks) compute_gates(c + 1, m_new_cur, gn, rho_next, m_new_next, sep_next);
     if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
     ++mma_uses;
     tc::tc_fence_after();
@@ -434,20 +508,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       loads_issued = c + 2;
     }
     // SSD D skip: this row's x values from the staged V (= x) panel, before it is scaled
-    uint4 xrow[kDV / 8];
+    uint4 xrow[4];
     if (MODE == kSsd) {
 #pragma unroll
-      for (int q = 0; q < kDV / 8; ++q)
-        xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(tid, 8 * q));
+      for (int q = 0; q < 4; ++q)
+        xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(row, ch + 8 * q));
     }
-    // ---- V rows *= kscale (row s = this thread); the normalizer's K^T operand
-    //      row 0 = kscale: the state update below is K^T (kscale . V) ---------
+    // ---- V rows *= kscale (row s = this thread's row); the normalizer's K^T
+    //      operand row 0 = kscale: the state update below is K^T (kscale . V) ---
     {
-      const float ks = rowK[tid];
+      const float ks = gc.ks;
       unsigned char* vrow = sm + Lt::kV;
 #pragma unroll
-      for (int q = 0; q < kDV / 8; ++q) {
-        uint4* ptr = reinterpret_cast<uint4*>(vrow + tc::sw128_offset(tid, 8 * q));
+      for (int q = 0; q < 4; ++q) {
+        uint4* ptr = reinterpret_cast<uint4*>(vrow + tc::sw128_offset(row, ch + 8 * q));
         uint4 w = *ptr;
         uint32_t* e = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
@@ -457,9 +531,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         *ptr = w;
       }
-      if (kNorm) {
+      if (kNorm && hf == 0) {
         __nv_bfloat16* kv = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kOnes);
-        kv[((tid / 64) * 2048 + tc::sw128_offset(0, tid % 64)) / 2] = __float2bfloat16_rn(ks);
+        kv[((row / 64) * 2048 + tc::sw128_offset(0, row % 64)) / 2] = __float2bfloat16_rn(ks);
       }
     }
     tc::fence_async_smem();
@@ -468,72 +542,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- B: state += K^T (kscale . V), n += K^T kscale -------------------------
     if (tid == 0) {
       tc::tc_fence_after();
+      const uint32_t tb = *tmem_slot;
 #pragma unroll
       for (int blk = 0; blk < Lt::kNB; ++blk) {
 #pragma unroll
         for (int ks = 0; ks < kC / 16; ++ks) {
           // A = K^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO = panel stride); K step = 16 rows
           const uint64_t ad = tc::desc_add(dKT, (2 * blk) * kPanel + ks * 2048);
-          tc::mma_bf16(tm + Lt::tAcc + blk * 64, ad, tc::desc_add(dV, ks * 2048), idAcc, true);
+          tc::mma_bf16(tb + Lt::tAcc + blk * 64, ad, tc::desc_add(dV, ks * 2048), idAcc, true);
           if (kNorm)
-            tc::mma_bf16(tm + Lt::tAccN + blk * 32, ad, tc::desc_add(dOnes, (ks / 4) * 2048 + (ks % 4) * 32),
+            tc::mma_bf16(tb + Lt::tAccN + blk * 32, ad, tc::desc_add(dOnes, (ks / 4) * 2048 + (ks % 4) * 32),
                          idAccN, true);
         }
       }
       tc::mma_commit(bar_mma);
     }
-    // ---- epilogue: output row t -------------------------------------------------
+    // ---- epilogue: output row t, this half's 32 columns ---------------------------
     {
-      const float bt2 = rowB[tid], Mt2 = rowM[tid];
-      const float sc = ex2_approx(bt2 + m_prev * kLog2e - Mt2);
-      float qn = 0.f;
-      if (kNorm) {
-        float v[32];
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tQN), v);
-        tc::tmem_wait_ld();
-        qn = v[0];
-      }
-      const float den = fmaxf(sc * qn + den_intra, ex2_approx(-Mt2));
-      const float inv = 1.f / den;
-      const bool ok = valid;
-      __nv_bfloat16* orow = p.out + b * p.so[0] + h * p.so[1] + (int64_t)tg * p.so[2] + e0;
-#pragma unroll
-      for (int c0 = 0; c0 < kDV; c0 += 32) {
+      const float den_intra = denp[row] + denp[kC + row];
+      float o[32];
+      {
         float hi[32], ha[32];
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tHint + c0), hi);
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tHintra + c0), ha);
+        tc::tmem_ld32(tm + Lt::tHint + ch, hi);
+        tc::tmem_ld32(tm + Lt::tHintra + ch, ha);
+        const float qn = kNorm ? tc::tmem_ld1(tm + Lt::tQN) : 0.f;
         tc::tmem_wait_ld();
-        float o[32];
         if (kNorm) {
+          const float den = fmaxf(gc.sc * qn + gc.R * den_intra, gc.F);
+          const float inv = 1.f / den;
+          const float a = gc.sc * inv, r = gc.R * inv;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = (sc * hi[j] + ha[j]) * inv;
+          for (int j = 0; j < 32; ++j) o[j] = fmaf(a, hi[j], r * ha[j]);
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = fmaf(sc, hi[j], ha[j]);
-          if (ok && Dh != 0.f && e0 + c0 < p.dv) {
+          for (int j = 0; j < 32; ++j) o[j] = fmaf(gc.sc, hi[j], gc.R * ha[j]);
+        }
+      }
+      const bool ok = valid && e0 + ch < p.dv;
+      if (MODE == kSsd && ok && Dh != 0.f) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 w = xrow[c0 / 8 + q];
-              const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = xrow[q];
+          const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float2 f = __bfloat1622float2(x2[j]);
-                o[8 * q + 2 * j] = fmaf(Dh, f.x, o[8 * q + 2 * j]);
-                o[8 * q + 2 * j + 1] = fmaf(Dh, f.y, o[8 * q + 2 * j + 1]);
-              }
-            }
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(x2[j]);
+            o[8 * q + 2 * j] = fmaf(Dh, f.x, o[8 * q + 2 * j]);
+            o[8 * q + 2 * j + 1] = fmaf(Dh, f.y, o[8 * q + 2 * j + 1]);
           }
         }
-        if (ok && e0 + c0 < p.dv) {
+      }
+      if (ok) {
+        __nv_bfloat16* orow = p.out + b * p.so[0] + h * p.so[1] + (int64_t)tg * p.so[2] + e0 + ch;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = pack2<__nv_bfloat16>(o[8 * q + 0], o[8 * q + 1]);
-            w.y = pack2<__nv_bfloat16>(o[8 * q + 2], o[8 * q + 3]);
-            w.z = pack2<__nv_bfloat16>(o[8 * q + 4], o[8 * q + 5]);
-            w.w = pack2<__nv_bfloat16>(o[8 * q + 6], o[8 * q + 7]);
-            *reinterpret_cast<uint4*>(orow + c0 + 8 * q) = w;
-          }
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack2<__nv_bfloat16>(o[8 * q + 0], o[8 * q + 1]);
+          w.y = pack2<__nv_bfloat16>(o[8 * q + 2], o[8 * q + 3]);
+          w.z = pack2<__nv_bfloat16>(o[8 * q + 4], o[8 * q + 5]);
+          w.w = pack2<__nv_bfloat16>(o[8 * q + 6], o[8 * q + 7]);
+          *reinterpret_cast<uint4*>(orow + 8 * q) = w;
         }
       }
     }
@@ -547,6 +615,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     m_prev = m_new_cur;
     m_new_cur = m_new_next;
     rho_cur = rho_next;
+    gc = gn;
+    sep_cur = sep_next;
     tc::fence_async_smem();
     tc::tc_fence_before();
     __syncthreads();
@@ -564,28 +634,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::tc_fence_after();
 #pragma unroll 1
     for (int blk = 0; blk < Lt::kNB; ++blk) {
-      const int row = blk * 128 + warp * 32 + lane;
+      const int srow = blk * 128 + row;
       if (p.CT) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < kDV; c0 += 32) {
-          float v[32];
-          tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tAcc + blk * 64 + c0), v);
-          tc::tmem_wait_ld();
+        float v[32];
+        tc::tmem_ld32(tm + Lt::tAcc + blk * 64 + ch, v);
+        tc::tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = e0 + c0 + j;
-            if (col < p.dv) {
-              if (p.state_t) p.CT[((int64_t)bh * p.dv + col) * DK + row] = v[j];
-              else p.CT[((int64_t)bh * DK + row) * p.dv + col] = v[j];
-            }
+        for (int j = 0; j < 32; ++j) {
+          const int col = e0 + ch + j;
+          if (col < p.dv) {
+            if (p.state_t) p.CT[((int64_t)bh * p.dv + col) * DK + srow] = v[j];
+            else p.CT[((int64_t)bh * DK + srow) * p.dv + col] = v[j];
           }
         }
       }
-      if (kNorm && p.nT && blockIdx.x == 0) {
-        float v[32];
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, Lt::tAccN + blk * 32), v);
+      if (kNorm && p.nT && blockIdx.x == 0 && hf == 1) {
+        const float n = tc::tmem_ld1(tm + Lt::tAccN + blk * 32);
         tc::tmem_wait_ld();
-        p.nT[(int64_t)bh * DK + row] = v[0];
+        p.nT[(int64_t)bh * DK + srow] = n;
       }
     }
     if (kNorm && p.mT && blockIdx.x == 0 && tid == 0) p.mT[bh] = m_prev;
@@ -596,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tm, 512);
+    tc::tmem_dealloc(*tmem_slot, 512);
   }
 }
 

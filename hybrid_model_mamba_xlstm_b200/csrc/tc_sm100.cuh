@@ -138,6 +138,12 @@ HXM_DEV void tmem_st16(uint32_t addr, const float (&v)[16]) {
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
+// One fp32 column of this thread's lane.
+HXM_DEV float tmem_ld1(uint32_t addr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(addr));
+  return __uint_as_float(r);
+}
 HXM_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 HXM_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
