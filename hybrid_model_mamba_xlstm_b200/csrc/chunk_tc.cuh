@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tmV, const Params p) {
   using Lt = Layout<DK>;
   constexpr bool kNorm = MODE == kMlstm;
+  constexpr bool kScaleK = DK == 128;  // key rows scaled (one MMA batch per chunk)
   constexpr int kNP = DK / 64;  // Q/K panels
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzled panels
@@ -278,8 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   constexpr uint32_t kLoadBytes = (2 * kNP + 1) * kPanel;
-  // Chunk c's operands arrive in two parts on one barrier phase: Q (free once
-  // the Hint / qn MMAs are done) and K, V (free once the state update is done).
+  // Chunk c's operands arrive on one barrier phase, in one part (DK = 128) or
+  // in two: Q (free once the Hint / qn MMAs are done) and K, V (free once the
+  // state update is done).
   auto issue_load_q = [&](int c) {
     tc::mbar_expect_tx(bar_load, kLoadBytes);
     const int hq = (MODE == kSsd) ? 0 : h;
@@ -453,6 +455,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       denp[hf * kC + row] = den;
     }
+    // ---- kscale (row s = this thread's row): DK = 128 scales the K rows here
+    //      (this half's dk panel), so that one MMA batch below does the outputs
+    //      and the state update, (kscale . K)^T V; DK = 256 scales the V rows
+    //      after the output MMAs (half the elements of a K row).
+    if (kScaleK) {
+      const float ks = gc.ks;
+      unsigned char* krow = sm + Lt::kK + hf * kPanel;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        uint4* ptr = reinterpret_cast<uint4*>(krow + tc::sw128_offset(row, 8 * q));
+        uint4 w = *ptr;
+        uint32_t* e = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j]));
+          e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+        }
+        *ptr = w;
+      }
+    }
+    // SSD D skip: this row's x values from the staged V (= x) panel
+    uint4 xrow[4];
+    if (MODE == kSsd) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(row, ch + 8 * q));
+    }
     // ---- state *= rho (TMEM read-modify-write, this half's columns) -------------
     const float rho = rho_cur;
     if (rho != 1.f) {
@@ -479,10 +508,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_async_smem();
     tc::tc_fence_before();
     if (__syncthreads_or(bad)) { bad = 1; break; }
-    // ---- A: Hint = Q.Snap, qn = Q.n, Hintra = P.V ------------------------------
+    // ---- MMAs: Hint = Q.Snap, qn = Q.n, Hintra = P.V; with DK = 128 also the
+    //      state update state += K'^T V, n += K'^T 1 (K' = kscale . K) ---------------
+    const uint32_t tb = *tmem_slot;
+    // state update (A = K^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO =
+    // panel stride); K step = 16 rows); the normalizer's B row 0 is 1 (K scaled)
+    // or kscale (V scaled)
+    auto issue_update = [&]() {
+#pragma unroll
+      for (int blk = 0; blk < Lt::kNB; ++blk) {
+#pragma unroll
+        for (int ks = 0; ks < kC / 16; ++ks) {
+          const uint64_t ad = tc::desc_add(dKT, (2 * blk) * kPanel + ks * 2048);
+          tc::mma_bf16(tb + Lt::tAcc + blk * 64, ad, tc::desc_add(dV, ks * 2048), idAcc, true);
+          if (kNorm)
+            tc::mma_bf16(tb + Lt::tAccN + blk * 32, ad, tc::desc_add(dOnes, (ks / 4) * 2048 + (ks % 4) * 32),
+                         idAccN, true);
+        }
+      }
+    };
     if (tid == 0) {
       tc::tc_fence_after();
-      const uint32_t tb = *tmem_slot;
 #pragma unroll
       for (int ks = 0; ks < DK / 16; ++ks) {
         const uint64_t ad = tc::desc_add(dQ, (ks / 4) * kPanel + (ks % 4) * 32);
@@ -493,6 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < kC / 16; ++ks)
         tc::mma_bf16(tb + Lt::tHintra, tc::desc_add(dP, (ks / 4) * kPanel + (ks % 4) * 32),
                      tc::desc_add(dV, ks * 2048), idH, ks > 0);
+      if (kScaleK) issue_update();
       tc::mma_commit(bar_mma);
     }
     // next chunk's gates while the tensor core works on this chunk
@@ -503,59 +550,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
     ++mma_uses;
     tc::tc_fence_after();
-    if (tid == 0 && !bad && c + 1 < nchunks) {  // the MMAs reading Q are done
-      issue_load_q(c + 1);
-      loads_issued = c + 2;
-    }
-    // SSD D skip: this row's x values from the staged V (= x) panel, before it is scaled
-    uint4 xrow[4];
-    if (MODE == kSsd) {
+    if (kScaleK) {
+      // Q, K, V of this chunk are consumed: the next chunk's load lands under
+      // the epilogue and the snapshot
+      if (tid == 0 && !bad && c + 1 < nchunks) {
+        issue_load_q(c + 1);
+        issue_load_kv(c + 1);
+        loads_issued = c + 2;
+      }
+    } else {
+      // Q is consumed: its next panels load under the state update
+      if (tid == 0 && !bad && c + 1 < nchunks) {
+        issue_load_q(c + 1);
+        loads_issued = c + 2;
+      }
+      // V rows *= kscale, the normalizer's B row 0 = kscale; then the update
+      {
+        const float ks = gc.ks;
+        unsigned char* vrow = sm + Lt::kV;
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(row, ch + 8 * q));
-    }
-    // ---- V rows *= kscale (row s = this thread's row); the normalizer's K^T
-    //      operand row 0 = kscale: the state update below is K^T (kscale . V) ---
-    {
-      const float ks = gc.ks;
-      unsigned char* vrow = sm + Lt::kV;
+        for (int q = 0; q < 4; ++q) {
+          uint4* ptr = reinterpret_cast<uint4*>(vrow + tc::sw128_offset(row, ch + 8 * q));
+          uint4 w = *ptr;
+          uint32_t* e = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4* ptr = reinterpret_cast<uint4*>(vrow + tc::sw128_offset(row, ch + 8 * q));
-        uint4 w = *ptr;
-        uint32_t* e = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j]));
-          e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j]));
+            e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+          }
+          *ptr = w;
         }
-        *ptr = w;
-      }
-      if (kNorm && hf == 0) {
-        __nv_bfloat16* kv = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kOnes);
-        kv[((row / 64) * 2048 + tc::sw128_offset(0, row % 64)) / 2] = __float2bfloat16_rn(ks);
-      }
-    }
-    tc::fence_async_smem();
-    tc::tc_fence_before();
-    if (__syncthreads_or(bad)) { bad = 1; break; }
-    // ---- B: state += K^T (kscale . V), n += K^T kscale -------------------------
-    if (tid == 0) {
-      tc::tc_fence_after();
-      const uint32_t tb = *tmem_slot;
-#pragma unroll
-      for (int blk = 0; blk < Lt::kNB; ++blk) {
-#pragma unroll
-        for (int ks = 0; ks < kC / 16; ++ks) {
-          // A = K^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO = panel stride); K step = 16 rows
-          const uint64_t ad = tc::desc_add(dKT, (2 * blk) * kPanel + ks * 2048);
-          tc::mma_bf16(tb + Lt::tAcc + blk * 64, ad, tc::desc_add(dV, ks * 2048), idAcc, true);
-          if (kNorm)
-            tc::mma_bf16(tb + Lt::tAccN + blk * 32, ad, tc::desc_add(dOnes, (ks / 4) * 2048 + (ks % 4) * 32),
-                         idAccN, true);
+        if (kNorm && hf == 0) {
+          __nv_bfloat16* kv = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kOnes);
+          kv[((row / 64) * 2048 + tc::sw128_offset(0, row % 64)) / 2] = __float2bfloat16_rn(ks);
         }
       }
-      tc::mma_commit(bar_mma);
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      if (__syncthreads_or(bad)) { bad = 1; break; }
+      if (tid == 0) {
+        tc::tc_fence_after();
+        issue_update();
+        tc::mma_commit(bar_mma);
+      }
     }
     // ---- epilogue: output row t, this half's 32 columns ---------------------------
     {
@@ -605,12 +642,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    // ---- wait B (the state update ran under the epilogue); refill; snapshot -----
-    if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
-    ++mma_uses;
-    tc::tc_fence_after();
-    if (__syncthreads_or(bad)) { bad = 1; break; }
-    if (tid == 0 && c + 1 < nchunks) issue_load_kv(c + 1);
+    // ---- (DK = 256: wait for the update, refill K, V); snapshot of the updated
+    //      state for the next chunk's Hint ------------------------------------------
+    if (!kScaleK) {
+      if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
+      ++mma_uses;
+      tc::tc_fence_after();
+      if (__syncthreads_or(bad)) { bad = 1; break; }
+      if (tid == 0 && c + 1 < nchunks) issue_load_kv(c + 1);
+    }
     snapshot();
     m_prev = m_new_cur;
     m_new_cur = m_new_next;
