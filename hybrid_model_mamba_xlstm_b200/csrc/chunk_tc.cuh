@@ -33,6 +33,8 @@
 // block, and of P the 64-column half h).
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "tc_sm100.cuh"
 
@@ -94,69 +96,6 @@ struct Layout {
   static_assert(tAcc + 64 * kNB <= tQN, "TMEM layout");
   static_assert(tAccN + 32 * kNB <= 512, "TMEM layout");
 };
-
-// ---- scans over the 128 chunk rows ------------------------------------------
-// Each half of the CTA (warps 0-3, warps 4-7) holds all 128 rows (row =
-// 32 (warp % 4) + lane) and scans them on its own; red = float[64].
-HXM_DEV float rows_incl_sum(float v, float* red) {
-  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3, hf = threadIdx.x >> 7;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float n = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += n;
-  }
-  if (lane == 31) red[hf * 16 + w] = v;
-  __syncthreads();
-  float pre = 0.f;
-  for (int i = 0; i < w; ++i) pre += red[hf * 16 + i];
-  __syncthreads();
-  return v + pre;
-}
-HXM_DEV float rows_incl_max(float v, float* red) {
-  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3, hf = threadIdx.x >> 7;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float n = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v = fmaxf(v, n);
-  }
-  if (lane == 31) red[hf * 16 + w] = v;
-  __syncthreads();
-  float pre = -INFINITY;
-  for (int i = 0; i < w; ++i) pre = fmaxf(pre, red[hf * 16 + i]);
-  __syncthreads();
-  return fmaxf(v, pre);
-}
-// value of row `src` to every thread of the half
-HXM_DEV float rows_bcast(float v, int src, float* red) {
-  const int hf = threadIdx.x >> 7;
-  if ((threadIdx.x & 127) == src) red[hf * 16 + 8] = v;
-  __syncthreads();
-  const float r = red[hf * 16 + 8];
-  __syncthreads();
-  return r;
-}
-// component-wise max over the 128 rows of four values
-HXM_DEV float4 rows_max4(float4 v, float* red) {
-  const int lane = threadIdx.x & 31, w = (threadIdx.x >> 5) & 3, hf = threadIdx.x >> 7;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    v.x = fmaxf(v.x, __shfl_xor_sync(0xffffffffu, v.x, o));
-    v.y = fmaxf(v.y, __shfl_xor_sync(0xffffffffu, v.y, o));
-    v.z = fmaxf(v.z, __shfl_xor_sync(0xffffffffu, v.z, o));
-    v.w = fmaxf(v.w, __shfl_xor_sync(0xffffffffu, v.w, o));
-  }
-  float4* r4 = reinterpret_cast<float4*>(red + 32 + hf * 16);
-  if (lane == 0) r4[w] = v;
-  __syncthreads();
-  float4 r = r4[0];
-#pragma unroll
-  for (int i = 1; i < 4; ++i) {
-    const float4 o = r4[i];
-    r = make_float4(fmaxf(r.x, o.x), fmaxf(r.y, o.y), fmaxf(r.z, o.z), fmaxf(r.w, o.w));
-  }
-  __syncthreads();
-  return r;
-}
 
 // Per-row gate values of one chunk, held by the threads of that row.
 struct RowGates {
@@ -289,6 +228,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int pnl = 0; pnl < kNP; ++pnl)
       tc::tma_load_4d(sm + Lt::kQ + pnl * kPanel, &tmQ, bar_load, pnl * 64, c * kC, hq, b);
   };
+  // all of chunk c's panels, one per lane of warp 0 (DK = 128; called by warp 0)
+  auto issue_load_warp = [&](int c) {
+    if (lane == 0) tc::mbar_expect_tx(bar_load, kLoadBytes);
+    __syncwarp();
+    const int hq = (MODE == kSsd) ? 0 : h;
+    if (lane < kNP) tc::tma_load_4d(sm + Lt::kQ + lane * kPanel, &tmQ, bar_load, lane * 64, c * kC, hq, b);
+    else if (lane < 2 * kNP)
+      tc::tma_load_4d(sm + Lt::kK + (lane - kNP) * kPanel, &tmK, bar_load, (lane - kNP) * 64, c * kC, hq, b);
+    else if (lane == 2 * kNP) tc::tma_load_4d(sm + Lt::kV, &tmV, bar_load, e0, c * kC, h, b);
+  };
   auto issue_load_kv = [&](int c) {
     const int hq = (MODE == kSsd) ? 0 : h;
 #pragma unroll 1
@@ -319,39 +268,103 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float dtb = (MODE == kSsd && p.dt_bias) ? p.dt_bias[h] : 0.f;
   const float Dh = (MODE == kSsd && p.Dskip) ? p.Dskip[h] : 0.f;
 
+  // This row's raw gate inputs of chunk cc (global loads, issued a chunk
+  // ahead of their use): mLSTM log i, log f; SSD raw dt.
+  auto load_gates = [&](int cc, float& x0, float& x1) {
+    const int tgc = cc * kC + row;
+    x0 = 0.f;
+    x1 = 0.f;
+    if (tgc < p.seqlen) {
+      x0 = p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tgc * p.sg0[2]];
+      if (MODE == kMlstm) x1 = p.g1[b * p.sg1[0] + h * p.sg1[1] + (int64_t)tgc * p.sg1[2]];
+    }
+  };
   // Gates of chunk cc: b_t = cumsum log f, u_s, the stabilizers M_t / m_new
   // (from m_in, the state's scale entering the chunk), the state's decay rho,
   // this row's RowGates, whether the weights separate, and the column vector
-  // colw (C_s, or u_s * log2e).  Every thread takes part (row scans); colw is
-  // written after the caller's last read of the previous chunk's values.
-  auto compute_gates = [&](int cc, float m_in, RowGates& rg, float& rho_out, float& m_out, bool& sep_out) {
-    const int tgc = cc * kC + row;
-    const bool v = tgc < p.seqlen;
+  // colw (C_s, or u_s * log2e).  Every thread takes part (two barriers); colw
+  // is written after the caller's last read of the previous chunk's values.
+  auto compute_gates = [&](int cc, float x0, float x1, float m_in, RowGates& rg, float& rho_out, float& m_out,
+                           bool& sep_out) {
+    const bool v = cc * kC + row < p.seqlen;
     float li, lf;
     if (MODE == kMlstm) {
-      li = v ? p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tgc * p.sg0[2]] : -INFINITY;
-      lf = v ? p.g1[b * p.sg1[0] + h * p.sg1[1] + (int64_t)tgc * p.sg1[2]] : 0.f;
+      li = v ? x0 : -INFINITY;
+      lf = v ? x1 : 0.f;
     } else {
-      float dtv = v ? p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tgc * p.sg0[2]] + dtb : 0.f;
+      float dtv = v ? x0 + dtb : 0.f;
       if (p.dt_softplus) dtv = (dtv > 20.f) ? dtv : log1pf(__expf(dtv));
       li = (v && dtv > 0.f) ? __logf(dtv) : -INFINITY;
       lf = v ? dtv * A_h : 0.f;
     }
-    const float bt = rows_incl_sum(lf, red);
-    const float g = rows_bcast(bt, kC - 1, red);
+    // pass 1: b_t = inclusive sum of log f over the rows, g = the chunk total
+    float bt = lf;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n = __shfl_up_sync(0xffffffffu, bt, o);
+      if (lane >= o) bt += n;
+    }
+    if (lane == 31) red[hf * 4 + wq] = bt;
+    __syncthreads();
+    float g = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x = red[hf * 4 + i];
+      if (i < wq) bt += x;
+      g += x;
+    }
     const float us = li - bt;
-    float rt, m_new;
+    // pass 2: prefix max of u (mLSTM), extremes of u (and of b, SSD), u_0
+    float pm = us, umin = us, bmax = bt, bmin = bt;
     if (kNorm) {
-      const float pm = rows_incl_max(us, red);
-      const float pmax = rows_bcast(pm, kC - 1, red);
-      const float Mt = bt + fmaxf(m_in, pm);
-      m_new = g + fmaxf(m_in, pmax);
-      rt = bt - Mt;
-      rg.sc = __expf(bt + m_in - Mt);
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, pm, o);
+        if (lane >= o) pm = fmaxf(pm, n);
+      }
+    } else {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o));
+        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+        bmin = fminf(bmin, __shfl_xor_sync(0xffffffffu, bmin, o));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) umin = fminf(umin, __shfl_xor_sync(0xffffffffu, umin, o));
+    if (lane == 31) {
+      red[8 + hf * 4 + wq] = pm;  // the warp's max of u
+      red[16 + hf * 4 + wq] = umin;
+      red[24 + hf * 4 + wq] = bmax;
+      red[32 + hf * 4 + wq] = bmin;
+    }
+    if (row == 0) red[40 + hf] = us;
+    __syncthreads();
+    float U = -INFINITY, umn = INFINITY, bmx = -INFINITY, bmn = INFINITY, pre = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x = red[8 + hf * 4 + i];
+      if (i < wq) pre = fmaxf(pre, x);
+      U = fmaxf(U, x);
+      umn = fminf(umn, red[16 + hf * 4 + i]);
+      bmx = fmaxf(bmx, red[24 + hf * 4 + i]);
+      bmn = fminf(bmn, red[32 + hf * 4 + i]);
+    }
+    float rt, m_new, rmax, rmin;
+    if (kNorm) {
+      const float mx = fmaxf(m_in, fmaxf(pm, pre));  // max(m_in, prefix max of u)
+      const float Mt = bt + mx;
+      m_new = g + fmaxf(m_in, U);
+      rt = -mx;  // b_t - M_t, nonincreasing in t
+      rmax = -fmaxf(m_in, red[40 + hf]);
+      rmin = -fmaxf(m_in, U);
+      rg.sc = __expf(m_in - mx);
       rg.F = __expf(-Mt);
     } else {
       m_new = 0.f;
       rt = bt;
+      rmax = bmx;
+      rmin = bmn;
       rg.sc = __expf(bt);
       rg.F = 0.f;
     }
@@ -360,9 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     rho_out = __expf(g + m_in - m_new);
     m_out = m_new;
     // a shift c0 with every rt + c0 and us - c0 inside [-40, 40]?
-    const float4 ext = rows_max4(make_float4(rt, -rt, us, -us), red);  // max r, -min r, max u, -min u
-    const float lo = fmaxf(ext.y - 40.f, ext.z - 40.f);
-    const float hi = fminf(40.f - ext.x, 40.f - ext.w);
+    const float lo = fmaxf(-rmin - 40.f, U - 40.f);
+    const float hi = fminf(40.f - rmax, 40.f + umn);
     const bool sep = lo <= hi;  // false for any non-finite extreme (e.g. a row past the end)
     const float c0 = 0.5f * (lo + hi);
     rg.R = sep ? __expf(rt + c0) : 1.f;
@@ -372,7 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   RowGates gc;
   float rho_cur, m_new_cur;
   bool sep_cur;
-  compute_gates(0, m_prev, gc, rho_cur, m_new_cur, sep_cur);
+  float gx0, gx1;  // the next chunk's raw gate inputs
+  load_gates(0, gx0, gx1);
+  compute_gates(0, gx0, gx1, m_prev, gc, rho_cur, m_new_cur, sep_cur);
+  if (nchunks > 1) load_gates(1, gx0, gx1);
   __syncthreads();
 
   int bad = 0;
@@ -411,7 +426,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::tmem_ld32(tm + Lt::tS + s0, v);
           tc::tmem_wait_ld();
           const float4* cw = reinterpret_cast<const float4*>(colw + s0);
-          if (sep_cur) {
+          // DIAG: the block on the diagonal (s0 = 32 (warp % 4)), where column
+          // s0 + j is causal for this row iff j <= lane; blocks left of it are all causal
+          auto weigh = [&](auto diag_tag, auto sep_tag) {
+            constexpr bool kDiag = decltype(diag_tag)::value;
+            constexpr bool kSep = decltype(sep_tag)::value;
 #pragma unroll
             for (int j4 = 0; j4 < 8; ++j4) {
               const float4 c4 = cw[j4];
@@ -419,25 +438,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
                 const int j = 4 * j4 + k;
-                const float pv = (s0 + j <= row) ? v[j] * cv[k] : 0.f;
+                float pv = v[j] * (kSep ? cv[k] : ex2_approx(gc.r2 + cv[k]));
+                if (kDiag && j > lane) pv = 0.f;
                 v[j] = pv;
                 den += pv;
               }
             }
+          };
+          if (s0 == wq * 32) {
+            if (sep_cur) weigh(std::true_type{}, std::true_type{});
+            else weigh(std::true_type{}, std::false_type{});
           } else {
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 c4 = cw[j4];
-              const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const int j = 4 * j4 + k;
-                const float w = ex2_approx(gc.r2 + cv[k]);
-                const float pv = (s0 + j <= row) ? v[j] * w : 0.f;
-                v[j] = pv;
-                den += pv;
-              }
-            }
+            if (sep_cur) weigh(std::false_type{}, std::true_type{});
+            else weigh(std::false_type{}, std::false_type{});
           }
         } else {
 #pragma unroll
@@ -546,16 +559,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     RowGates gn = gc;
     float rho_next = 1.f, m_new_next = m_new_cur;
     bool sep_next = sep_cur;
-    if (c + 1 < nchunks) compute_gates(c + 1, m_new_cur, gn, rho_next, m_new_next, sep_next);
+    if (c + 1 < nchunks) {
+      compute_gates(c + 1, gx0, gx1, m_new_cur, gn, rho_next, m_new_next, sep_next);
+      if (c + 2 < nchunks) load_gates(c + 2, gx0, gx1);
+    }
     if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
     ++mma_uses;
     tc::tc_fence_after();
     if (kScaleK) {
       // Q, K, V of this chunk are consumed: the next chunk's load lands under
       // the epilogue and the snapshot
-      if (tid == 0 && !bad && c + 1 < nchunks) {
-        issue_load_q(c + 1);
-        issue_load_kv(c + 1);
+      if (warp == 0 && c + 1 < nchunks && !__any_sync(0xffffffffu, bad)) {
+        issue_load_warp(c + 1);
         loads_issued = c + 2;
       }
     } else {
