@@ -186,14 +186,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc::tmem_wait_st();
 
-  // state (TMEM fp32) -> bf16 snapshots in shared memory
-  auto snapshot = [&]() {
+  // state (TMEM fp32) -> bf16 snapshots in shared memory, then the state is
+  // decayed in place by the next chunk's rho (one TMEM pass for both)
+  auto snapshot = [&](float rho) {
 #pragma unroll 1
     for (int blk = 0; blk < Lt::kNB; ++blk) {
       const int srow = blk * 128 + row;
       unsigned char* sp = sm + Lt::kSnap;
       float v[32];
-      tc::tmem_ld32(tm + Lt::tAcc + blk * 64 + ch, v);
+      const uint32_t a = tm + Lt::tAcc + blk * 64 + ch;
+      tc::tmem_ld32(a, v);
       tc::tmem_wait_ld();
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -204,18 +206,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
         *reinterpret_cast<uint4*>(sp + tc::sw128_offset(srow, ch + 8 * q)) = w;
       }
+      if (rho != 1.f) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= rho;
+        tc::tmem_st32(a, v);
+      }
       if (kNorm && hf == 1) {
-        const float n = tc::tmem_ld1(tm + Lt::tAccN + blk * 32);
+        const uint32_t an = tm + Lt::tAccN + blk * 32;
+        const float n = tc::tmem_ld1(an);
         tc::tmem_wait_ld();
         __nv_bfloat16* nb = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kN + (srow / 64) * 2048 + tc::sw128_offset(0, srow % 64));
         *nb = __float2bfloat16_rn(n);
+        if (rho != 1.f) tc::tmem_st1(an, n * rho);
       }
     }
+    tc::tmem_wait_st();
   };
-  snapshot();
-  tc::fence_async_smem();
-  tc::tc_fence_before();
-  __syncthreads();
 
   constexpr uint32_t kLoadBytes = (2 * kNP + 1) * kPanel;
   // Chunk c's operands arrive on one barrier phase, in one part (DK = 128) or
@@ -388,6 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   load_gates(0, gx0, gx1);
   compute_gates(0, gx0, gx1, m_prev, gc, rho_cur, m_new_cur, sep_cur);
   if (nchunks > 1) load_gates(1, gx0, gx1);
+  snapshot(rho_cur);
+  tc::fence_async_smem();
+  tc::tc_fence_before();
   __syncthreads();
 
   int bad = 0;
@@ -402,11 +411,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- S = Q K^T --------------------------------------------------------
     if (tid == 0) {
       tc::tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < DK / 16; ++ks) {
-        const uint32_t off = (ks / 4) * kPanel + (ks % 4) * 32;
-        tc::mma_bf16(*tmem_slot + Lt::tS, tc::desc_add(dQ, off), tc::desc_add(dK, off), idS, ks > 0);
-      }
+      const uint32_t tS = *tmem_slot + Lt::tS;
+      tc::static_for<DK / 16>([&](auto KS) {
+        constexpr int ks = decltype(KS)::value;
+        constexpr uint32_t off = (ks / 4) * kPanel + (ks % 4) * 32;
+        tc::mma_bf16_at<off, off>(tS, dQ, dK, idS, ks > 0);
+      });
       tc::mma_commit(bar_mma);
     }
     const int tg = t0 + row;
@@ -418,11 +428,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     {
       float den = 0.f;
       unsigned char* pp = sm + Lt::kP + hf * kPanel;
-#pragma unroll 1
-      for (int sb = 0; sb < 2; ++sb) {
+      auto block = [&](int sb) {
         const int s0 = 64 * hf + 32 * sb;
         float v[32];
-        if (s0 <= wq * 32 + 31) {  // warp-uniform: some row of this warp reaches column s0
+        const bool need = s0 <= wq * 32 + 31;
+        if (need) {
           tc::tmem_ld32(tm + Lt::tS + s0, v);
           tc::tmem_wait_ld();
           const float4* cw = reinterpret_cast<const float4*>(colw + s0);
@@ -465,7 +475,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
           *reinterpret_cast<uint4*>(pp + tc::sw128_offset(row, 32 * sb + 8 * q)) = w;
         }
-      }
+      };
+      block(0);
+      block(1);
       denp[hf * kC + row] = den;
     }
     // ---- kscale (row s = this thread's row): DK = 128 scales the K rows here
@@ -495,29 +507,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int q = 0; q < 4; ++q)
         xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(row, ch + 8 * q));
     }
-    // ---- state *= rho (TMEM read-modify-write, this half's columns) -------------
-    const float rho = rho_cur;
-    if (rho != 1.f) {
-#pragma unroll 1
-      for (int blk = 0; blk < Lt::kNB; ++blk) {
-        float v[32];
-        const uint32_t a = tm + Lt::tAcc + blk * 64 + ch;
-        tc::tmem_ld32(a, v);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] *= rho;
-        tc::tmem_st32(a, v);
-        if (kNorm && hf == 1) {
-          const uint32_t an = tm + Lt::tAccN + blk * 32;
-          tc::tmem_ld32(an, v);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= rho;
-          tc::tmem_st32(an, v);
-        }
-      }
-      tc::tmem_wait_st();
-    }
     tc::fence_async_smem();
     tc::tc_fence_before();
     if (__syncthreads_or(bad)) { bad = 1; break; }
@@ -528,30 +517,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     // panel stride); K step = 16 rows); the normalizer's B row 0 is 1 (K scaled)
     // or kscale (V scaled)
     auto issue_update = [&]() {
-#pragma unroll
-      for (int blk = 0; blk < Lt::kNB; ++blk) {
-#pragma unroll
-        for (int ks = 0; ks < kC / 16; ++ks) {
-          const uint64_t ad = tc::desc_add(dKT, (2 * blk) * kPanel + ks * 2048);
-          tc::mma_bf16(tb + Lt::tAcc + blk * 64, ad, tc::desc_add(dV, ks * 2048), idAcc, true);
-          if (kNorm)
-            tc::mma_bf16(tb + Lt::tAccN + blk * 32, ad, tc::desc_add(dOnes, (ks / 4) * 2048 + (ks % 4) * 32),
-                         idAccN, true);
-        }
-      }
+      tc::static_for<Lt::kNB * (kC / 16)>([&](auto I) {
+        constexpr int blk = decltype(I)::value / (kC / 16), ks = decltype(I)::value % (kC / 16);
+        constexpr uint32_t aoff = (2 * blk) * kPanel + ks * 2048;
+        tc::mma_bf16_at<aoff, ks * 2048>(tb + Lt::tAcc + blk * 64, dKT, dV, idAcc, true);
+        if (kNorm) tc::mma_bf16_at<aoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tAccN + blk * 32, dKT, dOnes, idAccN, true);
+      });
     };
     if (tid == 0) {
       tc::tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < DK / 16; ++ks) {
-        const uint64_t ad = tc::desc_add(dQ, (ks / 4) * kPanel + (ks % 4) * 32);
-        tc::mma_bf16(tb + Lt::tHint, ad, tc::desc_add(dSnap, ks * 2048), idH, ks > 0);
-        if (kNorm) tc::mma_bf16(tb + Lt::tQN, ad, tc::desc_add(dN, (ks / 4) * 2048 + (ks % 4) * 32), idQN, ks > 0);
-      }
-#pragma unroll
-      for (int ks = 0; ks < kC / 16; ++ks)
-        tc::mma_bf16(tb + Lt::tHintra, tc::desc_add(dP, (ks / 4) * kPanel + (ks % 4) * 32),
-                     tc::desc_add(dV, ks * 2048), idH, ks > 0);
+      tc::static_for<DK / 16>([&](auto KS) {
+        constexpr int ks = decltype(KS)::value;
+        constexpr uint32_t qoff = (ks / 4) * kPanel + (ks % 4) * 32;
+        tc::mma_bf16_at<qoff, ks * 2048>(tb + Lt::tHint, dQ, dSnap, idH, ks > 0);
+        if (kNorm) tc::mma_bf16_at<qoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tQN, dQ, dN, idQN, ks > 0);
+      });
+      tc::static_for<kC / 16>([&](auto KS) {
+        constexpr int ks = decltype(KS)::value;
+        tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tb + Lt::tHintra, dP, dV, idH, ks > 0);
+      });
       if (kScaleK) issue_update();
       tc::mma_commit(bar_mma);
     }
@@ -666,10 +650,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__syncthreads_or(bad)) { bad = 1; break; }
       if (tid == 0 && c + 1 < nchunks) issue_load_kv(c + 1);
     }
-    snapshot();
+    snapshot(rho_next);
     m_prev = m_new_cur;
     m_new_cur = m_new_next;
-    rho_cur = rho_next;
     gc = gn;
     sep_cur = sep_next;
     tc::fence_async_smem();

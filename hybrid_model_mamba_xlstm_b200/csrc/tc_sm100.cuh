@@ -16,6 +16,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+#include <utility>
+
 #include "common.cuh"
 
 namespace hxm {
@@ -144,6 +147,9 @@ HXM_DEV float tmem_ld1(uint32_t addr) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(addr));
   return __uint_as_float(r);
 }
+HXM_DEV void tmem_st1(uint32_t addr, float v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(addr), "r"(__float_as_uint(v)) : "memory");
+}
 HXM_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 HXM_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -157,6 +163,32 @@ HXM_DEV void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
       : "memory");
 }
+// The same with compile-time byte offsets added to the two descriptors inside
+// the instruction's own asm block: only the base descriptors stay live, and no
+// per-MMA address arithmetic is scheduled ahead of the MMAs.
+template <uint32_t AOFF, uint32_t BOFF>
+HXM_DEV void mma_bf16_at(uint32_t d_tmem, uint64_t abase, uint64_t bbase, uint32_t idesc, bool accumulate) {
+  static_assert(AOFF % 16 == 0 && BOFF % 16 == 0, "descriptor offsets are in 16-byte units");
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\t"
+      "add.s64 a, %1, %5;\n\t"
+      "add.s64 b, %2, %6;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(abase), "l"(bbase), "r"(idesc), "r"((uint32_t)accumulate), "n"(AOFF >> 4), "n"(BOFF >> 4)
+      : "memory");
+}
+
+// f(std::integral_constant<int, i>) for i = 0 .. N-1, unrolled at compile time.
+template <typename F, int... I>
+HXM_DEV void static_for_impl(F& f, std::integer_sequence<int, I...>) {
+  (f(std::integral_constant<int, I>{}), ...);
+}
+template <int N, typename F>
+HXM_DEV void static_for(F&& f) {
+  static_for_impl(f, std::make_integer_sequence<int, N>{});
+}
+
 // Arrive on `bar` once every previously issued tcgen05 op of this thread completed.
 HXM_DEV void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
