@@ -43,7 +43,8 @@ namespace chunk {
 
 constexpr int kC = 128;      // chunk length (TMEM lanes / MMA M)
 constexpr int kDV = 64;      // value columns per CTA
-constexpr int kThreads = 256;
+constexpr int kWorkerWarps = 8;                 // element-wise warps
+constexpr int kThreads = 32 * kWorkerWarps + 32;  // + one control warp (TMA, MMA)
 constexpr int kPanel = 16384;  // one 128-row x 128-byte swizzled panel
 
 enum Mode : int { kMlstm = 0, kSsd = 1 };
@@ -85,10 +86,10 @@ struct Layout {
   static constexpr int kOnes = kN + DK / 64 * 2048;  // K-major [16][128]: 2 panels of 2 KB
   static constexpr int kMisc = kOnes + 2 * 2048;
   static constexpr int kColW = kMisc;          // float[128]: C_s (separable) or u_s * log2e, by column s
-  static constexpr int kDen = kColW + 512;     // float[2][128]: rowsum(P) partials of the two column halves
-  static constexpr int kRed = kDen + 1024;     // float[64] reductions
-  static constexpr int kBar = kRed + 256;      // 2 x uint64
-  static constexpr int kTmemSlot = kBar + 16;
+  static constexpr int kDen = kColW + 512;     // float[2][2][128]: rowsum(P) partials of the two column halves, by chunk parity
+  static constexpr int kRed = kDen + 2048;     // float[64] reductions
+  static constexpr int kBar = kRed + 256;      // 7 x uint64
+  static constexpr int kTmemSlot = kBar + 64;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kBytes = kAbort + 12;
   // TMEM columns
@@ -106,6 +107,22 @@ struct RowGates {
   float ks;  // key scale of row s: exp(g + u_s - m_new)
 };
 
+// Named barrier 1 over the 256 element-wise threads (warps 0-7); the control
+// warp never takes part.  `_or` returns whether any thread passed v != 0.
+HXM_DEV void workers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+HXM_DEV int workers_sync_or(int v) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.s32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 256, p;\n\t"
+      "selp.s32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(v)
+      : "memory");
+  return r;
+}
+
 template <int DK, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     chunk_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -118,16 +135,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   // 1024-byte alignment for the swizzled panels
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   float* colw = reinterpret_cast<float*>(sm + Lt::kColW);
-  float* denp = reinterpret_cast<float*>(sm + Lt::kDen);
+  float* denp0 = reinterpret_cast<float*>(sm + Lt::kDen);
   float* red = reinterpret_cast<float*>(sm + Lt::kRed);
-  uint64_t* bar_load = reinterpret_cast<uint64_t*>(sm + Lt::kBar);
-  uint64_t* bar_mma = bar_load + 1;
+  uint64_t* bar_load = reinterpret_cast<uint64_t*>(sm + Lt::kBar);  // TMA: this chunk's Q, K, V
+  uint64_t* bar_s = bar_load + 1;       // MMA: S done
+  uint64_t* bar_a = bar_load + 2;       // MMA: outputs (+ state update, DK = 128) done
+  uint64_t* bar_b = bar_load + 3;       // MMA: state update done (DK = 256)
+  uint64_t* bar_pready = bar_load + 4;  // workers: P, scaled K, snapshot, decayed state ready
+  uint64_t* bar_vready = bar_load + 5;  // workers: scaled V ready (DK = 256)
+  uint64_t* bar_fin = bar_load + 6;     // MMA: drain before exit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Lt::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + Lt::kAbort);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool worker = warp < kWorkerWarps;
   const int wq = warp & 3;         // TMEM lane quarter
-  const int hf = warp >> 2;        // column half
+  const int hf = (warp >> 2) & 1;  // column half
   const int row = wq * 32 + lane;  // chunk row t / state row within a 128-row block
   const int ch = 32 * hf;          // this thread's first column of a 64-wide block
   const int e0 = blockIdx.x * kDV;
@@ -140,7 +163,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
     tc::mbar_init(bar_load, 1);
-    tc::mbar_init(bar_mma, 1);
+    tc::mbar_init(bar_s, 1);
+    tc::mbar_init(bar_a, 1);
+    tc::mbar_init(bar_b, 1);
+    tc::mbar_init(bar_pready, kWorkerWarps);
+    tc::mbar_init(bar_vready, kWorkerWarps);
+    tc::mbar_init(bar_fin, 1);
     tc::fence_mbar_init();
     *abort_flag = 0;
     tc::prefetch_tmap(&tmQ);
@@ -158,103 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ones[(panel * 2048 + tc::sw128_offset(0, col)) / 2] = __float2bfloat16_rn(1.f);
     }
   }
+  tc::fence_async_smem();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tm = *tmem_slot + tlane;
-
-  // ---- initial state -> TMEM (fp32) ----------------------------------------
-  float m_prev = (kNorm && p.m0) ? p.m0[bh] : 0.f;
-#pragma unroll 1
-  for (int blk = 0; blk < Lt::kNB; ++blk) {
-    const int srow = blk * 128 + row;  // state row (dk index)
-    float v[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int col = e0 + ch + j;
-      float x = 0.f;
-      if (p.C0 && col < p.dv)
-        x = p.state_t ? p.C0[((int64_t)bh * p.dv + col) * DK + srow] : p.C0[((int64_t)bh * DK + srow) * p.dv + col];
-      v[j] = x;
-    }
-    tc::tmem_st32(tm + Lt::tAcc + blk * 64 + ch, v);
-    if (hf == 1) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0.f;
-      if (kNorm && p.n0) v[0] = p.n0[(int64_t)bh * DK + srow];
-      tc::tmem_st32(tm + Lt::tAccN + blk * 32, v);
-    }
-  }
-  tc::tmem_wait_st();
-
-  // state (TMEM fp32) -> bf16 snapshots in shared memory, then the state is
-  // decayed in place by the next chunk's rho (one TMEM pass for both)
-  auto snapshot = [&](float rho) {
-#pragma unroll 1
-    for (int blk = 0; blk < Lt::kNB; ++blk) {
-      const int srow = blk * 128 + row;
-      unsigned char* sp = sm + Lt::kSnap;
-      float v[32];
-      const uint32_t a = tm + Lt::tAcc + blk * 64 + ch;
-      tc::tmem_ld32(a, v);
-      tc::tmem_wait_ld();
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 w;
-        w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
-        w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
-        w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
-        w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
-        *reinterpret_cast<uint4*>(sp + tc::sw128_offset(srow, ch + 8 * q)) = w;
-      }
-      if (rho != 1.f) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] *= rho;
-        tc::tmem_st32(a, v);
-      }
-      if (kNorm && hf == 1) {
-        const uint32_t an = tm + Lt::tAccN + blk * 32;
-        const float n = tc::tmem_ld1(an);
-        tc::tmem_wait_ld();
-        __nv_bfloat16* nb = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kN + (srow / 64) * 2048 + tc::sw128_offset(0, srow % 64));
-        *nb = __float2bfloat16_rn(n);
-        if (rho != 1.f) tc::tmem_st1(an, n * rho);
-      }
-    }
-    tc::tmem_wait_st();
-  };
-
-  constexpr uint32_t kLoadBytes = (2 * kNP + 1) * kPanel;
-  // Chunk c's operands arrive on one barrier phase, in one part (DK = 128) or
-  // in two: Q (free once the Hint / qn MMAs are done) and K, V (free once the
-  // state update is done).
-  auto issue_load_q = [&](int c) {
-    tc::mbar_expect_tx(bar_load, kLoadBytes);
-    const int hq = (MODE == kSsd) ? 0 : h;
-#pragma unroll 1
-    for (int pnl = 0; pnl < kNP; ++pnl)
-      tc::tma_load_4d(sm + Lt::kQ + pnl * kPanel, &tmQ, bar_load, pnl * 64, c * kC, hq, b);
-  };
-  // all of chunk c's panels, one per lane of warp 0 (DK = 128; called by warp 0)
-  auto issue_load_warp = [&](int c) {
-    if (lane == 0) tc::mbar_expect_tx(bar_load, kLoadBytes);
-    __syncwarp();
-    const int hq = (MODE == kSsd) ? 0 : h;
-    if (lane < kNP) tc::tma_load_4d(sm + Lt::kQ + lane * kPanel, &tmQ, bar_load, lane * 64, c * kC, hq, b);
-    else if (lane < 2 * kNP)
-      tc::tma_load_4d(sm + Lt::kK + (lane - kNP) * kPanel, &tmK, bar_load, (lane - kNP) * 64, c * kC, hq, b);
-    else if (lane == 2 * kNP) tc::tma_load_4d(sm + Lt::kV, &tmV, bar_load, e0, c * kC, h, b);
-  };
-  auto issue_load_kv = [&](int c) {
-    const int hq = (MODE == kSsd) ? 0 : h;
-#pragma unroll 1
-    for (int pnl = 0; pnl < kNP; ++pnl)
-      tc::tma_load_4d(sm + Lt::kK + pnl * kPanel, &tmK, bar_load, pnl * 64, c * kC, hq, b);
-    tc::tma_load_4d(sm + Lt::kV, &tmV, bar_load, e0, c * kC, h, b);
-  };
-  if (tid == 0) {
-    issue_load_q(0);
-    issue_load_kv(0);
-  }
 
   // operand descriptors at the region bases; an MMA adds its byte offset
   const uint64_t dQ = tc::sdesc_sw128(sbase + Lt::kQ, 16, 1024);      // K-major rows t (Q) or s (K)
@@ -270,202 +205,139 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t idQN = tc::idesc_bf16(128, 16, false, false);
   constexpr uint32_t idAcc = tc::idesc_bf16(128, kDV, true, true);
   constexpr uint32_t idAccN = tc::idesc_bf16(128, 16, true, false);
-  const float A_h = (MODE == kSsd) ? p.A[h] : 0.f;
-  const float dtb = (MODE == kSsd && p.dt_bias) ? p.dt_bias[h] : 0.f;
-  const float Dh = (MODE == kSsd && p.Dskip) ? p.Dskip[h] : 0.f;
 
-  // This row's raw gate inputs of chunk cc (global loads, issued a chunk
-  // ahead of their use): mLSTM log i, log f; SSD raw dt.
-  auto load_gates = [&](int cc, float& x0, float& x1) {
-    const int tgc = cc * kC + row;
-    x0 = 0.f;
-    x1 = 0.f;
-    if (tgc < p.seqlen) {
-      x0 = p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tgc * p.sg0[2]];
-      if (MODE == kMlstm) x1 = p.g1[b * p.sg1[0] + h * p.sg1[1] + (int64_t)tgc * p.sg1[2]];
-    }
-  };
-  // Gates of chunk cc: b_t = cumsum log f, u_s, the stabilizers M_t / m_new
-  // (from m_in, the state's scale entering the chunk), the state's decay rho,
-  // this row's RowGates, whether the weights separate, and the column vector
-  // colw (C_s, or u_s * log2e).  Every thread takes part (two barriers); colw
-  // is written after the caller's last read of the previous chunk's values.
-  auto compute_gates = [&](int cc, float x0, float x1, float m_in, RowGates& rg, float& rho_out, float& m_out,
-                           bool& sep_out) {
-    const bool v = cc * kC + row < p.seqlen;
-    float li, lf;
-    if (MODE == kMlstm) {
-      li = v ? x0 : -INFINITY;
-      lf = v ? x1 : 0.f;
-    } else {
-      float dtv = v ? x0 + dtb : 0.f;
-      if (p.dt_softplus) dtv = (dtv > 20.f) ? dtv : log1pf(__expf(dtv));
-      li = (v && dtv > 0.f) ? __logf(dtv) : -INFINITY;
-      lf = v ? dtv * A_h : 0.f;
-    }
-    // pass 1: b_t = inclusive sum of log f over the rows, g = the chunk total
-    float bt = lf;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float n = __shfl_up_sync(0xffffffffu, bt, o);
-      if (lane >= o) bt += n;
-    }
-    if (lane == 31) red[hf * 4 + wq] = bt;
-    __syncthreads();
-    float g = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float x = red[hf * 4 + i];
-      if (i < wq) bt += x;
-      g += x;
-    }
-    const float us = li - bt;
-    // pass 2: prefix max of u (mLSTM), extremes of u (and of b, SSD), u_0
-    float pm = us, umin = us, bmax = bt, bmin = bt;
-    if (kNorm) {
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float n = __shfl_up_sync(0xffffffffu, pm, o);
-        if (lane >= o) pm = fmaxf(pm, n);
-      }
-    } else {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o));
-        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
-        bmin = fminf(bmin, __shfl_xor_sync(0xffffffffu, bmin, o));
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) umin = fminf(umin, __shfl_xor_sync(0xffffffffu, umin, o));
-    if (lane == 31) {
-      red[8 + hf * 4 + wq] = pm;  // the warp's max of u
-      red[16 + hf * 4 + wq] = umin;
-      red[24 + hf * 4 + wq] = bmax;
-      red[32 + hf * 4 + wq] = bmin;
-    }
-    if (row == 0) red[40 + hf] = us;
-    __syncthreads();
-    float U = -INFINITY, umn = INFINITY, bmx = -INFINITY, bmn = INFINITY, pre = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float x = red[8 + hf * 4 + i];
-      if (i < wq) pre = fmaxf(pre, x);
-      U = fmaxf(U, x);
-      umn = fminf(umn, red[16 + hf * 4 + i]);
-      bmx = fmaxf(bmx, red[24 + hf * 4 + i]);
-      bmn = fminf(bmn, red[32 + hf * 4 + i]);
-    }
-    float rt, m_new, rmax, rmin;
-    if (kNorm) {
-      const float mx = fmaxf(m_in, fmaxf(pm, pre));  // max(m_in, prefix max of u)
-      const float Mt = bt + mx;
-      m_new = g + fmaxf(m_in, U);
-      rt = -mx;  // b_t - M_t, nonincreasing in t
-      rmax = -fmaxf(m_in, red[40 + hf]);
-      rmin = -fmaxf(m_in, U);
-      rg.sc = __expf(m_in - mx);
-      rg.F = __expf(-Mt);
-    } else {
-      m_new = 0.f;
-      rt = bt;
-      rmax = bmx;
-      rmin = bmn;
-      rg.sc = __expf(bt);
-      rg.F = 0.f;
-    }
-    rg.ks = __expf(g + us - m_new);
-    rg.r2 = rt * kLog2e;
-    rho_out = __expf(g + m_in - m_new);
-    m_out = m_new;
-    // a shift c0 with every rt + c0 and us - c0 inside [-40, 40]?
-    const float lo = fmaxf(-rmin - 40.f, U - 40.f);
-    const float hi = fminf(40.f - rmax, 40.f + umn);
-    const bool sep = lo <= hi;  // false for any non-finite extreme (e.g. a row past the end)
-    const float c0 = 0.5f * (lo + hi);
-    rg.R = sep ? __expf(rt + c0) : 1.f;
-    if (hf == 0) colw[row] = sep ? __expf(us - c0) : us * kLog2e;
-    sep_out = sep;
-  };
-  RowGates gc;
-  float rho_cur, m_new_cur;
-  bool sep_cur;
-  float gx0, gx1;  // the next chunk's raw gate inputs
-  load_gates(0, gx0, gx1);
-  compute_gates(0, gx0, gx1, m_prev, gc, rho_cur, m_new_cur, sep_cur);
-  if (nchunks > 1) load_gates(1, gx0, gx1);
-  snapshot(rho_cur);
-  tc::fence_async_smem();
-  tc::tc_fence_before();
-  __syncthreads();
-
-  int bad = 0;
-  uint32_t mma_uses = 0;
-  int loads_issued = 1, loads_done = 0;  // TMA load phases issued / waited (tid 0's view)
+  float m_final = 0.f;  // the stabilizer after the last chunk (workers)
+  if (!worker) {
+    // ================= control warp: TMA loads and MMAs (one lane) =================
+    if (lane == 0) {
+      const int hq = (MODE == kSsd) ? 0 : h;
+      constexpr uint32_t kLoadBytes = (2 * kNP + 1) * kPanel;
+      // Chunk c's operands arrive on one barrier phase, in one part (DK = 128)
+      // or in two: Q (free once the output MMAs are done) and K, V (free once
+      // the state update is done).
+      auto load_q = [&](int c) {
+        tc::mbar_expect_tx(bar_load, kLoadBytes);
+        for (int pnl = 0; pnl < kNP; ++pnl)
+          tc::tma_load_4d(sm + Lt::kQ + pnl * kPanel, &tmQ, bar_load, pnl * 64, c * kC, hq, b);
+      };
+      auto load_kv = [&](int c) {
+        for (int pnl = 0; pnl < kNP; ++pnl)
+          tc::tma_load_4d(sm + Lt::kK + pnl * kPanel, &tmK, bar_load, pnl * 64, c * kC, hq, b);
+        tc::tma_load_4d(sm + Lt::kV, &tmV, bar_load, e0, c * kC, h, b);
+      };
+      const uint32_t tb = *tmem_slot;
+      // state update (A = K^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO =
+      // panel stride); K step = 16 rows); the normalizer's B row 0 is 1 (K
+      // scaled) or kscale (V scaled)
+      auto issue_update = [&]() {
+        tc::static_for<Lt::kNB * (kC / 16)>([&](auto I) {
+          constexpr int blk = decltype(I)::value / (kC / 16), ks = decltype(I)::value % (kC / 16);
+          constexpr uint32_t aoff = (2 * blk) * kPanel + ks * 2048;
+          tc::mma_bf16_at<aoff, ks * 2048>(tb + Lt::tAcc + blk * 64, dKT, dV, idAcc, true);
+          if (kNorm)
+            tc::mma_bf16_at<aoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tAccN + blk * 32, dKT, dOnes, idAccN,
+                                                                   true);
+        });
+      };
+      int loads_issued = 1, loads_done = 0;
+      load_q(0);
+      load_kv(0);
 #pragma unroll 1
-  for (int c = 0; c < nchunks; ++c) {
-    const int t0 = c * kC;
-    if (!tc::mbar_wait(bar_load, c & 1, abort_flag)) bad = 1;
-    loads_done = c + 1;
-    if (__syncthreads_or(bad)) { bad = 1; break; }
-    // ---- S = Q K^T --------------------------------------------------------
-    if (tid == 0) {
-      tc::tc_fence_after();
-      const uint32_t tS = *tmem_slot + Lt::tS;
-      tc::static_for<DK / 16>([&](auto KS) {
-        constexpr int ks = decltype(KS)::value;
-        constexpr uint32_t off = (ks / 4) * kPanel + (ks % 4) * 32;
-        tc::mma_bf16_at<off, off>(tS, dQ, dK, idS, ks > 0);
-      });
-      tc::mma_commit(bar_mma);
-    }
-    const int tg = t0 + row;
-    const bool valid = tg < p.seqlen;
-    // ---- wait S; P = causal(S) * weight -> smem (bf16), this half's 64 columns ----
-    if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
-    ++mma_uses;
-    tc::tc_fence_after();
-    {
-      float den = 0.f;
-      unsigned char* pp = sm + Lt::kP + hf * kPanel;
-      auto block = [&](int sb) {
-        const int s0 = 64 * hf + 32 * sb;
-        float v[32];
-        const bool need = s0 <= wq * 32 + 31;
-        if (need) {
-          tc::tmem_ld32(tm + Lt::tS + s0, v);
-          tc::tmem_wait_ld();
-          const float4* cw = reinterpret_cast<const float4*>(colw + s0);
-          // DIAG: the block on the diagonal (s0 = 32 (warp % 4)), where column
-          // s0 + j is causal for this row iff j <= lane; blocks left of it are all causal
-          auto weigh = [&](auto diag_tag, auto sep_tag) {
-            constexpr bool kDiag = decltype(diag_tag)::value;
-            constexpr bool kSep = decltype(sep_tag)::value;
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 c4 = cw[j4];
-              const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const int j = 4 * j4 + k;
-                float pv = v[j] * (kSep ? cv[k] : ex2_approx(gc.r2 + cv[k]));
-                if (kDiag && j > lane) pv = 0.f;
-                v[j] = pv;
-                den += pv;
-              }
-            }
-          };
-          if (s0 == wq * 32) {
-            if (sep_cur) weigh(std::true_type{}, std::true_type{});
-            else weigh(std::true_type{}, std::false_type{});
-          } else {
-            if (sep_cur) weigh(std::false_type{}, std::true_type{});
-            else weigh(std::false_type{}, std::false_type{});
+      for (int c = 0; c < nchunks; ++c) {
+        if (!tc::mbar_wait(bar_load, c & 1, abort_flag)) break;
+        loads_done = c + 1;
+        tc::tc_fence_after();
+        // S = Q K^T
+        tc::static_for<DK / 16>([&](auto KS) {
+          constexpr int ks = decltype(KS)::value;
+          constexpr uint32_t off = (ks / 4) * kPanel + (ks % 4) * 32;
+          tc::mma_bf16_at<off, off>(tb + Lt::tS, dQ, dK, idS, ks > 0);
+        });
+        tc::mma_commit(bar_s);
+        // Hint = Q.Snap, qn = Q.n, Hintra = P.V (+ the state update, DK = 128)
+        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag)) break;
+        tc::tc_fence_after();
+        tc::static_for<DK / 16>([&](auto KS) {
+          constexpr int ks = decltype(KS)::value;
+          constexpr uint32_t qoff = (ks / 4) * kPanel + (ks % 4) * 32;
+          tc::mma_bf16_at<qoff, ks * 2048>(tb + Lt::tHint, dQ, dSnap, idH, ks > 0);
+          if (kNorm) tc::mma_bf16_at<qoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tQN, dQ, dN, idQN, ks > 0);
+        });
+        tc::static_for<kC / 16>([&](auto KS) {
+          constexpr int ks = decltype(KS)::value;
+          tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tb + Lt::tHintra, dP, dV, idH, ks > 0);
+        });
+        if (kScaleK) issue_update();
+        tc::mma_commit(bar_a);
+        if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) break;
+        if (kScaleK) {
+          if (c + 1 < nchunks) {
+            load_q(c + 1);
+            load_kv(c + 1);
+            loads_issued = c + 2;
           }
         } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          if (c + 1 < nchunks) {
+            load_q(c + 1);
+            loads_issued = c + 2;
+          }
+          if (!tc::mbar_wait(bar_vready, c & 1, abort_flag)) break;
+          tc::tc_fence_after();
+          issue_update();
+          tc::mma_commit(bar_b);
+          if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) break;
+          if (c + 1 < nchunks) load_kv(c + 1);
         }
+      }
+      // Leave nothing in flight: every MMA of this thread done, and (after a
+      // wait that gave up) the last load landed — both bounded.
+      volatile int no_abort = 0;
+      tc::mma_commit(bar_fin);
+      tc::mbar_wait(bar_fin, 0, &no_abort, 20000000ll);
+      if (*abort_flag && loads_issued > loads_done) tc::mbar_wait(bar_load, (loads_issued - 1) & 1, &no_abort, 20000000ll);
+    }
+    __syncwarp();
+  } else {
+    // ================= workers: gates, P, scaling, epilogue, snapshots =================
+    const float A_h = (MODE == kSsd) ? p.A[h] : 0.f;
+    const float dtb = (MODE == kSsd && p.dt_bias) ? p.dt_bias[h] : 0.f;
+    const float Dh = (MODE == kSsd && p.Dskip) ? p.Dskip[h] : 0.f;
+
+    // ---- initial state -> TMEM (fp32) ----------------------------------------
+    float m_prev = (kNorm && p.m0) ? p.m0[bh] : 0.f;
+#pragma unroll 1
+    for (int blk = 0; blk < Lt::kNB; ++blk) {
+      const int srow = blk * 128 + row;  // state row (dk index)
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = e0 + ch + j;
+        float x = 0.f;
+        if (p.C0 && col < p.dv)
+          x = p.state_t ? p.C0[((int64_t)bh * p.dv + col) * DK + srow] : p.C0[((int64_t)bh * DK + srow) * p.dv + col];
+        v[j] = x;
+      }
+      tc::tmem_st32(tm + Lt::tAcc + blk * 64 + ch, v);
+      if (hf == 1) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        if (kNorm && p.n0) v[0] = p.n0[(int64_t)bh * DK + srow];
+        tc::tmem_st32(tm + Lt::tAccN + blk * 32, v);
+      }
+    }
+    tc::tmem_wait_st();
+
+    // state (TMEM fp32) -> bf16 snapshots in shared memory, then the state is
+    // decayed in place by the next chunk's rho (one TMEM pass for both)
+    auto snapshot = [&](float rho) {
+#pragma unroll 1
+      for (int blk = 0; blk < Lt::kNB; ++blk) {
+        const int srow = blk * 128 + row;
+        unsigned char* sp = sm + Lt::kSnap;
+        float v[32];
+        const uint32_t a = tm + Lt::tAcc + blk * 64 + ch;
+        tc::tmem_ld32(a, v);
+        tc::tmem_wait_ld();
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 w;
@@ -473,98 +345,260 @@ __global__ void __launch_bounds__(kThreads, 1)
           w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
           w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
           w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
-          *reinterpret_cast<uint4*>(pp + tc::sw128_offset(row, 32 * sb + 8 * q)) = w;
+          *reinterpret_cast<uint4*>(sp + tc::sw128_offset(srow, ch + 8 * q)) = w;
         }
-      };
-      block(0);
-      block(1);
-      denp[hf * kC + row] = den;
-    }
-    // ---- kscale (row s = this thread's row): DK = 128 scales the K rows here
-    //      (this half's dk panel), so that one MMA batch below does the outputs
-    //      and the state update, (kscale . K)^T V; DK = 256 scales the V rows
-    //      after the output MMAs (half the elements of a K row).
-    if (kScaleK) {
-      const float ks = gc.ks;
-      unsigned char* krow = sm + Lt::kK + hf * kPanel;
+        if (rho != 1.f) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint4* ptr = reinterpret_cast<uint4*>(krow + tc::sw128_offset(row, 8 * q));
-        uint4 w = *ptr;
-        uint32_t* e = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j]));
-          e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+          for (int j = 0; j < 32; ++j) v[j] *= rho;
+          tc::tmem_st32(a, v);
         }
-        *ptr = w;
+        if (kNorm && hf == 1) {
+          const uint32_t an = tm + Lt::tAccN + blk * 32;
+          const float n = tc::tmem_ld1(an);
+          tc::tmem_wait_ld();
+          __nv_bfloat16* nb =
+              reinterpret_cast<__nv_bfloat16*>(sm + Lt::kN + (srow / 64) * 2048 + tc::sw128_offset(0, srow % 64));
+          *nb = __float2bfloat16_rn(n);
+          if (rho != 1.f) tc::tmem_st1(an, n * rho);
+        }
       }
-    }
-    // SSD D skip: this row's x values from the staged V (= x) panel
-    uint4 xrow[4];
-    if (MODE == kSsd) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(row, ch + 8 * q));
-    }
+      tc::tmem_wait_st();
+    };
+
+    // This row's raw gate inputs of chunk cc (global loads, issued a chunk
+    // ahead of their use): mLSTM log i, log f; SSD raw dt.
+    auto load_gates = [&](int cc, float& x0, float& x1) {
+      const int tgc = cc * kC + row;
+      x0 = 0.f;
+      x1 = 0.f;
+      if (tgc < p.seqlen) {
+        x0 = p.g0[b * p.sg0[0] + h * p.sg0[1] + (int64_t)tgc * p.sg0[2]];
+        if (MODE == kMlstm) x1 = p.g1[b * p.sg1[0] + h * p.sg1[1] + (int64_t)tgc * p.sg1[2]];
+      }
+    };
+    // Gates of chunk cc: b_t = cumsum log f, u_s, the stabilizers M_t / m_new
+    // (from m_in, the state's scale entering the chunk), the state's decay rho,
+    // this row's RowGates, whether the weights separate, and the column vector
+    // colw (C_s, or u_s * log2e).  Every thread takes part (two barriers); colw
+    // is written after the caller's last read of the previous chunk's values.
+    auto compute_gates = [&](int cc, float x0, float x1, float m_in, RowGates& rg, float& rho_out, float& m_out,
+                             bool& sep_out) {
+      const bool v = cc * kC + row < p.seqlen;
+      float li, lf;
+      if (MODE == kMlstm) {
+        li = v ? x0 : -INFINITY;
+        lf = v ? x1 : 0.f;
+      } else {
+        float dtv = v ? x0 + dtb : 0.f;
+        if (p.dt_softplus) dtv = (dtv > 20.f) ? dtv : log1pf(__expf(dtv));
+        li = (v && dtv > 0.f) ? __logf(dtv) : -INFINITY;
+        lf = v ? dtv * A_h : 0.f;
+      }
+      // pass 1: b_t = inclusive sum of log f over the rows, g = the chunk total
+      float bt = lf;
+  #pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, bt, o);
+        if (lane >= o) bt += n;
+      }
+      if (lane == 31) red[hf * 4 + wq] = bt;
+      workers_sync();
+      float g = 0.f;
+  #pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x = red[hf * 4 + i];
+        if (i < wq) bt += x;
+        g += x;
+      }
+      const float us = li - bt;
+      // pass 2: prefix max of u (mLSTM), extremes of u (and of b, SSD), u_0
+      float pm = us, umin = us, bmax = bt, bmin = bt;
+      if (kNorm) {
+  #pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float n = __shfl_up_sync(0xffffffffu, pm, o);
+          if (lane >= o) pm = fmaxf(pm, n);
+        }
+      } else {
+  #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o));
+          bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, o));
+          bmin = fminf(bmin, __shfl_xor_sync(0xffffffffu, bmin, o));
+        }
+      }
+  #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) umin = fminf(umin, __shfl_xor_sync(0xffffffffu, umin, o));
+      if (lane == 31) {
+        red[8 + hf * 4 + wq] = pm;  // the warp's max of u
+        red[16 + hf * 4 + wq] = umin;
+        red[24 + hf * 4 + wq] = bmax;
+        red[32 + hf * 4 + wq] = bmin;
+      }
+      if (row == 0) red[40 + hf] = us;
+      workers_sync();
+      float U = -INFINITY, umn = INFINITY, bmx = -INFINITY, bmn = INFINITY, pre = -INFINITY;
+  #pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x = red[8 + hf * 4 + i];
+        if (i < wq) pre = fmaxf(pre, x);
+        U = fmaxf(U, x);
+        umn = fminf(umn, red[16 + hf * 4 + i]);
+        bmx = fmaxf(bmx, red[24 + hf * 4 + i]);
+        bmn = fminf(bmn, red[32 + hf * 4 + i]);
+      }
+      float rt, m_new, rmax, rmin;
+      if (kNorm) {
+        const float mx = fmaxf(m_in, fmaxf(pm, pre));  // max(m_in, prefix max of u)
+        const float Mt = bt + mx;
+        m_new = g + fmaxf(m_in, U);
+        rt = -mx;  // b_t - M_t, nonincreasing in t
+        rmax = -fmaxf(m_in, red[40 + hf]);
+        rmin = -fmaxf(m_in, U);
+        rg.sc = __expf(m_in - mx);
+        rg.F = __expf(-Mt);
+      } else {
+        m_new = 0.f;
+        rt = bt;
+        rmax = bmx;
+        rmin = bmn;
+        rg.sc = __expf(bt);
+        rg.F = 0.f;
+      }
+      rg.ks = __expf(g + us - m_new);
+      rg.r2 = rt * kLog2e;
+      rho_out = __expf(g + m_in - m_new);
+      m_out = m_new;
+      // a shift c0 with every rt + c0 and us - c0 inside [-40, 40]?
+      const float lo = fmaxf(-rmin - 40.f, U - 40.f);
+      const float hi = fminf(40.f - rmax, 40.f + umn);
+      const bool sep = lo <= hi;  // false for any non-finite extreme (e.g. a row past the end)
+      const float c0 = 0.5f * (lo + hi);
+      rg.R = sep ? __expf(rt + c0) : 1.f;
+      if (hf == 0) colw[row] = sep ? __expf(us - c0) : us * kLog2e;
+      sep_out = sep;
+    };
+
+    RowGates gc;
+    float rho_cur, m_new_cur;
+    bool sep_cur;
+    float gx0, gx1;  // the next chunk's raw gate inputs
+    load_gates(0, gx0, gx1);
+    compute_gates(0, gx0, gx1, m_prev, gc, rho_cur, m_new_cur, sep_cur);
+    if (nchunks > 1) load_gates(1, gx0, gx1);
+    snapshot(rho_cur);
     tc::fence_async_smem();
     tc::tc_fence_before();
-    if (__syncthreads_or(bad)) { bad = 1; break; }
-    // ---- MMAs: Hint = Q.Snap, qn = Q.n, Hintra = P.V; with DK = 128 also the
-    //      state update state += K'^T V, n += K'^T 1 (K' = kscale . K) ---------------
-    const uint32_t tb = *tmem_slot;
-    // state update (A = K^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO =
-    // panel stride); K step = 16 rows); the normalizer's B row 0 is 1 (K scaled)
-    // or kscale (V scaled)
-    auto issue_update = [&]() {
-      tc::static_for<Lt::kNB * (kC / 16)>([&](auto I) {
-        constexpr int blk = decltype(I)::value / (kC / 16), ks = decltype(I)::value % (kC / 16);
-        constexpr uint32_t aoff = (2 * blk) * kPanel + ks * 2048;
-        tc::mma_bf16_at<aoff, ks * 2048>(tb + Lt::tAcc + blk * 64, dKT, dV, idAcc, true);
-        if (kNorm) tc::mma_bf16_at<aoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tAccN + blk * 32, dKT, dOnes, idAccN, true);
-      });
-    };
-    if (tid == 0) {
+
+    int bad = 0;
+#pragma unroll 1
+    for (int c = 0; c < nchunks; ++c) {
+      const int t0 = c * kC;
+      const int tg = t0 + row;
+      const bool valid = tg < p.seqlen;
+      float* denp = denp0 + (c & 1) * 2 * kC;
+      // ---- wait S; P = causal(S) * weight -> smem (bf16), this half's 64 columns ----
+      if (!tc::mbar_wait(bar_s, c & 1, abort_flag)) bad = 1;
       tc::tc_fence_after();
-      tc::static_for<DK / 16>([&](auto KS) {
-        constexpr int ks = decltype(KS)::value;
-        constexpr uint32_t qoff = (ks / 4) * kPanel + (ks % 4) * 32;
-        tc::mma_bf16_at<qoff, ks * 2048>(tb + Lt::tHint, dQ, dSnap, idH, ks > 0);
-        if (kNorm) tc::mma_bf16_at<qoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tQN, dQ, dN, idQN, ks > 0);
-      });
-      tc::static_for<kC / 16>([&](auto KS) {
-        constexpr int ks = decltype(KS)::value;
-        tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tb + Lt::tHintra, dP, dV, idH, ks > 0);
-      });
-      if (kScaleK) issue_update();
-      tc::mma_commit(bar_mma);
-    }
-    // next chunk's gates while the tensor core works on this chunk
-    RowGates gn = gc;
-    float rho_next = 1.f, m_new_next = m_new_cur;
-    bool sep_next = sep_cur;
-    if (c + 1 < nchunks) {
-      compute_gates(c + 1, gx0, gx1, m_new_cur, gn, rho_next, m_new_next, sep_next);
-      if (c + 2 < nchunks) load_gates(c + 2, gx0, gx1);
-    }
-    if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
-    ++mma_uses;
-    tc::tc_fence_after();
-    if (kScaleK) {
-      // Q, K, V of this chunk are consumed: the next chunk's load lands under
-      // the epilogue and the snapshot
-      if (warp == 0 && c + 1 < nchunks && !__any_sync(0xffffffffu, bad)) {
-        issue_load_warp(c + 1);
-        loads_issued = c + 2;
-      }
-    } else {
-      // Q is consumed: its next panels load under the state update
-      if (tid == 0 && !bad && c + 1 < nchunks) {
-        issue_load_q(c + 1);
-        loads_issued = c + 2;
-      }
-      // V rows *= kscale, the normalizer's B row 0 = kscale; then the update
       {
+        float den = 0.f;
+        unsigned char* pp = sm + Lt::kP + hf * kPanel;
+        auto block = [&](int sb) {
+          const int s0 = 64 * hf + 32 * sb;
+          float v[32];
+          const bool need = s0 <= wq * 32 + 31;
+          if (need) {
+            tc::tmem_ld32(tm + Lt::tS + s0, v);
+            tc::tmem_wait_ld();
+            const float4* cw = reinterpret_cast<const float4*>(colw + s0);
+            // DIAG: the block on the diagonal (s0 = 32 (warp % 4)), where column
+            // s0 + j is causal for this row iff j <= lane; blocks left of it are all causal
+            auto weigh = [&](auto diag_tag, auto sep_tag) {
+              constexpr bool kDiag = decltype(diag_tag)::value;
+              constexpr bool kSep = decltype(sep_tag)::value;
+  #pragma unroll
+              for (int j4 = 0; j4 < 8; ++j4) {
+                const float4 c4 = cw[j4];
+                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+  #pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const int j = 4 * j4 + k;
+                  float pv = v[j] * (kSep ? cv[k] : ex2_approx(gc.r2 + cv[k]));
+                  if (kDiag && j > lane) pv = 0.f;
+                  v[j] = pv;
+                  den += pv;
+                }
+              }
+            };
+            if (s0 == wq * 32) {
+              if (sep_cur) weigh(std::true_type{}, std::true_type{});
+              else weigh(std::true_type{}, std::false_type{});
+            } else {
+              if (sep_cur) weigh(std::false_type{}, std::true_type{});
+              else weigh(std::false_type{}, std::false_type{});
+            }
+          } else {
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+  #pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
+            w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
+            w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
+            w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
+            *reinterpret_cast<uint4*>(pp + tc::sw128_offset(row, 32 * sb + 8 * q)) = w;
+          }
+        };
+        block(0);
+        block(1);
+        denp[hf * kC + row] = den;
+      }
+      // ---- kscale (row s = this thread's row): DK = 128 scales the K rows here
+      //      (this half's dk panel), so that one MMA batch below does the outputs
+      //      and the state update, (kscale . K)^T V; DK = 256 scales the V rows
+      //      after the output MMAs (half the elements of a K row).
+      if (kScaleK) {
+        const float ks = gc.ks;
+        unsigned char* krow = sm + Lt::kK + hf * kPanel;
+  #pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint4* ptr = reinterpret_cast<uint4*>(krow + tc::sw128_offset(row, 8 * q));
+          uint4 w = *ptr;
+          uint32_t* e = reinterpret_cast<uint32_t*>(&w);
+  #pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j]));
+            e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+          }
+          *ptr = w;
+        }
+      }
+      // SSD D skip: this row's x values from the staged V (= x) panel
+      uint4 xrow[4];
+      if (MODE == kSsd) {
+  #pragma unroll
+        for (int q = 0; q < 4; ++q)
+          xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(row, ch + 8 * q));
+      }
+      // ---- P, scaled K, the snapshot and the decayed state are ready ----------------
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_pready);
+      // next chunk's gates while the tensor core works on this chunk
+      RowGates gn = gc;
+      float rho_next = 1.f, m_new_next = m_new_cur;
+      bool sep_next = sep_cur;
+      if (c + 1 < nchunks) {
+        compute_gates(c + 1, gx0, gx1, m_new_cur, gn, rho_next, m_new_next, sep_next);
+        if (c + 2 < nchunks) load_gates(c + 2, gx0, gx1);
+      }
+      if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) bad = 1;
+      tc::tc_fence_after();
+      if (!kScaleK) {
+        // V rows *= kscale, the normalizer's B row 0 = kscale: the update is K^T (kscale . V)
         const float ks = gc.ks;
         unsigned char* vrow = sm + Lt::kV;
 #pragma unroll
@@ -583,92 +617,82 @@ __global__ void __launch_bounds__(kThreads, 1)
           __nv_bfloat16* kv = reinterpret_cast<__nv_bfloat16*>(sm + Lt::kOnes);
           kv[((row / 64) * 2048 + tc::sw128_offset(0, row % 64)) / 2] = __float2bfloat16_rn(ks);
         }
+        tc::fence_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_vready);
       }
-      tc::fence_async_smem();
-      tc::tc_fence_before();
-      if (__syncthreads_or(bad)) { bad = 1; break; }
-      if (tid == 0) {
-        tc::tc_fence_after();
-        issue_update();
-        tc::mma_commit(bar_mma);
-      }
-    }
-    // ---- epilogue: output row t, this half's 32 columns ---------------------------
-    {
-      const float den_intra = denp[row] + denp[kC + row];
-      float o[32];
+      // every worker agrees to go on (and the rowsum partials of P are visible)
+      if (workers_sync_or(bad)) { bad = 1; break; }
+      // ---- epilogue: output row t, this half's 32 columns ---------------------------
       {
-        float hi[32], ha[32];
-        tc::tmem_ld32(tm + Lt::tHint + ch, hi);
-        tc::tmem_ld32(tm + Lt::tHintra + ch, ha);
-        const float qn = kNorm ? tc::tmem_ld1(tm + Lt::tQN) : 0.f;
-        tc::tmem_wait_ld();
-        if (kNorm) {
-          const float den = fmaxf(gc.sc * qn + gc.R * den_intra, gc.F);
-          const float inv = 1.f / den;
-          const float a = gc.sc * inv, r = gc.R * inv;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = fmaf(a, hi[j], r * ha[j]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = fmaf(gc.sc, hi[j], gc.R * ha[j]);
+        const float den_intra = denp[row] + denp[kC + row];
+        float o[32];
+        {
+          float hi[32], ha[32];
+          tc::tmem_ld32(tm + Lt::tHint + ch, hi);
+          tc::tmem_ld32(tm + Lt::tHintra + ch, ha);
+          const float qn = kNorm ? tc::tmem_ld1(tm + Lt::tQN) : 0.f;
+          tc::tmem_wait_ld();
+          if (kNorm) {
+            const float den = fmaxf(gc.sc * qn + gc.R * den_intra, gc.F);
+            const float inv = 1.f / den;
+            const float a = gc.sc * inv, r = gc.R * inv;
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] = fmaf(a, hi[j], r * ha[j]);
+          } else {
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] = fmaf(gc.sc, hi[j], gc.R * ha[j]);
+          }
         }
-      }
-      const bool ok = valid && e0 + ch < p.dv;
-      if (MODE == kSsd && ok && Dh != 0.f) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 w = xrow[q];
-          const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(x2[j]);
-            o[8 * q + 2 * j] = fmaf(Dh, f.x, o[8 * q + 2 * j]);
-            o[8 * q + 2 * j + 1] = fmaf(Dh, f.y, o[8 * q + 2 * j + 1]);
+        const bool ok = valid && e0 + ch < p.dv;
+        if (MODE == kSsd && ok && Dh != 0.f) {
+  #pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 w = xrow[q];
+            const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+  #pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(x2[j]);
+              o[8 * q + 2 * j] = fmaf(Dh, f.x, o[8 * q + 2 * j]);
+              o[8 * q + 2 * j + 1] = fmaf(Dh, f.y, o[8 * q + 2 * j + 1]);
+            }
+          }
+        }
+        if (ok) {
+          __nv_bfloat16* orow = p.out + b * p.so[0] + h * p.so[1] + (int64_t)tg * p.so[2] + e0 + ch;
+  #pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack2<__nv_bfloat16>(o[8 * q + 0], o[8 * q + 1]);
+            w.y = pack2<__nv_bfloat16>(o[8 * q + 2], o[8 * q + 3]);
+            w.z = pack2<__nv_bfloat16>(o[8 * q + 4], o[8 * q + 5]);
+            w.w = pack2<__nv_bfloat16>(o[8 * q + 6], o[8 * q + 7]);
+            *reinterpret_cast<uint4*>(orow + 8 * q) = w;
           }
         }
       }
-      if (ok) {
-        __nv_bfloat16* orow = p.out + b * p.so[0] + h * p.so[1] + (int64_t)tg * p.so[2] + e0 + ch;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 w;
-          w.x = pack2<__nv_bfloat16>(o[8 * q + 0], o[8 * q + 1]);
-          w.y = pack2<__nv_bfloat16>(o[8 * q + 2], o[8 * q + 3]);
-          w.z = pack2<__nv_bfloat16>(o[8 * q + 4], o[8 * q + 5]);
-          w.w = pack2<__nv_bfloat16>(o[8 * q + 6], o[8 * q + 7]);
-          *reinterpret_cast<uint4*>(orow + 8 * q) = w;
-        }
+      if (!kScaleK) {
+        if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) bad = 1;
+        tc::tc_fence_after();
       }
+      // ---- snapshot of the updated state for the next chunk's Hint, decayed state ----
+      snapshot(rho_next);
+      m_prev = m_new_cur;
+      m_new_cur = m_new_next;
+      gc = gn;
+      sep_cur = sep_next;
+      tc::fence_async_smem();
+      tc::tc_fence_before();
     }
-    // ---- (DK = 256: wait for the update, refill K, V); snapshot of the updated
-    //      state for the next chunk's Hint ------------------------------------------
-    if (!kScaleK) {
-      if (!tc::mbar_wait(bar_mma, mma_uses & 1, abort_flag)) bad = 1;
-      ++mma_uses;
-      tc::tc_fence_after();
-      if (__syncthreads_or(bad)) { bad = 1; break; }
-      if (tid == 0 && c + 1 < nchunks) issue_load_kv(c + 1);
-    }
-    snapshot(rho_next);
-    m_prev = m_new_cur;
-    m_new_cur = m_new_next;
-    gc = gn;
-    sep_cur = sep_next;
-    tc::fence_async_smem();
-    tc::tc_fence_before();
-    __syncthreads();
+    m_final = m_prev;
   }
 
-  // A wait that gave up can leave a load in flight: let it land (bounded)
-  // before the shared memory is released.
-  if (bad && tid == 0 && loads_issued > loads_done) {
-    volatile int no_abort = 0;
-    tc::mbar_wait(bar_load, (loads_issued - 1) & 1, &no_abort, 20000000ll);
-  }
+  // ---- final state (none after a wait that gave up: every give-up raised the
+  //      abort flag, read by all threads after the barrier) ------------------------
+  tc::tc_fence_before();
   __syncthreads();
-  // ---- final state ---------------------------------------------------------------
-  if (!bad) {
+  const bool ok = *abort_flag == 0;
+  if (worker && ok) {
     tc::tc_fence_after();
 #pragma unroll 1
     for (int blk = 0; blk < Lt::kNB; ++blk) {
@@ -692,8 +716,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         p.nT[(int64_t)bh * DK + srow] = n;
       }
     }
-    if (kNorm && p.mT && blockIdx.x == 0 && tid == 0) p.mT[bh] = m_prev;
-  } else if (tid == 0) {
+    if (kNorm && p.mT && blockIdx.x == 0 && tid == 0) p.mT[bh] = m_final;
+  } else if (!ok && tid == 0) {
     if (p.error_flag) atomicExch(p.error_flag, 1);
   }
   tc::tc_fence_before();
