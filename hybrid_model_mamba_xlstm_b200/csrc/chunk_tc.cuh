@@ -77,10 +77,14 @@ struct Params {
 template <int DK>
 struct Layout {
   static constexpr int kNB = DK / 128;         // 128-row TMEM blocks of the state
+  // Q, K, V of a chunk form one stage; DK = 128 double-buffers them (the next
+  // chunk loads, and its S = Q K^T runs, while this chunk finishes)
+  static constexpr int kStages = DK == 128 ? 2 : 1;
   static constexpr int kQ = 0;                  // DK/64 panels
   static constexpr int kK = kQ + DK / 64 * kPanel;
   static constexpr int kV = kK + DK / 64 * kPanel;
-  static constexpr int kP = kV + kPanel;        // 2 panels
+  static constexpr int kStage = kV + kPanel;    // bytes of one stage
+  static constexpr int kP = kStages * kStage;   // 2 panels
   static constexpr int kSnap = kP + 2 * kPanel; // DK rows x 128 B (MN-major, one N panel)
   static constexpr int kN = kSnap + DK * 128;   // n snapshot, K-major [16][DK]: DK/64 panels of 2 KB
   static constexpr int kOnes = kN + DK / 64 * 2048;  // K-major [16][128]: 2 panels of 2 KB
@@ -88,7 +92,7 @@ struct Layout {
   static constexpr int kColW = kMisc;          // float[128]: C_s (separable) or u_s * log2e, by column s
   static constexpr int kDen = kColW + 512;     // float[2][2][128]: rowsum(P) partials of the two column halves, by chunk parity
   static constexpr int kRed = kDen + 2048;     // float[64] reductions
-  static constexpr int kBar = kRed + 256;      // 7 x uint64
+  static constexpr int kBar = kRed + 256;      // 8 x uint64
   static constexpr int kTmemSlot = kBar + 64;
   static constexpr int kAbort = kTmemSlot + 4;
   static constexpr int kBytes = kAbort + 12;
@@ -137,13 +141,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* colw = reinterpret_cast<float*>(sm + Lt::kColW);
   float* denp0 = reinterpret_cast<float*>(sm + Lt::kDen);
   float* red = reinterpret_cast<float*>(sm + Lt::kRed);
-  uint64_t* bar_load = reinterpret_cast<uint64_t*>(sm + Lt::kBar);  // TMA: this chunk's Q, K, V
-  uint64_t* bar_s = bar_load + 1;       // MMA: S done
-  uint64_t* bar_a = bar_load + 2;       // MMA: outputs (+ state update, DK = 128) done
-  uint64_t* bar_b = bar_load + 3;       // MMA: state update done (DK = 256)
-  uint64_t* bar_pready = bar_load + 4;  // workers: P, scaled K, snapshot, decayed state ready
-  uint64_t* bar_vready = bar_load + 5;  // workers: scaled V ready (DK = 256)
-  uint64_t* bar_fin = bar_load + 6;     // MMA: drain before exit
+  uint64_t* bar_load = reinterpret_cast<uint64_t*>(sm + Lt::kBar);  // TMA: a stage's Q, K, V (one per stage)
+  uint64_t* bar_s = bar_load + 2;       // MMA: S done
+  uint64_t* bar_a = bar_load + 3;       // MMA: outputs (+ state update, DK = 128) done
+  uint64_t* bar_b = bar_load + 4;       // MMA: state update done (DK = 256)
+  uint64_t* bar_pready = bar_load + 5;  // workers: P, scaled K, snapshot, decayed state ready
+  uint64_t* bar_vready = bar_load + 6;  // workers: scaled V ready (DK = 256)
+  uint64_t* bar_fin = bar_load + 7;     // MMA: drain before exit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + Lt::kTmemSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + Lt::kAbort);
 
@@ -163,6 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
     tc::mbar_init(bar_load, 1);
+    tc::mbar_init(bar_load + 1, 1);
     tc::mbar_init(bar_s, 1);
     tc::mbar_init(bar_a, 1);
     tc::mbar_init(bar_b, 1);
@@ -212,89 +217,128 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const int hq = (MODE == kSsd) ? 0 : h;
       constexpr uint32_t kLoadBytes = (2 * kNP + 1) * kPanel;
-      // Chunk c's operands arrive on one barrier phase, in one part (DK = 128)
-      // or in two: Q (free once the output MMAs are done) and K, V (free once
-      // the state update is done).
+      int waits[2] = {0, 0};     // completed waits per stage barrier (its phase)
+      bool pend[2] = {false, false};  // a load issued and not yet waited, per stage
+      // Chunk c's operands (stage c % kStages) arrive on the stage's barrier, in
+      // one part or in two: Q (free once the output MMAs are done) and K, V
+      // (free once the state update is done).
       auto load_q = [&](int c) {
-        tc::mbar_expect_tx(bar_load, kLoadBytes);
+        const int st = c % Lt::kStages;
+        tc::mbar_expect_tx(bar_load + st, kLoadBytes);
+        pend[st] = true;
         for (int pnl = 0; pnl < kNP; ++pnl)
-          tc::tma_load_4d(sm + Lt::kQ + pnl * kPanel, &tmQ, bar_load, pnl * 64, c * kC, hq, b);
+          tc::tma_load_4d(sm + st * Lt::kStage + Lt::kQ + pnl * kPanel, &tmQ, bar_load + st, pnl * 64, c * kC, hq, b);
       };
       auto load_kv = [&](int c) {
+        const int st = c % Lt::kStages;
         for (int pnl = 0; pnl < kNP; ++pnl)
-          tc::tma_load_4d(sm + Lt::kK + pnl * kPanel, &tmK, bar_load, pnl * 64, c * kC, hq, b);
-        tc::tma_load_4d(sm + Lt::kV, &tmV, bar_load, e0, c * kC, h, b);
+          tc::tma_load_4d(sm + st * Lt::kStage + Lt::kK + pnl * kPanel, &tmK, bar_load + st, pnl * 64, c * kC, hq, b);
+        tc::tma_load_4d(sm + st * Lt::kStage + Lt::kV, &tmV, bar_load + st, e0, c * kC, h, b);
+      };
+      auto wait_load = [&](int c) {
+        const int st = c % Lt::kStages;
+        const bool ok = tc::mbar_wait(bar_load + st, waits[st] & 1, abort_flag);
+        if (ok) {
+          ++waits[st];
+          pend[st] = false;
+        }
+        return ok;
       };
       const uint32_t tb = *tmem_slot;
-      // state update (A = K^T: M = 128 state rows = K panels 2blk, 2blk+1 (LBO =
-      // panel stride); K step = 16 rows); the normalizer's B row 0 is 1 (K
-      // scaled) or kscale (V scaled)
-      auto issue_update = [&]() {
-        tc::static_for<Lt::kNB * (kC / 16)>([&](auto I) {
-          constexpr int blk = decltype(I)::value / (kC / 16), ks = decltype(I)::value % (kC / 16);
-          constexpr uint32_t aoff = (2 * blk) * kPanel + ks * 2048;
-          tc::mma_bf16_at<aoff, ks * 2048>(tb + Lt::tAcc + blk * 64, dKT, dV, idAcc, true);
-          if (kNorm)
-            tc::mma_bf16_at<aoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tAccN + blk * 32, dKT, dOnes, idAccN,
-                                                                   true);
-        });
-      };
-      int loads_issued = 1, loads_done = 0;
-      load_q(0);
-      load_kv(0);
-#pragma unroll 1
-      for (int c = 0; c < nchunks; ++c) {
-        if (!tc::mbar_wait(bar_load, c & 1, abort_flag)) break;
-        loads_done = c + 1;
-        tc::tc_fence_after();
-        // S = Q K^T
+      // S = Q K^T of chunk c
+      auto issue_s = [&](int c) {
+        const uint32_t so = (c % Lt::kStages) * Lt::kStage;
+        const uint64_t q = tc::desc_add(dQ, so), k = tc::desc_add(dK, so);
         tc::static_for<DK / 16>([&](auto KS) {
           constexpr int ks = decltype(KS)::value;
           constexpr uint32_t off = (ks / 4) * kPanel + (ks % 4) * 32;
-          tc::mma_bf16_at<off, off>(tb + Lt::tS, dQ, dK, idS, ks > 0);
+          tc::mma_bf16_at<off, off>(tb + Lt::tS, q, k, idS, ks > 0);
         });
         tc::mma_commit(bar_s);
-        // Hint = Q.Snap, qn = Q.n, Hintra = P.V (+ the state update, DK = 128)
-        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag)) break;
-        tc::tc_fence_after();
+      };
+      // Hint = Q.Snap, qn = Q.n, Hintra = P.V of chunk c
+      auto issue_out = [&](int c) {
+        const uint32_t so = (c % Lt::kStages) * Lt::kStage;
+        const uint64_t q = tc::desc_add(dQ, so), v = tc::desc_add(dV, so);
         tc::static_for<DK / 16>([&](auto KS) {
           constexpr int ks = decltype(KS)::value;
           constexpr uint32_t qoff = (ks / 4) * kPanel + (ks % 4) * 32;
-          tc::mma_bf16_at<qoff, ks * 2048>(tb + Lt::tHint, dQ, dSnap, idH, ks > 0);
-          if (kNorm) tc::mma_bf16_at<qoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tQN, dQ, dN, idQN, ks > 0);
+          tc::mma_bf16_at<qoff, ks * 2048>(tb + Lt::tHint, q, dSnap, idH, ks > 0);
+          if (kNorm) tc::mma_bf16_at<qoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tQN, q, dN, idQN, ks > 0);
         });
         tc::static_for<kC / 16>([&](auto KS) {
           constexpr int ks = decltype(KS)::value;
-          tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tb + Lt::tHintra, dP, dV, idH, ks > 0);
+          tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tb + Lt::tHintra, dP, v, idH, ks > 0);
         });
-        if (kScaleK) issue_update();
-        tc::mma_commit(bar_a);
-        if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) break;
+      };
+      // state update of chunk c (A = K^T: M = 128 state rows = K panels 2blk,
+      // 2blk+1 (LBO = panel stride); K step = 16 rows); the normalizer's B row
+      // 0 is 1 (K scaled) or kscale (V scaled)
+      auto issue_update = [&](int c) {
+        const uint32_t so = (c % Lt::kStages) * Lt::kStage;
+        const uint64_t kt = tc::desc_add(dKT, so), v = tc::desc_add(dV, so);
+        tc::static_for<Lt::kNB * (kC / 16)>([&](auto I) {
+          constexpr int blk = decltype(I)::value / (kC / 16), ks = decltype(I)::value % (kC / 16);
+          constexpr uint32_t aoff = (2 * blk) * kPanel + ks * 2048;
+          tc::mma_bf16_at<aoff, ks * 2048>(tb + Lt::tAcc + blk * 64, kt, v, idAcc, true);
+          if (kNorm)
+            tc::mma_bf16_at<aoff, (ks / 4) * 2048 + (ks % 4) * 32>(tb + Lt::tAccN + blk * 32, kt, dOnes, idAccN, true);
+        });
+      };
+      load_q(0);
+      load_kv(0);
+      if (Lt::kStages == 2 && nchunks > 1) {
+        load_q(1);
+        load_kv(1);
+      }
+      bool ok = wait_load(0);
+      if (ok) {
+        tc::tc_fence_after();
+        issue_s(0);
+      }
+#pragma unroll 1
+      for (int c = 0; ok && c < nchunks; ++c) {
+        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag)) break;
+        tc::tc_fence_after();
+        issue_out(c);
         if (kScaleK) {
+          issue_update(c);
+          tc::mma_commit(bar_a);
+          // the next chunk's S right behind (its stage loaded a chunk ahead)
           if (c + 1 < nchunks) {
-            load_q(c + 1);
-            load_kv(c + 1);
-            loads_issued = c + 2;
+            if (!wait_load(c + 1)) break;
+            tc::tc_fence_after();
+            issue_s(c + 1);
+          }
+          if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) break;
+          if (c + 2 < nchunks) {  // this chunk's stage is free
+            load_q(c + 2);
+            load_kv(c + 2);
           }
         } else {
-          if (c + 1 < nchunks) {
-            load_q(c + 1);
-            loads_issued = c + 2;
-          }
+          tc::mma_commit(bar_a);
+          if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) break;
+          if (c + 1 < nchunks) load_q(c + 1);
           if (!tc::mbar_wait(bar_vready, c & 1, abort_flag)) break;
           tc::tc_fence_after();
-          issue_update();
+          issue_update(c);
           tc::mma_commit(bar_b);
           if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) break;
-          if (c + 1 < nchunks) load_kv(c + 1);
+          if (c + 1 < nchunks) {
+            load_kv(c + 1);
+            if (!wait_load(c + 1)) break;
+            tc::tc_fence_after();
+            issue_s(c + 1);
+          }
         }
       }
       // Leave nothing in flight: every MMA of this thread done, and (after a
-      // wait that gave up) the last load landed — both bounded.
+      // wait that gave up) the loads issued and not waited landed — all bounded.
       volatile int no_abort = 0;
       tc::mma_commit(bar_fin);
       tc::mbar_wait(bar_fin, 0, &no_abort, 20000000ll);
-      if (*abort_flag && loads_issued > loads_done) tc::mbar_wait(bar_load, (loads_issued - 1) & 1, &no_abort, 20000000ll);
+      for (int st = 0; st < Lt::kStages; ++st)
+        if (pend[st]) tc::mbar_wait(bar_load + st, waits[st] & 1, &no_abort, 20000000ll);
     }
     __syncwarp();
   } else {
@@ -501,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!tc::mbar_wait(bar_s, c & 1, abort_flag)) bad = 1;
       tc::tc_fence_after();
       {
-        float den = 0.f;
+        float2 den2 = make_float2(0.f, 0.f);  // rowsum of P, two partial sums
         unsigned char* pp = sm + Lt::kP + hf * kPanel;
         auto block = [&](int sb) {
           const int s0 = 64 * hf + 32 * sb;
@@ -519,14 +563,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   #pragma unroll
               for (int j4 = 0; j4 < 8; ++j4) {
                 const float4 c4 = cw[j4];
-                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
   #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const int j = 4 * j4 + k;
-                  float pv = v[j] * (kSep ? cv[k] : ex2_approx(gc.r2 + cv[k]));
-                  if (kDiag && j > lane) pv = 0.f;
-                  v[j] = pv;
-                  den += pv;
+                for (int k = 0; k < 2; ++k) {
+                  const int j = 4 * j4 + 2 * k;
+                  float2 w = k ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+                  if (!kSep) {
+                    w = __fadd2_rn(make_float2(gc.r2, gc.r2), w);
+                    w = make_float2(ex2_approx(w.x), ex2_approx(w.y));
+                  }
+                  float2 pv = __fmul2_rn(make_float2(v[j], v[j + 1]), w);
+                  if (kDiag) {
+                    if (j > lane) pv.x = 0.f;
+                    if (j + 1 > lane) pv.y = 0.f;
+                  }
+                  v[j] = pv.x;
+                  v[j + 1] = pv.y;
+                  den2 = __fadd2_rn(den2, pv);
                 }
               }
             };
@@ -553,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         block(0);
         block(1);
-        denp[hf * kC + row] = den;
+        denp[hf * kC + row] = den2.x + den2.y;
       }
       // ---- kscale (row s = this thread's row): DK = 128 scales the K rows here
       //      (this half's dk panel), so that one MMA batch below does the outputs
@@ -561,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       //      after the output MMAs (half the elements of a K row).
       if (kScaleK) {
         const float ks = gc.ks;
-        unsigned char* krow = sm + Lt::kK + hf * kPanel;
+        unsigned char* krow = sm + (c % Lt::kStages) * Lt::kStage + Lt::kK + hf * kPanel;
   #pragma unroll
         for (int q = 0; q < 8; ++q) {
           uint4* ptr = reinterpret_cast<uint4*>(krow + tc::sw128_offset(row, 8 * q));
@@ -569,8 +621,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t* e = reinterpret_cast<uint32_t*>(&w);
   #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j]));
-            e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+            const float2 f = __fmul2_rn(__bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j])), make_float2(ks, ks));
+            e[j] = pack2<__nv_bfloat16>(f.x, f.y);
           }
           *ptr = w;
         }
@@ -580,7 +632,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (MODE == kSsd) {
   #pragma unroll
         for (int q = 0; q < 4; ++q)
-          xrow[q] = *reinterpret_cast<const uint4*>(sm + Lt::kV + tc::sw128_offset(row, ch + 8 * q));
+          xrow[q] = *reinterpret_cast<const uint4*>(sm + (c % Lt::kStages) * Lt::kStage + Lt::kV +
+                                                    tc::sw128_offset(row, ch + 8 * q));
       }
       // ---- P, scaled K, the snapshot and the decayed state are ready ----------------
       tc::fence_async_smem();
@@ -608,8 +661,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t* e = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j]));
-            e[j] = pack2<__nv_bfloat16>(f.x * ks, f.y * ks);
+            const float2 f = __fmul2_rn(__bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[j])), make_float2(ks, ks));
+            e[j] = pack2<__nv_bfloat16>(f.x, f.y);
           }
           *ptr = w;
         }
