@@ -531,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     compute_gates(0, gx0, gx1, m_prev, gc, rho_cur, m_new_cur, sep_cur);
     if (nchunks > 1) load_gates(1, gx0, gx1);
     snapshot(rho_cur);
+    workers_sync();  // colw of chunk 0 written
     tc::fence_async_smem();
     tc::tc_fence_before();
 
