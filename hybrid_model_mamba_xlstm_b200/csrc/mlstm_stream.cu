@@ -41,7 +41,8 @@ constexpr int kStages = 3;
 // grid (B*H*nchunks, ceil(DK/128)), block 128: thread = key channel j.
 template <typename T>
 __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks,
-                                                             __nv_bfloat16* Kh, float* decay, float* rho_e) {
+                                                             __nv_bfloat16* Kh, float* decay, float* rho_e,
+                                                             float* nadd) {
   const int nch = (p.seqlen + kC - 1) / kC;
   const int c = blockIdx.x % nch;
   const int bh = blockIdx.x / nch;
@@ -59,60 +60,95 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
   for (int t = 0; t < tn; ++t) g += lf[(int64_t)(t0 + t) * p.tf + gj];
   const float rho = 0.5f * g;
   const int64_t ob = (int64_t)bh * p.seqlen * p.dqk;
-  float bt = 0.f;
+  float bt = 0.f, ksum = 0.f;
   for (int t = 0; t < tn; ++t) {
     const int64_t tt = t0 + t;
     bt += lf[tt * p.tf + gj];
     const float lit = li[tt * p.ti + gj];
     const float qv = to_f32<T>(q[tt * p.tq + j]);
     const float kv = to_f32<T>(k[tt * p.tk + j]);
+    const float kh = kv * __expf(g - bt + lit);
     Qs[ob + tt * p.dqk + j] = __float2bfloat16_rn(qv * __expf(bt - rho));
     Ks[ob + tt * p.dqk + j] = __float2bfloat16_rn(kv * __expf(rho - bt + lit));
-    Kh[ob + tt * p.dqk + j] = __float2bfloat16_rn(kv * __expf(g - bt + lit));
+    Kh[ob + tt * p.dqk + j] = __float2bfloat16_rn(kh);
+    ksum += kh;
   }
-  decay[((int64_t)bh * nch + c) * p.dqk + j] = __expf(g);
-  rho_e[((int64_t)bh * nch + c) * p.dqk + j] = __expf(rho);
+  const int64_t vi = ((int64_t)bh * nch + c) * p.dqk + j;
+  decay[vi] = __expf(g);
+  rho_e[vi] = __expf(rho);
+  nadd[vi] = ksum;  // the chunk's Kh^T 1: the normalizer's increment
 }
 
 // ------------------------------------------------------------ stream kernel --
+// Warps 0-7: element-wise work (warp w reads TMEM lanes 32 (w % 4) .., the two
+// warps of a lane quarter split the columns: half h = w / 4).  Warp 8: the
+// MMA issuer (and the V loads).  Warp 9: the TMA producer of the Q/K panel ring.
+constexpr int kWorkers = 8;
+constexpr int kStreamThreads = 32 * kWorkers + 64;
+
 template <int DK>
 struct SL {
   static constexpr int kNP = DK / 64;                 // key panels
   static constexpr int kNB = DK / 128;                // state row blocks (TMEM 128 lanes)
+  static constexpr int kLPC = kNP + kNB;              // ring loads per chunk
   static constexpr int kRing = 0;                     // kStages x 32 KB
   static constexpr int kSnap = kRing + kStages * 2 * kPanel;  // DK rows x 128 B (MN-major B, one 64-wide N panel)
   static constexpr int kP = kSnap + DK * 128;         // 2 panels
   static constexpr int kV = kP + 2 * kPanel;          // 1 panel
-  static constexpr int kOnes = kV + kPanel;           // K-major [16][128] = 2 x 2 KB
-  static constexpr int kNs = kOnes + 4096;            // float [DK]  rho_e . n   (for qn)
-  static constexpr int kBar = kNs + DK * 4;           // full[kStages], empty[kStages], v, s, h, acc
-  static constexpr int kSlot = kBar + 8 * (2 * kStages + 4);
+  static constexpr int kN = kV + kPanel;              // float [DK]  n, the normalizer state
+  static constexpr int kNs = kN + DK * 4;             // float [DK]  rho_e . n   (for qn)
+  static constexpr int kRow = kNs + DK * 4;           // float [2 parity][2 (qn, rowsum)][2 half][128]
+  static constexpr int kBar = kRow + 2 * 2 * 2 * 128 * 4;  // full[kStages], empty[kStages], v, s, pready, b, snap, fin
+  static constexpr int kSlot = kBar + 8 * (2 * kStages + 6);
   static constexpr int kAbort = kSlot + 4;
   static constexpr int kBytes = kAbort + 12;
-  // TMEM columns: S 0..127, H 128..191, state blocks 256 + 64 b, n blocks 192 + 16 b
-  static constexpr int tS = 0, tH = 128, tN = 192, tAcc = 256;
-  static_assert(tN + 16 * kNB <= tAcc && tAcc + 64 * kNB <= 512, "TMEM layout");
+  // TMEM columns: S 0..127, H (double buffered) 128..255, state blocks 256 + 64 b
+  static constexpr int tS = 0, tH = 128, tAcc = 256;
+  static_assert(tAcc + 64 * kNB <= 512, "TMEM layout");
 };
 
+// Named barrier 1 over the 256 element-wise threads; `_or`: any thread's v != 0.
+HXM_DEV void stream_workers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+HXM_DEV int stream_workers_sync_or(int v) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.s32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 256, p;\n\t"
+      "selp.s32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(v)
+      : "memory");
+  return r;
+}
+
 template <int DK>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kStreamThreads, 1)
     mlstm_stream_kernel(const __grid_constant__ CUtensorMap tmQs, const __grid_constant__ CUtensorMap tmKs,
                         const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmV,
-                        const Params p, const float* __restrict__ decay, const float* __restrict__ rho_e) {
+                        const Params p, const float* __restrict__ decay, const float* __restrict__ rho_e,
+                        const float* __restrict__ nadd) {
   using L = SL<DK>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::kBar);
   uint64_t* empty = full + kStages;
-  uint64_t* bar_v = empty + kStages;
-  uint64_t* bar_s = bar_v + 1;   // S and Qs.Snap done
-  uint64_t* bar_h = bar_v + 2;   // P.V done
-  uint64_t* bar_a = bar_v + 3;   // state update done
+  uint64_t* bar_v = empty + kStages;  // TMA: V of the chunk
+  uint64_t* bar_s = bar_v + 1;        // MMA: S and Qs.Snap of the chunk
+  uint64_t* bar_pready = bar_v + 2;   // workers: P written
+  uint64_t* bar_b = bar_v + 3;        // MMA: P.V and the state update
+  uint64_t* bar_snap = bar_v + 4;     // workers: snapshot, decayed state; the older H buffer read
+  uint64_t* bar_fin = bar_v + 5;      // MMA: drain before exit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L::kSlot);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kAbort);
+  float* nst = reinterpret_cast<float*>(sm + L::kN);
   float* ns = reinterpret_cast<float*>(sm + L::kNs);
+  float* rowv = reinterpret_cast<float*>(sm + L::kRow);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int wq = warp & 3, hf = (warp >> 2) & 1;
+  const int row = wq * 32 + lane;  // chunk row t / state row within a 128-row block
+  const int ch = 32 * hf;
   const int e0 = blockIdx.x * kDV, h = blockIdx.y, b = blockIdx.z;
   const int bh = b * p.heads + h;
   const int nch = (p.seqlen + kC - 1) / kC;
@@ -122,287 +158,297 @@ __global__ void __launch_bounds__(128, 1)
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       tc::mbar_init(&full[i], 1);
-      tc::mbar_init(&empty[i], 1 + 4);  // MMA commit + one arrive per consumer warp
+      tc::mbar_init(&empty[i], 1 + kWorkers);  // MMA commit + one arrive per worker warp
     }
     tc::mbar_init(bar_v, 1);
     tc::mbar_init(bar_s, 1);
-    tc::mbar_init(bar_h, 1);
-    tc::mbar_init(bar_a, 1);
+    tc::mbar_init(bar_pready, kWorkers);
+    tc::mbar_init(bar_b, 1);
+    tc::mbar_init(bar_snap, kWorkers);
+    tc::mbar_init(bar_fin, 1);
     tc::fence_mbar_init();
     *abort_flag = 0;
   }
-  {  // ones operand: K-major [16][128], row 0 = 1
-    uint4* z = reinterpret_cast<uint4*>(sm + L::kOnes);
-    for (int i = tid; i < 4096 / 16; i += 128) z[i] = make_uint4(0, 0, 0, 0);
-    __syncthreads();
-    __nv_bfloat16* ones = reinterpret_cast<__nv_bfloat16*>(sm + L::kOnes);
-    ones[((tid / 64) * 2048 + tc::sw128_offset(0, tid % 64)) / 2] = __float2bfloat16_rn(1.f);
+  {  // P: blocks right of the diagonal are never written again
+    uint4* zp = reinterpret_cast<uint4*>(sm + L::kP);
+    for (int i = tid; i < 2 * kPanel / 16; i += kStreamThreads) zp[i] = make_uint4(0, 0, 0, 0);
   }
+  tc::fence_async_smem();
   __syncthreads();
   tc::tc_fence_after();
-  const uint32_t tm = *tmem_slot;
+  const uint32_t tb = *tmem_slot;
+  const uint32_t tm = tb + ((uint32_t)(wq * 32) << 16);
+  const uint64_t dSnap = tc::sdesc_sw128(sbase + L::kSnap, kPanel, 1024);
+  const uint64_t dP = tc::sdesc_sw128(sbase + L::kP, 16, 1024);
+  const uint64_t dV = tc::sdesc_sw128(sbase + L::kV, kPanel, 1024);
+  constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, false);
+  constexpr uint32_t idH = tc::idesc_bf16(128, kDV, false, true);
+  constexpr uint32_t idAcc = tc::idesc_bf16(128, kDV, true, true);
+  const int total_loads = nch * L::kLPC;
 
-  // initial state -> TMEM (the caller's stabilized C0/n0 scaled by e^m0)
-  const float s0 = p.m0 ? __expf(p.m0[bh]) : 1.f;
+  if (warp == kWorkers) {
+    // ================= MMA issuer (one lane) =================
+    if (lane == 0) {
+      int loads_v = 0, waited_v = 0;
+      auto load_v = [&](int c) {
+        tc::mbar_expect_tx(bar_v, kPanel);
+        tc::tma_load_4d(sm + L::kV, &tmV, bar_v, e0, c * kC, h, b);
+        ++loads_v;
+      };
+      load_v(0);
 #pragma unroll 1
-  for (int blk = 0; blk < L::kNB; ++blk) {
-    const int row = blk * 128 + warp * 32 + lane;
+      for (int c = 0; c < nch; ++c) {
+        const uint32_t tH = tb + L::tH + (c & 1) * kDV;
+        if (!tc::mbar_wait(bar_snap, c & 1, abort_flag)) break;
+        tc::tc_fence_after();
+        // pass A: S = Qs Ks^T, H = Qs Snap (panel by panel from the ring)
+        bool ok = true;
 #pragma unroll 1
-    for (int c0 = 0; c0 < kDV; c0 += 32) {
+        for (int pnl = 0; pnl < L::kNP; ++pnl) {
+          const int idx = c * L::kLPC + pnl, slot = idx % kStages;
+          if (!tc::mbar_wait(&full[slot], (idx / kStages) & 1, abort_flag)) { ok = false; break; }
+          tc::tc_fence_after();
+          const uint64_t dq = tc::sdesc_sw128(sbase + L::kRing + slot * 2 * kPanel, 16, 1024);
+          const uint64_t dsn = tc::desc_add(dSnap, pnl * 4 * 2048);
+          const bool acc = pnl > 0;
+          tc::static_for<4>([&](auto KK) {
+            constexpr int kk = decltype(KK)::value;
+            tc::mma_bf16_at<kk * 32, kPanel + kk * 32>(tb + L::tS, dq, dq, idS, acc || kk > 0);
+            tc::mma_bf16_at<kk * 32, kk * 2048>(tH, dq, dsn, idH, acc || kk > 0);
+          });
+          tc::mma_commit(&empty[slot]);
+        }
+        if (!ok) break;
+        tc::mma_commit(bar_s);
+        // H += P V once P is written and V landed
+        if (!tc::mbar_wait(bar_v, waited_v & 1, abort_flag)) break;
+        ++waited_v;
+        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag)) break;
+        tc::tc_fence_after();
+        tc::static_for<kC / 16>([&](auto KS) {
+          constexpr int ks = decltype(KS)::value;
+          tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tH, dP, dV, idH, true);
+        });
+        // pass B: state += Kh^T V, block by block
+#pragma unroll 1
+        for (int blk = 0; blk < L::kNB; ++blk) {
+          const int idx = c * L::kLPC + L::kNP + blk, slot = idx % kStages;
+          if (!tc::mbar_wait(&full[slot], (idx / kStages) & 1, abort_flag)) { ok = false; break; }
+          tc::tc_fence_after();
+          const uint64_t dk = tc::sdesc_sw128(sbase + L::kRing + slot * 2 * kPanel, kPanel, 1024);
+          const uint32_t tAcc = tb + L::tAcc + blk * 64;
+          tc::static_for<kC / 16>([&](auto KS) {
+            constexpr int ks = decltype(KS)::value;
+            tc::mma_bf16_at<ks * 2048, ks * 2048>(tAcc, dk, dV, idAcc, true);
+          });
+          tc::mma_commit(&empty[slot]);
+        }
+        if (!ok) break;
+        tc::mma_commit(bar_b);
+        if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) break;
+        if (c + 1 < nch) load_v(c + 1);  // V is free
+      }
+      // leave nothing in flight (bounded): the MMAs, and a V load not waited for
+      volatile int no_abort = 0;
+      tc::mma_commit(bar_fin);
+      tc::mbar_wait(bar_fin, 0, &no_abort, 20000000ll);
+      if (loads_v > waited_v) tc::mbar_wait(bar_v, waited_v & 1, &no_abort, 20000000ll);
+    }
+    __syncwarp();
+  } else if (warp == kWorkers + 1) {
+    // ================= TMA producer of the panel ring (one lane) =================
+    if (lane == 0) {
+      int issued = 0;
+#pragma unroll 1
+      for (int idx = 0; idx < total_loads; ++idx) {
+        const int slot = idx % kStages;
+        if (idx >= kStages && !tc::mbar_wait(&empty[slot], ((idx / kStages) - 1) & 1, abort_flag)) break;
+        const int c = idx / L::kLPC, r = idx % L::kLPC;
+        unsigned char* dst = sm + L::kRing + slot * 2 * kPanel;
+        tc::mbar_expect_tx(&full[slot], 2 * kPanel);
+        if (r < L::kNP) {
+          tc::tma_load_4d(dst, &tmQs, &full[slot], r * 64, c * kC, h, b);
+          tc::tma_load_4d(dst + kPanel, &tmKs, &full[slot], r * 64, c * kC, h, b);
+        } else {
+          const int blk = r - L::kNP;
+          tc::tma_load_4d(dst, &tmKh, &full[slot], blk * 128, c * kC, h, b);
+          tc::tma_load_4d(dst + kPanel, &tmKh, &full[slot], blk * 128 + 64, c * kC, h, b);
+        }
+        ++issued;
+      }
+      // after a give-up: the loads of the last kStages issues land before exit (bounded)
+      if (*abort_flag) {
+        volatile int no_abort = 0;
+        for (int idx = issued - kStages; idx < issued; ++idx)
+          if (idx >= 0) tc::mbar_wait(&full[idx % kStages], (idx / kStages) & 1, &no_abort, 20000000ll);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ================= workers =================
+    // initial state -> TMEM (the caller's stabilized C0 / n0 scaled by e^m0), n -> smem
+    const float s0 = p.m0 ? __expf(p.m0[bh]) : 1.f;
+#pragma unroll 1
+    for (int blk = 0; blk < L::kNB; ++blk) {
+      const int srow = blk * 128 + row;
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const int col = e0 + c0 + j;
-        v[j] = (p.C0 && col < p.dv) ? s0 * p.C0[((int64_t)bh * DK + row) * p.dv + col] : 0.f;
+        const int col = e0 + ch + j;
+        v[j] = (p.C0 && col < p.dv) ? s0 * p.C0[((int64_t)bh * DK + srow) * p.dv + col] : 0.f;
       }
-      tc::tmem_st32(tc::taddr(tm, warp * 32, L::tAcc + blk * 64 + c0), v);
+      tc::tmem_st32(tm + L::tAcc + blk * 64 + ch, v);
     }
-    float v[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = 0.f;
-    if (p.n0) v[0] = s0 * p.n0[(int64_t)bh * DK + row];
-    tc::tmem_st16(tc::taddr(tm, warp * 32, L::tN + blk * 16), v);
-  }
-  tc::tmem_wait_st();
+    for (int j = tid; j < DK; j += 32 * kWorkers) nst[j] = p.n0 ? s0 * p.n0[(int64_t)bh * DK + j] : 0.f;
+    tc::tmem_wait_st();
+    stream_workers_sync();
 
-  // state (TMEM) -> rho_e(c)-scaled bf16 snapshot (smem) and rho_e . n (smem fp32)
-  auto snapshot = [&](int c) {
-    const float* re = rho_e + ((int64_t)bh * nch + c) * DK;
+    // Entering chunk c (after the update of chunk c-1): the bf16 snapshot
+    // rho_e(c) . state for Qs Snap, the state decayed in place by decay(c) (one
+    // TMEM pass), ns = rho_e(c) . n and n = decay(c) . n + (Kh^T 1 of chunk c).
+    auto snapshot = [&](int c) {
+      const int64_t vo = ((int64_t)bh * nch + c) * DK;
 #pragma unroll 1
-    for (int blk = 0; blk < L::kNB; ++blk) {
-      const int row = blk * 128 + warp * 32 + lane;
-      const float r = re[row];
-#pragma unroll 1
-      for (int c0 = 0; c0 < kDV; c0 += 32) {
+      for (int blk = 0; blk < L::kNB; ++blk) {
+        const int srow = blk * 128 + row;
+        const float re = rho_e[vo + srow], dc = decay[vo + srow];
         float v[32];
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, L::tAcc + blk * 64 + c0), v);
+        const uint32_t a = tm + L::tAcc + blk * 64 + ch;
+        tc::tmem_ld32(a, v);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 w;
-          w.x = pack2<__nv_bfloat16>(r * v[8 * q + 0], r * v[8 * q + 1]);
-          w.y = pack2<__nv_bfloat16>(r * v[8 * q + 2], r * v[8 * q + 3]);
-          w.z = pack2<__nv_bfloat16>(r * v[8 * q + 4], r * v[8 * q + 5]);
-          w.w = pack2<__nv_bfloat16>(r * v[8 * q + 6], r * v[8 * q + 7]);
-          *reinterpret_cast<uint4*>(sm + L::kSnap + tc::sw128_offset(row, c0 + 8 * q)) = w;
+          w.x = pack2<__nv_bfloat16>(re * v[8 * q + 0], re * v[8 * q + 1]);
+          w.y = pack2<__nv_bfloat16>(re * v[8 * q + 2], re * v[8 * q + 3]);
+          w.z = pack2<__nv_bfloat16>(re * v[8 * q + 4], re * v[8 * q + 5]);
+          w.w = pack2<__nv_bfloat16>(re * v[8 * q + 6], re * v[8 * q + 7]);
+          *reinterpret_cast<uint4*>(sm + L::kSnap + tc::sw128_offset(srow, ch + 8 * q)) = w;
         }
-      }
-      float v[16];
-      tc::tmem_ld16(tc::taddr(tm, warp * 32, L::tN + blk * 16), v);
-      tc::tmem_wait_ld();
-      ns[row] = r * v[0];
-    }
-  };
-
-  // producer state (thread 0): a global sequence of 32 KB stage loads
-  //   per chunk: kNP panel loads (Qs_p + Ks_p) then kNB pair loads (Kh rows 128 blk ..)
-  constexpr int kLoadsPerChunk = L::kNP + L::kNB;
-  const int total_loads = nch * kLoadsPerChunk;
-  int next_load = 0;
-  auto issue_stage = [&](int idx) {
-    const int slot = idx % kStages;
-    const int c = idx / kLoadsPerChunk, r = idx % kLoadsPerChunk;
-    unsigned char* dst = sm + L::kRing + slot * 2 * kPanel;
-    tc::mbar_expect_tx(&full[slot], 2 * kPanel);
-    const int t0 = c * kC;
-    if (r < L::kNP) {
-      tc::tma_load_4d(dst, &tmQs, &full[slot], r * 64, t0, h, b);
-      tc::tma_load_4d(dst + kPanel, &tmKs, &full[slot], r * 64, t0, h, b);
-    } else {
-      const int blk = r - L::kNP;
-      tc::tma_load_4d(dst, &tmKh, &full[slot], blk * 128, t0, h, b);
-      tc::tma_load_4d(dst + kPanel, &tmKh, &full[slot], blk * 128 + 64, t0, h, b);
-    }
-  };
-  // stage reuse: load idx >= kStages needs the consumers of load idx - kStages done
-  auto produce_until = [&](int upto, bool& ok) {
-    while (next_load < total_loads && next_load < upto) {
-      if (next_load >= kStages) {
-        const int prev = next_load - kStages;
-        if (!tc::mbar_wait(&empty[prev % kStages], (prev / kStages) & 1, abort_flag)) { ok = false; return; }
-      }
-      issue_stage(next_load);
-      ++next_load;
-    }
-  };
-
-  snapshot(0);
-  tc::fence_async_smem();
-  tc::tc_fence_before();
-  __syncthreads();
-
-  constexpr uint32_t idS = tc::idesc_bf16(128, 128, false, false);
-  constexpr uint32_t idH = tc::idesc_bf16(128, kDV, false, true);
-  constexpr uint32_t idAcc = tc::idesc_bf16(128, kDV, true, true);
-  constexpr uint32_t idN = tc::idesc_bf16(128, 16, true, false);
-
-  bool okp = true;
-  if (tid == 0) {
-    tc::mbar_expect_tx(bar_v, kPanel);
-    tc::tma_load_4d(sm + L::kV, &tmV, bar_v, e0, 0, h, b);
-    produce_until(kStages, okp);
-  }
-  int bad = okp ? 0 : 1;
-  int cons = 0;  // stage loads consumed so far (same sequence on every thread)
-#pragma unroll 1
-  for (int c = 0; c < nch; ++c) {
-    const int t0 = c * kC;
-    const int tg = t0 + tid;
-    // ---- pass A: S = Qs Ks^T, H = Qs Snap, qn on CUDA cores ------------------------
-    float qn = 0.f;
-#pragma unroll 1
-    for (int pnl = 0; pnl < L::kNP; ++pnl, ++cons) {
-      const int slot = cons % kStages;
-      if (!tc::mbar_wait(&full[slot], (cons / kStages) & 1, abort_flag)) bad = 1;
-      const uint32_t qaddr = sbase + L::kRing + slot * 2 * kPanel;
-      if (tid == 0 && !bad) {
-        tc::tc_fence_after();
-        const uint64_t dq = tc::sdesc_sw128(qaddr, 16, 1024);
-        const uint64_t dsn = tc::sdesc_sw128(sbase + L::kSnap + pnl * 4 * 2048, kPanel, 1024);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = tc::desc_add(dq, kk * 32);
-          tc::mma_bf16(tm + L::tS, ad, tc::desc_add(dq, kPanel + kk * 32), idS, pnl > 0 || kk > 0);
-          tc::mma_bf16(tm + L::tH, ad, tc::desc_add(dsn, kk * 2048), idH, pnl > 0 || kk > 0);
+        for (int j = 0; j < 32; j += 2) {
+          const float2 d2 = __fmul2_rn(make_float2(v[j], v[j + 1]), make_float2(dc, dc));
+          v[j] = d2.x;
+          v[j + 1] = d2.y;
         }
-        tc::mma_commit(&empty[slot]);
+        tc::tmem_st32(a, v);
       }
-      // qn_t += sum_{j in panel} Qs[t, j] * ns[j]
-      {
-        const unsigned char* qrow = sm + L::kRing + slot * 2 * kPanel;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const uint4 w = *reinterpret_cast<const uint4*>(qrow + tc::sw128_offset(tid, ch * 8));
-          const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(x2[e]);
-            qn = fmaf(f.x, ns[pnl * 64 + ch * 8 + 2 * e], qn);
-            qn = fmaf(f.y, ns[pnl * 64 + ch * 8 + 2 * e + 1], qn);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&empty[slot]);
-      if (tid == 0 && !bad) {
-        bool ok = true;
-        produce_until(cons + kStages + 1, ok);
-        if (!ok) bad = 1;
-      }
-    }
-    if (tid == 0 && !bad) tc::mma_commit(bar_s);
-    if (!tc::mbar_wait(bar_v, c & 1, abort_flag)) bad = 1;
-    if (!tc::mbar_wait(bar_s, c & 1, abort_flag)) bad = 1;
-    tc::tc_fence_after();
-    if (__syncthreads_or(bad)) { bad = 1; break; }
-    // ---- P = causal(S) -> smem, den_intra ------------------------------------------
-    float den_intra = 0.f;
-#pragma unroll 1
-    for (int s0 = 0; s0 < kC; s0 += 32) {
-      float v[32];
-      tc::tmem_ld32(tc::taddr(tm, warp * 32, L::tS + s0), v);
-      tc::tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        v[j] = (s0 + j <= tid) ? v[j] : 0.f;
-        den_intra += v[j];
-      }
-      unsigned char* prow = sm + L::kP + (s0 / 64) * kPanel;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 w;
-        w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
-        w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
-        w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
-        w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
-        *reinterpret_cast<uint4*>(prow + tc::sw128_offset(tid, (s0 % 64) + 8 * q)) = w;
-      }
-    }
-    // ---- state and n *= decay(c) (per key row = TMEM lane) ---------------------------
-    {
-      const float* dc = decay + ((int64_t)bh * nch + c) * DK;
-#pragma unroll 1
-      for (int blk = 0; blk < L::kNB; ++blk) {
-        const float dr = dc[blk * 128 + warp * 32 + lane];
-#pragma unroll 1
-        for (int c0 = 0; c0 < kDV; c0 += 32) {
-          float v[32];
-          const uint32_t a = tc::taddr(tm, warp * 32, L::tAcc + blk * 64 + c0);
-          tc::tmem_ld32(a, v);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= dr;
-          tc::tmem_st32(a, v);
-        }
-        float v[16];  // n blocks are 16 columns apart: touch exactly 16
-        const uint32_t a = tc::taddr(tm, warp * 32, L::tN + blk * 16);
-        tc::tmem_ld16(a, v);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] *= dr;
-        tc::tmem_st16(a, v);
+      for (int j = tid; j < DK; j += 32 * kWorkers) {
+        const float n = nst[j];
+        ns[j] = rho_e[vo + j] * n;
+        nst[j] = decay[vo + j] * n + nadd[vo + j];
       }
       tc::tmem_wait_st();
-    }
-    tc::fence_async_smem();
-    tc::tc_fence_before();
-    if (__syncthreads_or(bad)) { bad = 1; break; }
-    // ---- H += P V;  pass B: state += Kh^T V, n += Kh^T 1 ------------------------------------
-    if (tid == 0) {
-      tc::tc_fence_after();
-      const uint64_t dp = tc::sdesc_sw128(sbase + L::kP, 16, 1024);
-      const uint64_t dv = tc::sdesc_sw128(sbase + L::kV, kPanel, 1024);
-#pragma unroll
-      for (int ks = 0; ks < kC / 16; ++ks)
-        tc::mma_bf16(tm + L::tH, tc::desc_add(dp, (ks / 4) * kPanel + (ks % 4) * 32), tc::desc_add(dv, ks * 2048),
-                     idH, true);
-      tc::mma_commit(bar_h);
-    }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+    };
+    snapshot(0);
+    stream_workers_sync();  // ns of chunk 0 written
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(bar_snap);
+
+    int bad = 0;
 #pragma unroll 1
-    for (int blk = 0; blk < L::kNB; ++blk, ++cons) {
-      const int slot = cons % kStages;
-      if (!tc::mbar_wait(&full[slot], (cons / kStages) & 1, abort_flag)) bad = 1;
-      const uint32_t kaddr = sbase + L::kRing + slot * 2 * kPanel;
-      if (tid == 0 && !bad) {
-        tc::tc_fence_after();
-        const uint64_t dk = tc::sdesc_sw128(kaddr, kPanel, 1024);
-        const uint64_t dv = tc::sdesc_sw128(sbase + L::kV, kPanel, 1024);
-        const uint64_t d1 = tc::sdesc_sw128(sbase + L::kOnes, 16, 1024);
+    for (int c = 0; c < nch; ++c) {
+      float* qnp = rowv + (c & 1) * 512;  // [2 half][128]
+      float* denp = qnp + 256;            // [2 half][128]
+      // ---- pass A: this half's panels' qn_t partial = Qs[t, panel] . ns[panel] ---------
+      float qn = 0.f;
+#pragma unroll 1
+      for (int pnl = 0; pnl < L::kNP; ++pnl) {
+        const int idx = c * L::kLPC + pnl, slot = idx % kStages;
+        if (!tc::mbar_wait(&full[slot], (idx / kStages) & 1, abort_flag)) bad = 1;
+        if ((pnl & 1) == hf) {
+          const unsigned char* qrow = sm + L::kRing + slot * 2 * kPanel;
+          const float4* n4 = reinterpret_cast<const float4*>(ns + pnl * 64);
+          float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int ks = 0; ks < kC / 16; ++ks) {
-          const uint64_t ad = tc::desc_add(dk, ks * 2048);
-          tc::mma_bf16(tm + L::tAcc + blk * 64, ad, tc::desc_add(dv, ks * 2048), idAcc, true);
-          tc::mma_bf16(tm + L::tN + blk * 16, ad, tc::desc_add(d1, (ks / 4) * 2048 + (ks % 4) * 32), idN, true);
+          for (int q = 0; q < 8; ++q) {
+            const uint4 w = *reinterpret_cast<const uint4*>(qrow + tc::sw128_offset(row, q * 8));
+            const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+            const float4 na = n4[2 * q], nb = n4[2 * q + 1];
+            acc = __ffma2_rn(__bfloat1622float2(x2[0]), make_float2(na.x, na.y), acc);
+            acc = __ffma2_rn(__bfloat1622float2(x2[1]), make_float2(na.z, na.w), acc);
+            acc = __ffma2_rn(__bfloat1622float2(x2[2]), make_float2(nb.x, nb.y), acc);
+            acc = __ffma2_rn(__bfloat1622float2(x2[3]), make_float2(nb.z, nb.w), acc);
+          }
+          qn += acc.x + acc.y;
         }
-        tc::mma_commit(&empty[slot]);
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[slot]);
       }
-      if (lane == 0) tc::mbar_arrive(&empty[slot]);
-      if (tid == 0 && !bad) {
-        bool ok = true;
-        produce_until(cons + kStages + 1, ok);
-        if (!ok) bad = 1;
-      }
-    }
-    if (tid == 0 && !bad) tc::mma_commit(bar_a);
-    if (!tc::mbar_wait(bar_h, c & 1, abort_flag)) bad = 1;
-    if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) bad = 1;
-    tc::tc_fence_after();
-    if (__syncthreads_or(bad)) { bad = 1; break; }
-    // next chunk's V (its MMAs are done)
-    if (tid == 0 && c + 1 < nch) {
-      tc::mbar_expect_tx(bar_v, kPanel);
-      tc::tma_load_4d(sm + L::kV, &tmV, bar_v, e0, t0 + kC, h, b);
-    }
-    // ---- epilogue: h_t = H / max(den, 1) ------------------------------------------------
-    {
-      const float inv = 1.f / fmaxf(qn + den_intra, 1.f);
-      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.h) + b * p.sh[0] + h * p.sh[1] + (int64_t)tg * p.th + e0;
+      qnp[hf * kC + row] = qn;
+      // ---- P = causal(S) -> smem (bf16), this half's 64 columns; rowsum partial --------
+      if (!tc::mbar_wait(bar_s, c & 1, abort_flag)) bad = 1;
+      tc::tc_fence_after();
+      {
+        float2 den2 = make_float2(0.f, 0.f);
+        unsigned char* pp = sm + L::kP + hf * kPanel;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kDV; c0 += 32) {
+        for (int sb = 0; sb < 2; ++sb) {
+          const int s0 = 64 * hf + 32 * sb;
+          if (s0 > wq * 32 + 31) continue;  // warp-uniform: right of the diagonal, stays zero
+          float v[32];
+          tc::tmem_ld32(tm + L::tS + s0, v);
+          tc::tmem_wait_ld();
+          const bool diag = s0 == wq * 32;  // column s0 + j causal for this row iff j <= lane
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float2 pv = make_float2(v[j], v[j + 1]);
+            if (diag) {
+              if (j > lane) pv.x = 0.f;
+              if (j + 1 > lane) pv.y = 0.f;
+            }
+            v[j] = pv.x;
+            v[j + 1] = pv.y;
+            den2 = __fadd2_rn(den2, pv);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
+            w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
+            w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
+            w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
+            *reinterpret_cast<uint4*>(pp + tc::sw128_offset(row, 32 * sb + 8 * q)) = w;
+          }
+        }
+        denp[hf * kC + row] = den2.x + den2.y;
+      }
+      tc::fence_async_smem();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(bar_pready);
+      // ---- pass B's ring loads (read by the tensor core only): release them ----------
+#pragma unroll 1
+      for (int blk = 0; blk < L::kNB; ++blk) {
+        const int idx = c * L::kLPC + L::kNP + blk, slot = idx % kStages;
+        if (!tc::mbar_wait(&full[slot], (idx / kStages) & 1, abort_flag)) bad = 1;
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&empty[slot]);
+      }
+      if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) bad = 1;
+      tc::tc_fence_after();
+      // every worker agrees to go on (the qn / rowsum partials are visible)
+      if (stream_workers_sync_or(bad)) { bad = 1; break; }
+      // ---- the next chunk's snapshot; its Qs . Snap may start while this chunk's
+      //      outputs leave from the other H buffer ---------------------------------------
+      if (c + 1 < nch) {
+        snapshot(c + 1);
+        stream_workers_sync();  // ns of chunk c + 1 written
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar_snap);
+      }
+      // ---- epilogue: h_t = H / max(qn + rowsum, 1), this half's 32 columns -----------
+      {
+        const int tg = c * kC + row;
+        const float inv = 1.f / fmaxf(qnp[row] + qnp[kC + row] + denp[row] + denp[kC + row], 1.f);
         float v[32];
-        tc::tmem_ld32(tc::taddr(tm, warp * 32, L::tH + c0), v);
+        tc::tmem_ld32(tm + L::tH + (c & 1) * kDV + ch, v);
         tc::tmem_wait_ld();
-        if (tg < p.seqlen && e0 + c0 < p.dv) {
+        if (tg < p.seqlen && e0 + ch < p.dv) {
+          __nv_bfloat16* orow =
+              static_cast<__nv_bfloat16*>(p.h) + b * p.sh[0] + h * p.sh[1] + (int64_t)tg * p.th + e0 + ch;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 w;
@@ -410,48 +456,41 @@ __global__ void __launch_bounds__(128, 1)
             w.y = pack2<__nv_bfloat16>(v[8 * q + 2] * inv, v[8 * q + 3] * inv);
             w.z = pack2<__nv_bfloat16>(v[8 * q + 4] * inv, v[8 * q + 5] * inv);
             w.w = pack2<__nv_bfloat16>(v[8 * q + 6] * inv, v[8 * q + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c0 + 8 * q) = w;
+            *reinterpret_cast<uint4*>(orow + 8 * q) = w;
           }
         }
+        tc::tc_fence_before();
       }
     }
-    if (c + 1 < nch) snapshot(c + 1);
-    tc::fence_async_smem();
-    tc::tc_fence_before();
-    __syncthreads();
   }
 
-  // ---- final state: true state = TMEM state (m = 0) ----------------------------------------
-  if (!bad) {
+  // ---- final state (none after a wait that gave up) ------------------------------------
+  tc::tc_fence_before();
+  __syncthreads();
+  const bool ok = *abort_flag == 0;
+  if (warp < kWorkers && ok) {
     tc::tc_fence_after();
 #pragma unroll 1
     for (int blk = 0; blk < L::kNB; ++blk) {
-      const int row = blk * 128 + warp * 32 + lane;
+      const int srow = blk * 128 + row;
       if (p.CT) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < kDV; c0 += 32) {
-          float v[32];
-          tc::tmem_ld32(tc::taddr(tm, warp * 32, L::tAcc + blk * 64 + c0), v);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (e0 + c0 + j < p.dv) p.CT[((int64_t)bh * DK + row) * p.dv + e0 + c0 + j] = v[j];
-        }
-      }
-      if (p.nT && blockIdx.x == 0) {
-        float v[16];
-        tc::tmem_ld16(tc::taddr(tm, warp * 32, L::tN + blk * 16), v);
+        float v[32];
+        tc::tmem_ld32(tm + L::tAcc + blk * 64 + ch, v);
         tc::tmem_wait_ld();
-        p.nT[(int64_t)bh * DK + row] = v[0];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (e0 + ch + j < p.dv) p.CT[((int64_t)bh * DK + srow) * p.dv + e0 + ch + j] = v[j];
       }
     }
+    if (p.nT && blockIdx.x == 0)
+      for (int j = tid; j < DK; j += 32 * kWorkers) p.nT[(int64_t)bh * DK + j] = nst[j];
     if (p.mT && blockIdx.x == 0 && tid == 0) p.mT[bh] = 0.f;
   }
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tm, 512);
+    tc::tmem_dealloc(tb, 512);
   }
 }
 
@@ -462,7 +501,7 @@ size_t stream_workspace(const Params& p) {
   const size_t nch = (p.seqlen + kC - 1) / kC;
   const size_t ops = (size_t)p.batch * p.heads * p.seqlen * p.dqk * 2;  // bf16 tensor
   const size_t vec = (size_t)p.batch * p.heads * nch * p.dqk * 4;
-  return 3 * align256(ops) + 2 * align256(vec);
+  return 3 * align256(ops) + 3 * align256(vec);
 }
 
 bool stream_shape_ok(const Params& p) {
@@ -491,8 +530,9 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   __nv_bfloat16* Kh = reinterpret_cast<__nv_bfloat16*>(ws + 2 * ops);
   float* decay = reinterpret_cast<float*>(ws + 3 * ops);
   float* rho_e = reinterpret_cast<float*>(ws + 3 * ops + vec);
+  float* nadd = reinterpret_cast<float*>(ws + 3 * ops + 2 * vec);
   dim3 pg(p.batch * p.heads * nch, (DK + 127) / 128);
-  mlstm_prescale_kernel<__nv_bfloat16><<<pg, 128, 0, st>>>(p, Qs, Ks, Kh, decay, rho_e);
+  mlstm_prescale_kernel<__nv_bfloat16><<<pg, 128, 0, st>>>(p, Qs, Ks, Kh, decay, rho_e, nadd);
   hxm_status s = check_launch("hxm_mlstm_chunkwise_fwd (prescale)");
   if (s != HXM_OK) return s;
   CUtensorMap mq, mk, mh, mv;
@@ -508,7 +548,7 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   auto kern = mlstm_stream_kernel<DK>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dv + kDV - 1) / kDV, p.heads, p.batch);
-  kern<<<grid, 128, smem, st>>>(mq, mk, mh, mv, p, decay, rho_e);
+  kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mh, mv, p, decay, rho_e, nadd);
   return check_launch("hxm_mlstm_chunkwise_fwd (stream)");
 }
 
