@@ -35,11 +35,11 @@ namespace mlstm {
 constexpr int kC = 128;
 constexpr int kDV = 64;
 constexpr int kPanel = 16384;
-constexpr int kStages = 3;
 
 // ---------------------------------------------------------------- pre-pass --
-// grid (B*H*nchunks, ceil(DK/128)), block 128: thread = key channel j.
-template <typename T>
+// grid (B*H*nchunks, ceil(DK/(128*NJ))), block 128: thread = NJ adjacent key
+// channels (NJ = 2: bf16x2 loads and stores, 128 bytes per warp access).
+template <typename T, int NJ>
 __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks,
                                                              __nv_bfloat16* Kh, float* decay, float* rho_e,
                                                              float* nadd) {
@@ -47,36 +47,67 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
   const int c = blockIdx.x % nch;
   const int bh = blockIdx.x / nch;
   const int b = bh / p.heads, h = bh % p.heads;
-  const int j = blockIdx.y * 128 + threadIdx.x;
-  if (j >= p.dqk) return;
+  const int j0 = (blockIdx.y * 128 + threadIdx.x) * NJ;
+  if (j0 >= p.dqk) return;
   const int t0 = c * kC, tn = min(kC, p.seqlen - t0);
   const T* q = static_cast<const T*>(p.q) + b * p.sq[0] + h * p.sq[1];
   const T* k = static_cast<const T*>(p.k) + b * p.sk[0] + h * p.sk[1];
   const float* li = p.log_i + b * p.si[0] + h * p.si[1];
   const float* lf = p.log_f + b * p.sf[0] + h * p.sf[1];
   const bool pc = p.gate_mode == 1;
-  const int gj = pc ? j : 0;
-  float g = 0.f;
-  for (int t = 0; t < tn; ++t) g += lf[(int64_t)(t0 + t) * p.tf + gj];
-  const float rho = 0.5f * g;
+  float g[NJ], bt[NJ], ksum[NJ];
+#pragma unroll
+  for (int u = 0; u < NJ; ++u) g[u] = bt[u] = ksum[u] = 0.f;
+#pragma unroll 4
+  for (int t = 0; t < tn; ++t) {
+#pragma unroll
+    for (int u = 0; u < NJ; ++u) g[u] += lf[(int64_t)(t0 + t) * p.tf + (pc ? j0 + u : 0)];
+  }
   const int64_t ob = (int64_t)bh * p.seqlen * p.dqk;
-  float bt = 0.f, ksum = 0.f;
+#pragma unroll 4
   for (int t = 0; t < tn; ++t) {
     const int64_t tt = t0 + t;
-    bt += lf[tt * p.tf + gj];
-    const float lit = li[tt * p.ti + gj];
-    const float qv = to_f32<T>(q[tt * p.tq + j]);
-    const float kv = to_f32<T>(k[tt * p.tk + j]);
-    const float kh = kv * __expf(g - bt + lit);
-    Qs[ob + tt * p.dqk + j] = __float2bfloat16_rn(qv * __expf(bt - rho));
-    Ks[ob + tt * p.dqk + j] = __float2bfloat16_rn(kv * __expf(rho - bt + lit));
-    Kh[ob + tt * p.dqk + j] = __float2bfloat16_rn(kh);
-    ksum += kh;
+    float qv[NJ], kv[NJ];
+    if (NJ == 2) {
+      const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(q + tt * p.tq + j0);
+      const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162*>(k + tt * p.tk + j0);
+      const float2 qf = __bfloat1622float2(q2), kf = __bfloat1622float2(k2);
+      qv[0] = qf.x; qv[NJ - 1] = qf.y;
+      kv[0] = kf.x; kv[NJ - 1] = kf.y;
+    } else {
+      qv[0] = to_f32<T>(q[tt * p.tq + j0]);
+      kv[0] = to_f32<T>(k[tt * p.tk + j0]);
+    }
+    float qs[NJ], ks[NJ], kh[NJ];
+#pragma unroll
+    for (int u = 0; u < NJ; ++u) {
+      const int gj = pc ? j0 + u : 0;
+      bt[u] += lf[tt * p.tf + gj];
+      const float lit = li[tt * p.ti + gj];
+      const float rho = 0.5f * g[u];
+      qs[u] = qv[u] * __expf(bt[u] - rho);
+      ks[u] = kv[u] * __expf(rho - bt[u] + lit);
+      kh[u] = kv[u] * __expf(g[u] - bt[u] + lit);
+      ksum[u] += kh[u];
+    }
+    const int64_t o = ob + tt * p.dqk + j0;
+    if (NJ == 2) {
+      *reinterpret_cast<uint32_t*>(Qs + o) = pack2<__nv_bfloat16>(qs[0], qs[NJ - 1]);
+      *reinterpret_cast<uint32_t*>(Ks + o) = pack2<__nv_bfloat16>(ks[0], ks[NJ - 1]);
+      *reinterpret_cast<uint32_t*>(Kh + o) = pack2<__nv_bfloat16>(kh[0], kh[NJ - 1]);
+    } else {
+      Qs[o] = __float2bfloat16_rn(qs[0]);
+      Ks[o] = __float2bfloat16_rn(ks[0]);
+      Kh[o] = __float2bfloat16_rn(kh[0]);
+    }
   }
-  const int64_t vi = ((int64_t)bh * nch + c) * p.dqk + j;
-  decay[vi] = __expf(g);
-  rho_e[vi] = __expf(rho);
-  nadd[vi] = ksum;  // the chunk's Kh^T 1: the normalizer's increment
+#pragma unroll
+  for (int u = 0; u < NJ; ++u) {
+    const int64_t vi = ((int64_t)bh * nch + c) * p.dqk + j0 + u;
+    decay[vi] = __expf(g[u]);
+    rho_e[vi] = __expf(0.5f * g[u]);
+    nadd[vi] = ksum[u];  // the chunk's Kh^T 1: the normalizer's increment
+  }
 }
 
 // ------------------------------------------------------------ stream kernel --
@@ -91,10 +122,15 @@ struct SL {
   static constexpr int kNP = DK / 64;                 // key panels
   static constexpr int kNB = DK / 128;                // state row blocks (TMEM 128 lanes)
   static constexpr int kLPC = kNP + kNB;              // ring loads per chunk
+  // P lives inside the snapshot buffer when that is large enough (the
+  // snapshot is consumed by the chunk's Qs.Snap MMAs before P is written, and
+  // rewritten only after P.V is done); the space saved is a fourth ring stage
+  static constexpr bool kPinSnap = DK >= 256;
+  static constexpr int kStages = kPinSnap ? 4 : 3;
   static constexpr int kRing = 0;                     // kStages x 32 KB
   static constexpr int kSnap = kRing + kStages * 2 * kPanel;  // DK rows x 128 B (MN-major B, one 64-wide N panel)
-  static constexpr int kP = kSnap + DK * 128;         // 2 panels
-  static constexpr int kV = kP + 2 * kPanel;          // 1 panel
+  static constexpr int kP = kPinSnap ? kSnap : kSnap + DK * 128;  // 2 panels
+  static constexpr int kV = kPinSnap ? kSnap + DK * 128 : kP + 2 * kPanel;  // 1 panel
   static constexpr int kN = kV + kPanel;              // float [DK]  n, the normalizer state
   static constexpr int kNs = kN + DK * 4;             // float [DK]  rho_e . n   (for qn)
   static constexpr int kRow = kNs + DK * 4;           // float [2 parity][2 (qn, rowsum)][2 half][128]
@@ -132,8 +168,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::kBar);
-  uint64_t* empty = full + kStages;
-  uint64_t* bar_v = empty + kStages;  // TMA: V of the chunk
+  uint64_t* empty = full + L::kStages;
+  uint64_t* bar_v = empty + L::kStages;  // TMA: V of the chunk
   uint64_t* bar_s = bar_v + 1;        // MMA: S and Qs.Snap of the chunk
   uint64_t* bar_pready = bar_v + 2;   // workers: P written
   uint64_t* bar_b = bar_v + 3;        // MMA: P.V and the state update
@@ -156,7 +192,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < L::kStages; ++i) {
       tc::mbar_init(&full[i], 1);
       tc::mbar_init(&empty[i], 1 + kWorkers);  // MMA commit + one arrive per worker warp
     }
@@ -169,7 +205,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     tc::fence_mbar_init();
     *abort_flag = 0;
   }
-  {  // P: blocks right of the diagonal are never written again
+  if (!L::kPinSnap) {  // P: blocks right of the diagonal are never written again
     uint4* zp = reinterpret_cast<uint4*>(sm + L::kP);
     for (int i = tid; i < 2 * kPanel / 16; i += kStreamThreads) zp[i] = make_uint4(0, 0, 0, 0);
   }
@@ -205,8 +241,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         bool ok = true;
 #pragma unroll 1
         for (int pnl = 0; pnl < L::kNP; ++pnl) {
-          const int idx = c * L::kLPC + pnl, slot = idx % kStages;
-          if (!tc::mbar_wait(&full[slot], (idx / kStages) & 1, abort_flag)) { ok = false; break; }
+          const int idx = c * L::kLPC + pnl, slot = idx % L::kStages;
+          if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) { ok = false; break; }
           tc::tc_fence_after();
           const uint64_t dq = tc::sdesc_sw128(sbase + L::kRing + slot * 2 * kPanel, 16, 1024);
           const uint64_t dsn = tc::desc_add(dSnap, pnl * 4 * 2048);
@@ -232,8 +268,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         // pass B: state += Kh^T V, block by block
 #pragma unroll 1
         for (int blk = 0; blk < L::kNB; ++blk) {
-          const int idx = c * L::kLPC + L::kNP + blk, slot = idx % kStages;
-          if (!tc::mbar_wait(&full[slot], (idx / kStages) & 1, abort_flag)) { ok = false; break; }
+          const int idx = c * L::kLPC + L::kNP + blk, slot = idx % L::kStages;
+          if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) { ok = false; break; }
           tc::tc_fence_after();
           const uint64_t dk = tc::sdesc_sw128(sbase + L::kRing + slot * 2 * kPanel, kPanel, 1024);
           const uint32_t tAcc = tb + L::tAcc + blk * 64;
@@ -261,8 +297,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       int issued = 0;
 #pragma unroll 1
       for (int idx = 0; idx < total_loads; ++idx) {
-        const int slot = idx % kStages;
-        if (idx >= kStages && !tc::mbar_wait(&empty[slot], ((idx / kStages) - 1) & 1, abort_flag)) break;
+        const int slot = idx % L::kStages;
+        if (idx >= L::kStages && !tc::mbar_wait(&empty[slot], ((idx / L::kStages) - 1) & 1, abort_flag)) break;
         const int c = idx / L::kLPC, r = idx % L::kLPC;
         unsigned char* dst = sm + L::kRing + slot * 2 * kPanel;
         tc::mbar_expect_tx(&full[slot], 2 * kPanel);
@@ -276,11 +312,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         }
         ++issued;
       }
-      // after a give-up: the loads of the last kStages issues land before exit (bounded)
+      // after a give-up: the last kStages loads issued land before exit (bounded)
       if (*abort_flag) {
         volatile int no_abort = 0;
-        for (int idx = issued - kStages; idx < issued; ++idx)
-          if (idx >= 0) tc::mbar_wait(&full[idx % kStages], (idx / kStages) & 1, &no_abort, 20000000ll);
+        for (int idx = issued - L::kStages; idx < issued; ++idx)
+          if (idx >= 0) tc::mbar_wait(&full[idx % L::kStages], (idx / L::kStages) & 1, &no_abort, 20000000ll);
       }
     }
     __syncwarp();
@@ -306,16 +342,33 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // Entering chunk c (after the update of chunk c-1): the bf16 snapshot
     // rho_e(c) . state for Qs Snap, the state decayed in place by decay(c) (one
     // TMEM pass), ns = rho_e(c) . n and n = decay(c) . n + (Kh^T 1 of chunk c).
-    auto snapshot = [&](int c) {
+    // This thread's per-chunk vectors: rho_e, decay of its state rows (one per
+    // block) and of its normalizer entries j = tid, tid + 256; loaded a chunk
+    // ahead of their use.
+    constexpr int kNJ = (DK + 32 * kWorkers - 1) / (32 * kWorkers);
+    struct ChunkVec {
+      float re[L::kNB], dc[L::kNB], nre[kNJ], ndc[kNJ], nad[kNJ];
+    };
+    auto load_vec = [&](int c, ChunkVec& cv) {
       const int64_t vo = ((int64_t)bh * nch + c) * DK;
-#pragma unroll 1
+#pragma unroll
       for (int blk = 0; blk < L::kNB; ++blk) {
+        cv.re[blk] = rho_e[vo + blk * 128 + row];
+        cv.dc[blk] = decay[vo + blk * 128 + row];
+      }
+#pragma unroll
+      for (int i = 0; i < kNJ; ++i) {
+        const int j = tid + i * 32 * kWorkers;
+        cv.nre[i] = j < DK ? rho_e[vo + j] : 0.f;
+        cv.ndc[i] = j < DK ? decay[vo + j] : 0.f;
+        cv.nad[i] = j < DK ? nadd[vo + j] : 0.f;
+      }
+    };
+    auto snapshot = [&](const ChunkVec& cv) {
+      // state blocks two at a time (both TMEM loads in flight before the wait)
+      auto block = [&](int blk, float (&v)[32]) {
         const int srow = blk * 128 + row;
-        const float re = rho_e[vo + srow], dc = decay[vo + srow];
-        float v[32];
-        const uint32_t a = tm + L::tAcc + blk * 64 + ch;
-        tc::tmem_ld32(a, v);
-        tc::tmem_wait_ld();
+        const float re = cv.re[blk], dc = cv.dc[blk];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 w;
@@ -331,22 +384,72 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           v[j] = d2.x;
           v[j + 1] = d2.y;
         }
-        tc::tmem_st32(a, v);
+        tc::tmem_st32(tm + L::tAcc + blk * 64 + ch, v);
+      };
+      if constexpr (L::kNB == 1) {
+        float v[32];
+        tc::tmem_ld32(tm + L::tAcc + ch, v);
+        tc::tmem_wait_ld();
+        block(0, v);
+      } else {
+#pragma unroll
+        for (int blk = 0; blk < L::kNB; blk += 2) {
+          float v0[32], v1[32];
+          tc::tmem_ld32(tm + L::tAcc + blk * 64 + ch, v0);
+          tc::tmem_ld32(tm + L::tAcc + (blk + 1) * 64 + ch, v1);
+          tc::tmem_wait_ld();
+          block(blk, v0);
+          block(blk + 1, v1);
+        }
       }
-      for (int j = tid; j < DK; j += 32 * kWorkers) {
-        const float n = nst[j];
-        ns[j] = rho_e[vo + j] * n;
-        nst[j] = decay[vo + j] * n + nadd[vo + j];
+#pragma unroll
+      for (int i = 0; i < kNJ; ++i) {
+        const int j = tid + i * 32 * kWorkers;
+        if (j < DK) {
+          const float n = nst[j];
+          ns[j] = cv.nre[i] * n;
+          nst[j] = cv.ndc[i] * n + cv.nad[i];
+        }
       }
       tc::tmem_wait_st();
       tc::fence_async_smem();
       tc::tc_fence_before();
     };
-    snapshot(0);
+    ChunkVec cvn;  // the next snapshot's vectors
+    load_vec(0, cvn);
+    snapshot(cvn);
+    if (nch > 1) load_vec(1, cvn);
     stream_workers_sync();  // ns of chunk 0 written
     __syncwarp();
     if (lane == 0) tc::mbar_arrive(bar_snap);
 
+    // Output rows of chunk c: h_t = H / max(qn + rowsum, 1), this half's 32
+    // columns, from H buffer c & 1 (the next chunk's Qs.Snap runs into the other).
+    auto epilogue = [&](int c) {
+      {
+        const int tg = c * kC + row;
+        const float* qnp = rowv + (c & 1) * 512;
+        const float* denp = qnp + 256;
+        const float inv = 1.f / fmaxf(qnp[row] + qnp[kC + row] + denp[row] + denp[kC + row], 1.f);
+        float v[32];
+        tc::tmem_ld32(tm + L::tH + (c & 1) * kDV + ch, v);
+        tc::tmem_wait_ld();
+        if (tg < p.seqlen && e0 + ch < p.dv) {
+          __nv_bfloat16* orow =
+              static_cast<__nv_bfloat16*>(p.h) + b * p.sh[0] + h * p.sh[1] + (int64_t)tg * p.th + e0 + ch;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack2<__nv_bfloat16>(v[8 * q + 0] * inv, v[8 * q + 1] * inv);
+            w.y = pack2<__nv_bfloat16>(v[8 * q + 2] * inv, v[8 * q + 3] * inv);
+            w.z = pack2<__nv_bfloat16>(v[8 * q + 4] * inv, v[8 * q + 5] * inv);
+            w.w = pack2<__nv_bfloat16>(v[8 * q + 6] * inv, v[8 * q + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + 8 * q) = w;
+          }
+        }
+        tc::tc_fence_before();
+      }
+    };
     int bad = 0;
 #pragma unroll 1
     for (int c = 0; c < nch; ++c) {
@@ -356,8 +459,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       float qn = 0.f;
 #pragma unroll 1
       for (int pnl = 0; pnl < L::kNP; ++pnl) {
-        const int idx = c * L::kLPC + pnl, slot = idx % kStages;
-        if (!tc::mbar_wait(&full[slot], (idx / kStages) & 1, abort_flag)) bad = 1;
+        const int idx = c * L::kLPC + pnl, slot = idx % L::kStages;
+        if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) bad = 1;
         if ((pnl & 1) == hf) {
           const unsigned char* qrow = sm + L::kRing + slot * 2 * kPanel;
           const float4* n4 = reinterpret_cast<const float4*>(ns + pnl * 64);
@@ -376,6 +479,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[slot]);
+        // the previous chunk's outputs leave while this chunk's later panels load
+        if (pnl == L::kNP / 2 - 1 && c > 0) epilogue(c - 1);
       }
       qnp[hf * kC + row] = qn;
       // ---- P = causal(S) -> smem (bf16), this half's 64 columns; rowsum partial --------
@@ -387,8 +492,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll 1
         for (int sb = 0; sb < 2; ++sb) {
           const int s0 = 64 * hf + 32 * sb;
-          if (s0 > wq * 32 + 31) continue;  // warp-uniform: right of the diagonal, stays zero
           float v[32];
+          if (s0 > wq * 32 + 31) {  // warp-uniform: right of the diagonal
+            if (!L::kPinSnap) continue;  // stays zero from the start
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(pp + tc::sw128_offset(row, 32 * sb + 8 * q)) = make_uint4(0, 0, 0, 0);
+            continue;
+          }
           tc::tmem_ld32(tm + L::tS + s0, v);
           tc::tmem_wait_ld();
           const bool diag = s0 == wq * 32;  // column s0 + j causal for this row iff j <= lane
@@ -422,8 +533,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       // ---- pass B's ring loads (read by the tensor core only): release them ----------
 #pragma unroll 1
       for (int blk = 0; blk < L::kNB; ++blk) {
-        const int idx = c * L::kLPC + L::kNP + blk, slot = idx % kStages;
-        if (!tc::mbar_wait(&full[slot], (idx / kStages) & 1, abort_flag)) bad = 1;
+        const int idx = c * L::kLPC + L::kNP + blk, slot = idx % L::kStages;
+        if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) bad = 1;
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[slot]);
       }
@@ -434,34 +545,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       // ---- the next chunk's snapshot; its Qs . Snap may start while this chunk's
       //      outputs leave from the other H buffer ---------------------------------------
       if (c + 1 < nch) {
-        snapshot(c + 1);
+        snapshot(cvn);
+        if (c + 2 < nch) load_vec(c + 2, cvn);
         stream_workers_sync();  // ns of chunk c + 1 written
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(bar_snap);
       }
-      // ---- epilogue: h_t = H / max(qn + rowsum, 1), this half's 32 columns -----------
-      {
-        const int tg = c * kC + row;
-        const float inv = 1.f / fmaxf(qnp[row] + qnp[kC + row] + denp[row] + denp[kC + row], 1.f);
-        float v[32];
-        tc::tmem_ld32(tm + L::tH + (c & 1) * kDV + ch, v);
-        tc::tmem_wait_ld();
-        if (tg < p.seqlen && e0 + ch < p.dv) {
-          __nv_bfloat16* orow =
-              static_cast<__nv_bfloat16*>(p.h) + b * p.sh[0] + h * p.sh[1] + (int64_t)tg * p.th + e0 + ch;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = pack2<__nv_bfloat16>(v[8 * q + 0] * inv, v[8 * q + 1] * inv);
-            w.y = pack2<__nv_bfloat16>(v[8 * q + 2] * inv, v[8 * q + 3] * inv);
-            w.z = pack2<__nv_bfloat16>(v[8 * q + 4] * inv, v[8 * q + 5] * inv);
-            w.w = pack2<__nv_bfloat16>(v[8 * q + 6] * inv, v[8 * q + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + 8 * q) = w;
-          }
-        }
-        tc::tc_fence_before();
-      }
     }
+    if (!bad) epilogue(nch - 1);
   }
 
   // ---- final state (none after a wait that gave up) ------------------------------------
@@ -531,8 +622,17 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   float* decay = reinterpret_cast<float*>(ws + 3 * ops);
   float* rho_e = reinterpret_cast<float*>(ws + 3 * ops + vec);
   float* nadd = reinterpret_cast<float*>(ws + 3 * ops + 2 * vec);
-  dim3 pg(p.batch * p.heads * nch, (DK + 127) / 128);
-  mlstm_prescale_kernel<__nv_bfloat16><<<pg, 128, 0, st>>>(p, Qs, Ks, Kh, decay, rho_e, nadd);
+  // two channels per thread when q, k rows allow 4-byte loads
+  const bool pair = p.tq % 2 == 0 && p.tk % 2 == 0 && p.sq[0] % 2 == 0 && p.sq[1] % 2 == 0 && p.sk[0] % 2 == 0 &&
+                    p.sk[1] % 2 == 0 && reinterpret_cast<uintptr_t>(p.q) % 4 == 0 &&
+                    reinterpret_cast<uintptr_t>(p.k) % 4 == 0;
+  if (pair) {
+    dim3 pg(p.batch * p.heads * nch, (DK + 255) / 256);
+    mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, Kh, decay, rho_e, nadd);
+  } else {
+    dim3 pg(p.batch * p.heads * nch, (DK + 127) / 128);
+    mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, Kh, decay, rho_e, nadd);
+  }
   hxm_status s = check_launch("hxm_mlstm_chunkwise_fwd (prescale)");
   if (s != HXM_OK) return s;
   CUtensorMap mq, mk, mh, mv;
