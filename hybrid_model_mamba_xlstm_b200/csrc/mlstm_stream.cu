@@ -39,29 +39,70 @@ constexpr int kPanel = 16384;
 // ---------------------------------------------------------------- pre-pass --
 // grid (B*H*nchunks, ceil(DK/(128*NJ))), block 128: thread = NJ adjacent key
 // channels (NJ = 2: bf16x2 loads and stores, 128 bytes per warp access).
+// Per-head gates: the factors e^(b_t - rho), e^(rho - b_t + log i_t) are the
+// same for every channel, so the block forms them once per step (thread t,
+// one scan over the chunk) and the channels only multiply; per-channel gates
+// take two exponentials per element.  Kh = Ks e^(g - rho) either way.
 template <typename T, int NJ>
 __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks,
                                                              __nv_bfloat16* Kh, float* decay, float* rho_e,
                                                              float* nadd) {
+  __shared__ float fq[kC], fk[kC], red[4];
   const int nch = (p.seqlen + kC - 1) / kC;
   const int c = blockIdx.x % nch;
   const int bh = blockIdx.x / nch;
   const int b = bh / p.heads, h = bh % p.heads;
-  const int j0 = (blockIdx.y * 128 + threadIdx.x) * NJ;
-  if (j0 >= p.dqk) return;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int j0 = (blockIdx.y * 128 + tid) * NJ;
+  const bool active = j0 < p.dqk;  // every thread takes part in the block scan below
   const int t0 = c * kC, tn = min(kC, p.seqlen - t0);
   const T* q = static_cast<const T*>(p.q) + b * p.sq[0] + h * p.sq[1];
   const T* k = static_cast<const T*>(p.k) + b * p.sk[0] + h * p.sk[1];
   const float* li = p.log_i + b * p.si[0] + h * p.si[1];
   const float* lf = p.log_f + b * p.sf[0] + h * p.sf[1];
-  const bool pc = p.gate_mode == 1;
-  float g[NJ], bt[NJ], ksum[NJ];
+  const bool pc = p.gate_mode == 1;  // uniform over the grid
+  float g[NJ];
+  if (!pc) {
+    // per-step factors of the chunk: thread t holds step t
+    const float lft = tid < tn ? lf[(int64_t)(t0 + tid) * p.tf] : 0.f;
+    const float lit = tid < tn ? li[(int64_t)(t0 + tid) * p.ti] : 0.f;
+    float bt = lft;
 #pragma unroll
-  for (int u = 0; u < NJ; ++u) g[u] = bt[u] = ksum[u] = 0.f;
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n = __shfl_up_sync(0xffffffffu, bt, o);
+      if (lane >= o) bt += n;
+    }
+    if (lane == 31) red[w] = bt;
+    __syncthreads();
+    float gs = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i < w) bt += red[i];
+      gs += red[i];
+    }
+    const float rho = 0.5f * gs;
+    fq[tid] = __expf(bt - rho);
+    fk[tid] = __expf(rho - bt + lit);
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < NJ; ++u) g[u] = gs;
+  } else {
+#pragma unroll
+    for (int u = 0; u < NJ; ++u) g[u] = 0.f;
+    if (active) {
 #pragma unroll 4
-  for (int t = 0; t < tn; ++t) {
+      for (int t = 0; t < tn; ++t) {
 #pragma unroll
-    for (int u = 0; u < NJ; ++u) g[u] += lf[(int64_t)(t0 + t) * p.tf + (pc ? j0 + u : 0)];
+        for (int u = 0; u < NJ; ++u) g[u] += lf[(int64_t)(t0 + t) * p.tf + j0 + u];
+      }
+    }
+  }
+  if (!active) return;  // no barrier below
+  float bt[NJ], ksum[NJ], eh[NJ];
+#pragma unroll
+  for (int u = 0; u < NJ; ++u) {
+    bt[u] = ksum[u] = 0.f;
+    eh[u] = __expf(0.5f * g[u]);  // Kh / Ks = e^(g - rho)
   }
   const int64_t ob = (int64_t)bh * p.seqlen * p.dqk;
 #pragma unroll 4
@@ -81,13 +122,19 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
     float qs[NJ], ks[NJ], kh[NJ];
 #pragma unroll
     for (int u = 0; u < NJ; ++u) {
-      const int gj = pc ? j0 + u : 0;
-      bt[u] += lf[tt * p.tf + gj];
-      const float lit = li[tt * p.ti + gj];
-      const float rho = 0.5f * g[u];
-      qs[u] = qv[u] * __expf(bt[u] - rho);
-      ks[u] = kv[u] * __expf(rho - bt[u] + lit);
-      kh[u] = kv[u] * __expf(g[u] - bt[u] + lit);
+      float a, e;
+      if (!pc) {
+        a = fq[t];
+        e = fk[t];
+      } else {
+        bt[u] += lf[tt * p.tf + j0 + u];
+        const float rho = 0.5f * g[u];
+        a = __expf(bt[u] - rho);
+        e = __expf(rho - bt[u] + li[tt * p.ti + j0 + u]);
+      }
+      qs[u] = qv[u] * a;
+      ks[u] = kv[u] * e;
+      kh[u] = ks[u] * eh[u];
       ksum[u] += kh[u];
     }
     const int64_t o = ob + tt * p.dqk + j0;
@@ -105,7 +152,7 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
   for (int u = 0; u < NJ; ++u) {
     const int64_t vi = ((int64_t)bh * nch + c) * p.dqk + j0 + u;
     decay[vi] = __expf(g[u]);
-    rho_e[vi] = __expf(0.5f * g[u]);
+    rho_e[vi] = eh[u];
     nadd[vi] = ksum[u];  // the chunk's Kh^T 1: the normalizer's increment
   }
 }
