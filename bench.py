@@ -249,16 +249,22 @@ def prefill_metric(args, dev, world, rank):
     g = torch.Generator(device=dev)
     g.manual_seed(99 + rank)
     out = {}
+    pieces = 4
     for kind, per in (("weak", gb), ("strong", max(1, gb // world))):
         ids = torch.randint(0, 50304, (per, seqlen), generator=g, device=dev)
         with torch.no_grad():
-            ms = _time_cuda(lambda: model(ids), 3, 2, dev, world)
+            pg = Lyr.PrefillGraph(model, per, seqlen, pieces=pieces, device=dev)
+            ms = _time_cuda(lambda: pg(ids), 3, 2, dev, world)
+            ms_eager = _time_cuda(lambda: model(ids), 2, 1, dev, world)
         out[kind] = {"metric": "hybrid-350M prefill tokens/s", "value": world * per * seqlen / ms * 1e3,
                      "unit": "tok/s", "ms_per_step": ms, "batch_per_rank": per, "global_batch": world * per,
                      "seqlen": seqlen, "params": nparam,
+                     "schedule": f"CUDA-graph wavefront: {pieces} sequence pieces x 24 layers, one stream per layer",
+                     "single_stream_forward_ms": ms_eager,
                      "scaling": "weak (batch 8 per rank)" if kind == "weak" else "strong (global batch 8 split over ranks)",
                      "parallelism": f"dp{world}"}
-        del ids
+        del ids, pg
+        torch.cuda.empty_cache()
     del model
     return out
 

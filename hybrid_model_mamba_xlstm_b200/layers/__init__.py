@@ -1,6 +1,6 @@
 """Layer callers of the hot path (mirror of hybrid_xmamba.layers / .models)."""
 from .blocks import HybridBlock, MambaBlock, RMSNorm, mLSTMBlock, sLSTMBlock
-from .model import GraphDecoder, HybridConfig, HybridLanguageModel, hybrid_350m_config
+from .model import GraphDecoder, HybridConfig, HybridLanguageModel, PrefillGraph, hybrid_350m_config
 
 __all__ = ["RMSNorm", "MambaBlock", "mLSTMBlock", "sLSTMBlock", "HybridBlock", "HybridConfig",
-           "HybridLanguageModel", "GraphDecoder", "hybrid_350m_config"]
+           "HybridLanguageModel", "GraphDecoder", "PrefillGraph", "hybrid_350m_config"]

@@ -139,6 +139,70 @@ class HybridLanguageModel(nn.Module):
         return self.lm_head(h)
 
     @torch.no_grad()
+    def prefill(self, input_ids, pieces=4, caches=None, return_hidden=False):
+        """Logits of :meth:`forward`, scheduled as a wavefront over layers and
+        sequence pieces: the sequence is cut into ``pieces`` consecutive pieces,
+        layer i runs on its own CUDA stream and takes piece k once layer i-1 has
+        finished piece k (its own piece k-1 is done by stream order, the
+        recurrent states carried in ``caches``).  The recurrences are exact
+        across pieces (the same continuation as :meth:`forward` with caches), so
+        the result is the whole-sequence forward; what changes is that layers
+        working on different pieces run concurrently — the sLSTM recurrence
+        occupies 8 SMs per head for thousands of sequential steps, and the other
+        layers' kernels fill the rest of the GPU meanwhile.  On CPU, or with one
+        piece, this is :meth:`forward`."""
+        L = input_ids.shape[1]
+        if caches is None:
+            caches = self.init_caches()
+        if not input_ids.is_cuda or pieces <= 1 or L < 2 * pieces:
+            return self.forward(input_ids, return_hidden=return_hidden, caches=caches)
+        dev = input_ids.device
+        step = -(-L // pieces)
+        step = -(-step // 128) * 128  # whole 128-step chunks per piece
+        bounds = [(a, min(a + step, L)) for a in range(0, L, step)]
+        main = torch.cuda.current_stream(dev)
+        nl = len(self.layers)
+        streams = [torch.cuda.Stream(dev) for _ in range(nl + 1)]
+        start = torch.cuda.Event()
+        start.record(main)
+        for s in streams:
+            s.wait_event(start)
+        outs = [None] * len(bounds)
+        for k, (a, b) in enumerate(bounds):
+            ev = None
+            with torch.cuda.stream(streams[0]):
+                h = self.embeddings.token_embedding(input_ids[:, a:b])
+            pending = None
+            for i, layer in enumerate(self.layers):
+                st = streams[i]
+                with torch.cuda.stream(st):
+                    if ev is not None:
+                        st.wait_event(ev)
+                    h, pending = layer.forward_pending(h, pending, cache=caches[i])
+                    ev = torch.cuda.Event()
+                    ev.record(st)
+                # the activations move on to the next layer's stream: the allocator
+                # must not hand their memory out again before that stream used them
+                nxt = streams[i + 1]
+                h.record_stream(nxt)
+                if pending is not None:
+                    pending.record_stream(nxt)
+            st = streams[nl]
+            with torch.cuda.stream(st):
+                st.wait_event(ev)
+                if pending is None:
+                    y = self.final_norm(h)
+                elif isinstance(self.final_norm, RMSNorm):
+                    y, _ = self.final_norm(pending, residual=h)
+                else:
+                    y = self.final_norm(h + pending)
+                outs[k] = y if return_hidden else self.lm_head(y)
+                outs[k].record_stream(main)
+        for s in streams:
+            main.wait_stream(s)
+        return torch.cat(outs, dim=1)
+
+    @torch.no_grad()
     def generate(self, input_ids, max_new_tokens=100, temperature=1.0, top_k=None, top_p=None, cuda_graph=True):
         """Autoregressive sampling with the reference's interface and sampling rule
         (hybrid_xmamba/models/hybrid_lm.py:211-267), but one prefill over the
@@ -173,6 +237,43 @@ class HybridLanguageModel(nn.Module):
             if i + 1 < max_new_tokens:
                 logits = step(nxt)[:, -1, :]
         return torch.cat(out, dim=1)
+
+
+class PrefillGraph:
+    """:meth:`HybridLanguageModel.prefill` of one (batch, seqlen) shape captured
+    once into a CUDA graph and replayed: the wavefront's thousands of kernel
+    launches across the per-layer streams cost no host time on replay, and the
+    graph keeps the event dependencies between layers and pieces, so the GPU
+    runs layers of different pieces concurrently.  ``__call__`` copies the
+    token ids into the graph's input buffer and returns the graph's logits
+    buffer (overwritten by the next call); :meth:`states` returns copies of
+    the recurrent states after the prompt, to continue the sequence with
+    :meth:`HybridLanguageModel.forward` (the graph's own state buffers must
+    stay in place for the next replay)."""
+
+    def __init__(self, model, batch, seqlen, pieces=4, device="cuda"):
+        self.model, self.pieces = model, pieces
+        dev = torch.device(device)
+        self.ids = torch.zeros(batch, seqlen, dtype=torch.long, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.no_grad():
+            model.prefill(self.ids, pieces=pieces)  # warm-up: parameter caches, workspaces, kernel setup
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.no_grad():
+            self.caches = model.init_caches()
+            self.logits = model.prefill(self.ids, pieces=pieces, caches=self.caches)
+
+    def __call__(self, input_ids):
+        self.ids.copy_(input_ids)
+        self.graph.replay()
+        return self.logits
+
+    def states(self):
+        """Per-layer caches (copies) holding the states after the last replay."""
+        return [{k: v.clone() for k, v in c.items()} for c in self.caches]
 
 
 class GraphDecoder:

@@ -53,6 +53,43 @@ def test_pieces_equal_full_prefill_fp32(L, split):
     assert rel_err(np64(torch.cat(parts, 1)), np64(full)) < 1e-4
 
 
+@pytest.mark.parametrize("pieces", [2, 3])
+def test_wavefront_prefill_equals_full_forward(L, pieces):
+    """HybridLanguageModel.prefill: layers on their own streams, the sequence in
+    pieces of whole 128-step chunks handed from layer to layer by events — the
+    logits of the single-stream whole-sequence forward (fp32 1e-4, bf16 with the
+    prefill's tensor-core paths 3e-2), and the carried states continue it."""
+    for dtype, kw, tol in ((torch.float32, {}, 1e-4),
+                           (torch.bfloat16, dict(recurrent=True, head_dim=128, dim=256, slstm_heads=2), 3e-2)):
+        model = _small(L, dtype, **kw)
+        ids = torch.randint(0, 97, (2, 400), device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+        with torch.no_grad():
+            full = model(ids)
+            caches = model.init_caches()
+            wave = model.prefill(ids[:, :384], pieces=pieces, caches=caches)
+            nxt = model(ids[:, 384:], caches=caches)
+        assert rel_err(np64(torch.cat([wave, nxt], 1)), np64(full)) < tol, (dtype, pieces)
+
+
+def test_prefill_graph_replays_the_wavefront(L):
+    """PrefillGraph: the captured wavefront prefill replayed on new token ids
+    gives the eager wavefront's logits (bitwise: same kernels, same inputs),
+    twice in a row, and its states continue the sequence."""
+    model = _small(L, torch.bfloat16, recurrent=True, head_dim=128, dim=256, slstm_heads=2)
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    with torch.no_grad():
+        pg = L.PrefillGraph(model, 2, 384, pieces=3)
+        for _ in range(2):
+            ids = torch.randint(0, 97, (2, 400), device="cuda", generator=gen)
+            got = pg(ids[:, :384]).clone()
+            caches = model.init_caches()
+            want = model.prefill(ids[:, :384], pieces=3, caches=caches)
+            assert torch.equal(got, want)
+            a = model(ids[:, 384:], caches=pg.states())
+            b = model(ids[:, 384:], caches=caches)
+            assert torch.equal(a, b)
+
+
 def test_pieces_equal_full_prefill_bf16_tensor_core_paths(L):
     """bf16 with the prefill's kernel paths: mLSTM heads of 128 with per-channel
     gates (key-streaming tcgen05 kernel), sLSTM heads of 128 with recurrent
