@@ -17,6 +17,7 @@ cases (default sizes):
   conv         B D L             (8 4096 2048)    causal depthwise conv1d(4) + SiLU
   mamba_layer  B L               (8 2048)         one hybrid-350M Mamba block
   prefill      B L               (8 2048)         the hybrid-350M model forward
+  prefill_graph B L PIECES       (8 2048 4)       the same prefill as a wavefront replayed from a CUDA graph
   decode       B P               (1 512)          hybrid-350M: prefill P tokens, then time one-token steps
                                                   (eager, and replayed from a CUDA graph)
 """
@@ -119,6 +120,16 @@ def main(argv=None):
             ids = torch.randint(0, model.config.vocab_size, (B, L), device=dev)
             fn = lambda: model(ids)  # noqa: E731
         extra = {"tokens": B * L}
+    elif a.case == "prefill_graph":
+        from . import layers as Lyr
+        B, L, pieces = (s + [8, 2048, 4][len(s):])[:3]
+        torch.manual_seed(0)
+        model = Lyr.HybridLanguageModel(Lyr.hybrid_350m_config()).to(dev).to(torch.bfloat16).eval()
+        ids = torch.randint(0, model.config.vocab_size, (B, L), device=dev)
+        with torch.no_grad():
+            pg = Lyr.PrefillGraph(model, B, L, pieces=pieces, device=dev)
+        fn = lambda: pg(ids)  # noqa: E731
+        extra = {"tokens": B * L, "pieces": pieces}
     elif a.case == "decode":
         from . import layers as Lyr
         B, P = (s + [1, 512][len(s):])[:2]
