@@ -7,19 +7,22 @@
 //     the chunk, g[j] = b_127[j] and the midpoint rho[j] = g[j] / 2:
 //        Qs[t,j] = q[t,j] e^(b_t - rho)              (|exponent| <= |g|/2)
 //        Ks[s,j] = k[s,j] e^(rho - b_s + log i_s)
-//        Kh[s,j] = k[s,j] e^(g - b_s + log i_s)
-//        decay[j] = e^g,  rho_e[j] = e^rho
+//        decay[j] = e^g,  rho_e[j] = e^rho,  nadd[j] = sum_s Ks[s,j] e^rho
 //     so that  sum_j q_t k_s e^(b_t - b_s + log i_s) = Qs_t . Ks_s  (intra-chunk)
-//     and      state' = diag(e^g) state + Kh^T v       (inter-chunk), the
-//     recurrence of tfla_forward_pytorch (tfla_interface.py:113-137) with
+//     and      state' = diag(e^g) state + diag(e^rho) Ks^T v   (inter-chunk),
+//     the recurrence of tfla_forward_pytorch (tfla_interface.py:113-137) with
 //     gates multiplying along the key dimension (mlstm_block.py:117-129).
 //  2. mlstm_stream_kernel (tcgen05): per (b, h, 64-wide value tile), per chunk
 //        S  = Qs Ks^T, H = Qs (rho_e . state) + causal(S) V     (TMEM)
 //        qn = Qs (rho_e . n) on CUDA cores,  den = qn + rowsum(causal S)
 //        h  = H / max(den, 1)
-//        state = decay . state + Kh^T V,  n = decay . n + Kh^T 1   (TMEM)
-//     Q/K panels (64 key channels) stream through a 3-stage TMA ring; the state
-//     (dqk x 64 fp32) and n live in TMEM.  No overflow as long as the total
+//        state = decay . state + rho_e . Ks^T V,  n = decay . n + nadd
+//     TMEM keeps the state divided by the current chunk's rho_e per key row,
+//     so the update adds plain Ks^T V from the same Ks panels as S, and the
+//     per-row factors rho_e(c-1), rho_e(c) (snapshot and decay at once) are
+//     applied when the state is read back for the next chunk.  Two 64-channel
+//     key panels (Qs and Ks of each) per 64 KB slot stream through a 2-slot
+//     TMA ring; n lives in shared memory.  No overflow as long as the total
 //     log forget gate of one 128-step chunk stays above about -160 per channel
 //     (exponents are bounded by half of it); the reference itself overflows
 //     for input-gate pre-activations above ~88 and so does this kernel.
@@ -42,11 +45,10 @@ constexpr int kPanel = 16384;
 // Per-head gates: the factors e^(b_t - rho), e^(rho - b_t + log i_t) are the
 // same for every channel, so the block forms them once per step (thread t,
 // one scan over the chunk) and the channels only multiply; per-channel gates
-// take two exponentials per element.  Kh = Ks e^(g - rho) either way.
+// take two exponentials per element.
 template <typename T, int NJ>
 __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks,
-                                                             __nv_bfloat16* Kh, float* decay, float* rho_e,
-                                                             float* nadd) {
+                                                             float* decay, float* rho_e, float* nadd) {
   __shared__ float fq[kC], fk[kC], red[4];
   const int nch = (p.seqlen + kC - 1) / kC;
   const int c = blockIdx.x % nch;
@@ -102,7 +104,7 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
 #pragma unroll
   for (int u = 0; u < NJ; ++u) {
     bt[u] = ksum[u] = 0.f;
-    eh[u] = __expf(0.5f * g[u]);  // Kh / Ks = e^(g - rho)
+    eh[u] = __expf(0.5f * g[u]);  // e^rho
   }
   const int64_t ob = (int64_t)bh * p.seqlen * p.dqk;
 #pragma unroll 4
@@ -141,11 +143,9 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
     if (NJ == 2) {
       *reinterpret_cast<uint32_t*>(Qs + o) = pack2<__nv_bfloat16>(qs[0], qs[NJ - 1]);
       *reinterpret_cast<uint32_t*>(Ks + o) = pack2<__nv_bfloat16>(ks[0], ks[NJ - 1]);
-      *reinterpret_cast<uint32_t*>(Kh + o) = pack2<__nv_bfloat16>(kh[0], kh[NJ - 1]);
     } else {
       Qs[o] = __float2bfloat16_rn(qs[0]);
       Ks[o] = __float2bfloat16_rn(ks[0]);
-      Kh[o] = __float2bfloat16_rn(kh[0]);
     }
   }
 #pragma unroll
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
     const int64_t vi = ((int64_t)bh * nch + c) * p.dqk + j0 + u;
     decay[vi] = __expf(g[u]);
     rho_e[vi] = eh[u];
-    nadd[vi] = ksum[u];  // the chunk's Kh^T 1: the normalizer's increment
+    nadd[vi] = ksum[u];  // e^rho Ks^T 1: the normalizer's increment
   }
 }
 
@@ -168,14 +168,18 @@ template <int DK>
 struct SL {
   static constexpr int kNP = DK / 64;                 // key panels
   static constexpr int kNB = DK / 128;                // state row blocks (TMEM 128 lanes)
-  static constexpr int kLPC = kNP + kNB;              // ring loads per chunk
+  // a ring slot holds the Qs and Ks panels of two consecutive 64-channel key
+  // panels, [Qs 2i | Ks 2i | Qs 2i+1 | Ks 2i+1]: the S and Qs.Snap MMAs of both
+  // and the state update of block i (its 128 key rows = the two Ks panels) read it
+  static constexpr int kLPC = (DK + 127) / 128;       // ring loads per chunk
+  static constexpr int kSlotB = 4 * kPanel;           // bytes per slot
   // P lives inside the snapshot buffer when that is large enough (the
   // snapshot is consumed by the chunk's Qs.Snap MMAs before P is written, and
-  // rewritten only after P.V is done); the space saved is a fourth ring stage
+  // rewritten only after P.V is done)
   static constexpr bool kPinSnap = DK >= 256;
-  static constexpr int kStages = kPinSnap ? 4 : 3;
-  static constexpr int kRing = 0;                     // kStages x 32 KB
-  static constexpr int kSnap = kRing + kStages * 2 * kPanel;  // DK rows x 128 B (MN-major B, one 64-wide N panel)
+  static constexpr int kStages = 2;
+  static constexpr int kRing = 0;                     // kStages x 64 KB
+  static constexpr int kSnap = kRing + kStages * kSlotB;  // DK rows x 128 B (MN-major B, one 64-wide N panel)
   static constexpr int kP = kPinSnap ? kSnap : kSnap + DK * 128;  // 2 panels
   static constexpr int kV = kPinSnap ? kSnap + DK * 128 : kP + 2 * kPanel;  // 1 panel
   static constexpr int kN = kV + kPanel;              // float [DK]  n, the normalizer state
@@ -208,7 +212,7 @@ HXM_DEV int stream_workers_sync_or(int v) {
 template <int DK>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     mlstm_stream_kernel(const __grid_constant__ CUtensorMap tmQs, const __grid_constant__ CUtensorMap tmKs,
-                        const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmV,
                         const Params p, const float* __restrict__ decay, const float* __restrict__ rho_e,
                         const float* __restrict__ nadd) {
   using L = SL<DK>;
@@ -284,42 +288,34 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         const uint32_t tH = tb + L::tH + (c & 1) * kDV;
         if (!tc::mbar_wait(bar_snap, c & 1, abort_flag)) break;
         tc::tc_fence_after();
-        // pass A: S = Qs Ks^T, H = Qs Snap (panel by panel from the ring)
-        bool ok = true;
-#pragma unroll 1
-        for (int pnl = 0; pnl < L::kNP; ++pnl) {
-          const int idx = c * L::kLPC + pnl, slot = idx % L::kStages;
-          if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) { ok = false; break; }
-          tc::tc_fence_after();
-          const uint64_t dq = tc::sdesc_sw128(sbase + L::kRing + slot * 2 * kPanel, 16, 1024);
-          const uint64_t dsn = tc::desc_add(dSnap, pnl * 4 * 2048);
-          const bool acc = pnl > 0;
-          tc::static_for<4>([&](auto KK) {
-            constexpr int kk = decltype(KK)::value;
-            tc::mma_bf16_at<kk * 32, kPanel + kk * 32>(tb + L::tS, dq, dq, idS, acc || kk > 0);
-            tc::mma_bf16_at<kk * 32, kk * 2048>(tH, dq, dsn, idH, acc || kk > 0);
-          });
-          tc::mma_commit(&empty[slot]);
-        }
-        if (!ok) break;
-        tc::mma_commit(bar_s);
-        // H += P V once P is written and V landed
+        // the state update below needs this chunk's V
         if (!tc::mbar_wait(bar_v, waited_v & 1, abort_flag)) break;
         ++waited_v;
-        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag)) break;
         tc::tc_fence_after();
-        tc::static_for<kC / 16>([&](auto KS) {
-          constexpr int ks = decltype(KS)::value;
-          tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tH, dP, dV, idH, true);
-        });
-        // pass B: state += Kh^T V, block by block
+        // S = Qs Ks^T, H = Qs Snap and state += Ks^T V, slot by slot from the ring
+        bool ok = true;
 #pragma unroll 1
-        for (int blk = 0; blk < L::kNB; ++blk) {
-          const int idx = c * L::kLPC + L::kNP + blk, slot = idx % L::kStages;
+        for (int i = 0; i < L::kLPC; ++i) {
+          const int idx = c * L::kLPC + i, slot = idx % L::kStages;
           if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) { ok = false; break; }
           tc::tc_fence_after();
-          const uint64_t dk = tc::sdesc_sw128(sbase + L::kRing + slot * 2 * kPanel, kPanel, 1024);
-          const uint32_t tAcc = tb + L::tAcc + blk * 64;
+          const uint32_t sb = sbase + L::kRing + slot * L::kSlotB;
+#pragma unroll
+          for (int pp = 0; pp < 2; ++pp) {
+            const int pnl = 2 * i + pp;
+            const uint64_t dq = tc::sdesc_sw128(sb + pp * 2 * kPanel, 16, 1024);
+            const uint64_t dsn = tc::desc_add(dSnap, pnl * 4 * 2048);
+            const bool acc = pnl > 0;
+            tc::static_for<4>([&](auto KK) {
+              constexpr int kk = decltype(KK)::value;
+              tc::mma_bf16_at<kk * 32, kPanel + kk * 32>(tb + L::tS, dq, dq, idS, acc || kk > 0);
+              tc::mma_bf16_at<kk * 32, kk * 2048>(tH, dq, dsn, idH, acc || kk > 0);
+            });
+          }
+          if (i + 1 == L::kLPC) tc::mma_commit(bar_s);
+          // block i: A = Ks^T (MN-major, the two Ks panels 2 panels apart)
+          const uint64_t dk = tc::sdesc_sw128(sb + kPanel, 2 * kPanel, 1024);
+          const uint32_t tAcc = tb + L::tAcc + i * 64;
           tc::static_for<kC / 16>([&](auto KS) {
             constexpr int ks = decltype(KS)::value;
             tc::mma_bf16_at<ks * 2048, ks * 2048>(tAcc, dk, dV, idAcc, true);
@@ -327,6 +323,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
           tc::mma_commit(&empty[slot]);
         }
         if (!ok) break;
+        // H += P V once P is written
+        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag)) break;
+        tc::tc_fence_after();
+        tc::static_for<kC / 16>([&](auto KS) {
+          constexpr int ks = decltype(KS)::value;
+          tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tH, dP, dV, idH, true);
+        });
         tc::mma_commit(bar_b);
         if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) break;
         if (c + 1 < nch) load_v(c + 1);  // V is free
@@ -346,16 +349,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       for (int idx = 0; idx < total_loads; ++idx) {
         const int slot = idx % L::kStages;
         if (idx >= L::kStages && !tc::mbar_wait(&empty[slot], ((idx / L::kStages) - 1) & 1, abort_flag)) break;
-        const int c = idx / L::kLPC, r = idx % L::kLPC;
-        unsigned char* dst = sm + L::kRing + slot * 2 * kPanel;
-        tc::mbar_expect_tx(&full[slot], 2 * kPanel);
-        if (r < L::kNP) {
-          tc::tma_load_4d(dst, &tmQs, &full[slot], r * 64, c * kC, h, b);
-          tc::tma_load_4d(dst + kPanel, &tmKs, &full[slot], r * 64, c * kC, h, b);
-        } else {
-          const int blk = r - L::kNP;
-          tc::tma_load_4d(dst, &tmKh, &full[slot], blk * 128, c * kC, h, b);
-          tc::tma_load_4d(dst + kPanel, &tmKh, &full[slot], blk * 128 + 64, c * kC, h, b);
+        const int c = idx / L::kLPC, i = idx % L::kLPC;
+        unsigned char* dst = sm + L::kRing + slot * L::kSlotB;
+        tc::mbar_expect_tx(&full[slot], L::kSlotB);
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+          const int pnl = 2 * i + pp;
+          tc::tma_load_4d(dst + pp * 2 * kPanel, &tmQs, &full[slot], pnl * 64, c * kC, h, b);
+          tc::tma_load_4d(dst + pp * 2 * kPanel + kPanel, &tmKs, &full[slot], pnl * 64, c * kC, h, b);
         }
         ++issued;
       }
@@ -388,20 +389,21 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 
     // Entering chunk c (after the update of chunk c-1): the bf16 snapshot
     // rho_e(c) . state for Qs Snap, the state decayed in place by decay(c) (one
-    // TMEM pass), ns = rho_e(c) . n and n = decay(c) . n + (Kh^T 1 of chunk c).
+    // TMEM pass), ns = rho_e(c) . n and n = decay(c) . n + nadd(c).
     // This thread's per-chunk vectors: rho_e, decay of its state rows (one per
     // block) and of its normalizer entries j = tid, tid + 256; loaded a chunk
     // ahead of their use.
     constexpr int kNJ = (DK + 32 * kWorkers - 1) / (32 * kWorkers);
+    // fp, fc: the per-row factors rho_e(c-1), rho_e(c) of the state pass below
     struct ChunkVec {
-      float re[L::kNB], dc[L::kNB], nre[kNJ], ndc[kNJ], nad[kNJ];
+      float fp[L::kNB], fc[L::kNB], nre[kNJ], ndc[kNJ], nad[kNJ];
     };
     auto load_vec = [&](int c, ChunkVec& cv) {
       const int64_t vo = ((int64_t)bh * nch + c) * DK;
 #pragma unroll
       for (int blk = 0; blk < L::kNB; ++blk) {
-        cv.re[blk] = rho_e[vo + blk * 128 + row];
-        cv.dc[blk] = decay[vo + blk * 128 + row];
+        cv.fc[blk] = rho_e[vo + blk * 128 + row];
+        cv.fp[blk] = c > 0 ? rho_e[vo - DK + blk * 128 + row] : 1.f;
       }
 #pragma unroll
       for (int i = 0; i < kNJ; ++i) {
@@ -411,25 +413,33 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         cv.nad[i] = j < DK ? nadd[vo + j] : 0.f;
       }
     };
+    // TMEM holds the state divided by the current chunk's e^(g/2) per key row
+    // (the update adds Ks^T V, rho_e^-1 of the true increment); entering chunk c, the
+    // factors rho_e(c-1) (back to the true state) then rho_e(c) per row both form the
+    // snapshot rho_e(c) . state and decay the stored state for chunk c.  Applied one
+    // after the other: their product alone falls below the fp32 normal range once the
+    // two chunks' log forget gates sum below about -175, while each partial result
+    // stays in range.
     auto snapshot = [&](const ChunkVec& cv) {
       // state blocks two at a time (both TMEM loads in flight before the wait)
       auto block = [&](int blk, float (&v)[32]) {
         const int srow = blk * 128 + row;
-        const float re = cv.re[blk], dc = cv.dc[blk];
+        const float fp = cv.fp[blk], fc = cv.fc[blk];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float2 t2 = __fmul2_rn(make_float2(v[j], v[j + 1]), make_float2(fp, fp));
+          const float2 d2 = __fmul2_rn(t2, make_float2(fc, fc));
+          v[j] = d2.x;
+          v[j + 1] = d2.y;
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint4 w;
-          w.x = pack2<__nv_bfloat16>(re * v[8 * q + 0], re * v[8 * q + 1]);
-          w.y = pack2<__nv_bfloat16>(re * v[8 * q + 2], re * v[8 * q + 3]);
-          w.z = pack2<__nv_bfloat16>(re * v[8 * q + 4], re * v[8 * q + 5]);
-          w.w = pack2<__nv_bfloat16>(re * v[8 * q + 6], re * v[8 * q + 7]);
+          w.x = pack2<__nv_bfloat16>(v[8 * q + 0], v[8 * q + 1]);
+          w.y = pack2<__nv_bfloat16>(v[8 * q + 2], v[8 * q + 3]);
+          w.z = pack2<__nv_bfloat16>(v[8 * q + 4], v[8 * q + 5]);
+          w.w = pack2<__nv_bfloat16>(v[8 * q + 6], v[8 * q + 7]);
           *reinterpret_cast<uint4*>(sm + L::kSnap + tc::sw128_offset(srow, ch + 8 * q)) = w;
-        }
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float2 d2 = __fmul2_rn(make_float2(v[j], v[j + 1]), make_float2(dc, dc));
-          v[j] = d2.x;
-          v[j + 1] = d2.y;
         }
         tc::tmem_st32(tm + L::tAcc + blk * 64 + ch, v);
       };
@@ -505,11 +515,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       // ---- pass A: this half's panels' qn_t partial = Qs[t, panel] . ns[panel] ---------
       float qn = 0.f;
 #pragma unroll 1
-      for (int pnl = 0; pnl < L::kNP; ++pnl) {
-        const int idx = c * L::kLPC + pnl, slot = idx % L::kStages;
+      for (int i = 0; i < L::kLPC; ++i) {
+        const int idx = c * L::kLPC + i, slot = idx % L::kStages;
         if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) bad = 1;
-        if ((pnl & 1) == hf) {
-          const unsigned char* qrow = sm + L::kRing + slot * 2 * kPanel;
+        {  // this half's panel of the slot: 2i + hf
+          const int pnl = 2 * i + hf;
+          const unsigned char* qrow = sm + L::kRing + slot * L::kSlotB + hf * 2 * kPanel;
           const float4* n4 = reinterpret_cast<const float4*>(ns + pnl * 64);
           float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
@@ -527,7 +538,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&empty[slot]);
         // the previous chunk's outputs leave while this chunk's later panels load
-        if (pnl == L::kNP / 2 - 1 && c > 0) epilogue(c - 1);
+        if (i == (L::kLPC + 1) / 2 - 1 && c > 0) epilogue(c - 1);
       }
       qnp[hf * kC + row] = qn;
       // ---- P = causal(S) -> smem (bf16), this half's 64 columns; rowsum partial --------
@@ -577,14 +588,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_pready);
-      // ---- pass B's ring loads (read by the tensor core only): release them ----------
-#pragma unroll 1
-      for (int blk = 0; blk < L::kNB; ++blk) {
-        const int idx = c * L::kLPC + L::kNP + blk, slot = idx % L::kStages;
-        if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) bad = 1;
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&empty[slot]);
-      }
       if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) bad = 1;
       tc::tc_fence_after();
       // every worker agrees to go on (the qn / rowsum partials are visible)
@@ -612,12 +615,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     for (int blk = 0; blk < L::kNB; ++blk) {
       const int srow = blk * 128 + row;
       if (p.CT) {
+        // the stored state times the last chunk's rho_e
+        const float rl = rho_e[((int64_t)bh * nch + nch - 1) * DK + srow];
         float v[32];
         tc::tmem_ld32(tm + L::tAcc + blk * 64 + ch, v);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (e0 + ch + j < p.dv) p.CT[((int64_t)bh * DK + srow) * p.dv + e0 + ch + j] = v[j];
+          if (e0 + ch + j < p.dv) p.CT[((int64_t)bh * DK + srow) * p.dv + e0 + ch + j] = rl * v[j];
       }
     }
     if (p.nT && blockIdx.x == 0)
@@ -639,7 +644,7 @@ size_t stream_workspace(const Params& p) {
   const size_t nch = (p.seqlen + kC - 1) / kC;
   const size_t ops = (size_t)p.batch * p.heads * p.seqlen * p.dqk * 2;  // bf16 tensor
   const size_t vec = (size_t)p.batch * p.heads * nch * p.dqk * 4;
-  return 3 * align256(ops) + 3 * align256(vec);
+  return 2 * align256(ops) + 3 * align256(vec);
 }
 
 bool stream_shape_ok(const Params& p) {
@@ -665,37 +670,35 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   unsigned char* ws = static_cast<unsigned char*>(p.workspace);
   __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(ws);
   __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(ws + ops);
-  __nv_bfloat16* Kh = reinterpret_cast<__nv_bfloat16*>(ws + 2 * ops);
-  float* decay = reinterpret_cast<float*>(ws + 3 * ops);
-  float* rho_e = reinterpret_cast<float*>(ws + 3 * ops + vec);
-  float* nadd = reinterpret_cast<float*>(ws + 3 * ops + 2 * vec);
+  float* decay = reinterpret_cast<float*>(ws + 2 * ops);
+  float* rho_e = reinterpret_cast<float*>(ws + 2 * ops + vec);
+  float* nadd = reinterpret_cast<float*>(ws + 2 * ops + 2 * vec);
   // two channels per thread when q, k rows allow 4-byte loads
   const bool pair = p.tq % 2 == 0 && p.tk % 2 == 0 && p.sq[0] % 2 == 0 && p.sq[1] % 2 == 0 && p.sk[0] % 2 == 0 &&
                     p.sk[1] % 2 == 0 && reinterpret_cast<uintptr_t>(p.q) % 4 == 0 &&
                     reinterpret_cast<uintptr_t>(p.k) % 4 == 0;
   if (pair) {
     dim3 pg(p.batch * p.heads * nch, (DK + 255) / 256);
-    mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, Kh, decay, rho_e, nadd);
+    mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd);
   } else {
     dim3 pg(p.batch * p.heads * nch, (DK + 127) / 128);
-    mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, Kh, decay, rho_e, nadd);
+    mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd);
   }
   hxm_status s = check_launch("hxm_mlstm_chunkwise_fwd (prescale)");
   if (s != HXM_OK) return s;
-  CUtensorMap mq, mk, mh, mv;
+  CUtensorMap mq, mk, mv;
   const uint64_t dd[4] = {(uint64_t)DK, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
   const uint64_t sd[3] = {(uint64_t)DK * 2, (uint64_t)p.seqlen * DK * 2, (uint64_t)p.heads * p.seqlen * DK * 2};
   const uint64_t dvd[4] = {(uint64_t)p.dv, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
   const uint64_t sv[3] = {(uint64_t)p.tv * 2, (uint64_t)p.sv[1] * 2, (uint64_t)p.sv[0] * 2};
   if ((s = make_map_bf16_4d(&mq, Qs, dd, sd, "mlstm Qs")) != HXM_OK) return s;
   if ((s = make_map_bf16_4d(&mk, Ks, dd, sd, "mlstm Ks")) != HXM_OK) return s;
-  if ((s = make_map_bf16_4d(&mh, Kh, dd, sd, "mlstm Kh")) != HXM_OK) return s;
   if ((s = make_map_bf16_4d(&mv, p.v, dvd, sv, "mlstm v")) != HXM_OK) return s;
   const size_t smem = L::kBytes + 1024;
   auto kern = mlstm_stream_kernel<DK>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dv + kDV - 1) / kDV, p.heads, p.batch);
-  kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mh, mv, p, decay, rho_e, nadd);
+  kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mv, p, decay, rho_e, nadd);
   return check_launch("hxm_mlstm_chunkwise_fwd (stream)");
 }
 

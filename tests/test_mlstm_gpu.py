@@ -176,6 +176,32 @@ def test_stream_kernel_channel_gates(ops, d):
     assert rel_err(np64(n) * em[..., None], nr) < TOL16
 
 
+@pytest.mark.parametrize("d", [128, 512])
+def test_stream_kernel_strong_channel_decay_segmented(ops, d):
+    """Per-channel forget gates near sigmoid(N(0, 1)) (mLSTMBlock at init): the
+    log forget gate of one 128-step chunk sums to about -100 per channel, so
+    the per-chunk factors e^(g/2) of two chunks multiply below the fp32 normal
+    range; the carried state must still reach the next chunk and the next call."""
+    g = torch.Generator().manual_seed(23)
+    b, h, L = 1, 2, 512
+    q = (torch.randn(b, h, L, d, generator=g) / d ** 0.5).to("cuda", torch.bfloat16)
+    k = torch.randn(b, h, L, d, generator=g).to("cuda", torch.bfloat16)
+    v = torch.randn(b, h, L, d, generator=g).to("cuda", torch.bfloat16)
+    li = (torch.randn(b, h, L, d, generator=g) * 0.5).cuda()
+    lf = torch.nn.functional.logsigmoid(torch.randn(b, h, L, d, generator=g)).cuda()
+    ref, Cr, nr = R.tfla_recurrent(np64(q), np64(k), np64(v), np.exp(np64(li)), np.exp(np64(lf)))
+    out, (C, n, m) = ops.mlstm_chunkwise_fwd(q, k, v, li, lf, return_state=True)
+    assert rel_err(np64(out), ref) < TOL16
+    em = np.exp(np64(m))
+    assert rel_err(np64(C) * em[..., None, None], Cr) < TOL16
+    assert rel_err(np64(n) * em[..., None], nr) < TOL16
+    s = 256
+    a, st = ops.mlstm_chunkwise_fwd(q[:, :, :s], k[:, :, :s], v[:, :, :s], li[:, :, :s], lf[:, :, :s],
+                                    return_state=True)
+    b2 = ops.mlstm_chunkwise_fwd(q[:, :, s:], k[:, :, s:], v[:, :, s:], li[:, :, s:], lf[:, :, s:], *st)
+    assert rel_err(np64(b2), ref[:, :, s:]) < TOL16
+
+
 def test_stream_kernel_scalar_gates_d512_segmented(ops):
     """Per-head gates with dqk = dv = 512 (the long-context configuration's head
     size) on the streaming kernel; state carried across a split."""
