@@ -143,6 +143,35 @@ class MlstmGatesArgs(ct.Structure):
     ]
 
 
+class MlstmBwdArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("heads", ct.c_int32), ("seqlen", ct.c_int32), ("dqk", ct.c_int32),
+        ("chunk", ct.c_int32), ("gate_mode", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("q", ct.c_void_p), ("q_stride", _i64x3),
+        ("k", ct.c_void_p), ("k_stride", _i64x3),
+        ("log_i", ct.c_void_p), ("i_stride", _i64x3),
+        ("log_f", ct.c_void_p), ("f_stride", _i64x3),
+        ("q_scaled", ct.c_void_p), ("k_scaled", ct.c_void_p),
+        ("rho", ct.c_void_p), ("e_rho", ct.c_void_p), ("e_g", ct.c_void_p),
+        ("dq_scaled", ct.c_void_p), ("dk_scaled", ct.c_void_p),
+        ("chunk_sum", ct.c_void_p),
+        ("dq", ct.c_void_p), ("dk", ct.c_void_p), ("dlog_i", ct.c_void_p), ("dlog_f", ct.c_void_p),
+        ("d_i", ct.c_void_p),
+    ]
+
+
+class ChunkScanArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("groups", ct.c_int64),
+        ("nchunks", ct.c_int32), ("rows", ct.c_int32), ("cols", ct.c_int32),
+        ("x", ct.c_void_p), ("decay", ct.c_void_p),
+        ("reverse", ct.c_int32),
+    ]
+
+
 # symbol -> (restype, argtypes)
 SYMBOLS = {
     "hxm_abi_version": (ct.c_int, []),
@@ -153,6 +182,9 @@ SYMBOLS = {
     "hxm_mlstm_workspace_size": (ct.c_size_t, [ct.POINTER(MlstmArgs)]),
     "hxm_mlstm_chunkwise_fwd": (ct.c_int, [ct.POINTER(MlstmArgs), ct.c_void_p]),
     "hxm_mlstm_chunkwise_fwd_noalloc": (ct.c_int, [ct.POINTER(MlstmArgs), ct.c_void_p]),
+    "hxm_mlstm_bwd_prepare": (ct.c_int, [ct.POINTER(MlstmBwdArgs), ct.c_void_p]),
+    "hxm_mlstm_bwd_finalize": (ct.c_int, [ct.POINTER(MlstmBwdArgs), ct.c_void_p]),
+    "hxm_chunk_state_scan": (ct.c_int, [ct.POINTER(ChunkScanArgs), ct.c_void_p]),
     "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),
     "hxm_ssd_chunk_scan_fwd": (ct.c_int, [ct.POINTER(SsdArgs), ct.c_void_p]),
     "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),

@@ -1,0 +1,243 @@
+// mlstm_bwd.cu — element-wise and scan kernels of the chunkwise mLSTM
+// backward (sm_100a).
+//
+// The reference's backward (TFLAFunction.backward,
+// hybrid_xmamba/kernels/tfla/tfla_interface.py:52-81) re-runs the step loop
+// tfla_forward_pytorch (:84-139) under autograd.  The chunkwise form used
+// here: for a chunk of c steps and key channel j, b_t = sum_{s<=t} log f_s
+// (inside the chunk), g = b_{c-1}, rho = g/2 and
+//     Qs_t = q_t e^(b_t - rho),   Ks_s = k_s e^(log i_s + rho - b_s)
+// so that q_t . (e^(b_t - b_s) i_s k_s) = Qs_t . Ks_s (intra-chunk) and the
+// state entering the next chunk is  e^g C + e^rho Ks^T [v | 1]  (the
+// normalizer n rides along as an extra column of ones).  The batched chunk
+// GEMMs (S = Qs Ks^T, its gradients, the chunk-state increments) run as
+// library GEMMs between these kernels:
+//   prepare   q, k, log gates -> Qs, Ks, rho, e^rho, e^g per chunk
+//   scan      exclusive chunk-level recurrences s' = diag(decay) s + x, run
+//             forward for the states entering each chunk and in reverse for
+//             the state adjoints leaving each chunk
+//   finalize  dL/dQs, dL/dKs -> dq = e^(b - rho) dL/dQs,
+//             dk = i e^(rho - b) dL/dKs, dlog_i = Ks . dL/dKs and
+//             dlog_f_t = sum_{s >= t} (Qs . dL/dQs - Ks . dL/dKs)_s
+// The last line is the gate identity of decayed linear recurrences: the loss
+// sees log f only through b, whose gradient at step t is
+// q_t dq_t - (i k)_t d(i k)_t, and log f_t enters every b_s with s >= t.
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace hxm {
+namespace mlstm_bwd {
+
+struct Params {
+  int batch, heads, seqlen, dqk, chunk, nch, gate_mode;
+  const void* q;
+  int64_t sq[3];
+  const void* k;
+  int64_t sk[3];
+  const float* log_i;
+  int64_t si[3];
+  const float* log_f;
+  int64_t sf[3];
+  float *qs, *ks, *rho, *erho, *eg;
+  const float *dqs, *dks;
+  float* csum;
+  float *dq, *dk, *dli, *dlf, *di;
+};
+
+// grid (batch*heads*nch, ceil(dqk/128)), block 128: thread = key channel j of one chunk
+template <typename T>
+__global__ void __launch_bounds__(128) prepare_kernel(const Params p) {
+  const int j = blockIdx.y * 128 + threadIdx.x;
+  if (j >= p.dqk) return;
+  const int kc = blockIdx.x % p.nch, bh = blockIdx.x / p.nch;
+  const int b = bh / p.heads, h = bh % p.heads;
+  const int t0 = kc * p.chunk, tn = min(p.chunk, p.seqlen - t0);
+  const int64_t jg = p.gate_mode ? j : 0;
+  const float* lf = p.log_f + b * p.sf[0] + h * p.sf[1] + jg;
+  const float* li = p.log_i + b * p.si[0] + h * p.si[1] + jg;
+  const T* q = static_cast<const T*>(p.q) + b * p.sq[0] + h * p.sq[1] + j;
+  const T* k = static_cast<const T*>(p.k) + b * p.sk[0] + h * p.sk[1] + j;
+  float g = 0.f;
+  for (int s = 0; s < tn; ++s) g += lf[(int64_t)(t0 + s) * p.sf[2]];
+  const float rho = 0.5f * g;
+  const int64_t vo = ((int64_t)bh * p.nch + kc) * p.dqk + j;
+  p.rho[vo] = rho;
+  p.erho[vo] = expf(rho);
+  p.eg[vo] = expf(g);
+  const int64_t ro = ((int64_t)bh * p.nch + kc) * p.chunk * p.dqk + j;
+  float bt = 0.f;
+  for (int s = 0; s < p.chunk; ++s) {
+    float qv = 0.f, kv = 0.f;
+    if (s < tn) {
+      const int64_t t = t0 + s;
+      bt += lf[t * p.sf[2]];
+      qv = to_f32<T>(q[t * p.sq[2]]) * expf(bt - rho);
+      kv = to_f32<T>(k[t * p.sk[2]]) * expf(li[t * p.si[2]] + rho - bt);
+    }
+    p.qs[ro + (int64_t)s * p.dqk] = qv;
+    p.ks[ro + (int64_t)s * p.dqk] = kv;
+  }
+}
+
+// grid (batch*heads*nch, ceil(dqk/128)), block 128: the chunk's steps in reverse,
+// b_t rebuilt from g = 2 rho; the within-chunk suffix sum of the gate identity
+// goes to dlog_f and the chunk total to csum.  di (optional): the gradient
+// with respect to the gate value i = e^(log_i), k . dL/d(i k), formed without
+// dividing by i.
+template <typename T>
+__global__ void __launch_bounds__(128) finalize_kernel(const Params p) {
+  const int j = blockIdx.y * 128 + threadIdx.x;
+  if (j >= p.dqk) return;
+  const int kc = blockIdx.x % p.nch, bh = blockIdx.x / p.nch;
+  const int b = bh / p.heads, h = bh % p.heads;
+  const int t0 = kc * p.chunk, tn = min(p.chunk, p.seqlen - t0);
+  const int64_t jg = p.gate_mode ? j : 0;
+  const float* lf = p.log_f + b * p.sf[0] + h * p.sf[1] + jg;
+  const float* li = p.log_i + b * p.si[0] + h * p.si[1] + jg;
+  const T* k = static_cast<const T*>(p.k) + b * p.sk[0] + h * p.sk[1] + j;
+  const int64_t vo = ((int64_t)bh * p.nch + kc) * p.dqk + j;
+  const float rho = p.rho[vo];
+  float bt = 2.f * rho;  // b at the chunk's last real step
+  const int64_t ro = ((int64_t)bh * p.nch + kc) * p.chunk * p.dqk + j;
+  const int64_t oo = ((int64_t)bh * p.seqlen + t0) * p.dqk + j;
+  float acc = 0.f;
+  for (int s = tn - 1; s >= 0; --s) {
+    const int64_t t = t0 + s;
+    const int64_t r = ro + (int64_t)s * p.dqk, o = oo + (int64_t)s * p.dqk;
+    const float P = p.dqs[r], R = p.dks[r], Qv = p.qs[r], Kv = p.ks[r];
+    p.dq[o] = expf(bt - rho) * P;
+    const float ek = expf(rho - bt) * R;  // dL/d(i k)
+    const float iv = expf(li[t * p.si[2]]);
+    p.dk[o] = iv * ek;
+    if (p.di) p.di[o] = to_f32<T>(k[t * p.sk[2]]) * ek;
+    p.dli[o] = Kv * R;
+    acc += Qv * P - Kv * R;
+    // f at the sequence's first step multiplies the zero initial state: its
+    // gradient is exactly zero (the identity's sum cancels to rounding there)
+    p.dlf[o] = t == 0 ? 0.f : acc;
+    bt -= lf[t * p.sf[2]];
+  }
+  p.csum[vo] = acc;
+}
+
+// dlog_f[b, h, t, j] += csum[b, h, t / chunk, j] (csum holds the suffix sums of later chunks)
+__global__ void __launch_bounds__(256) add_offsets_kernel(const Params p) {
+  const int64_t n = (int64_t)p.batch * p.heads * p.seqlen * p.dqk;
+  for (int64_t e = blockIdx.x * 256ll + threadIdx.x; e < n; e += (int64_t)gridDim.x * 256) {
+    const int j = (int)(e % p.dqk);
+    const int64_t bt = e / p.dqk;
+    const int t = (int)(bt % p.seqlen);
+    const int64_t bh = bt / p.seqlen;
+    if (t > 0) p.dlf[e] += p.csum[(bh * p.nch + t / p.chunk) * p.dqk + j];
+  }
+}
+
+// grid-stride over groups*rows*cols elements; each runs its chunks in order
+__global__ void __launch_bounds__(256) chunk_scan_kernel(float* x, const float* decay, int64_t groups, int nch,
+                                                         int rows, int cols, int reverse) {
+  const int64_t rc = (int64_t)rows * cols;
+  const int64_t n = groups * rc;
+  for (int64_t e = blockIdx.x * 256ll + threadIdx.x; e < n; e += (int64_t)gridDim.x * 256) {
+    const int64_t grp = e / rc, w = e % rc;
+    const int r = (int)(w / cols);
+    float* xp = x + grp * nch * rc + w;
+    const float* dp = decay ? decay + grp * nch * rows + r : nullptr;
+    float s = 0.f;
+#pragma unroll 4
+    for (int it = 0; it < nch; ++it) {
+      const int kc = reverse ? nch - 1 - it : it;
+      const float y = xp[kc * rc];
+      xp[kc * rc] = s;
+      s = (dp ? dp[(int64_t)kc * rows] : 1.f) * s + y;
+    }
+  }
+}
+
+static int grid_1d(int64_t n) {
+  const int64_t b = (n + 255) / 256;
+  return (int)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
+}
+
+static hxm_status fill(const hxm_mlstm_bwd_args* a, Params& p, const char* who) {
+  HXM_REQUIRE(a != nullptr, "%s: args is NULL", who);
+  HXM_REQUIRE(a->struct_size == sizeof(hxm_mlstm_bwd_args), "%s: struct_size %zu != %zu", who, a->struct_size,
+              sizeof(hxm_mlstm_bwd_args));
+  HXM_REQUIRE(a->batch >= 1 && a->heads >= 1 && a->seqlen >= 0 && a->dqk >= 1,
+              "%s: bad sizes batch=%d heads=%d seqlen=%d dqk=%d", who, a->batch, a->heads, a->seqlen, a->dqk);
+  HXM_REQUIRE(a->chunk >= 1 && a->chunk <= 1024, "%s: chunk must be in [1, 1024] (got %d)", who, a->chunk);
+  HXM_REQUIRE(a->gate_mode == 0 || a->gate_mode == 1, "%s: gate_mode must be 0 or 1", who);
+  HXM_REQUIRE(a->io_dtype == HXM_F32 || a->io_dtype == HXM_BF16, "%s: io_dtype must be f32 or bf16", who);
+  p.batch = a->batch; p.heads = a->heads; p.seqlen = a->seqlen; p.dqk = a->dqk; p.chunk = a->chunk;
+  p.nch = (a->seqlen + a->chunk - 1) / a->chunk;
+  p.gate_mode = a->gate_mode;
+  p.q = a->q; p.k = a->k; p.log_i = a->log_i; p.log_f = a->log_f;
+  for (int i = 0; i < 3; ++i) {
+    p.sq[i] = a->q_stride[i]; p.sk[i] = a->k_stride[i]; p.si[i] = a->i_stride[i]; p.sf[i] = a->f_stride[i];
+  }
+  p.qs = a->q_scaled; p.ks = a->k_scaled; p.rho = a->rho; p.erho = a->e_rho; p.eg = a->e_g;
+  p.dqs = a->dq_scaled; p.dks = a->dk_scaled; p.csum = a->chunk_sum;
+  p.dq = a->dq; p.dk = a->dk; p.dli = a->dlog_i; p.dlf = a->dlog_f; p.di = a->d_i;
+  HXM_REQUIRE(p.log_i && p.log_f && p.qs && p.ks && p.rho, "%s: NULL gate or chunk-operand pointer", who);
+  return HXM_OK;
+}
+
+}  // namespace mlstm_bwd
+}  // namespace hxm
+
+extern "C" hxm_status hxm_mlstm_bwd_prepare(const hxm_mlstm_bwd_args* a, void* stream) {
+  using namespace hxm;
+  clear_error();
+  mlstm_bwd::Params p{};
+  hxm_status s = mlstm_bwd::fill(a, p, "hxm_mlstm_bwd_prepare");
+  if (s != HXM_OK) return s;
+  HXM_REQUIRE(p.q && p.k && p.erho && p.eg, "hxm_mlstm_bwd_prepare: NULL q, k, e_rho or e_g");
+  if (p.nch == 0) return HXM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)(p.batch * p.heads * p.nch), (unsigned)((p.dqk + 127) / 128));
+  if (a->io_dtype == HXM_F32) mlstm_bwd::prepare_kernel<float><<<grid, 128, 0, st>>>(p);
+  else mlstm_bwd::prepare_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(p);
+  return check_launch("hxm_mlstm_bwd_prepare");
+}
+
+extern "C" hxm_status hxm_mlstm_bwd_finalize(const hxm_mlstm_bwd_args* a, void* stream) {
+  using namespace hxm;
+  clear_error();
+  mlstm_bwd::Params p{};
+  hxm_status s = mlstm_bwd::fill(a, p, "hxm_mlstm_bwd_finalize");
+  if (s != HXM_OK) return s;
+  HXM_REQUIRE(p.dqs && p.dks && p.csum && p.dq && p.dk && p.dli && p.dlf,
+              "hxm_mlstm_bwd_finalize: NULL gradient or chunk_sum pointer");
+  if (p.nch == 0) return HXM_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)(p.batch * p.heads * p.nch), (unsigned)((p.dqk + 127) / 128));
+  HXM_REQUIRE(p.k || !p.di, "hxm_mlstm_bwd_finalize: d_i needs k");
+  if (a->io_dtype == HXM_F32) mlstm_bwd::finalize_kernel<float><<<grid, 128, 0, st>>>(p);
+  else mlstm_bwd::finalize_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(p);
+  if ((s = check_launch("hxm_mlstm_bwd_finalize")) != HXM_OK) return s;
+  if (p.nch > 1) {
+    mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_1d((int64_t)p.batch * p.heads * p.dqk), 256, 0, st>>>(
+        p.csum, nullptr, (int64_t)p.batch * p.heads, p.nch, p.dqk, 1, 1);
+    if ((s = check_launch("hxm_mlstm_bwd_finalize (chunk sums)")) != HXM_OK) return s;
+    mlstm_bwd::add_offsets_kernel<<<mlstm_bwd::grid_1d((int64_t)p.batch * p.heads * p.seqlen * p.dqk), 256, 0,
+                                    st>>>(p);
+    return check_launch("hxm_mlstm_bwd_finalize (offsets)");
+  }
+  return HXM_OK;
+}
+
+extern "C" hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* a, void* stream) {
+  using namespace hxm;
+  clear_error();
+  HXM_REQUIRE(a != nullptr, "hxm_chunk_state_scan: args is NULL");
+  HXM_REQUIRE(a->struct_size == sizeof(hxm_chunk_scan_args), "hxm_chunk_state_scan: struct_size %zu != %zu",
+              a->struct_size, sizeof(hxm_chunk_scan_args));
+  HXM_REQUIRE(a->groups >= 0 && a->nchunks >= 0 && a->rows >= 1 && a->cols >= 1,
+              "hxm_chunk_state_scan: bad sizes groups=%lld nchunks=%d rows=%d cols=%d", (long long)a->groups,
+              a->nchunks, a->rows, a->cols);
+  if (a->groups == 0 || a->nchunks == 0) return HXM_OK;
+  HXM_REQUIRE(a->x != nullptr, "hxm_chunk_state_scan: x is NULL");
+  const int64_t n = a->groups * a->rows * (int64_t)a->cols;
+  mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_1d(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      a->x, a->decay, a->groups, a->nchunks, a->rows, a->cols, a->reverse ? 1 : 0);
+  return check_launch("hxm_chunk_state_scan");
+}

@@ -8,8 +8,8 @@ Mirrors hybrid_xmamba/kernels/tfla/tfla_interface.py:
     per-head scalars broadcast over D (an ``expand``ed view, stride 0 on D)
     take the scalar-gate kernel without being materialised.
   * ``TFLAFunction`` — autograd Function with the reference's name (:18-81);
-    backward recomputes the recurrence under autograd with torch ops, as the
-    reference does (:52-81).
+    its backward is the chunkwise one of ``tfla_bwd`` (the reference re-runs
+    the step loop under autograd, :52-81).
   * ``mlstm_chunkwise_fwd(q, k, v, log_i, log_f, ...)`` — the extended entry:
     gates in log space (log_i = input-gate pre-activation, log_f =
     logsigmoid(forget pre-activation)), per head (B, H, L) or per channel
@@ -24,8 +24,9 @@ import torch
 
 from ... import _lib
 from .._common import dtype_code, ptr, require_cuda, stream_of
+from .tfla_bwd import mlstm_chunkwise_bwd
 
-__all__ = ["apply_tfla", "mlstm_chunkwise_fwd", "TFLAFunction"]
+__all__ = ["apply_tfla", "mlstm_chunkwise_fwd", "mlstm_chunkwise_bwd", "TFLAFunction"]
 
 
 def _unit_last(t):
@@ -99,24 +100,13 @@ def _gate_logs(i_gate, f_gate):
     return torch.log(i_gate.float()), torch.log(f_gate.float())
 
 
-def _tfla_torch(q, k, v, ig, fg):
-    """Differentiable torch restatement (backward only; reference :84-139)."""
-    bsz, nh, L, d = q.shape
-    C = torch.zeros(bsz, nh, d, v.shape[-1], device=q.device, dtype=torch.float32)
-    n = torch.zeros(bsz, nh, d, device=q.device, dtype=torch.float32)
-    hs = []
-    for t in range(L):
-        f_t, i_t = fg[:, :, t].float(), ig[:, :, t].float()
-        C = f_t[..., None] * C + i_t[..., None] * (k[:, :, t, :, None].float() * v[:, :, t, None, :].float())
-        n = f_t * n + i_t * k[:, :, t].float()
-        num = torch.einsum("bhd,bhde->bhe", q[:, :, t].float(), C)
-        den = torch.clamp(torch.einsum("bhd,bhd->bh", q[:, :, t].float(), n), min=1.0)[..., None]
-        hs.append(num / den)
-    return torch.stack(hs, 2)
-
-
 class TFLAFunction(torch.autograd.Function):
-    """Autograd wrapper with the reference's name (tfla_interface.py:18-81)."""
+    """Autograd wrapper with the reference's name (tfla_interface.py:18-81).
+
+    The reference's backward re-runs the step loop under autograd (:52-81);
+    this one is the chunkwise backward of ``tfla_bwd.mlstm_chunkwise_bwd``
+    (same gradients, fp32 arithmetic).  Gates given as expanded per-head
+    views get their per-channel gradients; autograd sums them over D."""
 
     @staticmethod
     def forward(ctx, q, k, v, i_gate, f_gate):
@@ -127,12 +117,11 @@ class TFLAFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_output):
         q, k, v, i_gate, f_gate = ctx.saved_tensors
-        with torch.enable_grad():
-            ins = [t.detach().requires_grad_(True) for t in (q, k, v, i_gate, f_gate)]
-            out = _tfla_torch(*ins)
-            out.backward(grad_output.float())
-        return tuple(t.grad.to(o.dtype) if t.grad is not None else None
-                     for t, o in zip(ins, (q, k, v, i_gate, f_gate)))
+        log_i, log_f = _gate_logs(i_gate, f_gate)
+        dq, dk, dv, _, dlog_f, di = mlstm_chunkwise_bwd(q, k, v, log_i, log_f, grad_output, chunk=64,
+                                                        gate_grads="channel")
+        df = dlog_f / f_gate.float()
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), di.to(i_gate.dtype), df.to(f_gate.dtype)
 
 
 def apply_tfla(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, i_gate: torch.Tensor,

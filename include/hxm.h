@@ -172,6 +172,72 @@ hxm_status hxm_mlstm_chunkwise_fwd(const hxm_mlstm_args* args, void* stream);
 hxm_status hxm_mlstm_chunkwise_fwd_noalloc(const hxm_mlstm_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* 2b. mLSTM chunkwise backward (zero initial state)                          */
+/*                                                                           */
+/* Replaces the recompute-under-autograd backward of TFLAFunction            */
+/*   (hybrid_xmamba/kernels/tfla/tfla_interface.py:52-81), which re-runs the */
+/* step loop tfla_forward_pytorch (:84-139) under autograd.                  */
+/* Chunkwise form, per (b, h), chunk of `chunk` steps and key channel j, with*/
+/* b_t = sum of log_f over the chunk's steps up to t, g = b at the chunk's   */
+/* last step and rho = g / 2:                                                */
+/*   Qs_t = q_t e^(b_t - rho),  Ks_t = k_t e^(log_i_t + rho - b_t)            */
+/* (intra-chunk weights Qs_t . Ks_s; the state entering the next chunk is    */
+/* e^g C + e^rho Ks^T [v | 1], n riding as the column of ones).  The batched */
+/* chunk GEMMs between the two calls below are the caller's (cuBLAS).        */
+/*   hxm_mlstm_bwd_prepare: q, k (b, h, t) strided with dense dqk, log gates */
+/*     (b, h, t) strided, per head (gate_mode 0) or per channel (1, dense    */
+/*     dqk) -> q_scaled, k_scaled (b, h, nchunks*chunk, dqk), zero past      */
+/*     seqlen; rho, e_rho = e^rho, e_g = e^g (b, h, nchunks, dqk).  fp32,     */
+/*     dense.                                                                */
+/*   hxm_mlstm_bwd_finalize: dq_scaled = dL/dQs, dk_scaled = dL/dKs (layout   */
+/*     of q_scaled) plus q_scaled, k_scaled, rho and the gates ->             */
+/*     dq = e^(b - rho) dL/dQs, dk = e^(log_i + rho - b) dL/dKs,              */
+/*     dlog_i = Ks . dL/dKs (per channel), and                               */
+/*     dlog_f_t = sum over s >= t of (Qs . dL/dQs - Ks . dL/dKs)_s,           */
+/*     d_i = k e^(rho - b) dL/dKs (the gradient for the gate value i, with no */
+/*     division by i), all (b, h, seqlen, dqk) fp32 dense; chunk_sum          */
+/*     (b, h, nchunks, dqk) is scratch.  Per-head gate gradients are the      */
+/*     sums over dqk.                                                         */
+typedef struct hxm_mlstm_bwd_args {
+  size_t struct_size;
+  int32_t batch, heads, seqlen, dqk, chunk;
+  int32_t gate_mode;        /* 0 per head, 1 per channel                     */
+  hxm_dtype io_dtype;       /* q, k                                          */
+  const void* q; int64_t q_stride[3];          /* (b, h, t) element strides  */
+  const void* k; int64_t k_stride[3];
+  const float* log_i; int64_t i_stride[3];     /* (b, h, t)                  */
+  const float* log_f; int64_t f_stride[3];
+  float* q_scaled; float* k_scaled;
+  float* rho; float* e_rho; float* e_g;
+  const float* dq_scaled; const float* dk_scaled;
+  float* chunk_sum;
+  float* dq; float* dk; float* dlog_i; float* dlog_f;
+  float* d_i;               /* (b, h, seqlen, dqk) or NULL: dL/di, i = e^log_i */
+} hxm_mlstm_bwd_args;
+
+hxm_status hxm_mlstm_bwd_prepare(const hxm_mlstm_bwd_args* args, void* stream);
+hxm_status hxm_mlstm_bwd_finalize(const hxm_mlstm_bwd_args* args, void* stream);
+
+/* Exclusive chunk-level recurrence, in place, for the chunkwise backward:   */
+/* per group and element (r, c), s = 0 and for each chunk k in order         */
+/* (reverse = 0) or in reverse (reverse = 1):                                 */
+/*   y = x[k, r, c];  x[k, r, c] = s;  s = decay[k, r] * s + y               */
+/* so x becomes the states entering each chunk (forward) or the adjoints     */
+/* leaving each chunk (reverse).  x (groups, nchunks, rows, cols), decay     */
+/* (groups, nchunks, rows) or NULL (= 1), fp32 dense.  No reference          */
+/* counterpart: the reference's backward has no chunk states.                */
+typedef struct hxm_chunk_scan_args {
+  size_t struct_size;
+  int64_t groups;
+  int32_t nchunks, rows, cols;
+  float* x;
+  const float* decay;
+  int32_t reverse;
+} hxm_chunk_scan_args;
+
+hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* 3. Mamba-2 SSD chunked scan (ngroups = 1)                                  */
 /*                                                                           */
 /* No function of the reference computes this; its arithmetic is the Euler   */

@@ -41,7 +41,8 @@ def test_struct_sizes_match_header_layout():
                     (_lib.SsdArgs, "hxm_ssd_chunk_scan_fwd"), (_lib.SlstmArgs, "hxm_slstm_scan_fwd"),
                     (_lib.ConvArgs, "hxm_causal_conv1d_fwd"), (_lib.RmsnormArgs, "hxm_rmsnorm_fwd"),
                     (_lib.MlstmGatesArgs, "hxm_mlstm_gate_prologue"), (_lib.MlstmGatesArgs, "hxm_mlstm_gate_epilogue"),
-                    (_lib.ScanBwdArgs, "hxm_selective_scan_bwd")]:
+                    (_lib.ScanBwdArgs, "hxm_selective_scan_bwd"), (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_prepare"),
+                    (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_finalize"), (_lib.ChunkScanArgs, "hxm_chunk_state_scan")]:
         a = cls()
         a.struct_size = ct.sizeof(a) + 8
         st = getattr(_lib.lib(), fn)(ct.byref(a), None)
@@ -88,3 +89,26 @@ def test_conv_rejects_bad_arguments_without_cuda():
     assert lib.hxm_causal_conv1d_fwd(ct.byref(a), None) == _lib.HXM_EBADARG        # NULL weight
     a.batch = 0
     assert lib.hxm_causal_conv1d_fwd(ct.byref(a), None) == _lib.HXM_OK
+
+
+def test_mlstm_backward_entries_validate_without_cuda():
+    """The ctypes layouts of the backward structs match the header (the size
+    check passes and the next check fires), bad sizes are rejected and empty
+    work is a no-op success."""
+    lib = _lib.lib()
+    a = _lib.MlstmBwdArgs()
+    a.struct_size = ct.sizeof(a)
+    a.batch, a.heads, a.seqlen, a.dqk, a.chunk = 1, 1, 8, 4, 0
+    for fn in ("hxm_mlstm_bwd_prepare", "hxm_mlstm_bwd_finalize"):
+        assert getattr(lib, fn)(ct.byref(a), None) == _lib.HXM_EBADARG
+        assert b"chunk" in lib.hxm_last_error_string()
+    a.chunk, a.gate_mode = 4, 2
+    assert lib.hxm_mlstm_bwd_prepare(ct.byref(a), None) == _lib.HXM_EBADARG
+    assert b"gate_mode" in lib.hxm_last_error_string()
+    s = _lib.ChunkScanArgs()
+    s.struct_size = ct.sizeof(s)
+    s.groups, s.nchunks, s.rows, s.cols = 1, 3, 0, 4
+    assert lib.hxm_chunk_state_scan(ct.byref(s), None) == _lib.HXM_EBADARG
+    assert b"rows=0" in lib.hxm_last_error_string()
+    s.rows, s.groups = 2, 0
+    assert lib.hxm_chunk_state_scan(ct.byref(s), None) == _lib.HXM_OK

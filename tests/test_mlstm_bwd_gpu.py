@@ -1,0 +1,156 @@
+"""Chunkwise mLSTM backward vs autograd of the reference loop.
+
+The reference's backward (tfla_interface.py:52-81) re-runs the step loop
+tfla_forward_pytorch (:84-139) under autograd; the check here does the same in
+float64 on the same inputs and compares every gradient of apply_tfla (q, k, v,
+i_gate, f_gate).  Tolerances (normwise relative error): fp32 I/O 1e-4 (fp32
+chunk GEMMs and state); bf16 I/O 2e-2 against the loop on the bf16-rounded
+inputs.
+"""
+import ctypes as ct
+import math
+
+import pytest
+import torch
+
+from tests.conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TOL32, TOL16 = 1e-4, 2e-2
+
+
+@pytest.fixture(scope="module")
+def T():
+    if not torch.cuda.is_available():
+        pytest.skip("needs CUDA")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    from hybrid_model_mamba_xlstm_b200.kernels import tfla
+    return tfla
+
+
+def _loop(q, k, v, ig, fg):
+    """float64 restatement of tfla_forward_pytorch (tfla_interface.py:84-139)."""
+    bsz, nh, L, d = q.shape
+    C = torch.zeros(bsz, nh, d, v.shape[-1], dtype=q.dtype)
+    n = torch.zeros(bsz, nh, d, dtype=q.dtype)
+    hs = []
+    for t in range(L):
+        C = fg[:, :, t, :, None] * C + ig[:, :, t, :, None] * (k[:, :, t, :, None] * v[:, :, t, None, :])
+        n = fg[:, :, t] * n + ig[:, :, t] * k[:, :, t]
+        num = torch.einsum("bhd,bhde->bhe", q[:, :, t], C)
+        den = torch.clamp(torch.einsum("bhd,bhd->bh", q[:, :, t], n), min=1.0)[..., None]
+        hs.append(num / den)
+    return torch.stack(hs, 2)
+
+
+def _d64(t):
+    return t.detach().double().cpu()
+
+
+def _case(shape, dv, per_channel, fmu, seed, dtype, qscale=None):
+    bsz, nh, L, d = shape
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(bsz, nh, L, d, generator=g) * (qscale if qscale is not None else 1 / math.sqrt(d))
+    k = torch.randn(bsz, nh, L, d, generator=g)
+    v = torch.randn(bsz, nh, L, dv, generator=g)
+    gs = (bsz, nh, L, d) if per_channel else (bsz, nh, L, 1)
+    ipre = torch.randn(*gs, generator=g) * 0.5
+    fpre = torch.randn(*gs, generator=g) + fmu
+    dh = torch.randn(bsz, nh, L, dv, generator=g)
+    q, k, v, dh = (t.to(dtype) for t in (q, k, v, dh))
+    return q, k, v, torch.exp(ipre), torch.sigmoid(fpre), dh
+
+
+def _grads_gpu(T, q, k, v, ig, fg, dh, expand):
+    leaves = [t.cuda().requires_grad_(True) for t in (q, k, v, ig, fg)]
+    igx, fgx = leaves[3], leaves[4]
+    if expand:
+        igx, fgx = igx.expand(*q.shape), fgx.expand(*q.shape)
+    out = T.apply_tfla(leaves[0], leaves[1], leaves[2], igx, fgx)
+    out.backward(dh.cuda())
+    return out, [t.grad for t in leaves]
+
+
+def _grads_ref(q, k, v, ig, fg, dh, expand):
+    leaves = [_d64(t).requires_grad_(True) for t in (q, k, v, ig, fg)]
+    igx, fgx = leaves[3], leaves[4]
+    if expand:
+        igx, fgx = igx.expand(*q.shape), fgx.expand(*q.shape)
+    out = _loop(leaves[0], leaves[1], leaves[2], igx, fgx)
+    out.backward(_d64(dh))
+    return out, [t.grad for t in leaves]
+
+
+# the reference's own test shapes (tests/test_kernels.py) plus ragged lengths
+@pytest.mark.parametrize("shape,dv,per_channel,fmu", [
+    ((2, 4, 64, 32), 32, True, 3.0), ((2, 4, 32, 16), 16, True, 0.0), ((1, 2, 16, 8), 8, True, 3.0),
+    ((1, 2, 37, 16), 24, True, 0.0), ((2, 2, 130, 32), 32, False, 3.0), ((1, 1, 1, 8), 8, True, 3.0)])
+def test_apply_tfla_grads_fp32(T, shape, dv, per_channel, fmu):
+    case = _case(shape, dv, per_channel, fmu, seed=sum(shape), dtype=torch.float32)
+    out, got = _grads_gpu(T, *case, expand=not per_channel)
+    ref_out, want = _grads_ref(*case, expand=not per_channel)
+    assert rel_err(_d64(out).numpy(), ref_out.detach().numpy()) < 1e-5
+    for name, a, b in zip(("dq", "dk", "dv", "di", "df"), got, want):
+        assert a.shape == b.shape, name
+        assert rel_err(_d64(a).numpy(), b.numpy()) < TOL32, name
+
+
+def test_apply_tfla_grads_normalizer_clamp_active(T):
+    """Large q so that q.n > 1 on most steps: the den branch of the gradient."""
+    case = _case((1, 2, 96, 16), 16, True, 2.0, seed=5, dtype=torch.float32, qscale=1.0)
+    _, got = _grads_gpu(T, *case, expand=False)
+    _, want = _grads_ref(*case, expand=False)
+    for name, a, b in zip(("dq", "dk", "dv", "di", "df"), got, want):
+        assert rel_err(_d64(a).numpy(), b.numpy()) < TOL32, name
+
+
+def test_apply_tfla_grads_bf16_channel_gates(T):
+    """mLSTMBlock-like: bf16 q, k, v, head 128, per-channel gates near sigmoid(N(0, 1))."""
+    q, k, v, ig, fg, dh = _case((1, 2, 300, 128), 128, True, 0.0, seed=11, dtype=torch.bfloat16)
+    out, got = _grads_gpu(T, q, k, v, ig, fg, dh, expand=False)
+    _, want = _grads_ref(q, k, v, ig, fg, dh, expand=False)
+    assert got[0].dtype == torch.bfloat16
+    for name, a, b in zip(("dq", "dk", "dv", "di", "df"), got, want):
+        assert rel_err(_d64(a).numpy(), b.numpy()) < TOL16, name
+
+
+def test_log_gate_entry_per_head_sums(T):
+    """mlstm_chunkwise_bwd on (B, H, L) log gates returns the per-channel
+    gate gradients summed over Dqk, and d(log i) = i * dL/di."""
+    q, k, v, ig, fg, dh = (t.cuda() for t in _case((2, 2, 70, 16), 16, False, 3.0, seed=3, dtype=torch.float32))
+    li, lf = torch.log(ig[..., 0]), torch.log(fg[..., 0])
+    per_head = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, chunk=32)
+    per_chan = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, chunk=32, gate_grads="channel")
+    for a, b in zip(per_head[:3], per_chan[:3]):
+        assert torch.equal(a, b)
+    for a, b in zip(per_head[3:], per_chan[3:]):
+        assert a.shape == (2, 2, 70) and b.shape == (2, 2, 70, 16)
+        assert torch.allclose(a, b.sum(-1), rtol=1e-5, atol=1e-6)
+    assert torch.allclose(per_head[3], torch.exp(li) * per_head[5], rtol=1e-5, atol=1e-6)
+    # a different chunk length gives the same gradients
+    other = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, chunk=64)
+    for a, b in zip(per_head, other):
+        assert rel_err(_d64(a).numpy(), _d64(b).numpy()) < 1e-5
+
+
+def test_chunk_state_scan_forward_and_reverse(T):
+    """hxm_chunk_state_scan through the C ABI vs a host loop, with and without decay."""
+    from hybrid_model_mamba_xlstm_b200 import _lib
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(2, 3, 5, 7, 9, generator=g)
+    dec = torch.rand(2, 3, 5, 7, generator=g)
+    for reverse in (0, 1):
+        for use_decay in (True, False):
+            xd = x.clone().cuda()
+            dd = dec.cuda() if use_decay else None
+            a = _lib.ChunkScanArgs()
+            a.groups, a.nchunks, a.rows, a.cols = 6, 5, 7, 9
+            a.x, a.decay, a.reverse = xd.data_ptr(), None if dd is None else dd.data_ptr(), reverse
+            _lib.call("hxm_chunk_state_scan", a, torch.cuda.current_stream().cuda_stream)
+            want = torch.empty_like(x)
+            s = torch.zeros(2, 3, 7, 9)
+            order = range(4, -1, -1) if reverse else range(5)
+            for kc in order:
+                want[:, :, kc] = s
+                s = (dec[:, :, kc, :, None] if use_decay else 1.0) * s + x[:, :, kc]
+            assert torch.allclose(xd.cpu(), want, rtol=1e-6, atol=1e-6), (reverse, use_decay)
