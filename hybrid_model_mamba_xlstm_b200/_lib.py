@@ -156,7 +156,7 @@ class MlstmBwdArgs(ct.Structure):
         ("q_scaled", ct.c_void_p), ("k_scaled", ct.c_void_p),
         ("rho", ct.c_void_p), ("e_rho", ct.c_void_p), ("e_g", ct.c_void_p),
         ("dq_scaled", ct.c_void_p), ("dk_scaled", ct.c_void_p),
-        ("chunk_sum", ct.c_void_p),
+        ("chunk_dg", ct.c_void_p),
         ("dq", ct.c_void_p), ("dk", ct.c_void_p), ("dlog_i", ct.c_void_p), ("dlog_f", ct.c_void_p),
         ("d_i", ct.c_void_p),
     ]

@@ -18,10 +18,11 @@
 //             the state adjoints leaving each chunk
 //   finalize  dL/dQs, dL/dKs -> dq = e^(b - rho) dL/dQs,
 //             dk = i e^(rho - b) dL/dKs, dlog_i = Ks . dL/dKs and
-//             dlog_f_t = sum_{s >= t} (Qs . dL/dQs - Ks . dL/dKs)_s
-// The last line is the gate identity of decayed linear recurrences: the loss
-// sees log f only through b, whose gradient at step t is
-// q_t dq_t - (i k)_t d(i k)_t, and log f_t enters every b_s with s >= t.
+//             dlog_f_t = dg + sum_{s >= t in the chunk} (Qs . dL/dQs - Ks . dL/dKs)_s
+// The loss sees the chunk's log f only through the in-chunk prefix sums b
+// (gradient q_t dq_t - (i k)_t d(i k)_t at step t, the gate identity of decayed
+// linear recurrences) and through the chunk total g, whose gradient dg is the
+// inner product of the state leaving the chunk with its adjoint (an input).
 #include "capi_internal.h"
 #include "common.cuh"
 
@@ -40,7 +41,7 @@ struct Params {
   int64_t sf[3];
   float *qs, *ks, *rho, *erho, *eg;
   const float *dqs, *dks;
-  float* csum;
+  const float* dg;
   float *dq, *dk, *dli, *dlf, *di;
 };
 
@@ -80,8 +81,8 @@ __global__ void __launch_bounds__(128) prepare_kernel(const Params p) {
 }
 
 // grid (batch*heads*nch, ceil(dqk/128)), block 128: the chunk's steps in reverse,
-// b_t rebuilt from g = 2 rho; the within-chunk suffix sum of the gate identity
-// goes to dlog_f and the chunk total to csum.  di (optional): the gradient
+// b_t rebuilt from g = 2 rho; dlog_f = the chunk's dg plus the within-chunk
+// suffix sum of the gate identity.  di (optional): the gradient
 // with respect to the gate value i = e^(log_i), k . dL/d(i k), formed without
 // dividing by i.
 template <typename T>
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(128) finalize_kernel(const Params p) {
   float bt = 2.f * rho;  // b at the chunk's last real step
   const int64_t ro = ((int64_t)bh * p.nch + kc) * p.chunk * p.dqk + j;
   const int64_t oo = ((int64_t)bh * p.seqlen + t0) * p.dqk + j;
-  float acc = 0.f;
+  float acc = p.dg[vo];
   for (int s = tn - 1; s >= 0; --s) {
     const int64_t t = t0 + s;
     const int64_t r = ro + (int64_t)s * p.dqk, o = oo + (int64_t)s * p.dqk;
@@ -117,46 +118,44 @@ __global__ void __launch_bounds__(128) finalize_kernel(const Params p) {
     p.dlf[o] = t == 0 ? 0.f : acc;
     bt -= lf[t * p.sf[2]];
   }
-  p.csum[vo] = acc;
 }
 
-// dlog_f[b, h, t, j] += csum[b, h, t / chunk, j] (csum holds the suffix sums of later chunks)
-__global__ void __launch_bounds__(256) add_offsets_kernel(const Params p) {
-  const int64_t n = (int64_t)p.batch * p.heads * p.seqlen * p.dqk;
-  for (int64_t e = blockIdx.x * 256ll + threadIdx.x; e < n; e += (int64_t)gridDim.x * 256) {
-    const int j = (int)(e % p.dqk);
-    const int64_t bt = e / p.dqk;
-    const int t = (int)(bt % p.seqlen);
-    const int64_t bh = bt / p.seqlen;
-    if (t > 0) p.dlf[e] += p.csum[(bh * p.nch + t / p.chunk) * p.dqk + j];
-  }
-}
-
-// grid-stride over groups*rows*cols elements; each runs its chunks in order
-__global__ void __launch_bounds__(256) chunk_scan_kernel(float* x, const float* decay, int64_t groups, int nch,
-                                                         int rows, int cols, int reverse) {
+// one thread per (group, row, col) element, chunks in order (or reversed); the
+// loads of 8 chunks are issued before their dependent updates, so a thread
+// keeps 8 reads in flight instead of one load-store round trip per chunk
+__global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, const float* __restrict__ decay,
+                                                         int64_t groups, int nch, int rows, int cols, int reverse) {
+  constexpr int kB = 8;
   const int64_t rc = (int64_t)rows * cols;
-  const int64_t n = groups * rc;
-  for (int64_t e = blockIdx.x * 256ll + threadIdx.x; e < n; e += (int64_t)gridDim.x * 256) {
-    const int64_t grp = e / rc, w = e % rc;
-    const int r = (int)(w / cols);
-    float* xp = x + grp * nch * rc + w;
-    const float* dp = decay ? decay + grp * nch * rows + r : nullptr;
-    float s = 0.f;
-#pragma unroll 4
-    for (int it = 0; it < nch; ++it) {
+  const int64_t e = blockIdx.x * 256ll + threadIdx.x;
+  if (e >= groups * rc) return;
+  const int64_t grp = e / rc, w = e % rc;
+  const int r = (int)(w / cols);
+  float* xp = x + grp * nch * rc + w;
+  const float* dp = decay ? decay + grp * nch * rows + r : nullptr;
+  float s = 0.f;
+  for (int it0 = 0; it0 < nch; it0 += kB) {
+    float y[kB], dc[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int it = it0 + u;
       const int kc = reverse ? nch - 1 - it : it;
-      const float y = xp[kc * rc];
-      xp[kc * rc] = s;
-      s = (dp ? dp[(int64_t)kc * rows] : 1.f) * s + y;
+      y[u] = it < nch ? xp[kc * rc] : 0.f;
+      dc[u] = (it < nch && dp) ? dp[(int64_t)kc * rows] : 1.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int it = it0 + u;
+      if (it < nch) {
+        const int kc = reverse ? nch - 1 - it : it;
+        xp[kc * rc] = s;
+        s = dc[u] * s + y[u];
+      }
     }
   }
 }
 
-static int grid_1d(int64_t n) {
-  const int64_t b = (n + 255) / 256;
-  return (int)(b < 148 * 16 ? (b > 0 ? b : 1) : 148 * 16);
-}
+static unsigned grid_each(int64_t n) { return (unsigned)((n + 255) / 256); }
 
 static hxm_status fill(const hxm_mlstm_bwd_args* a, Params& p, const char* who) {
   HXM_REQUIRE(a != nullptr, "%s: args is NULL", who);
@@ -175,7 +174,7 @@ static hxm_status fill(const hxm_mlstm_bwd_args* a, Params& p, const char* who) 
     p.sq[i] = a->q_stride[i]; p.sk[i] = a->k_stride[i]; p.si[i] = a->i_stride[i]; p.sf[i] = a->f_stride[i];
   }
   p.qs = a->q_scaled; p.ks = a->k_scaled; p.rho = a->rho; p.erho = a->e_rho; p.eg = a->e_g;
-  p.dqs = a->dq_scaled; p.dks = a->dk_scaled; p.csum = a->chunk_sum;
+  p.dqs = a->dq_scaled; p.dks = a->dk_scaled; p.dg = a->chunk_dg;
   p.dq = a->dq; p.dk = a->dk; p.dli = a->dlog_i; p.dlf = a->dlog_f; p.di = a->d_i;
   HXM_REQUIRE(p.log_i && p.log_f && p.qs && p.ks && p.rho, "%s: NULL gate or chunk-operand pointer", who);
   return HXM_OK;
@@ -205,24 +204,15 @@ extern "C" hxm_status hxm_mlstm_bwd_finalize(const hxm_mlstm_bwd_args* a, void* 
   mlstm_bwd::Params p{};
   hxm_status s = mlstm_bwd::fill(a, p, "hxm_mlstm_bwd_finalize");
   if (s != HXM_OK) return s;
-  HXM_REQUIRE(p.dqs && p.dks && p.csum && p.dq && p.dk && p.dli && p.dlf,
-              "hxm_mlstm_bwd_finalize: NULL gradient or chunk_sum pointer");
+  HXM_REQUIRE(p.dqs && p.dks && p.dg && p.dq && p.dk && p.dli && p.dlf,
+              "hxm_mlstm_bwd_finalize: NULL gradient or chunk_dg pointer");
   if (p.nch == 0) return HXM_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((unsigned)(p.batch * p.heads * p.nch), (unsigned)((p.dqk + 127) / 128));
   HXM_REQUIRE(p.k || !p.di, "hxm_mlstm_bwd_finalize: d_i needs k");
   if (a->io_dtype == HXM_F32) mlstm_bwd::finalize_kernel<float><<<grid, 128, 0, st>>>(p);
   else mlstm_bwd::finalize_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(p);
-  if ((s = check_launch("hxm_mlstm_bwd_finalize")) != HXM_OK) return s;
-  if (p.nch > 1) {
-    mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_1d((int64_t)p.batch * p.heads * p.dqk), 256, 0, st>>>(
-        p.csum, nullptr, (int64_t)p.batch * p.heads, p.nch, p.dqk, 1, 1);
-    if ((s = check_launch("hxm_mlstm_bwd_finalize (chunk sums)")) != HXM_OK) return s;
-    mlstm_bwd::add_offsets_kernel<<<mlstm_bwd::grid_1d((int64_t)p.batch * p.heads * p.seqlen * p.dqk), 256, 0,
-                                    st>>>(p);
-    return check_launch("hxm_mlstm_bwd_finalize (offsets)");
-  }
-  return HXM_OK;
+  return check_launch("hxm_mlstm_bwd_finalize");
 }
 
 extern "C" hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* a, void* stream) {
@@ -237,7 +227,8 @@ extern "C" hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* a, void* s
   if (a->groups == 0 || a->nchunks == 0) return HXM_OK;
   HXM_REQUIRE(a->x != nullptr, "hxm_chunk_state_scan: x is NULL");
   const int64_t n = a->groups * a->rows * (int64_t)a->cols;
-  mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_1d(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  HXM_REQUIRE(n / 256 < (int64_t)0x7fffffff, "hxm_chunk_state_scan: too many elements (%lld)", (long long)n);
+  mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_each(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       a->x, a->decay, a->groups, a->nchunks, a->rows, a->cols, a->reverse ? 1 : 0);
   return check_launch("hxm_chunk_state_scan");
 }

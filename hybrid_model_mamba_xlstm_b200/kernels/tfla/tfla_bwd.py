@@ -16,14 +16,25 @@ of log f up to t, g its chunk total, rho = g / 2):
     dL/dQs = dS Ks + e^rho ([dnum | dden] X_k^T)
     dL/dKs = dS^T Qs + e^rho ([v | 1] Y_k^T)
     dv = S^T dnum + (e^rho Ks) Y_k[:, :dv]
-    dq, dk, dlog_i, dlog_f, di                               (hxm_mlstm_bwd_finalize)
+    dq, dk, dlog_i, di                                       (hxm_mlstm_bwd_finalize)
+    dlog_f_t = dg_k + sum_{s >= t in chunk k} (q . dq - (i k) . d(i k))_s,
+    dg_k = <Y_k, X_{k+1}> per key row (the chunk's total log forget gate
+    decays the state it passes on)                           (hxm_mlstm_bwd_finalize)
+
+That separable form serves per-channel gates.  Per-head gates take the exact
+decay-matrix form (``_bwd_heads``): S = causal(Q (i k)^T) * e^(b_t - b_s) with
+inter-chunk factors e^b and e^(g - b), all at most 1, so no decay overflows;
+their in-chunk gate term is rowsum(W) - colsum(W) + the two inter-chunk
+terms, W = dL/dS * S, with W's diagonal (the largest entries under strong
+decay, present in both sums) left out exactly instead of cancelled in
+rounding.
 
 The chunk GEMMs are batched fp32 cuBLAS calls (torch.matmul); the gate
 scaling, the two chunk-level recurrences and the gate gradients (a suffix sum
 over the whole sequence) are this library's kernels.  Memory: two fp32 state
-arrays of (B, H, L / chunk, dqk, dv + 1).  Exponents are bounded by half of a
-chunk's total log forget gate, which must stay above about -170 per channel
-for 64-step chunks.
+arrays of (B, H, L / chunk, dqk, w), w = dv + 1 rounded up to 8.  Exponents
+are bounded by half of a chunk's total log forget gate, which must stay above
+about -170 per channel for 64-step chunks.
 """
 from __future__ import annotations
 
@@ -40,6 +51,97 @@ def _scan(x, decay, reverse, stream):
     a.groups, a.nchunks, a.rows, a.cols = x.shape[0] * x.shape[1], x.shape[2], x.shape[3], x.shape[4]
     a.x, a.decay, a.reverse = ptr(x), ptr(decay), int(reverse)
     _lib.call("hxm_chunk_state_scan", a, stream)
+
+
+def _chunk_dg(Y, X, dims):
+    """<adjoint leaving chunk k, state leaving chunk k> = <Y_k, X_{k+1}> summed
+    over dims (0 for the last chunk, whose adjoint is zero)."""
+    out = torch.zeros(*Y.shape[:3], *[Y.shape[i] for i in range(3, Y.dim()) if i - Y.dim() not in dims],
+                      device=Y.device, dtype=Y.dtype)
+    if Y.shape[2] > 1:
+        out[:, :, :-1] = (Y[:, :, :-1] * X[:, :, 1:]).sum(dims)
+    return out
+
+
+def _bwd_heads(q, k, v, li, lf, dout, c, normalize, per_channel_out, st):
+    """Per-head gates li, lf (B, H, L): the exact decay-matrix chunkwise form.
+    normalize=False drops the normalizer (h = q C, the SSD recurrence)."""
+    bsz, nh, L, dqk = q.shape
+    dv = v.shape[-1]
+    dev = q.device
+    f32 = dict(device=dev, dtype=torch.float32)
+    nch = (L + c - 1) // c
+    Lp = nch * c
+    Q = torch.zeros(bsz, nh, Lp, dqk, **f32)
+    Q[:, :, :L] = q
+    K = torch.zeros(bsz, nh, Lp, dqk, **f32)
+    K[:, :, :L] = k
+    Q, K = Q.view(bsz, nh, nch, c, dqk), K.view(bsz, nh, nch, c, dqk)
+    w = (dv + int(normalize) + 7) // 8 * 8
+    va = torch.zeros(bsz, nh, Lp, w, **f32)
+    va[:, :, :L, :dv] = v
+    if normalize:
+        va[..., dv] = 1.0
+    Vc = va.view(bsz, nh, nch, c, w)
+    lip = torch.full((bsz, nh, Lp), float("-inf"), **f32)
+    lip[:, :, :L] = li
+    lfp = torch.zeros(bsz, nh, Lp, **f32)
+    lfp[:, :, :L] = lf
+    b = lfp.view(bsz, nh, nch, c).cumsum(-1)
+    g = b[..., -1:]
+    ig = torch.exp(lip).view(bsz, nh, nch, c)
+    Kp = K * ig.unsqueeze(-1)
+    causal = torch.ones(c, c, device=dev, dtype=torch.bool).tril_()
+    Lm = torch.exp((b.unsqueeze(-1) - b.unsqueeze(-2)).masked_fill_(~causal, float("-inf")))
+    eb = torch.exp(b).unsqueeze(-1)
+    egb = torch.exp(g - b).unsqueeze(-1)
+    eg = torch.exp(g[..., 0]).unsqueeze(-1).expand(bsz, nh, nch, dqk).contiguous()
+    Kd = Kp * egb
+    X = torch.matmul(Kd.transpose(-1, -2), Vc)  # increments -> states entering each chunk
+    _scan(X, eg, False, st)
+    S = torch.matmul(Q, Kp.transpose(-1, -2)).mul_(Lm)
+    Qe = Q * eb
+    QX = torch.matmul(Qe, X)
+    numa = QX + torch.matmul(S, Vc)
+    dHc = torch.zeros(bsz, nh, Lp, dv, **f32)
+    dHc[:, :, :L] = dout
+    dHc = dHc.view(bsz, nh, nch, c, dv)
+    dNa = torch.zeros(bsz, nh, nch, c, w, **f32)
+    if normalize:
+        num, den = numa[..., :dv], numa[..., dv]
+        Dm = den.clamp(min=1.0)
+        dnum = dHc / Dm.unsqueeze(-1)
+        dNa[..., :dv] = dnum
+        dNa[..., dv] = -(den >= 1.0).float() * (dnum * num).sum(-1) / Dm
+    else:
+        dNa[..., :dv] = dHc
+    Y = torch.matmul(Qe.transpose(-1, -2), dNa)  # increments -> adjoints leaving each chunk
+    _scan(Y, eg, True, st)
+    dSf = torch.matmul(dNa, Vc.transpose(-1, -2))  # dL/dS
+    dS = dSf * Lm                                     # dL/d(Q (i k)^T)
+    VY = torch.matmul(Vc, Y.transpose(-1, -2))
+    dQ = torch.matmul(dS, Kp).add_(eb * torch.matmul(dNa, X.transpose(-1, -2)))
+    dKp = torch.matmul(dS.transpose(-1, -2), Q).add_(egb * VY)
+    dVa = torch.matmul(S.transpose(-1, -2), dNa).add_(torch.matmul(Kd, Y))
+    un = lambda t: t.reshape(bsz, nh, Lp, *t.shape[4:])[:, :, :L]
+    dk = ig.unsqueeze(-1) * dKp
+    di_c = K * dKp                                   # per channel: k . d(i k)
+    if per_channel_out:  # the gate identity per channel, in-chunk part
+        db = Q * dQ - Kp * dKp
+        dg = _chunk_dg(Y, X, (-1,))
+    else:
+        di_c = di_c.sum(-1)
+        W = dSf.mul_(S)
+        W.diagonal(dim1=-2, dim2=-1).zero_()  # in both sums: its net term is exactly zero
+        db = W.sum(-1) - W.sum(-2) + (dNa * QX).sum(-1) - (Kd * VY).sum(-1)
+        dg = _chunk_dg(Y, X, (-1, -2))
+    dlf = db.flip(3).cumsum(3).flip(3).add_(dg.unsqueeze(3))
+    dlf = dlf.reshape(bsz, nh, Lp, *dlf.shape[4:])[:, :, :L]
+    dlf[:, :, 0] = 0.0  # f at the first step multiplies the zero state
+    di = di_c.reshape(bsz, nh, Lp, *di_c.shape[4:])[:, :, :L]
+    igL = torch.exp(li.float())
+    dli = di * (igL.unsqueeze(-1) if per_channel_out else igL)
+    return un(dQ), un(dk), un(dVa)[..., :dv], dli, dlf, di
 
 
 def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grads: str = "auto"):
@@ -77,9 +179,11 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     if gate_mode == 1:
         gi, gf = unit(gi), unit(gf)
     c = int(chunk)
+    st = stream_of(dev)
+    if gate_mode == 0:
+        return _bwd_heads(q, k, v, gi, gf, dh, c, True, per_channel_out, st)
     nch = (L + c - 1) // c
     Lp = nch * c
-    st = stream_of(dev)
 
     qs = torch.empty(bsz, nh, Lp, dqk, **f32)
     ks = torch.empty_like(qs)
@@ -97,10 +201,11 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     Qc = qs.view(bsz, nh, nch, c, dqk)
     Kc = ks.view(bsz, nh, nch, c, dqk)
     er = erho.unsqueeze(-2)  # (B, H, nch, 1, Dqk)
-    va = torch.zeros(bsz, nh, Lp, dv + 1, **f32)
+    w = (dv + 1 + 7) // 8 * 8  # [v | 1 | 0 ...]: rows of 32-byte multiples for the GEMMs
+    va = torch.zeros(bsz, nh, Lp, w, **f32)
     va[:, :, :L, :dv] = v
     va[..., dv] = 1.0
-    Vc = va.view(bsz, nh, nch, c, dv + 1)
+    Vc = va.view(bsz, nh, nch, c, w)
     dhp = torch.zeros(bsz, nh, Lp, dv, **f32)
     dhp[:, :, :L] = dh
     dHc = dhp.view(bsz, nh, nch, c, dv)
@@ -116,20 +221,20 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     Dm = den.clamp(min=1.0)
     dnum = dHc / Dm.unsqueeze(-1)
     dden = -(den >= 1.0).float() * (dnum * num).sum(-1) / Dm
-    dNa = torch.cat([dnum, dden.unsqueeze(-1)], -1)
+    dNa = torch.zeros(bsz, nh, nch, c, w, **f32)
+    dNa[..., :dv] = dnum
+    dNa[..., dv] = dden
     Y = torch.matmul(Qr.transpose(-1, -2), dNa)  # increments -> adjoints leaving each chunk
     _scan(Y, eg, True, st)
     dS = torch.matmul(dNa, Vc.transpose(-1, -2)).masked_fill_(~causal, 0.0)
     dQs = torch.matmul(dS, Kc).add_(er * torch.matmul(dNa, X.transpose(-1, -2)))
     dKs = torch.matmul(dS.transpose(-1, -2), Qc).add_(er * torch.matmul(Vc, Y.transpose(-1, -2)))
     dVa = torch.matmul(S.transpose(-1, -2), dNa).add_(torch.matmul(Kr, Y))
-    dv_out = dVa.view(bsz, nh, Lp, dv + 1)[:, :, :L, :dv]
+    dv_out = dVa.view(bsz, nh, Lp, w)[:, :, :L, :dv]
 
+    dg = _chunk_dg(Y, X, (-1,))
     dq, dk, dli, dlf, di = (torch.empty(bsz, nh, L, dqk, **f32) for _ in range(5))
-    csum = torch.empty(bsz, nh, nch, dqk, **f32)
-    a.dq_scaled, a.dk_scaled, a.chunk_sum = ptr(dQs), ptr(dKs), ptr(csum)
+    a.dq_scaled, a.dk_scaled, a.chunk_dg = ptr(dQs), ptr(dKs), ptr(dg)
     a.dq, a.dk, a.dlog_i, a.dlog_f, a.d_i = ptr(dq), ptr(dk), ptr(dli), ptr(dlf), ptr(di)
     _lib.call("hxm_mlstm_bwd_finalize", a, st)
-    if not per_channel_out:
-        dli, dlf, di = dli.sum(-1), dlf.sum(-1), di.sum(-1)
     return dq, dk, dv_out, dli, dlf, di

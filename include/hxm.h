@@ -193,11 +193,14 @@ hxm_status hxm_mlstm_chunkwise_fwd_noalloc(const hxm_mlstm_args* args, void* str
 /*     of q_scaled) plus q_scaled, k_scaled, rho and the gates ->             */
 /*     dq = e^(b - rho) dL/dQs, dk = e^(log_i + rho - b) dL/dKs,              */
 /*     dlog_i = Ks . dL/dKs (per channel), and                               */
-/*     dlog_f_t = sum over s >= t of (Qs . dL/dQs - Ks . dL/dKs)_s,           */
+/*     dlog_f_t = chunk_dg + sum over s >= t in the chunk of                 */
+/*                (Qs . dL/dQs - Ks . dL/dKs)_s,                             */
 /*     d_i = k e^(rho - b) dL/dKs (the gradient for the gate value i, with no */
-/*     division by i), all (b, h, seqlen, dqk) fp32 dense; chunk_sum          */
-/*     (b, h, nchunks, dqk) is scratch.  Per-head gate gradients are the      */
-/*     sums over dqk.                                                         */
+/*     division by i), all (b, h, seqlen, dqk) fp32 dense.  chunk_dg          */
+/*     (b, h, nchunks, dqk), an input: the gradient for the chunk's total     */
+/*     log forget gate through the state it passes on, i.e. per key row the   */
+/*     inner product of the state leaving the chunk with its adjoint (zero    */
+/*     for the last chunk).  Per-head gate gradients are the sums over dqk.   */
 typedef struct hxm_mlstm_bwd_args {
   size_t struct_size;
   int32_t batch, heads, seqlen, dqk, chunk;
@@ -210,7 +213,7 @@ typedef struct hxm_mlstm_bwd_args {
   float* q_scaled; float* k_scaled;
   float* rho; float* e_rho; float* e_g;
   const float* dq_scaled; const float* dk_scaled;
-  float* chunk_sum;
+  const float* chunk_dg;
   float* dq; float* dk; float* dlog_i; float* dlog_f;
   float* d_i;               /* (b, h, seqlen, dqk) or NULL: dL/di, i = e^log_i */
 } hxm_mlstm_bwd_args;

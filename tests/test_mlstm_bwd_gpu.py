@@ -123,9 +123,9 @@ def test_log_gate_entry_per_head_sums(T):
     per_chan = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, chunk=32, gate_grads="channel")
     for a, b in zip(per_head[:3], per_chan[:3]):
         assert torch.equal(a, b)
-    for a, b in zip(per_head[3:], per_chan[3:]):
+    for a, b in zip(per_head[3:], per_chan[3:]):  # the same sums in another order
         assert a.shape == (2, 2, 70) and b.shape == (2, 2, 70, 16)
-        assert torch.allclose(a, b.sum(-1), rtol=1e-5, atol=1e-6)
+        assert rel_err(_d64(a).numpy(), _d64(b.sum(-1)).numpy()) < 1e-5
     assert torch.allclose(per_head[3], torch.exp(li) * per_head[5], rtol=1e-5, atol=1e-6)
     # a different chunk length gives the same gradients
     other = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, chunk=64)
