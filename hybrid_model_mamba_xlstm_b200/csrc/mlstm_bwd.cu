@@ -155,6 +155,42 @@ __global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, 
   }
 }
 
+// The same with 4 adjacent columns of one row per thread (cols % 4 == 0, x
+// 16-byte aligned): 16-byte loads and stores, one decay load per 4 columns.
+__global__ void __launch_bounds__(256) chunk_scan4_kernel(float4* __restrict__ x, const float* __restrict__ decay,
+                                                          int64_t groups, int nch, int rows, int cols4, int reverse) {
+  constexpr int kB = 8;
+  const int64_t rc4 = (int64_t)rows * cols4;
+  const int64_t e = blockIdx.x * 256ll + threadIdx.x;
+  if (e >= groups * rc4) return;
+  const int64_t grp = e / rc4, w = e % rc4;
+  const int r = (int)(w / cols4);
+  float4* xp = x + grp * nch * rc4 + w;
+  const float* dp = decay ? decay + grp * nch * rows + r : nullptr;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int it0 = 0; it0 < nch; it0 += kB) {
+    float4 y[kB];
+    float dc[kB];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int it = it0 + u;
+      const int kc = reverse ? nch - 1 - it : it;
+      y[u] = it < nch ? xp[kc * rc4] : make_float4(0.f, 0.f, 0.f, 0.f);
+      dc[u] = (it < nch && dp) ? dp[(int64_t)kc * rows] : 1.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const int it = it0 + u;
+      if (it < nch) {
+        const int kc = reverse ? nch - 1 - it : it;
+        xp[kc * rc4] = s;
+        s = make_float4(fmaf(dc[u], s.x, y[u].x), fmaf(dc[u], s.y, y[u].y), fmaf(dc[u], s.z, y[u].z),
+                        fmaf(dc[u], s.w, y[u].w));
+      }
+    }
+  }
+}
+
 static unsigned grid_each(int64_t n) { return (unsigned)((n + 255) / 256); }
 
 static hxm_status fill(const hxm_mlstm_bwd_args* a, Params& p, const char* who) {
@@ -228,7 +264,12 @@ extern "C" hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* a, void* s
   HXM_REQUIRE(a->x != nullptr, "hxm_chunk_state_scan: x is NULL");
   const int64_t n = a->groups * a->rows * (int64_t)a->cols;
   HXM_REQUIRE(n / 256 < (int64_t)0x7fffffff, "hxm_chunk_state_scan: too many elements (%lld)", (long long)n);
-  mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_each(n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      a->x, a->decay, a->groups, a->nchunks, a->rows, a->cols, a->reverse ? 1 : 0);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a->cols % 4 == 0 && reinterpret_cast<uintptr_t>(a->x) % 16 == 0)
+    mlstm_bwd::chunk_scan4_kernel<<<mlstm_bwd::grid_each(n / 4), 256, 0, st>>>(
+        reinterpret_cast<float4*>(a->x), a->decay, a->groups, a->nchunks, a->rows, a->cols / 4, a->reverse ? 1 : 0);
+  else
+    mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_each(n), 256, 0, st>>>(a->x, a->decay, a->groups, a->nchunks,
+                                                                          a->rows, a->cols, a->reverse ? 1 : 0);
   return check_launch("hxm_chunk_state_scan");
 }

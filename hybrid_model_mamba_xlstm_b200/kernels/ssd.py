@@ -57,7 +57,7 @@ def _dt_eff(dt, dt_bias, dt_softplus):
     return (torch.nn.functional.softplus(z) if dt_softplus else z), z
 
 
-def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False, chunk=64):
+def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False, chunk=64, tf32=None):
     """Gradients of y = ssd_chunk_scan(x, dt, A, B, C, D, dt_bias, dt_softplus)
     from a zero state, for dy (B, L, H, P).  Returns fp32
     (dx, ddt, dA, dB, dC, dD, ddt_bias) (dD / ddt_bias None when D / dt_bias are).
@@ -68,15 +68,17 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False
     per-head mLSTM path (exact decay matrix, chunk-state scans on the GPU,
     batched fp32 chunk GEMMs) gives dq, dk, dv, dL/di and dL/dlog f; then
     ddt = dL/di + A dL/dlog f, dA = sum dt dL/dlog f, the shared B, C sum
-    over heads, and softplus / bias chain on."""
-    from .tfla.tfla_bwd import _bwd_heads
+    over heads, and softplus / bias chain on.  tf32: chunk GEMMs on TF32
+    tensor cores (default when x is bf16, as from the bf16 forward) or in full
+    fp32."""
+    from .tfla.tfla_bwd import _bwd_heads, _gemm_precision
     who = "ssd_chunk_scan_bwd"
     dev = require_cuda(x, dt, A, B, C, D, dy, dt_bias, who=who)
     bsz, L, nh, p = x.shape
     n = B.shape[-1]
     de, z = _dt_eff(dt, dt_bias, dt_softplus)                      # (B, L, H)
     Af = A.float()
-    with torch.no_grad():
+    with torch.no_grad(), _gemm_precision(x.dtype == torch.bfloat16 if tf32 is None else tf32):
         q = C.float().unsqueeze(1).expand(bsz, nh, L, n)
         k = B.float().unsqueeze(1).expand(bsz, nh, L, n)
         v = x.float().permute(0, 2, 1, 3)

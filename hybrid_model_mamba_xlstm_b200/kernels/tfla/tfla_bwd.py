@@ -38,12 +38,26 @@ about -170 per channel for 64-step chunks.
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 
 from ... import _lib
 from .._common import dtype_code, ptr, require_cuda, stream_of
 
 __all__ = ["mlstm_chunkwise_bwd"]
+
+
+@contextlib.contextmanager
+def _gemm_precision(tf32: bool):
+    """fp32 chunk GEMMs on the TF32 tensor-core path (10-bit operands, fp32
+    accumulation) while the block runs; restores the caller's setting."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = bool(tf32)
+    try:
+        yield
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 def _scan(x, decay, reverse, stream):
@@ -144,7 +158,7 @@ def _bwd_heads(q, k, v, li, lf, dout, c, normalize, per_channel_out, st):
     return un(dQ), un(dk), un(dVa)[..., :dv], dli, dlf, di
 
 
-def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grads: str = "auto"):
+def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grads: str = "auto", tf32=None):
     """Gradients of h = mLSTM(q, k, v, log_i, log_f) from a zero state.
 
     q, k (B, H, L, Dqk), v (B, H, L, Dv) bf16 or fp32; log_i, log_f fp32 per
@@ -152,7 +166,9 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     fp32 (dq, dk, dv, dlog_i, dlog_f, di): di is the gradient for the gate
     value i = exp(log_i), formed without dividing by i.  Gate gradients are
     per head for per-head gates unless gate_grads="channel" (the per-channel
-    values, e.g. for gates given as expanded (B, H, L, Dqk) views).
+    values, e.g. for gates given as expanded (B, H, L, Dqk) views).  tf32:
+    chunk GEMMs on TF32 tensor cores (default: when q is bf16, whose own
+    rounding is coarser; relative gradient error ~1e-3) or in full fp32.
     """
     who = "mlstm_chunkwise_bwd"
     dev = require_cuda(q, k, v, log_i, log_f, dh, who=who)
@@ -180,8 +196,18 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
         gi, gf = unit(gi), unit(gf)
     c = int(chunk)
     st = stream_of(dev)
-    if gate_mode == 0:
-        return _bwd_heads(q, k, v, gi, gf, dh, c, True, per_channel_out, st)
+    with _gemm_precision(io == torch.bfloat16 if tf32 is None else tf32):
+        if gate_mode == 0:
+            return _bwd_heads(q, k, v, gi, gf, dh, c, True, per_channel_out, st)
+        return _bwd_channels(q, k, v, gi, gf, dh, c, st)
+
+
+def _bwd_channels(q, k, v, gi, gf, dh, c, st):
+    """Per-channel gates: the separable chunk scaling of hxm_mlstm_bwd_prepare."""
+    bsz, nh, L, dqk = q.shape
+    dv = v.shape[-1]
+    dev = q.device
+    f32 = dict(device=dev, dtype=torch.float32)
     nch = (L + c - 1) // c
     Lp = nch * c
 
@@ -189,7 +215,7 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     ks = torch.empty_like(qs)
     rho, erho, eg = (torch.empty(bsz, nh, nch, dqk, **f32) for _ in range(3))
     a = _lib.MlstmBwdArgs()
-    a.batch, a.heads, a.seqlen, a.dqk, a.chunk, a.gate_mode = bsz, nh, L, dqk, c, gate_mode
+    a.batch, a.heads, a.seqlen, a.dqk, a.chunk, a.gate_mode = bsz, nh, L, dqk, c, 1
     a.io_dtype = dtype_code(q)
     a.q, a.q_stride = ptr(q), q.stride()[:3]
     a.k, a.k_stride = ptr(k), k.stride()[:3]

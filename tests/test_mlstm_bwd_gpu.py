@@ -5,7 +5,7 @@ tfla_forward_pytorch (:84-139) under autograd; the check here does the same in
 float64 on the same inputs and compares every gradient of apply_tfla (q, k, v,
 i_gate, f_gate).  Tolerances (normwise relative error): fp32 I/O 1e-4 (fp32
 chunk GEMMs and state); bf16 I/O 2e-2 against the loop on the bf16-rounded
-inputs.
+inputs (TF32 chunk GEMMs, ~1e-3).
 """
 import ctypes as ct
 import math
@@ -134,23 +134,40 @@ def test_log_gate_entry_per_head_sums(T):
 
 
 def test_chunk_state_scan_forward_and_reverse(T):
-    """hxm_chunk_state_scan through the C ABI vs a host loop, with and without decay."""
+    """hxm_chunk_state_scan through the C ABI vs a host loop, with and without
+    decay, on the scalar path (9 columns) and the 16-byte path (8 columns)."""
     from hybrid_model_mamba_xlstm_b200 import _lib
     g = torch.Generator().manual_seed(4)
-    x = torch.randn(2, 3, 5, 7, 9, generator=g)
-    dec = torch.rand(2, 3, 5, 7, generator=g)
-    for reverse in (0, 1):
-        for use_decay in (True, False):
-            xd = x.clone().cuda()
-            dd = dec.cuda() if use_decay else None
-            a = _lib.ChunkScanArgs()
-            a.groups, a.nchunks, a.rows, a.cols = 6, 5, 7, 9
-            a.x, a.decay, a.reverse = xd.data_ptr(), None if dd is None else dd.data_ptr(), reverse
-            _lib.call("hxm_chunk_state_scan", a, torch.cuda.current_stream().cuda_stream)
-            want = torch.empty_like(x)
-            s = torch.zeros(2, 3, 7, 9)
-            order = range(4, -1, -1) if reverse else range(5)
-            for kc in order:
-                want[:, :, kc] = s
-                s = (dec[:, :, kc, :, None] if use_decay else 1.0) * s + x[:, :, kc]
-            assert torch.allclose(xd.cpu(), want, rtol=1e-6, atol=1e-6), (reverse, use_decay)
+    for cols in (9, 8):
+        x = torch.randn(2, 3, 5, 7, cols, generator=g)
+        dec = torch.rand(2, 3, 5, 7, generator=g)
+        for reverse in (0, 1):
+            for use_decay in (True, False):
+                xd = x.clone().cuda()
+                dd = dec.cuda() if use_decay else None
+                a = _lib.ChunkScanArgs()
+                a.groups, a.nchunks, a.rows, a.cols = 6, 5, 7, cols
+                a.x, a.decay, a.reverse = xd.data_ptr(), None if dd is None else dd.data_ptr(), reverse
+                _lib.call("hxm_chunk_state_scan", a, torch.cuda.current_stream().cuda_stream)
+                want = torch.empty_like(x)
+                s = torch.zeros(2, 3, 7, cols)
+                order = range(4, -1, -1) if reverse else range(5)
+                for kc in order:
+                    want[:, :, kc] = s
+                    s = (dec[:, :, kc, :, None] if use_decay else 1.0) * s + x[:, :, kc]
+                assert torch.allclose(xd.cpu(), want, rtol=1e-6, atol=1e-6), (cols, reverse, use_decay)
+
+
+def test_bf16_tf32_gemms_close_to_fp32_gemms(T):
+    """The bf16 default (TF32 chunk GEMMs) against tf32=False on the same
+    inputs, per-channel and per-head gates: every gradient within 5e-3."""
+    for pc in (True, False):
+        q, k, v, ig, fg, dh = (t.cuda() for t in _case((2, 2, 256, 128), 128, pc, 0.0, seed=17,
+                                                        dtype=torch.bfloat16))
+        li, lf = torch.log(ig), torch.log(fg)
+        if not pc:
+            li, lf = li[..., 0], lf[..., 0]
+        fast = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh)
+        full = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, tf32=False)
+        for a, b in zip(fast, full):
+            assert rel_err(_d64(a).numpy(), _d64(b).numpy()) < 5e-3, pc
