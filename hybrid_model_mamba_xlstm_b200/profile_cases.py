@@ -13,6 +13,7 @@ cases (default sizes):
   ssd          B L H P N         (8 4096 32 64 128)
   mlstm        B H L D chunk     (8 8 2048 256 128)  per-head gates
   mlstm_stream B H L D           (8 4 2048 512)   per-channel gates (key-streaming kernel)
+  mlstm_bwd    B H L D           (8 4 2048 512)   chunkwise backward, per-channel gates, bf16 (TF32 chunk GEMMs)
   slstm        B L H HD          (8 256 4 256)    recurrent R
   conv         B D L             (8 4096 2048)    causal depthwise conv1d(4) + SiLU
   mamba_layer  B L               (8 2048)         one hybrid-350M Mamba block
@@ -130,6 +131,17 @@ def main(argv=None):
             pg = Lyr.PrefillGraph(model, B, L, pieces=pieces, device=dev)
         fn = lambda: pg(ids)  # noqa: E731
         extra = {"tokens": B * L, "pieces": pieces}
+    elif a.case == "mlstm_bwd":
+        # chunkwise mLSTM backward, per-channel gates (mLSTMBlock), bf16 q / k / v
+        from .kernels.tfla.tfla_bwd import mlstm_chunkwise_bwd
+        B, H, L, D = (s + [8, 4, 2048, 512][len(s):])[:4]
+        g = torch.Generator(device=dev).manual_seed(0)
+        q, k, v, dh = (torch.randn(B, H, L, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(4))
+        q.mul_(D ** -0.5)
+        li = torch.randn(B, H, L, D, generator=g, device=dev).mul_(0.5)
+        lf = torch.nn.functional.logsigmoid(torch.randn(B, H, L, D, generator=g, device=dev))
+        fn = lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh)  # noqa: E731
+        extra = {"chunk": 64}
     elif a.case == "decode":
         from . import layers as Lyr
         B, P = (s + [1, 512][len(s):])[:2]
