@@ -155,6 +155,7 @@ class MlstmBwdArgs(ct.Structure):
         ("log_f", ct.c_void_p), ("f_stride", _i64x3),
         ("q_scaled", ct.c_void_p), ("k_scaled", ct.c_void_p),
         ("rho", ct.c_void_p), ("e_rho", ct.c_void_p), ("e_g", ct.c_void_p),
+        ("q_decayed", ct.c_void_p), ("k_decayed", ct.c_void_p),
         ("dq_scaled", ct.c_void_p), ("dk_scaled", ct.c_void_p),
         ("chunk_dg", ct.c_void_p),
         ("dq", ct.c_void_p), ("dk", ct.c_void_p), ("dlog_i", ct.c_void_p), ("dlog_f", ct.c_void_p),
@@ -169,6 +170,29 @@ class ChunkScanArgs(ct.Structure):
         ("nchunks", ct.c_int32), ("rows", ct.c_int32), ("cols", ct.c_int32),
         ("x", ct.c_void_p), ("decay", ct.c_void_p),
         ("reverse", ct.c_int32),
+        ("scale", ct.c_void_p), ("scaled", ct.c_void_p),
+    ]
+
+
+class ChunkDotArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("groups", ct.c_int64),
+        ("nchunks", ct.c_int32), ("rows", ct.c_int32), ("cols", ct.c_int32),
+        ("adj", ct.c_void_p), ("state", ct.c_void_p), ("out", ct.c_void_p),
+    ]
+
+
+class MlstmBwdNormArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("heads", ct.c_int32), ("seqlen", ct.c_int32), ("padded_len", ct.c_int32),
+        ("dv", ct.c_int32), ("width", ct.c_int32),
+        ("normalize", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("outputs", ct.c_void_p),
+        ("dh", ct.c_void_p), ("dh_stride", _i64x3),
+        ("out", ct.c_void_p),
     ]
 
 
@@ -185,6 +209,8 @@ SYMBOLS = {
     "hxm_mlstm_bwd_prepare": (ct.c_int, [ct.POINTER(MlstmBwdArgs), ct.c_void_p]),
     "hxm_mlstm_bwd_finalize": (ct.c_int, [ct.POINTER(MlstmBwdArgs), ct.c_void_p]),
     "hxm_chunk_state_scan": (ct.c_int, [ct.POINTER(ChunkScanArgs), ct.c_void_p]),
+    "hxm_mlstm_bwd_normalizer": (ct.c_int, [ct.POINTER(MlstmBwdNormArgs), ct.c_void_p]),
+    "hxm_chunk_state_dot": (ct.c_int, [ct.POINTER(ChunkDotArgs), ct.c_void_p]),
     "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),
     "hxm_ssd_chunk_scan_fwd": (ct.c_int, [ct.POINTER(SsdArgs), ct.c_void_p]),
     "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),

@@ -39,7 +39,7 @@ struct Params {
   int64_t si[3];
   const float* log_f;
   int64_t sf[3];
-  float *qs, *ks, *rho, *erho, *eg;
+  float *qs, *ks, *rho, *erho, *eg, *qd, *kd;
   const float *dqs, *dks;
   const float* dg;
   float *dq, *dk, *dli, *dlf, *di;
@@ -62,8 +62,9 @@ __global__ void __launch_bounds__(128) prepare_kernel(const Params p) {
   for (int s = 0; s < tn; ++s) g += lf[(int64_t)(t0 + s) * p.sf[2]];
   const float rho = 0.5f * g;
   const int64_t vo = ((int64_t)bh * p.nch + kc) * p.dqk + j;
+  const float erho = expf(rho);
   p.rho[vo] = rho;
-  p.erho[vo] = expf(rho);
+  p.erho[vo] = erho;
   p.eg[vo] = expf(g);
   const int64_t ro = ((int64_t)bh * p.nch + kc) * p.chunk * p.dqk + j;
   float bt = 0.f;
@@ -77,6 +78,8 @@ __global__ void __launch_bounds__(128) prepare_kernel(const Params p) {
     }
     p.qs[ro + (int64_t)s * p.dqk] = qv;
     p.ks[ro + (int64_t)s * p.dqk] = kv;
+    if (p.qd) p.qd[ro + (int64_t)s * p.dqk] = qv * erho;  // q e^b
+    if (p.kd) p.kd[ro + (int64_t)s * p.dqk] = kv * erho;  // i k e^(g - b)
   }
 }
 
@@ -124,6 +127,7 @@ __global__ void __launch_bounds__(128) finalize_kernel(const Params p) {
 // loads of 8 chunks are issued before their dependent updates, so a thread
 // keeps 8 reads in flight instead of one load-store round trip per chunk
 __global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, const float* __restrict__ decay,
+                                                         const float* __restrict__ scale, float* __restrict__ scaled,
                                                          int64_t groups, int nch, int rows, int cols, int reverse) {
   constexpr int kB = 8;
   const int64_t rc = (int64_t)rows * cols;
@@ -132,7 +136,9 @@ __global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, 
   const int64_t grp = e / rc, w = e % rc;
   const int r = (int)(w / cols);
   float* xp = x + grp * nch * rc + w;
+  float* op = scaled ? scaled + grp * nch * rc + w : nullptr;
   const float* dp = decay ? decay + grp * nch * rows + r : nullptr;
+  const float* sp = scale ? scale + grp * nch * rows + r : nullptr;
   float s = 0.f;
   for (int it0 = 0; it0 < nch; it0 += kB) {
     float y[kB], dc[kB];
@@ -149,6 +155,7 @@ __global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, 
       if (it < nch) {
         const int kc = reverse ? nch - 1 - it : it;
         xp[kc * rc] = s;
+        if (op) op[kc * rc] = sp[(int64_t)kc * rows] * s;
         s = dc[u] * s + y[u];
       }
     }
@@ -158,6 +165,7 @@ __global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, 
 // The same with 4 adjacent columns of one row per thread (cols % 4 == 0, x
 // 16-byte aligned): 16-byte loads and stores, one decay load per 4 columns.
 __global__ void __launch_bounds__(256) chunk_scan4_kernel(float4* __restrict__ x, const float* __restrict__ decay,
+                                                          const float* __restrict__ scale, float4* __restrict__ scaled,
                                                           int64_t groups, int nch, int rows, int cols4, int reverse) {
   constexpr int kB = 8;
   const int64_t rc4 = (int64_t)rows * cols4;
@@ -166,7 +174,9 @@ __global__ void __launch_bounds__(256) chunk_scan4_kernel(float4* __restrict__ x
   const int64_t grp = e / rc4, w = e % rc4;
   const int r = (int)(w / cols4);
   float4* xp = x + grp * nch * rc4 + w;
+  float4* op = scaled ? scaled + grp * nch * rc4 + w : nullptr;
   const float* dp = decay ? decay + grp * nch * rows + r : nullptr;
+  const float* sp = scale ? scale + grp * nch * rows + r : nullptr;
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int it0 = 0; it0 < nch; it0 += kB) {
     float4 y[kB];
@@ -184,11 +194,87 @@ __global__ void __launch_bounds__(256) chunk_scan4_kernel(float4* __restrict__ x
       if (it < nch) {
         const int kc = reverse ? nch - 1 - it : it;
         xp[kc * rc4] = s;
+        if (op) {
+          const float f = sp[(int64_t)kc * rows];
+          op[kc * rc4] = make_float4(f * s.x, f * s.y, f * s.z, f * s.w);
+        }
         s = make_float4(fmaf(dc[u], s.x, y[u].x), fmaf(dc[u], s.y, y[u].y), fmaf(dc[u], s.z, y[u].z),
                         fmaf(dc[u], s.w, y[u].w));
       }
     }
   }
+}
+
+// Output-side gradients of one chunk row t (one warp per row): from the chunk
+// outputs [num | den] (width w, fp32) and dh, with D = max(den, 1),
+//   dnum = dh / D,  dden = -[den >= 1] (dnum . num) / D     (normalize)
+//   dnum = dh,      dden = 0                                 (no normalizer)
+// written as [dnum | dden | 0 ...] (width w); rows t >= seqlen are zero.
+template <typename T>
+__global__ void __launch_bounds__(256) normalizer_kernel(const float* __restrict__ numa, const T* __restrict__ dh,
+                                                         int64_t sb, int64_t sh, int64_t st, int heads, int seqlen,
+                                                         int lp, int dv, int w, int normalize, int64_t rows,
+                                                         float* __restrict__ dna) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * 8ll + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int t = (int)(row % lp);
+  const int64_t bh = row / lp;
+  const int b = (int)(bh / heads), h = (int)(bh % heads);
+  const float* nrow = numa + row * w;
+  float* orow = dna + row * w;
+  if (t >= seqlen) {
+    for (int e = lane; e < w; e += 32) orow[e] = 0.f;
+    return;
+  }
+  const T* drow = dh + b * sb + h * sh + (int64_t)t * st;
+  const float den = normalize ? nrow[dv] : 1.f;
+  const float inv = 1.f / fmaxf(den, 1.f);
+  float part = 0.f;
+  for (int e = lane; e < dv; e += 32) {
+    const float g = to_f32<T>(drow[e]) * inv;
+    orow[e] = g;
+    part = fmaf(g, nrow[e], part);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  for (int e = dv + lane; e < w; e += 32)
+    orow[e] = (e == dv && normalize && den >= 1.f) ? -part * inv : 0.f;
+}
+
+// out[g, k, r] = sum_c adj[g, k, r, c] * state[g, k + 1, r, c]  (0 for the last
+// chunk): one warp per (g, k, r) row, 16-byte loads when VEC.
+template <bool VEC>
+__global__ void __launch_bounds__(256) chunk_dot_kernel(const float* __restrict__ adj, const float* __restrict__ state,
+                                                        int64_t groups, int nch, int rows, int cols,
+                                                        float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * 8ll + (threadIdx.x >> 5);
+  if (row >= groups * nch * rows) return;
+  const int r = (int)(row % rows);
+  const int64_t gk = row / rows;
+  const int kc = (int)(gk % nch);
+  const int64_t grp = gk / nch;
+  if (kc == nch - 1) {
+    if (lane == 0) out[row] = 0.f;
+    return;
+  }
+  const float* a = adj + row * cols;
+  const float* x = state + ((grp * nch + kc + 1) * rows + r) * (int64_t)cols;
+  float acc = 0.f;
+  if (VEC) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int c = lane; c < cols / 4; c += 32) {
+      const float4 u = a4[c], v = x4[c];
+      acc = fmaf(u.x, v.x, fmaf(u.y, v.y, fmaf(u.z, v.z, fmaf(u.w, v.w, acc))));
+    }
+  } else {
+    for (int c = lane; c < cols; c += 32) acc = fmaf(a[c], x[c], acc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) out[row] = acc;
 }
 
 static unsigned grid_each(int64_t n) { return (unsigned)((n + 255) / 256); }
@@ -210,6 +296,7 @@ static hxm_status fill(const hxm_mlstm_bwd_args* a, Params& p, const char* who) 
     p.sq[i] = a->q_stride[i]; p.sk[i] = a->k_stride[i]; p.si[i] = a->i_stride[i]; p.sf[i] = a->f_stride[i];
   }
   p.qs = a->q_scaled; p.ks = a->k_scaled; p.rho = a->rho; p.erho = a->e_rho; p.eg = a->e_g;
+  p.qd = a->q_decayed; p.kd = a->k_decayed;
   p.dqs = a->dq_scaled; p.dks = a->dk_scaled; p.dg = a->chunk_dg;
   p.dq = a->dq; p.dk = a->dk; p.dli = a->dlog_i; p.dlf = a->dlog_f; p.di = a->d_i;
   HXM_REQUIRE(p.log_i && p.log_f && p.qs && p.ks && p.rho, "%s: NULL gate or chunk-operand pointer", who);
@@ -262,14 +349,71 @@ extern "C" hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* a, void* s
               a->nchunks, a->rows, a->cols);
   if (a->groups == 0 || a->nchunks == 0) return HXM_OK;
   HXM_REQUIRE(a->x != nullptr, "hxm_chunk_state_scan: x is NULL");
+  HXM_REQUIRE(!a->scaled || a->scale, "hxm_chunk_state_scan: scaled output needs scale");
   const int64_t n = a->groups * a->rows * (int64_t)a->cols;
   HXM_REQUIRE(n / 256 < (int64_t)0x7fffffff, "hxm_chunk_state_scan: too many elements (%lld)", (long long)n);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (a->cols % 4 == 0 && reinterpret_cast<uintptr_t>(a->x) % 16 == 0)
+  if (a->cols % 4 == 0 && reinterpret_cast<uintptr_t>(a->x) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(a->scaled) % 16 == 0)
     mlstm_bwd::chunk_scan4_kernel<<<mlstm_bwd::grid_each(n / 4), 256, 0, st>>>(
-        reinterpret_cast<float4*>(a->x), a->decay, a->groups, a->nchunks, a->rows, a->cols / 4, a->reverse ? 1 : 0);
+        reinterpret_cast<float4*>(a->x), a->decay, a->scale, reinterpret_cast<float4*>(a->scaled), a->groups,
+        a->nchunks, a->rows, a->cols / 4, a->reverse ? 1 : 0);
   else
-    mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_each(n), 256, 0, st>>>(a->x, a->decay, a->groups, a->nchunks,
-                                                                          a->rows, a->cols, a->reverse ? 1 : 0);
+    mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_each(n), 256, 0, st>>>(
+        a->x, a->decay, a->scale, a->scaled, a->groups, a->nchunks, a->rows, a->cols, a->reverse ? 1 : 0);
   return check_launch("hxm_chunk_state_scan");
+}
+
+extern "C" hxm_status hxm_mlstm_bwd_normalizer(const hxm_mlstm_bwd_norm_args* a, void* stream) {
+  using namespace hxm;
+  clear_error();
+  HXM_REQUIRE(a != nullptr, "hxm_mlstm_bwd_normalizer: args is NULL");
+  HXM_REQUIRE(a->struct_size == sizeof(hxm_mlstm_bwd_norm_args), "hxm_mlstm_bwd_normalizer: struct_size %zu != %zu",
+              a->struct_size, sizeof(hxm_mlstm_bwd_norm_args));
+  HXM_REQUIRE(a->batch >= 0 && a->heads >= 1 && a->seqlen >= 0 && a->padded_len >= a->seqlen && a->dv >= 1 &&
+                  a->width >= a->dv + (a->normalize ? 1 : 0),
+              "hxm_mlstm_bwd_normalizer: bad sizes batch=%d heads=%d seqlen=%d padded_len=%d dv=%d width=%d",
+              a->batch, a->heads, a->seqlen, a->padded_len, a->dv, a->width);
+  HXM_REQUIRE(a->io_dtype == HXM_F32 || a->io_dtype == HXM_BF16, "hxm_mlstm_bwd_normalizer: io_dtype must be f32 or bf16");
+  const int64_t rows = (int64_t)a->batch * a->heads * a->padded_len;
+  if (rows == 0) return HXM_OK;
+  HXM_REQUIRE(a->out && a->dh && (a->outputs || !a->normalize), "hxm_mlstm_bwd_normalizer: NULL pointer");
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float* numa = a->normalize ? a->outputs : a->out;  // unread without the normalizer
+  if (a->io_dtype == HXM_F32)
+    mlstm_bwd::normalizer_kernel<float><<<grid, 256, 0, st>>>(
+        numa, static_cast<const float*>(a->dh), a->dh_stride[0], a->dh_stride[1], a->dh_stride[2], a->heads,
+        a->seqlen, a->padded_len, a->dv, a->width, a->normalize ? 1 : 0, rows, a->out);
+  else
+    mlstm_bwd::normalizer_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        numa, static_cast<const __nv_bfloat16*>(a->dh), a->dh_stride[0], a->dh_stride[1], a->dh_stride[2], a->heads,
+        a->seqlen, a->padded_len, a->dv, a->width, a->normalize ? 1 : 0, rows, a->out);
+  return check_launch("hxm_mlstm_bwd_normalizer");
+}
+
+extern "C" hxm_status hxm_chunk_state_dot(const hxm_chunk_dot_args* a, void* stream) {
+  using namespace hxm;
+  clear_error();
+  HXM_REQUIRE(a != nullptr, "hxm_chunk_state_dot: args is NULL");
+  HXM_REQUIRE(a->struct_size == sizeof(hxm_chunk_dot_args), "hxm_chunk_state_dot: struct_size %zu != %zu",
+              a->struct_size, sizeof(hxm_chunk_dot_args));
+  HXM_REQUIRE(a->groups >= 0 && a->nchunks >= 0 && a->rows >= 1 && a->cols >= 1,
+              "hxm_chunk_state_dot: bad sizes groups=%lld nchunks=%d rows=%d cols=%d", (long long)a->groups,
+              a->nchunks, a->rows, a->cols);
+  const int64_t nrows = a->groups * a->nchunks * (int64_t)a->rows;
+  if (nrows == 0) return HXM_OK;
+  HXM_REQUIRE(a->adj && a->state && a->out, "hxm_chunk_state_dot: NULL pointer");
+  HXM_REQUIRE((nrows + 7) / 8 < (int64_t)0x7fffffff, "hxm_chunk_state_dot: too many rows (%lld)", (long long)nrows);
+  const unsigned grid = (unsigned)((nrows + 7) / 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool vec = a->cols % 4 == 0 && reinterpret_cast<uintptr_t>(a->adj) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a->state) % 16 == 0;
+  if (vec)
+    mlstm_bwd::chunk_dot_kernel<true><<<grid, 256, 0, st>>>(a->adj, a->state, a->groups, a->nchunks, a->rows, a->cols,
+                                                            a->out);
+  else
+    mlstm_bwd::chunk_dot_kernel<false><<<grid, 256, 0, st>>>(a->adj, a->state, a->groups, a->nchunks, a->rows,
+                                                             a->cols, a->out);
+  return check_launch("hxm_chunk_state_dot");
 }

@@ -60,21 +60,43 @@ def _gemm_precision(tf32: bool):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-def _scan(x, decay, reverse, stream):
+def _scan(x, decay, reverse, stream, scale=None, scaled=None):
     a = _lib.ChunkScanArgs()
     a.groups, a.nchunks, a.rows, a.cols = x.shape[0] * x.shape[1], x.shape[2], x.shape[3], x.shape[4]
     a.x, a.decay, a.reverse = ptr(x), ptr(decay), int(reverse)
+    a.scale, a.scaled = ptr(scale), ptr(scaled)
     _lib.call("hxm_chunk_state_scan", a, stream)
 
 
-def _chunk_dg(Y, X, dims):
-    """<adjoint leaving chunk k, state leaving chunk k> = <Y_k, X_{k+1}> summed
-    over dims (0 for the last chunk, whose adjoint is zero)."""
-    out = torch.zeros(*Y.shape[:3], *[Y.shape[i] for i in range(3, Y.dim()) if i - Y.dim() not in dims],
-                      device=Y.device, dtype=Y.dtype)
-    if Y.shape[2] > 1:
-        out[:, :, :-1] = (Y[:, :, :-1] * X[:, :, 1:]).sum(dims)
+def _out_grads(numa, dh, lp, w, normalize, st):
+    """[dnum | dden | 0 ...] per chunk row (hxm_mlstm_bwd_normalizer): dh over
+    max(den, 1) and the clamp branch's dden, or dh alone without the
+    normalizer; zero rows past the sequence."""
+    bsz, nh, L, dv = dh.shape
+    if dh.dtype not in (torch.float32, torch.bfloat16):
+        dh = dh.float()
+    if dh.stride(-1) != 1:
+        dh = dh.contiguous()
+    out = torch.empty(bsz, nh, lp, w, device=dh.device, dtype=torch.float32)
+    a = _lib.MlstmBwdNormArgs()
+    a.batch, a.heads, a.seqlen, a.padded_len, a.dv, a.width = bsz, nh, L, lp, dv, w
+    a.normalize, a.io_dtype = int(bool(normalize)), dtype_code(dh)
+    a.outputs, a.out = ptr(numa), ptr(out)
+    a.dh, a.dh_stride = ptr(dh), dh.stride()[:3]
+    _lib.call("hxm_mlstm_bwd_normalizer", a, st)
     return out
+
+
+def _chunk_dg(Y, X, dims):
+    """<adjoint leaving chunk k, state leaving chunk k> = <Y_k, X_{k+1}> per
+    key row (hxm_chunk_state_dot; 0 for the last chunk, whose adjoint is zero),
+    summed over the rows too when dims covers them."""
+    out = torch.empty(Y.shape[:4], device=Y.device, dtype=torch.float32)
+    a = _lib.ChunkDotArgs()
+    a.groups, a.nchunks, a.rows, a.cols = Y.shape[0] * Y.shape[1], Y.shape[2], Y.shape[3], Y.shape[4]
+    a.adj, a.state, a.out = ptr(Y), ptr(X), ptr(out)
+    _lib.call("hxm_chunk_state_dot", a, stream_of(Y.device))
+    return out.sum(-1) if -2 in dims else out
 
 
 def _bwd_heads(q, k, v, li, lf, dout, c, normalize, per_channel_out, st):
@@ -116,19 +138,9 @@ def _bwd_heads(q, k, v, li, lf, dout, c, normalize, per_channel_out, st):
     S = torch.matmul(Q, Kp.transpose(-1, -2)).mul_(Lm)
     Qe = Q * eb
     QX = torch.matmul(Qe, X)
-    numa = QX + torch.matmul(S, Vc)
-    dHc = torch.zeros(bsz, nh, Lp, dv, **f32)
-    dHc[:, :, :L] = dout
-    dHc = dHc.view(bsz, nh, nch, c, dv)
-    dNa = torch.zeros(bsz, nh, nch, c, w, **f32)
-    if normalize:
-        num, den = numa[..., :dv], numa[..., dv]
-        Dm = den.clamp(min=1.0)
-        dnum = dHc / Dm.unsqueeze(-1)
-        dNa[..., :dv] = dnum
-        dNa[..., dv] = -(den >= 1.0).float() * (dnum * num).sum(-1) / Dm
-    else:
-        dNa[..., :dv] = dHc
+    numa = QX + torch.matmul(S, Vc) if normalize else None
+    dNa = _out_grads(numa, dout, Lp, w, normalize, st).view(bsz, nh, nch, c, w)
+    del numa
     Y = torch.matmul(Qe.transpose(-1, -2), dNa)  # increments -> adjoints leaving each chunk
     _scan(Y, eg, True, st)
     dSf = torch.matmul(dNa, Vc.transpose(-1, -2))  # dL/dS
@@ -211,8 +223,7 @@ def _bwd_channels(q, k, v, gi, gf, dh, c, st):
     nch = (L + c - 1) // c
     Lp = nch * c
 
-    qs = torch.empty(bsz, nh, Lp, dqk, **f32)
-    ks = torch.empty_like(qs)
+    qs, ks, qd, kd = (torch.empty(bsz, nh, Lp, dqk, **f32) for _ in range(4))
     rho, erho, eg = (torch.empty(bsz, nh, nch, dqk, **f32) for _ in range(3))
     a = _lib.MlstmBwdArgs()
     a.batch, a.heads, a.seqlen, a.dqk, a.chunk, a.gate_mode = bsz, nh, L, dqk, c, 1
@@ -222,40 +233,38 @@ def _bwd_channels(q, k, v, gi, gf, dh, c, st):
     a.log_i, a.i_stride = ptr(gi), gi.stride()[:3]
     a.log_f, a.f_stride = ptr(gf), gf.stride()[:3]
     a.q_scaled, a.k_scaled, a.rho, a.e_rho, a.e_g = ptr(qs), ptr(ks), ptr(rho), ptr(erho), ptr(eg)
+    a.q_decayed, a.k_decayed = ptr(qd), ptr(kd)
     _lib.call("hxm_mlstm_bwd_prepare", a, st)
 
     Qc = qs.view(bsz, nh, nch, c, dqk)
     Kc = ks.view(bsz, nh, nch, c, dqk)
-    er = erho.unsqueeze(-2)  # (B, H, nch, 1, Dqk)
+    Qr = qd.view(bsz, nh, nch, c, dqk)  # e^rho Qs = q e^b
+    Kr = kd.view(bsz, nh, nch, c, dqk)  # e^rho Ks = i k e^(g - b)
     w = (dv + 1 + 7) // 8 * 8  # [v | 1 | 0 ...]: rows of 32-byte multiples for the GEMMs
     va = torch.zeros(bsz, nh, Lp, w, **f32)
     va[:, :, :L, :dv] = v
     va[..., dv] = 1.0
     Vc = va.view(bsz, nh, nch, c, w)
-    dhp = torch.zeros(bsz, nh, Lp, dv, **f32)
-    dhp[:, :, :L] = dh
-    dHc = dhp.view(bsz, nh, nch, c, dv)
 
-    Kr = Kc * er
-    X = torch.matmul(Kr.transpose(-1, -2), Vc)  # increments -> states entering each chunk
-    _scan(X, eg, False, st)
+    # states entering each chunk X (for dg) and their e^rho row-scaled copy Xs (for the GEMMs)
+    X = torch.matmul(Kr.transpose(-1, -2), Vc)
+    Xs = torch.empty_like(X)
+    _scan(X, eg, False, st, erho, Xs)
     causal = torch.ones(c, c, device=dev, dtype=torch.bool).tril_()
     S = torch.matmul(Qc, Kc.transpose(-1, -2)).masked_fill_(~causal, 0.0)
-    Qr = Qc * er
-    numa = torch.matmul(Qr, X).add_(torch.matmul(S, Vc))
-    num, den = numa[..., :dv], numa[..., dv]
-    Dm = den.clamp(min=1.0)
-    dnum = dHc / Dm.unsqueeze(-1)
-    dden = -(den >= 1.0).float() * (dnum * num).sum(-1) / Dm
-    dNa = torch.zeros(bsz, nh, nch, c, w, **f32)
-    dNa[..., :dv] = dnum
-    dNa[..., dv] = dden
-    Y = torch.matmul(Qr.transpose(-1, -2), dNa)  # increments -> adjoints leaving each chunk
-    _scan(Y, eg, True, st)
+    numa = torch.matmul(Qc, Xs).add_(torch.matmul(S, Vc))
+    dNa = _out_grads(numa, dh, Lp, w, True, st).view(bsz, nh, nch, c, w)
+    del numa
+    # adjoints leaving each chunk Y and their e^rho row-scaled copy Ys
+    Y = torch.matmul(Qr.transpose(-1, -2), dNa)
+    Ys = torch.empty_like(Y)
+    _scan(Y, eg, True, st, erho, Ys)
     dS = torch.matmul(dNa, Vc.transpose(-1, -2)).masked_fill_(~causal, 0.0)
-    dQs = torch.matmul(dS, Kc).add_(er * torch.matmul(dNa, X.transpose(-1, -2)))
-    dKs = torch.matmul(dS.transpose(-1, -2), Qc).add_(er * torch.matmul(Vc, Y.transpose(-1, -2)))
-    dVa = torch.matmul(S.transpose(-1, -2), dNa).add_(torch.matmul(Kr, Y))
+    dQs = torch.matmul(dS, Kc).add_(torch.matmul(dNa, Xs.transpose(-1, -2)))
+    del Xs
+    dKs = torch.matmul(dS.transpose(-1, -2), Qc).add_(torch.matmul(Vc, Ys.transpose(-1, -2)))
+    dVa = torch.matmul(S.transpose(-1, -2), dNa).add_(torch.matmul(Kc, Ys))
+    del Ys
     dv_out = dVa.view(bsz, nh, Lp, w)[:, :, :L, :dv]
 
     dg = _chunk_dg(Y, X, (-1,))

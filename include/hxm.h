@@ -212,6 +212,8 @@ typedef struct hxm_mlstm_bwd_args {
   const float* log_f; int64_t f_stride[3];
   float* q_scaled; float* k_scaled;
   float* rho; float* e_rho; float* e_g;
+  float* q_decayed; float* k_decayed;  /* prepare, optional (NULL = skip):    */
+                            /* q e^b and k e^(log_i + g - b), layout of q_scaled */
   const float* dq_scaled; const float* dk_scaled;
   const float* chunk_dg;
   float* dq; float* dk; float* dlog_i; float* dlog_f;
@@ -221,12 +223,36 @@ typedef struct hxm_mlstm_bwd_args {
 hxm_status hxm_mlstm_bwd_prepare(const hxm_mlstm_bwd_args* args, void* stream);
 hxm_status hxm_mlstm_bwd_finalize(const hxm_mlstm_bwd_args* args, void* stream);
 
+/* Output-side gradients of the chunkwise backward, one row per step t of    */
+/* each (b, h), t < padded_len (seqlen rounded up to whole chunks):          */
+/*   normalize: dnum = dh / max(den, 1), dden = -[den >= 1] dnum . num /     */
+/*              max(den, 1), from outputs[row] = [num (dv) | den | ...];     */
+/*   else:      dnum = dh, dden = 0;                                         */
+/* written as out[row] = [dnum | dden | 0 ...] (width floats; zero rows past */
+/* seqlen).  outputs, out: (b, h, padded_len, width) fp32 dense; dh          */
+/* (b, h, t) element strides, dense dv, io dtype.  Replaces the clamp branch */
+/* of the reference's recompute-under-autograd backward (tfla_interface.py: */
+/* 52-81 differentiating :133-137).                                          */
+typedef struct hxm_mlstm_bwd_norm_args {
+  size_t struct_size;
+  int32_t batch, heads, seqlen, padded_len, dv, width;
+  int32_t normalize;
+  hxm_dtype io_dtype;       /* dh                                            */
+  const float* outputs;
+  const void* dh; int64_t dh_stride[3];
+  float* out;
+} hxm_mlstm_bwd_norm_args;
+
+hxm_status hxm_mlstm_bwd_normalizer(const hxm_mlstm_bwd_norm_args* args, void* stream);
+
 /* Exclusive chunk-level recurrence, in place, for the chunkwise backward:   */
 /* per group and element (r, c), s = 0 and for each chunk k in order         */
 /* (reverse = 0) or in reverse (reverse = 1):                                 */
 /*   y = x[k, r, c];  x[k, r, c] = s;  s = decay[k, r] * s + y               */
 /* so x becomes the states entering each chunk (forward) or the adjoints     */
-/* leaving each chunk (reverse).  x (groups, nchunks, rows, cols), decay     */
+/* leaving each chunk (reverse); with `scaled`, also the row-scaled copy     */
+/* scaled[k, r, c] = scale[k, r] * x[k, r, c] of the output.                 */
+/* x (groups, nchunks, rows, cols), decay                                    */
 /* (groups, nchunks, rows) or NULL (= 1), fp32 dense.  No reference          */
 /* counterpart: the reference's backward has no chunk states.                */
 typedef struct hxm_chunk_scan_args {
@@ -236,9 +262,28 @@ typedef struct hxm_chunk_scan_args {
   float* x;
   const float* decay;
   int32_t reverse;
+  const float* scale;       /* (groups, nchunks, rows) or NULL              */
+  float* scaled;            /* layout of x, or NULL: scale[k, r] * x_out[k] */
 } hxm_chunk_scan_args;
 
 hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* args, void* stream);
+
+/* Per chunk and row, the inner product of the adjoint leaving the chunk     */
+/* with the state leaving it (the state entering the next chunk):            */
+/*   out[g, k, r] = sum_c adj[g, k, r, c] * state[g, k + 1, r, c],           */
+/* 0 for the last chunk: the gradient for the chunk's total log forget gate  */
+/* (chunk_dg of hxm_mlstm_bwd_finalize).  adj, state (groups, nchunks, rows, */
+/* cols), out (groups, nchunks, rows), fp32 dense.  No reference counterpart.*/
+typedef struct hxm_chunk_dot_args {
+  size_t struct_size;
+  int64_t groups;
+  int32_t nchunks, rows, cols;
+  const float* adj;
+  const float* state;
+  float* out;
+} hxm_chunk_dot_args;
+
+hxm_status hxm_chunk_state_dot(const hxm_chunk_dot_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* 3. Mamba-2 SSD chunked scan (ngroups = 1)                                  */

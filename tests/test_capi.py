@@ -42,7 +42,8 @@ def test_struct_sizes_match_header_layout():
                     (_lib.ConvArgs, "hxm_causal_conv1d_fwd"), (_lib.RmsnormArgs, "hxm_rmsnorm_fwd"),
                     (_lib.MlstmGatesArgs, "hxm_mlstm_gate_prologue"), (_lib.MlstmGatesArgs, "hxm_mlstm_gate_epilogue"),
                     (_lib.ScanBwdArgs, "hxm_selective_scan_bwd"), (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_prepare"),
-                    (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_finalize"), (_lib.ChunkScanArgs, "hxm_chunk_state_scan")]:
+                    (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_finalize"), (_lib.ChunkScanArgs, "hxm_chunk_state_scan"),
+                    (_lib.MlstmBwdNormArgs, "hxm_mlstm_bwd_normalizer"), (_lib.ChunkDotArgs, "hxm_chunk_state_dot")]:
         a = cls()
         a.struct_size = ct.sizeof(a) + 8
         st = getattr(_lib.lib(), fn)(ct.byref(a), None)
@@ -112,3 +113,12 @@ def test_mlstm_backward_entries_validate_without_cuda():
     assert b"rows=0" in lib.hxm_last_error_string()
     s.rows, s.groups = 2, 0
     assert lib.hxm_chunk_state_scan(ct.byref(s), None) == _lib.HXM_OK
+    n = _lib.MlstmBwdNormArgs()
+    n.struct_size = ct.sizeof(n)
+    n.batch, n.heads, n.seqlen, n.padded_len, n.dv, n.width, n.normalize = 1, 1, 8, 4, 4, 8, 1
+    assert lib.hxm_mlstm_bwd_normalizer(ct.byref(n), None) == _lib.HXM_EBADARG  # padded_len < seqlen
+    assert b"padded_len=4" in lib.hxm_last_error_string()
+    n.padded_len, n.width = 8, 4  # no room for the den column
+    assert lib.hxm_mlstm_bwd_normalizer(ct.byref(n), None) == _lib.HXM_EBADARG
+    n.width, n.batch = 8, 0
+    assert lib.hxm_mlstm_bwd_normalizer(ct.byref(n), None) == _lib.HXM_OK

@@ -135,12 +135,14 @@ def test_log_gate_entry_per_head_sums(T):
 
 def test_chunk_state_scan_forward_and_reverse(T):
     """hxm_chunk_state_scan through the C ABI vs a host loop, with and without
-    decay, on the scalar path (9 columns) and the 16-byte path (8 columns)."""
+    decay (and with the row-scaled copy of the output), on the scalar path
+    (9 columns) and the 16-byte path (8 columns)."""
     from hybrid_model_mamba_xlstm_b200 import _lib
     g = torch.Generator().manual_seed(4)
     for cols in (9, 8):
         x = torch.randn(2, 3, 5, 7, cols, generator=g)
         dec = torch.rand(2, 3, 5, 7, generator=g)
+        scl = torch.rand(2, 3, 5, 7, generator=g) + 0.5
         for reverse in (0, 1):
             for use_decay in (True, False):
                 xd = x.clone().cuda()
@@ -148,6 +150,9 @@ def test_chunk_state_scan_forward_and_reverse(T):
                 a = _lib.ChunkScanArgs()
                 a.groups, a.nchunks, a.rows, a.cols = 6, 5, 7, cols
                 a.x, a.decay, a.reverse = xd.data_ptr(), None if dd is None else dd.data_ptr(), reverse
+                sc, out = (scl.cuda(), torch.empty_like(xd)) if use_decay else (None, None)
+                if use_decay:
+                    a.scale, a.scaled = sc.data_ptr(), out.data_ptr()
                 _lib.call("hxm_chunk_state_scan", a, torch.cuda.current_stream().cuda_stream)
                 want = torch.empty_like(x)
                 s = torch.zeros(2, 3, 7, cols)
@@ -156,6 +161,8 @@ def test_chunk_state_scan_forward_and_reverse(T):
                     want[:, :, kc] = s
                     s = (dec[:, :, kc, :, None] if use_decay else 1.0) * s + x[:, :, kc]
                 assert torch.allclose(xd.cpu(), want, rtol=1e-6, atol=1e-6), (cols, reverse, use_decay)
+                if use_decay:
+                    assert torch.allclose(out.cpu(), scl[..., None] * want, rtol=1e-6, atol=1e-6), (cols, reverse)
 
 
 def test_bf16_tf32_gemms_close_to_fp32_gemms(T):
@@ -171,3 +178,20 @@ def test_bf16_tf32_gemms_close_to_fp32_gemms(T):
         full = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, tf32=False)
         for a, b in zip(fast, full):
             assert rel_err(_d64(a).numpy(), _d64(b).numpy()) < 5e-3, pc
+
+
+def test_chunk_state_dot(T):
+    """hxm_chunk_state_dot vs torch: <adj_k, state_{k+1}> per row, 0 for the last chunk."""
+    from hybrid_model_mamba_xlstm_b200 import _lib
+    g = torch.Generator().manual_seed(6)
+    for cols in (9, 8):
+        adj, state = torch.randn(2, 3, 5, 7, cols, generator=g), torch.randn(2, 3, 5, 7, cols, generator=g)
+        out = torch.full((2, 3, 5, 7), float("nan")).cuda()
+        a = _lib.ChunkDotArgs()
+        a.groups, a.nchunks, a.rows, a.cols = 6, 5, 7, cols
+        ad, sd = adj.cuda(), state.cuda()
+        a.adj, a.state, a.out = ad.data_ptr(), sd.data_ptr(), out.data_ptr()
+        _lib.call("hxm_chunk_state_dot", a, torch.cuda.current_stream().cuda_stream)
+        want = torch.zeros(2, 3, 5, 7)
+        want[:, :, :-1] = (adj[:, :, :-1] * state[:, :, 1:]).sum(-1)
+        assert torch.allclose(out.cpu(), want, rtol=1e-5, atol=1e-5), cols
