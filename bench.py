@@ -250,6 +250,16 @@ def secondary_metrics(args, dev, world, rank):
         "gemm_tflops": world * fl / ms / 1e9, "scaling": "weak", "higher_is_better": False,
         "kernels": "hxm mlstm_bwd prepare / chunk_scan / finalize + fp32 cuBLAS chunk GEMMs"}
     del q, k, v, dh, li, lf
+    # SSD backward at the SSD workload's shape (batch 8, 32 heads x 64, dstate 128, seqlen 4096)
+    from hybrid_model_mamba_xlstm_b200.kernels.ssd import ssd_chunk_scan_bwd
+    inp = ssd_inputs(8, 4096, 32, 64, 128, seed=rank, device=dev, on_device=True)
+    dy = torch.randn(8, 4096, 32, 64, generator=g, device=dev).to(torch.bfloat16)
+    ms = _time_cuda(lambda: ssd_chunk_scan_bwd(inp.x, inp.dt, inp.A, inp.B, inp.C, inp.D, dy), min(steps, 3), 2,
+                    dev, world)
+    out["ssd_bwd_b8_h32_p64_n128_l4096"] = {
+        "metric": "SSD backward ms", "value": ms, "unit": "ms", "scaling": "weak", "higher_is_better": False,
+        "kernels": "hxm chunk_scan / normalizer / chunk_dot + TF32 cuBLAS chunk GEMMs (exact per-head chunk form)"}
+    del inp, dy
     torch.cuda.empty_cache()
     out["prefill"] = prefill_metric(args, dev, world, rank)
     return out

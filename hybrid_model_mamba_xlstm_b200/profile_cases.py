@@ -14,6 +14,7 @@ cases (default sizes):
   mlstm        B H L D chunk     (8 8 2048 256 128)  per-head gates
   mlstm_stream B H L D           (8 4 2048 512)   per-channel gates (key-streaming kernel)
   mlstm_bwd    B H L D           (8 4 2048 512)   chunkwise backward, per-channel gates, bf16 (TF32 chunk GEMMs)
+  ssd_bwd      B L H P N         (8 4096 32 64 128)  SSD backward (exact per-head chunk form, TF32 chunk GEMMs)
   slstm        B L H HD          (8 256 4 256)    recurrent R
   conv         B D L             (8 4096 2048)    causal depthwise conv1d(4) + SiLU
   mamba_layer  B L               (8 2048)         one hybrid-350M Mamba block
@@ -142,6 +143,15 @@ def main(argv=None):
         lf = torch.nn.functional.logsigmoid(torch.randn(B, H, L, D, generator=g, device=dev))
         fn = lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh)  # noqa: E731
         extra = {"chunk": 64}
+    elif a.case == "ssd_bwd":
+        # SSD backward (exact per-head chunk form, TF32 chunk GEMMs) for the bf16 forward's inputs
+        from .kernels.ssd import ssd_chunk_scan_bwd
+        from .workloads import ssd_inputs
+        B, L, H, P, N = (s + [8, 4096, 32, 64, 128][len(s):])[:5]
+        inp = ssd_inputs(B, L, H, P, N, seed=0, device="cuda", on_device=True)
+        dy = torch.randn(B, L, H, P, device=dev).to(torch.bfloat16)
+        fn = lambda: ssd_chunk_scan_bwd(inp.x, inp.dt, inp.A, inp.B, inp.C, inp.D, dy)  # noqa: E731
+        extra = {}
     elif a.case == "decode":
         from . import layers as Lyr
         B, P = (s + [1, 512][len(s):])[:2]
