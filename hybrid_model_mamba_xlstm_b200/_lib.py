@@ -174,6 +174,15 @@ class ChunkScanArgs(ct.Structure):
     ]
 
 
+class SsdBwdIntraArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("nchunks", ct.c_int32), ("heads", ct.c_int32), ("chunk", ct.c_int32),
+        ("cb", ct.c_void_p), ("bcum", ct.c_void_p), ("dt", ct.c_void_p), ("dS", ct.c_void_p),
+        ("S", ct.c_void_p), ("M", ct.c_void_p), ("ddt", ct.c_void_p), ("db", ct.c_void_p),
+    ]
+
+
 class ChunkDotArgs(ct.Structure):
     _fields_ = [
         ("struct_size", ct.c_size_t),
@@ -211,6 +220,7 @@ SYMBOLS = {
     "hxm_chunk_state_scan": (ct.c_int, [ct.POINTER(ChunkScanArgs), ct.c_void_p]),
     "hxm_mlstm_bwd_normalizer": (ct.c_int, [ct.POINTER(MlstmBwdNormArgs), ct.c_void_p]),
     "hxm_chunk_state_dot": (ct.c_int, [ct.POINTER(ChunkDotArgs), ct.c_void_p]),
+    "hxm_ssd_bwd_intra": (ct.c_int, [ct.POINTER(SsdBwdIntraArgs), ct.c_void_p]),
     "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),
     "hxm_ssd_chunk_scan_fwd": (ct.c_int, [ct.POINTER(SsdArgs), ct.c_void_p]),
     "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),

@@ -57,6 +57,93 @@ def _dt_eff(dt, dt_bias, dt_softplus):
     return (torch.nn.functional.softplus(z) if dt_softplus else z), z
 
 
+def _intra(cb, bcum, dt, G, st):
+    """hxm_ssd_bwd_intra: (S_h, M, dL/d dt, dL/d b) of the per-head c x c terms."""
+    bsz, nch, c, nh = bcum.shape
+    S = torch.empty_like(G)
+    M = torch.empty_like(cb)
+    ddt, db = (torch.empty(bsz, nch, nh, c, device=G.device, dtype=torch.float32) for _ in range(2))
+    a = _lib.SsdBwdIntraArgs()
+    a.batch, a.nchunks, a.heads, a.chunk = bsz, nch, nh, c
+    a.cb, a.bcum, a.dt, a.dS = ptr(cb), ptr(bcum), ptr(dt), ptr(G)
+    a.S, a.M, a.ddt, a.db = ptr(S), ptr(M), ptr(ddt), ptr(db)
+    _lib.call("hxm_ssd_bwd_intra", a, st)
+    return S, M, ddt, db
+
+
+def _ssd_bwd_shared(x, de, Af, Bm, Cm, dy, c, st):
+    """Chunkwise SSD backward with B, C shared by the heads (ngroups = 1).
+
+    Per head h and chunk (b = in-chunk prefix sum of log f = dt A, g its total,
+    beta = e^b, alpha = dt e^(g - b)):
+        state entering chunk k, rows (h, p), columns n:
+            Z_{k+1} = e^g Z_k + (alpha x)^T B          (one GEMM over all heads)
+        adjoint leaving chunk k:
+            Y_k = e^g Y_{k+1} + (beta dy)^T C
+        intra-chunk weights S_h = (C B^T) * e^(b_t - b_s) * dt_s (causal)
+    so the state-side GEMMs fold the heads into their inner dimension
+    ((c x N) x (N x H*P) per chunk) and only the c x c decay matrices are per
+    head (hxm_ssd_bwd_intra forms them with the head sum on chip).  Returns
+    (dx (B, L, H, P), dL/d dt through the input gate and dL/dlog f (B, L, H),
+    dB, dC (B, L, N)); the gate identity is formed as in the per-head mLSTM
+    path (rowsum - colsum of W = dL/dS * S without its diagonal, the two
+    inter-chunk terms, and <Y_k, Z_{k+1}> per chunk)."""
+    from .tfla.tfla_bwd import _chunk_dg, _scan
+    if c not in (32, 64):
+        raise ValueError(f"ssd_chunk_scan_bwd: chunk must be 32 or 64 (got {c})")
+    bsz, L, nh, p = x.shape
+    n = Bm.shape[-1]
+    f32 = dict(device=x.device, dtype=torch.float32)
+    nch = (L + c - 1) // c
+    Lp = nch * c
+
+    def pad(t, *tail):
+        out = torch.zeros(bsz, Lp, *tail, **f32)
+        out[:, :L] = t
+        return out
+
+    xc = pad(x, nh, p).view(bsz, nch, c, nh, p)
+    dyc = pad(dy, nh, p).view(bsz, nch, c, nh, p)
+    Bc = pad(Bm, n).view(bsz, nch, c, n)
+    Cc = pad(Cm, n).view(bsz, nch, c, n)
+    dec = pad(de, nh).view(bsz, nch, c, nh)               # 0 past the sequence: no input there
+    b = (dec * Af).cumsum(2)                              # (B, nch, c, H)
+    g = b[:, :, -1:]
+    beta = torch.exp(b)
+    egb = torch.exp(g - b)
+    alpha = dec * egb
+    eg_rows = torch.exp(g[:, :, 0]).unsqueeze(-1).expand(bsz, nch, nh, p).reshape(bsz, nch, nh * p).contiguous()
+    ax = (xc * alpha.unsqueeze(-1)).reshape(bsz, nch, c, nh * p)
+    bdy = (dyc * beta.unsqueeze(-1)).reshape(bsz, nch, c, nh * p)
+    Z = torch.matmul(ax.transpose(-1, -2), Bc)            # increments -> states entering each chunk
+    _scan(Z.unsqueeze(1), eg_rows, False, st)
+    Yz = torch.matmul(bdy.transpose(-1, -2), Cc)          # increments -> adjoints leaving each chunk
+    _scan(Yz.unsqueeze(1), eg_rows, True, st)
+
+    # per-head c x c terms (hxm_ssd_bwd_intra: one block per (batch, chunk), the head sum on chip)
+    dyh = dyc.permute(0, 1, 3, 2, 4)                      # (B, nch, H, c, P)
+    G = torch.matmul(dyh, xc.permute(0, 1, 3, 4, 2))      # dL/dS_h = dy_h x_h^T
+    cb = torch.matmul(Cc, Bc.transpose(-1, -2))           # C B^T (B, nch, c, c)
+    S, M, di, db = _intra(cb, b, dec, G, st)
+    del G
+    dx = torch.matmul(S.transpose(-1, -2), dyh)           # intra-chunk dx (B, nch, H, c, P)
+    del S
+    # shared-operand GEMMs (heads folded into the inner dimension)
+    dC = torch.matmul(M, Bc).add_(torch.matmul(bdy, Z))
+    dB = torch.matmul(M.transpose(-1, -2), Cc).add_(torch.matmul(ax, Yz))
+    BY = torch.matmul(Bc, Yz.transpose(-1, -2)).view(bsz, nch, c, nh, p)
+    CZ = torch.matmul(Cc, Z.transpose(-1, -2)).view(bsz, nch, c, nh, p)
+    dx = dx.permute(0, 1, 3, 2, 4).add_(alpha.unsqueeze(-1) * BY)
+    xBY = (xc * BY).sum(-1)                               # (B, nch, c, H)
+    di = di.permute(0, 1, 3, 2).add_(egb * xBY)
+    db = db.permute(0, 1, 3, 2).add_(beta * (dyc * CZ).sum(-1)).sub_(alpha * xBY)
+    dg = _chunk_dg(Yz.unsqueeze(1), Z.unsqueeze(1), (-1,)).view(bsz, nch, nh, p).sum(-1)
+    dlf = db.flip(2).cumsum(2).flip(2).add_(dg.unsqueeze(2)).reshape(bsz, Lp, nh)[:, :L]
+    dlf[:, 0] = 0.0  # f at the first step multiplies the zero state
+    un = lambda t: t.reshape(bsz, Lp, *t.shape[3:])[:, :L]
+    return un(dx), un(di), dlf, un(dB), un(dC)
+
+
 def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False, chunk=64, tf32=None):
     """Gradients of y = ssd_chunk_scan(x, dt, A, B, C, D, dt_bias, dt_softplus)
     from a zero state, for dy (B, L, H, P).  Returns fp32
@@ -64,14 +151,14 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False
 
     Per head the SSD recurrence is the mLSTM state recurrence without its
     normalizer: q = C, k = B (shared by the heads), v = x[:, :, head], input
-    gate i = dt and forget gate f = exp(dt A).  The chunkwise backward of the
-    per-head mLSTM path (exact decay matrix, chunk-state scans on the GPU,
-    batched fp32 chunk GEMMs) gives dq, dk, dv, dL/di and dL/dlog f; then
-    ddt = dL/di + A dL/dlog f, dA = sum dt dL/dlog f, the shared B, C sum
-    over heads, and softplus / bias chain on.  tf32: chunk GEMMs on TF32
+    gate i = dt and forget gate f = exp(dt A).  The chunkwise backward
+    (_ssd_bwd_shared: exact decay matrix, chunk-state scans on the GPU,
+    batched chunk GEMMs with the heads folded in where B, C are shared) gives
+    dx, dB, dC, dL/di and dL/dlog f; then ddt = dL/di + A dL/dlog f,
+    dA = sum dt dL/dlog f, and softplus / bias chain on.  tf32: chunk GEMMs on TF32
     tensor cores (default when x is bf16, as from the bf16 forward) or in full
     fp32."""
-    from .tfla.tfla_bwd import _bwd_heads, _gemm_precision
+    from .tfla.tfla_bwd import _gemm_precision
     who = "ssd_chunk_scan_bwd"
     dev = require_cuda(x, dt, A, B, C, D, dy, dt_bias, who=who)
     bsz, L, nh, p = x.shape
@@ -79,24 +166,16 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False
     de, z = _dt_eff(dt, dt_bias, dt_softplus)                      # (B, L, H)
     Af = A.float()
     with torch.no_grad(), _gemm_precision(x.dtype == torch.bfloat16 if tf32 is None else tf32):
-        q = C.float().unsqueeze(1).expand(bsz, nh, L, n)
-        k = B.float().unsqueeze(1).expand(bsz, nh, L, n)
-        v = x.float().permute(0, 2, 1, 3)
-        li = torch.log(de).permute(0, 2, 1)
-        lf = (de * Af).permute(0, 2, 1)
-        dyh = dy.float().permute(0, 2, 1, 3)
-        dq, dk, dv, _, dlf, di = _bwd_heads(q, k, v, li, lf, dyh, int(chunk), False, False, stream_of(dev))
-        dlf, di = dlf.permute(0, 2, 1), di.permute(0, 2, 1)        # (B, L, H)
+        dx, di, dlf, dBm, dCm = _ssd_bwd_shared(x, de, Af, B, C, dy, int(chunk), stream_of(dev))
         dde = di + Af * dlf
         dA = (de * dlf).sum((0, 1))
-        dx = dv.permute(0, 2, 1, 3)
         dD = None
         if D is not None:
             dx = dx + D.float().view(1, 1, nh, 1) * dy.float()
             dD = (dy.float() * x.float()).sum((0, 1, 3))
         ddt = dde * torch.sigmoid(z) if dt_softplus else dde
         ddb = ddt.sum((0, 1)) if dt_bias is not None else None
-    return dx, ddt, dA, dk.sum(1), dq.sum(1), dD, ddb
+    return dx, ddt, dA, dBm, dCm, dD, ddb
 
 
 class SSDChunkScanFunction(torch.autograd.Function):

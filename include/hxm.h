@@ -312,6 +312,27 @@ typedef struct hxm_ssd_args {
 } hxm_ssd_args;
 
 size_t hxm_ssd_workspace_size(const hxm_ssd_args* args);
+
+/* SSD backward, per-head intra-chunk terms (no reference counterpart: the    */
+/* reference has no SSD; its arithmetic is the Euler scan of                 */
+/* scan_interface.py:132-150 with channel (head, p)).  Per (batch, chunk) of */
+/* `chunk` (32 or 64) steps and head h, with bcum the in-chunk prefix sum of */
+/* the head's log decay dt*A, cb = C B^T of the chunk and G = dL/dS_h:       */
+/*   S[h, t, s]  = cb[t, s] e^(bcum_t - bcum_s) dt_s   (s <= t, else 0)       */
+/*   M[t, s]     = sum_h G[h, t, s] e^(bcum_t - bcum_s) dt_s                  */
+/*   ddt[h, s]   = sum_t G[h, t, s] cb[t, s] e^(bcum_t - bcum_s)              */
+/*   db[h, t]    = rowsum(W)[t] - colsum(W)[t], W = G * S without its diagonal*/
+/* cb, M (batch*nchunks, chunk, chunk); bcum, dt (batch*nchunks, chunk,      */
+/* heads); dS = G and S (batch*nchunks, heads, chunk, chunk); ddt, db        */
+/* (batch*nchunks, heads, chunk).  fp32, dense.                               */
+typedef struct hxm_ssd_bwd_intra_args {
+  size_t struct_size;
+  int32_t batch, nchunks, heads, chunk;
+  const float* cb; const float* bcum; const float* dt; const float* dS;
+  float* S; float* M; float* ddt; float* db;
+} hxm_ssd_bwd_intra_args;
+
+hxm_status hxm_ssd_bwd_intra(const hxm_ssd_bwd_intra_args* args, void* stream);
 hxm_status hxm_ssd_chunk_scan_fwd(const hxm_ssd_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */

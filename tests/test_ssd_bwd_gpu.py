@@ -84,3 +84,25 @@ def test_ssd_bwd_entry_fp32_exact_and_large_decay(S):
     for name, a, b in zip(("dx", "ddt", "dA", "dB", "dC", "dD"), got, ref):
         assert torch.isfinite(a).all(), name
         assert rel_err(a.double().cpu().numpy(), b.grad.numpy()) < 1e-4, name
+
+
+@pytest.mark.parametrize("c", [32, 64])
+def test_ssd_bwd_intra_kernel_vs_formulas(S, c):
+    """hxm_ssd_bwd_intra (one block per (batch, chunk), the head sum on chip)
+    against the torch formulas of its outputs: S_h, M, dL/d dt and dL/d b."""
+    g = torch.Generator().manual_seed(c)
+    bsz, nch, nh = 2, 3, 5
+    cb = torch.randn(bsz, nch, c, c, generator=g)
+    bcum = (-torch.rand(bsz, nch, c, nh, generator=g)).cumsum(2)
+    dt = torch.rand(bsz, nch, c, nh, generator=g)
+    G = torch.randn(bsz, nch, nh, c, c, generator=g)
+    got = S._intra(cb.cuda(), bcum.cuda(), dt.cuda(), G.cuda(), torch.cuda.current_stream().cuda_stream)
+    bh = bcum.permute(0, 1, 3, 2)
+    causal = torch.ones(c, c, dtype=torch.bool).tril()
+    Lm = torch.exp((bh.unsqueeze(-1) - bh.unsqueeze(-2)).masked_fill(~causal, float("-inf")))
+    ds = dt.permute(0, 1, 3, 2).unsqueeze(-2)
+    V = G * Lm * cb.unsqueeze(2)
+    W = V * ds * (~torch.eye(c, dtype=torch.bool))
+    want = (cb.unsqueeze(2) * Lm * ds, (G * Lm * ds).sum(2), V.sum(-2), W.sum(-1) - W.sum(-2))
+    for name, a, b in zip(("S", "M", "ddt", "db"), got, want):
+        assert rel_err(a.double().cpu().numpy(), b.double().numpy()) < 1e-5, name
