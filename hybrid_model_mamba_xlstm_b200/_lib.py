@@ -183,6 +183,17 @@ class SsdBwdIntraArgs(ct.Structure):
     ]
 
 
+class SsdBwdRowsArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("nchunks", ct.c_int32), ("chunk", ct.c_int32), ("heads", ct.c_int32),
+        ("headdim", ct.c_int32), ("seqlen", ct.c_int32),
+        ("xh", ct.c_void_p), ("dyh", ct.c_void_p), ("dxi", ct.c_void_p),
+        ("BY", ct.c_void_p), ("CZ", ct.c_void_p), ("alpha", ct.c_void_p), ("D", ct.c_void_p),
+        ("dx", ct.c_void_p), ("xby", ct.c_void_p), ("dycz", ct.c_void_p), ("dyx", ct.c_void_p),
+    ]
+
+
 class ChunkDotArgs(ct.Structure):
     _fields_ = [
         ("struct_size", ct.c_size_t),
@@ -221,6 +232,7 @@ SYMBOLS = {
     "hxm_mlstm_bwd_normalizer": (ct.c_int, [ct.POINTER(MlstmBwdNormArgs), ct.c_void_p]),
     "hxm_chunk_state_dot": (ct.c_int, [ct.POINTER(ChunkDotArgs), ct.c_void_p]),
     "hxm_ssd_bwd_intra": (ct.c_int, [ct.POINTER(SsdBwdIntraArgs), ct.c_void_p]),
+    "hxm_ssd_bwd_rows": (ct.c_int, [ct.POINTER(SsdBwdRowsArgs), ct.c_void_p]),
     "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),
     "hxm_ssd_chunk_scan_fwd": (ct.c_int, [ct.POINTER(SsdArgs), ct.c_void_p]),
     "hxm_slstm_scan_fwd": (ct.c_int, [ct.POINTER(SlstmArgs), ct.c_void_p]),

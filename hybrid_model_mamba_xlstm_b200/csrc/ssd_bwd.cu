@@ -1,5 +1,5 @@
-// ssd_bwd.cu — the per-head intra-chunk terms of the chunkwise SSD backward
-// (sm_100a).
+// ssd_bwd.cu — the per-head intra-chunk terms and the row assembly of the
+// chunkwise SSD backward (sm_100a).
 //
 // The SSD recurrence (ngroups = 1: B, C shared by the heads; per-head scalar
 // decay) has no reference kernel; its arithmetic is the Euler selective scan
@@ -15,6 +15,9 @@
 //     dbi[t] = rowsum(W)[t] - colsum(W)[t],  W = G * S_h without its diagonal
 //                                                      (dL/d b_t, intra-chunk)
 // The diagonal of W appears in both sums, so it is left out exactly.
+// A second kernel assembles, per (batch, chunk, step, head) row, dx from its
+// intra-chunk part, the state part alpha * (B Y^T) and D * dy, and the
+// row dot products the dt, log-decay and D gradients need.
 #include "capi_internal.h"
 #include "common.cuh"
 
@@ -81,6 +84,54 @@ __global__ void __launch_bounds__(256) intra_kernel(const float* __restrict__ cb
   for (int i = 0; i < kN; ++i) M[bk * C * C + (int64_t)(256 * i + tid)] = macc[i];
 }
 
+// One warp per (batch, chunk, step t, head h) row of P values:
+//   dx[b, kc*C + t, h, :] = dxi[h, t, :] + alpha[t, h] BY[t, h, :] + D[h] dy
+//   xby[t, h] = x . BY,  dycz[t, h] = dy . CZ,  dyx[t, h] = dy . x
+// xh, dyh, dxi head-major (batch*nch, H, C, P); BY, CZ (batch*nch, C, H, P);
+// rows past seqlen write no dx.
+__global__ void __launch_bounds__(256) rows_kernel(const float* __restrict__ xh, const float* __restrict__ dyh,
+                                                   const float* __restrict__ dxi, const float* __restrict__ BY,
+                                                   const float* __restrict__ CZ, const float* __restrict__ alpha,
+                                                   const float* __restrict__ D, int nch, int C, int H, int P,
+                                                   int seqlen, int64_t rows, float* __restrict__ dx,
+                                                   float* __restrict__ xby, float* __restrict__ dycz,
+                                                   float* __restrict__ dyx) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = blockIdx.x * 8ll + (threadIdx.x >> 5);  // ((bk * C + t) * H + h)
+  if (row >= rows) return;
+  const int h = (int)(row % H);
+  const int64_t bt = row / H;
+  const int t = (int)(bt % C);
+  const int64_t bk = bt / C;
+  const int kc = (int)(bk % nch);
+  const int64_t bi = bk / nch;
+  const int64_t hm = ((bk * H + h) * C + t) * (int64_t)P;  // head-major row
+  const int64_t tm = row * (int64_t)P;                     // step-major row
+  const float al = alpha[row];
+  const float dd = D ? D[h] : 0.f;
+  const int tg = kc * C + t;
+  float* out = tg < seqlen ? dx + ((bi * seqlen + tg) * H + h) * (int64_t)P : nullptr;
+  float a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  for (int p = lane; p < P; p += 32) {
+    const float xv = xh[hm + p], gv = dyh[hm + p], by = BY[tm + p];
+    a1 = fmaf(xv, by, a1);
+    a2 = fmaf(gv, CZ[tm + p], a2);
+    a3 = fmaf(gv, xv, a3);
+    if (out) out[p] = dxi[hm + p] + al * by + dd * gv;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+    a2 += __shfl_xor_sync(0xffffffffu, a2, o);
+    a3 += __shfl_xor_sync(0xffffffffu, a3, o);
+  }
+  if (lane == 0) {
+    xby[row] = a1;
+    dycz[row] = a2;
+    if (dyx) dyx[row] = a3;
+  }
+}
+
 }  // namespace ssd_bwd
 }  // namespace hxm
 
@@ -107,4 +158,25 @@ extern "C" hxm_status hxm_ssd_bwd_intra(const hxm_ssd_bwd_intra_args* a, void* s
     ssd_bwd::intra_kernel<32><<<(unsigned)blocks, 256, 0, st>>>(a->cb, a->bcum, a->dt, a->dS, a->heads, a->S, a->M,
                                                                  a->ddt, a->db);
   return check_launch("hxm_ssd_bwd_intra");
+}
+
+extern "C" hxm_status hxm_ssd_bwd_rows(const hxm_ssd_bwd_rows_args* a, void* stream) {
+  using namespace hxm;
+  clear_error();
+  HXM_REQUIRE(a != nullptr, "hxm_ssd_bwd_rows: args is NULL");
+  HXM_REQUIRE(a->struct_size == sizeof(hxm_ssd_bwd_rows_args), "hxm_ssd_bwd_rows: struct_size %zu != %zu",
+              a->struct_size, sizeof(hxm_ssd_bwd_rows_args));
+  HXM_REQUIRE(a->batch >= 0 && a->nchunks >= 0 && a->chunk >= 1 && a->heads >= 1 && a->headdim >= 1 &&
+                  a->seqlen >= 0 && a->seqlen <= (int64_t)a->nchunks * a->chunk,
+              "hxm_ssd_bwd_rows: bad sizes batch=%d nchunks=%d chunk=%d heads=%d headdim=%d seqlen=%d", a->batch,
+              a->nchunks, a->chunk, a->heads, a->headdim, a->seqlen);
+  const int64_t rows = (int64_t)a->batch * a->nchunks * a->chunk * a->heads;
+  if (rows == 0) return HXM_OK;
+  HXM_REQUIRE(a->xh && a->dyh && a->dxi && a->BY && a->CZ && a->alpha && a->dx && a->xby && a->dycz,
+              "hxm_ssd_bwd_rows: NULL pointer");
+  HXM_REQUIRE((rows + 7) / 8 < (int64_t)0x7fffffff, "hxm_ssd_bwd_rows: too many rows (%lld)", (long long)rows);
+  ssd_bwd::rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      a->xh, a->dyh, a->dxi, a->BY, a->CZ, a->alpha, a->D, a->nchunks, a->chunk, a->heads, a->headdim, a->seqlen,
+      rows, a->dx, a->xby, a->dycz, a->dyx);
+  return check_launch("hxm_ssd_bwd_rows");
 }

@@ -71,7 +71,20 @@ def _intra(cb, bcum, dt, G, st):
     return S, M, ddt, db
 
 
-def _ssd_bwd_shared(x, de, Af, Bm, Cm, dy, c, st):
+def _rows(xh, dyh, dxi, BY, CZ, alpha, D, L, st):
+    """hxm_ssd_bwd_rows: dx (B, L, H, P) and the per-row x.BY, dy.CZ, dy.x."""
+    bsz, nch, nh, c, p = xh.shape
+    dx = torch.empty(bsz, L, nh, p, device=xh.device, dtype=torch.float32)
+    xby, dycz, dyx = (torch.empty(bsz, nch, c, nh, device=xh.device, dtype=torch.float32) for _ in range(3))
+    a = _lib.SsdBwdRowsArgs()
+    a.batch, a.nchunks, a.chunk, a.heads, a.headdim, a.seqlen = bsz, nch, c, nh, p, L
+    a.xh, a.dyh, a.dxi, a.BY, a.CZ, a.alpha, a.D = ptr(xh), ptr(dyh), ptr(dxi), ptr(BY), ptr(CZ), ptr(alpha), ptr(D)
+    a.dx, a.xby, a.dycz, a.dyx = ptr(dx), ptr(xby), ptr(dycz), ptr(dyx)
+    _lib.call("hxm_ssd_bwd_rows", a, st)
+    return dx, xby, dycz, dyx
+
+
+def _ssd_bwd_shared(x, de, Af, Bm, Cm, dy, c, st, D=None):
     """Chunkwise SSD backward with B, C shared by the heads (ngroups = 1).
 
     Per head h and chunk (b = in-chunk prefix sum of log f = dt A, g its total,
@@ -83,11 +96,14 @@ def _ssd_bwd_shared(x, de, Af, Bm, Cm, dy, c, st):
         intra-chunk weights S_h = (C B^T) * e^(b_t - b_s) * dt_s (causal)
     so the state-side GEMMs fold the heads into their inner dimension
     ((c x N) x (N x H*P) per chunk) and only the c x c decay matrices are per
-    head (hxm_ssd_bwd_intra forms them with the head sum on chip).  Returns
-    (dx (B, L, H, P), dL/d dt through the input gate and dL/dlog f (B, L, H),
-    dB, dC (B, L, N)); the gate identity is formed as in the per-head mLSTM
-    path (rowsum - colsum of W = dL/dS * S without its diagonal, the two
-    inter-chunk terms, and <Y_k, Z_{k+1}> per chunk)."""
+    head (hxm_ssd_bwd_intra forms them with the head sum on chip; x and dy are
+    laid out head-major once so the per-head GEMMs read them in place).
+    hxm_ssd_bwd_rows assembles dx (+ D dy) and the per-row dot products of the
+    dt / log-decay / D gradients.  Returns (dx (B, L, H, P), dL/d dt through
+    the input gate and dL/dlog f (B, L, H), dB, dC (B, L, N), dD or None); the
+    gate identity is formed as in the per-head mLSTM path (rowsum - colsum of
+    W = dL/dS * S without its diagonal, the two inter-chunk terms, and
+    <Y_k, Z_{k+1}> per chunk)."""
     from .tfla.tfla_bwd import _chunk_dg, _scan
     if c not in (32, 64):
         raise ValueError(f"ssd_chunk_scan_bwd: chunk must be 32 or 64 (got {c})")
@@ -96,14 +112,23 @@ def _ssd_bwd_shared(x, de, Af, Bm, Cm, dy, c, st):
     f32 = dict(device=x.device, dtype=torch.float32)
     nch = (L + c - 1) // c
     Lp = nch * c
+    nf = L // c
 
     def pad(t, *tail):
         out = torch.zeros(bsz, Lp, *tail, **f32)
         out[:, :L] = t
         return out
 
-    xc = pad(x, nh, p).view(bsz, nch, c, nh, p)
-    dyc = pad(dy, nh, p).view(bsz, nch, c, nh, p)
+    def pad_heads(t):  # (B, L, H, P) -> head-major chunks (B, nch, H, c, P), zero past L
+        out = torch.zeros(bsz, nch, nh, c, p, **f32)
+        if nf:
+            out[:, :nf].copy_(t[:, :nf * c].reshape(bsz, nf, c, nh, p).permute(0, 1, 3, 2, 4))
+        if L > nf * c:
+            out[:, nf, :, :L - nf * c].copy_(t[:, nf * c:].permute(0, 2, 1, 3))
+        return out
+
+    xh = pad_heads(x)
+    dyh = pad_heads(dy)
     Bc = pad(Bm, n).view(bsz, nch, c, n)
     Cc = pad(Cm, n).view(bsz, nch, c, n)
     dec = pad(de, nh).view(bsz, nch, c, nh)               # 0 past the sequence: no input there
@@ -113,35 +138,39 @@ def _ssd_bwd_shared(x, de, Af, Bm, Cm, dy, c, st):
     egb = torch.exp(g - b)
     alpha = dec * egb
     eg_rows = torch.exp(g[:, :, 0]).unsqueeze(-1).expand(bsz, nch, nh, p).reshape(bsz, nch, nh * p).contiguous()
-    ax = (xc * alpha.unsqueeze(-1)).reshape(bsz, nch, c, nh * p)
-    bdy = (dyc * beta.unsqueeze(-1)).reshape(bsz, nch, c, nh * p)
+    ax = torch.empty(bsz, nch, c, nh, p, **f32)
+    torch.mul(xh.permute(0, 1, 3, 2, 4), alpha.unsqueeze(-1), out=ax)
+    ax = ax.view(bsz, nch, c, nh * p)
+    bdy = torch.empty(bsz, nch, c, nh, p, **f32)
+    torch.mul(dyh.permute(0, 1, 3, 2, 4), beta.unsqueeze(-1), out=bdy)
+    bdy = bdy.view(bsz, nch, c, nh * p)
     Z = torch.matmul(ax.transpose(-1, -2), Bc)            # increments -> states entering each chunk
     _scan(Z.unsqueeze(1), eg_rows, False, st)
     Yz = torch.matmul(bdy.transpose(-1, -2), Cc)          # increments -> adjoints leaving each chunk
     _scan(Yz.unsqueeze(1), eg_rows, True, st)
 
     # per-head c x c terms (hxm_ssd_bwd_intra: one block per (batch, chunk), the head sum on chip)
-    dyh = dyc.permute(0, 1, 3, 2, 4)                      # (B, nch, H, c, P)
-    G = torch.matmul(dyh, xc.permute(0, 1, 3, 4, 2))      # dL/dS_h = dy_h x_h^T
+    G = torch.matmul(dyh, xh.transpose(-1, -2))           # dL/dS_h = dy_h x_h^T
     cb = torch.matmul(Cc, Bc.transpose(-1, -2))           # C B^T (B, nch, c, c)
     S, M, di, db = _intra(cb, b, dec, G, st)
     del G
-    dx = torch.matmul(S.transpose(-1, -2), dyh)           # intra-chunk dx (B, nch, H, c, P)
+    dxi = torch.matmul(S.transpose(-1, -2), dyh)          # intra-chunk dx, head-major
     del S
     # shared-operand GEMMs (heads folded into the inner dimension)
     dC = torch.matmul(M, Bc).add_(torch.matmul(bdy, Z))
     dB = torch.matmul(M.transpose(-1, -2), Cc).add_(torch.matmul(ax, Yz))
-    BY = torch.matmul(Bc, Yz.transpose(-1, -2)).view(bsz, nch, c, nh, p)
-    CZ = torch.matmul(Cc, Z.transpose(-1, -2)).view(bsz, nch, c, nh, p)
-    dx = dx.permute(0, 1, 3, 2, 4).add_(alpha.unsqueeze(-1) * BY)
-    xBY = (xc * BY).sum(-1)                               # (B, nch, c, H)
-    di = di.permute(0, 1, 3, 2).add_(egb * xBY)
-    db = db.permute(0, 1, 3, 2).add_(beta * (dyc * CZ).sum(-1)).sub_(alpha * xBY)
+    BY = torch.matmul(Bc, Yz.transpose(-1, -2))           # (B, nch, c, H*P)
+    CZ = torch.matmul(Cc, Z.transpose(-1, -2))
+    Df = None if D is None else D.float().contiguous()
+    dx, xby, dycz, dyx = _rows(xh, dyh, dxi, BY, CZ, alpha, Df, L, st)
+    di = di.permute(0, 1, 3, 2).add_(egb * xby)
+    db = db.permute(0, 1, 3, 2).add_(beta * dycz).sub_(alpha * xby)
     dg = _chunk_dg(Yz.unsqueeze(1), Z.unsqueeze(1), (-1,)).view(bsz, nch, nh, p).sum(-1)
     dlf = db.flip(2).cumsum(2).flip(2).add_(dg.unsqueeze(2)).reshape(bsz, Lp, nh)[:, :L]
     dlf[:, 0] = 0.0  # f at the first step multiplies the zero state
     un = lambda t: t.reshape(bsz, Lp, *t.shape[3:])[:, :L]
-    return un(dx), un(di), dlf, un(dB), un(dC)
+    dD = None if D is None else dyx.sum((0, 1, 2))
+    return dx, un(di), dlf, un(dB), un(dC), dD
 
 
 def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False, chunk=64, tf32=None):
@@ -166,13 +195,9 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False
     de, z = _dt_eff(dt, dt_bias, dt_softplus)                      # (B, L, H)
     Af = A.float()
     with torch.no_grad(), _gemm_precision(x.dtype == torch.bfloat16 if tf32 is None else tf32):
-        dx, di, dlf, dBm, dCm = _ssd_bwd_shared(x, de, Af, B, C, dy, int(chunk), stream_of(dev))
+        dx, di, dlf, dBm, dCm, dD = _ssd_bwd_shared(x, de, Af, B, C, dy, int(chunk), stream_of(dev), D)
         dde = di + Af * dlf
         dA = (de * dlf).sum((0, 1))
-        dD = None
-        if D is not None:
-            dx = dx + D.float().view(1, 1, nh, 1) * dy.float()
-            dD = (dy.float() * x.float()).sum((0, 1, 3))
         ddt = dde * torch.sigmoid(z) if dt_softplus else dde
         ddb = ddt.sum((0, 1)) if dt_bias is not None else None
     return dx, ddt, dA, dBm, dCm, dD, ddb

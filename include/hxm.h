@@ -333,6 +333,24 @@ typedef struct hxm_ssd_bwd_intra_args {
 } hxm_ssd_bwd_intra_args;
 
 hxm_status hxm_ssd_bwd_intra(const hxm_ssd_bwd_intra_args* args, void* stream);
+
+/* SSD backward, per (batch, chunk, step t, head h) row of headdim values    */
+/* (no reference counterpart, as above):                                     */
+/*   dx[b, t_global, h, :] = dxi + alpha[t, h] * BY + D[h] * dy               */
+/*   xby = x . BY,  dycz = dy . CZ,  dyx = dy . x        (per row)            */
+/* xh, dyh, dxi (batch*nchunks, heads, chunk, headdim) head-major; BY, CZ    */
+/* (batch*nchunks, chunk, heads, headdim); alpha, xby, dycz, dyx             */
+/* (batch*nchunks, chunk, heads); D (heads) or NULL; dyx may be NULL;        */
+/* dx (batch, seqlen, heads, headdim), rows past seqlen not written.  fp32.  */
+typedef struct hxm_ssd_bwd_rows_args {
+  size_t struct_size;
+  int32_t batch, nchunks, chunk, heads, headdim, seqlen;
+  const float* xh; const float* dyh; const float* dxi;
+  const float* BY; const float* CZ; const float* alpha; const float* D;
+  float* dx; float* xby; float* dycz; float* dyx;
+} hxm_ssd_bwd_rows_args;
+
+hxm_status hxm_ssd_bwd_rows(const hxm_ssd_bwd_rows_args* args, void* stream);
 hxm_status hxm_ssd_chunk_scan_fwd(const hxm_ssd_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */

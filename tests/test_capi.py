@@ -44,7 +44,7 @@ def test_struct_sizes_match_header_layout():
                     (_lib.ScanBwdArgs, "hxm_selective_scan_bwd"), (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_prepare"),
                     (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_finalize"), (_lib.ChunkScanArgs, "hxm_chunk_state_scan"),
                     (_lib.MlstmBwdNormArgs, "hxm_mlstm_bwd_normalizer"), (_lib.ChunkDotArgs, "hxm_chunk_state_dot"),
-                    (_lib.SsdBwdIntraArgs, "hxm_ssd_bwd_intra")]:
+                    (_lib.SsdBwdIntraArgs, "hxm_ssd_bwd_intra"), (_lib.SsdBwdRowsArgs, "hxm_ssd_bwd_rows")]:
         a = cls()
         a.struct_size = ct.sizeof(a) + 8
         st = getattr(_lib.lib(), fn)(ct.byref(a), None)
