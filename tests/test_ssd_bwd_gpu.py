@@ -106,3 +106,19 @@ def test_ssd_bwd_intra_kernel_vs_formulas(S, c):
     want = (cb.unsqueeze(2) * Lm * ds, (G * Lm * ds).sum(2), V.sum(-2), W.sum(-1) - W.sum(-2))
     for name, a, b in zip(("S", "M", "ddt", "db"), got, want):
         assert rel_err(a.double().cpu().numpy(), b.double().numpy()) < 1e-5, name
+
+
+def test_ssd_bwd_chunk32_ragged_matches_chunk64(S):
+    """32-step chunks (the intra kernel's other tile) on a ragged length give the
+    gradients of 64-step chunks and of the float64 loop."""
+    x, dt, A, B, C, D, bias, dy = _inputs(1, 77, 3, 32, 128, seed=12)
+    cu = lambda t: t.cuda()
+    g32 = S.ssd_chunk_scan_bwd(*map(cu, (x, dt, A, B, C, D, dy)), dt_bias=cu(bias), dt_softplus=True, chunk=32,
+                               tf32=False)
+    g64 = S.ssd_chunk_scan_bwd(*map(cu, (x, dt, A, B, C, D, dy)), dt_bias=cu(bias), dt_softplus=True, chunk=64,
+                               tf32=False)
+    ref = [t.double().requires_grad_(True) for t in (x, dt, A, B, C, D, bias)]
+    _loop(*ref, True).backward(dy.double())
+    for name, a, b, r in zip(("dx", "ddt", "dA", "dB", "dC", "dD", "ddt_bias"), g32, g64, ref):
+        assert rel_err(a.double().cpu().numpy(), b.double().cpu().numpy()) < 1e-5, name
+        assert rel_err(a.double().cpu().numpy(), r.grad.numpy()) < 1e-4, name
