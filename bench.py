@@ -248,7 +248,7 @@ def secondary_metrics(args, dev, world, rank):
     out["mlstm_bwd_b8_h4_l2048_d512_channel_gates"] = {
         "metric": "mLSTM backward ms (chunk GEMM TFLOP/s alongside)", "value": ms, "unit": "ms",
         "gemm_tflops": world * fl / ms / 1e9, "scaling": "weak", "higher_is_better": False,
-        "kernels": "hxm mlstm_bwd prepare / chunk_scan / finalize + fp32 cuBLAS chunk GEMMs"}
+        "kernels": "hxm mlstm_bwd prepare / normalizer / chunk_scan / chunk_dot / finalize + TF32 cuBLAS chunk GEMMs"}
     del q, k, v, dh, li, lf
     # SSD backward at the SSD workload's shape (batch 8, 32 heads x 64, dstate 128, seqlen 4096)
     from hybrid_model_mamba_xlstm_b200.kernels.ssd import ssd_chunk_scan_bwd
@@ -260,6 +260,22 @@ def secondary_metrics(args, dev, world, rank):
         "metric": "SSD backward ms", "value": ms, "unit": "ms", "scaling": "weak", "higher_is_better": False,
         "kernels": "hxm chunk_scan / normalizer / chunk_dot + TF32 cuBLAS chunk GEMMs (exact per-head chunk form)"}
     del inp, dy
+    # selective-scan backward at the 350M model's Mamba layer shape (batch 8, seqlen 2048, d_inner 2048, N 16)
+    from hybrid_model_mamba_xlstm_b200.kernels.selective_scan.scan_interface import selective_scan_bwd
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    sb, sl, sd = 8, 2048, 2048
+    inp = scan_inputs(sb, sl, sd, 16, torch.bfloat16, seed=rank, device=dev, on_device=True)
+    dout = torch.randn(sb, sd, sl, generator=g, device=dev).to(torch.bfloat16)
+    tr = lambda x: x.transpose(1, 2)
+    ms = _time_cuda(lambda: selective_scan_bwd(tr(dout), tr(inp.u), tr(inp.delta), inp.A, tr(inp.B), tr(inp.C),
+                                               inp.D, tr(inp.z), z_mode="silu", delta_bias=inp.delta_bias,
+                                               delta_softplus=True), min(steps, 3), 2, dev, world)
+    nbytes = sb * sl * sd * (4 * 2 + 3 * 4) + sb * sl * 16 * (2 * 2 + 2 * 4)
+    out["scan_bwd_b8_l2048_d2048_n16"] = {
+        "metric": "selective-scan backward GB/s (one read of each bf16 input, one write of each fp32 gradient)",
+        "value": world * nbytes / ms / 1e6, "unit": "GB/s", "ms": ms, "scaling": "weak",
+        "kernel": "hxm::scan::scan_bwd_kernel (checkpointed reverse recurrence)"}
+    del inp, dout
     torch.cuda.empty_cache()
     out["prefill"] = prefill_metric(args, dev, world, rank)
     return out

@@ -15,6 +15,7 @@ cases (default sizes):
   mlstm_stream B H L D           (8 4 2048 512)   per-channel gates (key-streaming kernel)
   mlstm_bwd    B H L D           (8 4 2048 512)   chunkwise backward, per-channel gates, bf16 (TF32 chunk GEMMs)
   ssd_bwd      B L H P N         (8 4096 32 64 128)  SSD backward (exact per-head chunk form, TF32 chunk GEMMs)
+  scan_bwd     B L D             (8 2048 2048)   selective-scan backward, bf16 inputs, fp32 gradients
   slstm        B L H HD          (8 256 4 256)    recurrent R
   conv         B D L             (8 4096 2048)    causal depthwise conv1d(4) + SiLU
   mamba_layer  B L               (8 2048)         one hybrid-350M Mamba block
@@ -143,6 +144,17 @@ def main(argv=None):
         lf = torch.nn.functional.logsigmoid(torch.randn(B, H, L, D, generator=g, device=dev))
         fn = lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh)  # noqa: E731
         extra = {"chunk": 64}
+    elif a.case == "scan_bwd":
+        # selective-scan backward (softplus(delta + bias), y * silu(z)), bf16 inputs, fp32 gradients
+        from .kernels.selective_scan.scan_interface import selective_scan_bwd
+        from .workloads import scan_inputs
+        B, L, D = (s + [8, 2048, 2048][len(s):])[:3]
+        inp = scan_inputs(B, L, D, 16, torch.bfloat16, seed=0, device="cuda", on_device=True)
+        dout = torch.randn(B, D, L, device=dev).to(torch.bfloat16)
+        t = lambda x: x.transpose(1, 2)  # noqa: E731
+        fn = lambda: selective_scan_bwd(t(dout), t(inp.u), t(inp.delta), inp.A, t(inp.B), t(inp.C), inp.D,  # noqa: E731
+                                        t(inp.z), z_mode="silu", delta_bias=inp.delta_bias, delta_softplus=True)
+        extra = {"bytes": B * L * D * (4 * 2 + 3 * 4) + B * L * 16 * (2 * 2 + 2 * 4)}
     elif a.case == "ssd_bwd":
         # SSD backward (exact per-head chunk form, TF32 chunk GEMMs) for the bf16 forward's inputs
         from .kernels.ssd import ssd_chunk_scan_bwd
