@@ -10,8 +10,10 @@
 //   dC_t += dy_t h_t,  dB_t += dh_t delta_t u_t,  dA += dh_t h_{t-1} a_t delta_t,
 //   ddelta_t = sum_n dh_t (h_{t-1} a_t A + B_t u_t),
 //   du_t = dy_t D + delta_t dh_t . B_t,  dD += dy_t u_t.
-// One thread per (batch row, channel), 16 fp32 states in registers.  A first
-// pass recomputes the forward and stores h every 16 steps in the workspace;
+// One thread per (batch row, channel), 16 fp32 states in registers; the B, C
+// rows of each 16-step chunk are staged in shared memory for the whole CTA.
+// A first pass recomputes the forward and stores h every 16 steps in the
+// workspace;
 // the reverse pass reloads each checkpoint, recomputes the chunk's h_{t-1}
 // into shared memory and walks it backwards.  dB, dC are sums over channels:
 // a warp reduce-scatter leaves lane l with the warp's sum of value l, one
@@ -72,21 +74,41 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
     return SP ? softplus<false>(raw) : raw;
   };
 
+  // B, C of one kT-step chunk staged in shared memory (fp32, zero past the
+  // sequence / dstate): every thread of the CTA reads the same rows
+  __shared__ float sbc[2][kT][NS];
+  auto stage = [&](int k, int nw) {
+    const int t0 = k * kT;
+    for (int e = tid; e < nw * kT * NS; e += CH) {
+      const int w = e / (kT * NS), i = (e / NS) % kT, n = e % NS;
+      const int t = t0 + i;
+      float v = 0.f;
+      if (t < p.seqlen && n < N) v = w ? ld<T>(p.C, p.sC, b, t, n) : ld<T>(p.B, p.sB, b, t, n);
+      sbc[w][i][n] = v;
+    }
+  };
+
   // ---- pass 1: forward recompute, checkpoints every kT steps -----------------
   float h[NS];
 #pragma unroll
   for (int n = 0; n < NS; ++n) h[n] = (p.h0 && n < N) ? p.h0[((int64_t)b * p.dim + dc) * N + n] : 0.f;
-  for (int t = 0; t < p.seqlen; ++t) {
-    if (t % kT == 0 && dvalid) {
+  for (int k = 0; k < nck; ++k) {
+    const int t0 = k * kT, tn = min(kT, p.seqlen - t0);
+    __syncthreads();  // the previous chunk's rows are consumed
+    stage(k, 1);
+    __syncthreads();
+    if (dvalid) {
 #pragma unroll
-      for (int n = 0; n < NS; ++n) ck[(t / kT) * NS + n] = h[n];
+      for (int n = 0; n < NS; ++n) ck[k * NS + n] = h[n];
     }
-    float raw;
-    const float dl = delta_of(t, raw);
-    const float du = dl * ld<T>(p.u, p.su, b, t, dc);
+    for (int i = 0; i < tn; ++i) {
+      float raw;
+      const float dl = delta_of(t0 + i, raw);
+      const float du = dl * ld<T>(p.u, p.su, b, t0 + i, dc);
 #pragma unroll
-    for (int n = 0; n < NS; ++n)
-      if (n < N) h[n] = fmaf(ex2_approx(dl * a2[n]), h[n], du * ld<T>(p.B, p.sB, b, t, n));
+      for (int n = 0; n < NS; ++n)
+        if (n < N) h[n] = fmaf(ex2_approx(dl * a2[n]), h[n], du * sbc[0][i][n]);
+    }
   }
 
   // ---- pass 2: reverse ------------------------------------------------------
@@ -96,6 +118,9 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
   float dDacc = 0.f, dbacc = 0.f;
   for (int k = nck - 1; k >= 0; --k) {
     const int t0 = k * kT, tn = min(kT, p.seqlen - t0);
+    __syncthreads();
+    stage(k, 2);
+    __syncthreads();
 #pragma unroll
     for (int n = 0; n < NS; ++n) h[n] = dvalid ? ck[k * NS + n] : 0.f;
     for (int i = 0; i < tn; ++i) {
@@ -107,7 +132,7 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
       const float du = dl * ld<T>(p.u, p.su, b, t, dc);
 #pragma unroll
       for (int n = 0; n < NS; ++n)
-        if (n < N) h[n] = fmaf(ex2_approx(dl * a2[n]), h[n], du * ld<T>(p.B, p.sB, b, t, n));
+        if (n < N) h[n] = fmaf(ex2_approx(dl * a2[n]), h[n], du * sbc[0][i][n]);
     }
     for (int i = tn - 1; i >= 0; --i) {
       const int t = t0 + i;
@@ -119,8 +144,8 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
       float y = Dd * u;
 #pragma unroll
       for (int n = 0; n < NS; ++n) {
-        Bv[n] = n < N ? ld<T>(p.B, p.sB, b, t, n) : 0.f;
-        Cv[n] = n < N ? ld<T>(p.C, p.sC, b, t, n) : 0.f;
+        Bv[n] = sbc[0][i][n];
+        Cv[n] = sbc[1][i][n];
         hp[n] = hs[(i * NS + n) * CH + tid];
         at[n] = n < N ? ex2_approx(dl * a2[n]) : 0.f;
         y = fmaf(Cv[n], fmaf(at[n], hp[n], dl * Bv[n] * u), y);
