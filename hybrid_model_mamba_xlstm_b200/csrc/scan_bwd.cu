@@ -48,7 +48,10 @@ HXM_DEV float ld(const void* base, const int64_t* s, int b, int t, int c) {
 
 template <typename T, int ZMODE, bool SP>
 __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
-  extern __shared__ float hs[];  // [kT][NS][CH]: h_{t-1} of the chunk
+  extern __shared__ float hs[];  // [kT][NS][CH]: h_{t-1} of the chunk, then [3][kT][CH]
+  float* sdl = hs + kT * NS * CH;   // delta_t of the chunk (per channel)
+  float* suv = sdl + kT * CH;       // u_t
+  float* ssg = suv + kT * CH;       // d delta / d raw (softplus' derivative, or 1)
   const int tid = threadIdx.x, lane = tid & 31;
   const int b = blockIdx.y;
   const int d = blockIdx.x * CH + tid;
@@ -129,16 +132,19 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
       for (int n = 0; n < NS; ++n) hs[(i * NS + n) * CH + tid] = h[n];
       float raw;
       const float dl = delta_of(t, raw);
-      const float du = dl * ld<T>(p.u, p.su, b, t, dc);
+      const float uv = ld<T>(p.u, p.su, b, t, dc);
+      const float du = dl * uv;
+      sdl[i * CH + tid] = dl;
+      suv[i * CH + tid] = uv;
+      ssg[i * CH + tid] = SP ? (raw > 20.f ? 1.f : sigmoid_acc(raw)) : 1.f;
 #pragma unroll
       for (int n = 0; n < NS; ++n)
         if (n < N) h[n] = fmaf(ex2_approx(dl * a2[n]), h[n], du * sbc[0][i][n]);
     }
     for (int i = tn - 1; i >= 0; --i) {
       const int t = t0 + i;
-      float raw;
-      const float dl = delta_of(t, raw);
-      const float u = ld<T>(p.u, p.su, b, t, dc);
+      const float dl = sdl[i * CH + tid];
+      const float u = suv[i * CH + tid];
       const float go = dvalid ? ld<T>(p.dout, p.sdo, b, t, dc) : 0.f;
       float Bv[NS], Cv[NS], hp[NS], at[NS];
       float y = Dd * u;
@@ -177,7 +183,7 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
         duv = fmaf(dh[n] * dl, Bv[n], duv);
         dh[n] *= at[n];
       }
-      const float draw = SP ? (raw > 20.f ? ddl : ddl * sigmoid_acc(raw)) : ddl;
+      const float draw = ddl * ssg[i * CH + tid];
       dbacc += draw;
       if (dvalid) {
         const int64_t o = ((int64_t)b * p.seqlen + t) * p.dim + d;
@@ -218,7 +224,7 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
 
 template <typename T, int ZMODE, bool SP>
 hxm_status launch(const Params& p, cudaStream_t st) {
-  const size_t smem = sizeof(float) * kT * NS * CH;
+  const size_t smem = sizeof(float) * kT * (NS + 3) * CH;
   auto kern = scan_bwd_kernel<T, ZMODE, SP>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dim + CH - 1) / CH, p.batch);
