@@ -29,7 +29,7 @@ terms, W = dL/dS * S, with W's diagonal (the largest entries under strong
 decay, present in both sums) left out exactly instead of cancelled in
 rounding.
 
-The chunk GEMMs are batched fp32 cuBLAS calls (torch.matmul); the gate
+The chunk GEMMs are batched cuBLAS calls (torch.matmul; fp32, or TF32 for bf16 inputs); the gate
 scaling, the two chunk-level recurrences and the gate gradients (a suffix sum
 over the whole sequence) are this library's kernels.  Memory: two fp32 state
 arrays of (B, H, L / chunk, dqk, w), w = dv + 1 rounded up to 8.  Exponents
