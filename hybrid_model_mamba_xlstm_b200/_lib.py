@@ -70,6 +70,7 @@ class MlstmArgs(ct.Structure):
         ("workspace", ct.c_void_p), ("workspace_bytes", ct.c_size_t),
         ("q_tstride", ct.c_int64), ("k_tstride", ct.c_int64), ("v_tstride", ct.c_int64),
         ("h_tstride", ct.c_int64), ("i_tstride", ct.c_int64), ("f_tstride", ct.c_int64),
+        ("error_flag", ct.c_void_p), ("wait_limit_cycles", ct.c_int64),
     ]
 
 
@@ -84,6 +85,7 @@ class SsdArgs(ct.Structure):
         ("D", ct.c_void_p), ("dt_bias", ct.c_void_p), ("dt_softplus", ct.c_int32),
         ("y", ct.c_void_p), ("h0", ct.c_void_p), ("hT", ct.c_void_p),
         ("workspace", ct.c_void_p), ("workspace_bytes", ct.c_size_t),
+        ("error_flag", ct.c_void_p), ("wait_limit_cycles", ct.c_int64),
     ]
 
 
@@ -97,7 +99,7 @@ class SlstmArgs(ct.Structure):
         ("h_out", ct.c_void_p),
         ("h0", ct.c_void_p), ("c0", ct.c_void_p),
         ("hT", ct.c_void_p), ("cT", ct.c_void_p),
-        ("error_flag", ct.c_void_p),
+        ("error_flag", ct.c_void_p), ("wait_limit_cycles", ct.c_int64),
     ]
 
 

@@ -71,7 +71,8 @@ struct Params {
   float* nT;
   float* mT;
   int state_t;  // state stored transposed (SSD: (b, h, p, n))
-  int* error_flag;
+  int* error_flag;       // set to 1 when a bounded wait gave up (outputs then unwritten)
+  long long wait_limit;  // SM cycles per bounded wait
 };
 
 template <int DK>
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto wait_load = [&](int c) {
         const int st = c % Lt::kStages;
-        const bool ok = tc::mbar_wait(bar_load + st, waits[st] & 1, abort_flag);
+        const bool ok = tc::mbar_wait(bar_load + st, waits[st] & 1, abort_flag, p.wait_limit);
         if (ok) {
           ++waits[st];
           pend[st] = false;
@@ -298,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll 1
       for (int c = 0; ok && c < nchunks; ++c) {
-        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag)) break;
+        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag, p.wait_limit)) break;
         tc::tc_fence_after();
         issue_out(c);
         if (kScaleK) {
@@ -310,20 +311,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc::tc_fence_after();
             issue_s(c + 1);
           }
-          if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) break;
+          if (!tc::mbar_wait(bar_a, c & 1, abort_flag, p.wait_limit)) break;
           if (c + 2 < nchunks) {  // this chunk's stage is free
             load_q(c + 2);
             load_kv(c + 2);
           }
         } else {
           tc::mma_commit(bar_a);
-          if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) break;
+          if (!tc::mbar_wait(bar_a, c & 1, abort_flag, p.wait_limit)) break;
           if (c + 1 < nchunks) load_q(c + 1);
-          if (!tc::mbar_wait(bar_vready, c & 1, abort_flag)) break;
+          if (!tc::mbar_wait(bar_vready, c & 1, abort_flag, p.wait_limit)) break;
           tc::tc_fence_after();
           issue_update(c);
           tc::mma_commit(bar_b);
-          if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) break;
+          if (!tc::mbar_wait(bar_b, c & 1, abort_flag, p.wait_limit)) break;
           if (c + 1 < nchunks) {
             load_kv(c + 1);
             if (!wait_load(c + 1)) break;
@@ -543,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = tg < p.seqlen;
       float* denp = denp0 + (c & 1) * 2 * kC;
       // ---- wait S; P = causal(S) * weight -> smem (bf16), this half's 64 columns ----
-      if (!tc::mbar_wait(bar_s, c & 1, abort_flag)) bad = 1;
+      if (!tc::mbar_wait(bar_s, c & 1, abort_flag, p.wait_limit)) bad = 1;
       tc::tc_fence_after();
       {
         float2 den2 = make_float2(0.f, 0.f);  // rowsum of P, two partial sums
@@ -649,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         compute_gates(c + 1, gx0, gx1, m_new_cur, gn, rho_next, m_new_next, sep_next);
         if (c + 2 < nchunks) load_gates(c + 2, gx0, gx1);
       }
-      if (!tc::mbar_wait(bar_a, c & 1, abort_flag)) bad = 1;
+      if (!tc::mbar_wait(bar_a, c & 1, abort_flag, p.wait_limit)) bad = 1;
       tc::tc_fence_after();
       if (!kScaleK) {
         // V rows *= kscale, the normalizer's B row 0 = kscale: the update is K^T (kscale . V)
@@ -726,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!kScaleK) {
-        if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) bad = 1;
+        if (!tc::mbar_wait(bar_b, c & 1, abort_flag, p.wait_limit)) bad = 1;
         tc::tc_fence_after();
       }
       // ---- snapshot of the updated state for the next chunk's Hint, decayed state ----

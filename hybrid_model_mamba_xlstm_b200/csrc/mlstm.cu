@@ -11,29 +11,42 @@
 
 using hxm::mlstm::Params;
 
-static hxm_status fill(const hxm_mlstm_args* a, Params& p) {
-  HXM_REQUIRE(a != nullptr, "hxm_mlstm_chunkwise_fwd: args is NULL");
-  HXM_REQUIRE(a->struct_size == sizeof(hxm_mlstm_args), "hxm_mlstm_chunkwise_fwd: struct_size %zu != %zu",
-              a->struct_size, sizeof(hxm_mlstm_args));
+namespace hxm {
+namespace mlstm {
+
+hxm_status fill(const hxm_mlstm_args* a, Params& p, const char* who) {
+  HXM_REQUIRE(a != nullptr, "%s: args is NULL", who);
+  HXM_REQUIRE(a->struct_size == sizeof(hxm_mlstm_args), "%s: struct_size %zu != %zu", who, a->struct_size,
+              sizeof(hxm_mlstm_args));
   HXM_REQUIRE(a->batch >= 0 && a->heads >= 0 && a->seqlen >= 0 && a->dqk >= 1 && a->dv >= 1,
-              "hxm_mlstm_chunkwise_fwd: bad dims B=%d H=%d L=%d dqk=%d dv=%d", a->batch, a->heads, a->seqlen,
-              a->dqk, a->dv);
-  HXM_REQUIRE(a->gate_mode == 0 || a->gate_mode == 1, "hxm_mlstm_chunkwise_fwd: bad gate_mode %d", a->gate_mode);
-  HXM_REQUIRE(a->io_dtype == HXM_F32 || a->io_dtype == HXM_BF16, "hxm_mlstm_chunkwise_fwd: io_dtype must be f32 or bf16");
-  HXM_REQUIRE(a->chunk == 64 || a->chunk == 128, "hxm_mlstm_chunkwise_fwd: chunk must be 64 or 128 (got %d)", a->chunk);
-  HXM_REQUIRE_SUPPORTED(a->dqk <= 512 && a->dv <= 512, "hxm_mlstm_chunkwise_fwd: dqk, dv <= 512 supported");
+              "%s: bad dims B=%d H=%d L=%d dqk=%d dv=%d", who, a->batch, a->heads, a->seqlen, a->dqk, a->dv);
+  HXM_REQUIRE(a->gate_mode == 0 || a->gate_mode == 1, "%s: bad gate_mode %d", who, a->gate_mode);
+  HXM_REQUIRE(a->io_dtype == HXM_F32 || a->io_dtype == HXM_BF16, "%s: io_dtype must be f32 or bf16", who);
+  // The tensor-core kernels tile time in 128-step chunks (the chunkwise result does not depend on
+  // the chunk length); other lengths are refused rather than silently replaced.
+  HXM_REQUIRE_SUPPORTED(a->chunk == 0 || a->chunk == kChunk,
+                        "%s: chunk %d unsupported (the kernels run %d-step chunks; pass 0 or %d)", who, a->chunk,
+                        kChunk, kChunk, kChunk);
+  HXM_REQUIRE_SUPPORTED(a->dqk <= 512 && a->dv <= 512, "%s: dqk, dv <= 512 supported", who);
   p.batch = a->batch; p.heads = a->heads; p.seqlen = a->seqlen; p.dqk = a->dqk; p.dv = a->dv;
-  p.chunk = a->chunk; p.gate_mode = a->gate_mode; p.io_dtype = a->io_dtype;
+  p.chunk = kChunk; p.gate_mode = a->gate_mode; p.io_dtype = a->io_dtype;
   p.q = a->q; p.k = a->k; p.v = a->v; p.log_i = a->log_i; p.log_f = a->log_f; p.h = a->h;
   for (int i = 0; i < 2; ++i) {
     p.sq[i] = a->q_stride[i]; p.sk[i] = a->k_stride[i]; p.sv[i] = a->v_stride[i];
     p.si[i] = a->i_stride[i]; p.sf[i] = a->f_stride[i]; p.sh[i] = a->h_stride[i];
   }
   p.C0 = a->C0; p.n0 = a->n0; p.m0 = a->m0; p.CT = a->CT; p.nT = a->nT; p.mT = a->mT;
-  hxm::mlstm::set_time_strides(p, a);
+  set_time_strides(p, a);
   p.workspace = a->workspace; p.workspace_bytes = a->workspace_bytes;
+  p.error_flag = a->error_flag;
+  p.wait_limit = a->wait_limit_cycles > 0 ? a->wait_limit_cycles : 4000000000ll;
   return HXM_OK;
 }
+
+}  // namespace mlstm
+}  // namespace hxm
+
+using hxm::mlstm::fill;
 
 static bool use_tc(const Params& p) {
   return p.io_dtype == HXM_BF16 && p.gate_mode == 0 && hxm::mlstm::chunkwise_tc_workspace(p) != (size_t)-1;
@@ -42,7 +55,7 @@ static bool use_stream(const Params& p) { return !use_tc(p) && hxm::mlstm::strea
 
 extern "C" size_t hxm_mlstm_workspace_size(const hxm_mlstm_args* a) {
   Params p{};
-  if (fill(a, p) != HXM_OK) return 0;
+  if (fill(a, p, "hxm_mlstm_workspace_size") != HXM_OK) return 0;
   if (use_tc(p)) return hxm::mlstm::chunkwise_tc_workspace(p);
   return use_stream(p) ? hxm::mlstm::stream_workspace(p) : 0;
 }
@@ -50,7 +63,7 @@ extern "C" size_t hxm_mlstm_workspace_size(const hxm_mlstm_args* a) {
 extern "C" hxm_status hxm_mlstm_chunkwise_fwd(const hxm_mlstm_args* a, void* stream) {
   hxm::clear_error();
   Params p{};
-  hxm_status s = fill(a, p);
+  hxm_status s = fill(a, p, "hxm_mlstm_chunkwise_fwd");
   if (s != HXM_OK) return s;
   if (p.batch == 0 || p.heads == 0) return HXM_OK;
   HXM_REQUIRE(p.seqlen == 0 || (p.q && p.k && p.v && p.log_i && p.log_f && p.h),

@@ -9,6 +9,8 @@
 namespace hxm {
 namespace mlstm {
 
+constexpr int kChunk = 128;  // time chunk of the tensor-core kernels
+
 struct Params {
   int batch, heads, seqlen, dqk, dv, chunk, gate_mode;
   hxm_dtype io_dtype;
@@ -33,6 +35,8 @@ struct Params {
   void* workspace;
   size_t workspace_bytes;
   int64_t tq, tk, tv, th, ti, tf;  // time strides (elements)
+  int* error_flag;                  // device int set to 1 when a bounded wait gave up, or NULL
+  long long wait_limit;             // SM cycles per bounded device wait
 };
 
 // Time strides from the ABI struct (0 = dense).
@@ -46,13 +50,19 @@ inline void set_time_strides(Params& p, const hxm_mlstm_args* a) {
   p.tf = a->f_tstride ? a->f_tstride : g;
 }
 
+// Checks an hxm_mlstm_args and fills p (workspace included); `who` names the entry point in errors.
+hxm_status fill(const hxm_mlstm_args* a, Params& p, const char* who);
+
 // Exact step-by-step recurrence on CUDA cores (any gate mode / dtype / dims <= 512).
-hxm_status launch_recurrent(const Params& p, cudaStream_t st);
+// only: NULL, or a device int per (b, h) selecting the pairs to run (nonzero).
+hxm_status launch_recurrent(const Params& p, cudaStream_t st, const int* only = nullptr);
 // tcgen05 chunkwise kernel (bf16, per-head gates, dqk 128/256, stabilized); no workspace.
 hxm_status launch_chunkwise_tc(const Params& p, cudaStream_t st);
 size_t chunkwise_tc_workspace(const Params& p);  // (size_t)-1 when the shape is not covered
 // Key-streaming tcgen05 kernel (bf16, per-head or per-channel gates, dqk 128/256/512) with a
-// prescale pass into a caller-owned workspace of stream_workspace() bytes.
+// prescale pass into a caller-owned workspace of stream_workspace() bytes.  (b, h) pairs whose
+// chunk scaling would leave the fp32 range (decided on the device by the prescale pass) are
+// run by the exact recurrent kernel instead, in the same call.
 bool stream_shape_ok(const Params& p);
 size_t stream_workspace(const Params& p);
 hxm_status launch_stream(const Params& p, cudaStream_t st);

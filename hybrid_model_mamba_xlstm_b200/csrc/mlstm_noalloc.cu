@@ -15,13 +15,16 @@
 //   - Scratch: one file-scope device array of kScratchBytes = 32 MiB.  Every
 //     GPU that loads this library holds those 32 MiB until the process exits.
 //   - Requests whose scratch exceeds 32 MiB are rejected with HXM_EBADARG
-//     (scratch = 2 * B*H*L*dqk * 2 bytes + 3 * B*H*ceil(L/128)*dqk * 4 bytes,
-//     each rounded up to 256 bytes).
+//     (scratch = 2 * B*H*L*dqk * 2 bytes + 3 * B*H*ceil(L/128)*dqk * 4 bytes
+//     + B*H * 4 bytes, each rounded up to 256 bytes).
 //   - The first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (with that device current); make that first call
-//     before any stream capture on the device.
-//   - All calls share the one array and each call fully rewrites the part it
-//     reads (nothing in it has to start at zero); calls whose executions
+//     cudaGetSymbolAddress (with that device current) and keeps it for the
+//     life of the process; make that first call before any stream capture on
+//     the device.  Resetting the device (cudaDeviceReset) after it is not
+//     supported: the kept address would be stale.
+//   - All calls share the one array.  Each call clears the part that must
+//     start at zero (the per-(b, h) range flags, by cudaMemsetAsync) and
+//     fully rewrites the rest before reading it; calls whose executions
 //     overlap on the GPU (other streams, or other host threads) race on it.
 //   - No cudaMalloc, cudaFree or allocating library routine is called.
 #include <mutex>
@@ -62,41 +65,27 @@ hxm_status scratch_for_current_device(void** out) {
 
 extern "C" hxm_status hxm_mlstm_chunkwise_fwd_noalloc(const hxm_mlstm_args* a, void* stream) {
   using hxm::mlstm::Params;
+  static const char* who = "hxm_mlstm_chunkwise_fwd_noalloc";
   hxm::clear_error();
-  HXM_REQUIRE(a != nullptr, "hxm_mlstm_chunkwise_fwd_noalloc: args is NULL");
-  HXM_REQUIRE(a->struct_size == sizeof(hxm_mlstm_args), "hxm_mlstm_chunkwise_fwd_noalloc: struct_size %zu != %zu",
-              a->struct_size, sizeof(hxm_mlstm_args));
-  HXM_REQUIRE(a->batch >= 0 && a->heads >= 0 && a->seqlen >= 0 && a->dqk >= 1 && a->dv >= 1,
-              "hxm_mlstm_chunkwise_fwd_noalloc: bad dims");
-  HXM_REQUIRE(a->gate_mode == 0 || a->gate_mode == 1, "hxm_mlstm_chunkwise_fwd_noalloc: bad gate_mode %d",
-              a->gate_mode);
   Params p{};
-  p.batch = a->batch; p.heads = a->heads; p.seqlen = a->seqlen; p.dqk = a->dqk; p.dv = a->dv;
-  p.chunk = a->chunk; p.gate_mode = a->gate_mode; p.io_dtype = a->io_dtype;
-  p.q = a->q; p.k = a->k; p.v = a->v; p.log_i = a->log_i; p.log_f = a->log_f; p.h = a->h;
-  for (int i = 0; i < 2; ++i) {
-    p.sq[i] = a->q_stride[i]; p.sk[i] = a->k_stride[i]; p.sv[i] = a->v_stride[i];
-    p.si[i] = a->i_stride[i]; p.sf[i] = a->f_stride[i]; p.sh[i] = a->h_stride[i];
-  }
-  p.C0 = a->C0; p.n0 = a->n0; p.m0 = a->m0; p.CT = a->CT; p.nT = a->nT; p.mT = a->mT;
-  hxm::mlstm::set_time_strides(p, a);
+  hxm_status s = hxm::mlstm::fill(a, p, who);  // the same argument checks as hxm_mlstm_chunkwise_fwd
+  if (s != HXM_OK) return s;
   if (p.batch == 0 || p.heads == 0 || p.seqlen == 0) {
-    hxm::set_error("hxm_mlstm_chunkwise_fwd_noalloc: empty problem (batch, heads and seqlen must be > 0)");
+    hxm::set_error("%s: empty problem (batch, heads and seqlen must be > 0)", who);
     return HXM_EBADARG;
   }
   HXM_REQUIRE_SUPPORTED(hxm::mlstm::stream_shape_ok(p),
-                        "hxm_mlstm_chunkwise_fwd_noalloc: needs bf16, dqk in {128, 256, 512}, dv %% 32 == 0 and "
-                        "16-byte aligned v / h");
-  HXM_REQUIRE(p.q && p.k && p.v && p.log_i && p.log_f && p.h, "hxm_mlstm_chunkwise_fwd_noalloc: NULL tensor pointer");
+                        "%s: needs bf16, dqk in {128, 256, 512}, dv %% 32 == 0 and 16-byte aligned v / h", who);
+  HXM_REQUIRE(p.q && p.k && p.v && p.log_i && p.log_f && p.h, "%s: NULL tensor pointer", who);
   const size_t need = hxm::mlstm::stream_workspace(p);
   HXM_REQUIRE(need <= kScratchBytes,
-              "hxm_mlstm_chunkwise_fwd_noalloc: needs %zu bytes of scratch, the fixed device array holds %zu "
-              "(32 MiB); use hxm_mlstm_chunkwise_fwd with a workspace",
-              need, kScratchBytes);
+              "%s: needs %zu bytes of scratch, the fixed device array holds %zu (32 MiB); use "
+              "hxm_mlstm_chunkwise_fwd with a workspace",
+              who, need, kScratchBytes);
   void* scratch = nullptr;
-  hxm_status s = scratch_for_current_device(&scratch);
+  s = scratch_for_current_device(&scratch);
   if (s != HXM_OK) return s;
-  p.workspace = scratch;
+  p.workspace = scratch;  // args->workspace is ignored
   p.workspace_bytes = kScratchBytes;
   return hxm::mlstm::launch_stream(p, static_cast<cudaStream_t>(stream));
 }

@@ -22,10 +22,15 @@
 //     per-row factors rho_e(c-1), rho_e(c) (snapshot and decay at once) are
 //     applied when the state is read back for the next chunk.  Two 64-channel
 //     key panels (Qs and Ks of each) per 64 KB slot stream through a 2-slot
-//     TMA ring; n lives in shared memory.  No overflow as long as the total
-//     log forget gate of one 128-step chunk stays above about -160 per channel
-//     (exponents are bounded by half of it); the reference itself overflows
-//     for input-gate pre-activations above ~88 and so does this kernel.
+//     TMA ring; n lives in shared memory.
+//  Range: every factor above is e^x with x <= |g|/2 + log i.  The prescale
+//  pass checks each exponent it forms against kMaxExp (fp32 / bf16 hold e^88;
+//  the margin covers |q|, |k|, |v| and the sums over keys and steps) and
+//  flags the (b, h) pair when one is larger or not finite, e.g. a chunk whose
+//  forget gates sum below about -128 per channel, or f = 0.  The stream
+//  kernel skips flagged pairs and the exact recurrent kernel
+//  (mlstm_recurrent.cu) runs them in the same call, so the results hold for
+//  any gate values the reference itself computes without overflow.
 #include "capi_internal.h"
 #include "common.cuh"
 #include "mlstm.h"
@@ -38,6 +43,7 @@ namespace mlstm {
 constexpr int kC = 128;
 constexpr int kDV = 64;
 constexpr int kPanel = 16384;
+constexpr float kMaxExp = 64.f;  // largest exponent of a chunk factor the stream kernel takes
 
 // ---------------------------------------------------------------- pre-pass --
 // grid (B*H*nchunks, ceil(DK/(128*NJ))), block 128: thread = NJ adjacent key
@@ -46,9 +52,10 @@ constexpr int kPanel = 16384;
 // same for every channel, so the block forms them once per step (thread t,
 // one scan over the chunk) and the channels only multiply; per-channel gates
 // take two exponentials per element.
+// unsafe[b*heads + h] is set to 1 when an exponent exceeds kMaxExp or is not finite.
 template <typename T, int NJ>
 __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks,
-                                                             float* decay, float* rho_e, float* nadd) {
+                                                             float* decay, float* rho_e, float* nadd, int* unsafe) {
   __shared__ float fq[kC], fk[kC], red[4];
   const int nch = (p.seqlen + kC - 1) / kC;
   const int c = blockIdx.x % nch;
@@ -83,8 +90,11 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
       gs += red[i];
     }
     const float rho = 0.5f * gs;
-    fq[tid] = __expf(bt - rho);
-    fk[tid] = __expf(rho - bt + lit);
+    const float xq = bt - rho, xk = rho - bt + lit;
+    // !(x <= max) also catches NaN (e.g. log f = -inf); one store per flagged block suffices
+    if (!(xq <= kMaxExp) || !(xk <= kMaxExp)) unsafe[bh] = 1;
+    fq[tid] = __expf(xq);
+    fk[tid] = __expf(xk);
     __syncthreads();
 #pragma unroll
     for (int u = 0; u < NJ; ++u) g[u] = gs;
@@ -107,6 +117,7 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
     eh[u] = __expf(0.5f * g[u]);  // e^rho
   }
   const int64_t ob = (int64_t)bh * p.seqlen * p.dqk;
+  bool bad = false;
 #pragma unroll 4
   for (int t = 0; t < tn; ++t) {
     const int64_t tt = t0 + t;
@@ -131,8 +142,10 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
       } else {
         bt[u] += lf[tt * p.tf + j0 + u];
         const float rho = 0.5f * g[u];
-        a = __expf(bt[u] - rho);
-        e = __expf(rho - bt[u] + li[tt * p.ti + j0 + u]);
+        const float xq = bt[u] - rho, xk = rho - bt[u] + li[tt * p.ti + j0 + u];
+        bad |= !(xq <= kMaxExp) || !(xk <= kMaxExp);
+        a = __expf(xq);
+        e = __expf(xk);
       }
       qs[u] = qv[u] * a;
       ks[u] = kv[u] * e;
@@ -148,6 +161,7 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
       Ks[o] = __float2bfloat16_rn(ks[0]);
     }
   }
+  if (bad) unsafe[bh] = 1;
 #pragma unroll
   for (int u = 0; u < NJ; ++u) {
     const int64_t vi = ((int64_t)bh * nch + c) * p.dqk + j0 + u;
@@ -214,7 +228,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     mlstm_stream_kernel(const __grid_constant__ CUtensorMap tmQs, const __grid_constant__ CUtensorMap tmKs,
                         const __grid_constant__ CUtensorMap tmV,
                         const Params p, const float* __restrict__ decay, const float* __restrict__ rho_e,
-                        const float* __restrict__ nadd) {
+                        const float* __restrict__ nadd, const int* __restrict__ unsafe) {
+  // pairs flagged by the prescale pass are run by the recurrent kernel (uniform over the CTA)
+  if (unsafe[blockIdx.z * p.heads + blockIdx.y]) return;
   using L = SL<DK>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -286,10 +302,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
         const uint32_t tH = tb + L::tH + (c & 1) * kDV;
-        if (!tc::mbar_wait(bar_snap, c & 1, abort_flag)) break;
+        if (!tc::mbar_wait(bar_snap, c & 1, abort_flag, p.wait_limit)) break;
         tc::tc_fence_after();
         // the state update below needs this chunk's V
-        if (!tc::mbar_wait(bar_v, waited_v & 1, abort_flag)) break;
+        if (!tc::mbar_wait(bar_v, waited_v & 1, abort_flag, p.wait_limit)) break;
         ++waited_v;
         tc::tc_fence_after();
         // S = Qs Ks^T, H = Qs Snap and state += Ks^T V, slot by slot from the ring
@@ -297,7 +313,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll 1
         for (int i = 0; i < L::kLPC; ++i) {
           const int idx = c * L::kLPC + i, slot = idx % L::kStages;
-          if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) { ok = false; break; }
+          if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag, p.wait_limit)) { ok = false; break; }
           tc::tc_fence_after();
           const uint32_t sb = sbase + L::kRing + slot * L::kSlotB;
 #pragma unroll
@@ -324,14 +340,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         }
         if (!ok) break;
         // H += P V once P is written
-        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag)) break;
+        if (!tc::mbar_wait(bar_pready, c & 1, abort_flag, p.wait_limit)) break;
         tc::tc_fence_after();
         tc::static_for<kC / 16>([&](auto KS) {
           constexpr int ks = decltype(KS)::value;
           tc::mma_bf16_at<(ks / 4) * kPanel + (ks % 4) * 32, ks * 2048>(tH, dP, dV, idH, true);
         });
         tc::mma_commit(bar_b);
-        if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) break;
+        if (!tc::mbar_wait(bar_b, c & 1, abort_flag, p.wait_limit)) break;
         if (c + 1 < nch) load_v(c + 1);  // V is free
       }
       // leave nothing in flight (bounded): the MMAs, and a V load not waited for
@@ -348,7 +364,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll 1
       for (int idx = 0; idx < total_loads; ++idx) {
         const int slot = idx % L::kStages;
-        if (idx >= L::kStages && !tc::mbar_wait(&empty[slot], ((idx / L::kStages) - 1) & 1, abort_flag)) break;
+        if (idx >= L::kStages && !tc::mbar_wait(&empty[slot], ((idx / L::kStages) - 1) & 1, abort_flag, p.wait_limit)) break;
         const int c = idx / L::kLPC, i = idx % L::kLPC;
         unsigned char* dst = sm + L::kRing + slot * L::kSlotB;
         tc::mbar_expect_tx(&full[slot], L::kSlotB);
@@ -517,7 +533,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #pragma unroll 1
       for (int i = 0; i < L::kLPC; ++i) {
         const int idx = c * L::kLPC + i, slot = idx % L::kStages;
-        if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag)) bad = 1;
+        if (!tc::mbar_wait(&full[slot], (idx / L::kStages) & 1, abort_flag, p.wait_limit)) bad = 1;
         {  // this half's panel of the slot: 2i + hf
           const int pnl = 2 * i + hf;
           const unsigned char* qrow = sm + L::kRing + slot * L::kSlotB + hf * 2 * kPanel;
@@ -542,7 +558,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
       qnp[hf * kC + row] = qn;
       // ---- P = causal(S) -> smem (bf16), this half's 64 columns; rowsum partial --------
-      if (!tc::mbar_wait(bar_s, c & 1, abort_flag)) bad = 1;
+      if (!tc::mbar_wait(bar_s, c & 1, abort_flag, p.wait_limit)) bad = 1;
       tc::tc_fence_after();
       {
         float2 den2 = make_float2(0.f, 0.f);
@@ -588,7 +604,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(bar_pready);
-      if (!tc::mbar_wait(bar_b, c & 1, abort_flag)) bad = 1;
+      if (!tc::mbar_wait(bar_b, c & 1, abort_flag, p.wait_limit)) bad = 1;
       tc::tc_fence_after();
       // every worker agrees to go on (the qn / rowsum partials are visible)
       if (stream_workers_sync_or(bad)) { bad = 1; break; }
@@ -628,6 +644,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     if (p.nT && blockIdx.x == 0)
       for (int j = tid; j < DK; j += 32 * kWorkers) p.nT[(int64_t)bh * DK + j] = nst[j];
     if (p.mT && blockIdx.x == 0 && tid == 0) p.mT[bh] = 0.f;
+  } else if (!ok && tid == 0 && p.error_flag) {
+    atomicExch(p.error_flag, 1);  // a bounded wait gave up: this tile's outputs are not written
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -644,7 +662,8 @@ size_t stream_workspace(const Params& p) {
   const size_t nch = (p.seqlen + kC - 1) / kC;
   const size_t ops = (size_t)p.batch * p.heads * p.seqlen * p.dqk * 2;  // bf16 tensor
   const size_t vec = (size_t)p.batch * p.heads * nch * p.dqk * 4;
-  return 2 * align256(ops) + 3 * align256(vec);
+  const size_t flags = (size_t)p.batch * p.heads * 4;  // per (b, h): out of the kernel's range
+  return 2 * align256(ops) + 3 * align256(vec) + align256(flags);
 }
 
 bool stream_shape_ok(const Params& p) {
@@ -673,16 +692,18 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   float* decay = reinterpret_cast<float*>(ws + 2 * ops);
   float* rho_e = reinterpret_cast<float*>(ws + 2 * ops + vec);
   float* nadd = reinterpret_cast<float*>(ws + 2 * ops + 2 * vec);
+  int* unsafe = reinterpret_cast<int*>(ws + 2 * ops + 3 * vec);
+  HXM_CUDA_TRY(cudaMemsetAsync(unsafe, 0, sizeof(int) * (size_t)p.batch * p.heads, st));
   // two channels per thread when q, k rows allow 4-byte loads
   const bool pair = p.tq % 2 == 0 && p.tk % 2 == 0 && p.sq[0] % 2 == 0 && p.sq[1] % 2 == 0 && p.sk[0] % 2 == 0 &&
                     p.sk[1] % 2 == 0 && reinterpret_cast<uintptr_t>(p.q) % 4 == 0 &&
                     reinterpret_cast<uintptr_t>(p.k) % 4 == 0;
   if (pair) {
     dim3 pg(p.batch * p.heads * nch, (DK + 255) / 256);
-    mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd);
+    mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe);
   } else {
     dim3 pg(p.batch * p.heads * nch, (DK + 127) / 128);
-    mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd);
+    mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe);
   }
   hxm_status s = check_launch("hxm_mlstm_chunkwise_fwd (prescale)");
   if (s != HXM_OK) return s;
@@ -698,8 +719,10 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   auto kern = mlstm_stream_kernel<DK>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dv + kDV - 1) / kDV, p.heads, p.batch);
-  kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mv, p, decay, rho_e, nadd);
-  return check_launch("hxm_mlstm_chunkwise_fwd (stream)");
+  kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mv, p, decay, rho_e, nadd, unsafe);
+  if ((s = check_launch("hxm_mlstm_chunkwise_fwd (stream)")) != HXM_OK) return s;
+  // the flagged pairs, exactly (every other CTA of this launch returns at once)
+  return launch_recurrent(p, st, unsafe);
 }
 
 hxm_status launch_stream(const Params& p, cudaStream_t st) {

@@ -41,7 +41,8 @@ static hxm_status launch_dk(const Params& p, cudaStream_t st) {
   cp.so[0] = p.sh[0]; cp.so[1] = p.sh[1]; cp.so[2] = p.th;
   cp.C0 = p.C0; cp.n0 = p.n0; cp.m0 = p.m0; cp.CT = p.CT; cp.nT = p.nT; cp.mT = p.mT;
   cp.state_t = 0;
-  cp.error_flag = nullptr;
+  cp.error_flag = p.error_flag;
+  cp.wait_limit = p.wait_limit;
   const size_t smem = Layout<DK>::kBytes + 1024;
   auto kern = chunk_tc_kernel<DK, kMlstm>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

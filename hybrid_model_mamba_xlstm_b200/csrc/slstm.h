@@ -23,6 +23,7 @@ struct Params {
   float* hT;
   float* cT;
   int* error_flag;
+  long long wait_limit;        // cycles per bounded cross-CTA wait
 };
 
 hxm_status launch_simple(const Params& p, cudaStream_t st);

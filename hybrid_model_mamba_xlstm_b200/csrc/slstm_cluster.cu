@@ -69,12 +69,13 @@ HXM_DEV bool try_wait_cluster(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait on phase `parity`: false if it gave up (~2 s at the SM clock).
-HXM_DEV bool wait_bounded(uint64_t* bar, uint32_t parity) {
+// Bounded wait on phase `parity`: false if it gave up after `limit` SM cycles
+// (the caller's wait_limit_cycles; 4e9 ~ 2 s by default).
+HXM_DEV bool wait_bounded(uint64_t* bar, uint32_t parity, long long limit) {
   if (try_wait_cluster(bar, parity)) return true;
   const long long t0 = clock64();
   while (!try_wait_cluster(bar, parity))
-    if (clock64() - t0 > 4000000000ll) return false;
+    if (clock64() - t0 > limit) return false;
   return true;
 }
 HXM_DEV void cluster_sync() {
@@ -270,7 +271,7 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
     //     t + 1 before the barrier below: peers send step t + 1 partials only
     //     after their step t + 1 MMA, which needs this CTA's step t h, sent
     //     after that barrier.
-    bad = !wait_bounded(&bars[0], parity);
+    bad = !wait_bounded(&bars[0], parity, p.wait_limit);
     if (tid == 0 && !bad && t + 1 < p.seqlen) arm_tx(&bars[0], L::kPartTx);
     if (__syncthreads_or(bad)) {
       bad = true;
@@ -310,7 +311,7 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
     // (e) wait for every CTA's h (bounded); it lands directly in hprev.  Re-arm
     //     for step t + 1 first: peers send step t + 1 h only after this CTA's
     //     step t + 1 partials, sent after the barrier below.
-    bad = !wait_bounded(&bars[1], parity);
+    bad = !wait_bounded(&bars[1], parity, p.wait_limit);
     if (tid == 0 && !bad && t + 1 < p.seqlen) arm_tx(&bars[1], L::kHTx);
     if (__syncthreads_or(bad)) {
       bad = true;

@@ -34,6 +34,8 @@ static hxm_status launch_ssd(const hxm_ssd_args* a, cudaStream_t st) {
   cp.out = static_cast<__nv_bfloat16*>(a->y);
   cp.so[0] = cp.sx[0]; cp.so[1] = cp.sx[1]; cp.so[2] = cp.sx[2];
   cp.C0 = a->h0; cp.CT = a->hT; cp.state_t = 1;
+  cp.error_flag = a->error_flag;
+  cp.wait_limit = a->wait_limit_cycles > 0 ? a->wait_limit_cycles : 4000000000ll;
   const size_t smem = Layout<DK>::kBytes + 1024;
   auto kern = chunk_tc_kernel<DK, kSsd>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -49,7 +51,11 @@ extern "C" hxm_status hxm_ssd_chunk_scan_fwd(const hxm_ssd_args* a, void* stream
               a->struct_size, sizeof(hxm_ssd_args));
   HXM_REQUIRE(a->batch >= 0 && a->seqlen >= 0 && a->heads >= 0 && a->headdim >= 1 && a->dstate >= 1,
               "hxm_ssd_chunk_scan_fwd: bad dims");
-  HXM_REQUIRE(a->chunk == 64 || a->chunk == 128 || a->chunk == 256, "hxm_ssd_chunk_scan_fwd: chunk must be 64/128/256");
+  // the kernel tiles time in 128-step chunks (the chunkwise result does not depend on the length);
+  // other lengths are refused rather than silently replaced
+  HXM_REQUIRE_SUPPORTED(a->chunk == 0 || a->chunk == kC,
+                        "hxm_ssd_chunk_scan_fwd: chunk %d unsupported (the kernel runs %d-step chunks; pass 0 or %d)",
+                        a->chunk, kC, kC);
   HXM_REQUIRE(a->io_dtype == HXM_BF16, "hxm_ssd_chunk_scan_fwd: io_dtype must be bf16");
   HXM_REQUIRE_SUPPORTED(a->dstate == 128 || a->dstate == 256, "hxm_ssd_chunk_scan_fwd: dstate %d (128 or 256 supported)",
                         a->dstate);

@@ -17,11 +17,13 @@ __all__ = ["slstm_scan"]
 
 
 def slstm_scan(gates_pre, norm_weight, *, R=None, eps=1e-6, exponential_gate=True, h0=None, c0=None,
-               return_state=True, error_flag=None):
+               return_state=True, error_flag=None, wait_limit_cycles=0):
     """gates_pre (B, L, H, 4, hd) — gate_proj output viewed per head, blocks
     [i | f | o | c~]; norm_weight (hd,); R (H, hd, 4*hd) or None;
     h0, c0 (B, H, hd) fp32: the true hidden / cell state (the reference's
-    cache['h'], cache['c']).
+    cache['h'], cache['c']).  error_flag: a device int32 tensor set to 1 if a
+    bounded cross-CTA wait gave up; wait_limit_cycles: that bound in SM
+    cycles (0 = about 2 s).
     Returns h_seq (B, L, H, hd) in gates_pre's dtype [and (h, c) fp32]."""
     who = "slstm_scan"
     dev = require_cuda(gates_pre, norm_weight, R, h0, c0, who=who)
@@ -54,6 +56,6 @@ def slstm_scan(gates_pre, norm_weight, *, R=None, eps=1e-6, exponential_gate=Tru
     a.h0, a.c0 = ptr(h0), ptr(c0)
     if st is not None:
         a.hT, a.cT = ptr(st[0]), ptr(st[1])
-    a.error_flag = ptr(error_flag)
+    a.error_flag, a.wait_limit_cycles = ptr(error_flag), int(wait_limit_cycles)
     _lib.call("hxm_slstm_scan_fwd", a, stream_of(dev))
     return (out, st) if return_state else out

@@ -17,11 +17,16 @@ from ._common import dtype_code, ptr, require_cuda, stream_of
 __all__ = ["ssd_chunk_scan", "ssd_chunk_scan_bwd", "SSDChunkScanFunction", "ssd_chunk_scan_fn"]
 
 
-def ssd_chunk_scan(x, dt, A, B, C, D=None, *, dt_bias=None, dt_softplus=False, chunk=256, initial_state=None,
-                   return_final_state=True):
+def ssd_chunk_scan(x, dt, A, B, C, D=None, *, dt_bias=None, dt_softplus=False, chunk=128, initial_state=None,
+                   return_final_state=True, error_flag=None, wait_limit_cycles=0):
     """x (B, L, H, P) bf16; dt (B, L, H) fp32; A (H,) fp32 (negative);
     B, C (B, L, N) bf16; D, dt_bias (H,) fp32; initial_state (B, H, P, N) fp32.
-    Returns y (B, L, H, P) [and the final state (B, H, P, N) fp32]."""
+    Returns y (B, L, H, P) [and the final state (B, H, P, N) fp32].
+    chunk: the kernel's time chunk, 128 (or 0 for the same); the chunkwise
+    result does not depend on it and other values raise.  error_flag: a
+    device int32 tensor set to 1 if a bounded device wait gave up (the
+    outputs are then not written); wait_limit_cycles: that bound in SM
+    cycles (0 = about 2 s)."""
     who = "ssd_chunk_scan"
     dev = require_cuda(x, dt, A, B, C, D, dt_bias, initial_state, who=who)
     if x.dim() != 4:
@@ -48,6 +53,7 @@ def ssd_chunk_scan(x, dt, A, B, C, D=None, *, dt_bias=None, dt_softplus=False, c
     ws_bytes = int(_lib.lib().hxm_ssd_workspace_size(a))
     ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
     a.workspace, a.workspace_bytes = ptr(ws), ws_bytes
+    a.error_flag, a.wait_limit_cycles = ptr(error_flag), int(wait_limit_cycles)
     _lib.call("hxm_ssd_chunk_scan_fwd", a, stream_of(dev))
     return (y, hT) if return_final_state else y
 
@@ -223,6 +229,6 @@ class SSDChunkScanFunction(torch.autograd.Function):
                 None, None)
 
 
-def ssd_chunk_scan_fn(x, dt, A, B, C, D=None, *, dt_bias=None, dt_softplus=False, chunk=256):
+def ssd_chunk_scan_fn(x, dt, A, B, C, D=None, *, dt_bias=None, dt_softplus=False, chunk=128):
     """Differentiable y = ssd_chunk_scan(x, dt, A, B, C, D, ...) (zero initial state)."""
     return SSDChunkScanFunction.apply(x, dt, A, B, C, D, dt_bias, dt_softplus, chunk)

@@ -32,9 +32,15 @@ rounding.
 The chunk GEMMs are batched cuBLAS calls (torch.matmul; fp32, or TF32 for bf16 inputs); the gate
 scaling, the two chunk-level recurrences and the gate gradients (a suffix sum
 over the whole sequence) are this library's kernels.  Memory: two fp32 state
-arrays of (B, H, L / chunk, dqk, w), w = dv + 1 rounded up to 8.  Exponents
-are bounded by half of a chunk's total log forget gate, which must stay above
-about -170 per channel for 64-step chunks.
+arrays of (B, H, L / chunk, dqk, w), w = dv + 1 rounded up to 8.
+
+Range (per-channel gates): the factors above are e^x with x at most
+|g| / 2 + max(log i, 0) over the chunk.  ``_channel_chunk`` picks the longest
+chunk (the requested one, then halves down to 8 steps) for which every chunk
+of the input keeps x <= MAX_EXP, so strong forget gates (e.g. logsigmoid of
+N(-4, 1) pre-activations, about -520 per 128 steps) shorten the chunk instead
+of overflowing; gates out of reach even at 8 steps (or not finite, f = 0)
+raise.  Per-head gates need no such choice (their form has no growing factor).
 """
 from __future__ import annotations
 
@@ -46,6 +52,9 @@ from ... import _lib
 from .._common import dtype_code, ptr, require_cuda, stream_of
 
 __all__ = ["mlstm_chunkwise_bwd"]
+
+MAX_EXP = 60.0  # largest exponent of a chunk factor (fp32 holds e^88; margin for the GEMM sums)
+MIN_CHUNK = 8
 
 
 @contextlib.contextmanager
@@ -211,7 +220,37 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     with _gemm_precision(io == torch.bfloat16 if tf32 is None else tf32):
         if gate_mode == 0:
             return _bwd_heads(q, k, v, gi, gf, dh, c, True, per_channel_out, st)
-        return _bwd_channels(q, k, v, gi, gf, dh, c, st)
+        return _bwd_channels(q, k, v, gi, gf, dh, _channel_chunk(gi, gf, c), st)
+
+
+def _channel_chunk(gi, gf, chunk):
+    """The longest chunk length <= chunk (halving, at least MIN_CHUNK) whose
+    separable factors stay within e^MAX_EXP for these per-channel gates
+    (B, H, L, Dqk): max over chunks and channels of |g| / 2 + max(log i, 0),
+    g the chunk's total log forget gate.  One host synchronization."""
+    bsz, nh, L, dqk = gf.shape
+    cands = []
+    c = int(chunk)
+    while c >= MIN_CHUNK:
+        cands.append(c)
+        c //= 2
+    if not cands:
+        raise ValueError(f"mlstm_chunkwise_bwd: chunk {chunk} < {MIN_CHUNK}")
+    worst = []
+    for c in cands:
+        nch = (L + c - 1) // c
+        pad = nch * c - L
+        lf = torch.nn.functional.pad(gf, (0, 0, 0, pad)).view(bsz, nh, nch, c, dqk)
+        li = torch.nn.functional.pad(gi, (0, 0, 0, pad)).view(bsz, nh, nch, c, dqk)
+        x = -0.5 * lf.sum(3) + li.amax(3).clamp_min(0.0)
+        worst.append(torch.nan_to_num(x, nan=float("inf")).amax())
+    worst = torch.stack(worst).cpu()
+    for c, w in zip(cands, worst.tolist()):
+        if w <= MAX_EXP:
+            return c
+    raise RuntimeError(
+        f"mlstm_chunkwise_bwd: per-channel gates out of range for the chunkwise backward (a {cands[-1]}-step "
+        f"chunk needs e^{worst[-1].item():.1f} > e^{MAX_EXP:.0f}: forget gates near 0 or not finite)")
 
 
 def _bwd_channels(q, k, v, gi, gf, dh, c, st):

@@ -34,9 +34,15 @@ def _unit_last(t):
     return t if t.stride(-1) == 1 or t.shape[-1] == 1 else t.contiguous()
 
 
-def mlstm_chunkwise_fwd(q, k, v, log_i, log_f, C0=None, n0=None, m0=None, *, chunk=64, return_state=False,
-                        out=None):
+def mlstm_chunkwise_fwd(q, k, v, log_i, log_f, C0=None, n0=None, m0=None, *, chunk=128, return_state=False,
+                        out=None, error_flag=None, wait_limit_cycles=0):
     """h (B, H, L, Dv) [, (C, n, m)] of the mLSTM recurrence with log-space gates.
+
+    chunk: the time chunk of the tensor-core kernels, 128 (or 0 for the same);
+    the chunkwise result does not depend on it and other values raise.
+    error_flag: a device int32 tensor set to 1 if a bounded device wait of
+    the tensor-core kernels gave up (their outputs are then not written);
+    wait_limit_cycles: that bound in SM cycles (0 = about 2 s).
 
     q, k: (B, H, L, Dqk); v: (B, H, L, Dv) — bf16 runs the tcgen05 chunkwise
     kernel, fp32 runs the exact fp32 recurrent kernel.  log_i, log_f: fp32
@@ -89,6 +95,7 @@ def mlstm_chunkwise_fwd(q, k, v, log_i, log_f, C0=None, n0=None, m0=None, *, chu
     ws_bytes = _lib.lib().hxm_mlstm_workspace_size(a)
     ws = torch.empty(max(int(ws_bytes), 1), device=dev, dtype=torch.uint8) if ws_bytes else None
     a.workspace, a.workspace_bytes = ptr(ws), int(ws_bytes)
+    a.error_flag, a.wait_limit_cycles = ptr(error_flag), int(wait_limit_cycles)
     _lib.call("hxm_mlstm_chunkwise_fwd", a, stream_of(dev))
     return (h, st) if return_state else h
 

@@ -135,11 +135,16 @@ hxm_status hxm_selective_scan_bwd(const hxm_scan_bwd_args* args, void* stream);
 /* a time stride (*_tstride; 0 = d, one dense (t, d) panel per head), so     */
 /* (b, t, h, d) projection outputs are passed without a transpose.           */
 /* Requires a workspace of hxm_mlstm_workspace_size() bytes.                 */
+/* Any gate values: (b, h) pairs whose chunk scaling would leave the fp32    */
+/* range on the key-streaming path (e.g. a 128-step chunk whose forget gates */
+/* sum below about -128, or f = 0) are detected on the device and run by the */
+/* exact recurrent kernel within the same call (no host synchronization).   */
 /* ------------------------------------------------------------------------ */
 typedef struct hxm_mlstm_args {
   size_t struct_size;
   int32_t batch, heads, seqlen, dqk, dv;
-  int32_t chunk;            /* chunk length (64 or 128)                      */
+  int32_t chunk;            /* 0 or 128: the kernels' time chunk (the result */
+                            /* does not depend on it); others: EUNSUPPORTED  */
   int32_t gate_mode;        /* 0 scalar per head, 1 per channel              */
   hxm_dtype io_dtype;       /* q, k, v, h                                    */
   const void* q; int64_t q_stride[2];   /* (b, h) strides; time: q_tstride   */
@@ -154,6 +159,12 @@ typedef struct hxm_mlstm_args {
   /* time strides in elements; 0 = dense (dqk for q, k; dv for v, h; 1 per-head */
   /* or dqk per-channel gates)                                                 */
   int64_t q_tstride, k_tstride, v_tstride, h_tstride, i_tstride, f_tstride;
+  /* Bounded device waits of the tensor-core kernels: error_flag (device int */
+  /* or NULL) is set to 1 when one gives up (its outputs are then not       */
+  /* written); wait_limit_cycles bounds each wait in SM clock cycles        */
+  /* (0 = 4e9, about 2 s).                                                  */
+  int32_t* error_flag;
+  int64_t wait_limit_cycles;
 } hxm_mlstm_args;
 
 size_t hxm_mlstm_workspace_size(const hxm_mlstm_args* args);
@@ -167,8 +178,9 @@ hxm_status hxm_mlstm_chunkwise_fwd(const hxm_mlstm_args* args, void* stream);
  * no workspace — args->workspace is ignored — and allocates nothing.  Its
  * scratch is one library-owned 32 MiB device array per GPU, held until exit;
  * requests needing more return HXM_EBADARG.  The first call on a device looks
- * up the array's address (make it before any stream capture); calls that
- * overlap on the GPU race on the shared array. */
+ * up the array's address and keeps it for the life of the process (make it
+ * before any stream capture; a cudaDeviceReset afterwards is not supported);
+ * calls that overlap on the GPU race on the shared array. */
 hxm_status hxm_mlstm_chunkwise_fwd_noalloc(const hxm_mlstm_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
@@ -298,7 +310,8 @@ hxm_status hxm_chunk_state_dot(const hxm_chunk_dot_args* args, void* stream);
 typedef struct hxm_ssd_args {
   size_t struct_size;
   int32_t batch, seqlen, heads, headdim, dstate;
-  int32_t chunk;            /* 64, 128 or 256                                */
+  int32_t chunk;            /* 0 or 128: the kernel's time chunk (the result */
+                            /* does not depend on it); others: EUNSUPPORTED  */
   hxm_dtype io_dtype;       /* x, B, C, y                                    */
   const void* x; const float* dt; const float* A;
   const void* B; const void* C;
@@ -309,6 +322,8 @@ typedef struct hxm_ssd_args {
   const float* h0;          /* (b, heads, p, n) or NULL                      */
   float* hT;                /* (b, heads, p, n) or NULL                      */
   void* workspace; size_t workspace_bytes;
+  int32_t* error_flag;      /* device int set to 1 if a bounded wait gave up */
+  int64_t wait_limit_cycles;/* per wait, SM clock cycles (0 = 4e9, ~2 s)     */
 } hxm_ssd_args;
 
 size_t hxm_ssd_workspace_size(const hxm_ssd_args* args);
@@ -384,6 +399,7 @@ typedef struct hxm_slstm_args {
   const float* h0; const float* c0;
   float* hT; float* cT;
   int32_t* error_flag;      /* device int or NULL                            */
+  int64_t wait_limit_cycles;/* per cross-CTA wait, SM cycles (0 = 4e9, ~2 s) */
 } hxm_slstm_args;
 
 hxm_status hxm_slstm_scan_fwd(const hxm_slstm_args* args, void* stream);

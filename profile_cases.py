@@ -1,6 +1,6 @@
 """Small, self-contained GPU workloads for profiling one kernel family at a time.
 
-    python -m hybrid_model_mamba_xlstm_b200.profile_cases <case> [sizes...] [--reps N]
+    python profile_cases.py <case> [sizes...] [--reps N]
 
 Each case builds seeded synthetic inputs on ``cuda:0``, runs the public entry
 point ``reps`` times (default 2: one warm-up launch, one to capture) and prints
@@ -28,8 +28,12 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
+import sys
 
 import torch
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 
 def _time(fn, reps):
@@ -56,29 +60,29 @@ def main(argv=None):
     s = a.sizes
 
     if a.case == "scan":
-        from .kernels.selective_scan import selective_scan_fn
-        from .workloads import scan_inputs
+        from hybrid_model_mamba_xlstm_b200.kernels.selective_scan import selective_scan_fn
+        from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
         B, L, D = (s + [8, 4096, 4096][len(s):])[:3]
         inp = scan_inputs(B, L, D, 16, torch.bfloat16, seed=0, device="cuda", on_device=True)
         fn = lambda: selective_scan_fn(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, z=inp.z,  # noqa: E731
                                        delta_bias=inp.delta_bias, delta_softplus=True, return_last_state=True)
         extra = {"GB/s": None, "bytes": inp.bytes_moved()}
     elif a.case == "ssd":
-        from .kernels.ssd import ssd_chunk_scan
-        from .workloads import ssd_inputs
+        from hybrid_model_mamba_xlstm_b200.kernels.ssd import ssd_chunk_scan
+        from hybrid_model_mamba_xlstm_b200.workloads import ssd_inputs
         B, L, H, P, N = (s + [8, 4096, 32, 64, 128][len(s):])[:5]
         inp = ssd_inputs(B, L, H, P, N, seed=0, device="cuda")
         fn = lambda: ssd_chunk_scan(inp.x, inp.dt, inp.A, inp.B, inp.C, inp.D)  # noqa: E731
         extra = {"flops": inp.flops(256)}
     elif a.case == "mlstm":
-        from .kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
-        from .workloads import mlstm_inputs
+        from hybrid_model_mamba_xlstm_b200.kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
+        from hybrid_model_mamba_xlstm_b200.workloads import mlstm_inputs
         B, H, L, D, c = (s + [8, 8, 2048, 256, 128][len(s):])[:5]
         inp = mlstm_inputs(B, H, L, D, torch.bfloat16, seed=0, device="cuda", on_device=True)
         fn = lambda: mlstm_chunkwise_fwd(inp.q, inp.k, inp.v, inp.log_i, inp.log_f, chunk=c)  # noqa: E731
         extra = {"flops": inp.flops(c)}
     elif a.case == "mlstm_stream":
-        from .kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
+        from hybrid_model_mamba_xlstm_b200.kernels.tfla.tfla_interface import mlstm_chunkwise_fwd
         B, H, L, D = (s + [8, 4, 2048, 512][len(s):])[:4]
         g = torch.Generator(device=dev)
         g.manual_seed(0)
@@ -90,7 +94,7 @@ def main(argv=None):
         fn = lambda: mlstm_chunkwise_fwd(q, k, v, li, lf)  # noqa: E731
         extra = {}
     elif a.case == "slstm":
-        from .kernels.slstm import slstm_scan
+        from hybrid_model_mamba_xlstm_b200.kernels.slstm import slstm_scan
         B, L, H, HD = (s + [8, 256, 4, 256][len(s):])[:4]
         g = torch.Generator(device=dev)
         g.manual_seed(0)
@@ -100,7 +104,7 @@ def main(argv=None):
         fn = lambda: slstm_scan(gates, w, R=R)  # noqa: E731
         extra = {"steps": L}
     elif a.case == "conv":
-        from .kernels.conv import causal_conv1d
+        from hybrid_model_mamba_xlstm_b200.kernels.conv import causal_conv1d
         B, D, L = (s + [8, 4096, 2048][len(s):])[:3]
         g = torch.Generator(device=dev)
         g.manual_seed(0)
@@ -110,7 +114,7 @@ def main(argv=None):
         fn = lambda: causal_conv1d(x, w, bias, activation="silu")  # noqa: E731
         extra = {"bytes": 2 * x.numel() * 2}
     elif a.case in ("mamba_layer", "prefill"):
-        from . import layers as Lyr
+        from hybrid_model_mamba_xlstm_b200 import layers as Lyr
         B, L = (s + [8, 2048][len(s):])[:2]
         torch.manual_seed(0)
         if a.case == "mamba_layer":
@@ -124,7 +128,7 @@ def main(argv=None):
             fn = lambda: model(ids)  # noqa: E731
         extra = {"tokens": B * L}
     elif a.case == "prefill_graph":
-        from . import layers as Lyr
+        from hybrid_model_mamba_xlstm_b200 import layers as Lyr
         B, L, pieces = (s + [8, 2048, 4][len(s):])[:3]
         torch.manual_seed(0)
         model = Lyr.HybridLanguageModel(Lyr.hybrid_350m_config()).to(dev).to(torch.bfloat16).eval()
@@ -135,7 +139,7 @@ def main(argv=None):
         extra = {"tokens": B * L, "pieces": pieces}
     elif a.case == "mlstm_bwd":
         # chunkwise mLSTM backward, per-channel gates (mLSTMBlock), bf16 q / k / v
-        from .kernels.tfla.tfla_bwd import mlstm_chunkwise_bwd
+        from hybrid_model_mamba_xlstm_b200.kernels.tfla.tfla_bwd import mlstm_chunkwise_bwd
         B, H, L, D = (s + [8, 4, 2048, 512][len(s):])[:4]
         g = torch.Generator(device=dev).manual_seed(0)
         q, k, v, dh = (torch.randn(B, H, L, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(4))
@@ -146,8 +150,8 @@ def main(argv=None):
         extra = {"chunk": 64}
     elif a.case == "scan_bwd":
         # selective-scan backward (softplus(delta + bias), y * silu(z)), bf16 inputs, fp32 gradients
-        from .kernels.selective_scan.scan_interface import selective_scan_bwd
-        from .workloads import scan_inputs
+        from hybrid_model_mamba_xlstm_b200.kernels.selective_scan.scan_interface import selective_scan_bwd
+        from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
         B, L, D = (s + [8, 2048, 2048][len(s):])[:3]
         inp = scan_inputs(B, L, D, 16, torch.bfloat16, seed=0, device="cuda", on_device=True)
         dout = torch.randn(B, D, L, device=dev).to(torch.bfloat16)
@@ -157,15 +161,15 @@ def main(argv=None):
         extra = {"bytes": B * L * D * (4 * 2 + 3 * 4) + B * L * 16 * (2 * 2 + 2 * 4)}
     elif a.case == "ssd_bwd":
         # SSD backward (exact per-head chunk form, TF32 chunk GEMMs) for the bf16 forward's inputs
-        from .kernels.ssd import ssd_chunk_scan_bwd
-        from .workloads import ssd_inputs
+        from hybrid_model_mamba_xlstm_b200.kernels.ssd import ssd_chunk_scan_bwd
+        from hybrid_model_mamba_xlstm_b200.workloads import ssd_inputs
         B, L, H, P, N = (s + [8, 4096, 32, 64, 128][len(s):])[:5]
         inp = ssd_inputs(B, L, H, P, N, seed=0, device="cuda", on_device=True)
         dy = torch.randn(B, L, H, P, device=dev).to(torch.bfloat16)
         fn = lambda: ssd_chunk_scan_bwd(inp.x, inp.dt, inp.A, inp.B, inp.C, inp.D, dy)  # noqa: E731
         extra = {}
     elif a.case == "decode":
-        from . import layers as Lyr
+        from hybrid_model_mamba_xlstm_b200 import layers as Lyr
         B, P = (s + [1, 512][len(s):])[:2]
         torch.manual_seed(0)
         model = Lyr.HybridLanguageModel(Lyr.hybrid_350m_config()).to(dev).to(torch.bfloat16).eval()

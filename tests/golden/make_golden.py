@@ -1,14 +1,16 @@
 """Generate golden input/output vectors by running the REFERENCE itself.
 
-Run in a container where the reference checkout exists (default
-``/root/reference``; override with HXM_REFERENCE_ROOT).  The reference is
-imported read-only and executed in float64 on CPU; the fixtures (small .npz
-files in this directory) are committed so that the tests never need the
-reference at run time.
+Run where a checkout of the reference exists and name its root in the
+environment variable HXM_REFERENCE_ROOT (the directory that holds the
+``hybrid_xmamba`` package).  The reference is imported read-only and executed
+in float64 on CPU; the fixtures (small .npz files in this directory) are
+committed so that the tests never need the reference at run time.
 
 What each fixture pins (reference file:line of the code that produced it):
   scan_*.npz     selective_scan_pytorch / selective_scan
                  (hybrid_xmamba/kernels/selective_scan/scan_interface.py:103-180)
+  scan_zoh.npz   the ZOH / Taylor discretization of MambaBlock._selective_scan_pytorch
+                 (hybrid_xmamba/layers/mamba_block_v2.py:280-351)
   tfla_*.npz     tfla_forward_pytorch (hybrid_xmamba/kernels/tfla/tfla_interface.py:84-139)
   slstm_*.npz    sLSTMBlock.forward with a correctly shaped cache
                  (hybrid_xmamba/layers/slstm_block.py:64-143); gate_proj output and
@@ -34,10 +36,12 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("HXM_REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("HXM_REFERENCE_ROOT", "")
 
 
 def _import_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "hybrid_xmamba")):
+        sys.exit("set HXM_REFERENCE_ROOT to the reference checkout (the directory holding hybrid_xmamba/)")
     if REF not in sys.path:
         sys.path.insert(0, REF)
     from hybrid_xmamba.kernels.selective_scan import scan_interface
@@ -200,12 +204,36 @@ def make_lm(hl, cfgmod, sb):
         sb.sLSTMBlock.forward = orig
 
 
+def make_zoh():
+    """MambaBlock._selective_scan_pytorch of the v2 block (mamba_block_v2.py:280-351):
+    Bbar = (exp(dA) - 1) / A * B, or dt * B where |dA| < 0.01 (its Taylor branch).
+    The method uses no module state, so it is called unbound.  delta spans both
+    branches: softplus(N(0, 0.5^2) + softplus^-1(dt0)), dt0 log-uniform in
+    [1e-3, 1e-1], against A = -(1..16)."""
+    from hybrid_xmamba.layers import mamba_block_v2 as mb2
+    gen = torch.Generator().manual_seed(7)
+    bsz, L, dm, n = 2, 48, 24, 16
+    x = torch.randn(bsz, L, dm, generator=gen, dtype=torch.float64)
+    dt0 = torch.exp(torch.rand(dm, generator=gen, dtype=torch.float64) * (math.log(1e-1) - math.log(1e-3))
+                    + math.log(1e-3))
+    raw = 0.5 * torch.randn(bsz, L, dm, generator=gen, dtype=torch.float64)
+    delta = torch.nn.functional.softplus(raw + dt0 + torch.log(-torch.expm1(-dt0)))
+    A = -torch.arange(1, n + 1, dtype=torch.float64).repeat(dm, 1)
+    Bm = torch.randn(bsz, L, n, generator=gen, dtype=torch.float64)
+    Cm = torch.randn(bsz, L, n, generator=gen, dtype=torch.float64)
+    D = torch.randn(dm, generator=gen, dtype=torch.float64)
+    y = mb2.MambaBlock._selective_scan_pytorch(None, x, delta, A, Bm, Cm, D)
+    taylor = float(((delta[..., None] * A).abs() < 0.01).double().mean())
+    np.savez_compressed(os.path.join(HERE, "scan_zoh.npz"), x=x.numpy(), delta=delta.numpy(), A=A.numpy(),
+                        B=Bm.numpy(), C=Cm.numpy(), D=D.numpy(), y=y.numpy(), taylor_fraction=taylor)
+
+
 def main():
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     si, ti, sb, mb, lb, hl, cfgmod = _import_reference()
     if len(sys.argv) > 1:
         args = {"make_scan": (si,), "make_tfla": (ti,), "make_slstm": (sb,), "make_layers": (mb, lb),
-                "make_conv": (mb,), "make_lm": (hl, cfgmod, sb)}
+                "make_conv": (mb,), "make_lm": (hl, cfgmod, sb), "make_zoh": ()}
         for name in sys.argv[1:]:
             globals()[name](*args[name])
         return
@@ -215,6 +243,7 @@ def main():
     make_layers(mb, lb)
     make_conv(mb)
     make_lm(hl, cfgmod, sb)
+    make_zoh()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f"{f:28s} {os.path.getsize(os.path.join(HERE, f)) / 1024:8.1f} KiB")

@@ -21,6 +21,15 @@ def test_scan_small_matches_reference(golden):
     assert rel_err(yz, g["y_z"]) < TOL64
 
 
+def test_scan_zoh_matches_reference(golden):
+    """The ZOH / Taylor rule against MambaBlock._selective_scan_pytorch of the
+    v2 block (mamba_block_v2.py:280-351), both branches present."""
+    g = golden("scan_zoh")
+    assert 0.02 < float(g["taylor_fraction"]) < 0.98
+    y, _ = R.selective_scan(g["x"], g["delta"], g["A"], g["B"], g["C"], g["D"], discretization="zoh")
+    assert rel_err(y, g["y"]) < TOL64
+
+
 def test_scan_cfg1_slice_matches_reference(golden):
     g = golden("scan_cfg1_slice")
     t = lambda a: np.swapaxes(a, 1, 2)

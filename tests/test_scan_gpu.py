@@ -127,6 +127,15 @@ def test_dstate_sizes(ops, n):
     assert rel_err(np64(h), hr) < TOL32
 
 
+def test_golden_zoh_reference_fp32(ops, golden):
+    """discretization="zoh" against the reference's own ZOH / Taylor scan
+    (mamba_block_v2.py:280-351), generated by running it: fp32 within 1e-5."""
+    g = golden("scan_zoh")
+    y = ops.selective_scan_raw(cu(g["x"]), cu(g["delta"]), cu(g["A"]), cu(g["B"]), cu(g["C"]), cu(g["D"]),
+                               discretization="zoh")
+    assert rel_err(np64(y), g["y"]) < TOL32
+
+
 def test_zoh_discretization(ops):
     x, dt, A, B, C, D, z = _rand_blD(2, 64, 64, 16, 5, torch.float32)
     dt = dt * 0.2  # straddle the |dt*A| < 0.01 Taylor threshold
