@@ -39,7 +39,7 @@ hxm_status fill(const hxm_mlstm_args* a, Params& p, const char* who) {
   set_time_strides(p, a);
   p.workspace = a->workspace; p.workspace_bytes = a->workspace_bytes;
   p.error_flag = a->error_flag;
-  p.wait_limit = a->wait_limit_cycles > 0 ? a->wait_limit_cycles : 4000000000ll;
+  p.wait_limit = a->wait_limit_cycles != 0 ? a->wait_limit_cycles : 4000000000ll;
   return HXM_OK;
 }
 

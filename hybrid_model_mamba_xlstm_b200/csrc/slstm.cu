@@ -123,7 +123,7 @@ extern "C" hxm_status hxm_slstm_scan_fwd(const hxm_slstm_args* a, void* stream) 
   p.gates = a->gates_pre; p.R = static_cast<const __nv_bfloat16*>(a->R); p.w = a->norm_weight; p.eps = a->eps;
   p.exp_gate = a->exponential_gate; p.h_out = a->h_out; p.h0 = a->h0; p.c0 = a->c0; p.hT = a->hT; p.cT = a->cT;
   p.error_flag = a->error_flag;
-  p.wait_limit = a->wait_limit_cycles > 0 ? a->wait_limit_cycles : 4000000000ll;
+  p.wait_limit = a->wait_limit_cycles != 0 ? a->wait_limit_cycles : 4000000000ll;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p.R && (p.hd == 128 || p.hd == 256) && p.seqlen > 0) {
     hxm_status s = slstm::launch_cluster(p, st);

@@ -212,8 +212,12 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
   T* hout = static_cast<T*>(p.h_out);
   bool bad = false;
   float hlast = 0.f;
+  // wait_limit < 0 (the error-path test): wait -wait_limit cycles on step 0's partials before
+  // any CTA has sent them, so the wait runs out with no exchange in flight
+  if (p.wait_limit < 0) bad = !wait_bounded(&bars[0], 0, -p.wait_limit);
+  if (__syncthreads_or(bad)) bad = true;
 
-  for (int t = 0; t < p.seqlen; ++t) {
+  for (int t = 0; !bad && t < p.seqlen; ++t) {
     const uint32_t parity = t & 1;
     float gnext[kGE];
     fetch_gates(t + 1, gnext);  // consumed at the end of the step: latency hidden behind the step

@@ -35,7 +35,7 @@ static hxm_status launch_ssd(const hxm_ssd_args* a, cudaStream_t st) {
   cp.so[0] = cp.sx[0]; cp.so[1] = cp.sx[1]; cp.so[2] = cp.sx[2];
   cp.C0 = a->h0; cp.CT = a->hT; cp.state_t = 1;
   cp.error_flag = a->error_flag;
-  cp.wait_limit = a->wait_limit_cycles > 0 ? a->wait_limit_cycles : 4000000000ll;
+  cp.wait_limit = a->wait_limit_cycles != 0 ? a->wait_limit_cycles : 4000000000ll;
   const size_t smem = Layout<DK>::kBytes + 1024;
   auto kern = chunk_tc_kernel<DK, kSsd>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

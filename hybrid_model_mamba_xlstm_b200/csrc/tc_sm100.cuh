@@ -54,6 +54,11 @@ HXM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // per poll by every waiting thread competes with the tensor core for
 // shared-memory bandwidth.
 HXM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, long long limit_cycles = 4000000000ll) {
+  // a negative limit (the callers' error-path test) gives up before polling, whatever the barrier's state
+  if (limit_cycles < 0) {
+    *abort = 1;
+    return false;
+  }
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t i = 1;; ++i) {

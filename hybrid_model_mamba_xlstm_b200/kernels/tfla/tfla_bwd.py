@@ -34,8 +34,8 @@ scaling, the two chunk-level recurrences and the gate gradients (a suffix sum
 over the whole sequence) are this library's kernels.  Memory: two fp32 state
 arrays of (B, H, L / chunk, dqk, w), w = dv + 1 rounded up to 8.
 
-Range (per-channel gates): the factors above are e^x with x at most
-|g| / 2 + max(log i, 0) over the chunk.  ``_channel_chunk`` picks the longest
+Range (per-channel gates): the factors above are e^x with |x| at most
+|g| / 2 + max |log i| over the chunk.  ``_channel_chunk`` picks the longest
 chunk (the requested one, then halves down to 8 steps) for which every chunk
 of the input keeps x <= MAX_EXP, so strong forget gates (e.g. logsigmoid of
 N(-4, 1) pre-activations, about -520 per 128 steps) shorten the chunk instead
@@ -189,7 +189,8 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     per head for per-head gates unless gate_grads="channel" (the per-channel
     values, e.g. for gates given as expanded (B, H, L, Dqk) views).  tf32:
     chunk GEMMs on TF32 tensor cores (default: when q is bf16, whose own
-    rounding is coarser; relative gradient error ~1e-3) or in full fp32.
+    rounding is coarser; relative gradient error ~1e-3 — except per-channel
+    gates strong enough to shorten the chunk, which run fp32) or in full fp32.
     """
     who = "mlstm_chunkwise_bwd"
     dev = require_cuda(q, k, v, log_i, log_f, dh, who=who)
@@ -217,16 +218,20 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
         gi, gf = unit(gi), unit(gf)
     c = int(chunk)
     st = stream_of(dev)
-    with _gemm_precision(io == torch.bfloat16 if tf32 is None else tf32):
-        if gate_mode == 0:
+    if gate_mode == 0:
+        with _gemm_precision(io == torch.bfloat16 if tf32 is None else tf32):
             return _bwd_heads(q, k, v, gi, gf, dh, c, True, per_channel_out, st)
-        return _bwd_channels(q, k, v, gi, gf, dh, _channel_chunk(gi, gf, c), st)
+    cc = _channel_chunk(gi, gf, c)
+    # Gates strong enough to shorten the chunk make the forget-gate gradient a difference of
+    # large in-chunk sums: TF32 operands (10-bit mantissa) lose it, so those run in fp32.
+    with _gemm_precision((io == torch.bfloat16 and cc == c) if tf32 is None else tf32):
+        return _bwd_channels(q, k, v, gi, gf, dh, cc, st)
 
 
 def _channel_chunk(gi, gf, chunk):
     """The longest chunk length <= chunk (halving, at least MIN_CHUNK) whose
-    separable factors stay within e^MAX_EXP for these per-channel gates
-    (B, H, L, Dqk): max over chunks and channels of |g| / 2 + max(log i, 0),
+    separable factors stay within e^+-MAX_EXP for these per-channel gates
+    (B, H, L, Dqk): max over chunks and channels of |g| / 2 + max |log i|,
     g the chunk's total log forget gate.  One host synchronization."""
     bsz, nh, L, dqk = gf.shape
     cands = []
@@ -242,7 +247,7 @@ def _channel_chunk(gi, gf, chunk):
         pad = nch * c - L
         lf = torch.nn.functional.pad(gf, (0, 0, 0, pad)).view(bsz, nh, nch, c, dqk)
         li = torch.nn.functional.pad(gi, (0, 0, 0, pad)).view(bsz, nh, nch, c, dqk)
-        x = -0.5 * lf.sum(3) + li.amax(3).clamp_min(0.0)
+        x = -0.5 * lf.sum(3) + li.abs().amax(3)
         worst.append(torch.nan_to_num(x, nan=float("inf")).amax())
     worst = torch.stack(worst).cpu()
     for c, w in zip(cands, worst.tolist()):

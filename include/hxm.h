@@ -162,7 +162,8 @@ typedef struct hxm_mlstm_args {
   /* Bounded device waits of the tensor-core kernels: error_flag (device int */
   /* or NULL) is set to 1 when one gives up (its outputs are then not       */
   /* written); wait_limit_cycles bounds each wait in SM clock cycles        */
-  /* (0 = 4e9, about 2 s).                                                  */
+  /* (0 = 4e9, about 2 s; < 0: every wait gives up at once, which exercises */
+  /* the error path — the kernel still drains its own MMAs and loads).      */
   int32_t* error_flag;
   int64_t wait_limit_cycles;
 } hxm_mlstm_args;
@@ -323,7 +324,8 @@ typedef struct hxm_ssd_args {
   float* hT;                /* (b, heads, p, n) or NULL                      */
   void* workspace; size_t workspace_bytes;
   int32_t* error_flag;      /* device int set to 1 if a bounded wait gave up */
-  int64_t wait_limit_cycles;/* per wait, SM clock cycles (0 = 4e9, ~2 s)     */
+  int64_t wait_limit_cycles;/* per wait, SM clock cycles (0 = 4e9, ~2 s;     */
+                            /* < 0: every wait gives up at once)             */
 } hxm_ssd_args;
 
 size_t hxm_ssd_workspace_size(const hxm_ssd_args* args);
@@ -399,7 +401,9 @@ typedef struct hxm_slstm_args {
   const float* h0; const float* c0;
   float* hT; float* cT;
   int32_t* error_flag;      /* device int or NULL                            */
-  int64_t wait_limit_cycles;/* per cross-CTA wait, SM cycles (0 = 4e9, ~2 s) */
+  int64_t wait_limit_cycles;/* per cross-CTA wait, SM cycles (0 = 4e9, ~2 s; */
+                            /* < 0: the first exchange is waited for -limit */
+                            /* cycles before any CTA sends, so it runs out)  */
 } hxm_slstm_args;
 
 hxm_status hxm_slstm_scan_fwd(const hxm_slstm_args* args, void* stream);

@@ -22,6 +22,8 @@ What each fixture pins (reference file:line of the code that produced it):
   hybrid_lm.npz  HybridLanguageModel.forward (hybrid_xmamba/models/hybrid_lm.py:145-209)
                  at a tiny size; sLSTM blocks get the correctly shaped zero cache
                  (the reference crashes without it, slstm_block.py:109-112)
+  hybrid_lm350m.npz  the same forward at the hybrid-350M architecture, batch 1 x 256,
+                 with name-seeded weights (lm350m_weights.py); logit slices and sums
 
 Usage:  python tests/golden/make_golden.py [fixture-function ...]
         (no argument: all fixtures; e.g. ``make_conv`` regenerates one)
@@ -204,6 +206,53 @@ def make_lm(hl, cfgmod, sb):
         sb.sLSTMBlock.forward = orig
 
 
+def make_lm350m(hl, cfgmod, sb):
+    """HybridLanguageModel.forward (hybrid_lm.py:145-209) at the hybrid-350M
+    architecture (d 1024, 24 layers of [Mamba, Mamba, mLSTM, sLSTM], Mamba
+    expand 2 / d_state 16 / conv 4, mLSTM 4 heads x 512, sLSTM 4 heads, vocab
+    50304, the reference's default MLP), float64, batch 1 x 256 tokens, with
+    the name-seeded weights of lm350m_weights.py (the reference has no sLSTM
+    recurrent weights: R = 0).  Stored: slices of the logits (every position
+    over the first 512 vocabulary entries, five positions over all of it), the
+    sum / sum of squares of all logits, and how far the reference's own fp32
+    run lands from its float64 run on the same slices (the model amplifies
+    rounding late in the sequence, so that is the scale an fp32 port is judged
+    against)."""
+    sys.path.insert(0, HERE)
+    import lm350m_weights as W
+    orig = sb.sLSTMBlock.forward
+
+    def fwd_with_cache(self, x, cache=None):
+        if cache is None:
+            z = torch.zeros(x.shape[0], self.num_heads, self.head_dim, dtype=x.dtype)
+            cache = {"h": z.clone(), "c": z.clone()}
+        return orig(self, x, cache=cache)
+
+    sb.sLSTMBlock.forward = fwd_with_cache
+    try:
+        cfg = cfgmod.HybridConfig(vocab_size=50304, dim=1024, num_layers=24,
+                                  layer_pattern=["mamba", "mamba", "mlstm", "slstm"], state_size=16, conv_size=4,
+                                  expand_factor=2, head_dim=512, num_heads=4, slstm_num_heads=4, dropout=0.0)
+        model = hl.HybridLanguageModel(cfg)
+        names = W.fill_(model)
+        model = model.eval()
+        ids = torch.randint(0, 50304, (1, 256), generator=torch.Generator().manual_seed(8))
+        pos = np.array([0, 63, 127, 191, 255])
+        with torch.no_grad():
+            l32 = model(ids).logits[0].double()  # the reference's own fp32 run
+            logits = model.double()(ids).logits[0]
+        rel = lambda a, b: float(torch.linalg.norm(a - b) / torch.linalg.norm(b))
+        np.savez_compressed(os.path.join(HERE, "hybrid_lm350m.npz"), ids=ids.numpy(),
+                            logits_head=logits[:, :512].float().numpy(), positions=pos,
+                            logits_rows=logits[pos].float().numpy(), logit_sum=float(logits.sum()),
+                            logit_sumsq=float((logits * logits).sum()), n_filled=len(names),
+                            n_params=sum(p.numel() for p in model.parameters()),
+                            ref_fp32_err_head=rel(l32[:, :512], logits[:, :512]),
+                            ref_fp32_err_rows=rel(l32[pos], logits[pos]))
+    finally:
+        sb.sLSTMBlock.forward = orig
+
+
 def make_zoh():
     """MambaBlock._selective_scan_pytorch of the v2 block (mamba_block_v2.py:280-351):
     Bbar = (exp(dA) - 1) / A * B, or dt * B where |dA| < 0.01 (its Taylor branch).
@@ -233,7 +282,8 @@ def main():
     si, ti, sb, mb, lb, hl, cfgmod = _import_reference()
     if len(sys.argv) > 1:
         args = {"make_scan": (si,), "make_tfla": (ti,), "make_slstm": (sb,), "make_layers": (mb, lb),
-                "make_conv": (mb,), "make_lm": (hl, cfgmod, sb), "make_zoh": ()}
+                "make_conv": (mb,), "make_lm": (hl, cfgmod, sb), "make_zoh": (),
+                "make_lm350m": (hl, cfgmod, sb)}
         for name in sys.argv[1:]:
             globals()[name](*args[name])
         return
@@ -244,6 +294,7 @@ def main():
     make_conv(mb)
     make_lm(hl, cfgmod, sb)
     make_zoh()
+    make_lm350m(hl, cfgmod, sb)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f"{f:28s} {os.path.getsize(os.path.join(HERE, f)) / 1024:8.1f} KiB")

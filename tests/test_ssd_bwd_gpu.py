@@ -59,7 +59,7 @@ def _inputs(bsz, L, nh, p, n, seed):
 def test_ssd_grads_vs_float64_loop(S, shape):
     x, dt, A, B, C, D, bias, dy = _inputs(*shape, seed=sum(shape))
     cu = [t.cuda().requires_grad_(True) for t in (x, dt, A, B, C, D, bias)]
-    y = S.ssd_chunk_scan_fn(cu[0], cu[1], cu[2], cu[3], cu[4], cu[5], dt_bias=cu[6], dt_softplus=True, chunk=64)
+    y = S.ssd_chunk_scan_fn(cu[0], cu[1], cu[2], cu[3], cu[4], cu[5], dt_bias=cu[6], dt_softplus=True)
     y.backward(dy.cuda().bfloat16())
     ref = [t.detach().double().requires_grad_(True) for t in (x, dt, A, B, C, D, bias)]
     yr = _loop(*ref, True)

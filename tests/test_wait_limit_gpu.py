@@ -2,20 +2,22 @@
 
 Every mbarrier / cluster wait in the tensor-core kernels (chunkwise mLSTM and
 SSD, key-streaming mLSTM, the sLSTM cluster exchange) gives up after
-``wait_limit_cycles`` SM cycles (about 2 s by default).  Here the limit is
-set far below the latency of the first TMA load or peer exchange, so a wait
-runs out on every CTA: the kernel raises its abort flag, drains what it has
-in flight (its own MMAs and loads, on a separate bound), frees its TMEM,
-sets the caller's error word and returns.  The test checks the word on the
-host, that the CUDA context reports no error, and that the next call with
-the default limit gives the same result as before.  No fault, trap or hang
-is involved.
+``wait_limit_cycles`` SM cycles (about 2 s by default).  A negative limit
+makes the waits run out for certain: in the chunkwise and key-streaming
+kernels every wait gives up at once, after the first TMA loads were issued;
+in the sLSTM cluster kernel every CTA waits (for -limit cycles) on the first
+exchange before any CTA sends it.  The kernel then raises its abort flag,
+drains what it has in flight (its own MMAs and loads, on a separate bound),
+frees its TMEM, sets the caller's error word and returns.  The test checks
+the word on the host, that the CUDA context reports no error, and that the
+next call with the default limit gives the same result as before.  No
+fault, trap or hang is involved.
 """
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-TINY = 64  # SM cycles: shorter than any TMA load or cluster exchange
+GIVE_UP = -100000  # negative: the waits run out (the sLSTM exchange after 1e5 cycles, ~50 us)
 
 
 @pytest.fixture(scope="module")
@@ -27,12 +29,12 @@ def dev():
 
 
 def _run_three(fn):
-    """fn(error_flag, wait_limit_cycles) -> tensors; default, tiny limit, default."""
+    """fn(error_flag, wait_limit_cycles) -> tensors; default limit, GIVE_UP, default again."""
     flag = torch.zeros(1, device="cuda", dtype=torch.int32)
     first = [t.clone() for t in fn(flag, 0)]
     torch.cuda.synchronize()
     assert int(flag.item()) == 0
-    fn(flag, TINY)
+    fn(flag, GIVE_UP)
     torch.cuda.synchronize()  # raises if the context had faulted
     assert int(flag.item()) == 1
     flag.zero_()
