@@ -4,8 +4,8 @@ The recurrent workloads shard over independent units — (batch row, channel)
 for the selective scan, (batch, head) for mLSTM / SSD / sLSTM, batch rows for
 the hybrid prefill — so no collective sits on the data path.  NCCL (over
 NVLink / NVSwitch) is used only around the timed region: a barrier, the
-max-over-ranks reduction of device times, and an all-gather of per-rank
-output checksums for verification.  Every function works with the ``gloo``
+max-over-ranks reduction of device times, and all-gathers of output shards
+(``gather_rows``) or per-rank figures for verification after timing.  Every function works with the ``gloo``
 backend on CPU tensors as well, which is how the multi-rank logic is tested.
 """
 from __future__ import annotations
@@ -78,6 +78,21 @@ def gather_checksums(values, world: int):
     out = [torch.empty_like(v) for _ in range(world)]
     dist.all_gather(out, v)
     return torch.stack(out).cpu()
+
+
+def gather_rows(t: torch.Tensor, n_rows: int, world: int) -> torch.Tensor:
+    """All-gather row shards (dim 0) cut by ``shard_range(n_rows, world, rank)``
+    into the full (n_rows, ...) tensor on every rank, in rank order.  Shards
+    of unequal size are padded to the largest for the collective."""
+    if world == 1:
+        return t
+    per = max(b - a for a, b in (shard_range(n_rows, world, r) for r in range(world)))
+    buf = t.new_zeros((per,) + tuple(t.shape[1:]))
+    buf[:t.shape[0]] = t
+    out = t.new_empty((world * per,) + tuple(t.shape[1:]))
+    dist.all_gather_into_tensor(out, buf.contiguous())
+    parts = [out[r * per:r * per + (b - a)] for r, (a, b) in enumerate(shard_range(n_rows, world, r) for r in range(world))]
+    return torch.cat(parts, 0)
 
 
 def checksum(t: torch.Tensor):

@@ -144,3 +144,45 @@ def ssd_inputs(batch, seqlen, heads, headdim, dstate, seed=0, device="cpu", on_d
     D = torch.ones(heads, device=gdev)
     bf = lambda t: t.to(device=device, dtype=torch.bfloat16)
     return SsdInputs(bf(x), dt.to(device), A.to(device), bf(Bm), bf(Cm), D.to(device))
+
+
+def scan_rows(rows, seqlen, dim, dstate=16, dtype=torch.bfloat16, seed=0, device="cpu"):
+    """Batch rows ``rows`` (a range) of one global selective-scan workload, so
+    that ranks holding different rows — and a checker regenerating one row —
+    see the same numbers: the per-channel parameters (A, D, delta_bias) come
+    from ``seed`` and row b's u, delta, z, B, C from seed * 1000 + 1 + b, each
+    drawn on ``device``.  Distributions as ``scan_inputs``."""
+    g = _gen(seed, device)
+    f = dict(generator=g, device=device, dtype=torch.float32)
+    dt0 = torch.exp(torch.rand(dim, **f) * (math.log(1e-1) - math.log(1e-3)) + math.log(1e-3))
+    bias = softplus_inv(dt0)
+    A = -torch.arange(1, dstate + 1, dtype=torch.float32, device=device).repeat(dim, 1)
+    D = torch.ones(dim, device=device)
+    parts = {k: [] for k in ("u", "delta", "z", "B", "C")}
+    for b in rows:
+        gr = _gen(seed * 1000 + 1 + b, device)
+        fr = dict(generator=gr, device=device, dtype=torch.float32)
+        parts["u"].append(torch.randn(1, dim, seqlen, **fr).to(dtype))
+        parts["z"].append(torch.randn(1, dim, seqlen, **fr).to(dtype))
+        parts["delta"].append(torch.randn(1, dim, seqlen, **fr).mul_(0.5).to(dtype))
+        parts["B"].append(torch.randn(1, dstate, seqlen, **fr).to(dtype))
+        parts["C"].append(torch.randn(1, dstate, seqlen, **fr).to(dtype))
+    cat = {k: torch.cat(v, 0) for k, v in parts.items()}
+    return ScanInputs(cat["u"], cat["delta"], cat["z"], A, cat["B"], cat["C"], D, bias)
+
+
+def mlstm_rows(rows, heads, seqlen, d, dtype=torch.bfloat16, seed=0, device="cpu"):
+    """Batch rows ``rows`` of one global mLSTM workload with per-head gates,
+    row b drawn from seed * 1000 + 1 + b on ``device`` (distributions as
+    ``mlstm_inputs``), so any rank or checker can regenerate any row."""
+    parts = {k: [] for k in ("q", "k", "v", "li", "lf")}
+    for b in rows:
+        g = _gen(seed * 1000 + 1 + b, device)
+        f = dict(generator=g, device=device, dtype=torch.float32)
+        parts["q"].append(torch.randn(1, heads, seqlen, d, **f).mul_(1.0 / math.sqrt(d)).to(dtype))
+        parts["k"].append(torch.randn(1, heads, seqlen, d, **f).to(dtype))
+        parts["v"].append(torch.randn(1, heads, seqlen, d, **f).to(dtype))
+        parts["li"].append(torch.randn(1, heads, seqlen, **f))
+        parts["lf"].append(torch.nn.functional.logsigmoid(torch.randn(1, heads, seqlen, **f).add_(3.0)))
+    cat = {k: torch.cat(v, 0) for k, v in parts.items()}
+    return MlstmInputs(cat["q"], cat["k"], cat["v"], cat["li"], cat["lf"])

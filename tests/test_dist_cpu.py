@@ -1,6 +1,6 @@
 """Multi-rank host logic with 2 gloo ranks on CPU: sharding covers every unit
-exactly once, times reduce to the slowest rank, checksums gather in rank
-order, and a rank that raises does not leave its peer hanging (the process
+exactly once, times reduce to the slowest rank, checksums and row shards
+(unequal ones too) gather in rank order, and a rank that raises does not leave its peer hanging (the process
 group timeout ends the collective with an error)."""
 import os
 import socket
@@ -43,8 +43,10 @@ def _worker(rank, world, port, q, mode):
             a, b = D.shard_range(8, w, r)
             data = torch.arange(a, b, dtype=torch.float64)
             cs = D.gather_checksums(D.checksum(data), w)
+            a7, b7 = D.shard_range(7, w, r)  # unequal shards (4 + 3 rows)
+            full = D.gather_rows(torch.arange(a7 * 3, b7 * 3, dtype=torch.float32).view(-1, 3), 7, w)
             D.barrier(w)
-            q.put((rank, t, cs.tolist()))
+            q.put((rank, t, cs.tolist(), full.tolist()))
         else:  # rank 1 fails before the collective; rank 0 must get an error, not hang
             if rank == 1:
                 raise RuntimeError("planted failure on rank 1")
@@ -79,9 +81,10 @@ def _run(mode):
 
 def test_two_gloo_ranks_reduce_and_gather():
     out = _run("ok")
-    for rank, t, cs in out:
+    for rank, t, cs, full in out:
         assert t == 2.5  # max of 1.5, 2.5
         assert cs[0][0] == sum(range(0, 4)) and cs[1][0] == sum(range(4, 8))
+        assert full == torch.arange(21, dtype=torch.float32).view(7, 3).tolist()  # shards in rank order
 
 
 def test_failed_rank_ends_peer_collective_with_error():
