@@ -239,6 +239,20 @@ def _time_cuda(fn, steps, warmup, dev, world):
     return max_over_ranks(e0.elapsed_time(e1) / steps, world)
 
 
+def roofline_obj(bound, achieved, unit, kernel_key, algorithmic, per_launch_scale=1.0):
+    """A roofline object for a secondary workload: `achieved` against the
+    measured peak of its bound (HBM GB/s or dense bf16 TFLOP/s, burst), and the
+    DRAM traffic of one launch from the committed ncu captures
+    (profiles/traffic.json, `kernel_key`), scaled by `per_launch_scale` when
+    the capture ran a smaller case of the same kernel."""
+    pk, kind = peaks()
+    peak = pk["hbm_gbs"] if bound == "hbm" else pk["bf16_tflops"]
+    t = profile_traffic(kernel_key)
+    return {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+            "peak_kind": kind, "traffic": None if t is None else t * per_launch_scale,
+            "traffic_key": kernel_key, "algorithmic": algorithmic}
+
+
 def secondary_metrics(args, dev, world, rank):
     """The other hot-path workloads, each timed on every rank (same order on all ranks)."""
     from hybrid_model_mamba_xlstm_b200.kernels.slstm import slstm_scan
@@ -259,10 +273,12 @@ def secondary_metrics(args, dev, world, rank):
         ms = _time_cuda(lambda: mlstm_chunkwise_fwd(inp.q, inp.k, inp.v, inp.log_i, inp.log_f, chunk=c),
                         steps, 3, dev, world)
         fl = inp.flops(c)
+        kern = "chunk_tc_kernel<%d, mLSTM>" % d if d <= 256 else "mlstm_stream_kernel<%d>" % d
         out[name] = {"metric": "mLSTM chunkwise TFLOP/s (algorithmic)", "value": world * fl / ms / 1e9,
                      "unit": "TFLOP/s", "ms": ms, "chunk": c, "frac_of_bf16_peak": fl / ms / 1e9 / tf_peak,
-                     "peak_kind": pk_kind, "scaling": "weak",
-                     "kernel": "chunk_tc_kernel<%d, mLSTM>" % d if d <= 256 else "mlstm_stream_kernel<%d>" % d}
+                     "peak_kind": pk_kind, "scaling": "weak", "kernel": kern,
+                     "roofline": roofline_obj("tensor", fl / ms / 1e9, "TFLOP/s", f"{kern} {name}",
+                                              {"flops": fl, "bytes": inp.bytes_moved()})}
         del inp
     # Mamba-2 SSD, batch 8, 32 heads x 64, dstate 128, seqlen 4096 (tcgen05)
     inp = ssd_inputs(8, 4096, 32, 64, 128, seed=rank, device=dev, on_device=True)
@@ -272,7 +288,10 @@ def secondary_metrics(args, dev, world, rank):
                                                   "that runs)",
                                         "value": world * fl / ms / 1e9, "unit": "TFLOP/s", "ms": ms, "chunk": 128,
                                         "frac_of_bf16_peak": fl / ms / 1e9 / tf_peak, "peak_kind": pk_kind,
-                                        "scaling": "weak", "kernel": "chunk_tc_kernel<128, SSD>"}
+                                        "scaling": "weak", "kernel": "chunk_tc_kernel<128, SSD>",
+                                        "roofline": roofline_obj("tensor", fl / ms / 1e9, "TFLOP/s",
+                                                                 "chunk_tc_kernel<128, SSD> ssd_b8_h32_p64_n128_l4096",
+                                                                 {"flops": fl, "bytes": inp.bytes_moved()})}
     del inp
     # sLSTM recurrence with block-diagonal R, the prefill's layer shape: batch 8, 4 heads x 256, seqlen 2048
     g = torch.Generator(device=dev)
@@ -327,7 +346,9 @@ def secondary_metrics(args, dev, world, rank):
     out["scan_bwd_b8_l2048_d2048_n16"] = {
         "metric": "selective-scan backward GB/s (one read of each bf16 input, one write of each fp32 gradient)",
         "value": world * nbytes / ms / 1e6, "unit": "GB/s", "ms": ms, "scaling": "weak",
-        "kernel": "hxm::scan::scan_bwd_kernel (checkpointed reverse recurrence)"}
+        "kernel": "hxm::scan::scan_bwd_kernel (checkpointed reverse recurrence)",
+        "roofline": roofline_obj("hbm", nbytes / ms / 1e6, "GB/s", "scan_bwd_kernel scan_bwd_b8_l2048_d2048_n16",
+                                 {"bytes": nbytes})}
     del inp, dout
     torch.cuda.empty_cache()
     out["prefill"] = prefill_metric(args, dev, world, rank)
@@ -348,6 +369,14 @@ def prefill_metric(args, dev, world, rank):
     g.manual_seed(99 + rank)
     out = {}
     pieces = 4
+    # algorithmic FLOPs of one forward token: 2 x every weight used per token (the token embedding is a
+    # lookup, the LM head a GEMM) + the chunkwise mLSTM's intra-chunk terms (4 c d per head and token)
+    cfg = model.config
+    n_w = sum(p.numel() for n_, p in model.named_parameters() if "token_embedding" not in n_)
+    n_mlstm = sum(1 for i in range(cfg.num_layers) if cfg.layer_pattern[i % len(cfg.layer_pattern)] == "mlstm")
+    tied = model.lm_head.weight is model.embeddings.token_embedding.weight  # then n_w lacks the head's GEMM
+    flop_tok = 2 * n_w + (2 * cfg.dim * cfg.vocab_size if tied else 0) + \
+        n_mlstm * cfg.num_heads * 4 * 128 * cfg.head_dim
     for kind, per in (("weak", gb), ("strong", max(1, gb // world))):
         ids = torch.randint(0, 50304, (per, seqlen), generator=g, device=dev)
         with torch.no_grad():
@@ -360,7 +389,9 @@ def prefill_metric(args, dev, world, rank):
                      "schedule": f"CUDA-graph wavefront: {pieces} sequence pieces x 24 layers, one stream per layer",
                      "single_stream_forward_ms": ms_eager,
                      "scaling": "weak (batch 8 per rank)" if kind == "weak" else "strong (global batch 8 split over ranks)",
-                     "parallelism": f"dp{world}"}
+                     "parallelism": f"dp{world}",
+                     "roofline": roofline_obj("tensor", per * seqlen * flop_tok / ms / 1e9, "TFLOP/s",
+                                              "prefill hybrid350m", {"flops_per_token": flop_tok})}
         del ids, pg
         torch.cuda.empty_cache()
     del model
