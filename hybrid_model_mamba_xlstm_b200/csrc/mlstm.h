@@ -54,8 +54,8 @@ inline void set_time_strides(Params& p, const hxm_mlstm_args* a) {
 hxm_status fill(const hxm_mlstm_args* a, Params& p, const char* who);
 
 // Exact step-by-step recurrence on CUDA cores (any gate mode / dtype / dims <= 512).
-// only: NULL, or a device int per (b, h) selecting the pairs to run (nonzero).
-hxm_status launch_recurrent(const Params& p, cudaStream_t st, const int* only = nullptr);
+// only: NULL, or a device int per (b, h); then the pairs whose entry equals `want` run.
+hxm_status launch_recurrent(const Params& p, cudaStream_t st, const int* only = nullptr, int want = 1);
 // tcgen05 chunkwise kernel (bf16, per-head gates, dqk 128/256, stabilized); no workspace.
 hxm_status launch_chunkwise_tc(const Params& p, cudaStream_t st);
 size_t chunkwise_tc_workspace(const Params& p);  // (size_t)-1 when the shape is not covered

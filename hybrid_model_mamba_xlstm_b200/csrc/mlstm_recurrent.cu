@@ -28,10 +28,11 @@ constexpr int kRG = 8;       // row groups
 constexpr int kThreads = kE * kRG;
 
 // only: NULL (every (b, h)) or a device int per (b, h); then only the pairs
-// whose entry is nonzero run (the rest of the grid returns at once).
+// whose entry equals `want` run (the rest of the grid returns at once).
 template <typename T, int RPT>  // RPT = rows per thread = ceil(dqk / kRG)
-__global__ void __launch_bounds__(kThreads) mlstm_recurrent_kernel(const Params p, const int* __restrict__ only) {
-  if (only && only[blockIdx.y] == 0) return;  // uniform over the CTA
+__global__ void __launch_bounds__(kThreads) mlstm_recurrent_kernel(const Params p, const int* __restrict__ only,
+                                                                   int want) {
+  if (only && only[blockIdx.y] != want) return;  // uniform over the CTA
   extern __shared__ __align__(16) float sm[];
   const int dqk = p.dqk;
   float* q_s = sm;              // [dqk]  q~ = q * e^(m'-M)
@@ -180,29 +181,29 @@ __global__ void __launch_bounds__(kThreads) mlstm_recurrent_kernel(const Params 
 }
 
 template <typename T, int RPT>
-static hxm_status launch_rpt(const Params& p, cudaStream_t st, const int* only) {
+static hxm_status launch_rpt(const Params& p, cudaStream_t st, const int* only, int want) {
   const size_t smem = sizeof(float) * (4 * (size_t)p.dqk + kE + kRG * kE + 16);
   auto kern = mlstm_recurrent_kernel<T, RPT>;
   if (smem > 48 * 1024) HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dv + kE - 1) / kE, p.batch * p.heads);
-  kern<<<grid, kThreads, smem, st>>>(p, only);
+  kern<<<grid, kThreads, smem, st>>>(p, only, want);
   return check_launch("hxm_mlstm_chunkwise_fwd (recurrent)");
 }
 
 template <typename T>
-static hxm_status launch_t(const Params& p, cudaStream_t st, const int* only) {
+static hxm_status launch_t(const Params& p, cudaStream_t st, const int* only, int want) {
   const int rpt = (p.dqk + kRG - 1) / kRG;
-  if (rpt <= 8) return launch_rpt<T, 8>(p, st, only);
-  if (rpt <= 16) return launch_rpt<T, 16>(p, st, only);
-  if (rpt <= 32) return launch_rpt<T, 32>(p, st, only);
-  if (rpt <= 64) return launch_rpt<T, 64>(p, st, only);
+  if (rpt <= 8) return launch_rpt<T, 8>(p, st, only, want);
+  if (rpt <= 16) return launch_rpt<T, 16>(p, st, only, want);
+  if (rpt <= 32) return launch_rpt<T, 32>(p, st, only, want);
+  if (rpt <= 64) return launch_rpt<T, 64>(p, st, only, want);
   set_error("hxm_mlstm_chunkwise_fwd: dqk=%d > 512 unsupported by the recurrent kernel", p.dqk);
   return HXM_EUNSUPPORTED;
 }
 
-hxm_status launch_recurrent(const Params& p, cudaStream_t st, const int* only) {
-  if (p.io_dtype == HXM_F32) return launch_t<float>(p, st, only);
-  return launch_t<__nv_bfloat16>(p, st, only);
+hxm_status launch_recurrent(const Params& p, cudaStream_t st, const int* only, int want) {
+  if (p.io_dtype == HXM_F32) return launch_t<float>(p, st, only, want);
+  return launch_t<__nv_bfloat16>(p, st, only, want);
 }
 
 }  // namespace mlstm

@@ -56,19 +56,23 @@ constexpr float kMaxExp = 80.f;  // largest |exponent| of a chunk factor the str
 // same for every channel, so the block forms them once per step (thread t,
 // one scan over the chunk) and the channels only multiply; per-channel gates
 // take two exponentials per element.
-// unsafe[b*heads + h] is set to 1 when an exponent is beyond +-kMaxExp or not finite.
+// Chunks of kc steps (128, or 64 for the pairs a 128-step pass flagged).  unsafe[b*heads + h]
+// is raised to level + 1 when an exponent is beyond +-kMaxExp or not finite; with level 1 only
+// the pairs flagged by the level-0 pass are processed (the rest of the grid returns at once).
 template <typename T, int NJ>
 __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks,
-                                                             float* decay, float* rho_e, float* nadd, int* unsafe) {
+                                                             float* decay, float* rho_e, float* nadd, int* unsafe,
+                                                             int kc, int level) {
   __shared__ float fq[kC], fk[kC], red[4];
-  const int nch = (p.seqlen + kC - 1) / kC;
+  const int nch = (p.seqlen + kc - 1) / kc;
   const int c = blockIdx.x % nch;
   const int bh = blockIdx.x / nch;
+  if (level > 0 && unsafe[bh] == 0) return;  // uniform over the block
   const int b = bh / p.heads, h = bh % p.heads;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int j0 = (blockIdx.y * 128 + tid) * NJ;
   const bool active = j0 < p.dqk;  // every thread takes part in the block scan below
-  const int t0 = c * kC, tn = min(kC, p.seqlen - t0);
+  const int t0 = c * kc, tn = min(kc, p.seqlen - t0);
   const T* q = static_cast<const T*>(p.q) + b * p.sq[0] + h * p.sq[1];
   const T* k = static_cast<const T*>(p.k) + b * p.sk[0] + h * p.sk[1];
   const float* li = p.log_i + b * p.si[0] + h * p.si[1];
@@ -96,7 +100,7 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
     const float rho = 0.5f * gs;
     const float xq = bt - rho, xk = rho - bt + lit;
     // !(x <= max) also catches NaN (e.g. log f = -inf); one store per flagged block suffices
-    if (!(fabsf(xq) <= kMaxExp) || !(fabsf(xk) <= kMaxExp)) unsafe[bh] = 1;
+    if (!(fabsf(xq) <= kMaxExp) || !(fabsf(xk) <= kMaxExp)) unsafe[bh] = level + 1;
     fq[tid] = __expf(xq);
     fk[tid] = __expf(xk);
     __syncthreads();
@@ -165,7 +169,7 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
       Ks[o] = __float2bfloat16_rn(ks[0]);
     }
   }
-  if (bad) unsafe[bh] = 1;
+  if (bad) unsafe[bh] = level + 1;
 #pragma unroll
   for (int u = 0; u < NJ; ++u) {
     const int64_t vi = ((int64_t)bh * nch + c) * p.dqk + j0 + u;
@@ -232,9 +236,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     mlstm_stream_kernel(const __grid_constant__ CUtensorMap tmQs, const __grid_constant__ CUtensorMap tmKs,
                         const __grid_constant__ CUtensorMap tmV,
                         const Params p, const float* __restrict__ decay, const float* __restrict__ rho_e,
-                        const float* __restrict__ nadd, const int* __restrict__ unsafe) {
-  // pairs flagged by the prescale pass are run by the recurrent kernel (uniform over the CTA)
-  if (unsafe[blockIdx.z * p.heads + blockIdx.y]) return;
+                        const float* __restrict__ nadd, const int* __restrict__ unsafe, int kc, int want) {
+  // this launch runs the pairs whose range level is `want` (0: 128-step chunks, 1: 64-step
+  // chunks); the others belong to another launch (uniform over the CTA)
+  if (unsafe[blockIdx.z * p.heads + blockIdx.y] != want) return;
   using L = SL<DK>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -258,8 +263,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   const int ch = 32 * hf;
   const int e0 = blockIdx.x * kDV, h = blockIdx.y, b = blockIdx.z;
   const int bh = b * p.heads + h;
-  const int nch = (p.seqlen + kC - 1) / kC;
+  const int nch = (p.seqlen + kc - 1) / kc;
   const uint32_t sbase = smem_u32(sm);
+  // 64-step chunks load 64-row boxes into the upper half of each 128-row operand panel; the
+  // lower half stays zero (zeroed here), so every MMA keeps its 128-row shape and the extra
+  // rows contribute nothing
+  const uint32_t slot_bytes = kc == kC ? L::kSlotB : L::kSlotB / 2;
+  const uint32_t v_bytes = kc == kC ? kPanel : kPanel / 2;
 
   if (warp == 0) tc::tmem_alloc(tmem_slot, 512);
   if (tid == 0) {
@@ -280,6 +290,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     uint4* zp = reinterpret_cast<uint4*>(sm + L::kP);
     for (int i = tid; i < 2 * kPanel / 16; i += kStreamThreads) zp[i] = make_uint4(0, 0, 0, 0);
   }
+  if (kc != kC) {  // the ring's and V's rows past the chunk: zero for the whole launch
+    uint4* zr = reinterpret_cast<uint4*>(sm + L::kRing);
+    for (int i = tid; i < L::kStages * L::kSlotB / 16; i += kStreamThreads) zr[i] = make_uint4(0, 0, 0, 0);
+    uint4* zv = reinterpret_cast<uint4*>(sm + L::kV);
+    for (int i = tid; i < kPanel / 16; i += kStreamThreads) zv[i] = make_uint4(0, 0, 0, 0);
+  }
   tc::fence_async_smem();
   __syncthreads();
   tc::tc_fence_after();
@@ -298,8 +314,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     if (lane == 0) {
       int loads_v = 0, waited_v = 0;
       auto load_v = [&](int c) {
-        tc::mbar_expect_tx(bar_v, kPanel);
-        tc::tma_load_4d(sm + L::kV, &tmV, bar_v, e0, c * kC, h, b);
+        tc::mbar_expect_tx(bar_v, v_bytes);
+        tc::tma_load_4d(sm + L::kV, &tmV, bar_v, e0, c * kc, h, b);
         ++loads_v;
       };
       load_v(0);
@@ -371,12 +387,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         if (idx >= L::kStages && !tc::mbar_wait(&empty[slot], ((idx / L::kStages) - 1) & 1, abort_flag, p.wait_limit)) break;
         const int c = idx / L::kLPC, i = idx % L::kLPC;
         unsigned char* dst = sm + L::kRing + slot * L::kSlotB;
-        tc::mbar_expect_tx(&full[slot], L::kSlotB);
+        tc::mbar_expect_tx(&full[slot], slot_bytes);
 #pragma unroll
         for (int pp = 0; pp < 2; ++pp) {
           const int pnl = 2 * i + pp;
-          tc::tma_load_4d(dst + pp * 2 * kPanel, &tmQs, &full[slot], pnl * 64, c * kC, h, b);
-          tc::tma_load_4d(dst + pp * 2 * kPanel + kPanel, &tmKs, &full[slot], pnl * 64, c * kC, h, b);
+          tc::tma_load_4d(dst + pp * 2 * kPanel, &tmQs, &full[slot], pnl * 64, c * kc, h, b);
+          tc::tma_load_4d(dst + pp * 2 * kPanel + kPanel, &tmKs, &full[slot], pnl * 64, c * kc, h, b);
         }
         ++issued;
       }
@@ -504,14 +520,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     // columns, from H buffer c & 1 (the next chunk's Qs.Snap runs into the other).
     auto epilogue = [&](int c) {
       {
-        const int tg = c * kC + row;
+        const int tg = c * kc + row;
         const float* qnp = rowv + (c & 1) * 512;
         const float* denp = qnp + 256;
         const float inv = 1.f / fmaxf(qnp[row] + qnp[kC + row] + denp[row] + denp[kC + row], 1.f);
         float v[32];
         tc::tmem_ld32(tm + L::tH + (c & 1) * kDV + ch, v);
         tc::tmem_wait_ld();
-        if (tg < p.seqlen && e0 + ch < p.dv) {
+        if (row < kc && tg < p.seqlen && e0 + ch < p.dv) {
           __nv_bfloat16* orow =
               static_cast<__nv_bfloat16*>(p.h) + b * p.sh[0] + h * p.sh[1] + (int64_t)tg * p.th + e0 + ch;
 #pragma unroll
@@ -663,7 +679,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 size_t stream_workspace(const Params& p) {
-  const size_t nch = (p.seqlen + kC - 1) / kC;
+  const size_t nch = (p.seqlen + kC / 2 - 1) / (kC / 2);  // per-chunk vectors sized for 64-step chunks
   const size_t ops = (size_t)p.batch * p.heads * p.seqlen * p.dqk * 2;  // bf16 tensor
   const size_t vec = (size_t)p.batch * p.heads * nch * p.dqk * 4;
   const size_t flags = (size_t)p.batch * p.heads * 4;  // per (b, h): out of the kernel's range
@@ -687,9 +703,9 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
               p.workspace_bytes);
     return HXM_EBADARG;
   }
-  const int nch = (p.seqlen + kC - 1) / kC;
+  const int nch64 = (p.seqlen + kC / 2 - 1) / (kC / 2);
   const size_t ops = align256((size_t)p.batch * p.heads * p.seqlen * DK * 2);
-  const size_t vec = align256((size_t)p.batch * p.heads * nch * DK * 4);
+  const size_t vec = align256((size_t)p.batch * p.heads * nch64 * DK * 4);
   unsigned char* ws = static_cast<unsigned char*>(p.workspace);
   __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(ws);
   __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(ws + ops);
@@ -702,31 +718,43 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   const bool pair = p.tq % 2 == 0 && p.tk % 2 == 0 && p.sq[0] % 2 == 0 && p.sq[1] % 2 == 0 && p.sk[0] % 2 == 0 &&
                     p.sk[1] % 2 == 0 && reinterpret_cast<uintptr_t>(p.q) % 4 == 0 &&
                     reinterpret_cast<uintptr_t>(p.k) % 4 == 0;
-  if (pair) {
-    dim3 pg(p.batch * p.heads * nch, (DK + 255) / 256);
-    mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe);
-  } else {
-    dim3 pg(p.batch * p.heads * nch, (DK + 127) / 128);
-    mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe);
-  }
-  hxm_status s = check_launch("hxm_mlstm_chunkwise_fwd (prescale)");
-  if (s != HXM_OK) return s;
-  CUtensorMap mq, mk, mv;
-  const uint64_t dd[4] = {(uint64_t)DK, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
-  const uint64_t sd[3] = {(uint64_t)DK * 2, (uint64_t)p.seqlen * DK * 2, (uint64_t)p.heads * p.seqlen * DK * 2};
-  const uint64_t dvd[4] = {(uint64_t)p.dv, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
-  const uint64_t sv[3] = {(uint64_t)p.tv * 2, (uint64_t)p.sv[1] * 2, (uint64_t)p.sv[0] * 2};
-  if ((s = make_map_bf16_4d(&mq, Qs, dd, sd, "mlstm Qs")) != HXM_OK) return s;
-  if ((s = make_map_bf16_4d(&mk, Ks, dd, sd, "mlstm Ks")) != HXM_OK) return s;
-  if ((s = make_map_bf16_4d(&mv, p.v, dvd, sv, "mlstm v")) != HXM_OK) return s;
+  auto prescale = [&](int kc, int level) {
+    const int nch = (p.seqlen + kc - 1) / kc;
+    if (pair) {
+      dim3 pg(p.batch * p.heads * nch, (DK + 255) / 256);
+      mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level);
+    } else {
+      dim3 pg(p.batch * p.heads * nch, (DK + 127) / 128);
+      mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level);
+    }
+    return check_launch("hxm_mlstm_chunkwise_fwd (prescale)");
+  };
   const size_t smem = L::kBytes + 1024;
   auto kern = mlstm_stream_kernel<DK>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dv + kDV - 1) / kDV, p.heads, p.batch);
-  kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mv, p, decay, rho_e, nadd, unsafe);
-  if ((s = check_launch("hxm_mlstm_chunkwise_fwd (stream)")) != HXM_OK) return s;
-  // the flagged pairs, exactly (every other CTA of this launch returns at once)
-  return launch_recurrent(p, st, unsafe);
+  auto stream = [&](int kc, int want) {
+    CUtensorMap mq, mk, mv;
+    const uint64_t dd[4] = {(uint64_t)DK, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
+    const uint64_t sd[3] = {(uint64_t)DK * 2, (uint64_t)p.seqlen * DK * 2, (uint64_t)p.heads * p.seqlen * DK * 2};
+    const uint64_t dvd[4] = {(uint64_t)p.dv, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
+    const uint64_t sv[3] = {(uint64_t)p.tv * 2, (uint64_t)p.sv[1] * 2, (uint64_t)p.sv[0] * 2};
+    hxm_status s;
+    if ((s = make_map_bf16_4d(&mq, Qs, dd, sd, "mlstm Qs", kc)) != HXM_OK) return s;
+    if ((s = make_map_bf16_4d(&mk, Ks, dd, sd, "mlstm Ks", kc)) != HXM_OK) return s;
+    if ((s = make_map_bf16_4d(&mv, p.v, dvd, sv, "mlstm v", kc)) != HXM_OK) return s;
+    kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mv, p, decay, rho_e, nadd, unsafe, kc, want);
+    return check_launch("hxm_mlstm_chunkwise_fwd (stream)");
+  };
+  // 128-step chunks for every pair in range; the pairs out of it are prescaled again in 64-step
+  // chunks (halving each chunk's exponent range) and run with those; the pairs out of range even
+  // then take the exact recurrent kernel.  Each launch's other CTAs return at once.
+  hxm_status s;
+  if ((s = prescale(kC, 0)) != HXM_OK) return s;
+  if ((s = stream(kC, 0)) != HXM_OK) return s;
+  if ((s = prescale(kC / 2, 1)) != HXM_OK) return s;
+  if ((s = stream(kC / 2, 1)) != HXM_OK) return s;
+  return launch_recurrent(p, st, unsafe, 2);
 }
 
 hxm_status launch_stream(const Params& p, cudaStream_t st) {

@@ -9,10 +9,10 @@
 
 namespace hxm {
 
-// 4-D bf16 tensor map with a {64, 128, 1, 1} box and 128-byte swizzle.
-// dims / strides are innermost-first; strides in bytes for dims 1..3.
+// 4-D bf16 tensor map with a {64, box_rows, 1, 1} box (box_rows <= 256; 128 unless given) and
+// 128-byte swizzle.  dims / strides are innermost-first; strides in bytes for dims 1..3.
 inline hxm_status make_map_bf16_4d(CUtensorMap* map, const void* base, const uint64_t dims[4],
-                                   const uint64_t stride_bytes[3], const char* who) {
+                                   const uint64_t stride_bytes[3], const char* who, uint32_t box_rows = 128) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (!encode) {
     void* fn = nullptr;
@@ -35,7 +35,7 @@ inline hxm_status make_map_bf16_4d(CUtensorMap* map, const void* base, const uin
     }
   cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
   cuuint64_t st[3] = {stride_bytes[0], stride_bytes[1], stride_bytes[2]};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), d, st, box, es,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

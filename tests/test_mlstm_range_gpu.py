@@ -1,12 +1,14 @@
 """mLSTM over the whole gate range, forward and backward, against the float64 oracle.
 
-Strong forget gates (logsigmoid of N(-2, 1) and N(-4, 1) pre-activations,
-about -280 and -520 per 128 steps) push the key-streaming kernel's chunk
-factors e^(|g|/2) past the fp32 range: the prescale pass flags those
-(batch, head) pairs on the device and the exact recurrent kernel runs them
-in the same call.  The reference loop (tfla_interface.py:84-139) multiplies
-by f step by step and has no such limit, so neither may this path.  The
-chunkwise backward shortens its chunk for such gates.
+Strong forget gates push the key-streaming kernel's chunk factors e^(|g|/2)
+past the fp32 range (logsigmoid of N(-1.5, 1), N(-2, 1) and N(-4, 1)
+pre-activations sum to about -230, -280 and -520 per 128 steps): the prescale
+pass flags those (batch, head) pairs on the device, they are prescaled again
+in 64-step chunks and run with those, and the pairs still out of range (the
+N(-4, 1) case) take the exact recurrent kernel — all in the same call.  The
+reference loop (tfla_interface.py:84-139) multiplies by f step by step and
+has no such limit, so neither may this path.  The chunkwise backward shortens
+its chunk for such gates.
 
 Tolerances: bf16 I/O 2e-2 normwise relative error against the float64
 oracle on the same bf16-rounded inputs, final states included (as
@@ -62,12 +64,26 @@ def _check(ops, q, k, v, li, lf):
     return out
 
 
-@pytest.mark.parametrize("d", [128, 512])
-@pytest.mark.parametrize("fmu", [-2.0, -4.0])
+@pytest.mark.parametrize("d", [128, 256, 512])
+@pytest.mark.parametrize("fmu", [-1.5, -2.0, -4.0])
 def test_strong_channel_forget_gates(ops, d, fmu):
     """Per-channel gates (mLSTMBlock) with strong forgetting, lengths that are
-    not a multiple of the 128-step chunk."""
+    not a multiple of the 128- or 64-step chunk."""
     _check(ops, *_inputs((1, 2, 300, d), fmu, seed=int(-10 * fmu) + d))
+
+
+def test_64_step_chunks_long_and_segmented(ops):
+    """Every pair in the 64-step range (forget pre-activation N(-1.5, 1)),
+    700 steps, with an initial state: the state carried across a split of
+    the sequence and across the 64-step chunks matches one pass."""
+    q, k, v, li, lf = _inputs((2, 2, 700, 256), -1.5, seed=47)
+    out = _check(ops, q, k, v, li, lf)
+    s = 333
+    a, st = ops.mlstm_chunkwise_fwd(q[:, :, :s], k[:, :, :s], v[:, :, :s], li[:, :, :s], lf[:, :, :s],
+                                    return_state=True)
+    b2, _ = ops.mlstm_chunkwise_fwd(q[:, :, s:], k[:, :, s:], v[:, :, s:], li[:, :, s:], lf[:, :, s:], *st,
+                                    return_state=True)
+    assert rel_err(np64(torch.cat([a, b2], 2)), np64(out)) < TOL16
 
 
 @pytest.mark.parametrize("d", [256, 512])
@@ -78,14 +94,16 @@ def test_strong_head_forget_gates(ops, d):
 
 
 def test_mixed_heads_stream_and_fallback(ops):
-    """One call where some (batch, head) pairs stay in the streaming kernel's
-    range and others do not: each pair is run by exactly one kernel and the
-    outputs and states of both kinds match the oracle."""
+    """One call where (batch, head) pairs take all three routes — 128-step
+    chunks, 64-step chunks, the exact recurrence: each pair is run by exactly
+    one kernel and the outputs and states of every kind match the oracle."""
     q, k, v, li, lf = _inputs((2, 3, 260, 128), 3.0, seed=41)
     g = torch.Generator().manual_seed(42)
     strong = torch.nn.functional.logsigmoid(torch.randn(260, 128, generator=g) - 4.0).cuda()
+    medium = torch.nn.functional.logsigmoid(torch.randn(260, 128, generator=g) - 1.5).cuda()
     lf[0, 1] = strong
     lf[1, 2] = strong
+    lf[1, 0] = medium
     out = _check(ops, q, k, v, li, lf)
     # the pairs left in range agree with a call that holds only them (no cross-talk)
     alone = ops.mlstm_chunkwise_fwd(q[:1, :1], k[:1, :1], v[:1, :1], li[:1, :1], lf[:1, :1])
