@@ -153,29 +153,31 @@ class SelectiveScanFunction(torch.autograd.Function):
 
 class SelectiveScanFnFunction(torch.autograd.Function):
     """Autograd of ``selective_scan_fn`` ((batch, dim, seqlen) layout, softplus(delta + bias),
-    y * silu(z)): forward and backward both on the hxm kernels."""
+    y * silu(z), optional initial state h0): forward and backward both on the hxm kernels
+    (the backward kernel also returns dL/dh0)."""
 
     @staticmethod
-    def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus):
+    def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0):
         t = lambda a: None if a is None else a.transpose(1, 2)
-        ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias)
+        ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, h0)
         ctx.delta_softplus = delta_softplus
         y = torch.empty(u.shape, device=u.device,
                         dtype=u.dtype if u.dtype in (torch.float32, torch.bfloat16) else torch.float32)
         selective_scan_raw(t(u), t(delta), A, t(B), t(C), D, t(z), z_mode="silu" if z is not None else None,
-                           delta_bias=delta_bias, delta_softplus=delta_softplus, out=y.transpose(1, 2))
+                           delta_bias=delta_bias, delta_softplus=delta_softplus, h0=h0, out=y.transpose(1, 2))
         return y
 
     @staticmethod
     def backward(ctx, grad_output):
-        u, delta, A, B, C, D, z, delta_bias = ctx.saved_tensors
+        u, delta, A, B, C, D, z, delta_bias, h0 = ctx.saved_tensors
         t = lambda a: None if a is None else a.transpose(1, 2)
         g = selective_scan_bwd(t(grad_output), t(u), t(delta), A, t(B), t(C), D, t(z),
                                z_mode="silu" if z is not None else None, delta_bias=delta_bias,
-                               delta_softplus=ctx.delta_softplus)
+                               delta_softplus=ctx.delta_softplus, h0=h0)
         cast = lambda x, o: None if (x is None or o is None) else x.to(o.dtype)
         return (cast(t(g["u"]), u), cast(t(g["delta"]), delta), cast(g["A"], A), cast(t(g["B"]), B),
-                cast(t(g["C"]), C), cast(g["D"], D), cast(t(g["z"]), z), cast(g["delta_bias"], delta_bias), None)
+                cast(t(g["C"]), C), cast(g["D"], D), cast(t(g["z"]), z), cast(g["delta_bias"], delta_bias), None,
+                cast(g["h0"], h0))
 
 
 def selective_scan(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor,
@@ -193,11 +195,19 @@ def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_
     u, delta, z: (B, D, L); B, C: (B, N, L); A: (D, N); D, delta_bias: (D,).
     Computes softplus(delta + delta_bias) (if requested), the scan, + D*u and
     y * silu(z).  Returns y (B, D, L) [and the final state (B, D, N) fp32].
+    Differentiable (Euler) through y, into every input and initial_state; the
+    final state is not differentiable, so asking for it (or for the ZOH rule)
+    while gradients are needed raises instead of silently dropping them.
     """
     needs_grad = torch.is_grad_enabled() and any(
-        x is not None and x.requires_grad for x in (u, delta, A, B, C, D, z, delta_bias))
-    if needs_grad and discretization == "euler" and not return_last_state and initial_state is None:
-        return SelectiveScanFnFunction.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus)
+        x is not None and x.requires_grad for x in (u, delta, A, B, C, D, z, delta_bias, initial_state))
+    if needs_grad:
+        if discretization != "euler":
+            raise NotImplementedError("selective_scan_fn: the backward covers the Euler rule only")
+        if return_last_state:
+            raise NotImplementedError("selective_scan_fn: the final state is not differentiable; call with "
+                                      "return_last_state=False under autograd (or under torch.no_grad())")
+        return SelectiveScanFnFunction.apply(u, delta, A, B, C, D, z, delta_bias, delta_softplus, initial_state)
     t = lambda a: None if a is None else a.transpose(1, 2)
     y_bld = torch.empty((u.shape[0], u.shape[1], u.shape[2]), device=u.device,
                         dtype=u.dtype if u.dtype in (torch.float32, torch.bfloat16) else torch.float32)

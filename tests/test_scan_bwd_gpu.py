@@ -106,3 +106,46 @@ def test_empty_sequence_zero_gradients(S):
     y = S.selective_scan(x, x, A, B, B, D)
     y.sum().backward()
     assert float(A.grad.abs().sum()) == 0.0 and float(D.grad.abs().sum()) == 0.0
+
+
+def _loop_h0(x, dt, A, B, C, D, h0):
+    """The loop of _loop started from a state h0 (the continuation of an earlier segment)."""
+    h = h0
+    ys = []
+    for t in range(x.shape[1]):
+        h = torch.exp(A[None] * dt[:, t, :, None]) * h + (dt[:, t] * x[:, t])[..., None] * B[:, t, None]
+        ys.append((h * C[:, t, None]).sum(-1) + D * x[:, t])
+    return torch.stack(ys, 1)
+
+
+def test_fused_entry_initial_state_gradient(S):
+    """selective_scan_fn with initial_state under autograd: the gradient of the
+    initial state (and of every input) against float64 autograd of the loop."""
+    x, dt, A, B, C, D, z, go = _inputs(2, 40, 32, 16, seed=13, dtype=torch.float32)
+    h0 = torch.randn(2, 32, 16, generator=torch.Generator().manual_seed(14))
+    t = lambda a: a.transpose(1, 2).contiguous()
+    ins = {"u": t(x), "delta": t(dt), "A": A, "B": t(B), "C": t(C), "D": D, "h0": h0}
+    cu = {k: v.cuda().requires_grad_(True) for k, v in ins.items()}
+    y = S.selective_scan_fn(cu["u"], cu["delta"], cu["A"], cu["B"], cu["C"], cu["D"], initial_state=cu["h0"])
+    y.backward(t(go).cuda())
+    rf = {k: v.double().requires_grad_(True) for k, v in ins.items()}
+    tb = lambda a: a.transpose(1, 2)
+    yr = _loop_h0(tb(rf["u"]), tb(rf["delta"]), rf["A"], tb(rf["B"]), tb(rf["C"]), rf["D"], rf["h0"])
+    yr.backward(go.double())
+    for k in ins:
+        assert rel_err(np64(cu[k].grad), np64(rf[k].grad)) < 1e-4, k
+
+
+def test_fused_entry_refuses_what_it_cannot_differentiate(S):
+    """Under autograd, asking for the (non-differentiable) final state or the
+    ZOH rule raises instead of returning outputs with no gradient path."""
+    x, dt, A, B, C, D, z, go = _inputs(1, 8, 32, 16, seed=15, dtype=torch.float32)
+    t = lambda a: a.transpose(1, 2).contiguous().cuda()
+    u = t(x).requires_grad_(True)
+    with pytest.raises(NotImplementedError):
+        S.selective_scan_fn(u, t(dt), A.cuda(), t(B), t(C), D.cuda(), return_last_state=True)
+    with pytest.raises(NotImplementedError):
+        S.selective_scan_fn(u, t(dt), A.cuda(), t(B), t(C), D.cuda(), discretization="zoh")
+    with torch.no_grad():
+        y, h = S.selective_scan_fn(u, t(dt), A.cuda(), t(B), t(C), D.cuda(), return_last_state=True)
+    assert y.shape == u.shape and h.shape == (1, 32, 16)
