@@ -38,6 +38,7 @@ class ScanArgs(ct.Structure):
         ("h0", ct.c_void_p),
         ("hT", ct.c_void_p),
         ("z_mode", ct.c_int32), ("delta_softplus", ct.c_int32), ("discretization", ct.c_int32),
+        ("workspace", ct.c_void_p), ("workspace_bytes", ct.c_size_t),
     ]
 
 
@@ -223,6 +224,7 @@ SYMBOLS = {
     "hxm_abi_version": (ct.c_int, []),
     "hxm_last_error_string": (ct.c_char_p, []),
     "hxm_selective_scan_fwd": (ct.c_int, [ct.POINTER(ScanArgs), ct.c_void_p]),
+    "hxm_selective_scan_workspace_size": (ct.c_size_t, [ct.POINTER(ScanArgs)]),
     "hxm_selective_scan_bwd_workspace_size": (ct.c_size_t, [ct.POINTER(ScanBwdArgs)]),
     "hxm_selective_scan_bwd": (ct.c_int, [ct.POINTER(ScanBwdArgs), ct.c_void_p]),
     "hxm_mlstm_workspace_size": (ct.c_size_t, [ct.POINTER(MlstmArgs)]),

@@ -15,7 +15,7 @@
 // Euler (reference) or ZOH update, the C.h + D*u readout and the z gate
 // (y*z or y*silu(z)).  y overwrites u's staging slot and leaves with 16-byte
 // stores.
-#include "scan_kernel.cuh"
+#include "scan_fast.cuh"
 
 #include <cstdlib>
 
@@ -32,6 +32,25 @@ static int io_mode(const void* ptr, const int64_t* s, size_t esize, int tile_inn
   return kGeneric;
 }
 
+}  // namespace scan
+}  // namespace hxm
+
+namespace hxm {
+namespace scan {
+// The fast kernel's time segments for this request (1 when it runs another kernel or needs no
+// split) and the scratch they take.
+static int segments_for(const hxm_scan_args* a, const Params& p, int* seg_len, size_t* bytes) {
+  *bytes = 0;
+  *seg_len = p.seqlen;
+  if (a->io_dtype != HXM_BF16 || a->discretization != 0 || !fast_ok(p, 2) || p.seqlen <= 0) return 1;
+  int dev = 0, num_sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    num_sms = 148;
+  const int nseg = fast_segments(p, num_sms, seg_len);
+  if (nseg > 1) *bytes = sizeof(float) * 17 * (size_t)p.batch * p.dim * (nseg - 1);
+  return nseg;
+}
 }  // namespace scan
 }  // namespace hxm
 
@@ -89,6 +108,18 @@ extern "C" hxm_status hxm_selective_scan_fwd(const hxm_scan_args* a, void* strea
   p.mode_y = io_mode(a->y, p.sy, es, 1);
   // y leaves through u's slot: the slot's layout is u's staging layout.
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  {  // time segments when the caller's workspace holds their scratch (otherwise one pass)
+    int seg_len = 0;
+    size_t need = 0;
+    const int nseg = segments_for(a, p, &seg_len, &need);
+    p.nseg = 1;
+    p.seg_len = p.seqlen;
+    if (nseg > 1 && a->workspace && a->workspace_bytes >= need) {
+      p.nseg = nseg;
+      p.seg_len = seg_len;
+      p.seg_ws = static_cast<float*>(a->workspace);
+    }
+  }
   const bool acc = a->io_dtype == HXM_F32;
   const bool zoh = a->discretization == 1;
   (void)acc;
@@ -104,3 +135,28 @@ int env_knob(const char* name) {
 }
 }  // namespace scan
 }  // namespace hxm
+
+// Scratch bytes for hxm_selective_scan_fwd's time segments (0: none needed).  Mirrors the
+// forward's argument handling; invalid args report 0 (the forward then reports the error).
+extern "C" size_t hxm_selective_scan_workspace_size(const hxm_scan_args* a) {
+  using namespace hxm::scan;
+  if (!a || a->struct_size != sizeof(hxm_scan_args) || a->batch <= 0 || a->dim <= 0 || a->seqlen <= 0 ||
+      a->dstate < 1 || a->dstate > 64 || !a->u || !a->delta || !a->B || !a->C || !a->y)
+    return 0;
+  Params p{};
+  p.batch = a->batch; p.seqlen = a->seqlen; p.dim = a->dim; p.dstate = a->dstate;
+  p.u = a->u; p.dt = a->delta; p.B = a->B; p.C = a->C; p.z = a->z; p.y = a->y;
+  for (int i = 0; i < 3; ++i) {
+    p.su[i] = a->u_stride[i]; p.sdt[i] = a->delta_stride[i]; p.sB[i] = a->B_stride[i];
+    p.sC[i] = a->C_stride[i]; p.sz[i] = a->z_stride[i]; p.sy[i] = a->y_stride[i];
+  }
+  const size_t es = a->io_dtype == HXM_F32 ? 4 : 2;
+  p.mode_u = io_mode(a->u, p.su, es, 1);
+  p.mode_dt = io_mode(a->delta, p.sdt, es, 1);
+  p.mode_z = a->z ? io_mode(a->z, p.sz, es, 1) : kGeneric;
+  p.mode_y = io_mode(a->y, p.sy, es, 1);
+  int seg_len = 0;
+  size_t bytes = 0;
+  segments_for(a, p, &seg_len, &bytes);
+  return bytes;
+}

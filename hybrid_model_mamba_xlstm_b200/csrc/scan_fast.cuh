@@ -149,6 +149,9 @@ HXM_DEV void fast_tile(T* us, const T* ds, const T* zs, const float* __restrict_
   }
 }
 
+// Time segments: blockIdx.z = segment s of p.nseg (steps [tb, te)); a segment s > 0 starts
+// from the carry h_s = exp(A * sum delta_{s-1}) . h_{s-1} + E_{s-1} of the earlier segments'
+// zero-start end states E and delta sums, which scan_fast_state_kernel wrote to p.seg_ws.
 template <typename T, int CH, int kT, int ZMODE, bool SP, bool CM>
 __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   using S = FastSmem<T, CH, kT>;
@@ -163,6 +166,9 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   const int d = d0 + tid;
   const bool dvalid = d < p.dim;
   const int dc = dvalid ? d : 0;
+  const int seg = blockIdx.z;
+  const int tb = p.nseg > 1 ? seg * p.seg_len : 0;
+  const int te = p.nseg > 1 ? min(p.seqlen, tb + p.seg_len) : p.seqlen;
 
   bool pattern = true;
   const float a0 = p.A[(int64_t)dc * p.sA[0]];
@@ -182,6 +188,18 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   }
   const bool use_pow = __all_sync(0xffffffffu, pattern);
   const float a0l2 = a0 * kLog2e;
+  if (seg > 0) {
+    // carry into this segment from the earlier segments' zero-start summaries
+    const float* ws = p.seg_ws + ((int64_t)b * p.dim + dc) * (p.nseg - 1) * 17;
+    for (int s2 = 0; s2 < seg; ++s2) {
+      const float sdl = ws[s2 * 17 + 16];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float2 P = make_float2(ex2_approx(Ash[tid * 16 + 2 * q] * sdl), ex2_approx(Ash[tid * 16 + 2 * q + 1] * sdl));
+        h[q] = __ffma2_rn(P, h[q], make_float2(ws[s2 * 17 + 2 * q], ws[s2 * 17 + 2 * q + 1]));
+      }
+    }
+  }
   const float Dd = (p.D && dvalid) ? p.D[d] : 0.f;
   const float bias = (p.bias && dvalid) ? p.bias[d] : 0.f;
   const bool has_z = ZMODE != 0;
@@ -193,12 +211,12 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   const T* Bg = static_cast<const T*>(p.B) + b * p.sB[0];
   const T* Cg = static_cast<const T*>(p.C) + b * p.sC[0];
   T* yg = static_cast<T*>(p.y) + b * p.sy[0];
-  const int ntiles = (p.seqlen + kT - 1) / kT;
+  const int ntiles = (te - tb + kT - 1) / kT;
 
   auto stage_ptr = [&](int st) { return reinterpret_cast<T*>(smem_raw + st * S::kStageBytes); };
   auto issue = [&](int k) {
     T* base = stage_ptr(k & 1);
-    const int t0 = k * kT, tk = min(kT, p.seqlen - t0);
+    const int t0 = tb + k * kT, tk = min(kT, te - t0);
     constexpr int kChunks = kT / kE;
     // u, delta, z rows
 #pragma unroll 1
@@ -254,7 +272,7 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   issue(0);
   for (int k = 0; k < ntiles; ++k) {
     const int st = k & 1;
-    const int t0 = k * kT, tk = min(kT, p.seqlen - t0);
+    const int t0 = tb + k * kT, tk = min(kT, te - t0);
     cp_async_wait<0>();
     __syncthreads();  // tile k staged; previous tile's y stored and bc table consumed
     if (k + 1 < ntiles) issue(k + 1);
@@ -320,7 +338,7 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
     }
   }
 
-  if (p.hT && dvalid) {
+  if (p.hT && dvalid && te == p.seqlen) {
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       if (2 * q < p.dstate) p.hT[((int64_t)b * p.dim + d) * p.dstate + 2 * q] = h[q].x;
@@ -329,14 +347,192 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   }
 }
 
+// State-only pass over the first nseg - 1 segments (whole tiles): each (channel, segment) runs
+// the recurrence from a zero state over its steps — no readout, no z, no y — and records the
+// state it reaches and its sum of delta (after softplus) in p.seg_ws.  Same staging as the
+// main kernel minus z and C.
+template <typename T, int CH, int kT, bool SP, bool CM>
+__global__ void __launch_bounds__(CH) scan_fast_state_kernel(const Params p) {
+  using S = FastSmem<T, CH, kT>;
+  constexpr int kE = 16 / sizeof(T);
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* bcf = reinterpret_cast<float*>(smem_raw + 2 * S::kStageBytes);  // [kT][32] fp32 (B half used)
+  __shared__ __align__(16) float Ash[CH * 16];
+
+  const int tid = threadIdx.x;
+  const int b = blockIdx.y;
+  const int d0 = blockIdx.x * CH;
+  const int d = d0 + tid;
+  const bool dvalid = d < p.dim;
+  const int dc = dvalid ? d : 0;
+  const int seg = blockIdx.z;  // < nseg - 1: full tiles only
+  const int tb = seg * p.seg_len;
+  const int ntiles = p.seg_len / kT;
+
+  bool pattern = true;
+  const float a0 = p.A[(int64_t)dc * p.sA[0]];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const float a = n < p.dstate ? p.A[(int64_t)dc * p.sA[0] + (int64_t)n * p.sA[1]] : 0.f;
+    Ash[tid * 16 + n] = a * kLog2e;
+    if (n < p.dstate && a != a0 * (float)(n + 1)) pattern = false;
+  }
+  const bool use_pow = __all_sync(0xffffffffu, pattern);
+  const float a0l2 = a0 * kLog2e;
+  const float bias = (p.bias && dvalid) ? p.bias[d] : 0.f;
+  float2 h[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) h[q] = make_float2(0.f, 0.f);
+  float sdl = 0.f;
+
+  const T* ug = static_cast<const T*>(p.u) + b * p.su[0];
+  const T* dtg = static_cast<const T*>(p.dt) + b * p.sdt[0];
+  const T* Bg = static_cast<const T*>(p.B) + b * p.sB[0];
+  auto stage_ptr = [&](int st) { return reinterpret_cast<T*>(smem_raw + st * S::kStageBytes); };
+  auto issue = [&](int k) {
+    T* base = stage_ptr(k & 1);
+    const int t0 = tb + k * kT;
+    constexpr int kChunks = kT / kE;
+#pragma unroll 1
+    for (int which = 0; which < 2; ++which) {
+      const T* g = which == 0 ? ug : dtg;
+      T* slot = base + which * S::kIoSlot;
+      if (CM) {
+        const int64_t st = which == 0 ? p.su[1] : p.sdt[1];
+        constexpr int kRowChunks = CH / kE;
+        for (int c = tid; c < kT * kRowChunks; c += CH) {
+          const int t = c / kRowChunks, ch = (c % kRowChunks) * kE;
+          const int valid = max(0, min(kE, p.dim - (d0 + ch)));
+          const T* src = valid > 0 ? g + (int64_t)(t0 + t) * st + d0 + ch : g;
+          cp_async16(slot + t * CH + ch, src, valid * (int)sizeof(T));
+        }
+      } else {
+        const int64_t sd = which == 0 ? p.su[2] : p.sdt[2];
+        for (int c = tid; c < CH * kChunks; c += CH) {
+          const int ch = c / kChunks, t = (c % kChunks) * kE;
+          const int dd = d0 + ch;
+          const int valid = dd < p.dim ? kE : 0;
+          const T* src = valid > 0 ? g + (int64_t)dd * sd + t0 + t : g;
+          cp_async16(slot + ch * S::kTP + t, src, valid * (int)sizeof(T));
+        }
+      }
+    }
+    T* raw = base + 3 * S::kIoSlot;
+    if (CM) {  // B step rows [kT][B0..15]
+      constexpr int kRowChunks = 16 / kE;
+      for (int c = tid; c < kT * kRowChunks; c += CH) {
+        const int t = c / kRowChunks, n0 = (c % kRowChunks) * kE;
+        const int valid = max(0, min(kE, p.dstate - n0));
+        cp_async16(raw + t * 32 + n0, valid > 0 ? Bg + (int64_t)(t0 + t) * p.sB[1] + n0 : Bg, valid * (int)sizeof(T));
+      }
+    } else {  // B rows [16][kT]
+      for (int c = tid; c < 16 * kChunks; c += CH) {
+        const int n = c / kChunks, t = (c % kChunks) * kE;
+        const int valid = n < p.dstate ? kE : 0;
+        cp_async16(raw + n * S::kTP + t, valid > 0 ? Bg + (int64_t)n * p.sB[2] + t0 + t : Bg,
+                   valid * (int)sizeof(T));
+      }
+    }
+    cp_async_commit();
+  };
+
+  issue(0);
+  for (int k = 0; k < ntiles; ++k) {
+    const int st = k & 1;
+    cp_async_wait<0>();
+    __syncthreads();
+    if (k + 1 < ntiles) issue(k + 1);
+    {  // B rows -> fp32 [t][32] table (columns 0..15)
+      const T* raw = stage_ptr(st) + 3 * S::kIoSlot;
+      for (int c = tid; c < 16 * (kT / 8); c += CH) {
+        float v[8];
+        if (CM) {
+          const int t = c / 2, n8 = (c % 2) * 8;
+          read8<T, CH, kT>(raw + t * 32 + n8, kTimeMaj, 0, 0, v);
+          float4* dst = reinterpret_cast<float4*>(bcf + t * 32 + n8);
+          dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+          dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+          const int col = c % 16, t8 = (c / 16) * 8;
+          read8<T, CH, kT>(raw + col * S::kTP, kTimeMaj, 0, t8, v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) bcf[(t8 + j) * 32 + col] = v[j];
+        }
+      }
+    }
+    __syncthreads();
+    const T* us = stage_ptr(st);
+    const T* ds = us + S::kIoSlot;
+#pragma unroll 1
+    for (int tt = 0; tt < kT; tt += 8) {
+      float uv[8], dv[8];
+      tile_read8<T, CH, kT, CM>(us, tid, tt, uv);
+      tile_read8<T, CH, kT, CM>(ds, tid, tt, dv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float x = dv[j] + bias;
+        if (SP) x = softplus<false>(x);
+        sdl += x;
+        const float du = x * uv[j];
+        const float4* b4 = reinterpret_cast<const float4*>(bcf + (tt + j) * 32);
+        if (use_pow) {
+          const float r = ex2_approx(x * a0l2);
+          const float r2 = r * r, r4 = r2 * r2, r8 = r4 * r4;
+          float2 pw[8];
+          pw[0] = make_float2(r, r2);
+          pw[1] = make_float2(r2 * r, r4);
+          pw[2] = __fmul2_rn(f2(r4), pw[0]);
+          pw[3] = __fmul2_rn(f2(r4), pw[1]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) pw[4 + q] = __fmul2_rn(f2(r8), pw[q]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 bb = b4[q];
+            h[2 * q] = __ffma2_rn(pw[2 * q], h[2 * q], __fmul2_rn(f2(du), make_float2(bb.x, bb.y)));
+            h[2 * q + 1] = __ffma2_rn(pw[2 * q + 1], h[2 * q + 1], __fmul2_rn(f2(du), make_float2(bb.z, bb.w)));
+          }
+        } else {
+          const float4* a4 = reinterpret_cast<const float4*>(Ash + tid * 16);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 bb = b4[q], aa = a4[q];
+            h[2 * q] = __ffma2_rn(make_float2(ex2_approx(x * aa.x), ex2_approx(x * aa.y)), h[2 * q],
+                                  __fmul2_rn(f2(du), make_float2(bb.x, bb.y)));
+            h[2 * q + 1] = __ffma2_rn(make_float2(ex2_approx(x * aa.z), ex2_approx(x * aa.w)), h[2 * q + 1],
+                                      __fmul2_rn(f2(du), make_float2(bb.z, bb.w)));
+          }
+        }
+      }
+    }
+  }
+  if (dvalid) {
+    float* ws = p.seg_ws + (((int64_t)b * p.dim + d) * (p.nseg - 1) + seg) * 17;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      ws[2 * q] = h[q].x;
+      ws[2 * q + 1] = h[q].y;
+    }
+    ws[16] = sdl;
+  }
+}
+
 template <typename T, int CH, int kT, int ZMODE, bool SP, bool CM>
 hxm_status launch_fast(const Params& p, cudaStream_t stream) {
   using S = FastSmem<T, CH, kT>;
   const size_t smem = S::kBytes;
+  if (p.nseg > 1) {
+    auto skern = scan_fast_state_kernel<T, CH, kT, SP, CM>;
+    if (smem > 48 * 1024 - sizeof(float) * CH * 16)
+      HXM_CUDA_TRY(cudaFuncSetAttribute(skern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 sgrid((p.dim + CH - 1) / CH, p.batch, p.nseg - 1);
+    skern<<<sgrid, CH, smem, stream>>>(p);
+    hxm_status s = check_launch("hxm_selective_scan_fwd (segment states)");
+    if (s != HXM_OK) return s;
+  }
   auto kern = scan_fast_kernel<T, CH, kT, ZMODE, SP, CM>;
   if (smem > 48 * 1024 - sizeof(float) * CH * 16)
     HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid((p.dim + CH - 1) / CH, p.batch);
+  dim3 grid((p.dim + CH - 1) / CH, p.batch, p.nseg > 1 ? p.nseg : 1);
   kern<<<grid, CH, smem, stream>>>(p);
   return check_launch("hxm_selective_scan_fwd (fast)");
 }
@@ -371,6 +567,31 @@ hxm_status pick_fast_modes(const Params& p, cudaStream_t stream) {
   if (zm == 2) return launch_fast<T, CH, 32, 2, false, CM>(p, stream);
   if (zm == 1) return launch_fast<T, CH, 32, 1, false, CM>(p, stream);
   return launch_fast<T, CH, 32, 0, false, CM>(p, stream);
+}
+
+// Time segments for the fast kernel: a grid of fewer CTAs than SMs leaves most of the GPU idle
+// (one thread per channel; e.g. one batch row of 4096 channels = 64 CTAs on 148 SMs), so the
+// sequence is cut into 16 segments of >= 128 steps (a multiple of the 32-step tile) that run in
+// parallel after a state-only pass over the first 15 (about 40 % more work in all).  Measured on
+// B200 (one row x 32768 x 4096): 4.07 ms in one pass, 1.98 / 1.24 / 1.22 ms with 4 / 8 / 16
+// segments; with 2-4 segments the state pass itself is still occupancy-bound, and from about
+// one CTA per SM up (4 rows: 4.10 ms, 3.95 with 16; 8 rows: 5.44, 7.6) splitting does not pay.
+// HXM_SCAN_NSEG forces a count (1 = one pass).
+inline int fast_segments(const Params& p, int num_sms, int* seg_len) {
+  const int ch = p.dim >= 64 ? 64 : 32;
+  const int64_t ctas = (int64_t)((p.dim + ch - 1) / ch) * p.batch;
+  int nseg = env_knob("HXM_SCAN_NSEG");
+  if (nseg <= 0) nseg = ctas < (int64_t)num_sms ? 16 : 1;
+  nseg = max(1, min(nseg, 16));
+  int len = 0;
+  while (nseg > 1) {
+    len = ((p.seqlen + nseg - 1) / nseg + 31) / 32 * 32;
+    if (len >= 128 || env_knob("HXM_SCAN_NSEG") > 0) break;
+    nseg /= 2;
+  }
+  if (nseg > 1) nseg = (p.seqlen + len - 1) / len;  // segments actually covered
+  *seg_len = nseg > 1 ? len : p.seqlen;
+  return nseg > 1 ? nseg : 1;
 }
 
 // CTA width: 64 channels (two warps sharing one B, C table) unless the

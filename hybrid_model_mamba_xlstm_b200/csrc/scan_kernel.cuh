@@ -53,6 +53,12 @@ struct Params {
   float* hT;
   int z_mode, softplus;
   int mode_u, mode_dt, mode_z, mode_y;
+  // time segments of the fast kernel (nseg = 1: one pass over the whole sequence).  Segment s
+  // covers steps [s * seg_len, min((s + 1) * seg_len, seqlen)); seg_ws holds, per (batch,
+  // channel) and segment s < nseg - 1, the state that segment reaches from zero (dstate <= 16
+  // floats, padded to 16) and its sum of delta: 17 floats.
+  float* seg_ws;
+  int seg_len, nseg;
 };
 
 template <typename T, int CH, int kT>

@@ -98,6 +98,10 @@ def selective_scan_raw(u, delta, A, B, C, D=None, z=None, *, z_mode=None, delta_
     hT = torch.empty((bt, dm, A.shape[1]), device=dev, dtype=torch.float32) if return_last_state else None
     a.y, a.y_stride = ptr(y), y.stride()
     a.hT = ptr(hT)
+    # scratch for the time segments the library runs when the grid would not fill the GPU
+    ws_bytes = int(_lib.lib().hxm_selective_scan_workspace_size(a))
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8) if ws_bytes else None
+    a.workspace, a.workspace_bytes = ptr(ws), ws_bytes
     _lib.call("hxm_selective_scan_fwd", a, stream_of(dev))
     return (y, hT) if return_last_state else y
 

@@ -88,9 +88,18 @@ typedef struct hxm_scan_args {
   int32_t z_mode;           /* 0 none, 1 multiply, 2 silu-gate               */
   int32_t delta_softplus;   /* 0/1                                           */
   int32_t discretization;   /* 0 euler (reference CPU path), 1 zoh           */
+  void* workspace;          /* hxm_selective_scan_workspace_size() bytes, or */
+  size_t workspace_bytes;   /* NULL / 0: one pass (no time segments)         */
 } hxm_scan_args;
 
 hxm_status hxm_selective_scan_fwd(const hxm_scan_args* args, void* stream);
+/* Scratch the forward can use for time segments (0 = none): when the grid   */
+/* would not fill the GPU (few batch rows x channels, e.g. one shard of a   */
+/* batch split over GPUs), bf16 Euler requests run the sequence as up to 16 */
+/* parallel segments after a state-only pass; with workspace == NULL or too */
+/* small the forward runs one pass.  17 floats per (batch, channel) and     */
+/* segment boundary.                                                         */
+size_t hxm_selective_scan_workspace_size(const hxm_scan_args* args);
 
 /* Selective scan backward (Euler discretization).                           */
 /* Replaces the recompute-under-autograd backward of SelectiveScanFunction   */

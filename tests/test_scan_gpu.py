@@ -225,3 +225,84 @@ def test_bf16_channel_major_projection_views(ops):
     yr, _ = R.selective_scan(np64(u), np64(dt), np64(A), np64(Bm), np64(Cm), np64(D), z=np64(z), z_mode="silu",
                              delta_bias=np64(bias), delta_softplus=True)
     assert rel_err(np64(y), yr) < TOL16
+
+
+# ---------------------------------------------------------------- time segments --
+def _fused(ops, inp, h0=None, nseg=None):
+    """selective_scan_fn with HXM_SCAN_NSEG forcing the segment count (None: automatic)."""
+    import os
+    old = os.environ.get("HXM_SCAN_NSEG")
+    if nseg is not None:
+        os.environ["HXM_SCAN_NSEG"] = str(nseg)
+    try:
+        return ops.selective_scan_fn(inp.u, inp.delta, inp.A, inp.B, inp.C, inp.D, z=inp.z, delta_bias=inp.delta_bias,
+                                     delta_softplus=True, return_last_state=True, initial_state=h0)
+    finally:
+        if nseg is not None:
+            if old is None:
+                del os.environ["HXM_SCAN_NSEG"]
+            else:
+                os.environ["HXM_SCAN_NSEG"] = old
+
+
+@pytest.mark.parametrize("L,nseg", [(1000, 2), (1000, 3), (4101, 16), (2048, None)])
+def test_time_segments_match_one_pass_and_oracle(ops, L, nseg):
+    """A grid too small for the GPU (one batch row, 256 channels) runs as
+    parallel time segments after a state-only pass: y and the final state
+    match the float64 oracle (bf16 2e-2) and the one-pass kernel (1e-3: the
+    carry uses exp(A * sum delta) instead of the product of per-step
+    factors), from a nonzero initial state, with ragged segment ends."""
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+    inp = scan_inputs(1, L, 256, 16, torch.bfloat16, seed=21, device="cuda")
+    h0 = torch.randn(1, 256, 16, generator=torch.Generator().manual_seed(22)).cuda()
+    y, h = _fused(ops, inp, h0, nseg)
+    y1, h1 = _fused(ops, inp, h0, 1)
+    yr, hr = _oracle_bdl(inp, h0=np64(h0))
+    assert rel_err(np64(y), np.swapaxes(yr, 1, 2)) < TOL16
+    assert rel_err(np64(h), hr) < TOL16
+    assert rel_err(np64(y), np64(y1)) < 1e-3
+    assert rel_err(np64(h), np64(h1)) < 1e-3
+
+
+def test_time_segments_channel_major_views(ops):
+    """The Mamba layer's (B, L, D) projection views (channel-major fast path)
+    with few channels: segmented run vs the one-pass run and the oracle."""
+    g = torch.Generator().manual_seed(23)
+    bt, L, dm, n = 1, 1500, 128, 16
+    xz = torch.randn(bt, L, 2 * dm, generator=g).to("cuda", torch.bfloat16)
+    x, zz = xz[..., :dm], xz[..., dm:]
+    dt = (torch.rand(bt, L, dm, generator=g) * 0.1).to("cuda", torch.bfloat16)
+    bc = torch.randn(bt, L, 2 * n, generator=g).to("cuda", torch.bfloat16)
+    A = -torch.arange(1, n + 1, dtype=torch.float32).repeat(dm, 1).cuda()
+    D = torch.ones(dm, device="cuda")
+    import os
+    ys = []
+    for nseg in ("4", "1"):
+        os.environ["HXM_SCAN_NSEG"] = nseg
+        try:
+            ys.append(ops.selective_scan_raw(x, dt, A, bc[..., :n], bc[..., n:], D, zz, z_mode="silu",
+                                             return_last_state=True))
+        finally:
+            del os.environ["HXM_SCAN_NSEG"]
+    yr, hr = R.selective_scan(np64(x), np64(dt), np64(A), np64(bc[..., :n]), np64(bc[..., n:]), np64(D),
+                              z=np64(zz), z_mode="silu")
+    assert rel_err(np64(ys[0][0]), yr) < TOL16 and rel_err(np64(ys[0][1]), hr) < TOL16
+    assert rel_err(np64(ys[0][0]), np64(ys[1][0])) < 1e-3
+
+
+@pytest.mark.slow
+def test_time_segments_one_row_of_the_long_workload(ops):
+    """One batch row of the long-context scan (32768 steps x 4096 channels:
+    one GPU's share when batch 8 is split over 8 GPUs) runs in automatic time
+    segments; three channels checked against the C oracle over all steps."""
+    from hybrid_model_mamba_xlstm_b200.workloads import scan_rows
+    from oracle import build as OC
+    inp = scan_rows(range(5, 6), 32768, 4096, 16, torch.bfloat16, seed=11, device="cuda")
+    y, h = _fused(ops, inp)
+    for d in (0, 2049, 4095):
+        f = lambda t: t[:, d:d + 1].float().cpu().numpy()  # noqa: E731
+        yr, hr = OC.scan(f(inp.u), f(inp.delta), inp.A[d:d + 1].cpu().numpy(), inp.B.float().cpu().numpy(),
+                         inp.C.float().cpu().numpy(), inp.D[d:d + 1].cpu().numpy(), f(inp.z),
+                         inp.delta_bias[d:d + 1].cpu().numpy(), softplus=True, z_mode=2, disc=0)
+        assert rel_err(np64(y[0, d]), yr[0, 0]) < TOL16, d
+        assert rel_err(np64(h[0, d]), hr[0, 0]) < TOL16, d
