@@ -8,8 +8,17 @@ reference re-runs the whole prefix per generated token
 token per step on the carried states and must pick the same tokens.
 
 Tolerances (normwise relative error on the logits): fp32 model 1e-4, bf16
-model 3e-2 (one bf16 rounding of the activations per layer on either side).
+2e-2.  With random block-diagonal recurrent sLSTM weights the small test
+model is chaotic: rounding only its weights to bf16 moves its fp32 logits by
+0.8 % / 2.9 % / 15 % after 50 / 100 / 200 steps (measured on B200), so a bf16
+run of it cannot be held to the fp32 one; those tests hold a bf16 run cut into
+pieces to the uncut bf16 run (measured 1.6e-3), which is what the carried
+states must reproduce.  Without recurrent weights the model is stable and its
+bf16 run is held to the fp32 run on the same bf16-rounded weights
+(measured 1.0e-2).
 """
+import copy
+
 import numpy as np
 import pytest
 import torch
@@ -60,7 +69,8 @@ def test_wavefront_prefill_equals_full_forward(L, pieces):
     logits of the single-stream whole-sequence forward (fp32 1e-4, bf16 with the
     prefill's tensor-core paths 3e-2), and the carried states continue it."""
     for dtype, kw, tol in ((torch.float32, {}, 1e-4),
-                           (torch.bfloat16, dict(recurrent=True, head_dim=128, dim=256, slstm_heads=2), 3e-2)):
+                           (torch.bfloat16, dict(recurrent=True, head_dim=128, dim=256, slstm_heads=2), 2e-2),
+                           (torch.bfloat16, dict(recurrent=False, head_dim=128, dim=256, slstm_heads=2), 2e-2)):
         model = _small(L, dtype, **kw)
         ids = torch.randint(0, 97, (2, 400), device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
         with torch.no_grad():
@@ -68,7 +78,11 @@ def test_wavefront_prefill_equals_full_forward(L, pieces):
             caches = model.init_caches()
             wave = model.prefill(ids[:, :384], pieces=pieces, caches=caches)
             nxt = model(ids[:, 384:], caches=caches)
-        assert rel_err(np64(torch.cat([wave, nxt], 1)), np64(full)) < tol, (dtype, pieces)
+            stable_bf16 = dtype == torch.bfloat16 and not kw["recurrent"]
+            f32 = copy.deepcopy(model).float()(ids) if stable_bf16 else None
+        assert rel_err(np64(torch.cat([wave, nxt], 1)), np64(full)) < tol, (dtype, kw, pieces)
+        if stable_bf16:  # the bf16 arithmetic itself against fp32 on the same weights
+            assert rel_err(np64(full), np64(f32)) < tol, (dtype, kw, pieces)
 
 
 def test_prefill_graph_replays_the_wavefront(L):
@@ -102,7 +116,7 @@ def test_pieces_equal_full_prefill_bf16_tensor_core_paths(L):
         parts = [model(ids[:, :200], caches=caches), model(ids[:, 200:290], caches=caches)]
         for t in range(290, 300):
             parts.append(model(ids[:, t:t + 1], caches=caches))
-    assert rel_err(np64(torch.cat(parts, 1)), np64(full)) < 3e-2
+    assert rel_err(np64(torch.cat(parts, 1)), np64(full)) < 2e-2
 
 
 def test_generate_greedy_matches_full_recompute(L):

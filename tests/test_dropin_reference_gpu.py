@@ -10,7 +10,7 @@ and then runs the reference's MambaBlock / mLSTMBlock classes themselves on
 CUDA.  Their outputs must match the golden outputs the same reference
 produced on CPU in float64 (fp32: normwise relative error 1e-4), and a bf16
 block on the tensor-core path must match the reference block's own float64
-loop (3e-2, the bf16 block tolerance: bf16 GEMMs around the recurrence).
+loop on the same bf16-rounded weights and input (2e-2).
 """
 import os
 import sys
@@ -96,9 +96,10 @@ def test_reference_mlstm_block_bf16_tensor_core_path(ref):
     _, lb, calls = ref
     torch.manual_seed(5)
     blk = lb.mLSTMBlock(256, head_dim=128, num_heads=2).double()
-    for p in blk.parameters():
-        torch.nn.init.normal_(p, 0.0, 0.05)
-    x = torch.randn(2, 160, 256, dtype=torch.float64)
+    with torch.no_grad():
+        for p in blk.parameters():
+            p.copy_(torch.randn_like(p).mul_(0.05).to(torch.bfloat16).double())
+    x = torch.randn(2, 160, 256).to(torch.bfloat16).double()
     mine = lb.apply_tfla
     import hybrid_xmamba.kernels.tfla.tfla_interface as ti
     lb.apply_tfla = ti.apply_tfla  # the reference's own path, float64 on CPU
@@ -111,4 +112,4 @@ def test_reference_mlstm_block_bf16_tensor_core_path(ref):
     with torch.no_grad():
         got = blk.to("cuda", torch.bfloat16)(x.to("cuda", torch.bfloat16))
     assert calls["tfla"] == n0 + 1
-    assert rel_err(np64(got), want.numpy()) < 3e-2
+    assert rel_err(np64(got), want.numpy()) < 2e-2

@@ -2,8 +2,10 @@
 forward outputs (golden fixtures made by running the reference in float64).
 
 Reference state_dicts load unchanged.  fp32: normwise relative error 1e-4
-(cuBLAS fp32 GEMMs + fp32 kernels); bf16 model: 5e-2 on the logits
-(bf16 weights, activations and GEMM inputs through 4 layers).
+(cuBLAS fp32 GEMMs + fp32 kernels).  bf16: the fp32 path is the one pinned
+to the reference, so a bf16 model is checked against that fp32 path on the
+same bf16-rounded weights, at 2e-2 — the bf16 arithmetic alone (the reference
+itself does not run in bf16: its scan returns fp32 into a bf16 projection).
 """
 import numpy as np
 import pytest
@@ -80,11 +82,16 @@ def test_hybrid_lm_logits_match_reference_fp32(L, golden):
 
 
 def test_hybrid_lm_logits_bf16(L, golden):
+    """The bf16 model against the fp32 model (the path pinned to the reference
+    above) with the same bf16-rounded weights: 2e-2."""
+    import copy
     g = golden("hybrid_lm")
-    model = _lm(L, g).to(torch.bfloat16).eval()
+    m16 = _lm(L, g).to(torch.bfloat16).eval()
+    m32 = copy.deepcopy(m16).float()
+    ids = torch.as_tensor(g["ids"]).cuda()
     with torch.no_grad():
-        logits = model(torch.as_tensor(g["ids"]).cuda())
-    assert rel_err(np64(logits), g["logits"]) < 5e-2
+        logits, want = m16(ids), m32(ids)
+    assert rel_err(np64(logits), np64(want)) < 2e-2
 
 
 def test_hybrid_350m_logits_match_reference_fp32(L, golden):
