@@ -15,7 +15,7 @@
 //   - Scratch: one file-scope device array of kScratchBytes = 32 MiB.  Every
 //     GPU that loads this library holds those 32 MiB until the process exits.
 //   - Requests whose scratch exceeds 32 MiB are rejected with HXM_EBADARG
-//     (scratch = 2 * B*H*L*dqk * 2 bytes + 3 * B*H*ceil(L/64)*dqk * 4 bytes
+//     (scratch = 2 * B*H*L*dqk * 2 bytes + 3 * B*H*ceil(L/64)*dqk * 4 bytes + B*H*L * 4 bytes
 //     + B*H * 4 bytes, each rounded up to 256 bytes).
 //   - The first call on a device resolves the array's device address with
 //     cudaGetSymbolAddress (with that device current) and keeps it for the

@@ -59,10 +59,12 @@ constexpr float kMaxExp = 80.f;  // largest |exponent| of a chunk factor the str
 // Chunks of kc steps (128, or 64 for the pairs a 128-step pass flagged).  unsafe[b*heads + h]
 // is raised to level + 1 when an exponent is beyond +-kMaxExp or not finite; with level 1 only
 // the pairs flagged by the level-0 pass are processed (the rest of the grid returns at once).
+// fqg != NULL (per-head gates, raw-q mode): the per-step query factors e^(b_t - rho) go to
+// fqg[b*heads + h][t] instead of into a scaled copy of q; Qs is neither read nor written.
 template <typename T, int NJ>
 __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks,
                                                              float* decay, float* rho_e, float* nadd, int* unsafe,
-                                                             int kc, int level) {
+                                                             int kc, int level, float* fqg) {
   __shared__ float fq[kC], fk[kC], red[4];
   const int nch = (p.seqlen + kc - 1) / kc;
   const int c = blockIdx.x % nch;
@@ -103,6 +105,7 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
     if (!(fabsf(xq) <= kMaxExp) || !(fabsf(xk) <= kMaxExp)) unsafe[bh] = level + 1;
     fq[tid] = __expf(xq);
     fk[tid] = __expf(xk);
+    if (fqg && blockIdx.y == 0 && tid < tn) fqg[(int64_t)bh * p.seqlen + t0 + tid] = fq[tid];
     __syncthreads();
 #pragma unroll
     for (int u = 0; u < NJ; ++u) g[u] = gs;
@@ -129,16 +132,18 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
 #pragma unroll 4
   for (int t = 0; t < tn; ++t) {
     const int64_t tt = t0 + t;
-    float qv[NJ], kv[NJ];
+    float qv[NJ] = {}, kv[NJ];
     if (NJ == 2) {
-      const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(q + tt * p.tq + j0);
       const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162*>(k + tt * p.tk + j0);
-      const float2 qf = __bfloat1622float2(q2), kf = __bfloat1622float2(k2);
-      qv[0] = qf.x; qv[NJ - 1] = qf.y;
+      const float2 kf = __bfloat1622float2(k2);
       kv[0] = kf.x; kv[NJ - 1] = kf.y;
+      if (!fqg) {
+        const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(q + tt * p.tq + j0));
+        qv[0] = qf.x; qv[NJ - 1] = qf.y;
+      }
     } else {
-      qv[0] = to_f32<T>(q[tt * p.tq + j0]);
       kv[0] = to_f32<T>(k[tt * p.tk + j0]);
+      if (!fqg) qv[0] = to_f32<T>(q[tt * p.tq + j0]);
     }
     float qs[NJ], ks[NJ], kh[NJ];
 #pragma unroll
@@ -162,10 +167,10 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
     }
     const int64_t o = ob + tt * p.dqk + j0;
     if (NJ == 2) {
-      *reinterpret_cast<uint32_t*>(Qs + o) = pack2<__nv_bfloat16>(qs[0], qs[NJ - 1]);
+      if (!fqg) *reinterpret_cast<uint32_t*>(Qs + o) = pack2<__nv_bfloat16>(qs[0], qs[NJ - 1]);
       *reinterpret_cast<uint32_t*>(Ks + o) = pack2<__nv_bfloat16>(ks[0], ks[NJ - 1]);
     } else {
-      Qs[o] = __float2bfloat16_rn(qs[0]);
+      if (!fqg) Qs[o] = __float2bfloat16_rn(qs[0]);
       Ks[o] = __float2bfloat16_rn(ks[0]);
     }
   }
@@ -236,7 +241,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     mlstm_stream_kernel(const __grid_constant__ CUtensorMap tmQs, const __grid_constant__ CUtensorMap tmKs,
                         const __grid_constant__ CUtensorMap tmV,
                         const Params p, const float* __restrict__ decay, const float* __restrict__ rho_e,
-                        const float* __restrict__ nadd, const int* __restrict__ unsafe, int kc, int want) {
+                        const float* __restrict__ nadd, const int* __restrict__ unsafe, int kc, int want,
+                        const float* __restrict__ fqg) {
   // this launch runs the pairs whose range level is `want` (0: 128-step chunks, 1: 64-step
   // chunks); the others belong to another launch (uniform over the CTA)
   if (unsafe[blockIdx.z * p.heads + blockIdx.y] != want) return;
@@ -518,12 +524,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 
     // Output rows of chunk c: h_t = H / max(qn + rowsum, 1), this half's 32
     // columns, from H buffer c & 1 (the next chunk's Qs.Snap runs into the other).
+    // Raw-q mode (fqg): H, qn and the row sum were formed with q itself, so the
+    // step's query factor f_t scales them here: h_t = f_t H / max(f_t (qn + rowsum), 1).
     auto epilogue = [&](int c) {
       {
         const int tg = c * kc + row;
         const float* qnp = rowv + (c & 1) * 512;
         const float* denp = qnp + 256;
-        const float inv = 1.f / fmaxf(qnp[row] + qnp[kC + row] + denp[row] + denp[kC + row], 1.f);
+        const float fr = (fqg && row < kc && tg < p.seqlen) ? fqg[(int64_t)bh * p.seqlen + tg] : 1.f;
+        const float inv = fr / fmaxf(fr * (qnp[row] + qnp[kC + row] + denp[row] + denp[kC + row]), 1.f);
         float v[32];
         tc::tmem_ld32(tm + L::tH + (c & 1) * kDV + ch, v);
         tc::tmem_wait_ld();
@@ -683,7 +692,8 @@ size_t stream_workspace(const Params& p) {
   const size_t ops = (size_t)p.batch * p.heads * p.seqlen * p.dqk * 2;  // bf16 tensor
   const size_t vec = (size_t)p.batch * p.heads * nch * p.dqk * 4;
   const size_t flags = (size_t)p.batch * p.heads * 4;  // per (b, h): out of the kernel's range
-  return 2 * align256(ops) + 3 * align256(vec) + align256(flags);
+  const size_t fq = (size_t)p.batch * p.heads * p.seqlen * 4;  // per-step query factors (raw-q mode)
+  return 2 * align256(ops) + 3 * align256(vec) + align256(flags) + align256(fq);
 }
 
 bool stream_shape_ok(const Params& p) {
@@ -713,7 +723,14 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   float* rho_e = reinterpret_cast<float*>(ws + 2 * ops + vec);
   float* nadd = reinterpret_cast<float*>(ws + 2 * ops + 2 * vec);
   int* unsafe = reinterpret_cast<int*>(ws + 2 * ops + 3 * vec);
+  float* fq = reinterpret_cast<float*>(ws + 2 * ops + 3 * vec + align256((size_t)p.batch * p.heads * 4));
   HXM_CUDA_TRY(cudaMemsetAsync(unsafe, 0, sizeof(int) * (size_t)p.batch * p.heads, st));
+  // Per-head gates: the query factor is one scalar per step, so the tensor cores take q itself
+  // (TMA straight from the caller's tensor) and the epilogue applies the factor per row; the
+  // prescale pass then neither reads q nor writes a scaled copy of it.
+  const bool raw_q = p.gate_mode == 0 && reinterpret_cast<uintptr_t>(p.q) % 16 == 0 && p.tq % 8 == 0 &&
+                     p.sq[0] % 8 == 0 && p.sq[1] % 8 == 0;
+  float* fqg = raw_q ? fq : nullptr;
   // two channels per thread when q, k rows allow 4-byte loads
   const bool pair = p.tq % 2 == 0 && p.tk % 2 == 0 && p.sq[0] % 2 == 0 && p.sq[1] % 2 == 0 && p.sk[0] % 2 == 0 &&
                     p.sk[1] % 2 == 0 && reinterpret_cast<uintptr_t>(p.q) % 4 == 0 &&
@@ -722,10 +739,12 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
     const int nch = (p.seqlen + kc - 1) / kc;
     if (pair) {
       dim3 pg(p.batch * p.heads * nch, (DK + 255) / 256);
-      mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level);
+      mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level,
+                                                                  fqg);
     } else {
       dim3 pg(p.batch * p.heads * nch, (DK + 127) / 128);
-      mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level);
+      mlstm_prescale_kernel<__nv_bfloat16, 1><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level,
+                                                                  fqg);
     }
     return check_launch("hxm_mlstm_chunkwise_fwd (prescale)");
   };
@@ -740,10 +759,13 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
     const uint64_t dvd[4] = {(uint64_t)p.dv, (uint64_t)p.seqlen, (uint64_t)p.heads, (uint64_t)p.batch};
     const uint64_t sv[3] = {(uint64_t)p.tv * 2, (uint64_t)p.sv[1] * 2, (uint64_t)p.sv[0] * 2};
     hxm_status s;
-    if ((s = make_map_bf16_4d(&mq, Qs, dd, sd, "mlstm Qs", kc)) != HXM_OK) return s;
+    const uint64_t sq[3] = {(uint64_t)p.tq * 2, (uint64_t)p.sq[1] * 2, (uint64_t)p.sq[0] * 2};
+    if ((s = raw_q ? make_map_bf16_4d(&mq, p.q, dd, sq, "mlstm q", kc)
+                   : make_map_bf16_4d(&mq, Qs, dd, sd, "mlstm Qs", kc)) != HXM_OK)
+      return s;
     if ((s = make_map_bf16_4d(&mk, Ks, dd, sd, "mlstm Ks", kc)) != HXM_OK) return s;
     if ((s = make_map_bf16_4d(&mv, p.v, dvd, sv, "mlstm v", kc)) != HXM_OK) return s;
-    kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mv, p, decay, rho_e, nadd, unsafe, kc, want);
+    kern<<<grid, kStreamThreads, smem, st>>>(mq, mk, mv, p, decay, rho_e, nadd, unsafe, kc, want, fqg);
     return check_launch("hxm_mlstm_chunkwise_fwd (stream)");
   };
   // 128-step chunks for every pair in range; the pairs out of it are prescaled again in 64-step
