@@ -232,30 +232,25 @@ def _channel_chunk(gi, gf, chunk):
     """The longest chunk length <= chunk (halving, at least MIN_CHUNK) whose
     separable factors stay within e^+-MAX_EXP for these per-channel gates
     (B, H, L, Dqk): max over chunks and channels of |g| / 2 + max |log i|,
-    g the chunk's total log forget gate.  One host synchronization."""
+    g the chunk's total log forget gate.  Lengths are tried longest first, one
+    pass over the gates and one host synchronization each (usually just one)."""
     bsz, nh, L, dqk = gf.shape
-    cands = []
     c = int(chunk)
-    while c >= MIN_CHUNK:
-        cands.append(c)
-        c //= 2
-    if not cands:
+    if c < MIN_CHUNK:
         raise ValueError(f"mlstm_chunkwise_bwd: chunk {chunk} < {MIN_CHUNK}")
-    worst = []
-    for c in cands:
-        nch = (L + c - 1) // c
-        pad = nch * c - L
-        lf = torch.nn.functional.pad(gf, (0, 0, 0, pad)).view(bsz, nh, nch, c, dqk)
-        li = torch.nn.functional.pad(gi, (0, 0, 0, pad)).view(bsz, nh, nch, c, dqk)
-        x = -0.5 * lf.sum(3) + li.abs().amax(3)
-        worst.append(torch.nan_to_num(x, nan=float("inf")).amax())
-    worst = torch.stack(worst).cpu()
-    for c, w in zip(cands, worst.tolist()):
-        if w <= MAX_EXP:
+    worst = float("inf")
+    while c >= MIN_CHUNK:
+        nch, pad = (L + c - 1) // c, (-L) % c
+        lf = gf if not pad else torch.nn.functional.pad(gf, (0, 0, 0, pad))
+        li = gi if not pad else torch.nn.functional.pad(gi, (0, 0, 0, pad))
+        x = lf.reshape(bsz, nh, nch, c, dqk).sum(3).mul_(-0.5).add_(li.reshape(bsz, nh, nch, c, dqk).abs().amax(3))
+        worst = float(torch.nan_to_num(x.amax(), nan=float("inf")))
+        if worst <= MAX_EXP:
             return c
+        c //= 2
     raise RuntimeError(
-        f"mlstm_chunkwise_bwd: per-channel gates out of range for the chunkwise backward (a {cands[-1]}-step "
-        f"chunk needs e^{worst[-1].item():.1f} > e^{MAX_EXP:.0f}: forget gates near 0 or not finite)")
+        f"mlstm_chunkwise_bwd: per-channel gates out of range for the chunkwise backward (a {c * 2}-step "
+        f"chunk needs e^{worst:.1f} > e^{MAX_EXP:.0f}: forget gates near 0 or not finite)")
 
 
 def _bwd_channels(q, k, v, gi, gf, dh, c, st):
