@@ -45,17 +45,15 @@ HXM_DEV float fast_step(float r, float dl, float du, float u, const float* __res
   const float4* c4 = reinterpret_cast<const float4*>(bc + 16);
   float2 ya = make_float2(0.f, 0.f), yb = make_float2(0.f, 0.f);
   if (POW) {
-    // r^1..r^16 by a depth-4 product tree
+    // r^1..r^16: one FMUL and seven FMUL2 (pairs (r^2k+1, r^2k+2) from the pairs before)
     const float r2 = r * r;
-    const float r4 = r2 * r2;
-    const float r8 = r4 * r4;
     float2 pw[8];
     pw[0] = make_float2(r, r2);
-    pw[1] = make_float2(r2 * r, r4);
-    pw[2] = __fmul2_rn(f2(r4), pw[0]);
-    pw[3] = __fmul2_rn(f2(r4), pw[1]);
+    pw[1] = __fmul2_rn(f2(r2), pw[0]);   // r^3, r^4
+    pw[2] = __fmul2_rn(f2(pw[1].y), pw[0]);  // r^5, r^6
+    pw[3] = __fmul2_rn(f2(pw[1].y), pw[1]);  // r^7, r^8
 #pragma unroll
-    for (int q = 0; q < 4; ++q) pw[4 + q] = __fmul2_rn(f2(r8), pw[q]);
+    for (int q = 0; q < 4; ++q) pw[4 + q] = __fmul2_rn(f2(pw[3].y), pw[q]);  // r^9 .. r^16
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const float4 bb = b4[q], cc = c4[q];
