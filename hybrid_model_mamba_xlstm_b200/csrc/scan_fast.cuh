@@ -554,32 +554,46 @@ inline int fast_layout(const Params& p, size_t esize) {
 }
 inline bool fast_ok(const Params& p, size_t esize) { return fast_layout(p, esize) != 0; }
 
-template <typename T, int CH, bool CM>
-hxm_status pick_fast_modes(const Params& p, cudaStream_t stream) {
+template <typename T, int CH, int kT, bool CM>
+hxm_status pick_fast_modes_t(const Params& p, cudaStream_t stream) {
   const int zm = p.z ? p.z_mode : 0;
   if (p.softplus) {
-    if (zm == 2) return launch_fast<T, CH, 32, 2, true, CM>(p, stream);
-    if (zm == 1) return launch_fast<T, CH, 32, 1, true, CM>(p, stream);
-    return launch_fast<T, CH, 32, 0, true, CM>(p, stream);
+    if (zm == 2) return launch_fast<T, CH, kT, 2, true, CM>(p, stream);
+    if (zm == 1) return launch_fast<T, CH, kT, 1, true, CM>(p, stream);
+    return launch_fast<T, CH, kT, 0, true, CM>(p, stream);
   }
-  if (zm == 2) return launch_fast<T, CH, 32, 2, false, CM>(p, stream);
-  if (zm == 1) return launch_fast<T, CH, 32, 1, false, CM>(p, stream);
-  return launch_fast<T, CH, 32, 0, false, CM>(p, stream);
+  if (zm == 2) return launch_fast<T, CH, kT, 2, false, CM>(p, stream);
+  if (zm == 1) return launch_fast<T, CH, kT, 1, false, CM>(p, stream);
+  return launch_fast<T, CH, kT, 0, false, CM>(p, stream);
+}
+// Tile length: 32 steps in one pass; 16 with time segments (half the shared memory per CTA, so
+// more of the segments' CTAs are resident: one row x 32768 x 4096 in 16 segments 1.08 ms vs
+// 1.22 with 32-step tiles, four rows 3.47 vs 3.96; in one pass 32-step tiles are faster, 5.44
+// vs 5.60 ms for eight rows).  HXM_SCAN_FAST_T = 16 | 32 overrides.
+template <typename T, int CH, bool CM>
+hxm_status pick_fast_modes(const Params& p, cudaStream_t stream) {
+  int t = env_knob("HXM_SCAN_FAST_T");
+  if (t != 16 && t != 32) t = p.nseg > 1 ? 16 : 32;
+  if (t == 16) return pick_fast_modes_t<T, CH, 16, CM>(p, stream);  // segment lengths are multiples of 32
+  return pick_fast_modes_t<T, CH, 32, CM>(p, stream);
 }
 
-// Time segments for the fast kernel: a grid of fewer CTAs than SMs leaves most of the GPU idle
-// (one thread per channel; e.g. one batch row of 4096 channels = 64 CTAs on 148 SMs), so the
-// sequence is cut into 16 segments of >= 128 steps (a multiple of the 32-step tile) that run in
-// parallel after a state-only pass over the first 15 (about 40 % more work in all).  Measured on
-// B200 (one row x 32768 x 4096): 4.07 ms in one pass, 1.98 / 1.24 / 1.22 ms with 4 / 8 / 16
-// segments; with 2-4 segments the state pass itself is still occupancy-bound, and from about
-// one CTA per SM up (4 rows: 4.10 ms, 3.95 with 16; 8 rows: 5.44, 7.6) splitting does not pay.
+// Time segments for the fast kernel: a small grid leaves most of the GPU idle (one thread per
+// channel; e.g. one batch row of 4096 channels = 64 CTAs on 148 SMs), so the sequence is cut
+// into 16 segments of >= 128 steps (a multiple of 32) that run in parallel after a state-only
+// pass over the first 15 (about 40 % more work in all).  Measured on B200, x 32768 x 4096,
+// 16-step tiles: one row 4.09 ms in one pass -> 1.08 ms in 16 segments; four rows 4.13 -> 3.47;
+// eight rows (3.5 CTAs per SM) 5.44 in one pass against 6.74, so segments stop at 2.5 CTAs per
+// SM.  With fewer segments the state pass itself stays occupancy-bound (one row: 1.99 ms with 4).
+// Short sequences (the prefill's 256-2048-step pieces) run one pass: there the second launch and
+// the pipeline fill of short segments cost more than the idle SMs, which the other layers'
+// kernels of the wavefront occupy anyway (hybrid-350M prefill 31.1 ms one pass, 33.0 segmented).
 // HXM_SCAN_NSEG forces a count (1 = one pass).
 inline int fast_segments(const Params& p, int num_sms, int* seg_len) {
   const int ch = p.dim >= 64 ? 64 : 32;
   const int64_t ctas = (int64_t)((p.dim + ch - 1) / ch) * p.batch;
   int nseg = env_knob("HXM_SCAN_NSEG");
-  if (nseg <= 0) nseg = ctas < (int64_t)num_sms ? 16 : 1;
+  if (nseg <= 0) nseg = (ctas * 2 < (int64_t)num_sms * 5 && p.seqlen >= 8192) ? 16 : 1;
   nseg = max(1, min(nseg, 16));
   int len = 0;
   while (nseg > 1) {

@@ -127,19 +127,23 @@ def test_mlstm_backward_entries_validate_without_cuda():
 
 def test_scan_workspace_query_without_a_gpu():
     """hxm_selective_scan_workspace_size: the fast path's time segments need
-    scratch only when the grid is small (one batch row x 256 channels), none
-    for a large grid, fp32 or the ZOH rule, and bad args report 0."""
+    scratch only for a long sequence on a small grid (one batch row x 256
+    channels x 8192 steps), none for a short sequence, a large grid, fp32 or
+    the ZOH rule, and bad args report 0."""
     lib = _lib.lib()
     a = _lib.ScanArgs()
     a.struct_size = ct.sizeof(a)
-    a.batch, a.seqlen, a.dim, a.dstate, a.io_dtype = 1, 4096, 256, 16, _lib.HXM_BF16
+    a.batch, a.seqlen, a.dim, a.dstate, a.io_dtype = 1, 8192, 256, 16, _lib.HXM_BF16
     base = 1 << 20  # aligned placeholders: the query reads no memory
     for f in ("u", "delta", "B", "C", "y", "A"):
         setattr(a, f, base)
-    a.u_stride = a.delta_stride = a.y_stride = (256 * 4096, 1, 4096)  # time-major (b, t, d) view
-    a.B_stride = a.C_stride = (16 * 4096, 1, 4096)
+    a.u_stride = a.delta_stride = a.y_stride = (256 * 8192, 1, 8192)  # time-major (b, t, d) view
+    a.B_stride = a.C_stride = (16 * 8192, 1, 8192)
     small = lib.hxm_selective_scan_workspace_size(ct.byref(a))
     assert small > 0 and small % (17 * 4 * 256) == 0
+    a.seqlen = 4096  # short sequences run one pass
+    assert lib.hxm_selective_scan_workspace_size(ct.byref(a)) == 0
+    a.seqlen = 8192
     a.batch = 128  # 512 CTAs of 64 channels: over 2 per SM on 148 SMs
     assert lib.hxm_selective_scan_workspace_size(ct.byref(a)) == 0
     a.batch, a.discretization = 1, 1

@@ -245,7 +245,7 @@ def _fused(ops, inp, h0=None, nseg=None):
                 os.environ["HXM_SCAN_NSEG"] = old
 
 
-@pytest.mark.parametrize("L,nseg", [(1000, 2), (1000, 3), (4101, 16), (2048, None)])
+@pytest.mark.parametrize("L,nseg", [(1000, 2), (1000, 3), (4101, 16), (9000, None)])
 def test_time_segments_match_one_pass_and_oracle(ops, L, nseg):
     """A grid too small for the GPU (one batch row, 256 channels) runs as
     parallel time segments after a state-only pass: y and the final state
