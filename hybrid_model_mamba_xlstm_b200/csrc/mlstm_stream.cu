@@ -184,6 +184,108 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
   }
 }
 
+// Per-head gates with 16-byte-aligned k (and q) rows: the same outputs as the per-head branch
+// of mlstm_prescale_kernel, one block per (b, h, chunk) over every key channel, each thread
+// moving 8 channels (16 bytes) of one step per access — the other kernel's 4-byte accesses left
+// it latency-bound at about 1.5 TB/s.  Threads 0..kc-1 first scan the chunk's log forget gates
+// (one step each) into the per-step factors.
+constexpr int kPreThreads = 256;
+template <int DK>
+__global__ void __launch_bounds__(kPreThreads) mlstm_prescale_heads_kernel(
+    const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks, float* decay, float* rho_e, float* nadd, int* unsafe,
+    int kc, int level, float* fqg) {
+  constexpr int kOct = DK / 8;                 // 16-byte groups of a key row
+  constexpr int kRows = kPreThreads / kOct;    // steps handled in parallel
+  __shared__ float fq[kC], fk[kC], red[8];
+  __shared__ float ksum_s[kRows][DK];
+  const int nch = (p.seqlen + kc - 1) / kc;
+  const int c = blockIdx.x % nch;
+  const int bh = blockIdx.x / nch;
+  if (level > 0 && unsafe[bh] == 0) return;  // uniform over the block
+  const int b = bh / p.heads, h = bh % p.heads;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int t0 = c * kc, tn = min(kc, p.seqlen - t0);
+  const float* li = p.log_i + b * p.si[0] + h * p.si[1];
+  const float* lf = p.log_f + b * p.sf[0] + h * p.sf[1];
+  // per-step factors: thread t holds step t (warps 0-3), prefix sums by shuffles + 4 partials
+  float bt = 0.f, lit = 0.f;
+  if (tid < kC) {
+    bt = tid < tn ? lf[(int64_t)(t0 + tid) * p.tf] : 0.f;
+    lit = tid < tn ? li[(int64_t)(t0 + tid) * p.ti] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n = __shfl_up_sync(0xffffffffu, bt, o);
+      if (lane >= o) bt += n;
+    }
+    if (lane == 31) red[w] = bt;
+  }
+  __syncthreads();
+  float gs = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (tid < kC && i < w) bt += red[i];
+    gs += red[i];
+  }
+  const float rho = 0.5f * gs;
+  if (tid < kC) {
+    const float xq = bt - rho, xk = rho - bt + lit;
+    if (!(fabsf(xq) <= kMaxExp) || !(fabsf(xk) <= kMaxExp)) unsafe[bh] = level + 1;
+    fq[tid] = __expf(xq);
+    fk[tid] = __expf(xk);
+    if (fqg && tid < tn) fqg[(int64_t)bh * p.seqlen + t0 + tid] = fq[tid];
+  }
+  __syncthreads();
+  const float eh = __expf(rho);
+  const int oct = tid % kOct, r0 = tid / kOct, j0 = oct * 8;
+  const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q) + b * p.sq[0] + h * p.sq[1] + j0;
+  const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(p.k) + b * p.sk[0] + h * p.sk[1] + j0;
+  const int64_t ob = (int64_t)bh * p.seqlen * DK + j0;
+  float ks8[8] = {};
+#pragma unroll 4
+  for (int t = r0; t < tn; t += kRows) {
+    const int64_t tt = t0 + t;
+    const uint4 kw = *reinterpret_cast<const uint4*>(k + tt * p.tk);
+    const float e = fk[t];
+    const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kw);
+    uint4 ko;
+    uint32_t* kop = reinterpret_cast<uint32_t*>(&ko);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 kf = __bfloat1622float2(k2[i]);
+      const float a = kf.x * e, bb = kf.y * e;
+      ks8[2 * i] += a;
+      ks8[2 * i + 1] += bb;
+      kop[i] = pack2<__nv_bfloat16>(a, bb);
+    }
+    *reinterpret_cast<uint4*>(Ks + ob + tt * DK) = ko;
+    if (!fqg) {
+      const uint4 qw = *reinterpret_cast<const uint4*>(q + tt * p.tq);
+      const float f = fq[t];
+      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qw);
+      uint4 qo;
+      uint32_t* qop = reinterpret_cast<uint32_t*>(&qo);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 qf = __bfloat1622float2(q2[i]);
+        qop[i] = pack2<__nv_bfloat16>(qf.x * f, qf.y * f);
+      }
+      *reinterpret_cast<uint4*>(Qs + ob + tt * DK) = qo;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ksum_s[r0][j0 + i] = ks8[i];
+  __syncthreads();
+  for (int j = tid; j < DK; j += kPreThreads) {
+    float sum = 0.f;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) sum += ksum_s[r][j];
+    const int64_t vi = ((int64_t)bh * nch + c) * DK + j;
+    decay[vi] = __expf(gs);
+    rho_e[vi] = eh;
+    nadd[vi] = eh * sum;  // e^rho Ks^T 1: the normalizer's increment
+  }
+}
+
 // ------------------------------------------------------------ stream kernel --
 // Warps 0-7: element-wise work (warp w reads TMEM lanes 32 (w % 4) .., the two
 // warps of a lane quarter split the columns: half h = w / 4).  Warp 8: the
@@ -735,9 +837,17 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
   const bool pair = p.tq % 2 == 0 && p.tk % 2 == 0 && p.sq[0] % 2 == 0 && p.sq[1] % 2 == 0 && p.sk[0] % 2 == 0 &&
                     p.sk[1] % 2 == 0 && reinterpret_cast<uintptr_t>(p.q) % 4 == 0 &&
                     reinterpret_cast<uintptr_t>(p.k) % 4 == 0;
+  // per-head gates with 16-byte-aligned k (and, unless raw-q, q) rows: the vectorized pass
+  auto rows16 = [](const void* x, int64_t t, const int64_t* sx) {
+    return reinterpret_cast<uintptr_t>(x) % 16 == 0 && t % 8 == 0 && sx[0] % 8 == 0 && sx[1] % 8 == 0;
+  };
+  const bool heads16 = p.gate_mode == 0 && rows16(p.k, p.tk, p.sk) && (raw_q || rows16(p.q, p.tq, p.sq));
   auto prescale = [&](int kc, int level) {
     const int nch = (p.seqlen + kc - 1) / kc;
-    if (pair) {
+    if (heads16) {
+      mlstm_prescale_heads_kernel<DK><<<p.batch * p.heads * nch, kPreThreads, 0, st>>>(
+          p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level, fqg);
+    } else if (pair) {
       dim3 pg(p.batch * p.heads * nch, (DK + 255) / 256);
       mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level,
                                                                   fqg);
