@@ -305,22 +305,26 @@ def secondary_metrics(args, dev, world, rank):
                                       "kernel": "slstm_cluster_kernel<bf16, 256>"}
     del gates, Rw
     # mLSTM backward at the 350M model's mLSTM layer shape (batch 8, 4 heads x 512, seqlen 2048,
-    # per-channel gates): chunkwise, fp32 library chunk GEMMs around the hxm gate / chunk-scan kernels
-    from hybrid_model_mamba_xlstm_b200.kernels.tfla.tfla_bwd import mlstm_chunkwise_bwd
-    b, h, L, d, c = 8, 4, 2048, 512, 64
+    # per-channel gates): chunkwise, the chunk GEMMs on the tcgen05 chunk-GEMM kernel (bf16 high / low
+    # split operands) around the hxm gate / chunk-scan kernels; these gates' 128-step chunk factors
+    # exceed e^60, so the chunk that runs is 64 steps
+    from hybrid_model_mamba_xlstm_b200.kernels.tfla.tfla_bwd import _channel_chunk, mlstm_chunkwise_bwd
+    b, h, L, d = 8, 4, 2048, 512
     g.manual_seed(7 + rank)
     q, k, v, dh = (torch.randn(b, h, L, d, generator=g, device=dev).to(torch.bfloat16) for _ in range(4))
     q.mul_(d ** -0.5)
     li = torch.randn(b, h, L, d, generator=g, device=dev).mul_(0.5)
     lf = torch.nn.functional.logsigmoid(torch.randn(b, h, L, d, generator=g, device=dev))
-    ms = _time_cuda(lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh, chunk=c), min(steps, 3), 2, dev, world)
+    c = _channel_chunk(li, lf, 128)
+    ms = _time_cuda(lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh), min(steps, 3), 2, dev, world)
     w8 = (d + 1 + 7) // 8 * 8
     nch = L // c
-    fl = b * h * nch * (3 * 2 * c * c * d + 3 * 2 * c * c * w8 + 7 * 2 * c * d * w8)
+    fl = b * h * nch * (3 * 2 * c * c * d + 3 * 2 * c * c * w8 + 6 * 2 * c * d * w8)  # the 8 products that run
     out["mlstm_bwd_b8_h4_l2048_d512_channel_gates"] = {
         "metric": "mLSTM backward ms (chunk GEMM TFLOP/s alongside)", "value": ms, "unit": "ms",
         "gemm_tflops": world * fl / ms / 1e9, "scaling": "weak", "higher_is_better": False,
-        "kernels": "hxm mlstm_bwd prepare / normalizer / chunk_scan / chunk_dot / finalize + TF32 cuBLAS chunk GEMMs"}
+        "chunk": c, "kernels": "hxm mlstm_bwd prepare / normalizer / chunk_scan / chunk_dot / finalize + "
+        "chunk_gemm_kernel (tcgen05) chunk GEMMs"}
     del q, k, v, dh, li, lf
     # SSD backward at the SSD workload's shape (batch 8, 32 heads x 64, dstate 128, seqlen 4096)
     from hybrid_model_mamba_xlstm_b200.kernels.ssd import ssd_chunk_scan_bwd

@@ -159,6 +159,7 @@ class MlstmBwdArgs(ct.Structure):
         ("q_scaled", ct.c_void_p), ("k_scaled", ct.c_void_p),
         ("rho", ct.c_void_p), ("e_rho", ct.c_void_p), ("e_g", ct.c_void_p),
         ("q_decayed", ct.c_void_p), ("k_decayed", ct.c_void_p),
+        ("split_planes", ct.c_void_p),
         ("dq_scaled", ct.c_void_p), ("dk_scaled", ct.c_void_p),
         ("chunk_dg", ct.c_void_p),
         ("dq", ct.c_void_p), ("dk", ct.c_void_p), ("dlog_i", ct.c_void_p), ("dlog_f", ct.c_void_p),
@@ -174,6 +175,7 @@ class ChunkScanArgs(ct.Structure):
         ("x", ct.c_void_p), ("decay", ct.c_void_p),
         ("reverse", ct.c_int32),
         ("scale", ct.c_void_p), ("scaled", ct.c_void_p),
+        ("scaled_hi", ct.c_void_p), ("scaled_lo", ct.c_void_p),
     ]
 
 
@@ -216,6 +218,34 @@ class MlstmBwdNormArgs(ct.Structure):
         ("outputs", ct.c_void_p),
         ("dh", ct.c_void_p), ("dh_stride", _i64x3),
         ("out", ct.c_void_p),
+        ("out_hi", ct.c_void_p), ("out_lo", ct.c_void_p),
+    ]
+
+
+class GemmOperand(ct.Structure):
+    _fields_ = [
+        ("ptr", ct.c_void_p),
+        ("group_stride", ct.c_int64), ("row_stride", ct.c_int64),
+        ("rows", ct.c_int32), ("cols", ct.c_int32),
+        ("trans", ct.c_int32),
+    ]
+
+
+class ChunkGemmArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("groups", ct.c_int64),
+        ("m", ct.c_int32), ("n", ct.c_int32), ("nprod", ct.c_int32),
+        ("a", GemmOperand * 4), ("b", GemmOperand * 4),
+        ("alpha", ct.c_float),
+        ("mask", ct.c_int32),
+        ("decay", ct.c_void_p), ("decay_stride", ct.c_int64),
+        ("accumulate", ct.c_int32),
+        ("out", ct.c_void_p), ("out_group_stride", ct.c_int64), ("out_row_stride", ct.c_int64),
+        ("out_bf16", ct.c_void_p), ("outb_group_stride", ct.c_int64), ("outb_row_stride", ct.c_int64),
+        ("out_bf16_lo", ct.c_void_p),
+        ("error_flag", ct.c_void_p),
+        ("wait_limit_cycles", ct.c_int64),
     ]
 
 
@@ -235,6 +265,7 @@ SYMBOLS = {
     "hxm_chunk_state_scan": (ct.c_int, [ct.POINTER(ChunkScanArgs), ct.c_void_p]),
     "hxm_mlstm_bwd_normalizer": (ct.c_int, [ct.POINTER(MlstmBwdNormArgs), ct.c_void_p]),
     "hxm_chunk_state_dot": (ct.c_int, [ct.POINTER(ChunkDotArgs), ct.c_void_p]),
+    "hxm_chunk_gemm": (ct.c_int, [ct.POINTER(ChunkGemmArgs), ct.c_void_p]),
     "hxm_ssd_bwd_intra": (ct.c_int, [ct.POINTER(SsdBwdIntraArgs), ct.c_void_p]),
     "hxm_ssd_bwd_rows": (ct.c_int, [ct.POINTER(SsdBwdRowsArgs), ct.c_void_p]),
     "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),

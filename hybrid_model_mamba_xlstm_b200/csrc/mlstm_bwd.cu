@@ -40,6 +40,8 @@ struct Params {
   const float* log_f;
   int64_t sf[3];
   float *qs, *ks, *rho, *erho, *eg, *qd, *kd;
+  __nv_bfloat16* planes;  // optional: hi / lo planes of qs, ks, qd, kd (8 planes of `plane` elements)
+  int64_t plane;
   const float *dqs, *dks;
   const float* dg;
   float *dq, *dk, *dli, *dlf, *di;
@@ -76,11 +78,27 @@ __global__ void __launch_bounds__(128) prepare_kernel(const Params p) {
       qv = to_f32<T>(q[t * p.sq[2]]) * expf(bt - rho);
       kv = to_f32<T>(k[t * p.sk[2]]) * expf(li[t * p.si[2]] + rho - bt);
     }
-    p.qs[ro + (int64_t)s * p.dqk] = qv;
-    p.ks[ro + (int64_t)s * p.dqk] = kv;
-    if (p.qd) p.qd[ro + (int64_t)s * p.dqk] = qv * erho;  // q e^b
-    if (p.kd) p.kd[ro + (int64_t)s * p.dqk] = kv * erho;  // i k e^(g - b)
+    const int64_t o = ro + (int64_t)s * p.dqk;
+    if (p.qs) p.qs[o] = qv;
+    if (p.ks) p.ks[o] = kv;
+    if (p.qd) p.qd[o] = qv * erho;  // q e^b
+    if (p.kd) p.kd[o] = kv * erho;  // i k e^(g - b)
+    if (p.planes) {
+      const float vals[4] = {qv, kv, qv * erho, kv * erho};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const __nv_bfloat16 hi = __float2bfloat16_rn(vals[u]);
+        p.planes[(2 * u) * p.plane + o] = hi;
+        p.planes[(2 * u + 1) * p.plane + o] = __float2bfloat16_rn(vals[u] - __bfloat162float(hi));
+      }
+    }
   }
+}
+
+// q_scaled / k_scaled at element o: the fp32 arrays, or high + low from the split planes.
+HXM_DEV float scaled_at(const Params& p, const float* arr, int which, int64_t o) {
+  if (arr) return arr[o];
+  return __bfloat162float(p.planes[(2 * which) * p.plane + o]) + __bfloat162float(p.planes[(2 * which + 1) * p.plane + o]);
 }
 
 // grid (batch*heads*nch, ceil(dqk/128)), block 128: the chunk's steps in reverse,
@@ -108,7 +126,7 @@ __global__ void __launch_bounds__(128) finalize_kernel(const Params p) {
   for (int s = tn - 1; s >= 0; --s) {
     const int64_t t = t0 + s;
     const int64_t r = ro + (int64_t)s * p.dqk, o = oo + (int64_t)s * p.dqk;
-    const float P = p.dqs[r], R = p.dks[r], Qv = p.qs[r], Kv = p.ks[r];
+    const float P = p.dqs[r], R = p.dks[r], Qv = scaled_at(p, p.qs, 0, r), Kv = scaled_at(p, p.ks, 1, r);
     p.dq[o] = expf(bt - rho) * P;
     const float ek = expf(rho - bt) * R;  // dL/d(i k)
     const float iv = expf(li[t * p.si[2]]);
@@ -128,6 +146,7 @@ __global__ void __launch_bounds__(128) finalize_kernel(const Params p) {
 // keeps 8 reads in flight instead of one load-store round trip per chunk
 __global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, const float* __restrict__ decay,
                                                          const float* __restrict__ scale, float* __restrict__ scaled,
+                                                         __nv_bfloat16* __restrict__ shi, __nv_bfloat16* __restrict__ slo,
                                                          int64_t groups, int nch, int rows, int cols, int reverse) {
   constexpr int kB = 8;
   const int64_t rc = (int64_t)rows * cols;
@@ -155,7 +174,14 @@ __global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, 
       if (it < nch) {
         const int kc = reverse ? nch - 1 - it : it;
         xp[kc * rc] = s;
-        if (op) op[kc * rc] = sp[(int64_t)kc * rows] * s;
+        const float f = sp ? sp[(int64_t)kc * rows] : 1.f;
+        if (op) op[kc * rc] = f * s;
+        if (shi) {
+          const int64_t o = grp * nch * rc + w + kc * rc;
+          const __nv_bfloat16 hi = __float2bfloat16_rn(f * s);
+          shi[o] = hi;
+          if (slo) slo[o] = __float2bfloat16_rn(f * s - __bfloat162float(hi));
+        }
         s = dc[u] * s + y[u];
       }
     }
@@ -166,6 +192,7 @@ __global__ void __launch_bounds__(256) chunk_scan_kernel(float* __restrict__ x, 
 // 16-byte aligned): 16-byte loads and stores, one decay load per 4 columns.
 __global__ void __launch_bounds__(256) chunk_scan4_kernel(float4* __restrict__ x, const float* __restrict__ decay,
                                                           const float* __restrict__ scale, float4* __restrict__ scaled,
+                                                          uint2* __restrict__ shi, uint2* __restrict__ slo,
                                                           int64_t groups, int nch, int rows, int cols4, int reverse) {
   constexpr int kB = 8;
   const int64_t rc4 = (int64_t)rows * cols4;
@@ -194,9 +221,19 @@ __global__ void __launch_bounds__(256) chunk_scan4_kernel(float4* __restrict__ x
       if (it < nch) {
         const int kc = reverse ? nch - 1 - it : it;
         xp[kc * rc4] = s;
-        if (op) {
-          const float f = sp[(int64_t)kc * rows];
-          op[kc * rc4] = make_float4(f * s.x, f * s.y, f * s.z, f * s.w);
+        const float f = sp ? sp[(int64_t)kc * rows] : 1.f;
+        const float4 fs = make_float4(f * s.x, f * s.y, f * s.z, f * s.w);
+        if (op) op[kc * rc4] = fs;
+        if (shi) {  // 4 bf16 high parts (and low parts) in 8 bytes each
+          const int64_t o = grp * nch * rc4 + w + kc * rc4;
+          const __nv_bfloat162 h01 = __floats2bfloat162_rn(fs.x, fs.y), h23 = __floats2bfloat162_rn(fs.z, fs.w);
+          shi[o] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+          if (slo) {
+            const float2 b01 = __bfloat1622float2(h01), b23 = __bfloat1622float2(h23);
+            const __nv_bfloat162 l01 = __floats2bfloat162_rn(fs.x - b01.x, fs.y - b01.y);
+            const __nv_bfloat162 l23 = __floats2bfloat162_rn(fs.z - b23.x, fs.w - b23.y);
+            slo[o] = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+          }
         }
         s = make_float4(fmaf(dc[u], s.x, y[u].x), fmaf(dc[u], s.y, y[u].y), fmaf(dc[u], s.z, y[u].z),
                         fmaf(dc[u], s.w, y[u].w));
@@ -214,7 +251,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) normalizer_kernel(const float* __restrict__ numa, const T* __restrict__ dh,
                                                          int64_t sb, int64_t sh, int64_t st, int heads, int seqlen,
                                                          int lp, int dv, int w, int normalize, int64_t rows,
-                                                         float* __restrict__ dna) {
+                                                         float* __restrict__ dna, __nv_bfloat16* __restrict__ dhi,
+                                                         __nv_bfloat16* __restrict__ dlo) {
   const int lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x * 8ll + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -222,9 +260,17 @@ __global__ void __launch_bounds__(256) normalizer_kernel(const float* __restrict
   const int64_t bh = row / lp;
   const int b = (int)(bh / heads), h = (int)(bh % heads);
   const float* nrow = numa + row * w;
-  float* orow = dna + row * w;
+  // one output element: fp32 and / or the bf16 high / low parts
+  auto put = [&](int e, float x) {
+    if (dna) dna[row * w + e] = x;
+    if (dhi) {
+      const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+      dhi[row * w + e] = hi;
+      if (dlo) dlo[row * w + e] = __float2bfloat16_rn(x - __bfloat162float(hi));
+    }
+  };
   if (t >= seqlen) {
-    for (int e = lane; e < w; e += 32) orow[e] = 0.f;
+    for (int e = lane; e < w; e += 32) put(e, 0.f);
     return;
   }
   const T* drow = dh + b * sb + h * sh + (int64_t)t * st;
@@ -233,13 +279,12 @@ __global__ void __launch_bounds__(256) normalizer_kernel(const float* __restrict
   float part = 0.f;
   for (int e = lane; e < dv; e += 32) {
     const float g = to_f32<T>(drow[e]) * inv;
-    orow[e] = g;
-    part = fmaf(g, nrow[e], part);
+    put(e, g);
+    if (normalize) part = fmaf(g, nrow[e], part);  // (outputs is unread, and may be NULL, without it)
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-  for (int e = dv + lane; e < w; e += 32)
-    orow[e] = (e == dv && normalize && den >= 1.f) ? -part * inv : 0.f;
+  for (int e = dv + lane; e < w; e += 32) put(e, (e == dv && normalize && den >= 1.f) ? -part * inv : 0.f);
 }
 
 // out[g, k, r] = sum_c adj[g, k, r, c] * state[g, k + 1, r, c]  (0 for the last
@@ -297,9 +342,12 @@ static hxm_status fill(const hxm_mlstm_bwd_args* a, Params& p, const char* who) 
   }
   p.qs = a->q_scaled; p.ks = a->k_scaled; p.rho = a->rho; p.erho = a->e_rho; p.eg = a->e_g;
   p.qd = a->q_decayed; p.kd = a->k_decayed;
+  p.planes = static_cast<__nv_bfloat16*>(a->split_planes);
+  p.plane = (int64_t)p.batch * p.heads * p.nch * p.chunk * p.dqk;
   p.dqs = a->dq_scaled; p.dks = a->dk_scaled; p.dg = a->chunk_dg;
   p.dq = a->dq; p.dk = a->dk; p.dli = a->dlog_i; p.dlf = a->dlog_f; p.di = a->d_i;
-  HXM_REQUIRE(p.log_i && p.log_f && p.qs && p.ks && p.rho, "%s: NULL gate or chunk-operand pointer", who);
+  HXM_REQUIRE(p.log_i && p.log_f && ((p.qs && p.ks) || p.planes) && p.rho, "%s: NULL gate or chunk-operand pointer",
+              who);
   return HXM_OK;
 }
 
@@ -350,17 +398,21 @@ extern "C" hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* a, void* s
   if (a->groups == 0 || a->nchunks == 0) return HXM_OK;
   HXM_REQUIRE(a->x != nullptr, "hxm_chunk_state_scan: x is NULL");
   HXM_REQUIRE(!a->scaled || a->scale, "hxm_chunk_state_scan: scaled output needs scale");
+  HXM_REQUIRE(!a->scaled_lo || a->scaled_hi, "hxm_chunk_state_scan: scaled_lo needs scaled_hi");
   const int64_t n = a->groups * a->rows * (int64_t)a->cols;
   HXM_REQUIRE(n / 256 < (int64_t)0x7fffffff, "hxm_chunk_state_scan: too many elements (%lld)", (long long)n);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (a->cols % 4 == 0 && reinterpret_cast<uintptr_t>(a->x) % 16 == 0 &&
-      reinterpret_cast<uintptr_t>(a->scaled) % 16 == 0)
+      reinterpret_cast<uintptr_t>(a->scaled) % 16 == 0 && reinterpret_cast<uintptr_t>(a->scaled_hi) % 8 == 0 &&
+      reinterpret_cast<uintptr_t>(a->scaled_lo) % 8 == 0)
     mlstm_bwd::chunk_scan4_kernel<<<mlstm_bwd::grid_each(n / 4), 256, 0, st>>>(
-        reinterpret_cast<float4*>(a->x), a->decay, a->scale, reinterpret_cast<float4*>(a->scaled), a->groups,
-        a->nchunks, a->rows, a->cols / 4, a->reverse ? 1 : 0);
+        reinterpret_cast<float4*>(a->x), a->decay, a->scale, reinterpret_cast<float4*>(a->scaled),
+        static_cast<uint2*>(a->scaled_hi), static_cast<uint2*>(a->scaled_lo), a->groups, a->nchunks, a->rows,
+        a->cols / 4, a->reverse ? 1 : 0);
   else
     mlstm_bwd::chunk_scan_kernel<<<mlstm_bwd::grid_each(n), 256, 0, st>>>(
-        a->x, a->decay, a->scale, a->scaled, a->groups, a->nchunks, a->rows, a->cols, a->reverse ? 1 : 0);
+        a->x, a->decay, a->scale, a->scaled, static_cast<__nv_bfloat16*>(a->scaled_hi),
+        static_cast<__nv_bfloat16*>(a->scaled_lo), a->groups, a->nchunks, a->rows, a->cols, a->reverse ? 1 : 0);
   return check_launch("hxm_chunk_state_scan");
 }
 
@@ -377,18 +429,21 @@ extern "C" hxm_status hxm_mlstm_bwd_normalizer(const hxm_mlstm_bwd_norm_args* a,
   HXM_REQUIRE(a->io_dtype == HXM_F32 || a->io_dtype == HXM_BF16, "hxm_mlstm_bwd_normalizer: io_dtype must be f32 or bf16");
   const int64_t rows = (int64_t)a->batch * a->heads * a->padded_len;
   if (rows == 0) return HXM_OK;
-  HXM_REQUIRE(a->out && a->dh && (a->outputs || !a->normalize), "hxm_mlstm_bwd_normalizer: NULL pointer");
+  HXM_REQUIRE((a->out || a->out_hi) && a->dh && (a->outputs || !a->normalize), "hxm_mlstm_bwd_normalizer: NULL pointer");
+  HXM_REQUIRE(!a->out_lo || a->out_hi, "hxm_mlstm_bwd_normalizer: out_lo needs out_hi");
   const unsigned grid = (unsigned)((rows + 7) / 8);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const float* numa = a->normalize ? a->outputs : a->out;  // unread without the normalizer
+  const float* numa = a->outputs;  // unread without the normalizer
+  auto* ohi = static_cast<__nv_bfloat16*>(a->out_hi);
+  auto* olo = static_cast<__nv_bfloat16*>(a->out_lo);
   if (a->io_dtype == HXM_F32)
     mlstm_bwd::normalizer_kernel<float><<<grid, 256, 0, st>>>(
         numa, static_cast<const float*>(a->dh), a->dh_stride[0], a->dh_stride[1], a->dh_stride[2], a->heads,
-        a->seqlen, a->padded_len, a->dv, a->width, a->normalize ? 1 : 0, rows, a->out);
+        a->seqlen, a->padded_len, a->dv, a->width, a->normalize ? 1 : 0, rows, a->out, ohi, olo);
   else
     mlstm_bwd::normalizer_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
         numa, static_cast<const __nv_bfloat16*>(a->dh), a->dh_stride[0], a->dh_stride[1], a->dh_stride[2], a->heads,
-        a->seqlen, a->padded_len, a->dv, a->width, a->normalize ? 1 : 0, rows, a->out);
+        a->seqlen, a->padded_len, a->dv, a->width, a->normalize ? 1 : 0, rows, a->out, ohi, olo);
   return check_launch("hxm_mlstm_bwd_normalizer");
 }
 

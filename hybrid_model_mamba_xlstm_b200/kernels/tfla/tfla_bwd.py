@@ -29,7 +29,10 @@ terms, W = dL/dS * S, with W's diagonal (the largest entries under strong
 decay, present in both sums) left out exactly instead of cancelled in
 rounding.
 
-The chunk GEMMs are batched cuBLAS calls (torch.matmul; fp32, or TF32 for bf16 inputs); the gate
+For bf16 inputs the chunk GEMMs are this library's tcgen05 kernel
+(hxm_chunk_gemm, tfla_bwd_tc.py); otherwise (fp32 inputs, and per-channel
+gates too strong for 128-step chunks) they are batched cuBLAS calls
+(torch.matmul; fp32, or TF32 when asked for); the gate
 scaling, the two chunk-level recurrences and the gate gradients (a suffix sum
 over the whole sequence) are this library's kernels.  Memory: two fp32 state
 arrays of (B, H, L / chunk, dqk, w), w = dv + 1 rounded up to 8.
@@ -179,7 +182,8 @@ def _bwd_heads(q, k, v, li, lf, dout, c, normalize, per_channel_out, st):
     return un(dQ), un(dk), un(dVa)[..., :dv], dli, dlf, di
 
 
-def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grads: str = "auto", tf32=None):
+def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grads: str = "auto", tf32=None,
+                        tensor_cores=None):
     """Gradients of h = mLSTM(q, k, v, log_i, log_f) from a zero state.
 
     q, k (B, H, L, Dqk), v (B, H, L, Dv) bf16 or fp32; log_i, log_f fp32 per
@@ -191,6 +195,11 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     chunk GEMMs on TF32 tensor cores (default: when q is bf16, whose own
     rounding is coarser; relative gradient error ~1e-3 — except per-channel
     gates strong enough to shorten the chunk, which run fp32) or in full fp32.
+    tensor_cores: run the chunk GEMMs as hxm_chunk_gemm (tcgen05, bf16
+    operands, 128-step chunks; the default for bf16 inputs) instead of the
+    library GEMMs above (tf32 then does not apply); per-channel gates too
+    strong for 128-step chunk factors take the library path with a shorter
+    chunk.
     """
     who = "mlstm_chunkwise_bwd"
     dev = require_cuda(q, k, v, log_i, log_f, dh, who=who)
@@ -218,6 +227,19 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
         gi, gf = unit(gi), unit(gf)
     c = int(chunk)
     st = stream_of(dev)
+    use_tc = (io == torch.bfloat16) if tensor_cores is None else bool(tensor_cores)
+    if use_tc and io != torch.bfloat16:
+        raise ValueError(f"{who}: tensor_cores needs bf16 q, k (got {io})")
+    if use_tc:
+        v = unit(v if v.dtype == io else v.to(io))
+        from . import tfla_bwd_tc as tc
+        if gate_mode == 0:
+            return tc.bwd_heads_tc(q, k, v, gi, gf, dh, per_channel_out, st, _chunk_dg)
+        cc = _channel_chunk(gi, gf, tc.TC_CHUNKS[0])
+        if cc in tc.TC_CHUNKS:
+            return tc.bwd_channels_tc(q, k, v, gi, gf, dh, cc, st, _chunk_dg)
+        # gates too strong for 64-step chunk factors: the library path below, whose shorter
+        # chunk runs fp32 GEMMs
     if gate_mode == 0:
         with _gemm_precision(io == torch.bfloat16 if tf32 is None else tf32):
             return _bwd_heads(q, k, v, gi, gf, dh, c, True, per_channel_out, st)

@@ -236,6 +236,13 @@ typedef struct hxm_mlstm_bwd_args {
   float* rho; float* e_rho; float* e_g;
   float* q_decayed; float* k_decayed;  /* prepare, optional (NULL = skip):    */
                             /* q e^b and k e^(log_i + g - b), layout of q_scaled */
+  void* split_planes;       /* optional bf16 (8, b, h, nchunks*chunk, dqk):   */
+                            /* high / low parts (x = hi + lo to ~2^-16) of    */
+                            /* q_scaled, k_scaled, q_decayed, k_decayed in    */
+                            /* that order, the tensor-core chunk GEMMs'       */
+                            /* operands.  prepare writes them (q_scaled ...   */
+                            /* may then be NULL); finalize reads q_scaled,    */
+                            /* k_scaled from them when those are NULL.        */
   const float* dq_scaled; const float* dk_scaled;
   const float* chunk_dg;
   float* dq; float* dk; float* dlog_i; float* dlog_f;
@@ -254,7 +261,9 @@ hxm_status hxm_mlstm_bwd_finalize(const hxm_mlstm_bwd_args* args, void* stream);
 /* seqlen).  outputs, out: (b, h, padded_len, width) fp32 dense; dh          */
 /* (b, h, t) element strides, dense dv, io dtype.  Replaces the clamp branch */
 /* of the reference's recompute-under-autograd backward (tfla_interface.py: */
-/* 52-81 differentiating :133-137).                                          */
+/* 52-81 differentiating :133-137).  out_hi / out_lo (optional, bf16,       */
+/* layout of out): the same rows as a split operand (hi + lo to ~2^-16);     */
+/* out may then be NULL.                                                     */
 typedef struct hxm_mlstm_bwd_norm_args {
   size_t struct_size;
   int32_t batch, heads, seqlen, padded_len, dv, width;
@@ -263,6 +272,7 @@ typedef struct hxm_mlstm_bwd_norm_args {
   const float* outputs;
   const void* dh; int64_t dh_stride[3];
   float* out;
+  void* out_hi; void* out_lo;
 } hxm_mlstm_bwd_norm_args;
 
 hxm_status hxm_mlstm_bwd_normalizer(const hxm_mlstm_bwd_norm_args* args, void* stream);
@@ -286,6 +296,9 @@ typedef struct hxm_chunk_scan_args {
   int32_t reverse;
   const float* scale;       /* (groups, nchunks, rows) or NULL              */
   float* scaled;            /* layout of x, or NULL: scale[k, r] * x_out[k] */
+  void* scaled_hi;          /* optional bf16, layout of x: the scaled copy  */
+  void* scaled_lo;          /* (x_out when scale is NULL) as high / low     */
+                            /* parts, a split operand (hi + lo to ~2^-16)   */
 } hxm_chunk_scan_args;
 
 hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* args, void* stream);
@@ -306,6 +319,44 @@ typedef struct hxm_chunk_dot_args {
 } hxm_chunk_dot_args;
 
 hxm_status hxm_chunk_state_dot(const hxm_chunk_dot_args* args, void* stream);
+
+/* Batched chunk GEMM on the tensor cores (tcgen05; bf16 operands, fp32      */
+/* accumulation) for the chunk contractions of the chunkwise backward passes */
+/* (the intra-chunk products of the reference's recompute-under-autograd    */
+/* backward, tfla_interface.py:52-81 differentiating :113-137).  Per group g:*/
+/*   D = alpha * sum_{p < nprod} op(A_p) op(B_p)    (m x n, nprod 1 to 4)     */
+/* then: mask = 1 zeroes D[r, c] for c > r (a chunk's causal step matrix);   */
+/* with `decay`, D[r, c] *= exp(decay[g, r] - decay[g, c]) for c <= r;       */
+/* accumulate = 1 adds the fp32 output's current value; D is stored to `out` */
+/* (fp32) and / or `out_bf16` (with out_bf16_lo, also the low part: high +  */
+/* low carry ~16 mantissa bits, a split operand for the next products).  Each operand is a stored bf16 matrix per     */
+/* group (rows x cols, unit column stride, 16-byte aligned base, row and     */
+/* group strides multiples of 8 elements); trans = 1 uses it transposed, so  */
+/* op(A) is m x K and op(B) K x n.  groups <= 65535.                         */
+typedef struct hxm_gemm_operand {
+  const void* ptr;
+  int64_t group_stride, row_stride;   /* elements                            */
+  int32_t rows, cols;                 /* stored extent per group             */
+  int32_t trans;
+} hxm_gemm_operand;
+
+typedef struct hxm_chunk_gemm_args {
+  size_t struct_size;
+  int64_t groups;
+  int32_t m, n, nprod;
+  hxm_gemm_operand a[4], b[4];
+  float alpha;
+  int32_t mask;
+  const float* decay; int64_t decay_stride;   /* (groups, m) per step, or NULL */
+  int32_t accumulate;
+  float* out;     int64_t out_group_stride, out_row_stride;
+  void* out_bf16; int64_t outb_group_stride, outb_row_stride;
+  void* out_bf16_lo;          /* or NULL: bf16(D - bf16(D)), strides of out_bf16 */
+  int32_t* error_flag;        /* set to 1 when a bounded wait gave up, or NULL */
+  int64_t wait_limit_cycles;  /* 0: default (~2 s)                           */
+} hxm_chunk_gemm_args;
+
+hxm_status hxm_chunk_gemm(const hxm_chunk_gemm_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* 3. Mamba-2 SSD chunked scan (ngroups = 1)                                  */

@@ -147,7 +147,7 @@ def main(argv=None):
         li = torch.randn(B, H, L, D, generator=g, device=dev).mul_(0.5)
         lf = torch.nn.functional.logsigmoid(torch.randn(B, H, L, D, generator=g, device=dev))
         fn = lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh)  # noqa: E731
-        extra = {"chunk": 64}
+        extra = {"chunk": 128, "path": "tcgen05 chunk GEMMs"}
     elif a.case == "scan_bwd":
         # selective-scan backward (softplus(delta + bias), y * silu(z)), bf16 inputs, fp32 gradients
         from hybrid_model_mamba_xlstm_b200.kernels.selective_scan.scan_interface import selective_scan_bwd

@@ -44,7 +44,8 @@ def test_struct_sizes_match_header_layout():
                     (_lib.ScanBwdArgs, "hxm_selective_scan_bwd"), (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_prepare"),
                     (_lib.MlstmBwdArgs, "hxm_mlstm_bwd_finalize"), (_lib.ChunkScanArgs, "hxm_chunk_state_scan"),
                     (_lib.MlstmBwdNormArgs, "hxm_mlstm_bwd_normalizer"), (_lib.ChunkDotArgs, "hxm_chunk_state_dot"),
-                    (_lib.SsdBwdIntraArgs, "hxm_ssd_bwd_intra"), (_lib.SsdBwdRowsArgs, "hxm_ssd_bwd_rows")]:
+                    (_lib.SsdBwdIntraArgs, "hxm_ssd_bwd_intra"), (_lib.SsdBwdRowsArgs, "hxm_ssd_bwd_rows"),
+                    (_lib.ChunkGemmArgs, "hxm_chunk_gemm")]:
         a = cls()
         a.struct_size = ct.sizeof(a) + 8
         st = getattr(_lib.lib(), fn)(ct.byref(a), None)
@@ -123,6 +124,36 @@ def test_mlstm_backward_entries_validate_without_cuda():
     assert lib.hxm_mlstm_bwd_normalizer(ct.byref(n), None) == _lib.HXM_EBADARG
     n.width, n.batch = 8, 0
     assert lib.hxm_mlstm_bwd_normalizer(ct.byref(n), None) == _lib.HXM_OK
+
+
+def test_chunk_gemm_validates_without_cuda():
+    """hxm_chunk_gemm: the ctypes layout matches (the size check passes and the
+    next check fires), shape mismatches and misaligned strides are rejected,
+    empty work is a no-op success."""
+    lib = _lib.lib()
+    a = _lib.ChunkGemmArgs()
+    a.struct_size = ct.sizeof(a)
+    a.groups, a.m, a.n, a.nprod = 2, 128, 64, 5
+    assert lib.hxm_chunk_gemm(ct.byref(a), None) == _lib.HXM_EBADARG
+    assert b"nprod" in lib.hxm_last_error_string()
+    a.nprod = 1
+    assert lib.hxm_chunk_gemm(ct.byref(a), None) == _lib.HXM_EBADARG  # no output
+    assert b"no output" in lib.hxm_last_error_string()
+    a.out = 4096
+    for o, (rows, cols, trans) in ((a.a[0], (128, 96, 0)), (a.b[0], (96, 64, 0))):
+        o.ptr, o.rows, o.cols, o.trans = 1 << 20, rows, cols, trans
+        o.row_stride, o.group_stride = cols, rows * cols
+    a.b[0].rows = 80  # inner lengths 96 vs 80
+    assert lib.hxm_chunk_gemm(ct.byref(a), None) == _lib.HXM_EBADARG
+    assert b"inner lengths" in lib.hxm_last_error_string()
+    a.b[0].rows, a.a[0].row_stride = 96, 100  # row stride not a multiple of 8 elements
+    assert lib.hxm_chunk_gemm(ct.byref(a), None) == _lib.HXM_EBADARG
+    assert b"multiples of 8" in lib.hxm_last_error_string()
+    a.a[0].row_stride, a.a[0].trans = 96, 1  # op(A) = 96 x 128: m mismatch
+    assert lib.hxm_chunk_gemm(ct.byref(a), None) == _lib.HXM_EBADARG
+    assert b"rows for m" in lib.hxm_last_error_string()
+    a.a[0].trans, a.groups = 0, 0
+    assert lib.hxm_chunk_gemm(ct.byref(a), None) == _lib.HXM_OK
 
 
 def test_scan_workspace_query_without_a_gpu():

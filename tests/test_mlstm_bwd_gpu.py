@@ -5,7 +5,7 @@ tfla_forward_pytorch (:84-139) under autograd; the check here does the same in
 float64 on the same inputs and compares every gradient of apply_tfla (q, k, v,
 i_gate, f_gate).  Tolerances (normwise relative error): fp32 I/O 1e-4 (fp32
 chunk GEMMs and state); bf16 I/O 2e-2 against the loop on the bf16-rounded
-inputs (TF32 chunk GEMMs, ~1e-3).
+inputs (tcgen05 chunk GEMMs on bf16 operands, ~2e-3).
 """
 import ctypes as ct
 import math
@@ -112,6 +112,40 @@ def test_apply_tfla_grads_bf16_channel_gates(T):
     assert got[0].dtype == torch.bfloat16
     for name, a, b in zip(("dq", "dk", "dv", "di", "df"), got, want):
         assert rel_err(_d64(a).numpy(), b.numpy()) < TOL16, name
+
+
+@pytest.mark.parametrize("per_channel,d,dv,L", [(True, 128, 128, 300), (False, 128, 96, 260), (False, 256, 256, 200),
+                                                 (True, 512, 512, 150)])
+def test_tensor_core_backward_bf16_vs_loop(T, per_channel, d, dv, L):
+    """bf16 inputs take the tcgen05 chunk-GEMM backward (128-step chunks):
+    every gradient of apply_tfla against float64 autograd of the loop, per-
+    channel gates and per-head gates (expanded views), ragged lengths."""
+    q, k, v, ig, fg, dh = _case((1, 2, L, d), dv, per_channel, 1.0, seed=d + L, dtype=torch.bfloat16)
+    out, got = _grads_gpu(T, q, k, v, ig, fg, dh, expand=not per_channel)
+    _, want = _grads_ref(q, k, v, ig, fg, dh, expand=not per_channel)
+    for name, a, b in zip(("dq", "dk", "dv", "di", "df"), got, want):
+        assert torch.isfinite(a).all(), name
+        assert rel_err(_d64(a).numpy(), b.numpy()) < TOL16, name
+
+
+@pytest.mark.parametrize("gates", ["head", "channel"])
+def test_tensor_core_backward_matches_library_path(T, gates):
+    """The tcgen05 backward (bf16 high / low split operands) against the fp32
+    library-GEMM path on the same bf16 inputs (batch 2, 4 heads, 700 steps,
+    d 256): every output, per-head gate gradients through the W = dL/dS * S
+    identity included, within 1e-3 (TF32 GEMMs: ~1e-3 against float64)."""
+    bsz, nh, L, d = 2, 4, 700, 256
+    g = torch.Generator().manual_seed(77)
+    q = (torch.randn(bsz, nh, L, d, generator=g) / 16).to("cuda", torch.bfloat16)
+    k, v, dh = (torch.randn(bsz, nh, L, d, generator=g).to("cuda", torch.bfloat16) for _ in range(3))
+    gs = (bsz, nh, L) if gates == "head" else (bsz, nh, L, d)
+    li = (torch.randn(*gs, generator=g) * 0.5).cuda()
+    lf = torch.nn.functional.logsigmoid(torch.randn(*gs, generator=g) + 2.0).cuda()
+    tc = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, tensor_cores=True)
+    lib = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, tensor_cores=False, tf32=False)
+    for name, a, b in zip(("dq", "dk", "dv", "dlog_i", "dlog_f", "di"), tc, lib):
+        assert a.shape == b.shape, name
+        assert rel_err(_d64(a).numpy(), _d64(b).numpy()) < 1e-3, name
 
 
 def test_log_gate_entry_per_head_sums(T):
