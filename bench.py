@@ -317,14 +317,21 @@ def secondary_metrics(args, dev, world, rank):
     lf = torch.nn.functional.logsigmoid(torch.randn(b, h, L, d, generator=g, device=dev))
     c = _channel_chunk(li, lf, 128)
     ms = _time_cuda(lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh), min(steps, 3), 2, dev, world)
+    ms_fast = _time_cuda(lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh, precise=False), min(steps, 3), 2, dev,
+                         world)
+    ms_lib = _time_cuda(lambda: mlstm_chunkwise_bwd(q, k, v, li, lf, dh, chunk=64, tensor_cores=False, tf32=True),
+                        min(steps, 3), 2, dev, world)
     w8 = (d + 1 + 7) // 8 * 8
     nch = L // c
     fl = b * h * nch * (3 * 2 * c * c * d + 3 * 2 * c * c * w8 + 6 * 2 * c * d * w8)  # the 8 products that run
     out["mlstm_bwd_b8_h4_l2048_d512_channel_gates"] = {
         "metric": "mLSTM backward ms (chunk GEMM TFLOP/s alongside)", "value": ms, "unit": "ms",
         "gemm_tflops": world * fl / ms / 1e9, "scaling": "weak", "higher_is_better": False,
-        "chunk": c, "kernels": "hxm mlstm_bwd prepare / normalizer / chunk_scan / chunk_dot / finalize + "
-        "chunk_gemm_kernel (tcgen05) chunk GEMMs"}
+        "chunk": c, "precise_false_ms": ms_fast, "library_tf32_ms": ms_lib,
+        "kernels": "hxm mlstm_bwd prepare / normalizer / chunk_scan / chunk_dot / finalize + "
+        "chunk_gemm_kernel (tcgen05, bf16 high / low split operands) chunk GEMMs",
+        "accuracy": "default (precise): every fp32 operand split (~3e-5 vs float64); precise=False: gate-scaled "
+                    "q, k split (~1e-3); library_tf32: cuBLAS TF32 chunk GEMMs at chunk 64 (~1e-3)"}
     del q, k, v, dh, li, lf
     # SSD backward at the SSD workload's shape (batch 8, 32 heads x 64, dstate 128, seqlen 4096)
     from hybrid_model_mamba_xlstm_b200.kernels.ssd import ssd_chunk_scan_bwd

@@ -183,7 +183,7 @@ def _bwd_heads(q, k, v, li, lf, dout, c, normalize, per_channel_out, st):
 
 
 def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grads: str = "auto", tf32=None,
-                        tensor_cores=None):
+                        tensor_cores=None, precise: bool = True):
     """Gradients of h = mLSTM(q, k, v, log_i, log_f) from a zero state.
 
     q, k (B, H, L, Dqk), v (B, H, L, Dv) bf16 or fp32; log_i, log_f fp32 per
@@ -195,11 +195,16 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
     chunk GEMMs on TF32 tensor cores (default: when q is bf16, whose own
     rounding is coarser; relative gradient error ~1e-3 — except per-channel
     gates strong enough to shorten the chunk, which run fp32) or in full fp32.
-    tensor_cores: run the chunk GEMMs as hxm_chunk_gemm (tcgen05, bf16
-    operands, 128-step chunks; the default for bf16 inputs) instead of the
-    library GEMMs above (tf32 then does not apply); per-channel gates too
-    strong for 128-step chunk factors take the library path with a shorter
-    chunk.
+    tensor_cores: run the chunk GEMMs as hxm_chunk_gemm (tcgen05, bf16 high /
+    low split operands, 128-step chunks, 64 for per-channel gates whose
+    128-step factors leave e^+-MAX_EXP; the default for bf16 inputs) instead of
+    the library GEMMs above (tf32 then does not apply); gates too strong for
+    64-step chunk factors take the library path with a shorter chunk.
+    precise (default): every fp32 operand is split (gradient error ~3e-5
+    against float64); precise=False splits only the gate-scaled q, k (~1e-3,
+    as TF32 GEMMs, up to ~3e-2 for per-channel gates with long memory, where
+    the normalizer's dq = (C dh - n (dh . h)) / den cancels) in up to 0.7x
+    the time.
     """
     who = "mlstm_chunkwise_bwd"
     dev = require_cuda(q, k, v, log_i, log_f, dh, who=who)
@@ -234,10 +239,10 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
         v = unit(v if v.dtype == io else v.to(io))
         from . import tfla_bwd_tc as tc
         if gate_mode == 0:
-            return tc.bwd_heads_tc(q, k, v, gi, gf, dh, per_channel_out, st, _chunk_dg)
+            return tc.bwd_heads_tc(q, k, v, gi, gf, dh, per_channel_out, st, _chunk_dg, split_states=precise)
         cc = _channel_chunk(gi, gf, tc.TC_CHUNKS[0])
         if cc in tc.TC_CHUNKS:
-            return tc.bwd_channels_tc(q, k, v, gi, gf, dh, cc, st, _chunk_dg)
+            return tc.bwd_channels_tc(q, k, v, gi, gf, dh, cc, st, _chunk_dg, split_states=precise)
         # gates too strong for 64-step chunk factors: the library path below, whose shorter
         # chunk runs fp32 GEMMs
     if gate_mode == 0:

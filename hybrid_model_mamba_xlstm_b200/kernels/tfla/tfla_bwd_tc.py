@@ -16,14 +16,16 @@ Precision: the backward is a difference of large terms (the normalizer's
 dq = (C dh - n (dh . h)) / den, the gate identity q . dq - k . dk), so
 operand rounding is amplified: plain bf16 operands (unit roundoff 2^-8) give
 gradient errors of 1-7 % where the fp32 path gives 1e-6 and TF32 (2^-11)
-1e-3.  So every operand that is not already exact in bf16 is split into a
-bf16 high part and the bf16 rounding of its remainder (x = hi + lo to about
-2^-16), and a product of two split operands is formed as
-hi*hi + hi*lo + lo*hi (lo*lo is below the fp32 accumulation error): more
-accurate than TF32, at three bf16 MMAs per product.  The GEMM epilogue writes
-its results directly as split operands.  bf16 inputs q, k, v are exact (no
-split); the gate-scaled q, k, the states, adjoints and normalizer gradients
-are split.
+1e-3.  Measured on B200, the error comes first from the gate-scaled q and k
+(q e^(b - rho), i k e^(...)): rounding them alone gives 1-2 %.  So those are
+split into a bf16 high part and the bf16 rounding of the remainder
+(x = hi + lo to about 2^-16), and a product with a split operand is formed as
+hi*hi + hi*lo + lo*hi (lo*lo is below the fp32 accumulation error): gradient
+error ~1e-3 against float64, as with TF32 GEMMs.  With split_states (the
+callers' precise=True) the states, adjoints and normalizer gradients are split
+too: ~3e-5.  The producing kernels (hxm_mlstm_bwd_prepare, the chunk-state
+scan, the normalizer, the GEMM epilogue) write the split operands directly.
+bf16 inputs q, k, v are exact and never split.
 
 Chunk length: 128 steps (one 128-row MMA tile per chunk); per-channel gates
 whose 128-step chunk factors would leave e^+-MAX_EXP use 64 steps (rows 64..127
@@ -40,11 +42,12 @@ from ... import _lib
 from .._common import dtype_code, ptr
 from ..chunk_gemm import chunk_gemm
 
-MAX_GROUPS = 65535  # groups per hxm_chunk_gemm launch (grid z)
+MAX_GROUPS = 1 << 24  # groups per hxm_chunk_gemm launch
 MAX_PROD = 4        # products per launch
 # Split the states, adjoints and normalizer gradients too (not only the gate-scaled q, k):
-# gradient error ~3e-5 instead of ~2e-3 against float64 (TF32 GEMMs: ~2e-3).
-SPLIT_STATES = True
+# gradient error ~3e-5 instead of ~1e-3 against float64 (TF32 GEMMs: ~1e-3), at up to 1.4x
+# the time.  The callers' precise=False leaves them as bf16 high parts.
+SPLIT_STATES = False
 
 __all__ = ["bwd_channels_tc", "bwd_heads_tc", "TC_CHUNKS"]
 TC_CHUNKS = (128, 64)

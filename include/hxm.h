@@ -332,7 +332,9 @@ hxm_status hxm_chunk_state_dot(const hxm_chunk_dot_args* args, void* stream);
 /* low carry ~16 mantissa bits, a split operand for the next products).  Each operand is a stored bf16 matrix per     */
 /* group (rows x cols, unit column stride, 16-byte aligned base, row and     */
 /* group strides multiples of 8 elements); trans = 1 uses it transposed, so  */
-/* op(A) is m x K and op(B) K x n.  groups <= 65535.                         */
+/* op(A) is m x K and op(B) K x n.  groups <= 2^24.  Outputs: unit column   */
+/* stride, fp32 16-byte aligned / bf16 8-byte aligned, row and group strides */
+/* multiples of 4 elements.                                                  */
 typedef struct hxm_gemm_operand {
   const void* ptr;
   int64_t group_stride, row_stride;   /* elements                            */

@@ -129,11 +129,15 @@ def test_tensor_core_backward_bf16_vs_loop(T, per_channel, d, dv, L):
 
 
 @pytest.mark.parametrize("gates", ["head", "channel"])
-def test_tensor_core_backward_matches_library_path(T, gates):
+@pytest.mark.parametrize("precise", [False, True])
+def test_tensor_core_backward_matches_library_path(T, gates, precise):
     """The tcgen05 backward (bf16 high / low split operands) against the fp32
     library-GEMM path on the same bf16 inputs (batch 2, 4 heads, 700 steps,
     d 256): every output, per-head gate gradients through the W = dL/dS * S
-    identity included, within 1e-3 (TF32 GEMMs: ~1e-3 against float64)."""
+    identity included.  precise (the default, all fp32 operands split):
+    within 2e-4; precise=False (the gate-scaled q, k split): within 5e-2
+    (2.9e-2 measured for the per-channel gates, whose normalizer gradient
+    cancels over the long memory of these gates)."""
     bsz, nh, L, d = 2, 4, 700, 256
     g = torch.Generator().manual_seed(77)
     q = (torch.randn(bsz, nh, L, d, generator=g) / 16).to("cuda", torch.bfloat16)
@@ -141,11 +145,11 @@ def test_tensor_core_backward_matches_library_path(T, gates):
     gs = (bsz, nh, L) if gates == "head" else (bsz, nh, L, d)
     li = (torch.randn(*gs, generator=g) * 0.5).cuda()
     lf = torch.nn.functional.logsigmoid(torch.randn(*gs, generator=g) + 2.0).cuda()
-    tc = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, tensor_cores=True)
+    tc = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, tensor_cores=True, precise=precise)
     lib = T.mlstm_chunkwise_bwd(q, k, v, li, lf, dh, tensor_cores=False, tf32=False)
     for name, a, b in zip(("dq", "dk", "dv", "dlog_i", "dlog_f", "di"), tc, lib):
         assert a.shape == b.shape, name
-        assert rel_err(_d64(a).numpy(), _d64(b).numpy()) < 1e-3, name
+        assert rel_err(_d64(a).numpy(), _d64(b).numpy()) < (2e-4 if precise else 5e-2), name
 
 
 def test_log_gate_entry_per_head_sums(T):
