@@ -176,6 +176,9 @@ class ChunkScanArgs(ct.Structure):
         ("reverse", ct.c_int32),
         ("scale", ct.c_void_p), ("scaled", ct.c_void_p),
         ("scaled_hi", ct.c_void_p), ("scaled_lo", ct.c_void_p),
+        ("skip_state", ct.c_int32),
+        ("dot_hi", ct.c_void_p), ("dot_lo", ct.c_void_p),
+        ("dot_scale", ct.c_void_p), ("dot_out", ct.c_void_p),
     ]
 
 

@@ -242,6 +242,96 @@ __global__ void __launch_bounds__(256) chunk_scan4_kernel(float4* __restrict__ x
   }
 }
 
+// Row mode of the chunk-state scan (tensor-core backward): one warp per (group, row),
+// lane l owning the float4 columns l, l + 32, ... (NV of them).  Per chunk in order (or
+// reversed): the exclusive state s is written as the bf16 high / low split of scale * s
+// (and to x_out unless skipped), with dot the inner product of s with the next chunk's
+// state read back from the state scan's split copy (divided by its scale), reduced over
+// the warp; then s = decay * s + x_in[chunk].  The next chunk's increments are loaded
+// while the current one is written.
+template <int NV>
+__global__ void __launch_bounds__(256) chunk_scan_rows_kernel(
+    const float* __restrict__ x_in, float* __restrict__ x_out, const float* __restrict__ decay,
+    const float* __restrict__ scale, uint2* __restrict__ shi, uint2* __restrict__ slo, const uint2* __restrict__ dhi,
+    const uint2* __restrict__ dlo, const float* __restrict__ dscale, float* __restrict__ dout, int64_t groups, int nch,
+    int rows, int cols, int reverse) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wr = blockIdx.x * 8ll + (threadIdx.x >> 5);
+  if (wr >= groups * rows) return;
+  const int64_t grp = wr / rows;
+  const int r = (int)(wr % rows);
+  const int cols4 = cols >> 2;
+  const int64_t rc4 = (int64_t)rows * cols4;                 // float4s per chunk
+  const int64_t base4 = grp * nch * rc4 + (int64_t)r * cols4;  // (grp, chunk 0, r, 0)
+  const int64_t vbase = grp * nch * rows + r;
+  const float4* xin4 = reinterpret_cast<const float4*>(x_in);
+  float4* xout4 = reinterpret_cast<float4*>(x_out);
+  float4 s[NV], y[NV];
+  auto load = [&](int it, float4 (&dst)[NV]) {
+    const int kc = reverse ? nch - 1 - it : it;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int c4 = lane + 32 * v;
+      dst[v] = (it < nch && c4 < cols4) ? xin4[base4 + kc * rc4 + c4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+#pragma unroll
+  for (int v = 0; v < NV; ++v) s[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+  load(0, y);
+  for (int it = 0; it < nch; ++it) {
+    const int kc = reverse ? nch - 1 - it : it;
+    float4 yn[NV];
+    load(it + 1, yn);
+    const float dc = decay ? decay[vbase + (int64_t)kc * rows] : 1.f;
+    const float f = scale ? scale[vbase + (int64_t)kc * rows] : 1.f;
+    const int64_t o4 = base4 + kc * rc4;
+    const int kn = kc + 1;
+    const bool dot = dout && kn < nch;
+    const float inv = (dot && dscale) ? 1.f / dscale[vbase + (int64_t)kn * rows] : 1.f;
+    float part = 0.f;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int c4 = lane + 32 * v;
+      if (c4 >= cols4) continue;
+      const float4 z = s[v];
+      if (xout4) xout4[o4 + c4] = z;
+      const float4 fs = make_float4(f * z.x, f * z.y, f * z.z, f * z.w);
+      const __nv_bfloat162 h01 = __floats2bfloat162_rn(fs.x, fs.y), h23 = __floats2bfloat162_rn(fs.z, fs.w);
+      shi[o4 + c4] = make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+      if (slo) {
+        const float2 b01 = __bfloat1622float2(h01), b23 = __bfloat1622float2(h23);
+        const __nv_bfloat162 l01 = __floats2bfloat162_rn(fs.x - b01.x, fs.y - b01.y);
+        const __nv_bfloat162 l23 = __floats2bfloat162_rn(fs.z - b23.x, fs.w - b23.y);
+        slo[o4 + c4] = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+      }
+      if (dot) {  // the next chunk's state: (hi + lo) / its scale
+        const int64_t n4 = base4 + kn * rc4 + c4;
+        const uint2 hh = dhi[n4];
+        float2 a01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hh.x));
+        float2 a23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&hh.y));
+        if (dlo) {
+          const uint2 ll = dlo[n4];
+          const float2 c01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ll.x));
+          const float2 c23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ll.y));
+          a01.x += c01.x; a01.y += c01.y; a23.x += c23.x; a23.y += c23.y;
+        }
+        part = fmaf(z.x, a01.x, fmaf(z.y, a01.y, fmaf(z.z, a23.x, fmaf(z.w, a23.y, part))));
+      }
+    }
+    if (dout) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+      if (lane == 0) dout[vbase + (int64_t)kc * rows] = dot ? part * inv : 0.f;
+    }
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      s[v] = make_float4(fmaf(dc, s[v].x, y[v].x), fmaf(dc, s[v].y, y[v].y), fmaf(dc, s[v].z, y[v].z),
+                         fmaf(dc, s[v].w, y[v].w));
+      y[v] = yn[v];
+    }
+  }
+}
+
 // Output-side gradients of one chunk row t (one warp per row): from the chunk
 // outputs [num | den] (width w, fp32) and dh, with D = max(den, 1),
 //   dnum = dh / D,  dden = -[den >= 1] (dnum . num) / D     (normalize)
@@ -402,6 +492,36 @@ extern "C" hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* a, void* s
   const int64_t n = a->groups * a->rows * (int64_t)a->cols;
   HXM_REQUIRE(n / 256 < (int64_t)0x7fffffff, "hxm_chunk_state_scan: too many elements (%lld)", (long long)n);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool row_ok = a->scaled_hi && !a->scaled && a->cols % 4 == 0 && a->cols <= 640 &&
+                      reinterpret_cast<uintptr_t>(a->x) % 16 == 0 && reinterpret_cast<uintptr_t>(a->scaled_hi) % 8 == 0 &&
+                      reinterpret_cast<uintptr_t>(a->scaled_lo) % 8 == 0 &&
+                      reinterpret_cast<uintptr_t>(a->dot_hi) % 8 == 0 && reinterpret_cast<uintptr_t>(a->dot_lo) % 8 == 0;
+  HXM_REQUIRE_SUPPORTED(row_ok || (!a->dot_out && !a->skip_state),
+                        "hxm_chunk_state_scan: dot_out / skip_state need the row mode (scaled_hi without scaled, "
+                        "cols %% 4 == 0 and <= 640, aligned pointers)");
+  HXM_REQUIRE(!a->dot_out || a->dot_hi, "hxm_chunk_state_scan: dot_out needs dot_hi");
+  if (row_ok) {
+    const int nv = (a->cols / 4 + 31) / 32;
+    const unsigned grid = (unsigned)((a->groups * a->rows + 7) / 8);
+    float* xo = a->skip_state ? nullptr : a->x;
+    auto* hi = static_cast<uint2*>(a->scaled_hi);
+    auto* lo = static_cast<uint2*>(a->scaled_lo);
+    auto* dh = static_cast<const uint2*>(a->dot_hi);
+    auto* dl = static_cast<const uint2*>(a->dot_lo);
+#define HXM_ROWS(NV)                                                                                           \
+  mlstm_bwd::chunk_scan_rows_kernel<NV><<<grid, 256, 0, st>>>(a->x, xo, a->decay, a->scale, hi, lo, dh, dl,    \
+                                                              a->dot_scale, a->dot_out, a->groups, a->nchunks, \
+                                                              a->rows, a->cols, a->reverse ? 1 : 0)
+    switch (nv) {
+      case 1: HXM_ROWS(1); break;
+      case 2: HXM_ROWS(2); break;
+      case 3: HXM_ROWS(3); break;
+      case 4: HXM_ROWS(4); break;
+      default: HXM_ROWS(5); break;
+    }
+#undef HXM_ROWS
+    return check_launch("hxm_chunk_state_scan (rows)");
+  }
   if (a->cols % 4 == 0 && reinterpret_cast<uintptr_t>(a->x) % 16 == 0 &&
       reinterpret_cast<uintptr_t>(a->scaled) % 16 == 0 && reinterpret_cast<uintptr_t>(a->scaled_hi) % 8 == 0 &&
       reinterpret_cast<uintptr_t>(a->scaled_lo) % 8 == 0)

@@ -239,10 +239,10 @@ def mlstm_chunkwise_bwd(q, k, v, log_i, log_f, dh, *, chunk: int = 64, gate_grad
         v = unit(v if v.dtype == io else v.to(io))
         from . import tfla_bwd_tc as tc
         if gate_mode == 0:
-            return tc.bwd_heads_tc(q, k, v, gi, gf, dh, per_channel_out, st, _chunk_dg, split_states=precise)
+            return tc.bwd_heads_tc(q, k, v, gi, gf, dh, per_channel_out, st, split_states=precise)
         cc = _channel_chunk(gi, gf, tc.TC_CHUNKS[0])
         if cc in tc.TC_CHUNKS:
-            return tc.bwd_channels_tc(q, k, v, gi, gf, dh, cc, st, _chunk_dg, split_states=precise)
+            return tc.bwd_channels_tc(q, k, v, gi, gf, dh, cc, st, split_states=precise)
         # gates too strong for 64-step chunk factors: the library path below, whose shorter
         # chunk runs fp32 GEMMs
     if gate_mode == 0:

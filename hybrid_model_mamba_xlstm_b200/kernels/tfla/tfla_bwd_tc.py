@@ -142,16 +142,23 @@ def _view(op, *shape):
     return Split(op.hi.view(*shape), op.lo.view(*shape)) if isinstance(op, Split) else op.view(*shape)
 
 
-def _scan_split(x, decay, reverse, st, scale=None, split_lo=True):
-    """hxm_chunk_state_scan in place on x (groups, nch, rows, cols) fp32, with the
-    (scaled) result written as bf16 high / low parts; returns the operand."""
+def _scan_split(x, decay, reverse, st, scale=None, split_lo=True, dot=None):
+    """Row mode of hxm_chunk_state_scan over the increments x (groups, nch, rows,
+    cols) fp32, read only: the exclusive (scaled) states as a bf16 split operand
+    (the low part only when split_lo).  dot = (the state scan's Split, its scale or
+    None): also the chunk gradients <x_out[k], state[k + 1]> (groups, nch, rows).
+    Returns (operand, dg or None)."""
     hi, lo = _bf16_pair(x.shape, x.device, split_lo)
     a = _lib.ChunkScanArgs()
     a.groups, a.nchunks, a.rows, a.cols = x.shape[0] * x.shape[1], x.shape[2], x.shape[3], x.shape[4]
     a.x, a.decay, a.reverse = ptr(x), ptr(decay), int(reverse)
-    a.scale, a.scaled_hi, a.scaled_lo = ptr(scale), ptr(hi), ptr(lo)
+    a.scale, a.scaled_hi, a.scaled_lo, a.skip_state = ptr(scale), ptr(hi), ptr(lo), 1
+    dg = None
+    if dot is not None:
+        dg = torch.empty(x.shape[:4], device=x.device, dtype=torch.float32)
+        a.dot_hi, a.dot_lo, a.dot_scale, a.dot_out = ptr(dot[0].hi), ptr(dot[0].lo), ptr(dot[1]), ptr(dg)
     _lib.call("hxm_chunk_state_scan", a, st)
-    return _as_operand(hi, lo)
+    return _as_operand(hi, lo), dg
 
 
 def _normalizer(numa, dh, lp, w, st, want_fp32, split_lo=True):
@@ -173,12 +180,12 @@ def _normalizer(numa, dh, lp, w, st, want_fp32, split_lo=True):
     return out, _as_operand(hi, lo)
 
 
-def bwd_channels_tc(q, k, v, gi, gf, dh, c, st, chunk_dg, split_states=None):
+def bwd_channels_tc(q, k, v, gi, gf, dh, c, st, split_states=None):
     """Per-channel gates (B, H, L, Dqk): the separable chunk scaling of
     hxm_mlstm_bwd_prepare with c-step chunks; prepare writes the gate-scaled q, k
     straight as split operands, the chunk-state scans and the normalizer write
-    theirs (split_states=False keeps only their high parts).  chunk_dg is
-    tfla_bwd's wrapper of hxm_chunk_state_dot."""
+    theirs (split_states=False keeps only their high parts as GEMM operands);
+    the adjoint scan also forms the chunk gradients dg = <Y_k, X_{k+1}>."""
     split_states = SPLIT_STATES if split_states is None else split_states
     bsz, nh, L, dqk = q.shape
     dv = v.shape[-1]
@@ -207,7 +214,9 @@ def bwd_channels_tc(q, k, v, gi, gf, dh, c, st, chunk_dg, split_states=None):
     # states entering each chunk X (fp32, for dg) and their e^rho row-scaled copy Xs
     X = torch.empty(bsz, nh, nch, dqk, w, **f32)
     mm([(Kr, 1, Vc, 0)], dqk, w, out=X.view(G, dqk, w))
-    Xs = _view(_scan_split(X, eg, False, st, erho, split_states), G, dqk, w)
+    Xs5, _ = _scan_split(X, eg, False, st, erho)  # (the low part always: the chunk gradients read it)
+    del X
+    Xs = _view(Xs5, G, dqk, w) if split_states else Xs5.hi.view(G, dqk, w)
     _, S = mm([(Qc, 0, Kc, 1)], c, c, want_split=True, mask=True)
     numa = torch.empty(bsz, nh, nch, c, w, **f32)
     mm([(Qc, 0, Xs, 0), (S, 0, Vc, 0)], c, w, out=numa.view(G, c, w))
@@ -216,7 +225,9 @@ def bwd_channels_tc(q, k, v, gi, gf, dh, c, st, chunk_dg, split_states=None):
     # adjoints leaving each chunk Y and their e^rho row-scaled copy Ys
     Y = torch.empty(bsz, nh, nch, dqk, w, **f32)
     mm([(Qr, 1, dNa, 0)], dqk, w, out=Y.view(G, dqk, w))
-    Ys = _view(_scan_split(Y, eg, True, st, erho, split_states), G, dqk, w)
+    Ys, dg = _scan_split(Y, eg, True, st, erho, split_states, dot=(Xs5, erho))
+    del Y
+    Ys = _view(Ys, G, dqk, w)
     _, dS = mm([(dNa, 0, Vc, 1)], c, c, want_split=True, mask=True)
     dQs = torch.empty(bsz, nh, Lp, dqk, **f32)
     mm([(dS, 0, Kc, 0), (dNa, 0, Xs, 1)], c, dqk, out=dQs.view(G, c, dqk))
@@ -226,7 +237,6 @@ def bwd_channels_tc(q, k, v, gi, gf, dh, c, st, chunk_dg, split_states=None):
     mm([(S, 1, dNa[:, :, :dv], 0), (Kc, 0, Ys[:, :, :dv], 0)], c, dv, out=dVo.view(G, c, dv))
     del S, dS, Xs, Ys, dNa, Qc, Kc, Qr, Kr
 
-    dg = chunk_dg(Y, X, (-1,))
     dq, dk, dli, dlf, di = (torch.empty(bsz, nh, L, dqk, **f32) for _ in range(5))
     a.dq_scaled, a.dk_scaled, a.chunk_dg = ptr(dQs), ptr(dKs), ptr(dg)
     a.dq, a.dk, a.dlog_i, a.dlog_f, a.d_i = ptr(dq), ptr(dk), ptr(dli), ptr(dlf), ptr(di)
@@ -235,7 +245,7 @@ def bwd_channels_tc(q, k, v, gi, gf, dh, c, st, chunk_dg, split_states=None):
     return dq, dk, dVo[:, :, :L], dli, dlf, di
 
 
-def bwd_heads_tc(q, k, v, li, lf, dout, per_channel_out, st, chunk_dg, c=128, split_states=None):
+def bwd_heads_tc(q, k, v, li, lf, dout, per_channel_out, st, c=128, split_states=None):
     """Per-head gates (B, H, L): the exact decay-matrix form of tfla_bwd's
     _bwd_heads: S = causal(Q (i k)^T) * e^(b_t - b_s) and dS = dL/dS *
     e^(b_t - b_s) straight from the GEMM epilogue, the inter-chunk factors
@@ -275,7 +285,9 @@ def bwd_heads_tc(q, k, v, li, lf, dout, per_channel_out, st, chunk_dg, c=128, sp
 
     X = torch.empty(bsz, nh, nch, dqk, w, **f32)        # increments -> states entering each chunk
     mm([(Kds, 1, Vc, 0)], dqk, w, out=X.view(G, dqk, w))
-    Xs = _view(_scan_split(X, eg, False, st, None, split_states), G, dqk, w)
+    Xs5, _ = _scan_split(X, eg, False, st)  # (the low part always: the chunk gradients read it)
+    del X
+    Xs = _view(Xs5, G, dqk, w) if split_states else Xs5.hi.view(G, dqk, w)
     S, Ssp = mm([(Qb, 0, Kps, 1)], c, c, out=torch.empty(G, c, c, **f32), want_split=True, mask=True, decay=bdec)
     QX, _ = mm([(Qes, 0, Xs, 0)], c, w)
     numa = QX.clone()
@@ -285,7 +297,9 @@ def bwd_heads_tc(q, k, v, li, lf, dout, per_channel_out, st, chunk_dg, c=128, sp
     del numa
     Y = torch.empty(bsz, nh, nch, dqk, w, **f32)        # increments -> adjoints leaving each chunk
     mm([(Qes, 1, dNs, 0)], dqk, w, out=Y.view(G, dqk, w))
-    Ys = _view(_scan_split(Y, eg, True, st, None, split_states), G, dqk, w)
+    Ys, dg = _scan_split(Y, eg, True, st, None, split_states, dot=(Xs5, None))
+    del Y
+    Ys = _view(Ys, G, dqk, w)
     dSf, _ = mm([(dNs, 0, Vc, 1)], c, c, out=torch.empty(G, c, c, **f32), mask=True)  # dL/dS (causal part)
     _, dSs = mm([(dNs, 0, Vc, 1)], c, c, want_split=True, mask=True, decay=bdec)        # dL/d(Q (i k)^T)
     VY, _ = mm([(Vc, 0, Ys, 1)], c, dqk)
@@ -305,14 +319,13 @@ def bwd_heads_tc(q, k, v, li, lf, dout, per_channel_out, st, chunk_dg, c=128, sp
     di_c = K * dKp                                       # per channel: k . d(i k)
     if per_channel_out:  # the gate identity per channel, in-chunk part
         db = Q * dQ - Kp * dKp
-        dg = chunk_dg(Y, X, (-1,))
     else:
         di_c = di_c.sum(-1)
         W = dSf.mul_(S).view(bsz, nh, nch, c, c)
         W.diagonal(dim1=-2, dim2=-1).zero_()  # in both sums: its net term is exactly zero
         dNa5, QX5 = dNa.view(bsz, nh, nch, c, w), QX.view(bsz, nh, nch, c, w)
         db = W.sum(-1) - W.sum(-2) + (dNa5 * QX5).sum(-1) - (Kd * VY).sum(-1)
-        dg = chunk_dg(Y, X, (-1, -2))
+        dg = dg.sum(-1)
     dlf = db.flip(3).cumsum(3).flip(3).add_(dg.unsqueeze(3))
     dlf = dlf.reshape(bsz, nh, Lp, *dlf.shape[4:])[:, :, :L]
     dlf[:, :, 0] = 0.0  # f at the first step multiplies the zero state

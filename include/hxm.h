@@ -299,6 +299,17 @@ typedef struct hxm_chunk_scan_args {
   void* scaled_hi;          /* optional bf16, layout of x: the scaled copy  */
   void* scaled_lo;          /* (x_out when scale is NULL) as high / low     */
                             /* parts, a split operand (hi + lo to ~2^-16)   */
+  /* Row mode (scaled_hi set, rows x cols with cols % 4 == 0 and cols <= 640): */
+  /* with skip_state = 1, x is only read (the exclusive states go to the       */
+  /* split copy alone); with dot_out, also                                     */
+  /*   dot_out[g, k, r] = sum_c x_out[g, k, r, c] * (dot_hi + dot_lo)[g, k + 1, r, c] */
+  /*                      / dot_scale[g, k + 1, r]   (dot_scale NULL = 1)      */
+  /* and 0 for the last chunk: the chunk gradient of hxm_chunk_state_dot from  */
+  /* the adjoint scan and the split copy the state scan wrote.                 */
+  int32_t skip_state;
+  const void* dot_hi; const void* dot_lo;
+  const float* dot_scale;
+  float* dot_out;           /* (groups, nchunks, rows)                        */
 } hxm_chunk_scan_args;
 
 hxm_status hxm_chunk_state_scan(const hxm_chunk_scan_args* args, void* stream);

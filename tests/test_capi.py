@@ -115,6 +115,9 @@ def test_mlstm_backward_entries_validate_without_cuda():
     assert b"rows=0" in lib.hxm_last_error_string()
     s.rows, s.groups = 2, 0
     assert lib.hxm_chunk_state_scan(ct.byref(s), None) == _lib.HXM_OK
+    s.groups, s.cols, s.x, s.scaled_hi, s.dot_hi, s.dot_out = 1, 6, 1 << 20, 1 << 20, 1 << 20, 1 << 20
+    assert lib.hxm_chunk_state_scan(ct.byref(s), None) == _lib.HXM_EUNSUPPORTED  # row mode needs cols % 4 == 0
+    assert b"row mode" in lib.hxm_last_error_string()
     n = _lib.MlstmBwdNormArgs()
     n.struct_size = ct.sizeof(n)
     n.batch, n.heads, n.seqlen, n.padded_len, n.dv, n.width, n.normalize = 1, 1, 8, 4, 4, 8, 1

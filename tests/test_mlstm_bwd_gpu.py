@@ -203,6 +203,61 @@ def test_chunk_state_scan_forward_and_reverse(T):
                     assert torch.allclose(out.cpu(), scl[..., None] * want, rtol=1e-6, atol=1e-6), (cols, reverse)
 
 
+@pytest.mark.parametrize("cols", [8, 136, 520])
+def test_chunk_state_scan_row_mode_split_and_dot(T, cols):
+    """Row mode of hxm_chunk_state_scan (the tensor-core backward's): the scaled
+    exclusive states as bf16 high / low parts (x read only), and the chunk
+    gradients <out[k], state[k + 1]> read back from a state scan's split copy
+    divided by its scale, vs a host loop (float64)."""
+    from hybrid_model_mamba_xlstm_b200 import _lib
+    g = torch.Generator().manual_seed(cols)
+    G, nch, rows = 3, 6, 5
+    x = torch.randn(G, 1, nch, rows, cols, generator=g)
+    dec = torch.rand(G, 1, nch, rows, generator=g)
+    scl = torch.rand(G, 1, nch, rows, generator=g) + 0.5
+    st = torch.cuda.current_stream().cuda_stream
+
+    def scan(xs, reverse, scale, dot=None):
+        xd = xs.cuda()
+        hi = torch.empty(xd.shape, device="cuda", dtype=torch.bfloat16)
+        lo = torch.empty_like(hi)
+        dd, sd = dec.cuda(), scale.cuda()  # (kept alive until the scan has run)
+        a = _lib.ChunkScanArgs()
+        a.groups, a.nchunks, a.rows, a.cols = G, nch, rows, cols
+        a.x, a.decay, a.reverse, a.scale = xd.data_ptr(), dd.data_ptr(), reverse, sd.data_ptr()
+        a.scaled_hi, a.scaled_lo, a.skip_state = hi.data_ptr(), lo.data_ptr(), 1
+        keep = [xd, dd, sd]
+        dg = None
+        if dot is not None:
+            dg = torch.empty(G, 1, nch, rows, device="cuda")
+            ds = dot[2].cuda()
+            keep.append(ds)
+            a.dot_hi, a.dot_lo, a.dot_scale, a.dot_out = dot[0].data_ptr(), dot[1].data_ptr(), ds.data_ptr(), dg.data_ptr()
+        _lib.call("hxm_chunk_state_scan", a, st)
+        torch.cuda.synchronize()
+        assert torch.equal(xd.cpu(), xs)  # read only
+        return hi, lo, dg
+
+    def host(xs, reverse):
+        out = torch.empty_like(xs, dtype=torch.float64)
+        s = torch.zeros(G, 1, rows, cols, dtype=torch.float64)
+        for kc in (range(nch - 1, -1, -1) if reverse else range(nch)):
+            out[:, :, kc] = s
+            s = dec[:, :, kc, :, None].double() * s + xs[:, :, kc].double()
+        return out
+
+    fh, fl, _ = scan(x, 0, scl)
+    want_f = host(x, 0)
+    assert rel_err((fh.double() + fl.double()).cpu().numpy(), (scl[..., None].double() * want_f).numpy()) < 2e-5
+    y = torch.randn(G, 1, nch, rows, cols, generator=g)
+    sy = torch.rand(G, 1, nch, rows, generator=g) + 0.5
+    _, _, dg = scan(y, 1, sy, dot=(fh, fl, scl))
+    want_y = host(y, 1)
+    want_dg = torch.zeros(G, 1, nch, rows, dtype=torch.float64)
+    want_dg[:, :, :-1] = (want_y[:, :, :-1] * want_f[:, :, 1:]).sum(-1)
+    assert rel_err(dg.double().cpu().numpy(), want_dg.numpy()) < 2e-5
+
+
 def test_bf16_tf32_gemms_close_to_fp32_gemms(T):
     """The bf16 default (TF32 chunk GEMMs) against tf32=False on the same
     inputs, per-channel and per-head gates: every gradient within 5e-3."""
