@@ -225,6 +225,18 @@ class MlstmBwdNormArgs(ct.Structure):
     ]
 
 
+class ScaleSplitArgs(ct.Structure):
+    _fields_ = [
+        ("struct_size", ct.c_size_t),
+        ("batch", ct.c_int32), ("seqlen", ct.c_int32), ("padded_len", ct.c_int32), ("cols", ct.c_int32),
+        ("group", ct.c_int32),
+        ("io_dtype", ct.c_int),
+        ("x", ct.c_void_p), ("x_stride", ct.c_int64 * 2),
+        ("scale", ct.c_void_p),
+        ("hi", ct.c_void_p), ("lo", ct.c_void_p),
+    ]
+
+
 class GemmOperand(ct.Structure):
     _fields_ = [
         ("ptr", ct.c_void_p),
@@ -269,6 +281,7 @@ SYMBOLS = {
     "hxm_mlstm_bwd_normalizer": (ct.c_int, [ct.POINTER(MlstmBwdNormArgs), ct.c_void_p]),
     "hxm_chunk_state_dot": (ct.c_int, [ct.POINTER(ChunkDotArgs), ct.c_void_p]),
     "hxm_chunk_gemm": (ct.c_int, [ct.POINTER(ChunkGemmArgs), ct.c_void_p]),
+    "hxm_scale_split": (ct.c_int, [ct.POINTER(ScaleSplitArgs), ct.c_void_p]),
     "hxm_ssd_bwd_intra": (ct.c_int, [ct.POINTER(SsdBwdIntraArgs), ct.c_void_p]),
     "hxm_ssd_bwd_rows": (ct.c_int, [ct.POINTER(SsdBwdRowsArgs), ct.c_void_p]),
     "hxm_ssd_workspace_size": (ct.c_size_t, [ct.POINTER(SsdArgs)]),

@@ -477,3 +477,83 @@ extern "C" hxm_status hxm_chunk_gemm(const hxm_chunk_gemm_args* a, void* stream)
   if (bn <= 128) return hxm::cgemm::launch<128>(a, bn, st);
   return hxm::cgemm::launch<256>(a, bn, st);
 }
+
+// ----------------------------------------------------------------------------------------
+// hxm_scale_split: gate-scaled bf16 high / low operands, 8 columns per thread (16-byte
+// output stores when cols % 8 == 0), one pass.
+namespace hxm {
+namespace cgemm {
+
+template <typename T>
+__global__ void __launch_bounds__(256) scale_split_kernel(const T* __restrict__ x, int64_t sb, int64_t st,
+                                                          const float* __restrict__ scale, __nv_bfloat16* __restrict__ hi,
+                                                          __nv_bfloat16* __restrict__ lo, int batch, int seqlen,
+                                                          int lp, int cols, int group) {
+  const int c8 = (cols + 7) / 8;
+  const int64_t e = blockIdx.x * 256ll + threadIdx.x;
+  if (e >= (int64_t)batch * lp * c8) return;
+  const int cb = (int)(e % c8) * 8;
+  const int64_t row = e / c8;
+  const int t = (int)(row % lp), b = (int)(row / lp);
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = cb + j;
+    float x0 = 0.f;
+    if (t < seqlen && c < cols) {
+      x0 = to_f32<T>(x[b * sb + (int64_t)t * st + c]);
+      if (scale) x0 *= scale[row * (cols / group) + c / group];
+    }
+    v[j] = x0;
+  }
+  __nv_bfloat16 h[8], l[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    h[j] = __float2bfloat16_rn(v[j]);
+    l[j] = __float2bfloat16_rn(v[j] - __bfloat162float(h[j]));
+  }
+  const int64_t o = row * cols + cb;
+  if (cols % 8 == 0) {
+    *reinterpret_cast<uint4*>(hi + o) = *reinterpret_cast<const uint4*>(h);
+    if (lo) *reinterpret_cast<uint4*>(lo + o) = *reinterpret_cast<const uint4*>(l);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (cb + j < cols) {
+        hi[o + j] = h[j];
+        if (lo) lo[o + j] = l[j];
+      }
+  }
+}
+
+}  // namespace cgemm
+}  // namespace hxm
+
+extern "C" hxm_status hxm_scale_split(const hxm_scale_split_args* a, void* stream) {
+  hxm::clear_error();
+  HXM_REQUIRE(a && a->struct_size == sizeof(hxm_scale_split_args), "hxm_scale_split: bad args / struct_size");
+  HXM_REQUIRE(a->batch >= 0 && a->seqlen >= 0 && a->padded_len >= a->seqlen && a->cols >= 1 && a->group >= 1 &&
+                  a->cols % a->group == 0,
+              "hxm_scale_split: bad sizes batch=%d seqlen=%d padded_len=%d cols=%d group=%d", a->batch, a->seqlen,
+              a->padded_len, a->cols, a->group);
+  HXM_REQUIRE(a->io_dtype == HXM_F32 || a->io_dtype == HXM_BF16, "hxm_scale_split: io_dtype must be f32 or bf16");
+  const int64_t n = (int64_t)a->batch * a->padded_len * ((a->cols + 7) / 8);
+  if (n == 0) return HXM_OK;
+  HXM_REQUIRE(a->x && a->hi, "hxm_scale_split: NULL x or hi");
+  HXM_REQUIRE(a->cols % 8 != 0 || (reinterpret_cast<uintptr_t>(a->hi) % 16 == 0 &&
+                                    reinterpret_cast<uintptr_t>(a->lo) % 16 == 0),
+              "hxm_scale_split: hi / lo need 16-byte alignment");
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* hi = static_cast<__nv_bfloat16*>(a->hi);
+  auto* lo = static_cast<__nv_bfloat16*>(a->lo);
+  if (a->io_dtype == HXM_F32)
+    hxm::cgemm::scale_split_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(a->x), a->x_stride[0],
+                                                                a->x_stride[1], a->scale, hi, lo, a->batch, a->seqlen,
+                                                                a->padded_len, a->cols, a->group);
+  else
+    hxm::cgemm::scale_split_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(a->x), a->x_stride[0], a->x_stride[1], a->scale, hi, lo, a->batch,
+        a->seqlen, a->padded_len, a->cols, a->group);
+  return hxm::check_launch("hxm_scale_split");
+}

@@ -179,7 +179,8 @@ def _ssd_bwd_shared(x, de, Af, Bm, Cm, dy, c, st, D=None):
     return dx, un(di), dlf, un(dB), un(dC), dD
 
 
-def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False, chunk=64, tf32=None):
+def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False, chunk=64, tf32=None,
+                       tensor_cores=None, precise=True):
     """Gradients of y = ssd_chunk_scan(x, dt, A, B, C, D, dt_bias, dt_softplus)
     from a zero state, for dy (B, L, H, P).  Returns fp32
     (dx, ddt, dA, dB, dC, dD, ddt_bias) (dD / ddt_bias None when D / dt_bias are).
@@ -190,8 +191,11 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False
     (_ssd_bwd_shared: exact decay matrix, chunk-state scans on the GPU,
     batched chunk GEMMs with the heads folded in where B, C are shared) gives
     dx, dB, dC, dL/di and dL/dlog f; then ddt = dL/di + A dL/dlog f,
-    dA = sum dt dL/dlog f, and softplus / bias chain on.  tf32: chunk GEMMs on TF32
-    tensor cores (default when x is bf16, as from the bf16 forward) or in full
+    dA = sum dt dL/dlog f, and softplus / bias chain on.  tensor_cores (default
+    for bf16 x, as from the bf16 forward): the chunk GEMMs run as hxm_chunk_gemm
+    (tcgen05; ssd_bwd_tc), with bf16 high / low split operands (precise, ~1e-5
+    against float64) or high parts only (precise=False, ~1e-3); otherwise cuBLAS
+    (torch.matmul), on TF32 tensor cores when tf32 (default: bf16 x) or in full
     fp32."""
     from .tfla.tfla_bwd import _gemm_precision
     who = "ssd_chunk_scan_bwd"
@@ -200,8 +204,20 @@ def ssd_chunk_scan_bwd(x, dt, A, B, C, D, dy, *, dt_bias=None, dt_softplus=False
     n = B.shape[-1]
     de, z = _dt_eff(dt, dt_bias, dt_softplus)                      # (B, L, H)
     Af = A.float()
+    use_tc = (x.dtype == torch.bfloat16) if tensor_cores is None else bool(tensor_cores)
+    if use_tc and (p % 8 or n % 8 or n > 640):
+        if tensor_cores:
+            raise ValueError(f"{who}: tensor_cores needs headdim and dstate multiples of 8, dstate <= 640")
+        use_tc = False
     with torch.no_grad(), _gemm_precision(x.dtype == torch.bfloat16 if tf32 is None else tf32):
-        dx, di, dlf, dBm, dCm, dD = _ssd_bwd_shared(x, de, Af, B, C, dy, int(chunk), stream_of(dev), D)
+        if use_tc:
+            from .ssd_bwd_tc import ssd_bwd_shared_tc
+            if int(chunk) not in (32, 64):
+                raise ValueError(f"ssd_chunk_scan_bwd: chunk must be 32 or 64 (got {chunk})")
+            dx, di, dlf, dBm, dCm, dD = ssd_bwd_shared_tc(x, de, Af, B, C, dy, int(chunk), stream_of(dev), D,
+                                                          precise=precise)
+        else:
+            dx, di, dlf, dBm, dCm, dD = _ssd_bwd_shared(x, de, Af, B, C, dy, int(chunk), stream_of(dev), D)
         dde = di + Af * dlf
         dA = (de * dlf).sum((0, 1))
         ddt = dde * torch.sigmoid(z) if dt_softplus else dde

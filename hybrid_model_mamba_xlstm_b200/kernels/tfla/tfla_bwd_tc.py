@@ -69,6 +69,27 @@ def split(x: torch.Tensor) -> Split:
     return Split(hi, (x - hi.float()).to(torch.bfloat16))
 
 
+def scale_split(x, scale, padded_len, group, keep_lo=True):
+    """hxm_scale_split: x (batch, steps, cols) (unit column stride) times scale
+    (batch, padded_len, cols / group) fp32 (or None), zero past the steps, as a
+    bf16 split operand (batch, padded_len, cols) (the high part alone without
+    keep_lo) in one pass."""
+    if x.stride(-1) != 1 or x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float().contiguous()
+    bsz, L, cols = x.shape
+    hi, lo = _bf16_pair((bsz, padded_len, cols), x.device, keep_lo)
+    a = _lib.ScaleSplitArgs()
+    a.batch, a.seqlen, a.padded_len, a.cols, a.group = bsz, L, padded_len, cols, group
+    a.io_dtype = dtype_code(x)
+    a.x, a.x_stride = ptr(x), x.stride()[:2]
+    if scale is not None:
+        scale = scale.float().contiguous()
+        assert scale.numel() == bsz * padded_len * (cols // group)
+    a.scale, a.hi, a.lo = ptr(scale), ptr(hi), ptr(lo)
+    _lib.call("hxm_scale_split", a, torch.cuda.current_stream(x.device).cuda_stream)
+    return _as_operand(hi, lo)
+
+
 def _terms(A, ta, B, tb):
     """The bf16 products of op(A) op(B), A / B a bf16 tensor (exact) or a Split."""
     a_s, b_s = isinstance(A, Split), isinstance(B, Split)
@@ -279,8 +300,12 @@ def bwd_heads_tc(q, k, v, li, lf, dout, per_channel_out, st, c=128, split_states
     eg = torch.exp(g[..., 0]).unsqueeze(-1).expand(bsz, nh, nch, dqk).contiguous()
     Kd = Kp * egb
     g3 = lambda t, n: t.reshape(G, c, n)  # noqa: E731
-    Qb = g3(Q, dqk).to(torch.bfloat16)  # q itself: exact in bf16 for bf16 inputs
-    Kps, Kds, Qes = (split(g3(t, dqk)) for t in (Kp, Kd, Q * eb))
+    # bf16 operands straight from q, k (B*H, L, dqk): q itself (exact), i k, i k e^(g - b), q e^b
+    q3, k3 = q.reshape(bsz * nh, L, dqk), k.reshape(bsz * nh, L, dqk)
+    rowv = lambda t: t.reshape(bsz * nh, Lp, 1)  # noqa: E731
+    Qb = _view(scale_split(q3, None, Lp, dqk, keep_lo=False), G, c, dqk)
+    Kps, Kds, Qes = (_view(scale_split(x3, rowv(sc), Lp, dqk), G, c, dqk)
+                     for x3, sc in ((k3, ig), (k3, ig * egb[..., 0]), (q3, eb[..., 0])))
     bdec = b.reshape(G, c)
 
     X = torch.empty(bsz, nh, nch, dqk, w, **f32)        # increments -> states entering each chunk

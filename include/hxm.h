@@ -331,6 +331,27 @@ typedef struct hxm_chunk_dot_args {
 
 hxm_status hxm_chunk_state_dot(const hxm_chunk_dot_args* args, void* stream);
 
+/* Gate-scaled split operands of the chunkwise backward passes: for batch b,*/
+/* step t < padded_len and column c,                                          */
+/*   v = x[b, t, c] * scale[b, t, c / group]   (t < seqlen; scale NULL = 1)  */
+/*   v = 0                                      (seqlen <= t < padded_len)    */
+/*   hi[b, t, c] = bf16(v),  lo[b, t, c] = bf16(v - hi)  (lo may be NULL)     */
+/* x: io dtype, element strides (b, t), unit column stride; scale fp32 dense */
+/* (batch, padded_len, cols / group); hi, lo bf16 dense (batch, padded_len,  */
+/* cols).  One pass in place of the gate products, padding copies and the   */
+/* high / low rounding of the chunk GEMMs' operands (e.g. alpha x and beta dy */
+/* of the SSD backward, i k and e^b q of the per-head mLSTM backward).        */
+typedef struct hxm_scale_split_args {
+  size_t struct_size;
+  int32_t batch, seqlen, padded_len, cols, group;
+  hxm_dtype io_dtype;
+  const void* x; int64_t x_stride[2];
+  const float* scale;
+  void* hi; void* lo;
+} hxm_scale_split_args;
+
+hxm_status hxm_scale_split(const hxm_scale_split_args* args, void* stream);
+
 /* Batched chunk GEMM on the tensor cores (tcgen05; bf16 operands, fp32      */
 /* accumulation) for the chunk contractions of the chunkwise backward passes */
 /* (the intra-chunk products of the reference's recompute-under-autograd    */

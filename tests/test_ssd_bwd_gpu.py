@@ -122,3 +122,20 @@ def test_ssd_bwd_chunk32_ragged_matches_chunk64(S):
     for name, a, b, r in zip(("dx", "ddt", "dA", "dB", "dC", "dD", "ddt_bias"), g32, g64, ref):
         assert rel_err(a.double().cpu().numpy(), b.double().cpu().numpy()) < 1e-5, name
         assert rel_err(a.double().cpu().numpy(), r.grad.numpy()) < 1e-4, name
+
+
+@pytest.mark.parametrize("precise,chunk", [(True, 64), (False, 64), (True, 32)])
+def test_ssd_bwd_tensor_cores_match_library_path(S, precise, chunk):
+    """The tcgen05 chunk-GEMM backward (bf16 x, B, C; split operands) against
+    the fp32 library-GEMM path on the same inputs (batch 2, 300 steps, 8 heads
+    x 64, dstate 128): every gradient within 1e-3 (precise; measured 2.5e-4
+    on dA, a sum over every step and channel) or 2e-2 (high parts only, the
+    class of TF32 GEMMs; 7e-3 measured on ddt_bias)."""
+    x, dt, A, B, C, D, bias, dy = _inputs(2, 300, 8, 64, 128, seed=chunk + int(precise))
+    args = [t.cuda() for t in (x, dt, A, B, C, D)] + [dy.cuda().bfloat16()]
+    kw = dict(dt_bias=bias.cuda(), dt_softplus=True, chunk=chunk)
+    tc = S.ssd_chunk_scan_bwd(*args, **kw, tensor_cores=True, precise=precise)
+    lib = S.ssd_chunk_scan_bwd(*args, **kw, tensor_cores=False, tf32=False)
+    for name, a, b in zip(("dx", "ddt", "dA", "dB", "dC", "dD", "ddt_bias"), tc, lib):
+        assert torch.isfinite(a).all(), name
+        assert rel_err(a.double().cpu().numpy(), b.double().cpu().numpy()) < (1e-3 if precise else 2e-2), name
