@@ -337,11 +337,17 @@ def secondary_metrics(args, dev, world, rank):
     from hybrid_model_mamba_xlstm_b200.kernels.ssd import ssd_chunk_scan_bwd
     inp = ssd_inputs(8, 4096, 32, 64, 128, seed=rank, device=dev, on_device=True)
     dy = torch.randn(8, 4096, 32, 64, generator=g, device=dev).to(torch.bfloat16)
-    ms = _time_cuda(lambda: ssd_chunk_scan_bwd(inp.x, inp.dt, inp.A, inp.B, inp.C, inp.D, dy), min(steps, 3), 2,
-                    dev, world)
+    sargs = (inp.x, inp.dt, inp.A, inp.B, inp.C, inp.D, dy)
+    ms = _time_cuda(lambda: ssd_chunk_scan_bwd(*sargs), min(steps, 3), 2, dev, world)
+    ms_fast = _time_cuda(lambda: ssd_chunk_scan_bwd(*sargs, precise=False), min(steps, 3), 2, dev, world)
+    ms_lib = _time_cuda(lambda: ssd_chunk_scan_bwd(*sargs, tensor_cores=False, tf32=True), min(steps, 3), 2, dev,
+                        world)
     out["ssd_bwd_b8_h32_p64_n128_l4096"] = {
         "metric": "SSD backward ms", "value": ms, "unit": "ms", "scaling": "weak", "higher_is_better": False,
-        "kernels": "hxm chunk_scan / normalizer / chunk_dot + TF32 cuBLAS chunk GEMMs (exact per-head chunk form)"}
+        "chunk": 64, "precise_false_ms": ms_fast, "library_tf32_ms": ms_lib,
+        "kernels": "chunk_gemm_kernel (tcgen05, bf16 high / low split operands) + hxm scale_split / chunk-state "
+                   "scan (row mode) / ssd_bwd intra / rows (exact per-head chunk form)",
+        "accuracy": "default (precise): ~1e-5 vs float64; precise=False ~1e-3; library_tf32: cuBLAS TF32 ~1e-3"}
     del inp, dy
     # selective-scan backward at the 350M model's Mamba layer shape (batch 8, seqlen 2048, d_inner 2048, N 16)
     from hybrid_model_mamba_xlstm_b200.kernels.selective_scan.scan_interface import selective_scan_bwd
