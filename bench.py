@@ -21,9 +21,8 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
+import threading
 import time
 
 import torch
@@ -55,58 +54,83 @@ def profile_traffic(kernel_key):
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled every 5 ms during the timed
+    region, by NVML from a host thread (read-only queries; nvidia-smi's first sample
+    takes longer than a short timed region).  Samples are kept from mark() on."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
-        self.path = None
+    def __init__(self, device):
+        self.device = device
+        self.samples = []  # (sm_mhz, reason bits)
+        self.start = 0
+        self.max_mhz = None
+        self.handle = None
+        self.nvml = None
+        self.stop = threading.Event()
+        self.thread = None
+
+    def _handle(self, nv):
+        try:
+            props = torch.cuda.get_device_properties(self.device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.device.index)
+
+    def _run(self):
+        nv, h = self.nvml, self.handle
+        while not self.stop.is_set():
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except Exception:
+                return
+            time.sleep(0.005)
 
     def __enter__(self):
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "20"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nvml, self.handle = nv, self._handle(nv)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
         except Exception:
-            self.proc = None
+            self.thread = None
         return self
 
+    def mark(self):
+        """Start of the timed region."""
+        self.start = len(self.samples)
+
+    def hold(self, seconds=0.25):
+        """Wait (host side, the launches queued) until a sample inside the timed region exists."""
+        t_end = time.time() + seconds
+        while self.thread is not None and time.time() < t_end and len(self.samples) <= self.start:
+            time.sleep(0.002)
+
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        self.stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        if self.nvml is not None:
             try:
-                self.proc.wait(timeout=5)
+                self.nvml.nvmlShutdown()
             except Exception:
-                self.proc.kill()
+                pass
 
     def summary(self):
-        if not self.path or not os.path.exists(self.path):
+        got = self.samples[self.start:] or self.samples
+        if not got:
             return None
-        mhz, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    mhz.append(float(parts[1]))
-                    mx = float(parts[2])
-                except ValueError:
-                    continue
-                for nm, v in zip(names, parts[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(nm)
-        os.unlink(self.path)
-        if not mhz:
-            return None
-        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(mhz)}
+        reasons = sorted(name for name, const in self.REASONS
+                         if any(bits & getattr(self.nvml, const, 0) for _, bits in got))
+        return {"sm_mhz": statistics.median(m for m, _ in got), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(got), "source": "NVML, every 5 ms over the timed region"}
 
 
 def dist_setup(args):
@@ -436,13 +460,15 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize(dev)
     barrier(world)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    with ClockSampler(dev.index) as clk:
+    with ClockSampler(dev) as clk:
         torch.cuda.synchronize(dev)
         barrier(world)
+        clk.mark()
         ev[0].record(stream)
         for i in range(args.steps):
             step()
             ev[i + 1].record(stream)
+        clk.hold()  # the launches are queued: wait (host side) for a sample while they run
         torch.cuda.synchronize(dev)
         barrier(world)
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]

@@ -212,10 +212,38 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   const int ntiles = (te - tb + kT - 1) / kT;
 
   auto stage_ptr = [&](int st) { return reinterpret_cast<T*>(smem_raw + st * S::kStageBytes); };
+  // Whole tiles of a CTA whose channels and states all exist (time-major layout) take a lean
+  // path: the thread's copies sit at fixed row / step offsets from one base pointer per tensor,
+  // so a tile costs one address add per 16-byte copy and no bounds arithmetic (measured at
+  // 8 x 32768 x 4096: 5.45 -> 5.12 ms).
+  const bool lean = !CM && d0 + CH <= p.dim && p.dstate == 16;
   auto issue = [&](int k) {
     T* base = stage_ptr(k & 1);
     const int t0 = tb + k * kT, tk = min(kT, te - t0);
     constexpr int kChunks = kT / kE;
+    if (lean && tk == kT) {
+      constexpr int kRowStep = CH / kChunks;  // rows between one thread's consecutive copies
+      const int lr = tid / kChunks, lt = (tid % kChunks) * kE;
+#pragma unroll
+      for (int which = 0; which < 3; ++which) {
+        if (which == 2 && !has_z) break;
+        const T* g = which == 0 ? ug : (which == 1 ? dtg : zg);
+        const int64_t sd = which == 0 ? p.su[2] : (which == 1 ? p.sdt[2] : p.sz[2]);
+        const T* src = g + (int64_t)(d0 + lr) * sd + t0 + lt;
+        T* dst = base + which * S::kIoSlot + lr * S::kTP + lt;
+#pragma unroll
+        for (int i = 0; i < kChunks; ++i) cp_async16(dst + i * kRowStep * S::kTP, src + (int64_t)i * kRowStep * sd, 16);
+      }
+      T* raw = base + 3 * S::kIoSlot;  // B rows 0..15, C rows 16..31
+#pragma unroll
+      for (int i = 0; i < 32 * kChunks / CH; ++i) {
+        const int row = lr + i * kRowStep, n = row % 16;
+        const T* g = row >= 16 ? Cg + (int64_t)n * p.sC[2] : Bg + (int64_t)n * p.sB[2];
+        cp_async16(raw + row * S::kTP + lt, g + t0 + lt, 16);
+      }
+      cp_async_commit();
+      return;
+    }
     // u, delta, z rows
 #pragma unroll 1
     for (int which = 0; which < 3; ++which) {
