@@ -419,7 +419,7 @@ def prefill_metric(args, dev, world, rank):
         n_mlstm * cfg.num_heads * 4 * 128 * cfg.head_dim
     for kind, per in (("weak", gb), ("strong", max(1, gb // world))):
         # finer wavefront pieces when one GPU holds one or two sequences (measured at batch 1:
-        # 13.1 ms with 8 pieces, 14.0 with 4; at batch 8, 4 pieces)
+        # 11.6 ms with 8 pieces, 13.2 with 4, 14.0 with 16; at batch 8, 4 pieces: 29.5 ms)
         pieces = 8 if per <= 2 else 4
         ids = torch.randint(0, 50304, (per, seqlen), generator=g, device=dev)
         with torch.no_grad():

@@ -184,6 +184,96 @@ __global__ void __launch_bounds__(128) mlstm_prescale_kernel(const Params p, __n
   }
 }
 
+// Per-channel gates, two channels per thread (4-byte q, k accesses): the same outputs as the
+// per-channel branch of mlstm_prescale_kernel, with the chunk's steps split over 8 segments
+// (one warp each) instead of walked by one thread: block = 32 channel pairs x 8 segments.
+// Each thread sums its segment's log forget gates, the segments' sums are scanned through
+// shared memory, and each thread then forms its segment's factors from that prefix — so a
+// thread's serial chain is kc / 8 steps, and a small call (one sequence, four heads, one
+// 128-step chunk: 8 blocks of the one-thread-per-channel kernel, 140 us) spreads over 32 blocks
+// of 256 threads.  Warp accesses per step: 256 contiguous bytes of each gate row, 128 of q, k.
+constexpr int kPcSeg = 8;
+__global__ void __launch_bounds__(32 * kPcSeg) mlstm_prescale_channels_kernel(
+    const Params p, __nv_bfloat16* Qs, __nv_bfloat16* Ks, float* decay, float* rho_e, float* nadd, int* unsafe,
+    int kc, int level) {
+  __shared__ float2 part[kPcSeg][32];
+  const int nch = (p.seqlen + kc - 1) / kc;
+  const int c = blockIdx.x % nch;
+  const int bh = blockIdx.x / nch;
+  if (level > 0 && unsafe[bh] == 0) return;  // uniform over the block
+  const int b = bh / p.heads, h = bh % p.heads;
+  const int cp = threadIdx.x & 31, seg = threadIdx.x >> 5;
+  const int j0 = blockIdx.y * 64 + 2 * cp;
+  const bool active = j0 < p.dqk;  // every thread takes part in the barriers below
+  const int t0 = c * kc, tn = min(kc, p.seqlen - t0);
+  const int sl = kc / kPcSeg, ta = min(seg * sl, tn), te = min(ta + sl, tn);
+  const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(p.q) + b * p.sq[0] + h * p.sq[1];
+  const __nv_bfloat16* k = static_cast<const __nv_bfloat16*>(p.k) + b * p.sk[0] + h * p.sk[1];
+  const float* li = p.log_i + b * p.si[0] + h * p.si[1] + j0;
+  const float* lf = p.log_f + b * p.sf[0] + h * p.sf[1] + j0;
+  float2 s = make_float2(0.f, 0.f);
+  if (active) {
+#pragma unroll 4
+    for (int t = ta; t < te; ++t) {
+      const int64_t tt = t0 + t;
+      s.x += lf[tt * p.tf];
+      s.y += lf[tt * p.tf + 1];
+    }
+  }
+  part[seg][cp] = s;
+  __syncthreads();
+  float2 pre = make_float2(0.f, 0.f), g = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kPcSeg; ++i) {
+    const float2 v = part[i][cp];
+    if (i < seg) pre = make_float2(pre.x + v.x, pre.y + v.y);
+    g = make_float2(g.x + v.x, g.y + v.y);
+  }
+  const float rho[2] = {0.5f * g.x, 0.5f * g.y};
+  const float eh[2] = {__expf(rho[0]), __expf(rho[1])};
+  float bt[2] = {pre.x, pre.y}, ksum[2] = {0.f, 0.f};
+  bool bad = false;
+  const int64_t ob = (int64_t)bh * p.seqlen * p.dqk;
+  if (active) {
+#pragma unroll 4
+    for (int t = ta; t < te; ++t) {
+      const int64_t tt = t0 + t;
+      const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(k + tt * p.tk + j0));
+      const float2 qf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(q + tt * p.tq + j0));
+      const float kv[2] = {kf.x, kf.y}, qv[2] = {qf.x, qf.y};
+      float qs[2], ks[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        bt[u] += lf[tt * p.tf + u];
+        const float xq = bt[u] - rho[u], xk = rho[u] - bt[u] + li[tt * p.ti + u];
+        bad |= !(fabsf(xq) <= kMaxExp) || !(fabsf(xk) <= kMaxExp);  // also catches NaN
+        qs[u] = qv[u] * __expf(xq);
+        ks[u] = kv[u] * __expf(xk);
+        ksum[u] += ks[u] * eh[u];
+      }
+      const int64_t o = ob + tt * p.dqk + j0;
+      *reinterpret_cast<uint32_t*>(Qs + o) = pack2<__nv_bfloat16>(qs[0], qs[1]);
+      *reinterpret_cast<uint32_t*>(Ks + o) = pack2<__nv_bfloat16>(ks[0], ks[1]);
+    }
+  }
+  if (bad) unsafe[bh] = level + 1;
+  __syncthreads();  // every thread has read part[] above
+  part[seg][cp] = make_float2(ksum[0], ksum[1]);
+  __syncthreads();
+  if (seg == 0 && active) {
+    float2 tot = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kPcSeg; ++i) tot = make_float2(tot.x + part[i][cp].x, tot.y + part[i][cp].y);
+    const int64_t vi = ((int64_t)bh * nch + c) * p.dqk + j0;
+    decay[vi] = __expf(g.x);
+    decay[vi + 1] = __expf(g.y);
+    rho_e[vi] = eh[0];
+    rho_e[vi + 1] = eh[1];
+    nadd[vi] = tot.x;  // e^rho Ks^T 1: the normalizer's increment
+    nadd[vi + 1] = tot.y;
+  }
+}
+
 // Per-head gates with 16-byte-aligned k (and q) rows: the same outputs as the per-head branch
 // of mlstm_prescale_kernel, one block per (b, h, chunk) over every key channel, each thread
 // moving 8 channels (16 bytes) of one step per access — the other kernel's 4-byte accesses left
@@ -520,10 +610,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     for (int blk = 0; blk < L::kNB; ++blk) {
       const int srow = blk * 128 + row;
       float v[32];
+      const float* crow = p.C0 ? p.C0 + ((int64_t)bh * DK + srow) * p.dv + e0 + ch : nullptr;
+      if (crow && e0 + ch + 32 <= p.dv && p.dv % 4 == 0 && reinterpret_cast<uintptr_t>(p.C0) % 16 == 0) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int col = e0 + ch + j;
-        v[j] = (p.C0 && col < p.dv) ? s0 * p.C0[((int64_t)bh * DK + srow) * p.dv + col] : 0.f;
+        for (int j = 0; j < 32; j += 4) {  // the row's 128 bytes in 16-byte loads
+          const float4 c4 = *reinterpret_cast<const float4*>(crow + j);
+          v[j] = s0 * c4.x; v[j + 1] = s0 * c4.y; v[j + 2] = s0 * c4.z; v[j + 3] = s0 * c4.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = (crow && e0 + ch + j < p.dv) ? s0 * crow[j] : 0.f;
       }
       tc::tmem_st32(tm + L::tAcc + blk * 64 + ch, v);
     }
@@ -767,9 +863,16 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
         float v[32];
         tc::tmem_ld32(tm + L::tAcc + blk * 64 + ch, v);
         tc::tmem_wait_ld();
+        float* crow = p.CT + ((int64_t)bh * DK + srow) * p.dv + e0 + ch;
+        if (e0 + ch + 32 <= p.dv && p.dv % 4 == 0 && reinterpret_cast<uintptr_t>(p.CT) % 16 == 0) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (e0 + ch + j < p.dv) p.CT[((int64_t)bh * DK + srow) * p.dv + e0 + ch + j] = rl * v[j];
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(crow + j) = make_float4(rl * v[j], rl * v[j + 1], rl * v[j + 2], rl * v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (e0 + ch + j < p.dv) crow[j] = rl * v[j];
+        }
       }
     }
     if (p.nT && blockIdx.x == 0)
@@ -847,6 +950,9 @@ static hxm_status launch_stream_dk(const Params& p, cudaStream_t st) {
     if (heads16) {
       mlstm_prescale_heads_kernel<DK><<<p.batch * p.heads * nch, kPreThreads, 0, st>>>(
           p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level, fqg);
+    } else if (pair && p.gate_mode == 1 && p.dqk % 64 == 0) {
+      dim3 pg(p.batch * p.heads * nch, p.dqk / 64);
+      mlstm_prescale_channels_kernel<<<pg, 32 * kPcSeg, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level);
     } else if (pair) {
       dim3 pg(p.batch * p.heads * nch, (DK + 255) / 256);
       mlstm_prescale_kernel<__nv_bfloat16, 2><<<pg, 128, 0, st>>>(p, Qs, Ks, decay, rho_e, nadd, unsafe, kc, level,

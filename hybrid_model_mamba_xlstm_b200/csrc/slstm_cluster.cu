@@ -16,6 +16,8 @@
 // Waits are bounded (error flag + early exit, no hang).
 #include <cuda_bf16.h>
 
+#include <cstdlib>
+
 #include "capi_internal.h"
 #include "common.cuh"
 #include "slstm.h"
@@ -113,9 +115,16 @@ struct CL {
   static_assert(kH % 16 == 0 && kPart % 16 == 0 && (kHP * 2) % 16 == 0, "st.async alignment");
 };
 
-template <typename T, int HD>
+// HPC heads per cluster: 1, or 2 for small batches (at most kBR / 2 rows), where the kBR
+// (head, row) slots of the MMA's N dimension hold two heads' rows: every warp then runs both
+// heads' R fragments (twice the registers and MMAs, each head's columns kept) and a layer
+// occupies half the SMs — at batch 1 the 6 sLSTM layers of a prefill wavefront then fit on
+// the GPU at once beside the other layers.
+template <typename T, int HD, int HPC>
 __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_cluster_kernel(const Params p) {
   using L = CL<HD>;
+  constexpr int kRows = kBR / HPC;  // batch rows per head in one cluster
+  static_assert(L::kMW == 1, "one m-tile per warp");
   extern __shared__ __align__(16) unsigned char sm[];
   __nv_bfloat16* hprev = reinterpret_cast<__nv_bfloat16*>(sm + L::kH);
   float2* part = reinterpret_cast<float2*>(sm + L::kPart);
@@ -126,22 +135,25 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rank = (int)cluster_rank();
-  const int head = blockIdx.x / kCL;
-  const int b0 = blockIdx.y * kBR;
-  const int nb = min(kBR, p.batch - b0);
+  const int head0 = blockIdx.x / kCL * HPC;
+  const int b0 = blockIdx.y * kRows;
+  const int nb = min(kRows, p.batch - b0);
   const int c0 = rank * L::kCPC;  // first channel of this CTA
-  // this thread's (channel, batch row) pair: a row's kCPC channels are kCPC consecutive lanes
+  // this thread's (channel, slot) pair: a slot's kCPC channels are kCPC consecutive lanes;
+  // slot bl = (head head0 + bl / kRows, batch row b0 + bl % kRows)
   const int c = tid % L::kCPC, bl = tid / L::kCPC;
+  const int head = head0 + bl / kRows, brow = bl % kRows;
+  const bool live = brow < nb;
 
   // ---- R slice -> mma A fragments (registers), once ------------------------------
   // local column m = q*kCPC + c  <->  R[head][k][q*HD + c0 + c]
-  uint32_t afr[L::kMW][L::kKT][4];
+  uint32_t afr[HPC][L::kKT][4];
   {
-    const __nv_bfloat16* R = p.R + (int64_t)head * HD * 4 * HD;
     const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
-    for (int mw = 0; mw < L::kMW; ++mw) {
-      const int mt = warp * L::kMW + mw;
+    for (int mw = 0; mw < HPC; ++mw) {
+      const __nv_bfloat16* R = p.R + (int64_t)(head0 + mw) * HD * 4 * HD;
+      const int mt = warp;
 #pragma unroll
       for (int kt = 0; kt < L::kKT; ++kt) {
 #pragma unroll
@@ -163,7 +175,7 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
   for (int e = tid; e < kBR * HD; e += L::kNT) {
     const int r = e / HD, j = e % HD;
     float hv = 0.f;
-    if (r < nb && p.h0) hv = p.h0[((int64_t)(b0 + r) * p.heads + head) * HD + j];
+    if (r % kRows < nb && p.h0) hv = p.h0[((int64_t)(b0 + r % kRows) * p.heads + head0 + r / kRows) * HD + j];
     hprev[r * L::kHP + j] = __float2bfloat16_rn(hv);
   }
   if (tid == 0) {
@@ -177,7 +189,7 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
     arm_tx(&bars[1], L::kHTx);
   }
   // stabilized cell and its log-scale for this thread's pair
-  float cs = (bl < nb && p.c0) ? p.c0[((int64_t)(b0 + bl) * p.heads + head) * HD + c0 + c] : 0.f;
+  float cs = (live && p.c0) ? p.c0[((int64_t)(b0 + brow) * p.heads + head) * HD + c0 + c] : 0.f;
   float ms = 0.f;
   const float wc = p.w[c0 + c];
   const T* gsrc = static_cast<const T*>(p.gates);
@@ -188,8 +200,9 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
     for (int i = 0; i < kGE; ++i) {
       const int e = tid + i * L::kNT;
       const int cc = e % L::kCPC, q = (e / L::kCPC) % 4, r = e / (4 * L::kCPC);
-      v[i] = (r < nb && t < p.seqlen)
-                 ? to_f32<T>(gsrc[(((int64_t)(b0 + r) * p.seqlen + t) * p.heads + head) * 4 * HD + q * HD + c0 + cc])
+      const int rr = r % kRows, hh = head0 + r / kRows;
+      v[i] = (rr < nb && t < p.seqlen)
+                 ? to_f32<T>(gsrc[(((int64_t)(b0 + rr) * p.seqlen + t) * p.heads + hh) * 4 * HD + q * HD + c0 + cc])
                  : 0.f;
     }
   };
@@ -224,8 +237,11 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
     // (a) gate pre-activations R^T h_{t-1}: D[m][n] (m = gate column, n = batch row), 4 MMA chains
     {
       const int g = lane >> 2, t4 = lane & 3;
+      // D[m][n] (n = slot): with two heads, each head's MMA covers all 8 slots and this
+      // thread keeps the head of its own slots 2 t4, 2 t4 + 1 (both of head t4 / 2)
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int mw = 0; mw < L::kMW; ++mw) {
+      for (int mw = 0; mw < HPC; ++mw) {
         float acc[4][4] = {};
 #pragma unroll
         for (int kt = 0; kt < L::kKT; ++kt) {
@@ -234,10 +250,13 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
           const uint32_t b1r = *reinterpret_cast<const uint32_t*>(hb + 8);
           mma_16816(acc[kt & 3], afr[mw][kt], b0r, b1r);
         }
-        float d[4];
+        if (HPC == 1 || mw == (2 * t4) / kRows) {
 #pragma unroll
-        for (int r = 0; r < 4; ++r) d[r] = (acc[0][r] + acc[1][r]) + (acc[2][r] + acc[3][r]);
-        const int m = (warp * L::kMW + mw) * 16 + g;
+          for (int r = 0; r < 4; ++r) d[r] = (acc[0][r] + acc[1][r]) + (acc[2][r] + acc[3][r]);
+        }
+      }
+      {
+        const int m = warp * 16 + g;
         pre[(2 * t4) * L::kCols + m] = d[0];
         pre[(2 * t4 + 1) * L::kCols + m] = d[1];
         pre[(2 * t4) * L::kCols + m + 8] = d[2];
@@ -297,7 +316,7 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
       const float rinv = rsqrtf(S / HD + p.eps * ex2_approx(-2.f * M * kLog2e));
       const float hv = og * tanh_approx(wc * ex2_approx((ms - M) * kLog2e) * cs * rinv);
       hlast = hv;
-      if (bl < nb) hout[(((int64_t)(b0 + bl) * p.seqlen + t) * p.heads + head) * HD + c0 + c] = from_f32<T>(hv);
+      if (live) hout[(((int64_t)(b0 + brow) * p.seqlen + t) * p.heads + head) * HD + c0 + c] = from_f32<T>(hv);
       // pack: lane pairs -> bf16x2, then 4 pairs -> 16 bytes at the group's first lane
       const float hn = __shfl_down_sync(0xffffffffu, hv, 1);
       __nv_bfloat162 pr = __floats2bfloat162_rn(hv, hn);
@@ -324,22 +343,34 @@ __global__ void __cluster_dims__(kCL, 1, 1) __launch_bounds__(HD, 1) slstm_clust
   }
 
   if (!bad) {
-    if (p.hT && bl < nb) p.hT[((int64_t)(b0 + bl) * p.heads + head) * HD + c0 + c] = hlast;
-    if (p.cT && bl < nb) p.cT[((int64_t)(b0 + bl) * p.heads + head) * HD + c0 + c] = ex2_approx(ms * kLog2e) * cs;
+    if (p.hT && live) p.hT[((int64_t)(b0 + brow) * p.heads + head) * HD + c0 + c] = hlast;
+    if (p.cT && live) p.cT[((int64_t)(b0 + brow) * p.heads + head) * HD + c0 + c] = ex2_approx(ms * kLog2e) * cs;
   } else if (tid == 0 && p.error_flag) {
     atomicExch(p.error_flag, 1);
   }
   cluster_sync();  // no CTA leaves while peers may still write into its shared memory
 }
 
-template <typename T, int HD>
-static hxm_status launch_hd(const Params& p, cudaStream_t st) {
+template <typename T, int HD, int HPC>
+static hxm_status launch_hpc(const Params& p, cudaStream_t st) {
   using L = CL<HD>;
-  auto kern = slstm_cluster_kernel<T, HD>;
+  auto kern = slstm_cluster_kernel<T, HD, HPC>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-  dim3 grid(kCL * p.heads, (p.batch + kBR - 1) / kBR);
+  constexpr int kRows = kBR / HPC;
+  dim3 grid(kCL * p.heads / HPC, (p.batch + kRows - 1) / kRows);
   kern<<<grid, L::kNT, L::kBytes, st>>>(p);
   return check_launch("hxm_slstm_scan_fwd (cluster)");
+}
+// Two heads per cluster when every cluster then still holds all its rows (batch <= kBR / 2) and
+// the heads pair up; HXM_SLSTM_HPC = 1 | 2 overrides (2 only where it applies).
+template <typename T, int HD>
+static hxm_status launch_hd(const Params& p, cudaStream_t st) {
+  const char* knob = std::getenv("HXM_SLSTM_HPC");
+  int hpc = knob ? std::atoi(knob) : 0;
+  const bool pairable = p.heads % 2 == 0 && p.batch <= kBR / 2;
+  if (hpc != 1 && hpc != 2) hpc = pairable ? 2 : 1;
+  if (hpc == 2 && pairable) return launch_hpc<T, HD, 2>(p, st);
+  return launch_hpc<T, HD, 1>(p, st);
 }
 
 hxm_status launch_cluster(const Params& p, cudaStream_t st) {

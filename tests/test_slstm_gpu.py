@@ -102,3 +102,27 @@ def test_prefill_sized_sampled(slstm):
         ref, hr, cr = OC.slstm(np64(gates[bb:bb + 1]), np64(w), R=np64(Rm))
         assert rel_err(np64(out[bb:bb + 1]), ref) < 2e-2
         assert rel_err(np64(c[bb:bb + 1]), cr) < 2e-2
+
+
+@pytest.mark.parametrize("b,hd,dtype", [(1, 256, torch.bfloat16), (3, 128, torch.float32), (4, 256, torch.bfloat16)])
+def test_two_heads_per_cluster_matches_one(slstm, b, hd, dtype, monkeypatch):
+    """Batches of at most 4 rows run two heads per 8-CTA cluster (half the SMs):
+    each (head, row) slot takes the same MMA chain, norm and exchanges as with
+    one head per cluster, so outputs and final states agree bitwise; both also
+    match the oracle."""
+    gates, w, Rm = _inputs(b, 70, 4, hd, 11, dtype)
+    gen = torch.Generator().manual_seed(5)
+    h0 = (0.5 * torch.randn(b, 4, hd, generator=gen)).cuda()
+    c0 = torch.randn(b, 4, hd, generator=gen).cuda()
+    res = []
+    for hpc in ("1", "2"):
+        monkeypatch.setenv("HXM_SLSTM_HPC", hpc)
+        out, (h, c) = slstm(gates, w, R=Rm, h0=h0, c0=c0)
+        torch.cuda.synchronize()
+        res.append((out.clone(), h.clone(), c.clone()))
+    for x, y in zip(*res):
+        assert torch.equal(x, y)
+    ref, hr, cr = R.slstm_recurrent(np64(gates), np64(w), R=np64(Rm), h0=np64(h0), c0=np64(c0))
+    tol = 2e-3 if dtype == torch.float32 else 2e-2
+    assert rel_err(np64(res[1][0]), ref) < tol
+    assert rel_err(np64(res[1][2]), cr) < tol
