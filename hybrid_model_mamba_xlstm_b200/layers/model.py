@@ -138,6 +138,29 @@ class HybridLanguageModel(nn.Module):
             return h
         return self.lm_head(h)
 
+    @staticmethod
+    def _piece_bounds(L, pieces):
+        """[(start, end)] of the wavefront's sequence pieces: ``pieces`` equal
+        pieces of whole 128-step chunks, or explicit piece lengths (a sequence
+        of ints; the last piece takes whatever of L is left)."""
+        if isinstance(pieces, int):
+            if pieces <= 1 or L < 2 * pieces:
+                return [(0, L)]
+            step = -(-L // pieces)
+            step = -(-step // 128) * 128  # whole 128-step chunks per piece
+            return [(a, min(a + step, L)) for a in range(0, L, step)]
+        bounds, a = [], 0
+        for n in pieces:
+            if a >= L:
+                break
+            if n <= 0:
+                raise ValueError(f"prefill: piece lengths must be positive, got {list(pieces)}")
+            bounds.append((a, min(a + int(n), L)))
+            a += int(n)
+        if a < L:
+            bounds.append((a, L))
+        return bounds
+
     @torch.no_grad()
     def prefill(self, input_ids, pieces=4, caches=None, return_hidden=False):
         """Logits of :meth:`forward`, scheduled as a wavefront over layers and
@@ -150,16 +173,16 @@ class HybridLanguageModel(nn.Module):
         working on different pieces run concurrently — the sLSTM recurrence
         occupies 8 SMs per head for thousands of sequential steps, and the other
         layers' kernels fill the rest of the GPU meanwhile.  On CPU, or with one
-        piece, this is :meth:`forward`."""
+        piece, this is :meth:`forward`.  ``pieces`` may also list the piece
+        lengths: a short first piece shortens the pipeline fill (the time until
+        the last layer sees its first piece), which dominates at batch 1."""
         L = input_ids.shape[1]
         if caches is None:
             caches = self.init_caches()
-        if not input_ids.is_cuda or pieces <= 1 or L < 2 * pieces:
+        bounds = self._piece_bounds(L, pieces)
+        if not input_ids.is_cuda or len(bounds) <= 1:
             return self.forward(input_ids, return_hidden=return_hidden, caches=caches)
         dev = input_ids.device
-        step = -(-L // pieces)
-        step = -(-step // 128) * 128  # whole 128-step chunks per piece
-        bounds = [(a, min(a + step, L)) for a in range(0, L, step)]
         main = torch.cuda.current_stream(dev)
         nl = len(self.layers)
         streams = [torch.cuda.Stream(dev) for _ in range(nl + 1)]

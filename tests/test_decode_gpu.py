@@ -62,10 +62,11 @@ def test_pieces_equal_full_prefill_fp32(L, split):
     assert rel_err(np64(torch.cat(parts, 1)), np64(full)) < 1e-4
 
 
-@pytest.mark.parametrize("pieces", [2, 3])
+@pytest.mark.parametrize("pieces", [2, 3, (128, 256), (128, 128)])
 def test_wavefront_prefill_equals_full_forward(L, pieces):
     """HybridLanguageModel.prefill: layers on their own streams, the sequence in
-    pieces of whole 128-step chunks handed from layer to layer by events — the
+    pieces of whole 128-step chunks (equal, or of listed lengths; a list that
+    falls short leaves the rest to a last piece) handed from layer to layer by events — the
     logits of the single-stream whole-sequence forward (fp32 1e-4, bf16 with the
     prefill's tensor-core paths 3e-2), and the carried states continue it."""
     for dtype, kw, tol in ((torch.float32, {}, 1e-4),
