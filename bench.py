@@ -668,18 +668,69 @@ def attach_cpu_baselines(sec):
             sec[key]["cpu_baseline"] = {"value": value, "unit": unit, "cores": threads, "kind": "reference",
                                         "sample": sample, "seconds": secs}
 
-    # mLSTM: the exact 2 x 4 x 2048 x 256 workload in full; the long-context one as a 4096-step prefix
-    # of one (batch, head) pair (the loop's cost is linear in steps and pairs), scaled x 8 x 64
-    for key, (b, h, L, d, Ls, scale) in {"mlstm_b2_h4_l2048_d256": (2, 4, 2048, 256, 2048, 1.0),
-                                         "mlstm_b8_h8_l32768_d512": (1, 1, 4096, 512, 4096, 8.0 * 64)}.items():
+    # mLSTM: the exact 2 x 4 x 2048 x 256 workload in full; the larger ones as a 4096-step prefix of
+    # one (batch, head) pair (the loop's cost is linear in steps and pairs), scaled to the workload
+    for key, (b, h, L, d, Ls, scale, full) in {
+            "mlstm_b2_h4_l2048_d256": (2, 4, 2048, 256, 2048, 1.0, (2, 4, 2048)),
+            "mlstm_b8_h8_l8192_d256": (1, 1, 4096, 256, 4096, 8.0 * 8 * 2, (8, 8, 8192)),
+            "mlstm_b8_h8_l32768_d512": (1, 1, 4096, 512, 4096, 8.0 * 64, (8, 8, 32768))}.items():
+        if key not in sec:
+            continue
         inp = mlstm_inputs(b, h, Ls, d, torch.float32, seed=0)
         ex = lambda t: t[..., None].expand(*t.shape, d)  # noqa: E731
         args = (inp.q, inp.k, inp.v, ex(torch.exp(inp.log_i)), ex(torch.exp(inp.log_f)))
         secs = timed(lambda: ref["tfla"].tfla_forward_pytorch(*args))
-        fl = (8 if scale > 1 else b) * (8 if scale > 1 else h) * (32768 if scale > 1 else L) / 128 * \
-            (2 * 128 * 128 * d * 2 + 2 * 128 * d * d * 2)
+        fl = full[0] * full[1] * full[2] / 128 * (2 * 128 * 128 * d * 2 + 2 * 128 * d * d * 2)
         put(key, fl / (secs * scale) / 1e12, "TFLOP/s",
             f"tfla_forward_pytorch {b}x{h}x{Ls}x{d} fp32" + (f", scaled x{int(scale)}" if scale > 1 else ""), secs)
+
+    # backward: the reference's rule — its forward loop re-run under autograd
+    # (SelectiveScanFunction.backward, scan_interface.py:62-100; TFLAFunction.backward,
+    # tfla_interface.py:52-81) — timed for .backward() alone on a sample, scaled to the workload
+    def timed_bwd(fwd, leaves):
+        leaves = [t.detach().clone().requires_grad_(True) for t in leaves]
+        out = fwd(*leaves)
+        out = out[0] if isinstance(out, tuple) else out
+        g = torch.randn_like(out)
+        t0 = time.perf_counter()
+        out.backward(g)
+        return time.perf_counter() - t0
+
+    if "mlstm_bwd_b8_h4_l2048_d512_channel_gates" in sec:
+        # one (batch, head) pair x 512 steps of the 350M mLSTM layer shape, per-channel gates; x 32 pairs x 4
+        inp = mlstm_inputs(1, 1, 512, 512, torch.float32, seed=0)
+        g = torch.Generator().manual_seed(1)
+        li = 0.5 * torch.randn(1, 1, 512, 512, generator=g)
+        lf = torch.nn.functional.logsigmoid(torch.randn(1, 1, 512, 512, generator=g) + 3.0)
+        secs = timed_bwd(lambda q, k, v, a, f: ref["tfla"].tfla_forward_pytorch(q, k, v, torch.exp(a), torch.exp(f)),
+                         [inp.q, inp.k, inp.v, li, lf])
+        put("mlstm_bwd_b8_h4_l2048_d512_channel_gates", secs * 128 * 1e3, "ms",
+            "autograd backward of tfla_forward_pytorch, 1x1x512x512 per-channel gates, fp32, scaled x128", secs)
+    if "ssd_bwd_b8_h32_p64_n128_l4096" in sec:
+        # one batch row, 4 of the 32 heads (256 channels, head-repeated A and dt), 1024 of 4096 steps; x 8 x 8 x 4
+        si = ssd_inputs(1, 1024, 4, 64, 128, seed=0)
+        xs = si.x.float().reshape(1, 1024, 256)
+        dts = si.dt.repeat_interleave(64, dim=2)
+        As = si.A.repeat_interleave(64)[:, None].expand(256, 128).contiguous()
+        secs = timed_bwd(lambda x, dt, a, bm, cm: ref["scan"].selective_scan_pytorch(x, dt, a, bm, cm,
+                                                                                     si.D.repeat_interleave(64)),
+                         [xs, dts, As, si.B.float(), si.C.float()])
+        put("ssd_bwd_b8_h32_p64_n128_l4096", secs * 256 * 1e3, "ms",
+            "autograd backward of selective_scan_pytorch (head-repeated A, dt), 1 row x 4 heads x 1024 steps, fp32, "
+            "scaled x256", secs)
+    if "scan_bwd_b8_l2048_d2048_n16" in sec:
+        # one batch row x 256 of 2048 channels x 2048 steps; x 8 rows x 8
+        from hybrid_model_mamba_xlstm_b200.workloads import scan_inputs
+        s2 = scan_inputs(1, 2048, 256, 16, torch.float32, seed=0)
+        tr = lambda t: t.transpose(1, 2).contiguous()  # noqa: E731  (B, L, D) as the reference takes it
+        secs = timed_bwd(lambda u, dt, a, bm, cm: ref["scan"].selective_scan_pytorch(u, dt, a, bm, cm, s2.D),
+                         [tr(s2.u), tr(torch.nn.functional.softplus(s2.delta + s2.delta_bias[:, None])), s2.A,
+                          tr(s2.B), tr(s2.C)])
+        nbytes = sec["scan_bwd_b8_l2048_d2048_n16"].get("roofline", {}).get("algorithmic", {}).get("bytes")
+        if nbytes:
+            put("scan_bwd_b8_l2048_d2048_n16", nbytes / (secs * 64) / 1e9, "GB/s",
+                "autograd backward of selective_scan_pytorch, 1 row x 256 channels x 2048 steps, fp32, scaled x64",
+                secs)
     # SSD: one of the 8 batch rows in full (32 heads x 64 = 2048 channels, dstate 128, 4096 steps), x 8
     si = ssd_inputs(1, 4096, 32, 64, 128, seed=0)
     x = si.x.float().reshape(1, 4096, 2048)
