@@ -127,6 +127,17 @@ def main(argv=None):
             ids = torch.randint(0, model.config.vocab_size, (B, L), device=dev)
             fn = lambda: model(ids)  # noqa: E731
         extra = {"tokens": B * L}
+    elif a.case == "layer":
+        # one layer of the 350M model on a (batch, tokens) piece with its recurrent cache, as the
+        # prefill wavefront runs it: layer 0 Mamba, 2 mLSTM, 3 sLSTM
+        from hybrid_model_mamba_xlstm_b200 import layers as Lyr
+        idx, B, L = (s + [2, 1, 256][len(s):])[:3]
+        torch.manual_seed(0)
+        model = Lyr.HybridLanguageModel(Lyr.hybrid_350m_config()).to(dev).to(torch.bfloat16).eval()
+        blk, caches = model.layers[idx], model.init_caches()
+        x = torch.randn(B, L, model.config.dim, device=dev, dtype=torch.bfloat16)
+        fn = lambda: blk.forward_pending(x, None, cache=caches[idx])  # noqa: E731
+        extra = {"tokens": B * L, "mixer": type(blk.mixer).__name__}
     elif a.case == "prefill_graph":
         from hybrid_model_mamba_xlstm_b200 import layers as Lyr
         B, L, pieces = (s + [8, 2048, 4][len(s):])[:3]
