@@ -105,10 +105,10 @@ def main(argv=None):
         extra = {"steps": L}
     elif a.case == "conv":
         from hybrid_model_mamba_xlstm_b200.kernels.conv import causal_conv1d
-        B, D, L = (s + [8, 4096, 2048][len(s):])[:3]
+        B, D, L = (s + [8, 4096, 2048][len(s):])[:3]  # batch, channels, seqlen: x is (B, L, D)
         g = torch.Generator(device=dev)
         g.manual_seed(0)
-        x = torch.randn(B, D, L, generator=g, device=dev).to(torch.bfloat16)
+        x = torch.randn(B, L, D, generator=g, device=dev).to(torch.bfloat16)
         w = torch.randn(D, 4, generator=g, device=dev) * 0.5
         bias = torch.randn(D, generator=g, device=dev) * 0.1
         fn = lambda: causal_conv1d(x, w, bias, activation="silu")  # noqa: E731
