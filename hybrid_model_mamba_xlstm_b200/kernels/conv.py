@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
-from ._common import dtype_code, ptr, require_cuda, stream_of
+from ._common import dtype_code, f32_param, ptr, require_cuda, stream_of
 
 __all__ = ["causal_conv1d"]
 
@@ -31,13 +31,13 @@ def causal_conv1d(x, weight, bias=None, activation=None, *, initial_state=None, 
     bsz, L, d = x.shape
     if x.dtype not in (torch.float32, torch.bfloat16):
         raise TypeError(f"{who}: x must be fp32 or bf16, got {x.dtype}")
-    w = weight.reshape(weight.shape[0], weight.shape[-1]).float().contiguous()
+    w = f32_param(weight).reshape(weight.shape[0], weight.shape[-1])
     if w.shape[0] != d:
         raise ValueError(f"{who}: weight must be ({d}, width); got {tuple(weight.shape)}")
     width = w.shape[1]
     if activation not in _ACT:
         raise ValueError(f"{who}: activation must be None or 'silu'")
-    b = None if bias is None else bias.float().contiguous()
+    b = f32_param(bias)
     if b is not None and b.shape != (d,):
         raise ValueError(f"{who}: bias must be ({d},)")
     init = None

@@ -9,7 +9,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
-from ._common import dtype_code, ptr, require_cuda, stream_of
+from ._common import dtype_code, f32_param, ptr, require_cuda, stream_of
 
 __all__ = ["rmsnorm"]
 
@@ -40,7 +40,7 @@ def rmsnorm(x, weight=None, eps=1e-6, *, residual=None, return_sum=False, out=No
     if return_sum and residual is None:
         raise ValueError(f"{who}: return_sum needs a residual")
     dim = x.shape[-1]
-    w = None if weight is None else weight.float().contiguous()
+    w = f32_param(weight)
     if w is not None and w.shape != (dim,):
         raise ValueError(f"{who}: weight must be ({dim},)")
     xr, lead = _rows(x, who)

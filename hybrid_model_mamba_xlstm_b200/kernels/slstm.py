@@ -11,7 +11,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib
-from ._common import dtype_code, ptr, require_cuda, stream_of
+from ._common import dtype_code, f32_param, ptr, require_cuda, stream_of
 
 __all__ = ["slstm_scan"]
 
@@ -32,7 +32,7 @@ def slstm_scan(gates_pre, norm_weight, *, R=None, eps=1e-6, exponential_gate=Tru
     bsz, L, nh, _, hd = gates_pre.shape
     io = gates_pre.dtype if gates_pre.dtype in (torch.float32, torch.bfloat16) else torch.float32
     g = gates_pre.to(io).contiguous()
-    w = norm_weight.float().contiguous()
+    w = f32_param(norm_weight)
     if w.shape != (hd,):
         raise ValueError(f"{who}: norm_weight must be ({hd},)")
     Rb = None
