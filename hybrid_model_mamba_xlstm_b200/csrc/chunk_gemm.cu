@@ -54,6 +54,8 @@ constexpr int kPitch = 36;        // floats per row of a warp's 32 x 32 epilogue
 struct Params {
   int M, N, BN, ntn, ntm, ntiles;  // tiles: n tiles x m tiles x groups
   int ksteps[kMaxProd];
+  int nprod;       // products of the launch
+  int interleave;  // 1: all products have the same K; their slices alternate (see the loops)
   int a_mn[kMaxProd], b_mn[kMaxProd];
   float alpha;
   int mask;
@@ -213,8 +215,15 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_gemm_kernel(
   const int e0 = p.ksteps[0], e1 = e0 + p.ksteps[1], e2 = e1 + p.ksteps[2], kt = e2 + p.ksteps[3];
   const int amn0 = p.a_mn[0], amn1 = p.a_mn[1], amn2 = p.a_mn[2], amn3 = p.a_mn[3];
   const int bmn0 = p.b_mn[0], bmn1 = p.b_mn[1], bmn2 = p.b_mn[2], bmn3 = p.b_mn[3];
-  auto prod_of = [&](int j) { return (j >= e0) + (j >= e1) + (j >= e2); };
-  auto first_of = [&](int pi) { return pi == 0 ? 0 : (pi == 1 ? e0 : (pi == 2 ? e1 : e2)); };
+  // K slice j of a tile: product-major, or — when every product has the same K — slice-major
+  // with the products alternating, so that an operand shared by two products (the high part of
+  // a split operand meets both parts of the other) is re-read from L2 right after its first
+  // load instead of after the whole K loop of the product between them
+  const int np = p.nprod, il = p.interleave;
+  auto prod_of = [&](int j) { return il ? j % np : (j >= e0) + (j >= e1) + (j >= e2); };
+  auto kslice_of = [&](int j, int pi) {
+    return il ? j / np : j - (pi == 0 ? 0 : (pi == 1 ? e0 : (pi == 2 ? e1 : e2)));
+  };
 
   int issued = 0;  // producer: K slices whose loads were issued
   if (warp == kProducerWarp) {
@@ -233,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_gemm_kernel(
             break;
           }
           const int pi = prod_of(j);
-          const int k0 = (j - first_of(pi)) * kBK;
+          const int k0 = kslice_of(j, pi) * kBK;
           unsigned char* sa = sm + s * S::kStage;
           const int bmn = pi == 0 ? bmn0 : pi == 1 ? bmn1 : pi == 2 ? bmn2 : bmn3;
           tc::mbar_expect_tx(&full[s], kBM * 128 + (bmn ? ((BN + 63) / 64) * kPanel : BN * 128));
@@ -400,6 +409,15 @@ static hxm_status launch(const hxm_chunk_gemm_args* a, int BN, cudaStream_t st) 
     // B is MN-major when stored (K, N) (not transposed)
     p.b_mn[i] = B.trans ? 0 : 1;
     p.ksteps[i] = i < a->nprod ? (Op{&A}.k_len(true) + kBK - 1) / kBK : 0;
+  }
+  p.nprod = a->nprod;
+  p.interleave = 1;
+  for (int i = 1; i < a->nprod; ++i)
+    if (p.ksteps[i] != p.ksteps[0]) p.interleave = 0;
+  for (int i = 0; i < kMaxProd; ++i) {
+    const int pi = i < a->nprod ? i : 0;
+    const hxm_gemm_operand& A = a->a[pi];
+    const hxm_gemm_operand& B = a->b[pi];
     hxm_status s;
     if ((s = make_operand_map(&ma[i], A, a->groups, A.trans ? 64 : kBM, "hxm_chunk_gemm A")) != HXM_OK) return s;
     if ((s = make_operand_map(&mb[i], B, a->groups, B.trans ? BN : 64, "hxm_chunk_gemm B")) != HXM_OK) return s;
