@@ -123,12 +123,15 @@ def mm(pairs, m, n, *, out=None, want_split=False, mask=False, decay=None, accum
     prods = [t for p in pairs for t in _terms(*p)]
     G = prods[0][0].shape[0]
     dev = prods[0][0].device
-    # launches group products of equal K: the kernel then alternates their K slices, so the
-    # operand two terms of a split product share is read from L2 the second time
+    # launches group products of equal K when that takes no more launches (each extra launch
+    # re-reads and re-writes the fp32 output): the kernel then alternates their K slices, so
+    # the operand two terms of a split product share is read from L2 the second time
     by_k = {}
     for pr in prods:
         by_k.setdefault(pr[0].shape[1] if pr[1] else pr[0].shape[2], []).append(pr)
     calls = [g[i:i + MAX_PROD] for g in by_k.values() for i in range(0, len(g), MAX_PROD)]
+    if len(calls) > -(-len(prods) // MAX_PROD):
+        calls = [prods[i:i + MAX_PROD] for i in range(0, len(prods), MAX_PROD)]
     if out is None and (not want_split or len(calls) > 1):
         out = torch.empty(G, m, n, device=dev, dtype=torch.float32)
     sp = None
