@@ -418,9 +418,10 @@ def prefill_metric(args, dev, world, rank):
     flop_tok = 2 * n_w + (2 * cfg.dim * cfg.vocab_size if tied else 0) + \
         n_mlstm * cfg.num_heads * 4 * 128 * cfg.head_dim
     for kind, per in (("weak", gb), ("strong", max(1, gb // world))):
-        # finer wavefront pieces when one GPU holds one or two sequences (measured at batch 1:
-        # 11.6 ms with 8 pieces, 13.2 with 4, 14.0 with 16; at batch 8, 4 pieces: 29.5 ms)
-        pieces = 8 if per <= 2 else 4
+        # finer wavefront pieces when one GPU holds up to four sequences (measured: batch 1
+        # 11.2 ms with 8 pieces, 13.2 with 4, 14.0 with 16; batch 4 17.97 with 8, 18.43 with 4;
+        # batch 8, 4 pieces 29.5 ms)
+        pieces = 8 if per <= 4 else 4
         ids = torch.randint(0, 50304, (per, seqlen), generator=g, device=dev)
         with torch.no_grad():
             pg = Lyr.PrefillGraph(model, per, seqlen, pieces=pieces, device=dev)
