@@ -11,9 +11,11 @@ y*silu(z), final state) over the rank's batch.  Multi-GPU: every rank scans
 its own batch (units are independent channels; no collective on the data
 path) -> weak scaling; time = max over ranks of CUDA-event time.
 
-Prints ONE JSON line (rank 0).  ``--impl reference`` times the CPU
-restatement of the reference loop (the C oracle, all host threads) on a
-bounded sample of the same workload and prints the same metric.
+Prints ONE JSON line (rank 0).  ``--impl reference`` times the reference's
+own CPU path (its ``selective_scan_pytorch`` with the softplus / SiLU of
+``MambaBlock.forward``, from the unmodified install in baseline/_ref; the C
+restatement of that loop when the install is absent), all host threads, on a
+bounded sample of the same workload, and prints the same metric.
 """
 from __future__ import annotations
 
