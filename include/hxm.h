@@ -205,7 +205,7 @@ hxm_status hxm_mlstm_chunkwise_fwd_noalloc(const hxm_mlstm_args* args, void* str
 /*   Qs_t = q_t e^(b_t - rho),  Ks_t = k_t e^(log_i_t + rho - b_t)            */
 /* (intra-chunk weights Qs_t . Ks_s; the state entering the next chunk is    */
 /* e^g C + e^rho Ks^T [v | 1], n riding as the column of ones).  The batched */
-/* chunk GEMMs between the two calls below are the caller's (cuBLAS).        */
+/* chunk GEMMs between the calls below are the caller's (hxm_chunk_gemm).    */
 /*   hxm_mlstm_bwd_prepare: q, k (b, h, t) strided with dense dqk, log gates */
 /*     (b, h, t) strided, per head (gate_mode 0) or per channel (1, dense    */
 /*     dqk) -> q_scaled, k_scaled (b, h, nchunks*chunk, dqk), zero past      */
