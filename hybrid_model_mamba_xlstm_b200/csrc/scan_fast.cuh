@@ -212,16 +212,42 @@ __global__ void __launch_bounds__(CH) scan_fast_kernel(const Params p) {
   const int ntiles = (te - tb + kT - 1) / kT;
 
   auto stage_ptr = [&](int st) { return reinterpret_cast<T*>(smem_raw + st * S::kStageBytes); };
-  // Whole tiles of a CTA whose channels and states all exist (time-major layout) take a lean
-  // path: the thread's copies sit at fixed row / step offsets from one base pointer per tensor,
-  // so a tile costs one address add per 16-byte copy and no bounds arithmetic (measured at
-  // 8 x 32768 x 4096: 5.45 -> 5.12 ms).
-  const bool lean = !CM && d0 + CH <= p.dim && p.dstate == 16;
+  // Whole tiles of a CTA whose channels and states all exist take a lean path: the thread's
+  // copies sit at fixed row / step offsets from one base pointer per tensor, so a tile costs
+  // one address add per 16-byte copy and no bounds arithmetic (measured at 8 x 32768 x 4096,
+  // time-major: 5.45 -> 5.12 ms).
+  const bool lean = d0 + CH <= p.dim && p.dstate == 16;
   auto issue = [&](int k) {
     T* base = stage_ptr(k & 1);
     const int t0 = tb + k * kT, tk = min(kT, te - t0);
     constexpr int kChunks = kT / kE;
-    if (lean && tk == kT) {
+    if (CM && lean && tk == kT) {
+      // [kT][CH] step rows: thread = one 16-byte channel group of every (CH / kE)-th step row
+      constexpr int kRowChunks = CH / kE, kStepStep = CH / kRowChunks;
+      const int lt = tid / kRowChunks, lc = (tid % kRowChunks) * kE;
+#pragma unroll
+      for (int which = 0; which < 3; ++which) {
+        if (which == 2 && !has_z) break;
+        const T* g = which == 0 ? ug : (which == 1 ? dtg : zg);
+        const int64_t st = which == 0 ? p.su[1] : (which == 1 ? p.sdt[1] : p.sz[1]);
+        const T* src = g + (int64_t)(t0 + lt) * st + d0 + lc;
+        T* dst = base + which * S::kIoSlot + lt * CH + lc;
+#pragma unroll
+        for (int i = 0; i < kT * kRowChunks / CH; ++i)
+          cp_async16(dst + i * kStepStep * CH, src + (int64_t)i * kStepStep * st, 16);
+      }
+      // raw B, C step rows [kT][B0..15 C0..15]
+      constexpr int kBcChunks = 32 / kE, kBcStep = CH / kBcChunks;
+      const int bt = tid / kBcChunks, bn = (tid % kBcChunks) * kE;
+      const T* bsrc = bn < 16 ? Bg + (int64_t)(t0 + bt) * p.sB[1] + bn : Cg + (int64_t)(t0 + bt) * p.sC[1] + (bn - 16);
+      const int64_t bst = bn < 16 ? p.sB[1] : p.sC[1];
+      T* raw = base + 3 * S::kIoSlot + bt * 32 + bn;
+#pragma unroll
+      for (int i = 0; i < kT * kBcChunks / CH; ++i) cp_async16(raw + i * kBcStep * 32, bsrc + (int64_t)i * kBcStep * bst, 16);
+      cp_async_commit();
+      return;
+    }
+    if (!CM && lean && tk == kT) {
       constexpr int kRowStep = CH / kChunks;  // rows between one thread's consecutive copies
       const int lr = tid / kChunks, lt = (tid % kChunks) * kE;
 #pragma unroll
