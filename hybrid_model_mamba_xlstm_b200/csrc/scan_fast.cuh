@@ -441,10 +441,58 @@ __global__ void __launch_bounds__(CH) scan_fast_state_kernel(const Params p) {
   const T* dtg = static_cast<const T*>(p.dt) + b * p.sdt[0];
   const T* Bg = static_cast<const T*>(p.B) + b * p.sB[0];
   auto stage_ptr = [&](int st) { return reinterpret_cast<T*>(smem_raw + st * S::kStageBytes); };
+  const bool lean = d0 + CH <= p.dim && p.dstate == 16;  // whole tiles only here
   auto issue = [&](int k) {
     T* base = stage_ptr(k & 1);
     const int t0 = tb + k * kT;
     constexpr int kChunks = kT / kE;
+    if (lean) {  // fixed per-thread offsets, one address add per 16-byte copy (see scan_fast_kernel)
+      if (CM) {
+        constexpr int kRowChunks = CH / kE, kStepStep = CH / kRowChunks;
+        const int lt = tid / kRowChunks, lc = (tid % kRowChunks) * kE;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          const T* g = which == 0 ? ug : dtg;
+          const int64_t st = which == 0 ? p.su[1] : p.sdt[1];
+          const T* src = g + (int64_t)(t0 + lt) * st + d0 + lc;
+          T* dst = base + which * S::kIoSlot + lt * CH + lc;
+#pragma unroll
+          for (int i = 0; i < kT * kRowChunks / CH; ++i)
+            cp_async16(dst + i * kStepStep * CH, src + (int64_t)i * kStepStep * st, 16);
+        }
+        constexpr int kBChunks = 16 / kE, kBStep = CH / kBChunks;  // B step rows [kT][B0..15]
+        const int bt = tid / kBChunks, bn = (tid % kBChunks) * kE;
+        if (kT * kBChunks >= CH || tid < kT * kBChunks) {
+          T* raw = base + 3 * S::kIoSlot + bt * 32 + bn;
+          const T* bsrc = Bg + (int64_t)(t0 + bt) * p.sB[1] + bn;
+#pragma unroll
+          for (int i = 0; i < (kT * kBChunks + CH - 1) / CH; ++i)
+            cp_async16(raw + i * kBStep * 32, bsrc + (int64_t)i * kBStep * p.sB[1], 16);
+        }
+      } else {
+        constexpr int kRowStep = CH / kChunks;
+        const int lr = tid / kChunks, lt = (tid % kChunks) * kE;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          const T* g = which == 0 ? ug : dtg;
+          const int64_t sd = which == 0 ? p.su[2] : p.sdt[2];
+          const T* src = g + (int64_t)(d0 + lr) * sd + t0 + lt;
+          T* dst = base + which * S::kIoSlot + lr * S::kTP + lt;
+#pragma unroll
+          for (int i = 0; i < kChunks; ++i) cp_async16(dst + i * kRowStep * S::kTP, src + (int64_t)i * kRowStep * sd, 16);
+        }
+        if (16 * kChunks >= CH || tid < 16 * kChunks) {  // B rows [16][kT]
+          T* raw = base + 3 * S::kIoSlot;
+#pragma unroll
+          for (int i = 0; i < (16 * kChunks + CH - 1) / CH; ++i) {
+            const int n = lr + i * kRowStep;
+            cp_async16(raw + n * S::kTP + lt, Bg + (int64_t)n * p.sB[2] + t0 + lt, 16);
+          }
+        }
+      }
+      cp_async_commit();
+      return;
+    }
 #pragma unroll 1
     for (int which = 0; which < 2; ++which) {
       const T* g = which == 0 ? ug : dtg;
