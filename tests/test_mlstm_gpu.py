@@ -156,10 +156,11 @@ def test_empty_sequence_keeps_state(ops):
     assert torch.allclose(C * m.exp()[..., None, None], C0) and torch.allclose(n * m.exp()[..., None], n0)
 
 
-@pytest.mark.parametrize("d", [128, 256, 512])
-def test_stream_kernel_channel_gates(ops, d):
+@pytest.mark.parametrize("d,odd", [(128, False), (256, False), (512, False), (128, True)])
+def test_stream_kernel_channel_gates(ops, d, odd):
     """Per-channel gates (mLSTMBlock's i = exp(pre), f = sigmoid(pre), one per
-    key channel) on the key-streaming tcgen05 kernel vs the float64 oracle."""
+    key channel) on the key-streaming tcgen05 kernel vs the float64 oracle.
+    odd: the gate rows are views of (.., d + 1)-wide memory (odd time stride)."""
     g = torch.Generator().manual_seed(21)
     b, h, L = 1, 2, 300
     q = (torch.randn(b, h, L, d, generator=g) / d ** 0.5).to("cuda", torch.bfloat16)
@@ -168,6 +169,11 @@ def test_stream_kernel_channel_gates(ops, d):
     ipre = torch.randn(b, h, L, d, generator=g) * 0.5
     fpre = torch.randn(b, h, L, d, generator=g) + 1.0
     li, lf = ipre.cuda(), torch.nn.functional.logsigmoid(fpre).cuda()
+    if odd:
+        wide = torch.zeros(2, b, h, L, d + 1, device="cuda")
+        wide[0, ..., :d], wide[1, ..., :d] = li, lf
+        li, lf = wide[0, ..., :d], wide[1, ..., :d]
+        assert li.stride(2) % 2 == 1
     out, (C, n, m) = ops.mlstm_chunkwise_fwd(q, k, v, li, lf, return_state=True)
     ref, Cr, nr = R.tfla_recurrent(np64(q), np64(k), np64(v), np.exp(np64(li)), np.exp(np64(lf)))
     assert rel_err(np64(out), ref) < TOL16
