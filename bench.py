@@ -422,7 +422,7 @@ def prefill_metric(args, dev, world, rank):
     for kind, per in (("weak", gb), ("strong", max(1, gb // world))):
         # finer wavefront pieces when one GPU holds up to four sequences (measured: batch 1
         # 11.2 ms with 8 pieces, 13.2 with 4, 14.0 with 16; batch 4 17.97 with 8, 18.43 with 4;
-        # batch 8, 4 pieces 29.5 ms)
+        # batch 8, 4 pieces 29.5-29.7 ms, 6 pieces 31.0, 8 pieces 31.9)
         pieces = 8 if per <= 4 else 4
         ids = torch.randint(0, 50304, (per, seqlen), generator=g, device=dev)
         with torch.no_grad():
