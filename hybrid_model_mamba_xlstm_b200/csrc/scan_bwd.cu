@@ -10,24 +10,33 @@
 //   dC_t += dy_t h_t,  dB_t += dh_t delta_t u_t,  dA += dh_t h_{t-1} a_t delta_t,
 //   ddelta_t = sum_n dh_t (h_{t-1} a_t A + B_t u_t),
 //   du_t = dy_t D + delta_t dh_t . B_t,  dD += dy_t u_t.
-// One thread per (batch row, channel), 16 fp32 states in registers; the B, C
-// rows of each 16-step chunk are staged in shared memory for the whole CTA.
+// SPLIT threads per (batch row, channel), adjacent lanes, each holding
+// 16 / SPLIT of the 16 fp32 states in registers (the states of a channel
+// evolve independently; the sums over states — y, d delta, du — take
+// log2(SPLIT) shuffles each).  SPLIT = 2 (64 channels per CTA) when that grid
+// covers the SMs, else 4 (32 channels per CTA, twice the CTAs): batch 8 x 2048
+// x 2048 x 16 2.91 ms with 2 against 3.09 with 4, batch 1 2.16 against 1.85
+// (one thread per channel: 3.70 and 3.23).  The B, C rows of each 16-step chunk are staged in shared
+// memory for the whole CTA.
 // A first pass recomputes the forward and stores h every 16 steps in the
 // workspace;
 // the reverse pass reloads each checkpoint, recomputes the chunk's h_{t-1}
 // into shared memory and walks it backwards.  dB, dC are sums over channels:
-// a warp reduce-scatter leaves lane l with the warp's sum of value l, one
-// atomicAdd per warp.  dA, dD, dbias sum over time in registers and over the
-// batch with atomics.
+// a warp reduce-scatter over the lanes that hold the same states leaves every
+// lane with the warp's sum of one of the 32 values (dB and dC of each state),
+// the warps of the CTA add theirs through shared memory after the chunk, and
+// one atomic per (step, value) and CTA follows.  dA, dD, dbias sum over time in registers
+// and over the batch with atomics.
 #include "capi_internal.h"
 #include "common.cuh"
 
 namespace hxm {
 namespace scanbwd {
 
-constexpr int CH = 64;   // channels per CTA (one per thread)
-constexpr int kT = 16;   // checkpoint interval
-constexpr int NS = 16;   // max dstate
+constexpr int kT = 16;         // checkpoint interval
+constexpr int NS = 16;         // max dstate
+constexpr int kThreads = 128;  // SPLIT threads per channel x kThreads / SPLIT channels
+constexpr int kWarps = kThreads / 32;
 
 struct Params {
   int batch, seqlen, dim, dstate;
@@ -46,31 +55,42 @@ HXM_DEV float ld(const void* base, const int64_t* s, int b, int t, int c) {
   return to_f32<T>(static_cast<const T*>(base)[b * s[0] + (int64_t)t * s[1] + (int64_t)c * s[2]]);
 }
 
-template <typename T, int ZMODE, bool SP>
-__global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
-  extern __shared__ float hs[];  // [kT][NS][CH]: h_{t-1} of the chunk, then [3][kT][CH]
-  float* sdl = hs + kT * NS * CH;   // delta_t of the chunk (per channel)
-  float* suv = sdl + kT * CH;       // u_t
-  float* ssg = suv + kT * CH;       // d delta / d raw (softplus' derivative, or 1)
-  const int tid = threadIdx.x, lane = tid & 31;
+// dynamic shared memory, in floats:
+// (CH = kThreads / SPLIT channels per CTA, NH = NS / SPLIT states per thread)
+//   hs  [kT][NH][CH][SPLIT] h_{t-1} of the chunk (state hf*NH + j of channel c at [i][j][c][hf])
+//   sdl, suv, ssg [kT][CH] delta_t, u_t, d delta / d raw of the chunk
+//   sred [kWarps][kT][32] each warp's dB / dC sums of the chunk's steps
+constexpr int smem_floats(int CH) { return kT * NS * CH + 3 * kT * CH + kWarps * kT * 32; }
+
+template <typename T, int ZMODE, bool SP, int SPLIT>
+__global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const Params p) {
+  constexpr int CH = kThreads / SPLIT, NH = NS / SPLIT;
+  extern __shared__ float hs[];
+  float* sdl = hs + kT * NS * CH;
+  float* suv = sdl + kT * CH;
+  float* ssg = suv + kT * CH;
+  float* sred = ssg + kT * CH;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = tid / SPLIT, hf = tid % SPLIT;  // channel of the CTA, share of its states
   const int b = blockIdx.y;
-  const int d = blockIdx.x * CH + tid;
+  const int d = blockIdx.x * CH + c;
   const bool dvalid = d < p.dim;
   const int dc = dvalid ? d : 0;
   const int N = p.dstate;
+  const int n0 = hf * NH;  // this thread's states: n0 .. n0 + NH - 1
   const int nck = (p.seqlen + kT - 1) / kT;
 
-  // a[n] = A[d, n]; a2[n] = A[d, n] log2(e): exp(delta A) = 2^(delta a2) on the MUFU unit
+  // a[j] = A[d, n0 + j]; a2[j] = a[j] log2(e): exp(delta A) = 2^(delta a2) on the MUFU unit
   // (relative error ~2e-7, the forward kernel's exponential)
-  float a[NS], a2[NS];
+  float a[NH], a2[NH];
 #pragma unroll
-  for (int n = 0; n < NS; ++n) {
-    a[n] = n < N ? p.A[(int64_t)dc * p.sA[0] + (int64_t)n * p.sA[1]] : 0.f;
-    a2[n] = a[n] * kLog2e;
+  for (int j = 0; j < NH; ++j) {
+    a[j] = n0 + j < N ? p.A[(int64_t)dc * p.sA[0] + (int64_t)(n0 + j) * p.sA[1]] : 0.f;
+    a2[j] = a[j] * kLog2e;
   }
   const float Dd = p.D ? p.D[dc] : 0.f;
   const float bias = p.bias ? p.bias[dc] : 0.f;
-  float* ck = p.ckpt + ((int64_t)b * p.dim + dc) * nck * NS;
+  float* ck = p.ckpt + ((int64_t)b * p.dim + dc) * nck * NS + n0;
 
   auto delta_of = [&](int t, float& raw) {
     raw = ld<T>(p.dt, p.sdt, b, t, dc) + bias;
@@ -82,7 +102,7 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
   __shared__ float sbc[2][kT][NS];
   auto stage = [&](int k, int nw) {
     const int t0 = k * kT;
-    for (int e = tid; e < nw * kT * NS; e += CH) {
+    for (int e = tid; e < nw * kT * NS; e += kThreads) {
       const int w = e / (kT * NS), i = (e / NS) % kT, n = e % NS;
       const int t = t0 + i;
       float v = 0.f;
@@ -90,11 +110,12 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
       sbc[w][i][n] = v;
     }
   };
+  auto hs_at = [&](int i, int j) -> float& { return hs[((i * NH + j) * CH + c) * SPLIT + hf]; };
 
   // ---- pass 1: forward recompute, checkpoints every kT steps -----------------
-  float h[NS];
+  float h[NH];
 #pragma unroll
-  for (int n = 0; n < NS; ++n) h[n] = (p.h0 && n < N) ? p.h0[((int64_t)b * p.dim + dc) * N + n] : 0.f;
+  for (int j = 0; j < NH; ++j) h[j] = (p.h0 && n0 + j < N) ? p.h0[((int64_t)b * p.dim + dc) * N + n0 + j] : 0.f;
   for (int k = 0; k < nck; ++k) {
     const int t0 = k * kT, tn = min(kT, p.seqlen - t0);
     __syncthreads();  // the previous chunk's rows are consumed
@@ -102,60 +123,65 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
     __syncthreads();
     if (dvalid) {
 #pragma unroll
-      for (int n = 0; n < NS; ++n) ck[k * NS + n] = h[n];
+      for (int j = 0; j < NH; ++j) ck[k * NS + j] = h[j];
     }
     for (int i = 0; i < tn; ++i) {
       float raw;
       const float dl = delta_of(t0 + i, raw);
       const float du = dl * ld<T>(p.u, p.su, b, t0 + i, dc);
 #pragma unroll
-      for (int n = 0; n < NS; ++n)
-        if (n < N) h[n] = fmaf(ex2_approx(dl * a2[n]), h[n], du * sbc[0][i][n]);
+      for (int j = 0; j < NH; ++j) h[j] = fmaf(ex2_approx(dl * a2[j]), h[j], du * sbc[0][i][n0 + j]);
     }
   }
 
   // ---- pass 2: reverse ------------------------------------------------------
-  float dh[NS], dAacc[NS];
+  float dh[NH], dAacc[NH];
 #pragma unroll
-  for (int n = 0; n < NS; ++n) dh[n] = dAacc[n] = 0.f;
+  for (int j = 0; j < NH; ++j) dh[j] = dAacc[j] = 0.f;
   float dDacc = 0.f, dbacc = 0.f;
   for (int k = nck - 1; k >= 0; --k) {
     const int t0 = k * kT, tn = min(kT, p.seqlen - t0);
-    __syncthreads();
+    __syncthreads();  // the previous chunk's rows and sums are consumed
     stage(k, 2);
     __syncthreads();
 #pragma unroll
-    for (int n = 0; n < NS; ++n) h[n] = dvalid ? ck[k * NS + n] : 0.f;
+    for (int j = 0; j < NH; ++j) h[j] = dvalid ? ck[k * NS + j] : 0.f;
     for (int i = 0; i < tn; ++i) {
       const int t = t0 + i;
 #pragma unroll
-      for (int n = 0; n < NS; ++n) hs[(i * NS + n) * CH + tid] = h[n];
+      for (int j = 0; j < NH; ++j) hs_at(i, j) = h[j];
       float raw;
       const float dl = delta_of(t, raw);
       const float uv = ld<T>(p.u, p.su, b, t, dc);
       const float du = dl * uv;
-      sdl[i * CH + tid] = dl;
-      suv[i * CH + tid] = uv;
-      ssg[i * CH + tid] = SP ? (raw > 20.f ? 1.f : sigmoid_acc(raw)) : 1.f;
+      if (hf == 0) {
+        sdl[i * CH + c] = dl;
+        suv[i * CH + c] = uv;
+        ssg[i * CH + c] = SP ? (raw > 20.f ? 1.f : sigmoid_acc(raw)) : 1.f;
+      }
 #pragma unroll
-      for (int n = 0; n < NS; ++n)
-        if (n < N) h[n] = fmaf(ex2_approx(dl * a2[n]), h[n], du * sbc[0][i][n]);
+      for (int j = 0; j < NH; ++j) h[j] = fmaf(ex2_approx(dl * a2[j]), h[j], du * sbc[0][i][n0 + j]);
     }
+    __syncwarp();  // sdl / suv / ssg of a channel are written by its first lane
     for (int i = tn - 1; i >= 0; --i) {
       const int t = t0 + i;
-      const float dl = sdl[i * CH + tid];
-      const float u = suv[i * CH + tid];
+      const float dl = sdl[i * CH + c];
+      const float u = suv[i * CH + c];
       const float go = dvalid ? ld<T>(p.dout, p.sdo, b, t, dc) : 0.f;
-      float Bv[NS], Cv[NS], hp[NS], at[NS];
-      float y = Dd * u;
+      float Bv[NH], Cv[NH], hp[NH], at[NH], ht[NH];
+      float yp = 0.f;
 #pragma unroll
-      for (int n = 0; n < NS; ++n) {
-        Bv[n] = sbc[0][i][n];
-        Cv[n] = sbc[1][i][n];
-        hp[n] = hs[(i * NS + n) * CH + tid];
-        at[n] = n < N ? ex2_approx(dl * a2[n]) : 0.f;
-        y = fmaf(Cv[n], fmaf(at[n], hp[n], dl * Bv[n] * u), y);
+      for (int j = 0; j < NH; ++j) {
+        Bv[j] = sbc[0][i][n0 + j];
+        Cv[j] = sbc[1][i][n0 + j];
+        hp[j] = hs_at(i, j);
+        at[j] = n0 + j < N ? ex2_approx(dl * a2[j]) : 0.f;
+        ht[j] = fmaf(at[j], hp[j], dl * Bv[j] * u);
+        yp = fmaf(Cv[j], ht[j], yp);
       }
+#pragma unroll
+      for (int o = 1; o < SPLIT; o <<= 1) yp += __shfl_xor_sync(0xffffffffu, yp, o);
+      const float y = fmaf(Dd, u, yp);
       float dy = go, dzv = 0.f;
       if (ZMODE == 1) {
         const float zv = ld<T>(p.z, p.sz, b, t, dc);
@@ -168,80 +194,108 @@ __global__ void __launch_bounds__(CH) scan_bwd_kernel(const Params p) {
         dzv = go * y * s * (1.f + zv * (1.f - s));
       }
       dDacc = fmaf(dy, u, dDacc);
-      float duv = dy * Dd, ddl = 0.f;
-      float red[2 * NS];  // [dB_t partial | dC_t partial]
+      float dup = 0.f, ddp = 0.f;
+      float red[2 * NH];  // [dB_t partials of states n0.. | dC_t partials]
 #pragma unroll
-      for (int n = 0; n < NS; ++n) {
-        const float ht = fmaf(at[n], hp[n], dl * Bv[n] * u);
-        dh[n] = fmaf(dy, Cv[n], dh[n]);
-        red[NS + n] = dvalid ? dy * ht : 0.f;
-        const float da = dh[n] * hp[n];
-        ddl = fmaf(da * at[n], a[n], ddl);
-        ddl = fmaf(dh[n], Bv[n] * u, ddl);
-        dAacc[n] = fmaf(da * at[n], dl, dAacc[n]);
-        red[n] = dvalid ? dh[n] * dl * u : 0.f;
-        duv = fmaf(dh[n] * dl, Bv[n], duv);
-        dh[n] *= at[n];
+      for (int j = 0; j < NH; ++j) {
+        dh[j] = fmaf(dy, Cv[j], dh[j]);
+        red[NH + j] = dvalid ? dy * ht[j] : 0.f;
+        const float da = dh[j] * hp[j];
+        ddp = fmaf(da * at[j], a[j], ddp);
+        ddp = fmaf(dh[j], Bv[j] * u, ddp);
+        dAacc[j] = fmaf(da * at[j], dl, dAacc[j]);
+        red[j] = dvalid ? dh[j] * dl * u : 0.f;
+        dup = fmaf(dh[j] * dl, Bv[j], dup);
+        dh[j] *= at[j];
       }
-      const float draw = ddl * ssg[i * CH + tid];
+#pragma unroll
+      for (int o = 1; o < SPLIT; o <<= 1) {
+        dup += __shfl_xor_sync(0xffffffffu, dup, o);
+        ddp += __shfl_xor_sync(0xffffffffu, ddp, o);
+      }
+      const float duv = fmaf(dy, Dd, dup);
+      const float ddl = ddp;
+      const float draw = ddl * ssg[i * CH + c];
       dbacc += draw;
-      if (dvalid) {
+      if (dvalid && hf == 0) {
         const int64_t o = ((int64_t)b * p.seqlen + t) * p.dim + d;
         if (p.du) p.du[o] = duv;
         if (p.ddt) p.ddt[o] = draw;
         if (ZMODE != 0 && p.dz) p.dz[o] = dzv;
       }
-      // warp reduce-scatter of the 32 partials: lane l ends with the warp sum of red[l]
+      // reduce-scatter over the lanes with the same hf (xor offsets 16 .. SPLIT keep
+      // lane % SPLIT): lane l ends with the warp sum of red[l / SPLIT]
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
+      for (int off = 16, m = NH; off >= SPLIT; off >>= 1, m >>= 1) {
 #pragma unroll
-        for (int j = 0; j < off; ++j) {
+        for (int j = 0; j < m; ++j) {
           const bool up = lane & off;
-          const float send = up ? red[j] : red[j + off];
-          const float keep = up ? red[j + off] : red[j];
+          const float send = up ? red[j] : red[j + m];
+          const float keep = up ? red[j + m] : red[j];
           red[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
         }
       }
-      const int n = lane & (NS - 1);
-      if (n < N) {
-        float* dst = lane < NS ? p.dB : p.dC;
-        if (dst) atomicAdd(dst + ((int64_t)b * p.seqlen + t) * N + n, red[0]);
+      sred[(warp * kT + i) * 32 + lane] = red[0];
+    }
+    __syncthreads();  // every warp's sums of the chunk are in sred
+    for (int e = tid; e < tn * 32; e += kThreads) {
+      const int i = e >> 5, l = e & 31;
+      const int v = l / SPLIT, n = (l % SPLIT) * NH + v % NH;
+      float* dst = v < NH ? p.dB : p.dC;
+      if (dst && n < N) {
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) sum += sred[(w * kT + i) * 32 + l];
+        atomicAdd(dst + ((int64_t)b * p.seqlen + t0 + i) * N + n, sum);
       }
     }
   }
   if (dvalid) {
 #pragma unroll
-    for (int n = 0; n < NS; ++n) {
-      if (n < N) {
-        if (p.dA) atomicAdd(p.dA + (int64_t)d * N + n, dAacc[n]);
-        if (p.dh0) p.dh0[((int64_t)b * p.dim + d) * N + n] = dh[n];
+    for (int j = 0; j < NH; ++j) {
+      if (n0 + j < N) {
+        if (p.dA) atomicAdd(p.dA + (int64_t)d * N + n0 + j, dAacc[j]);
+        if (p.dh0) p.dh0[((int64_t)b * p.dim + d) * N + n0 + j] = dh[j];
       }
     }
-    if (p.dD) atomicAdd(p.dD + d, dDacc);
-    if (p.dbias) atomicAdd(p.dbias + d, dbacc);
+    if (hf == 0) {
+      if (p.dD) atomicAdd(p.dD + d, dDacc);
+      if (p.dbias) atomicAdd(p.dbias + d, dbacc);
+    }
   }
 }
 
-template <typename T, int ZMODE, bool SP>
+template <typename T, int ZMODE, bool SP, int SPLIT>
 hxm_status launch(const Params& p, cudaStream_t st) {
-  const size_t smem = sizeof(float) * kT * (NS + 3) * CH;
-  auto kern = scan_bwd_kernel<T, ZMODE, SP>;
+  constexpr int CH = kThreads / SPLIT;
+  const size_t smem = sizeof(float) * smem_floats(CH);
+  auto kern = scan_bwd_kernel<T, ZMODE, SP, SPLIT>;
   HXM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((p.dim + CH - 1) / CH, p.batch);
-  kern<<<grid, CH, smem, st>>>(p);
+  kern<<<grid, kThreads, smem, st>>>(p);
   return check_launch("hxm_selective_scan_bwd");
+}
+
+template <typename T, int SPLIT>
+hxm_status dispatch_split(const Params& p, int zmode, bool sp, cudaStream_t st) {
+  if (sp) {
+    if (zmode == 2) return launch<T, 2, true, SPLIT>(p, st);
+    if (zmode == 1) return launch<T, 1, true, SPLIT>(p, st);
+    return launch<T, 0, true, SPLIT>(p, st);
+  }
+  if (zmode == 2) return launch<T, 2, false, SPLIT>(p, st);
+  if (zmode == 1) return launch<T, 1, false, SPLIT>(p, st);
+  return launch<T, 0, false, SPLIT>(p, st);
 }
 
 template <typename T>
 hxm_status dispatch(const Params& p, int zmode, bool sp, cudaStream_t st) {
-  if (sp) {
-    if (zmode == 2) return launch<T, 2, true>(p, st);
-    if (zmode == 1) return launch<T, 1, true>(p, st);
-    return launch<T, 0, true>(p, st);
-  }
-  if (zmode == 2) return launch<T, 2, false>(p, st);
-  if (zmode == 1) return launch<T, 1, false>(p, st);
-  return launch<T, 0, false>(p, st);
+  int dev = 0, num_sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    num_sms = 148;
+  const int64_t ctas2 = (int64_t)((p.dim + kThreads / 2 - 1) / (kThreads / 2)) * p.batch;
+  return ctas2 >= num_sms ? dispatch_split<T, 2>(p, zmode, sp, st) : dispatch_split<T, 4>(p, zmode, sp, st);
 }
 
 static size_t workspace(const hxm_scan_args& f) {
