@@ -389,7 +389,7 @@ def secondary_metrics(args, dev, world, rank):
     out["scan_bwd_b8_l2048_d2048_n16"] = {
         "metric": "selective-scan backward GB/s (one read of each bf16 input, one write of each fp32 gradient)",
         "value": world * nbytes / ms / 1e6, "unit": "GB/s", "ms": ms, "scaling": "weak",
-        "kernel": "hxm::scan::scan_bwd_kernel (checkpointed reverse recurrence)",
+        "kernel": "hxm::scanbwd::scan_bwd_kernel (checkpointed reverse recurrence, 2 lanes per channel here)",
         "roofline": roofline_obj("hbm", nbytes / ms / 1e6, "GB/s", "scan_bwd_kernel scan_bwd_b8_l2048_d2048_n16",
                                  {"bytes": nbytes})}
     del inp, dout
